@@ -1,0 +1,143 @@
+// common.cuh -- shared device helpers for the GSD-LQ sm_100a kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/gsdlq.h"
+
+namespace gsdlq {
+
+constexpr int kWarp = 32;
+
+// Device-side error word.  Kernels never trap: on a violated precondition they
+// skip the offending access and OR a bit in here; the host reads it with
+// gsdlq_device_flags().
+extern __device__ unsigned int g_device_flags;
+
+__device__ __forceinline__ void raise_flag(unsigned int bit) { atomicOr(&g_device_flags, bit); }
+
+__device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+__device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
+
+// bf16 bits (high half of an fp32) <-> float
+__device__ __forceinline__ float bf16lo_to_f(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16hi_to_f(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// Pack (a, b) -> bf16x2 with a in the low half, round to nearest even.
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+
+// Split (a, b) into hi + lo bf16x2 parts: a ~= hi.x + lo.x to about 16 mantissa bits.
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf16x2(a, b);
+  const float ra = a - bf16lo_to_f(hi);
+  const float rb = b - bf16hi_to_f(hi);
+  lo = pack_bf16x2(ra, rb);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Streaming 8-byte global load that does not allocate in L1 (weights are read once).
+__device__ __forceinline__ uint2 ldg_stream_u2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t smem_addr) {
+  uint32_t r;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(r) : "r"(smem_addr));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + C, fp32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                               const float (&c)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%12,%13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+        "f"(c[3]));
+}
+
+// Bounded spin on a global counter: returns false (and raises a flag) when the
+// producer did not arrive within ~`max_ns` nanoseconds of %globaltimer.
+__device__ __forceinline__ bool wait_counter_geq(const unsigned int* ctr, unsigned int target,
+                                                 unsigned long long max_ns) {
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr));
+    if (v >= target) return true;
+    unsigned long long t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (t1 - t0 > max_ns) {
+      raise_flag(GSDLQ_FLAG_TIMEOUT);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
+// Monotone float -> uint32 map (larger float -> larger key).
+__device__ __forceinline__ uint32_t ordered_key(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key_to_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// The reference's nan_to_num before argmax (gsd_lq_cpu_runtime.py:423).
+__device__ __forceinline__ float sanitize_logit(float v) {
+  if (isnan(v)) return -1e4f;
+  if (isinf(v)) return v > 0.f ? 100.f : -1e4f;
+  return v;
+}
+
+// 64-bit argmax key: larger value wins, then the LOWER index wins.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+  return (static_cast<unsigned long long>(ordered_key(sanitize_logit(v))) << 32) |
+         static_cast<unsigned long long>(0xffffffffu - idx);
+}
+
+}  // namespace gsdlq
+
+#define GSDLQ_CUDA_CHECK_LAUNCH()                               \
+  do {                                                          \
+    cudaError_t _e = cudaGetLastError();                        \
+    if (_e != cudaSuccess) return gsdlq::record_cuda_error(_e); \
+  } while (0)
+
+namespace gsdlq {
+int record_cuda_error(cudaError_t e);
+int num_sms();
+}  // namespace gsdlq

@@ -1,0 +1,334 @@
+"""GSDLQModel: the reference's model surface on the B200 engine.
+
+Surface kept from the reference (gsd_lq_v2/run_gpu_native_chat.py:732-984 and
+gsd_lq_v2/gsd_lq_cpu_runtime.py:121-443):
+
+    m = GSDLQModel("model.gsd2", rope_interleaved=1)
+    logits = m.forward_token(token_id, pos, return_logits=True)   # np.float32[vocab] | None
+    nxt = m.sample_token(logits, temperature=0.0, top_p=0.9)
+    m.cfg, m.avg_bpw, m.vram_used_mb, m.cl.total_vram_mb, m.cl.release_all(), m.tokenizer
+
+One decode step is, per layer (5 launches; no host round trip inside a step):
+
+    1. QKV   fused linear: RMSNorm prologue (layer 0: embedding lookup), Q/K/V with
+             in-kernel low-rank + kinks, RoPE + fp16 KV append epilogue
+    2. attention (split-KV, last CTA combines)
+    3. O     fused linear, residual-add epilogue into x
+    4. gate/up fused linear: RMSNorm prologue, SwiGLU epilogue
+    5. down  fused linear, residual-add epilogue into x
+
+then the LM head (RMSNorm prologue, fused greedy argmax).  The layer stack and
+the head are each captured once in a CUDA graph and replayed; the token id and
+position are read from device memory, so replays need no re-capture.
+"""
+from __future__ import annotations
+
+import math
+import time
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from . import ops
+from .gsd2 import PackedModel, read_gsd2, HexTensor
+
+MAX_SEQ_LEN = 2048  # the reference's compile-time cache length (run_gpu_native_chat.py:99)
+
+
+class _DeviceInfo:
+    """Stands in for the reference's ``model.cl`` OpenCL runtime object."""
+
+    def __init__(self, model: "GSDLQModel"):
+        self._m = model
+        p = torch.cuda.get_device_properties(model.device)
+        self.total_vram_mb = p.total_memory / (1024 * 1024)
+        self.device_name = p.name
+
+    def release_all(self):
+        self._m.release()
+
+
+class SimpleTokenizer:
+    """Minimal tokenizer over the header's vocabulary (decode only; prompts are token ids)."""
+
+    def __init__(self, cfg: dict):
+        self.tokens = cfg.get("tokens", [])
+        self.bos_id = cfg.get("bos_id", 1)
+        self.eos_id = cfg.get("eos_id", 2)
+
+    def decode(self, ids) -> str:
+        out = []
+        for t in ids:
+            if t in (self.bos_id, self.eos_id) or t >= len(self.tokens):
+                continue
+            out.append(self.tokens[t].replace("▁", " "))
+        return "".join(out)
+
+
+class DevicePacked:
+    """A packed model whose tensors are already in device memory (GPU packer output)."""
+
+    def __init__(self, config: dict, hexes: dict, dense: dict, avg_bpw: float, mode: str):
+        self.config, self.hexes, self.dense, self.avg_bpw, self.mode = config, hexes, dense, avg_bpw, mode
+
+
+class GSDLQModel:
+    def __init__(self, source, rope_interleaved: int = 1, device=None, max_seq: int = MAX_SEQ_LEN,
+                 use_graph: bool = True, verbose: bool = False, tp=None):
+        t0 = time.time()
+        if not torch.cuda.is_available():
+            raise RuntimeError("GSDLQModel needs a CUDA device (there is no CPU path)")
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        torch.cuda.set_device(self.device)
+        L.load()
+        if rope_interleaved != 1:
+            raise NotImplementedError("the fused decode step implements interleaved RoPE, the only mode the "
+                                      "reference runtime uses (run_gpu_native_chat.py:1061-1077); the drop-in "
+                                      "gsdlq_rope_and_store_kv supports both")
+        self.rope_interleaved = rope_interleaved
+        self.max_seq = max_seq
+        self.use_graph = use_graph
+        self.tp = tp
+        if isinstance(source, str):
+            source = read_gsd2(source)
+        self._load(source)
+        self.cl = _DeviceInfo(self)
+        self.tokenizer = SimpleTokenizer(self.cfg)
+        self._graphs: dict = {}
+        self.load_seconds = time.time() - t0
+        if verbose:
+            print(f"[gsdlq] loaded in {self.load_seconds:.2f}s, {self.vram_used_mb:.1f} MB on {self.cl.device_name}")
+
+    # ------------------------------------------------------------------ loading
+    def _load(self, src):
+        dev = self.device
+        c = dict(src.config)
+        self.cfg = c
+        self.n_layers, self.hidden = c["n_layers"], c["hidden_size"]
+        self.n_heads, self.n_kv_heads, self.head_dim = c["n_heads"], c["n_kv_heads"], c["head_dim"]
+        self.ffn_size, self.vocab_size = c["ffn_size"], c["vocab_size"]
+        self.rms_eps, self.rope_theta = float(c["rms_eps"]), float(c["rope_theta"])
+        self.avg_bpw = float(src.avg_bpw)
+        self.mode = getattr(src, "mode", "unknown")
+        if self.tp is not None:
+            src = self.tp.shard(src)
+            c = self.cfg = dict(src.config)
+        self.n_heads_local = c.get("n_heads_local", self.n_heads)
+        self.n_kv_local = c.get("n_kv_heads_local", self.n_kv_heads)
+        self.ffn_local = c.get("ffn_size_local", self.ffn_size)
+        self.vocab_local = c.get("vocab_size_local", self.vocab_size)
+        if isinstance(src, DevicePacked):
+            self.hex = src.hexes
+            self.embed = src.dense["token_embd.weight"]
+            self.norms = {k: v for k, v in src.dense.items() if k != "token_embd.weight"}
+        else:
+            hexes: dict[str, HexTensor] = src.hex
+            blobs = [a for t in hexes.values() for a in t.blobs().values()]
+            arena = ops.Arena(ops.Arena.bytes_needed(blobs), dev)
+            self._arena = arena
+            self.hex = {n: ops.DeviceHex(t, dev, arena=arena) for n, t in hexes.items()}
+            self.embed = torch.from_numpy(np.ascontiguousarray(src.dense["token_embd.weight"])).to(dev)
+            self.norms = {k: torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32)).to(dev)
+                          for k, v in src.dense.items() if k != "token_embd.weight"}
+        H, Lc = self.hidden, self.n_layers
+        hd, kvl, hl = self.head_dim, self.n_kv_local, self.n_heads_local
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.k_cache = torch.zeros((Lc, self.max_seq, kvl, hd), dtype=torch.float16, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.x = torch.zeros(H, **f32)
+        self.q = torch.zeros(hl * hd, **f32)
+        self.att = torch.zeros(hl * hd, **f32)
+        self.h = torch.zeros(self.ffn_local, **f32)
+        self.logits = torch.zeros(self.vocab_local, **f32)
+        self.state = torch.zeros(4, dtype=torch.int32, device=dev)      # token, pos, step, spare
+        self.key = torch.zeros(2, dtype=torch.int64, device=dev)        # greedy argmax key (u64 bits)
+        self.out_ids = torch.zeros(max(self.max_seq, 1), dtype=torch.int32, device=dev)
+        self.rope_cs = torch.from_numpy(ops.rope_table(self.max_seq, hd, self.rope_theta)).to(dev)
+        n_sites = 4 * Lc + 1
+        self.ws = torch.zeros((n_sites, L.LINEAR_WS_WORDS), dtype=torch.int32, device=dev)
+        pb, wb = ops.attention_ws_size(hl, kvl, hd, self.max_seq)
+        self.attn_partial = torch.zeros(pb // 4 + 1, **f32)
+        self.attn_ws = torch.zeros(wb // 4 + 1, dtype=torch.int32, device=dev)
+        self._build_jobs()
+        torch.cuda.synchronize(dev)
+        self.vram_used_mb = self._bytes_resident() / (1024 * 1024)
+
+    def _bytes_resident(self) -> int:
+        n = sum(h.nbytes() for h in self.hex.values())
+        n += self.embed.numel() * 2 + sum(t.numel() * 4 for t in self.norms.values())
+        n += 2 * self.k_cache.numel() * 2
+        return n
+
+    def packed_bytes_per_token(self, pos: int | None = None) -> int:
+        """Algorithmic bytes one decode step must read: all packed linears + KV rows read + embedding row."""
+        n = sum(h.nbytes() for h in self.hex.values()) + self.hidden * 2
+        if pos is not None:
+            n += 2 * self.n_layers * (pos + 1) * self.n_kv_local * self.head_dim * 2
+        return n
+
+    # ------------------------------------------------------------------ jobs
+    def _job(self, mats, site, input_mode, x=None, norm=None, epilogue=L.EPI_STORE, ys=(), resid=None, layer=0,
+             argmax=False):
+        j = L.LinearJob()
+        for i, m in enumerate(mats):
+            j.mat[i] = m.desc()
+        j.n_mat = len(mats)
+        j.input_mode = input_mode
+        j.x = x.data_ptr() if x is not None else None
+        j.norm_w = norm.data_ptr() if norm is not None else None
+        j.eps = self.rms_eps
+        if input_mode == L.IN_EMBED:
+            j.embed = self.embed.data_ptr()
+            j.token = self.state.data_ptr()
+            j.vocab = self.vocab_size
+            j.x_out = self.x.data_ptr()
+        j.epilogue = epilogue
+        for i, y in enumerate(ys):
+            j.y[i] = y.data_ptr() if y is not None else None
+        j.resid = resid.data_ptr() if resid is not None else None
+        j.k_cache = self.k_cache.data_ptr()
+        j.v_cache = self.v_cache.data_ptr()
+        j.pos = self.state.data_ptr() + 4
+        j.rope_cs = self.rope_cs.data_ptr()
+        j.layer, j.max_seq, j.head_dim, j.interleaved = layer, self.max_seq, self.head_dim, 1
+        j.argmax_key = self.key.data_ptr() if argmax else None
+        j.workspace = self.ws[site].data_ptr()
+        return j
+
+    def _build_jobs(self):
+        self.layer_jobs = []
+        for l in range(self.n_layers):
+            p = f"blk.{l}."
+            hx = lambda n: self.hex[p + n + ".weight"]  # noqa: E731
+            an, fn = self.norms[p + "attn_norm.weight"], self.norms[p + "ffn_norm.weight"]
+            qkv = self._job([hx("attn_q"), hx("attn_k"), hx("attn_v")], 4 * l,
+                            L.IN_EMBED if l == 0 else L.IN_RMSNORM, x=self.x, norm=an,
+                            epilogue=L.EPI_ROPE_KV, ys=(self.q, None, None), layer=l)
+            att = L.AttnJob(q=self.q.data_ptr(), k_cache=self.k_cache.data_ptr(), v_cache=self.v_cache.data_ptr(),
+                            out=self.att.data_ptr(), pos_dev=self.state.data_ptr() + 4, pos_val=0, layer=l,
+                            n_heads=self.n_heads_local, n_kv_heads=self.n_kv_local, head_dim=self.head_dim,
+                            max_seq=self.max_seq, sm_scale=1.0 / math.sqrt(self.head_dim), block_table=None,
+                            page_size=0, partial=self.attn_partial.data_ptr(), workspace=self.attn_ws.data_ptr())
+            o = self._job([hx("attn_output")], 4 * l + 1, L.IN_PLAIN, x=self.att, epilogue=L.EPI_RESID,
+                          ys=(self.x,), resid=self.x)
+            gu = self._job([hx("ffn_gate"), hx("ffn_up")], 4 * l + 2, L.IN_RMSNORM, x=self.x, norm=fn,
+                           epilogue=L.EPI_SWIGLU, ys=(self.h,))
+            dn = self._job([hx("ffn_down")], 4 * l + 3, L.IN_PLAIN, x=self.h, epilogue=L.EPI_RESID,
+                           ys=(self.x,), resid=self.x)
+            self.layer_jobs.append((qkv, att, o, gu, dn))
+        self.head_job = self._job([self.hex["output.weight"]], 4 * self.n_layers, L.IN_RMSNORM, x=self.x,
+                                  norm=self.norms["output_norm.weight"], epilogue=L.EPI_STORE, ys=(self.logits,),
+                                  argmax=True)
+
+    # ------------------------------------------------------------------ step
+    def _run_layers(self):
+        allreduce = self.tp.allreduce if self.tp is not None else None
+        for qkv, att, o, gu, dn in self.layer_jobs:
+            ops.linear(qkv)
+            ops.attention(att)
+            ops.linear(o)
+            if allreduce:
+                allreduce(self, "o")
+            ops.linear(gu)
+            ops.linear(dn)
+            if allreduce:
+                allreduce(self, "down")
+
+    def _run_head(self, advance: bool = True):
+        ops.linear(self.head_job)
+        if self.tp is not None:
+            self.tp.finish_head(self)
+        if advance:
+            lib = L.load()
+            st = self.state.data_ptr()
+            L.check(lib.gsdlq_greedy_advance(self.key.data_ptr(), st, st + 4, st + 8, self.out_ids.data_ptr(),
+                                             self.out_ids.numel(), ops.stream_handle()), "greedy_advance")
+
+    def _graph(self, name, fn):
+        g = self._graphs.get(name)
+        if g is None:
+            fn()  # eager warm-up (sets kernel attributes outside capture)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            self._graphs[name] = g
+        return g
+
+    def step(self, with_head: bool = True):
+        """One decode step on the device (token/pos taken from self.state)."""
+        if self.use_graph:
+            self._graph("layers", self._run_layers).replay()
+            if with_head:
+                self._graph("head", self._run_head).replay()
+        else:
+            self._run_layers()
+            if with_head:
+                self._run_head()
+
+    def set_state(self, token_id: int, pos: int):
+        if not 0 <= pos < self.max_seq:
+            raise ValueError(f"pos {pos} outside [0, {self.max_seq})")
+        if not 0 <= token_id < self.vocab_size:
+            raise ValueError(f"token id {token_id} outside [0, {self.vocab_size})")
+        self.state[0:3].copy_(torch.tensor([token_id, pos, 0], dtype=torch.int32))
+
+    # ------------------------------------------------------------------ reference surface
+    def forward_token(self, token_id: int, pos: int, return_logits: bool = True):
+        self.set_state(int(token_id), int(pos))
+        self.step(with_head=return_logits)
+        if not return_logits:
+            return None
+        return self.logits_host()
+
+    def logits_host(self) -> np.ndarray:
+        if self.tp is not None:
+            return self.tp.gather_logits(self)
+        return self.logits.cpu().numpy()
+
+    def sample_token(self, logits, temperature: float = 0.0, top_p: float = 0.9) -> int:
+        """Greedy when temperature <= 0, else temperature + top-p sampling (gsd_lq_cpu_runtime.py:422-443)."""
+        logits = np.nan_to_num(np.asarray(logits, np.float32), nan=-1e4, posinf=100.0, neginf=-1e4)
+        if temperature <= 0.0:
+            return int(np.argmax(logits))
+        z = logits / max(temperature, 1e-4)
+        z -= np.max(z)
+        p = np.exp(z)
+        s = p.sum()
+        if s <= 0 or np.isnan(s):
+            return int(np.argmax(logits))
+        p /= s
+        idx = np.argsort(p)[::-1]
+        cp = np.cumsum(p[idx])
+        cut = int(np.argmax(cp > top_p)) + 1
+        top, pt = idx[:cut], p[idx[:cut]]
+        pt = pt / pt.sum()
+        return int(np.random.choice(top, p=pt))
+
+    def prefill(self, ids, start_pos: int = 0):
+        """Token-by-token prefill as the reference does (run_gpu_native_chat.py:1128-1131); no logits."""
+        for i, t in enumerate(ids):
+            self.set_state(int(t), start_pos + i)
+            self.step(with_head=False)
+
+    def generate(self, prompt_ids, max_new_tokens: int) -> list[int]:
+        """Greedy generation with the loop on the device: one graph replay per token, one D2H at the end.
+
+        Returns the generated ids (the reference's greedy smoke loop, run_gpu_native_chat.py:1039-1055,
+        without the EOS stop, which would need a host round trip per token)."""
+        ids = list(prompt_ids)
+        if len(ids) + max_new_tokens > self.max_seq:
+            raise ValueError("prompt + new tokens exceed max_seq")
+        self.prefill(ids[:-1])
+        self.set_state(ids[-1], len(ids) - 1)
+        for _ in range(max_new_tokens):
+            self.step(with_head=True)   # the head's advance kernel feeds the next replay
+        return self.out_ids[:max_new_tokens].cpu().tolist()
+
+    def release(self):
+        self._graphs.clear()
+        for k in ("hex", "embed", "norms", "k_cache", "v_cache", "_arena"):
+            if hasattr(self, k):
+                delattr(self, k)
+        torch.cuda.empty_cache()

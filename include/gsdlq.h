@@ -1,0 +1,226 @@
+/*
+ * gsdlq.h -- C ABI of libgsdlq_cuda.so, the B200 (sm_100a) decode engine for
+ * GSD-LQ-packed decoders.
+ *
+ * Conventions
+ *   - Every pointer argument that names tensor data is a DEVICE pointer unless
+ *     stated otherwise.  The caller owns all buffers.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy default
+ *     stream).  All calls are asynchronous on that stream.
+ *   - Every entry point returns an int status: GSDLQ_OK (0) or a negative
+ *     GSDLQ_ERR_* code.  Argument errors are reported before any launch.
+ *   - Kernels never trap.  A precondition that can only be checked on the
+ *     device (a code >= n_pts, a kink column >= cols, pos >= max_seq, a table
+ *     that is not an A2 lattice, a bounded wait that timed out) skips the
+ *     offending access and sets a bit in a device flag word, read and cleared
+ *     with gsdlq_device_flags().
+ *
+ * Section 1 lists drop-in replacements for the seven functions of the
+ * reference C engine (gsd_lq_v2/gsd_lq_cpu_engine.c), bound by the reference
+ * runtime through ctypes at gsd_lq_v2/gsd_lq_cpu_runtime.py:91-108.  They take
+ * the same arguments in the same order with the same meaning, plus a trailing
+ * stream, and return a status instead of void.  Section 2 lists the engine's
+ * own fused entry points.
+ */
+#ifndef GSDLQ_H_
+#define GSDLQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status and device flags ------------------------------------------------------- */
+#define GSDLQ_OK 0
+#define GSDLQ_ERR_INVALID (-1)     /* bad argument (shape, pointer, range) */
+#define GSDLQ_ERR_CUDA (-2)        /* a CUDA runtime call failed; see gsdlq_last_cuda_error */
+#define GSDLQ_ERR_UNSUPPORTED (-3) /* valid but not supported by this build */
+
+#define GSDLQ_FLAG_BAD_CODE 0x1u   /* a code index >= n_pts was decoded as 0 */
+#define GSDLQ_FLAG_BAD_KINK 0x2u   /* a kink column >= cols was skipped */
+#define GSDLQ_FLAG_BAD_POS 0x4u    /* pos >= max_seq: KV store / attention skipped */
+#define GSDLQ_FLAG_BAD_TABLE 0x8u  /* xy_table entry is not an A2 lattice point */
+#define GSDLQ_FLAG_TIMEOUT 0x10u   /* a bounded device-side wait gave up */
+#define GSDLQ_FLAG_BAD_TOKEN 0x20u /* token id >= vocab: embedding row skipped */
+
+typedef void *gsdlq_stream_t;
+
+/* Human-readable name of a status code (static string). */
+const char *gsdlq_status_string(int status);
+/* The last cudaError_t seen by the library on this thread (0 if none). */
+int gsdlq_last_cuda_error(void);
+/* Copy the device flag word to *flags (host pointer), clear it, synchronise `stream`. */
+int gsdlq_device_flags(unsigned int *flags, gsdlq_stream_t stream);
+/* Library version string, e.g. "0.1.0 sm_100a". */
+const char *gsdlq_version(void);
+
+/* ---- 1. drop-in replacements for the reference C engine ------------------------------ */
+
+/* out = x * (1/sqrt(mean(x^2) + eps)) * weight.
+ * Replaces gsd_cpu_rmsnorm, gsd_lq_cpu_engine.c:67-82. */
+int gsdlq_rmsnorm(const float *x, const float *weight, float *out, int dim, float eps,
+                  gsdlq_stream_t stream);
+
+/* y = a + b (y may alias a or b).  Replaces gsd_cpu_vec_add, gsd_lq_cpu_engine.c:85-94. */
+int gsdlq_vec_add(float *y, const float *a, const float *b, int dim, gsdlq_stream_t stream);
+
+/* out = silu(gate) * up (out may alias gate).  Replaces gsd_cpu_swiglu,
+ * gsd_lq_cpu_engine.c:97-108. */
+int gsdlq_swiglu(const float *gate, const float *up, float *out, int dim, gsdlq_stream_t stream);
+
+/* tmp_k[j] = S[j] * sum_c x[c] * f16(Vt[j*cols + c]), j < k_dim <= 16.
+ * Replaces gsd_cpu_lowrank_proj, gsd_lq_cpu_engine.c:111-127. */
+int gsdlq_lowrank_proj(const float *x, const uint16_t *Vt, const float *S, float *tmp_k, int k_dim,
+                       int cols, gsdlq_stream_t stream);
+
+/* y[r] = sum_p (xy[c].x*x[2p] + xy[c].y*x[2p+1]) * f16(scales[(r*cols)/64 + p/32])
+ *        + sum_{kinks of r} delta*x[col] + sum_j f16(U[r*k+j]) * tmp_k[j],
+ * with c = codes[(r*cols)/2 + p].  cols % 64 == 0, k_dim <= 16, n_pts <= 256 and
+ * xy_table an A2 lattice table (the reference's _get_turbo_codebook).
+ * Replaces gsd_cpu_hex2d_matvec, gsd_lq_cpu_engine.c:130-183
+ * (OpenCL twin: gsd_hex2d_matvec_fused, run_gpu_native_chat.py:196-267). */
+int gsdlq_hex2d_matvec(const float *x, const uint8_t *codes, const uint16_t *scales,
+                       const float *xy_table, const uint16_t *U, const float *tmp_k,
+                       const uint32_t *kink_row_ptr, const uint16_t *kink_cols,
+                       const float *kink_deltas, float *y, int rows, int cols, int k_dim,
+                       int n_pts, gsdlq_stream_t stream);
+
+/* RoPE on q (in place) and k; k (rotated) and v stored as fp16 at position pos of
+ * a cache laid out [layer][max_seq_len][n_kv_heads][head_dim].  interleaved=1
+ * rotates pairs (2i, 2i+1), 0 rotates (i, i + head_dim/2).  The rotation angles
+ * are computed on the host with the reference's formula, so the result is
+ * bit-identical to the reference given identical inputs.
+ * Replaces gsd_cpu_rope_and_store_kv, gsd_lq_cpu_engine.c:186-262. */
+int gsdlq_rope_and_store_kv(float *q, const float *k, const float *v, uint16_t *k_cache,
+                            uint16_t *v_cache, int layer_idx, int pos, int n_heads, int n_kv_heads,
+                            int head_dim, int max_seq_len, float rope_theta, int interleaved,
+                            gsdlq_stream_t stream);
+
+/* Decode attention for one query per head over positions 0..pos of the fp16
+ * cache above; kv head = h / (n_heads / n_kv_heads).
+ * Replaces gsd_cpu_gqa_attention, gsd_lq_cpu_engine.c:265-330. */
+int gsdlq_gqa_attention(const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                        float *attn_out, int layer_idx, int pos, int n_heads, int n_kv_heads,
+                        int head_dim, int max_seq_len, float sm_scale, gsdlq_stream_t stream);
+
+/* ---- 2. engine entry points ----------------------------------------------------------- */
+
+/* HOST function.  A2 lattice table of `radius` into xy_out (2*max_pts floats,
+ * host memory), bit-identical to _get_turbo_codebook (gsd_lq_cpu_runtime.py:111-118).
+ * Returns n_pts (127 for radius 6, 217 for radius 8), or GSDLQ_ERR_INVALID. */
+int gsdlq_codebook(int radius, float *xy_out, int max_pts);
+
+/* W[r,c] = xy[code][c&1] * f16->f32(scale): the dequantised weight as the
+ * reference's NumPy path defines it (gsd_lq_cpu_runtime.py:281-284), bit-exact. */
+int gsdlq_dequant(const uint8_t *codes, const uint16_t *scales, const float *xy_table, float *w,
+                  int rows, int cols, int n_pts, gsdlq_stream_t stream);
+
+/* Greedy pick over n logits with the reference's nan_to_num + first-maximum rule
+ * (gsd_lq_cpu_runtime.py:422-425).  *out_index (device int) receives the index. */
+int gsdlq_argmax(const float *logits, int n, int *out_index, gsdlq_stream_t stream);
+
+/* Packer: lattice codes, fp16 group scales and the fp32 residual W - dequant of a
+ * row-major fp32 [rows, cols] matrix.  Bit-identical to the NumPy packer
+ * (gsdlq_b200.packer.quantize_lattice).  No reference counterpart: the
+ * reference ships no packer. */
+int gsdlq_pack_lattice(const float *w, int rows, int cols, int radius, uint8_t *codes,
+                       uint16_t *scales, float *residual, gsdlq_stream_t stream);
+
+/* One packed linear (reference layout, device pointers). */
+typedef struct gsdlq_hexmat {
+  const uint8_t *codes;       /* [rows*cols/2]                          */
+  const uint16_t *scales;     /* [rows*cols/64] fp16                    */
+  const uint16_t *U;          /* [rows*k_dim] fp16 (unused if k_dim==0) */
+  const float *S;             /* [k_dim]                                */
+  const uint16_t *Vt;         /* [k_dim*cols] fp16                      */
+  const uint32_t *row_ptr;    /* [rows+1] CSR kink offsets              */
+  const uint16_t *kink_cols;  /* [nnz]                                  */
+  const float *kink_deltas;   /* [nnz]                                  */
+  int rows, cols, k_dim, radius;
+} gsdlq_hexmat_t;
+
+#define GSDLQ_EPI_STORE 0   /* y[m][r] = W_m x                                            */
+#define GSDLQ_EPI_RESID 1   /* y[0][r] = resid[r] + W_0 x   (y may alias resid)              */
+#define GSDLQ_EPI_SWIGLU 2  /* y[0][r] = silu(W_0 x) * (W_1 x)   (pair of equal-shape mats)  */
+#define GSDLQ_EPI_ROPE_KV 3 /* mats = Q, K, V: y[0] = RoPE(Qx); RoPE(Kx), Vx -> fp16 KV cache */
+
+#define GSDLQ_IN_PLAIN 0    /* input = x                                                  */
+#define GSDLQ_IN_RMSNORM 1  /* input = rmsnorm(x) * norm_w                                */
+#define GSDLQ_IN_EMBED 2    /* input = rmsnorm(f32(embed[*token])) * norm_w; CTA 0 writes the
+                               raw row to x_out (the residual stream)                      */
+
+#define GSDLQ_LINEAR_WS_WORDS 64 /* workspace words per fused-linear call site */
+
+/* A fused packed-linear launch: up to three matrices that share one input,
+ * the low-rank projection computed inside the same kernel, and an epilogue. */
+typedef struct gsdlq_linear_job {
+  gsdlq_hexmat_t mat[3];
+  int n_mat;
+  int input_mode;             /* GSDLQ_IN_*                                   */
+  const float *x;             /* [cols] (PLAIN, RMSNORM)                      */
+  const float *norm_w;        /* [cols] (RMSNORM, EMBED)                      */
+  float eps;
+  const uint16_t *embed;      /* [vocab, cols] fp16 (EMBED)                   */
+  const int *token;           /* device token id (EMBED)                      */
+  int vocab;
+  float *x_out;               /* EMBED: receives the f32 embedding row        */
+  int epilogue;               /* GSDLQ_EPI_*                                  */
+  float *y[3];
+  const float *resid;         /* RESID                                        */
+  /* ROPE_KV */
+  uint16_t *k_cache, *v_cache; /* [layers][max_seq][n_kv][head_dim] fp16       */
+  const int *pos;             /* device position                              */
+  const float *rope_cs;       /* [max_seq][head_dim/2] (cos, sin) pairs        */
+  int layer, max_seq, head_dim, interleaved;
+  /* optional fused greedy argmax of y[0] (EPI_STORE): atomicMax of a 64-bit
+   * (value, ~index) key; the key must start at 0 */
+  unsigned long long *argmax_key;
+  unsigned int *workspace;    /* GSDLQ_LINEAR_WS_WORDS words, zero before first use;
+                                 each launch leaves it zero again */
+} gsdlq_linear_job_t;
+
+/* Launch a fused packed linear.  `job` is a HOST pointer (read during the call). */
+int gsdlq_linear(const gsdlq_linear_job_t *job, gsdlq_stream_t stream);
+
+/* Split-KV decode attention.  q is already rotated.  pos is read from *pos_dev
+ * when non-NULL (CUDA-graph friendly), else pos_val.  The cache layout is the
+ * reference's [layer][max_seq][n_kv][head_dim] fp16 when block_table is NULL,
+ * else a paged pool [page][page_size][n_kv][head_dim] with block_table[t/page_size]
+ * giving the page of position t.  partial/workspace: see gsdlq_attention_ws_size. */
+typedef struct gsdlq_attn_job {
+  const float *q;
+  const uint16_t *k_cache, *v_cache;
+  float *out;
+  const int *pos_dev;
+  int pos_val;
+  int layer, n_heads, n_kv_heads, head_dim, max_seq;
+  float sm_scale;
+  const int *block_table;
+  int page_size;
+  float *partial;
+  unsigned int *workspace;
+} gsdlq_attn_job_t;
+
+/* Bytes of `partial` (floats) and `workspace` (uints) a gsdlq_attention call needs. */
+int gsdlq_attention_ws_size(int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                            size_t *partial_bytes, size_t *workspace_bytes);
+int gsdlq_attention(const gsdlq_attn_job_t *job, gsdlq_stream_t stream);
+
+/* Device-side greedy bookkeeping after a step whose LM head fed *argmax_key:
+ * *token = argmax index, out_ids[*step] = token (when out_ids != NULL and
+ * *step < max_out), *step += 1, *pos += 1, *argmax_key = 0.  One thread; lets a
+ * captured decode step be replayed back to back without host round trips. */
+int gsdlq_greedy_advance(unsigned long long *argmax_key, int *token, int *pos, int *step, int *out_ids,
+                         int max_out, gsdlq_stream_t stream);
+
+/* HOST function: (cos, sin) of the RoPE angles for positions [0, max_seq) into
+ * table (host, max_seq*head_dim floats), computed with the reference's formula
+ * (gsd_lq_cpu_engine.c:215-218) so that rotations match it bit for bit. */
+int gsdlq_rope_table(float *table, int max_seq, int head_dim, float rope_theta);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GSDLQ_H_ */

@@ -1,0 +1,88 @@
+"""Generate the golden fixtures in this directory from the REFERENCE implementation.
+
+Run in a container that holds the reference tree (default location taken from
+$GSDLQ_REFERENCE, else the standard mount); the fixtures are committed so the
+tests never need the reference at run time:
+
+    python tests/golden/make_golden.py
+
+What it records (all produced by the reference's own code):
+  codebook.npz     _get_turbo_codebook(6|8) from both reference copies
+                   (gsd_lq_cpu_runtime.py:111-118, run_gpu_native_chat.py:26-33)
+  tiny.gsd2        a small random-init model written by our packer
+  tiny_ref.npz     for tiny.gsd2, loaded by the reference's CPUMistralV2Model with its
+                   C engine (built from the reference source into oracle/_ref):
+                     - logits of forward_token over a fixed token sequence (with greedy picks)
+                     - _matvec_cpu(x, layer0.q) and (k_dim = 0 path) _matvec_cpu(x, layer0.k of a turbo file)
+                     - the NumPy-fallback dequantised weight W of layer0.q (the W definition)
+                       and its fallback matvec
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+REF = os.environ.get("GSDLQ_REFERENCE", "/root/reference")
+TOKENS = [1, 17, 300, 42, 255, 7, 299, 100]
+
+
+def main():
+    import gsdlq_b200.packer as P
+    import gsdlq_b200.gsd2 as G
+    import oracle as O  # only to locate/build the reference .so
+
+    O.build()
+    sys.path.insert(0, os.path.join(REF, "gsd_lq_v2"))
+    import gsd_lq_cpu_runtime as R
+    import run_gpu_native_chat as RG
+
+    np.savez(os.path.join(HERE, "codebook.npz"),
+             cpu6=R._get_turbo_codebook(6)[0], cpu8=R._get_turbo_codebook(8)[0],
+             gpu6=RG._get_turbo_codebook(6)[0], gpu8=RG._get_turbo_codebook(8)[0])
+
+    cfg = P.make_config("tiny", n_layers=2, hidden_size=128, n_heads=4, n_kv_heads=2, head_dim=32,
+                        ffn_size=256, vocab_size=320)
+    for mode in ("precision", "turbo"):
+        m = P.random_model(cfg, mode, seed=7, norm_jitter=0.1)
+        path = os.path.join(HERE, f"tiny_{mode}.gsd2")
+        G.write_gsd2(path, m)
+
+        R.LIB_PATH = O.REF_LIB  # use the reference engine built from its own source
+        ref = R.CPUMistralV2Model(path, rope_interleaved=1)
+        assert ref.cpu.lib is not None, "reference C engine did not load"
+        logits, picks = [], []
+        for pos, tok in enumerate(TOKENS):
+            lg = ref.forward_token(tok, pos, return_logits=True)
+            logits.append(lg)
+            picks.append(ref.sample_token(lg, temperature=0.0))
+        rng = np.random.default_rng(3)
+        x = rng.standard_normal(cfg["hidden_size"]).astype(np.float16).astype(np.float32)
+        outs = {}
+        for key in ("q", "k", "gate"):
+            y = np.zeros(ref.layers[0][key]["rows"], np.float32)
+            ref._matvec_cpu(x, ref.layers[0][key], y)
+            outs["mv_" + key] = y
+        # the NumPy fallback path (cpu.lib = None) defines the dequantised weight
+        lib = ref.cpu.lib
+        ref.cpu.lib = None
+        lyr = ref.layers[0]["q"]
+        scales_f32 = lyr["scales"].view(np.float16).astype(np.float32)
+        pts = lyr["xy_table"][lyr["codes"]].reshape(lyr["rows"], lyr["cols"])
+        W = pts * np.repeat(scales_f32.reshape(lyr["rows"], lyr["cols"] // 64), 64, axis=1)
+        y_fb = np.zeros(lyr["rows"], np.float32)
+        ref._matvec_cpu(x, lyr, y_fb)
+        ref.cpu.lib = lib
+        np.savez(os.path.join(HERE, f"tiny_{mode}_ref.npz"), tokens=np.array(TOKENS), logits=np.stack(logits),
+                 picks=np.array(picks), x=x, W_q=W, mv_q_fallback=y_fb, **outs)
+        print(mode, "picks", picks)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,204 @@
+"""Codebook, .gsd2 reader/writer, packer invariants, format fault injection (CPU)."""
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+import gsdlq_b200.codebook as cb
+import gsdlq_b200.gsd2 as G
+import gsdlq_b200.packer as P
+
+
+@pytest.mark.parametrize("radius,n", [(6, 127), (8, 217)])
+def test_codebook_bitexact_vs_reference_golden(radius, n, oracle_mod):
+    g = np.load(os.path.join(GOLDEN, "codebook.npz"))
+    t = cb.xy_table(radius)
+    assert t.shape == (n, 2) and cb.num_points(radius) == n
+    assert np.array_equal(t, g[f"cpu{radius}"]) and np.array_equal(t, g[f"gpu{radius}"])
+    assert np.array_equal(oracle_mod.codebook(radius)[0], t)
+    rr = cb.lattice_coords(radius).astype(np.float64)
+    assert np.array_equal((rr[:, 0] + 0.5 * rr[:, 1]).astype(np.float32), t[:, 0])
+    assert np.array_equal((rr[:, 1] * (np.sqrt(3.0) / 2.0)).astype(np.float32), t[:, 1])
+
+
+def test_codebook_c_restatement(restated):
+    import ctypes
+    for r in (6, 8):
+        buf = np.zeros(2 * 256, np.float32)
+        n = restated.lib.orc_codebook(r, buf.ctypes.data_as(ctypes.c_void_p), 256)
+        assert np.array_equal(buf[:2 * n].reshape(n, 2), cb.xy_table(r))
+
+
+def test_reader_matches_oracle_reader(oracle_mod):
+    path = os.path.join(GOLDEN, "tiny_precision.gsd2")
+    m = G.read_gsd2(path)
+    o = oracle_mod.read_gsd2(path)
+    assert m.config["n_layers"] == o["cfg"]["n_layers"]
+    t = m.hex["blk.1.ffn_down.weight"]
+    r = o["layers"][1]["down"]
+    for k in ("codes", "scales", "row_ptr", "kink_cols", "kink_deltas", "U", "S", "Vt"):
+        assert np.array_equal(getattr(t, k), r[k]), k
+    assert np.array_equal(m.dense["token_embd.weight"].astype(np.float32), o["embed"])
+
+
+def test_roundtrip(tmp_path):
+    cfg = P.make_config("tiny", n_layers=1, hidden_size=128, n_heads=2, n_kv_heads=1, head_dim=64,
+                        ffn_size=192, vocab_size=64)
+    m = P.random_model(cfg, "precision", seed=3)
+    p = str(tmp_path / "m.gsd2")
+    G.write_gsd2(p, m)
+    r = G.read_gsd2(p)
+    for n, t in m.hex.items():
+        for k, a in t.blobs().items():
+            assert np.array_equal(a, getattr(r.hex[n], k)), (n, k)
+    # every blob starts on a 256-byte boundary of the file
+    with open(p, "rb") as f:
+        f.read(4)
+        hlen = struct.unpack("<Q", f.read(8))[0]
+        hdr = json.loads(f.read(hlen))
+    assert (12 + hlen) % 256 == 0
+    for meta in hdr["tensors"].values():
+        for v in meta.values():
+            if isinstance(v, dict) and "offset" in v:
+                assert v["offset"] % 256 == 0
+
+
+def test_packer_invariants_and_determinism():
+    rng = np.random.default_rng(0)
+    w = (rng.standard_normal((48, 256)) * 0.02).astype(np.float32)
+    a = P.pack_matrix(w, "precision")
+    b = P.pack_matrix(w, "precision")
+    for k in ("codes", "scales", "row_ptr", "kink_cols", "kink_deltas"):
+        assert np.array_equal(getattr(a, k), getattr(b, k))
+    assert a.k_dim == 16 and a.nnz == 48 * 4
+    assert np.all(np.diff(a.kink_cols.reshape(48, 4).astype(int), axis=1) > 0)
+    # reconstruction error of the lattice part is bounded by the scale (hexagon cell radius 1/sqrt3)
+    W = P.dequant(a.codes, a.scales, a.radius, 48, 256)
+    s = np.repeat(a.scales.view(np.float16).astype(np.float32).reshape(48, 4), 64, axis=1)
+    err = np.hypot(*(w - W).reshape(-1, 2).T)
+    assert np.all(err <= s.reshape(-1, 2)[:, 0] * (1 / np.sqrt(3) + 1e-3))
+    t = P.pack_matrix(w, "turbo")
+    assert t.k_dim == 0 and t.nnz == 0 and t.U is None
+    assert abs(G.compute_avg_bpw({"x": t}) - (4.25 + 32 * 49 / (48 * 256))) < 1e-6
+
+
+def test_packer_nearest_point_is_exact():
+    """Every code is a nearest hexagon point of (w0, w1)/scale (brute force over the table)."""
+    rng = np.random.default_rng(1)
+    w = (rng.standard_normal((8, 128)) * 0.02).astype(np.float32)
+    for radius in (6, 8):
+        codes, sb = P.quantize_lattice(w, radius)
+        s = np.repeat(sb.view(np.float16).astype(np.float32).reshape(8, 2), 32, axis=1).reshape(-1)
+        pr = w.reshape(-1, 2) / s[:, None]
+        t = cb.xy_table(radius)
+        d = ((pr[:, None, :] - t[None]) ** 2).sum(-1)
+        best = d.min(1)
+        assert np.allclose(d[np.arange(len(codes)), codes], best, rtol=0, atol=1e-5)
+
+
+# ---- fault injection: malformed files are rejected on the host -------------------------
+def _tiny_file(tmp_path):
+    cfg = P.make_config("tiny", n_layers=1, hidden_size=64, n_heads=1, n_kv_heads=1, head_dim=64,
+                        ffn_size=128, vocab_size=32)
+    m = P.random_model(cfg, "turbo", seed=5)
+    p = str(tmp_path / "t.gsd2")
+    G.write_gsd2(p, m)
+    return p
+
+
+def _rewrite_header(p, fn):
+    raw = open(p, "rb").read()
+    hlen = struct.unpack("<Q", raw[4:12])[0]
+    hdr = json.loads(raw[12:12 + hlen])
+    fn(hdr)
+    hb = json.dumps(hdr).encode()
+    hb += b" " * (hlen - len(hb)) if len(hb) <= hlen else b""
+    assert len(hb) == hlen
+    open(p, "wb").write(raw[:12] + hb + raw[12 + hlen:])
+
+
+def test_bad_magic(tmp_path):
+    p = _tiny_file(tmp_path)
+    raw = bytearray(open(p, "rb").read())
+    raw[:4] = b"GSD1"
+    open(p, "wb").write(bytes(raw))
+    with pytest.raises(G.FormatError, match="magic"):
+        G.read_gsd2(p)
+
+
+def test_truncated_file(tmp_path):
+    p = _tiny_file(tmp_path)
+    raw = open(p, "rb").read()
+    open(p, "wb").write(raw[:len(raw) - 1000])
+    with pytest.raises(G.FormatError, match="past the end"):
+        G.read_gsd2(p)
+
+
+def test_header_length_overflow(tmp_path):
+    p = _tiny_file(tmp_path)
+    raw = bytearray(open(p, "rb").read())
+    raw[4:12] = struct.pack("<Q", 1 << 40)
+    open(p, "wb").write(bytes(raw))
+    with pytest.raises(G.FormatError, match="exceeds"):
+        G.read_gsd2(p)
+
+
+def test_out_of_range_code_rejected(tmp_path):
+    p = _tiny_file(tmp_path)
+    m = G.read_gsd2(p)
+    raw = bytearray(open(p, "rb").read())
+    hlen = struct.unpack("<Q", raw[4:12])[0]
+    hdr = json.loads(raw[12:12 + hlen])
+    off = 12 + hlen + hdr["tensors"]["blk.0.attn_q.weight"]["codes"]["offset"]
+    raw[off + 5] = 250  # >= 217 points of radius 8
+    open(p, "wb").write(bytes(raw))
+    with pytest.raises(G.FormatError, match="code index"):
+        G.read_gsd2(p)
+    assert m is not None
+
+
+@pytest.mark.parametrize("mutate,msg", [
+    (lambda h: h["tensors"]["blk.0.attn_q.weight"].__setitem__("k_dim", 17), "k_dim"),
+    (lambda h: h["tensors"]["blk.0.attn_q.weight"].__setitem__("radius", 7), "radius"),
+    (lambda h: h["tensors"]["blk.0.attn_q.weight"].__setitem__("cols", 96), "multiple of 64"),
+    (lambda h: h["config"].__setitem__("n_kv_heads", 3), "multiple of n_kv_heads"),
+    (lambda h: h["tensors"].pop("blk.0.ffn_up.weight"), "missing tensor"),
+])
+def test_header_violations(tmp_path, mutate, msg):
+    p = _tiny_file(tmp_path)
+    _rewrite_header(p, mutate)
+    with pytest.raises(G.FormatError, match=msg):
+        G.read_gsd2(p)
+
+
+def test_kink_invariants():
+    t = P.pack_matrix((np.random.default_rng(2).standard_normal((16, 128)) * 0.02).astype(np.float32),
+                      "precision")
+    bad = G.HexTensor(**{**t.__dict__, "row_ptr": t.row_ptr[::-1].copy()})
+    with pytest.raises(G.FormatError, match="row_ptr"):
+        bad.validate()
+    kc = t.kink_cols.copy()
+    kc[0] = 200
+    with pytest.raises(G.FormatError, match="kink column"):
+        G.HexTensor(**{**t.__dict__, "kink_cols": kc}).validate()
+
+
+def test_shard_slices_sum_to_whole():
+    """Row shards concatenate and column shards sum (oracle numerics) to the unsharded matvec."""
+    import oracle
+    eng = oracle.CEngine.restatement()
+    rng = np.random.default_rng(9)
+    w = (rng.standard_normal((64, 256)) * 0.02).astype(np.float32)
+    t = P.pack_matrix(w, "precision")
+    x = rng.standard_normal(256).astype(np.float32)
+    tabs = {r: oracle.codebook(r) for r in (6, 8)}
+    rec = lambda h: oracle.hex_record({"radius": h.radius, "k_dim": h.k_dim, "rows": h.rows, "cols": h.cols},  # noqa
+                                      {k: v.tobytes() for k, v in h.blobs().items()}, tabs)
+    full = eng.matvec(x, rec(t))
+    rows = np.concatenate([eng.matvec(x, rec(t.row_slice(a, a + 16))) for a in range(0, 64, 16)])
+    assert np.array_equal(rows, full)
+    cols = sum(eng.matvec(x[a:a + 128], rec(t.col_slice(a, a + 128))) for a in (0, 128))
+    assert np.allclose(cols, full, rtol=1e-5, atol=1e-6)
