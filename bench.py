@@ -1,0 +1,418 @@
+"""Benchmark: batch-1 greedy decode of a Mistral-7B-v0.3-shape decoder packed in
+GSD-LQ Precision mode (random-init N(0, 0.02^2) weights, synthetic token ids).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one decode token (all 32 layers + LM head + greedy pick) at positions
+after a 1536-token prompt; positions wrap back to 1536 when the 2048-entry KV cache
+is full.  The timed region holds K steps, replayed as CUDA graphs with the token fed
+back on the device, bracketed by a barrier and device synchronisation; the device
+time is the max over ranks.  One JSON line is printed by rank 0.
+
+N > 1 runs tensor parallelism (strong scaling: the same single sequence, the packed
+linears sharded across ranks, NCCL all-reduce after the O and down projections).
+
+--impl reference times the reference's own C engine (oracle/_ref, built from the
+reference source with the reference's flags) on the host cores, on the same packed
+bytes; each of its steps is one bounded unit of a token (one decoder layer, or the
+final norm + LM head), and its tok/s is 1 / (sum of the units' mean times).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s batch1 Mistral-7B-shape Precision; unpack-matvec HBM GB/s % peak"
+PUBLISHED_TOKS = 6.5  # Mistral-7B Precision decode, AMD RX 5600 XT (README.md:32)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=512)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", default="mistral-7b")
+    ap.add_argument("--mode", default="precision", choices=["precision", "turbo"])
+    ap.add_argument("--prompt", type=int, default=1536)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="override n_layers (debug only; not a bench number)")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev_index: int):
+        self.dev, self.proc, self.out = dev_index, None, None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.dev)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def init_dist(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def build_model(args, world, rank, device):
+    import gsdlq_b200.packer as P
+    cfg = P.make_config(args.model, **({"n_layers": args.layers} if args.layers else {}))
+    t0 = time.time()
+    dm = P.random_model_cuda(cfg, args.mode, seed=args.seed, device=device)
+    return cfg, dm, time.time() - t0
+
+
+def time_region(fn, steps, world):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    fn(steps)
+    e.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    ms = s.elapsed_time(e)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def cpu_reference_sample(host_model, kv=None, pos=1536, layers_only=False):
+    """Time the reference C engine (oracle/_ref) on one decode token on the host cores."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle
+    eng = oracle.CEngine.reference()
+    kind = "reference"
+    if eng is None:
+        eng = oracle.CEngine.restatement()
+        kind = "port"
+    om = oracle_model(host_model, eng)
+    if kv is not None:
+        om.k_cache[...] = kv[0]
+        om.v_cache[...] = kv[1]
+    units = unit_times(om, pos, reps=1)
+    tok_s = 1.0 / sum(units)
+    return {"value": tok_s, "unit": "tok/s", "cores": os.cpu_count(), "kind": kind,
+            "sample": f"1 decode token at pos {pos} (32 layers + final norm + LM head) through the reference C engine "
+                      f"(OMP threads={os.environ.get('OMP_NUM_THREADS', os.cpu_count())})"}
+
+
+def oracle_model(host, eng, max_seq=2048):
+    import numpy as np
+    import oracle
+    tabs = {r: oracle.codebook(r) for r in (6, 8)}
+
+    def rec(t):
+        return oracle.hex_record({"radius": t.radius, "k_dim": t.k_dim, "rows": t.rows, "cols": t.cols},
+                                 {k: memoryview(np.ascontiguousarray(v)).cast("B") for k, v in t.blobs().items()},
+                                 tabs)
+    m = {"cfg": host.config, "embed": host.dense["token_embd.weight"].astype(np.float32),
+         "final_norm": host.dense["output_norm.weight"], "layers": []}
+    for l in range(host.config["n_layers"]):
+        lyr = {"attn_norm": host.dense[f"blk.{l}.attn_norm.weight"],
+               "ffn_norm": host.dense[f"blk.{l}.ffn_norm.weight"]}
+        for n, k in zip(oracle.LINEARS, oracle.KEYS):
+            lyr[k] = rec(host.hex[f"blk.{l}.{n}.weight"])
+        m["layers"].append(lyr)
+    m["lm_head"] = rec(host.hex["output.weight"])
+    return oracle.OracleModel(m, eng, max_seq=max_seq)
+
+
+def unit_times(om, pos, reps=1):
+    """Per-unit (each layer, then the head) seconds of one decode token through the C engine."""
+    import numpy as np
+    import oracle
+    om.x[:] = om.m["embed"][7]
+    ts = []
+    for l in range(om.n_layers):
+        t = time.perf_counter()
+        om.layer(l, pos)
+        ts.append(time.perf_counter() - t)
+    t = time.perf_counter()
+    xb = om.xb[:om.hidden]
+    om.e.rmsnorm(oracle._p(om.x), oracle._p(om.m["final_norm"]), oracle._p(xb), om.hidden, om.eps)
+    om._mv(xb, om.m["lm_head"], om.logits)
+    oracle.argmax(om.logits)
+    ts.append(time.perf_counter() - t)
+    return ts
+
+
+# ----------------------------------------------------------------------------------------------
+def run_ours(args):
+    import numpy as np
+    import torch
+    world, rank, local = init_dist(args)
+    device = torch.device("cuda", local)
+    from gsdlq_b200.model import GSDLQModel
+    from gsdlq_b200 import ops, _lib as L
+    tp = None
+    if world > 1:
+        from gsdlq_b200.tp import TensorParallel
+        tp = TensorParallel(rank, world)
+    cfg, dm, pack_s = build_model(args, world, rank, device)
+    model = GSDLQModel(dm, device=device, tp=tp)
+    host_model = None
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        import gsdlq_b200.packer as P
+        host_model = P.device_model_to_host(dm)
+    del dm
+    V, P0 = cfg["vocab_size"], args.prompt
+    rng = np.random.default_rng(args.seed + 1)
+    prompt = rng.integers(0, V, P0).tolist()
+    t0 = time.time()
+    model.prefill(prompt[:-1])
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+    span = model.max_seq - (P0 - 1)
+
+    state = {"pos": P0 - 1}
+    model.set_state(prompt[-1], P0 - 1)
+
+    def steps(n):
+        for _ in range(n):
+            if state["pos"] >= model.max_seq:
+                state["pos"] = P0 - 1
+                model.state[1:2].fill_(P0 - 1)  # device-side position reset (wrap), stream-ordered
+            model.step(with_head=True)
+            state["pos"] += 1
+
+    steps(args.warmup)
+    sampler = ClockSampler(local)
+    sampler.start()
+    ms = time_region(steps, args.steps, world)
+    clocks = sampler.stop()
+    flags = L.device_flags()
+    if flags:
+        raise RuntimeError(f"device flags raised during the bench: {L.flag_names(flags)}")
+    tok_s = args.steps / (ms / 1e3)
+    ms_step = ms / args.steps
+    mean_pos = P0 + span / 2
+    bytes_tok = model.packed_bytes_per_token(pos=int(mean_pos))
+    pk, pk_src = peaks()
+    hbm = float(pk["hbm_gbs"])
+
+    # dominant kernel: the fused gate/up linear (RMSNorm prologue, SwiGLU epilogue), one launch per layer,
+    # timed over all layers back to back (distinct weights: 2 GB >> L2) with CUDA events on the launch stream
+    gu_jobs = [lj[3] for lj in model.layer_jobs]
+    rep = 5
+
+    def gu(n):
+        for _ in range(n):
+            for j in gu_jobs:
+                ops.linear(j)
+    gu(1)
+    gu_ms = time_region(gu, rep, world) / (rep * len(gu_jobs))
+    lay0 = "blk.0."
+    gu_bytes = (model.hex[lay0 + "ffn_gate.weight"].nbytes() + model.hex[lay0 + "ffn_up.weight"].nbytes()
+                + model.hidden * 8 + model.ffn_local * 4)
+    gu_gbs = gu_bytes / (gu_ms / 1e3) / 1e9
+
+    e2e = None
+    if rank == 0 and world == 1 and args.e2e_steps > 0:
+        n = min(args.e2e_steps, model.max_seq - P0)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        tok = prompt[-1]
+        model.forward_token(tok, P0 - 1)
+        s.record()
+        for i in range(n):
+            lg = model.forward_token(tok, P0 + i)   # H2D (token, pos, step) + D2H logits each step
+            tok = int(np.argmax(lg))
+        e.record()
+        torch.cuda.synchronize()
+        e_ms = s.elapsed_time(e) / n
+        e2e = {"value": 1e3 / e_ms, "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4 * V,
+               "api": "GSDLQModel.forward_token(token_id, pos) -> np.float32[vocab]"}
+    elif world > 1:
+        e2e = None
+
+    cpu = None
+    if host_model is not None:
+        kv = (model.k_cache.cpu().numpy().view(np.uint16), model.v_cache.cpu().numpy().view(np.uint16))
+        cpu = cpu_reference_sample(host_model, kv=kv, pos=P0)
+
+    launches_per_step = 5 * model.n_layers + 2 + (2 * model.n_layers + 1 if world > 1 else 0)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": tok_s / PUBLISHED_TOKS, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"{args.model}-shape {args.mode} greedy decode, batch 1, positions "
+                                   f"{P0}..{model.max_seq - 1} (wrapping), random-init N(0,0.02^2) packed on the GPU",
+                       "model": args.model, "mode": args.mode, "prompt": P0, "global_batch": 1,
+                       "parallelism": f"tp{world}", "avg_bpw": round(model.avg_bpw, 4),
+                       "l2": "inputs larger than L2: every step streams all packed weights "
+                             f"({bytes_tok / 1e9:.2f} GB)",
+                       "n_layers": model.n_layers},
+            "token_bytes": bytes_tok, "token_gbs": bytes_tok / (ms_step / 1e3) / 1e9,
+            "token_hbm_frac": bytes_tok / (ms_step / 1e3) / 1e9 / hbm,
+            "roofline": {"bound": "hbm", "kernel": "hexmv_kernel<SWIGLU> (fused gate/up linear)",
+                         "achieved": gu_gbs, "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm,
+                         "peak_source": f"{pk_src} hbm_gbs", "bytes_per_launch": gu_bytes,
+                         "launch_ms": gu_ms, "traffic": None},
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks, "pack_s": round(pack_s, 2), "prefill_s": round(prefill_s, 2),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        model.release()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    import numpy as np
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    torch.cuda.set_device(0)
+    import gsdlq_b200.packer as P
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    eng = oracle.CEngine.reference()
+    kind = "reference"
+    if eng is None:
+        eng, kind = oracle.CEngine.restatement(), "port"
+    cfg, dm, pack_s = build_model(args, 1, 0, torch.device("cuda", 0))
+    host = P.device_model_to_host(dm)   # the same packed bytes as the ours arm (same seed)
+    del dm
+    torch.cuda.empty_cache()
+    om = oracle_model(host, eng)
+    rng = np.random.default_rng(args.seed + 2)
+    P0 = args.prompt
+    # KV state at the prompt length: seeded N(0,1) fp16 (attention cost depends on length, not values)
+    for c in (om.k_cache, om.v_cache):
+        c[:, :P0] = rng.standard_normal(c[:, :P0].shape, dtype=np.float32).astype(np.float16).view(np.uint16)
+    om.x[:] = om.m["embed"][7]
+    n_units = om.n_layers + 1
+    times: dict[int, list] = {}
+
+    def unit(i):
+        u = i % n_units
+        pos = P0 + (i // n_units) % (om.max_seq - P0)
+        t = time.perf_counter()
+        if u < om.n_layers:
+            om.layer(u, pos)
+        else:
+            xb = om.xb[:om.hidden]
+            om.e.rmsnorm(oracle._p(om.x), oracle._p(om.m["final_norm"]), oracle._p(xb), om.hidden, om.eps)
+            om._mv(xb, om.m["lm_head"], om.logits)
+            oracle.argmax(om.logits)
+        return u, time.perf_counter() - t
+
+    for i in range(args.warmup):
+        unit(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        u, dt = unit(args.warmup + i)
+        times.setdefault(u, []).append(dt)
+    wall = time.perf_counter() - t0
+    layer_mean = statistics.mean([statistics.mean(v) for k, v in times.items() if k < om.n_layers] or [float("nan")])
+    head_mean = statistics.mean(times[om.n_layers]) if om.n_layers in times else None
+    if head_mean is None:
+        _, head_mean = unit(om.n_layers)  # measured once if K never reached the head unit
+    tok_time = sum(statistics.mean(times[u]) if u in times else layer_mean for u in range(om.n_layers)) + head_mean
+    tok_s = 1.0 / tok_time
+    sample = (f"each step = one unit of a decode token at pos >= {P0} (one of {om.n_layers} decoder layers, or final "
+              f"norm + LM head), rotating; tok/s = 1/sum(unit means); OMP threads = "
+              f"{os.environ.get('OMP_NUM_THREADS', os.cpu_count())}")
+    line = {"metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * wall / max(args.steps, 1), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": tok_s / PUBLISHED_TOKS, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"{args.model}-shape {args.mode} greedy decode, batch 1, positions >= {P0}",
+                       "model": args.model, "mode": args.mode, "prompt": P0, "global_batch": 1,
+                       "parallelism": "host cores"},
+            "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": os.cpu_count(), "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)

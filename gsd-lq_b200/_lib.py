@@ -36,7 +36,7 @@ class LinearJob(ctypes.Structure):
                 ("eps", f32), ("embed", vp), ("token", vp), ("vocab", i32), ("x_out", vp), ("epilogue", i32),
                 ("y", vp * 3), ("resid", vp), ("k_cache", vp), ("v_cache", vp), ("pos", vp), ("rope_cs", vp),
                 ("layer", i32), ("max_seq", i32), ("head_dim", i32), ("interleaved", i32),
-                ("argmax_key", vp), ("workspace", vp)]
+                ("argmax_key", vp), ("argmax_index_base", i32), ("workspace", vp)]
 
 
 class AttnJob(ctypes.Structure):

@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
     const bool need_lr = (P.tmp_k_ext == nullptr) && P.n_lowrank_jobs > 0;
     if (need_lr && s_flags[1] == 0) {
       if (tid == 0) {
-        wait_counter_geq(&ws[1], (unsigned)P.n_lowrank_jobs, 2000000000ull);
+        wait_counter_geq(&ws[1], (unsigned)P.n_lowrank_jobs, 1000000000ull);  // 1 s bound
         __threadfence();
       }
       __syncthreads();
@@ -389,7 +389,8 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
           const int row = r0 + k;
           if (row < M.rows) {
             J.y[m0][row] = vals[0][k];
-            if (J.argmax_key) atomicMax(J.argmax_key, argmax_key(vals[0][k], (uint32_t)row));
+            if (J.argmax_key)
+              atomicMax(J.argmax_key, argmax_key(vals[0][k], (uint32_t)(row + J.argmax_index_base)));
           }
         }
       } else if constexpr (EPI == GSDLQ_EPI_RESID) {
@@ -451,9 +452,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
   if (P.n_lowrank_jobs > 0 && tid == 0) {
     __threadfence();
     if (atomicAdd(&ws[2], 1u) == gridDim.x - 1) {
-      ws[0] = 0u;
-      ws[1] = 0u;
-      ws[2] = 0u;
+      for (int i = 0; i < GSDLQ_LINEAR_WS_WORDS; ++i) ws[i] = 0u;  // counters and published tmp_k
       __threadfence();
     }
   }
@@ -462,6 +461,8 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
 // ---- host side ------------------------------------------------------------------------
 static int hexmv_validate_mat(const gsdlq_hexmat_t& M, int cols) {
   if (!M.codes || !M.scales || !M.row_ptr) return GSDLQ_ERR_INVALID;
+  // codes are read 8 bytes at a time from row starts (cols/2 is a multiple of 32)
+  if (reinterpret_cast<uintptr_t>(M.codes) & 7u) return GSDLQ_ERR_INVALID;
   if (M.rows <= 0 || M.cols != cols || cols <= 0 || cols % 64 != 0) return GSDLQ_ERR_INVALID;
   if (M.k_dim < 0 || M.k_dim > 16) return GSDLQ_ERR_INVALID;
   if (M.k_dim > 0 && (!M.U || !M.S || !M.Vt)) return GSDLQ_ERR_INVALID;
@@ -469,18 +470,28 @@ static int hexmv_validate_mat(const gsdlq_hexmat_t& M, int cols) {
   return GSDLQ_OK;
 }
 
+// Resident CTAs per SM for a given dynamic smem size, from the hardware limits (no runtime
+// occupancy query on the launch path): 228 KB of shared memory per SM with 1 KB reserved per CTA,
+// 64K registers per SM at <= 128 registers per thread (ptxas reports 123-128 for hexmv_kernel).
+static int hexmv_ctas_per_sm(size_t smem) {
+  const size_t per_cta = smem + 1024;
+  int by_smem = (int)((228u * 1024u) / per_cta);
+  const int by_regs = 65536 / (HX_THREADS * 128);
+  return std::max(0, std::min(by_smem, by_regs));
+}
+
 template <int EPI>
 static int hexmv_launch_t(const HexmvParams& P, cudaStream_t s) {
   const size_t smem = hexmv_smem_bytes(P.cols);
-  static int configured_max = 0;
-  if ((int)smem > configured_max) {
-    cudaError_t e = cudaFuncSetAttribute(hexmv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static int configured_max[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if ((int)smem > configured_max[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(hexmv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return record_cuda_error(e);
-    configured_max = (int)smem;
+    configured_max[dev] = 227 * 1024;
   }
-  int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, hexmv_kernel<EPI>, HX_THREADS, smem);
-  if (e != cudaSuccess) return record_cuda_error(e);
+  const int per_sm = hexmv_ctas_per_sm(smem);
   if (per_sm < 1) return GSDLQ_ERR_UNSUPPORTED;
   const int grid = std::max(1, std::min(P.units, per_sm * num_sms()));
   hexmv_kernel<EPI><<<grid, HX_THREADS, smem, s>>>(P);
@@ -500,6 +511,7 @@ int hexmv_launch(HexmvParams& P, cudaStream_t s) {
     if (J.mat[m].radius != J.mat[0].radius) return GSDLQ_ERR_INVALID;
   }
   if (J.input_mode == GSDLQ_IN_PLAIN && !J.x) return GSDLQ_ERR_INVALID;
+  if (J.input_mode != GSDLQ_IN_EMBED && (reinterpret_cast<uintptr_t>(J.x) & 7u)) return GSDLQ_ERR_INVALID;  // float2 loads
   if (J.input_mode == GSDLQ_IN_RMSNORM && (!J.x || !J.norm_w)) return GSDLQ_ERR_INVALID;
   if (J.input_mode == GSDLQ_IN_EMBED && (!J.embed || !J.token || !J.norm_w || J.vocab <= 0)) return GSDLQ_ERR_INVALID;
   if (J.input_mode < 0 || J.input_mode > 2) return GSDLQ_ERR_INVALID;

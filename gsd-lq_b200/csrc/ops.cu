@@ -254,6 +254,8 @@ __global__ void __launch_bounds__(AT_WARPS * 32) attn_kernel(const __grid_consta
 
 static int attention_launch(const gsdlq_attn_job_t& J, cudaStream_t s) {
   if (!J.q || !J.k_cache || !J.v_cache || !J.out || !J.partial || !J.workspace) return GSDLQ_ERR_INVALID;
+  // the kernel reads 4 fp16 of a key/value row per lane as one 8-byte load
+  if ((reinterpret_cast<uintptr_t>(J.k_cache) | reinterpret_cast<uintptr_t>(J.v_cache)) & 7u) return GSDLQ_ERR_INVALID;
   if (J.n_heads <= 0 || J.n_kv_heads <= 0 || J.n_heads % J.n_kv_heads) return GSDLQ_ERR_INVALID;
   if (J.n_heads / J.n_kv_heads > AT_MAX_GQ) return GSDLQ_ERR_UNSUPPORTED;
   if (J.max_seq <= 0 || J.layer < 0) return GSDLQ_ERR_INVALID;
@@ -263,6 +265,7 @@ static int attention_launch(const gsdlq_attn_job_t& J, cudaStream_t s) {
   dim3 grid(J.n_kv_heads, (J.max_seq + tps - 1) / tps);
   if (J.head_dim == 128) attn_kernel<128><<<grid, AT_WARPS * 32, 0, s>>>(J, tps);
   else if (J.head_dim == 64) attn_kernel<64><<<grid, AT_WARPS * 32, 0, s>>>(J, tps);
+  else if (J.head_dim == 32) attn_kernel<32><<<grid, AT_WARPS * 32, 0, s>>>(J, tps);
   else return GSDLQ_ERR_UNSUPPORTED;
   GSDLQ_CUDA_CHECK_LAUNCH();
   return GSDLQ_OK;
@@ -360,7 +363,9 @@ __global__ void pack_lattice_kernel(const float* __restrict__ w, int rows, int c
   const int R = radius;
   const int n_pts = (R == 8) ? 217 : 127;
   int code;
-  if (abs(b0) > R || abs(b1) > R || abs(b0 + b1) > R) {
+  // written so that garbage from non-finite inputs (floorf of NaN/inf) also takes the exhaustive path
+  const bool inside = b0 >= -R && b0 <= R && b1 >= -R && b1 <= R && b0 + b1 >= -R && b0 + b1 <= R;
+  if (!inside) {
     // nearest hexagon point by exhaustive search, first minimum wins (np.argmin)
     float best = 0.f;
     code = 0;
@@ -553,6 +558,7 @@ int gsdlq_gqa_attention(const float* q, const uint16_t* k_cache, const uint16_t*
                         int layer_idx, int pos, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
                         float sm_scale, gsdlq_stream_t stream) {
   if (n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads || max_seq_len <= 0) return GSDLQ_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 7u) return GSDLQ_ERR_INVALID;
   size_t pb = 0, wb = 0;
   attention_ws(n_heads, n_kv_heads, head_dim, max_seq_len, &pb, &wb);
   int dev = 0;

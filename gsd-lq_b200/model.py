@@ -193,6 +193,7 @@ class GSDLQModel:
         j.rope_cs = self.rope_cs.data_ptr()
         j.layer, j.max_seq, j.head_dim, j.interleaved = layer, self.max_seq, self.head_dim, 1
         j.argmax_key = self.key.data_ptr() if argmax else None
+        j.argmax_index_base = self.tp.rank * self.vocab_local if (argmax and self.tp is not None) else 0
         j.workspace = self.ws[site].data_ptr()
         return j
 
@@ -210,11 +211,14 @@ class GSDLQModel:
                             n_heads=self.n_heads_local, n_kv_heads=self.n_kv_local, head_dim=self.head_dim,
                             max_seq=self.max_seq, sm_scale=1.0 / math.sqrt(self.head_dim), block_table=None,
                             page_size=0, partial=self.attn_partial.data_ptr(), workspace=self.attn_ws.data_ptr())
-            o = self._job([hx("attn_output")], 4 * l + 1, L.IN_PLAIN, x=self.att, epilogue=L.EPI_RESID,
+            # tensor parallel: rank 0 adds its partial to the residual, the other ranks store their bare
+            # partials into x; the all-reduce(sum) that follows leaves x + sum of partials everywhere
+            res_epi = L.EPI_RESID if (self.tp is None or self.tp.rank == 0) else L.EPI_STORE
+            o = self._job([hx("attn_output")], 4 * l + 1, L.IN_PLAIN, x=self.att, epilogue=res_epi,
                           ys=(self.x,), resid=self.x)
             gu = self._job([hx("ffn_gate"), hx("ffn_up")], 4 * l + 2, L.IN_RMSNORM, x=self.x, norm=fn,
                            epilogue=L.EPI_SWIGLU, ys=(self.h,))
-            dn = self._job([hx("ffn_down")], 4 * l + 3, L.IN_PLAIN, x=self.h, epilogue=L.EPI_RESID,
+            dn = self._job([hx("ffn_down")], 4 * l + 3, L.IN_PLAIN, x=self.h, epilogue=res_epi,
                            ys=(self.x,), resid=self.x)
             self.layer_jobs.append((qkv, att, o, gu, dn))
         self.head_job = self._job([self.hex["output.weight"]], 4 * self.n_layers, L.IN_RMSNORM, x=self.x,

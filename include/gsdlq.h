@@ -177,6 +177,7 @@ typedef struct gsdlq_linear_job {
   /* optional fused greedy argmax of y[0] (EPI_STORE): atomicMax of a 64-bit
    * (value, ~index) key; the key must start at 0 */
   unsigned long long *argmax_key;
+  int argmax_index_base;      /* added to the row index in the key (vocab-parallel LM head) */
   unsigned int *workspace;    /* GSDLQ_LINEAR_WS_WORDS words, zero before first use;
                                  each launch leaves it zero again */
 } gsdlq_linear_job_t;

@@ -1,0 +1,207 @@
+"""The fused packed-linear launch (gsdlq_linear) against oracle compositions, plus
+the device-flag fault paths (host-made bad inputs; no GPU fault is provoked)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+from test_gpu_kernels import rand_hex, oracle_rec, rel_err, dev, _p, MATVEC_TOL  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def env(cuda_lib):
+    import gsdlq_b200.ops as ops
+    import gsdlq_b200._lib as L
+    L.device_flags()
+    return ops, L
+
+
+def make_job(L, mats, input_mode, x=None, norm=None, eps=1e-5, epilogue=0, ys=(), resid=None, ws=None, **kw):
+    j = L.LinearJob()
+    for i, m in enumerate(mats):
+        j.mat[i] = m.desc()
+    j.n_mat = len(mats)
+    j.input_mode = input_mode
+    j.x = x.data_ptr() if x is not None else None
+    j.norm_w = norm.data_ptr() if norm is not None else None
+    j.eps = eps
+    j.epilogue = epilogue
+    for i, y in enumerate(ys):
+        j.y[i] = y.data_ptr() if y is not None else None
+    j.resid = resid.data_ptr() if resid is not None else None
+    j.workspace = ws.data_ptr() if ws is not None else None
+    for k, v in kw.items():
+        setattr(j, k, v)
+    return j
+
+
+def oracle_matvec(restated, x, t):
+    return restated.matvec(np.ascontiguousarray(x, np.float32), oracle_rec(t))
+
+
+def rms(restated, x, w, eps=1e-5):
+    o = np.zeros_like(x)
+    restated.rmsnorm(_p(x), _p(w), _p(o), x.size, eps)
+    return o
+
+
+@pytest.mark.parametrize("rows,cols", [(512, 1024), (32768, 4096), (151936, 1536)])
+def test_rmsnorm_store_argmax(env, restated, oracle_mod, rng, rows, cols):
+    ops, L = env
+    t = rand_hex(rng, rows, cols, k=16, nnz=4)
+    h = ops.DeviceHex(t)
+    x = rng.standard_normal(cols).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    y = torch.zeros(rows, device="cuda")
+    key = torch.zeros(1, dtype=torch.int64, device="cuda")
+    ws = torch.zeros(64, dtype=torch.int32, device="cuda")
+    j = make_job(L, [h], L.IN_RMSNORM, x=dev(x), norm=dev(w), epilogue=L.EPI_STORE, ys=(y,), ws=ws,
+                 argmax_key=key.data_ptr())
+    yr = oracle_matvec(restated, rms(restated, x, w), t)
+    for rep in range(2):  # the workspace must come back to zero for the second launch
+        key.zero_()
+        ops.linear(j)
+        torch.cuda.synchronize()
+        assert rel_err(y.cpu().numpy(), yr) < MATVEC_TOL
+        k = int(key.item()) & 0xffffffff
+        assert 0xffffffff - k == oracle_mod.argmax(y.cpu().numpy())
+        assert int(ws.abs().sum().item()) == 0
+    assert L.device_flags() == 0
+
+
+def test_plain_resid(env, restated, rng):
+    ops, L = env
+    t = rand_hex(rng, 4096, 14336, k=16, nnz=56)
+    h = ops.DeviceHex(t)
+    x = rng.standard_normal(14336).astype(np.float32)
+    r0 = rng.standard_normal(4096).astype(np.float32)
+    res = dev(r0)
+    ws = torch.zeros(64, dtype=torch.int32, device="cuda")
+    j = make_job(L, [h], L.IN_PLAIN, x=dev(x), epilogue=L.EPI_RESID, ys=(res,), resid=res, ws=ws)
+    ops.linear(j)
+    yr = r0 + oracle_matvec(restated, x, t)
+    assert rel_err(res.cpu().numpy(), yr) < MATVEC_TOL
+
+
+@pytest.mark.parametrize("rows,cols", [(14336, 4096), (8960, 1536), (512, 256)])
+def test_rmsnorm_swiglu(env, restated, rng, rows, cols):
+    ops, L = env
+    tg, tu = rand_hex(rng, rows, cols, k=16, nnz=4), rand_hex(rng, rows, cols, k=16, nnz=4)
+    x = rng.standard_normal(cols).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    hout = torch.zeros(rows, device="cuda")
+    ws = torch.zeros(64, dtype=torch.int32, device="cuda")
+    j = make_job(L, [ops.DeviceHex(tg), ops.DeviceHex(tu)], L.IN_RMSNORM, x=dev(x), norm=dev(w),
+                 epilogue=L.EPI_SWIGLU, ys=(hout,), ws=ws)
+    ops.linear(j)
+    xn = rms(restated, x, w)
+    g, u = oracle_matvec(restated, xn, tg), oracle_matvec(restated, xn, tu)
+    ref = np.zeros_like(g)
+    restated.swiglu(_p(g), _p(u), _p(ref), rows)
+    # swiglu amplifies the relative error of g where silu'(g) g/silu(g) > 1; keep the bound loose-ish
+    assert rel_err(hout.cpu().numpy(), ref) < 2 * MATVEC_TOL
+    assert int(ws.abs().sum().item()) == 0
+
+
+@pytest.mark.parametrize("nh,nkv,hd,H", [(32, 8, 128, 4096), (12, 2, 128, 1536), (32, 32, 64, 2048)])
+def test_embed_qkv_rope_kv(env, restated, rng, nh, nkv, hd, H):
+    ops, L = env
+    V, S, layer = 1000, 128, 1
+    tq = rand_hex(rng, nh * hd, H, k=16, nnz=4)
+    tk = rand_hex(rng, nkv * hd, H, k=16, nnz=4)
+    tv = rand_hex(rng, nkv * hd, H, k=0, nnz=0)
+    emb = (rng.standard_normal((V, H)) * 0.5).astype(np.float16)
+    w = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    kd = torch.zeros((2, S, nkv, hd), dtype=torch.int16, device="cuda")
+    vd = torch.zeros_like(kd)
+    q = torch.zeros(nh * hd, device="cuda")
+    kout, vout = torch.zeros(nkv * hd, device="cuda"), torch.zeros(nkv * hd, device="cuda")
+    xo = torch.zeros(H, device="cuda")
+    state = torch.tensor([777, 0], dtype=torch.int32, device="cuda")
+    cs = torch.from_numpy(ops.rope_table(S, hd, 1e6)).cuda()
+    ws = torch.zeros(64, dtype=torch.int32, device="cuda")
+    embd = dev(emb.view(np.int16))
+    j = make_job(L, [ops.DeviceHex(tq), ops.DeviceHex(tk), ops.DeviceHex(tv)], L.IN_EMBED, norm=dev(w),
+                 epilogue=L.EPI_ROPE_KV, ys=(q, kout, vout), ws=ws, embed=embd.data_ptr(), token=state.data_ptr(),
+                 vocab=V, x_out=xo.data_ptr(), k_cache=kd.data_ptr(), v_cache=vd.data_ptr(),
+                 pos=state.data_ptr() + 4, rope_cs=cs.data_ptr(), layer=layer, max_seq=S, head_dim=hd,
+                 interleaved=1)
+    kc = np.zeros((2, S, nkv, hd), np.uint16)
+    vc = np.zeros_like(kc)
+    for pos in (0, 5, 127):
+        state[1] = pos
+        ops.linear(j)
+        x = emb[777].astype(np.float32)
+        xn = rms(restated, x, w)
+        qr, kr, vr = (oracle_matvec(restated, xn, t) for t in (tq, tk, tv))
+        restated.rope_and_store_kv(_p(qr), _p(kr), _p(vr), _p(kc), _p(vc), layer, pos, nh, nkv, hd, S, 1e6, 1)
+        torch.cuda.synchronize()
+        assert np.array_equal(xo.cpu().numpy(), x)
+        assert rel_err(q.cpu().numpy(), qr) < MATVEC_TOL
+        kg = kd.cpu().numpy().view(np.float16)[layer, pos].astype(np.float32).reshape(-1)
+        vg = vd.cpu().numpy().view(np.float16)[layer, pos].astype(np.float32).reshape(-1)
+        assert rel_err(kg, kc.view(np.float16)[layer, pos].astype(np.float32).reshape(-1)) < MATVEC_TOL
+        assert rel_err(vg, vc.view(np.float16)[layer, pos].astype(np.float32).reshape(-1)) < MATVEC_TOL
+        assert rel_err(vout.cpu().numpy(), vr) < MATVEC_TOL
+    assert int(ws.abs().sum().item()) == 0
+    assert L.device_flags() == 0
+
+
+def test_flags_bad_kink_and_bad_pos(env, restated, rng):
+    """Host-made bad inputs: the kernels skip the access and raise a flag instead of faulting."""
+    ops, L = env
+    t = rand_hex(rng, 64, 256, k=0, nnz=2)
+    h = ops.DeviceHex(t)
+    bad = t.kink_cols.copy()
+    bad[3] = 300  # column >= cols
+    h.kink_cols = dev(bad.view(np.int16))
+    x = rng.standard_normal(256).astype(np.float32)
+    y = torch.zeros(64, device="cuda")
+    j = make_job(L, [h], L.IN_PLAIN, x=dev(x), epilogue=L.EPI_STORE, ys=(y,))
+    ops.linear(j)
+    flags = L.device_flags()
+    assert flags & 0x2, L.flag_names(flags)
+    t2 = rand_hex(np.random.default_rng(0), 64, 256, k=0, nnz=2)
+    t2.kink_cols[:] = t.kink_cols
+    t2.codes[:] = t.codes
+    t2.scales[:] = t.scales
+    t2.kink_deltas[:] = t.kink_deltas
+    t2.kink_deltas[3] = 0.0  # the skipped kink contributes nothing
+    assert rel_err(y.cpu().numpy(), oracle_matvec(restated, x, t2)) < MATVEC_TOL
+    # pos >= max_seq read from device memory: no KV store, flag raised
+    tq = rand_hex(rng, 128, 128, k=0, nnz=0)
+    tk = rand_hex(rng, 64, 128, k=0, nnz=0)
+    tv = rand_hex(rng, 64, 128, k=0, nnz=0)
+    S = 16
+    kd = torch.zeros((1, S, 1, 64), dtype=torch.int16, device="cuda")
+    vd = torch.zeros_like(kd)
+    q = torch.zeros(128, device="cuda")
+    state = torch.tensor([0, S + 3], dtype=torch.int32, device="cuda")
+    cs = torch.from_numpy(ops.rope_table(S, 64, 1e4)).cuda()
+    j = make_job(L, [ops.DeviceHex(tq), ops.DeviceHex(tk), ops.DeviceHex(tv)], L.IN_PLAIN,
+                 x=dev(rng.standard_normal(128).astype(np.float32)), epilogue=L.EPI_ROPE_KV, ys=(q, None, None),
+                 k_cache=kd.data_ptr(), v_cache=vd.data_ptr(), pos=state.data_ptr() + 4, rope_cs=cs.data_ptr(),
+                 layer=0, max_seq=S, head_dim=64, interleaved=1)
+    ops.linear(j)
+    flags = L.device_flags()
+    assert flags & 0x4, L.flag_names(flags)
+    assert int(kd.abs().sum().item()) == 0 and int(vd.abs().sum().item()) == 0
+
+
+def test_bounded_wait_times_out_without_hanging(env, rng):
+    """A low-rank counter that never reaches its target (a consumer-only launch with a
+    pre-filled ticket counter) makes the epilogue's bounded wait give up and flag."""
+    ops, L = env
+    t = rand_hex(rng, 64, 256, k=4, nnz=0)
+    x = rng.standard_normal(256).astype(np.float32)
+    y = torch.zeros(64, device="cuda")
+    ws = torch.zeros(64, dtype=torch.int32, device="cuda")
+    ws[0] = 1 << 20  # every ticket is already taken: nobody produces tmp_k
+    j = make_job(L, [ops.DeviceHex(t)], L.IN_PLAIN, x=dev(x), epilogue=L.EPI_STORE, ys=(y,), ws=ws)
+    ops.linear(j)
+    torch.cuda.synchronize()
+    flags = L.device_flags()
+    assert flags & 0x10, L.flag_names(flags)
