@@ -276,8 +276,8 @@ def run_ours(args):
 
     def gu(n):
         for _ in range(n):
-            for j in gu_jobs:
-                ops.linear(j)
+            for i, j in enumerate(gu_jobs):
+                ops.linear(j, model.ws[i % 2])  # consecutive launches alternate workspaces
     gu(1)
     gu_ms = time_region(gu, rep, world) / (rep * len(gu_jobs))
     lay0 = "blk.0."

@@ -20,7 +20,6 @@ szp = ctypes.POINTER(ctypes.c_size_t)
 GSDLQ_OK = 0
 EPI_STORE, EPI_RESID, EPI_SWIGLU, EPI_ROPE_KV = 0, 1, 2, 3
 IN_PLAIN, IN_RMSNORM, IN_EMBED = 0, 1, 2
-LINEAR_WS_WORDS = 64
 FLAG_NAMES = {0x1: "bad_code", 0x2: "bad_kink", 0x4: "bad_pos", 0x8: "bad_table", 0x10: "timeout",
               0x20: "bad_token"}
 
@@ -36,7 +35,7 @@ class LinearJob(ctypes.Structure):
                 ("eps", f32), ("embed", vp), ("token", vp), ("vocab", i32), ("x_out", vp), ("epilogue", i32),
                 ("y", vp * 3), ("resid", vp), ("k_cache", vp), ("v_cache", vp), ("pos", vp), ("rope_cs", vp),
                 ("layer", i32), ("max_seq", i32), ("head_dim", i32), ("interleaved", i32),
-                ("argmax_key", vp), ("argmax_index_base", i32), ("workspace", vp)]
+                ("argmax_key", vp), ("argmax_index_base", i32)]
 
 
 class AttnJob(ctypes.Structure):
@@ -61,7 +60,8 @@ SIGNATURES = {
     "gsdlq_dequant": ([vp, vp, vp, vp, i32, i32, i32, vp], i32),
     "gsdlq_argmax": ([vp, i32, vp, vp], i32),
     "gsdlq_pack_lattice": ([vp, i32, i32, i32, vp, vp, vp, vp], i32),
-    "gsdlq_linear": ([ctypes.POINTER(LinearJob), vp], i32),
+    "gsdlq_linear": ([ctypes.POINTER(LinearJob), vp, ctypes.c_size_t, vp], i32),
+    "gsdlq_linear_ws_size": ([ctypes.POINTER(LinearJob), szp], i32),
     "gsdlq_attention_ws_size": ([i32, i32, i32, i32, szp, szp], i32),
     "gsdlq_attention": ([ctypes.POINTER(AttnJob), vp], i32),
     "gsdlq_rope_table": ([vp, i32, i32, f32], i32),

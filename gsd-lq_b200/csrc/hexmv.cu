@@ -23,15 +23,23 @@
 // (PRMT: code -> bits 8..15, lane*4 -> bits 0..7) and one 32-bit shared load
 // from a 256-entry table replicated once per lane in the lane's own bank
 // (entry c of lane l at byte c*256 + l*4), so the 32 lookups of a warp never
-// conflict.
+// conflict.  The other half of every 256-byte table row holds 128 bytes of the
+// staged activation splits.
 //
-// Work split.  A CTA (8 warps) owns whole 16-row strips: every warp covers a
-// contiguous range of 64-column scale groups of the strip, partial row sums
-// meet in shared memory, and the epilogue sees complete rows.  CTAs are
-// persistent (grid <= resident capacity) so that the table build and the
-// input staging are paid once per CTA.  The low-rank projections are computed
-// by the first CTAs to start (an atomic ticket) and published through a
-// counter that the epilogues wait on with a bounded spin.
+// Work split: persistent stream-K.  One CTA per SM: 14 streaming warps and 2
+// helper warps.  The (16-row strip, 64-column group) iterations of the launch
+// are dealt to the streaming warps as equal contiguous ranges, so every warp
+// streams the same number of code bytes; codes are prefetched HX_PF groups
+// ahead in registers, across strip boundaries.  A warp's contribution to a
+// strip (a "segment") goes to a per-strip partial slot; a per-strip counter
+// tells the warp that completes a strip to sum the slots in slot order
+// (deterministic) and run the epilogue.  The helper warps compute the low-rank
+// projections (one tmp_k value per ticket) and then each strip's kink and
+// low-rank terms into one more slot, off the streaming warps' critical path.
+//
+// Launch order (programmatic dependent launch): decode table, staged scales
+// and the first code prefetches are issued BEFORE griddepcontrol.wait, so they
+// overlap the previous kernel; the input x is read only after it.
 #include <algorithm>
 #include <cstdio>
 
@@ -39,38 +47,69 @@
 
 namespace gsdlq {
 
-constexpr int HX_WARPS = 8;
+constexpr int HX_WARPS = 16;
+constexpr int HX_STREAM = 14;
 constexpr int HX_THREADS = HX_WARPS * kWarp;
 constexpr int HX_TAB_BYTES = 256 * 256;
-constexpr int HX_PF = 4;  // groups of codes kept in flight per warp
+constexpr int HX_PF = 6;  // groups of codes kept in flight per streaming warp
+
+// control words at the start of the workspace
+constexpr int CTL_TK_TICKET = 0;    // low-rank job tickets
+constexpr int CTL_TK_DONE = 1;      // low-rank jobs published
+constexpr int CTL_KINK_TICKET = 2;  // helper strip tickets
+constexpr int CTL_DONE = 3;         // CTAs finished
+constexpr int CTL_TMPK = 16;        // 48 floats: tmp_k[m][j]
+constexpr int CTL_WORDS = 64;
 
 struct HexmvParams {
   gsdlq_linear_job_t job;
-  const float* xy_table;     // drop-in path: decode table derived from this float table
-  const float* tmp_k_ext;    // drop-in path: caller-computed tmp_k for mat[0]
+  const float* xy_table;   // drop-in path: decode table derived from this float table
+  const float* tmp_k_ext;  // drop-in path: caller-computed tmp_k for mat[0]
   int n_pts;
-  int cols;
-  int units;
-  int unit_begin[4];         // prefix sums of strips per matrix (non-pair modes)
-  int n_lowrank_jobs;
-  int pair;                  // SWIGLU: mat[0], mat[1] processed strip by strip together
+  int cols, G, NP;
+  int n_strips, nmat;      // nmat: matrices per strip unit (2 in SwiGLU pair mode)
+  int strip_begin[4];      // prefix of strips per matrix (non-pair modes)
+  long long T;             // iterations = n_strips * G
+  int W;                   // streaming warps in the launch
+  int max_seg;             // partial slots per strip for streaming segments (+1 helper slot)
+  int n_lr_jobs;
+  int sc_strips;           // capacity of the staged-scale window (strips)
+  int sc_stride;           // u16 stride of a staged scale row (odd number of words)
+  int ovf_bytes;           // activation-split overflow region
+  unsigned* ctl;
+  unsigned* cnt;           // [n_strips]
+  float* part;             // [n_strips][max_seg + 1][nmat * 16]
 };
 
-struct HexmvSmem {
-  int cols;
-  __device__ __forceinline__ float* xf(uint8_t* base) const { return reinterpret_cast<float*>(base + HX_TAB_BYTES); }
-  __device__ __forceinline__ uint32_t* xs_hi(uint8_t* base) const { return reinterpret_cast<uint32_t*>(xf(base) + cols); }
-  __device__ __forceinline__ uint32_t* xs_lo(uint8_t* base) const { return xs_hi(base) + cols / 2; }
-  __device__ __forceinline__ float* scl(uint8_t* base) const { return reinterpret_cast<float*>(xs_lo(base) + cols / 2); }
-  // scale rows: 2 matrices x 16 rows x (G + 1) floats (row padded by one word)
-  __device__ __forceinline__ float* red(uint8_t* base) const { return scl(base) + 2 * 16 * (cols / 64 + 1); }
-  __device__ __forceinline__ float* misc(uint8_t* base) const { return red(base) + HX_WARPS * 32; }
+// ---- partition helpers (identical on host and device) --------------------------------
+__host__ __device__ __forceinline__ long long it_begin(int w, long long T, int W) { return (long long)w * T / W; }
+// warp whose range contains iteration i: the largest w with it_begin(w) <= i
+__host__ __device__ __forceinline__ int warp_of(long long i, long long T, int W) {
+  return (int)(((i + 1) * (long long)W - 1) / T);
+}
+
+inline size_t hexmv_ws_bytes_for(int n_strips, int max_seg, int nmat) {
+  return sizeof(unsigned) * (CTL_WORDS + (size_t)n_strips) +
+         sizeof(float) * (size_t)n_strips * (max_seg + 1) * nmat * 16 + 256;
+}
+
+// ---- shared memory --------------------------------------------------------------------
+struct HxLayout {
+  int sc_off, misc_off, total;
 };
 
-inline size_t hexmv_smem_bytes(int cols) {
-  const size_t g = cols / 64;
-  return HX_TAB_BYTES + 4ull * cols /*xf*/ + 4ull * cols /*xs hi+lo*/ + 4ull * 2 * 16 * (g + 1) +
-         4ull * HX_WARPS * 32 + 4ull * (8 + 3 * 16 + 8);
+__host__ __device__ inline HxLayout hx_layout(int ovf_bytes, int sc_strips, int nmat, int sc_stride) {
+  HxLayout L;
+  L.sc_off = HX_TAB_BYTES + ovf_bytes;
+  const int sc_bytes = sc_strips * nmat * 16 * sc_stride * 2;
+  L.misc_off = L.sc_off + ((sc_bytes + 15) & ~15);
+  L.total = L.misc_off + 64 * 4;
+  return L;
+}
+
+// byte offset of the 128-byte activation-split chunk `ch` (chunk 2g = hi words of group g, 2g+1 = lo)
+__device__ __forceinline__ uint32_t xs_chunk(int ch) {
+  return ch < 256 ? (uint32_t)ch * 256u + 128u : (uint32_t)HX_TAB_BYTES + (uint32_t)(ch - 256) * 128u;
 }
 
 // (r0, r1) of code c in the radius-R enumeration (r0 outer, r1 inner, |r0+r1| <= R).
@@ -88,7 +127,7 @@ __device__ __forceinline__ bool lattice_of_code(int c, int R, int& r0, int& r1) 
   return false;
 }
 
-__device__ void build_decode_table(uint8_t* smem, const HexmvParams& P) {
+__device__ __forceinline__ void build_decode_table(uint8_t* smem, const HexmvParams& P) {
   const int R = P.job.mat[0].radius;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) {
     int r0 = 0, r1 = 0;
@@ -112,68 +151,10 @@ __device__ void build_decode_table(uint8_t* smem, const HexmvParams& P) {
     }
     if (!ok) r0 = r1 = 0;
     const uint32_t e = pack_bf16x2((float)r0, (float)r1);
-    uint4 v = make_uint4(e, e, e, e);
+    const uint4 v = make_uint4(e, e, e, e);
     uint4* row = reinterpret_cast<uint4*>(smem + i * 256);
 #pragma unroll
     for (int w = 0; w < 8; ++w) row[w] = v;
-  }
-}
-
-// Input staging: xf = transformed fp32 input, xs_hi/xs_lo = bf16 splits of (a, b).
-__device__ void stage_input(uint8_t* smem, const HexmvSmem& L, const HexmvParams& P) {
-  const gsdlq_linear_job_t& J = P.job;
-  const int C = P.cols;
-  float* xf = L.xf(smem);
-  float* misc = L.misc(smem);
-  const int tid = threadIdx.x;
-  // 1. raw row into xf
-  if (J.input_mode == GSDLQ_IN_EMBED) {
-    int tok = *J.token;
-    if (tok < 0 || tok >= J.vocab) {
-      if (tid == 0) raise_flag(GSDLQ_FLAG_BAD_TOKEN);
-      tok = 0;
-    }
-    const uint16_t* row = J.embed + (size_t)tok * C;
-    for (int c = tid; c < C; c += blockDim.x) {
-      const float v = h2f(row[c]);
-      xf[c] = v;
-      if (blockIdx.x == 0 && J.x_out != nullptr) J.x_out[c] = v;
-    }
-  } else {
-    const float2* x2 = reinterpret_cast<const float2*>(J.x);
-    float2* xf2 = reinterpret_cast<float2*>(xf);
-    for (int p = tid; p < C / 2; p += blockDim.x) xf2[p] = x2[p];
-  }
-  __syncthreads();
-  // 2. RMSNorm: out = x * (1/sqrt(sum(x^2)/C + eps)) * w   (gsd_lq_cpu_engine.c:67-82)
-  if (J.input_mode != GSDLQ_IN_PLAIN) {
-    float ss = 0.f;
-    for (int c = tid; c < C; c += blockDim.x) ss += xf[c] * xf[c];
-    ss = warp_sum(ss);
-    float* red = L.red(smem);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    if (tid == 0) {
-      float t = 0.f;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
-      misc[0] = 1.0f / sqrtf(t / (float)C + J.eps);
-    }
-    __syncthreads();
-    const float inv = misc[0];
-    for (int c = tid; c < C; c += blockDim.x) xf[c] = __fmul_rn(__fmul_rn(xf[c], inv), J.norm_w[c]);
-    __syncthreads();
-  }
-  // 3. (a, b) = (x0, x0/2 + sqrt3/2 * x1) split into bf16 hi + lo
-  uint32_t* hi = L.xs_hi(smem);
-  uint32_t* lo = L.xs_lo(smem);
-  for (int p = tid; p < C / 2; p += blockDim.x) {
-    const float x0 = xf[2 * p], x1 = xf[2 * p + 1];
-    const float a = x0;
-    const float b = fmaf(0.8660254037844386f, x1, 0.5f * x0);
-    uint32_t h, l;
-    split_bf16x2(a, b, h, l);
-    hi[p] = h;
-    lo[p] = l;
   }
 }
 
@@ -182,7 +163,7 @@ __device__ __forceinline__ uint32_t tab_lookup(const uint8_t* smem, uint32_t wor
   return *reinterpret_cast<const uint32_t*>(smem + off);
 }
 
-// One 64-column scale group of one 16-row strip: 4 MMAs; returns hi+lo sums for rows g, g+8.
+// one 64-column scale group of one 16-row strip: 4 MMAs; returns hi+lo sums for rows g, g+8
 __device__ __forceinline__ void group_mma(const uint8_t* smem, uint2 ca, uint2 cb, const uint32_t (&bq)[8],
                                           uint32_t lane4, float& r_g, float& r_h) {
   float d[4] = {0.f, 0.f, 0.f, 0.f};
@@ -203,360 +184,575 @@ __device__ __forceinline__ void group_mma(const uint8_t* smem, uint2 ca, uint2 c
   r_h = d[2] + d[3];
 }
 
-// Block-wide dot of xf with one fp16 row of length C (for the low-rank projection).
-__device__ float block_dot_f16(const float* xf, const uint16_t* v, int C, float* red) {
-  float s = 0.f;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) s += xf[c] * h2f(v[c]);
-  s = warp_sum(s);
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-  __syncthreads();
-  float t = 0.f;
-  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
-  __syncthreads();
-  return t;
+__device__ __forceinline__ float ld_cg_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// transformed input element c (after the RMSNorm / embedding prologue), from global memory
+__device__ __forceinline__ float input_at(const gsdlq_linear_job_t& J, int c, int tok, float inv) {
+  if (J.input_mode == GSDLQ_IN_PLAIN) return J.x[c];
+  const float raw = (J.input_mode == GSDLQ_IN_EMBED) ? h2f(J.embed[(size_t)tok * J.mat[0].cols + c]) : J.x[c];
+  return __fmul_rn(__fmul_rn(raw, inv), J.norm_w[c]);
+}
+
+struct StripInfo {
+  int m0;     // matrix of the strip (the first of the pair in SwiGLU mode)
+  int rbase;  // first row of the strip within that matrix
+};
+
+template <int NMAT>
+__device__ __forceinline__ StripInfo strip_info(const HexmvParams& P, int s) {
+  StripInfo si;
+  if (NMAT == 2) {
+    si.m0 = 0;
+    si.rbase = s * 16;
+  } else {
+    int m = 0;
+    while (m < P.job.n_mat - 1 && s >= P.strip_begin[m + 1]) ++m;
+    si.m0 = m;
+    si.rbase = (s - P.strip_begin[m]) * 16;
+  }
+  return si;
+}
+
+// Epilogue of a completed strip.  Lane j holds the finished value of row (j & 15) of
+// matrix m0 + (j >> 4) (lanes >= 16 only carry data in pair mode).
+template <int EPI>
+__device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float v, int lane) {
+  const gsdlq_linear_job_t& J = P.job;
+  const int r = lane & 15;
+  const gsdlq_hexmat_t& M = J.mat[si.m0];
+  const int row = si.rbase + r;
+  const bool ok = row < M.rows;
+  if constexpr (EPI == GSDLQ_EPI_STORE) {
+    unsigned long long key = 0ull;
+    if (lane < 16 && ok) {
+      J.y[si.m0][row] = v;
+      if (J.argmax_key) key = argmax_key(v, (uint32_t)(row + J.argmax_index_base));
+    }
+    if (J.argmax_key) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+      }
+      if (lane == 0 && key) atomicMax(J.argmax_key, key);
+    }
+  } else if constexpr (EPI == GSDLQ_EPI_RESID) {
+    if (lane < 16 && ok) J.y[0][row] = J.resid[row] + v;
+  } else if constexpr (EPI == GSDLQ_EPI_SWIGLU) {
+    const float u = __shfl_down_sync(0xffffffffu, v, 16);
+    if (lane < 16 && ok) J.y[0][row] = (v / (1.0f + expf(-v))) * u;
+  } else if constexpr (EPI == GSDLQ_EPI_ROPE_KV) {
+    // rows (2i, 2i+1) of a head form one interleaved RoPE pair
+    const float other = __shfl_xor_sync(0xffffffffu, v, 1);
+    if (lane < 16 && ok) {
+      const bool even = (r & 1) == 0;
+      const float v0 = even ? v : other, v1 = even ? other : v;
+      const int pos = *J.pos;
+      const int hd = J.head_dim;
+      const bool pos_ok = pos >= 0 && pos < J.max_seq;
+      if (!pos_ok && lane == 0) raise_flag(GSDLQ_FLAG_BAD_POS);
+      if (si.m0 == 2) {  // V: stored unrotated
+        if (J.y[2]) J.y[2][row] = v;
+        if (pos_ok) J.v_cache[((size_t)J.layer * J.max_seq + pos) * M.rows + row] = f2h(v);
+      } else {
+        const int i = (row % hd) >> 1;
+        const float2 cs = pos_ok ? reinterpret_cast<const float2*>(J.rope_cs)[(size_t)pos * (hd / 2) + i]
+                                 : make_float2(1.f, 0.f);
+        const float o = even ? __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y))
+                             : __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+        if (si.m0 == 0) {
+          J.y[0][row] = o;
+        } else {
+          if (J.y[1]) J.y[1][row] = o;
+          if (pos_ok) J.k_cache[((size_t)J.layer * J.max_seq + pos) * M.rows + row] = f2h(o);
+        }
+      }
+    }
+  }
+}
+
+// Sum a completed strip's slots in slot order and run its epilogue (one warp).
+template <int EPI, int NMAT>
+__device__ void finish_strip(const HexmvParams& P, int s, int lane) {
+  __threadfence();
+  const int G = P.G;
+  const int w_first = warp_of((long long)s * G, P.T, P.W);
+  const int w_last = warp_of((long long)s * G + G - 1, P.T, P.W);
+  const int nseg = w_last - w_first + 1;
+  constexpr int width = NMAT * 16;
+  const float* base = P.part + (size_t)s * (P.max_seg + 1) * width;
+  float v = 0.f;
+  if (lane < width) {
+    for (int k = 0; k < nseg; ++k) v += ld_cg_f32(base + (size_t)k * width + lane);
+    v += ld_cg_f32(base + (size_t)P.max_seg * width + lane);  // helper slot: kinks + low rank
+  }
+  if (lane == 0) P.cnt[s] = 0u;  // ready for the next launch
+  strip_epilogue<EPI>(P, strip_info<NMAT>(P, s), v, lane);
+}
+
+// Count `units` toward strip s after this warp's slot writes; the warp completing the
+// strip (G streaming units + 1 helper unit) finishes it.
+template <int EPI, int NMAT>
+__device__ __forceinline__ void arrive(const HexmvParams& P, int s, unsigned units, int lane) {
+  __syncwarp();
+  unsigned fin = 0;
+  if (lane == 0) {
+    __threadfence();
+    const unsigned old = atomicAdd(&P.cnt[s], units);
+    fin = (old + units == (unsigned)P.G + 1u);
+  }
+  fin = __shfl_sync(0xffffffffu, fin, 0);
+  if (fin) finish_strip<EPI, NMAT>(P, s, lane);
 }
 
 template <int EPI>
 __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_constant__ HexmvParams P) {
+  constexpr int NMAT = (EPI == GSDLQ_EPI_SWIGLU) ? 2 : 1;
   extern __shared__ __align__(1024) uint8_t smem[];
   const gsdlq_linear_job_t& J = P.job;
-  const HexmvSmem L{P.cols};
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gl = lane >> 2, q = lane & 3;
-  const int C = P.cols, G = C / 64, NP = C / 2;
-  float* misc = L.misc(smem);
-  float* s_tmpk = misc + 8;              // [3][16]
-  int* s_flags = reinterpret_cast<int*>(misc + 8 + 48);  // [0]: ticket, [1]: tmpk ready
-  unsigned int* ws = J.workspace;
+  const int C = P.cols, G = P.G, NP = P.NP;
+  const HxLayout LY = hx_layout(P.ovf_bytes, P.sc_strips, NMAT, P.sc_stride);
+  uint16_t* s_sc = reinterpret_cast<uint16_t*>(smem + LY.sc_off);
+  float* misc = reinterpret_cast<float*>(smem + LY.misc_off);  // [0] 1/rms, [1..16] reduction
 
+  // ---- 1. independent prologue: decode table, this CTA's scale window, first code prefetches
   build_decode_table(smem, P);
-  stage_input(smem, L, P);
-  if (tid == 0) s_flags[1] = 0;
+  const int w_cta0 = blockIdx.x * HX_STREAM;
+  const long long cta_it0 = it_begin(min(w_cta0, P.W), P.T, P.W);
+  const long long cta_it1 = it_begin(min(w_cta0 + HX_STREAM, P.W), P.T, P.W);
+  const int sc_first = (int)(cta_it0 / G);
+  const int sc_n = (cta_it1 > cta_it0) ? (int)((cta_it1 - 1) / G) - sc_first + 1 : 0;
+  {
+    // raw fp16 bits: [local strip][mm][row][sc_stride]
+    const int per_strip = NMAT * 16 * G;
+    for (int i = tid; i < sc_n * per_strip; i += blockDim.x) {
+      const int ls = i / per_strip, rem = i - ls * per_strip;
+      const int mm = rem / (16 * G), rem2 = rem - mm * 16 * G;
+      const int rr = rem2 / G, gg = rem2 - rr * G;
+      const StripInfo si = strip_info<NMAT>(P, sc_first + ls);
+      const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
+      const int row = min(si.rbase + rr, M.rows - 1);
+      s_sc[((ls * NMAT + mm) * 16 + rr) * P.sc_stride + gg] = M.scales[(size_t)row * G + gg];
+    }
+  }
+  const int w = w_cta0 + warp;
+  const bool streamer = warp < HX_STREAM && w < P.W;
+  const long long it0 = streamer ? it_begin(w, P.T, P.W) : 0;
+  const long long it1 = streamer ? it_begin(w + 1, P.T, P.W) : 0;
+  uint2 pf[NMAT][HX_PF][2];  // [matrix][ring][row g / row g+8]
+  // prefetch cursor: (strip, group) of the next iteration to prefetch
+  int pf_s = (int)(it0 / G), pf_g = (int)(it0 - (long long)pf_s * G);
+  auto issue = [&](int slot_i) {
+    const StripInfo si = strip_info<NMAT>(P, pf_s);
+#pragma unroll
+    for (int mm = 0; mm < NMAT; ++mm) {
+      const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
+      const int ra = min(si.rbase + gl, M.rows - 1), rb = min(si.rbase + gl + 8, M.rows - 1);
+      const uint8_t* pa = M.codes + (size_t)ra * NP + pf_g * 32 + q * 8;
+      const uint8_t* pb = M.codes + (size_t)rb * NP + pf_g * 32 + q * 8;
+      pf[mm][slot_i][0] = ldg_stream_u2(pa);
+      pf[mm][slot_i][1] = ldg_stream_u2(pb);
+    }
+    if (++pf_g == G) {
+      pf_g = 0;
+      ++pf_s;
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < HX_PF; ++i)
+    if (it0 + i < it1) issue(i);
+
+  // ---- 2. wait for the producer of x, then stage the input splits --------------------------
+  pdl_wait();
+  int tok = 0;
+  if (J.input_mode == GSDLQ_IN_EMBED) {
+    tok = *J.token;
+    if (tok < 0 || tok >= J.vocab) {
+      if (tid == 0) raise_flag(GSDLQ_FLAG_BAD_TOKEN);
+      tok = 0;
+    }
+  }
+  float inv = 1.f;
+  if (J.input_mode != GSDLQ_IN_PLAIN) {
+    float ss = 0.f;
+    for (int c = tid; c < C; c += blockDim.x) {
+      const float v = (J.input_mode == GSDLQ_IN_EMBED) ? h2f(J.embed[(size_t)tok * C + c]) : J.x[c];
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) misc[1 + warp] = ss;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.f;
+      for (int k = 0; k < HX_WARPS; ++k) t += misc[1 + k];
+      misc[0] = 1.0f / sqrtf(t / (float)C + J.eps);  // gsd_lq_cpu_engine.c:78
+    }
+    __syncthreads();
+    inv = misc[0];
+  }
+  for (int p = tid; p < NP; p += blockDim.x) {
+    float x0, x1;
+    if (J.input_mode == GSDLQ_IN_EMBED) {
+      const uint32_t raw = *reinterpret_cast<const uint32_t*>(J.embed + (size_t)tok * C + 2 * p);
+      x0 = h2f(raw & 0xffffu);
+      x1 = h2f(raw >> 16);
+      if (blockIdx.x == 0 && J.x_out) {
+        J.x_out[2 * p] = x0;
+        J.x_out[2 * p + 1] = x1;
+      }
+    } else {
+      const float2 v = reinterpret_cast<const float2*>(J.x)[p];
+      x0 = v.x;
+      x1 = v.y;
+    }
+    if (J.input_mode != GSDLQ_IN_PLAIN) {
+      x0 = __fmul_rn(__fmul_rn(x0, inv), J.norm_w[2 * p]);
+      x1 = __fmul_rn(__fmul_rn(x1, inv), J.norm_w[2 * p + 1]);
+    }
+    const float b = fmaf(0.8660254037844386f, x1, 0.5f * x0);
+    uint32_t h, l;
+    split_bf16x2(x0, b, h, l);
+    const int g = p >> 5, i = p & 31;
+    *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g) + 4 * i) = h;
+    *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g + 1) + 4 * i) = l;
+  }
   __syncthreads();
 
-  // ---- low-rank producers: first CTAs to arrive compute tmp_k[m][j] --------------------
-  if (P.n_lowrank_jobs > 0) {
+  if (warp >= HX_STREAM) {
+    // ---- helper warps: low-rank projections, then per-strip kink + low-rank slots --------
+    unsigned* ctl = P.ctl;
     while (true) {
-      if (tid == 0) s_flags[0] = (int)atomicAdd(&ws[0], 1u);
-      __syncthreads();
-      const int t = s_flags[0];
-      __syncthreads();
-      if (t >= P.n_lowrank_jobs) break;
-      int m = 0, j = t;
-      while (m < P.job.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
+      unsigned t = 0;
+      if (lane == 0) t = atomicAdd(&ctl[CTL_TK_TICKET], 1u);
+      t = __shfl_sync(0xffffffffu, t, 0);
+      if ((int)t >= P.n_lr_jobs) break;
+      int m = 0, j = (int)t;
+      while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
       const gsdlq_hexmat_t& M = J.mat[m];
-      const float dot = block_dot_f16(L.xf(smem), M.Vt + (size_t)j * C, C, L.red(smem));
-      if (tid == 0) {
-        reinterpret_cast<volatile float*>(ws)[16 + m * 16 + j] = dot * M.S[j];
+      const uint16_t* vt = M.Vt + (size_t)j * C;
+      float acc = 0.f;
+      for (int c = lane * 8; c < C; c += 256) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(vt + c);
+        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc += input_at(J, c + 2 * k, tok, inv) * h2f(wv[k] & 0xffffu);
+          acc += input_at(J, c + 2 * k + 1, tok, inv) * h2f(wv[k] >> 16);
+        }
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) {
+        reinterpret_cast<volatile float*>(ctl)[CTL_TMPK + m * 16 + j] = acc * M.S[j];
         __threadfence();
-        atomicAdd(&ws[1], 1u);
+        atomicAdd(&ctl[CTL_TK_DONE], 1u);
       }
     }
-  }
-
-  const uint32_t lane4 = (uint32_t)lane * 4u;
-  const uint32_t* xs_hi = L.xs_hi(smem);
-  const uint32_t* xs_lo = L.xs_lo(smem);
-  float* scl = L.scl(smem);
-  float* red = L.red(smem);
-  const int nmat_unit = P.pair ? 2 : 1;
-
-  // this warp's range of scale groups
-  const int g_begin = (warp * G) / HX_WARPS, g_end = ((warp + 1) * G) / HX_WARPS;
-
-  for (int u = blockIdx.x; u < P.units; u += gridDim.x) {
-    int m0 = 0, strip = u;
-    if (!P.pair) {
-      while (m0 < J.n_mat - 1 && u >= P.unit_begin[m0 + 1]) ++m0;
-      strip = u - P.unit_begin[m0];
+    if (P.n_lr_jobs > 0) {
+      if (lane == 0) wait_counter_geq(&ctl[CTL_TK_DONE], (unsigned)P.n_lr_jobs, 1000000000ull);  // 1 s bound
+      __syncwarp();
+      __threadfence();
     }
-    const int rbase = strip * 16;
-    // stage this strip's scales (fp16 -> fp32) for the 1 or 2 matrices of the unit
-    for (int mm = 0; mm < nmat_unit; ++mm) {
-      const gsdlq_hexmat_t& M = J.mat[m0 + mm];
-      for (int i = tid; i < 16 * G; i += blockDim.x) {
-        const int rr = i / G, gg = i - rr * G;
-        const int row = min(rbase + rr, M.rows - 1);
-        scl[(mm * 16 + rr) * (G + 1) + gg] = h2f(M.scales[(size_t)row * G + gg]);
+    constexpr int width = NMAT * 16;
+    while (true) {
+      unsigned s = 0;
+      if (lane == 0) s = atomicAdd(&ctl[CTL_KINK_TICKET], 1u);
+      s = __shfl_sync(0xffffffffu, s, 0);
+      if ((int)s >= P.n_strips) break;
+      const StripInfo si = strip_info<NMAT>(P, (int)s);
+      const int r = lane & 15, hi = lane >> 4;
+      const int mm = (NMAT == 2) ? hi : 0;
+      const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
+      const int row = si.rbase + r;
+      float v = 0.f;
+      if (row < M.rows) {
+        const uint32_t e0 = M.row_ptr[row], e1 = M.row_ptr[row + 1];
+        constexpr int step = (NMAT == 2) ? 1 : 2;
+        for (uint32_t e = e0 + (NMAT == 2 ? 0 : hi); e < e1; e += step) {
+          const int col = M.kink_cols[e];
+          if (col < C) v += M.kink_deltas[e] * input_at(J, col, tok, inv);
+          else raise_flag(GSDLQ_FLAG_BAD_KINK);
+        }
+        if (M.k_dim > 0 && (NMAT == 2 || hi == 0)) {
+          const uint16_t* ur = M.U + (size_t)row * M.k_dim;
+          if (P.tmp_k_ext) {
+            for (int jj = 0; jj < M.k_dim; ++jj) v += h2f(ur[jj]) * P.tmp_k_ext[jj];
+          } else {
+            const volatile float* tk = reinterpret_cast<volatile float*>(ctl) + CTL_TMPK + (si.m0 + mm) * 16;
+            for (int jj = 0; jj < M.k_dim; ++jj) v += h2f(ur[jj]) * tk[jj];
+          }
+        }
       }
+      if (NMAT == 1) v += __shfl_xor_sync(0xffffffffu, v, 16);
+      float* slot = P.part + ((size_t)s * (P.max_seg + 1) + P.max_seg) * width;
+      if (lane < width) slot[lane] = v;
+      arrive<EPI, NMAT>(P, (int)s, 1u, lane);
     }
-    __syncthreads();
-
-    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-    for (int mm = 0; mm < nmat_unit; ++mm) {
-      const gsdlq_hexmat_t& M = J.mat[m0 + mm];
-      const int ra = min(rbase + gl, M.rows - 1), rb = min(rbase + gl + 8, M.rows - 1);
-      const uint8_t* pa = M.codes + (size_t)ra * NP + q * 8;
-      const uint8_t* pb = M.codes + (size_t)rb * NP + q * 8;
-      const float* sa = scl + (mm * 16 + gl) * (G + 1);
-      const float* sb = scl + (mm * 16 + gl + 8) * (G + 1);
-      uint2 ca[HX_PF], cb[HX_PF];
+  } else if (streamer) {
+    // ---- streaming warps --------------------------------------------------------------
+    const uint32_t lane4 = (uint32_t)lane * 4u;
+    // B fragments: lanes gl == 0 read the hi chunk, gl == 1 the lo chunk; the two 16-byte
+    // halves are read in opposite orders so that the 8 active lanes hit 32 distinct banks
+    const int bsel = gl & 1;
+    int cur_s = (int)(it0 / G), cur_g = (int)(it0 - (long long)cur_s * G);
+    int seg_s = cur_s, seg_g0 = cur_g;
+    float acc[NMAT][2];
+#pragma unroll
+    for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
+    auto emit = [&](int s, int g0, int g1) {
+      const int seg = w - warp_of((long long)s * G, P.T, P.W);
+      constexpr int width = NMAT * 16;
+      float* slot = P.part + ((size_t)s * (P.max_seg + 1) + seg) * width;
+      if (q == 0) {
+#pragma unroll
+        for (int mm = 0; mm < NMAT; ++mm) {
+          slot[mm * 16 + gl] = acc[mm][0];
+          slot[mm * 16 + gl + 8] = acc[mm][1];
+        }
+      }
+      arrive<EPI, NMAT>(P, s, (unsigned)(g1 - g0), lane);
+    };
+    for (long long base = it0; base < it1; base += HX_PF) {
 #pragma unroll
       for (int i = 0; i < HX_PF; ++i) {
-        if (g_begin + i < g_end) {
-          ca[i] = ldg_stream_u2(pa + (size_t)(g_begin + i) * 32);
-          cb[i] = ldg_stream_u2(pb + (size_t)(g_begin + i) * 32);
-        }
-      }
-      float accg = 0.f, acch = 0.f;
-      for (int g = g_begin; g < g_end; g += HX_PF) {
+        const long long it = base + i;
+        if (it < it1) {
+          if (cur_s != seg_s) {
+            emit(seg_s, seg_g0, G);
+            seg_s = cur_s;
+            seg_g0 = cur_g;
 #pragma unroll
-        for (int i = 0; i < HX_PF; ++i) {
-          const int gg = g + i;
-          if (gg < g_end) {
-            const uint2 a = ca[i], b = cb[i];
-            const int gn = gg + HX_PF;
-            if (gn < g_end) {
-              ca[i] = ldg_stream_u2(pa + (size_t)gn * 32);
-              cb[i] = ldg_stream_u2(pb + (size_t)gn * 32);
-            }
-            uint32_t bq[8];
-            if (gl < 2) {
-              const uint4* src = reinterpret_cast<const uint4*>((gl == 0 ? xs_hi : xs_lo) + gg * 32 + q * 8);
-              const uint4 v0 = src[0], v1 = src[1];
-              bq[0] = v0.x; bq[1] = v0.y; bq[2] = v0.z; bq[3] = v0.w;
-              bq[4] = v1.x; bq[5] = v1.y; bq[6] = v1.z; bq[7] = v1.w;
-            } else {
+            for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
+          }
+          uint2 cur[NMAT][2];
 #pragma unroll
-              for (int t = 0; t < 8; ++t) bq[t] = 0u;
-            }
-            float rg, rh;
-            group_mma(smem, a, b, bq, lane4, rg, rh);
-            accg = fmaf(sa[gg], rg, accg);
-            acch = fmaf(sb[gg], rh, acch);
+          for (int mm = 0; mm < NMAT; ++mm) {
+            cur[mm][0] = pf[mm][i][0];
+            cur[mm][1] = pf[mm][i][1];
           }
-        }
-      }
-      acc[mm][0] = accg;
-      acc[mm][1] = acch;
-    }
-    // lanes q == 0 hold the rows' sums (B columns 2..7 are zero)
-    if (q == 0) {
-      for (int mm = 0; mm < nmat_unit; ++mm) {
-        red[warp * 32 + mm * 16 + gl] = acc[mm][0];
-        red[warp * 32 + mm * 16 + gl + 8] = acc[mm][1];
-      }
-    }
-    __syncthreads();
-
-    // ---- epilogue: warp w finishes rows 2w and 2w+1 of each matrix of the unit -------
-    const bool need_lr = (P.tmp_k_ext == nullptr) && P.n_lowrank_jobs > 0;
-    if (need_lr && s_flags[1] == 0) {
-      if (tid == 0) {
-        wait_counter_geq(&ws[1], (unsigned)P.n_lowrank_jobs, 1000000000ull);  // 1 s bound
-        __threadfence();
-      }
-      __syncthreads();
-      for (int i = tid; i < 48; i += blockDim.x) s_tmpk[i] = reinterpret_cast<volatile float*>(ws)[16 + i];
-      if (tid == 0) s_flags[1] = 1;
-      __syncthreads();
-    }
-    float vals[2][2];
-    for (int mm = 0; mm < nmat_unit; ++mm) {
-      const int m = m0 + mm;
-      const gsdlq_hexmat_t& M = J.mat[m];
-      for (int k = 0; k < 2; ++k) {
-        const int ri = 2 * warp + k;
-        const int row = rbase + ri;
-        float v = 0.f;
-        if (row < M.rows) {
-          // kinks of this row, spread over the lanes
-          const uint32_t e0 = M.row_ptr[row], e1 = M.row_ptr[row + 1];
-          const float* xf = L.xf(smem);
-          for (uint32_t e = e0 + lane; e < e1; e += 32) {
-            const int col = M.kink_cols[e];
-            if (col < C) v += M.kink_deltas[e] * xf[col];
-            else raise_flag(GSDLQ_FLAG_BAD_KINK);
-          }
-          if (M.k_dim > 0 && lane < M.k_dim) {
-            const float tk = P.tmp_k_ext ? P.tmp_k_ext[lane] : s_tmpk[m * 16 + lane];
-            v += h2f(M.U[(size_t)row * M.k_dim + lane]) * tk;
-          }
-        }
-        v = warp_sum(v);
-        float s = 0.f;
-#pragma unroll
-        for (int w = 0; w < HX_WARPS; ++w) s += red[w * 32 + mm * 16 + ri];
-        vals[mm][k] = s + v;
-      }
-    }
-    if (lane == 0) {
-      const int r0 = rbase + 2 * warp;
-      if constexpr (EPI == GSDLQ_EPI_STORE) {
-        const gsdlq_hexmat_t& M = J.mat[m0];
-        for (int k = 0; k < 2; ++k) {
-          const int row = r0 + k;
-          if (row < M.rows) {
-            J.y[m0][row] = vals[0][k];
-            if (J.argmax_key)
-              atomicMax(J.argmax_key, argmax_key(vals[0][k], (uint32_t)(row + J.argmax_index_base)));
-          }
-        }
-      } else if constexpr (EPI == GSDLQ_EPI_RESID) {
-        const gsdlq_hexmat_t& M = J.mat[0];
-        for (int k = 0; k < 2; ++k) {
-          const int row = r0 + k;
-          if (row < M.rows) J.y[0][row] = J.resid[row] + vals[0][k];
-        }
-      } else if constexpr (EPI == GSDLQ_EPI_SWIGLU) {
-        const gsdlq_hexmat_t& M = J.mat[0];
-        for (int k = 0; k < 2; ++k) {
-          const int row = r0 + k;
-          if (row < M.rows) {
-            const float g = vals[0][k], up = vals[1][k];
-            J.y[0][row] = (g / (1.0f + expf(-g))) * up;
-          }
-        }
-      } else if constexpr (EPI == GSDLQ_EPI_ROPE_KV) {
-        // rows (r0, r0+1) are one interleaved RoPE pair of one head
-        const gsdlq_hexmat_t& M = J.mat[m0];
-        if (r0 + 1 < M.rows) {
-          const int pos = *J.pos;
-          const int hd = J.head_dim;
-          const int i = (r0 % hd) >> 1;
-          const float v0 = vals[0][0], v1 = vals[0][1];
-          const bool pos_ok = pos >= 0 && pos < J.max_seq;
-          if (!pos_ok) raise_flag(GSDLQ_FLAG_BAD_POS);
-          if (m0 == 2) {  // V: store unrotated
-            if (J.y[2]) { J.y[2][r0] = v0; J.y[2][r0 + 1] = v1; }
-            if (pos_ok) {
-              uint16_t* dst = J.v_cache + ((size_t)J.layer * J.max_seq + pos) * M.rows + r0;
-              dst[0] = f2h(v0);
-              dst[1] = f2h(v1);
-            }
+          if (it + HX_PF < it1) issue(i);
+          uint32_t bq[8];
+          if (gl < 2) {
+            const uint8_t* src = smem + xs_chunk(2 * cur_g + bsel) + q * 32;
+            const uint4 v0 = *reinterpret_cast<const uint4*>(src + 16 * bsel);
+            const uint4 v1 = *reinterpret_cast<const uint4*>(src + 16 * (1 - bsel));
+            const uint4 lo4 = bsel ? v1 : v0, hi4 = bsel ? v0 : v1;
+            bq[0] = lo4.x; bq[1] = lo4.y; bq[2] = lo4.z; bq[3] = lo4.w;
+            bq[4] = hi4.x; bq[5] = hi4.y; bq[6] = hi4.z; bq[7] = hi4.w;
           } else {
-            const float2 cs = pos_ok ? reinterpret_cast<const float2*>(J.rope_cs)[(size_t)pos * (hd / 2) + i]
-                                     : make_float2(1.f, 0.f);
-            const float o0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
-            const float o1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
-            if (m0 == 0) {
-              J.y[0][r0] = o0;
-              J.y[0][r0 + 1] = o1;
-            } else {
-              if (J.y[1]) { J.y[1][r0] = o0; J.y[1][r0 + 1] = o1; }
-              if (pos_ok) {
-                uint16_t* dst = J.k_cache + ((size_t)J.layer * J.max_seq + pos) * M.rows + r0;
-                dst[0] = f2h(o0);
-                dst[1] = f2h(o1);
-              }
-            }
+#pragma unroll
+            for (int t = 0; t < 8; ++t) bq[t] = 0u;
+          }
+          const int ls = cur_s - sc_first;
+#pragma unroll
+          for (int mm = 0; mm < NMAT; ++mm) {
+            const uint16_t* sr = s_sc + ((ls * NMAT + mm) * 16) * P.sc_stride + cur_g;
+            const float sa = h2f(sr[gl * P.sc_stride]), sb = h2f(sr[(gl + 8) * P.sc_stride]);
+            float rg, rh;
+            group_mma(smem, cur[mm][0], cur[mm][1], bq, lane4, rg, rh);
+            acc[mm][0] = fmaf(sa, rg, acc[mm][0]);
+            acc[mm][1] = fmaf(sb, rh, acc[mm][1]);
+          }
+          if (++cur_g == G) {
+            cur_g = 0;
+            ++cur_s;
           }
         }
       }
     }
-    __syncthreads();
+    if (it1 > it0) emit(seg_s, seg_g0, (cur_g == 0 && cur_s > seg_s) ? G : cur_g);
   }
 
-  // ---- the last CTA leaves the workspace counters at zero for the next launch ----------
-  if (P.n_lowrank_jobs > 0 && tid == 0) {
+  pdl_launch_dependents();
+  // ---- the last CTA leaves the control words at zero for the next launch ---------------
+  __syncthreads();
+  if (tid == 0) {
     __threadfence();
-    if (atomicAdd(&ws[2], 1u) == gridDim.x - 1) {
-      for (int i = 0; i < GSDLQ_LINEAR_WS_WORDS; ++i) ws[i] = 0u;  // counters and published tmp_k
+    if (atomicAdd(&P.ctl[CTL_DONE], 1u) == gridDim.x - 1) {
+      for (int i = 0; i < CTL_WORDS; ++i) P.ctl[i] = 0u;
       __threadfence();
     }
   }
 }
 
 // ---- host side ------------------------------------------------------------------------
-static int hexmv_validate_mat(const gsdlq_hexmat_t& M, int cols) {
+static int hexmv_validate_mat(const gsdlq_hexmat_t& M, int cols, bool own_lowrank) {
   if (!M.codes || !M.scales || !M.row_ptr) return GSDLQ_ERR_INVALID;
   // codes are read 8 bytes at a time from row starts (cols/2 is a multiple of 32)
   if (reinterpret_cast<uintptr_t>(M.codes) & 7u) return GSDLQ_ERR_INVALID;
   if (M.rows <= 0 || M.cols != cols || cols <= 0 || cols % 64 != 0) return GSDLQ_ERR_INVALID;
   if (M.k_dim < 0 || M.k_dim > 16) return GSDLQ_ERR_INVALID;
-  if (M.k_dim > 0 && (!M.U || !M.S || !M.Vt)) return GSDLQ_ERR_INVALID;
+  if (M.k_dim > 0 && !M.U) return GSDLQ_ERR_INVALID;
+  if (own_lowrank && M.k_dim > 0 && (!M.S || !M.Vt)) return GSDLQ_ERR_INVALID;
+  if (own_lowrank && M.k_dim > 0 && (reinterpret_cast<uintptr_t>(M.Vt) & 15u)) return GSDLQ_ERR_INVALID;  // 16-byte loads
   if (M.radius != 6 && M.radius != 8) return GSDLQ_ERR_INVALID;
   return GSDLQ_OK;
 }
 
-// Resident CTAs per SM for a given dynamic smem size, from the hardware limits (no runtime
-// occupancy query on the launch path): 228 KB of shared memory per SM with 1 KB reserved per CTA,
-// 64K registers per SM at <= 128 registers per thread (ptxas reports 123-128 for hexmv_kernel).
-static int hexmv_ctas_per_sm(size_t smem) {
-  const size_t per_cta = smem + 1024;
-  int by_smem = (int)((228u * 1024u) / per_cta);
-  const int by_regs = 65536 / (HX_THREADS * 128);
-  return std::max(0, std::min(by_smem, by_regs));
+// Geometry of a launch (everything but the workspace pointers).
+static int hexmv_plan(HexmvParams& P) {
+  const gsdlq_linear_job_t& J = P.job;
+  if (J.n_mat < 1 || J.n_mat > 3) return GSDLQ_ERR_INVALID;
+  const int C = J.mat[0].cols;
+  for (int m = 0; m < J.n_mat; ++m) {
+    const int st = hexmv_validate_mat(J.mat[m], C, P.tmp_k_ext == nullptr);
+    if (st != GSDLQ_OK) return st;
+    if (J.mat[m].radius != J.mat[0].radius) return GSDLQ_ERR_INVALID;
+  }
+  P.cols = C;
+  P.G = C / 64;
+  P.NP = C / 2;
+  if (C > 65535) return GSDLQ_ERR_UNSUPPORTED;  // u16 kink columns
+  P.nmat = (J.epilogue == GSDLQ_EPI_SWIGLU) ? 2 : 1;
+  if (P.nmat == 2) {
+    if (J.n_mat != 2) return GSDLQ_ERR_INVALID;
+    P.n_strips = (J.mat[0].rows + 15) / 16;
+  } else {
+    P.strip_begin[0] = 0;
+    for (int m = 0; m < J.n_mat; ++m) P.strip_begin[m + 1] = P.strip_begin[m] + (J.mat[m].rows + 15) / 16;
+    P.n_strips = P.strip_begin[J.n_mat];
+  }
+  P.T = (long long)P.n_strips * P.G;
+  const int max_w = num_sms() * HX_STREAM;
+  P.W = (int)std::min<long long>(max_w, P.T);
+  const long long lmin = P.T / P.W;
+  P.max_seg = (int)((P.G - 1 + lmin - 1) / lmin) + 1;
+  int lr = 0;
+  for (int m = 0; m < J.n_mat; ++m) lr += J.mat[m].k_dim;
+  P.n_lr_jobs = P.tmp_k_ext ? 0 : lr;
+  // staged-scale window: the most strips one CTA's 14 warps touch
+  const int grid = (P.W + HX_STREAM - 1) / HX_STREAM;
+  int sc = 1;
+  for (int c = 0; c < grid; ++c) {
+    const long long a = it_begin(std::min(c * HX_STREAM, P.W), P.T, P.W);
+    const long long b = it_begin(std::min((c + 1) * HX_STREAM, P.W), P.T, P.W);
+    if (b > a) sc = std::max(sc, (int)((b - 1) / P.G - a / P.G + 1));
+  }
+  P.sc_strips = sc;
+  int words = (P.G + 1) / 2;
+  if ((words & 1) == 0) ++words;
+  P.sc_stride = 2 * words;
+  P.ovf_bytes = std::max(0, 2 * P.G - 256) * 128;
+  return GSDLQ_OK;
 }
 
 template <int EPI>
 static int hexmv_launch_t(const HexmvParams& P, cudaStream_t s) {
-  const size_t smem = hexmv_smem_bytes(P.cols);
-  static int configured_max[64] = {0};
+  const HxLayout LY = hx_layout(P.ovf_bytes, P.sc_strips, P.nmat, P.sc_stride);
+  if (LY.total > 227 * 1024) return GSDLQ_ERR_UNSUPPORTED;
+  static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  if ((int)smem > configured_max[dev]) {
+  if (!configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(hexmv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return record_cuda_error(e);
-    configured_max[dev] = 227 * 1024;
+    configured[dev] = true;
   }
-  const int per_sm = hexmv_ctas_per_sm(smem);
-  if (per_sm < 1) return GSDLQ_ERR_UNSUPPORTED;
-  const int grid = std::max(1, std::min(P.units, per_sm * num_sms()));
-  hexmv_kernel<EPI><<<grid, HX_THREADS, smem, s>>>(P);
-  GSDLQ_CUDA_CHECK_LAUNCH();
+  const int grid = (P.W + HX_STREAM - 1) / HX_STREAM;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(HX_THREADS);
+  cfg.dynamicSmemBytes = LY.total;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, hexmv_kernel<EPI>, P);
+  if (e != cudaSuccess) return record_cuda_error(e);
   return GSDLQ_OK;
 }
 
-int hexmv_launch(HexmvParams& P, cudaStream_t s) {
+static int hexmv_check_io(const HexmvParams& P) {
   const gsdlq_linear_job_t& J = P.job;
-  if (J.n_mat < 1 || J.n_mat > 3) return GSDLQ_ERR_INVALID;
-  const int C = J.mat[0].cols;
-  P.cols = C;
-  if ((size_t)hexmv_smem_bytes(C) > 227 * 1024) return GSDLQ_ERR_UNSUPPORTED;
-  for (int m = 0; m < J.n_mat; ++m) {
-    const int st = hexmv_validate_mat(J.mat[m], C);
-    if (st != GSDLQ_OK) return st;
-    if (J.mat[m].radius != J.mat[0].radius) return GSDLQ_ERR_INVALID;
-  }
+  if (J.input_mode < 0 || J.input_mode > 2) return GSDLQ_ERR_INVALID;
   if (J.input_mode == GSDLQ_IN_PLAIN && !J.x) return GSDLQ_ERR_INVALID;
-  if (J.input_mode != GSDLQ_IN_EMBED && (reinterpret_cast<uintptr_t>(J.x) & 7u)) return GSDLQ_ERR_INVALID;  // float2 loads
   if (J.input_mode == GSDLQ_IN_RMSNORM && (!J.x || !J.norm_w)) return GSDLQ_ERR_INVALID;
   if (J.input_mode == GSDLQ_IN_EMBED && (!J.embed || !J.token || !J.norm_w || J.vocab <= 0)) return GSDLQ_ERR_INVALID;
-  if (J.input_mode < 0 || J.input_mode > 2) return GSDLQ_ERR_INVALID;
-  int lr = 0;
-  for (int m = 0; m < J.n_mat; ++m) lr += J.mat[m].k_dim;
-  P.n_lowrank_jobs = P.tmp_k_ext ? 0 : lr;
-  if (P.n_lowrank_jobs > 0 && !J.workspace) return GSDLQ_ERR_INVALID;
-  P.pair = 0;
-  P.unit_begin[0] = 0;
-  for (int m = 0; m < J.n_mat; ++m) P.unit_begin[m + 1] = P.unit_begin[m] + (J.mat[m].rows + 15) / 16;
-  P.units = P.unit_begin[J.n_mat];
+  if (J.input_mode != GSDLQ_IN_EMBED && (reinterpret_cast<uintptr_t>(J.x) & 7u)) return GSDLQ_ERR_INVALID;
+  if (J.input_mode == GSDLQ_IN_EMBED && (reinterpret_cast<uintptr_t>(J.embed) & 3u)) return GSDLQ_ERR_INVALID;
   switch (J.epilogue) {
     case GSDLQ_EPI_STORE:
       if (J.n_mat != 1 && J.argmax_key) return GSDLQ_ERR_INVALID;
       for (int m = 0; m < J.n_mat; ++m)
         if (!J.y[m]) return GSDLQ_ERR_INVALID;
-      return hexmv_launch_t<GSDLQ_EPI_STORE>(P, s);
+      return GSDLQ_OK;
     case GSDLQ_EPI_RESID:
-      if (J.n_mat != 1 || !J.y[0] || !J.resid) return GSDLQ_ERR_INVALID;
-      return hexmv_launch_t<GSDLQ_EPI_RESID>(P, s);
+      return (J.n_mat != 1 || !J.y[0] || !J.resid) ? GSDLQ_ERR_INVALID : GSDLQ_OK;
     case GSDLQ_EPI_SWIGLU:
-      if (J.n_mat != 2 || !J.y[0] || J.mat[0].rows != J.mat[1].rows) return GSDLQ_ERR_INVALID;
-      P.pair = 1;
-      P.units = (J.mat[0].rows + 15) / 16;
-      return hexmv_launch_t<GSDLQ_EPI_SWIGLU>(P, s);
+      return (J.n_mat != 2 || !J.y[0] || J.mat[0].rows != J.mat[1].rows) ? GSDLQ_ERR_INVALID : GSDLQ_OK;
     case GSDLQ_EPI_ROPE_KV:
       if (J.n_mat != 3 || !J.y[0] || !J.k_cache || !J.v_cache || !J.pos || !J.rope_cs) return GSDLQ_ERR_INVALID;
       if (J.interleaved != 1 || J.head_dim <= 0 || J.head_dim % 16 != 0 || J.max_seq <= 0) return GSDLQ_ERR_UNSUPPORTED;
       if (J.mat[1].rows != J.mat[2].rows || J.mat[0].rows % J.head_dim || J.mat[1].rows % J.head_dim)
         return GSDLQ_ERR_INVALID;
-      return hexmv_launch_t<GSDLQ_EPI_ROPE_KV>(P, s);
+      return GSDLQ_OK;
     default:
       return GSDLQ_ERR_INVALID;
   }
 }
 
+int hexmv_launch(HexmvParams& P, void* workspace, size_t ws_bytes, cudaStream_t s) {
+  int st = hexmv_plan(P);
+  if (st != GSDLQ_OK) return st;
+  st = hexmv_check_io(P);
+  if (st != GSDLQ_OK) return st;
+  const size_t need = hexmv_ws_bytes_for(P.n_strips, P.max_seg, P.nmat);
+  if (!workspace || ws_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u)) return GSDLQ_ERR_INVALID;
+  P.ctl = static_cast<unsigned*>(workspace);
+  P.cnt = P.ctl + CTL_WORDS;
+  const uintptr_t pb = reinterpret_cast<uintptr_t>(P.cnt + P.n_strips);
+  P.part = reinterpret_cast<float*>((pb + 15) & ~uintptr_t(15));
+  switch (P.job.epilogue) {
+    case GSDLQ_EPI_STORE: return hexmv_launch_t<GSDLQ_EPI_STORE>(P, s);
+    case GSDLQ_EPI_RESID: return hexmv_launch_t<GSDLQ_EPI_RESID>(P, s);
+    case GSDLQ_EPI_SWIGLU: return hexmv_launch_t<GSDLQ_EPI_SWIGLU>(P, s);
+    default: return hexmv_launch_t<GSDLQ_EPI_ROPE_KV>(P, s);
+  }
+}
+
+size_t hexmv_ws_bytes(HexmvParams& P) {
+  if (hexmv_plan(P) != GSDLQ_OK) return 0;
+  return hexmv_ws_bytes_for(P.n_strips, P.max_seg, P.nmat);
+}
+
+// Workspace of the drop-in gsdlq_hex2d_matvec, whose signature carries none: one buffer
+// per device, allocated on first use, grown on demand, zero-initialised.
+struct DropinWs {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+static DropinWs g_mv_ws[64];
+
 }  // namespace gsdlq
 
 using namespace gsdlq;
 
-extern "C" int gsdlq_linear(const gsdlq_linear_job_t* job, gsdlq_stream_t stream) {
+extern "C" int gsdlq_linear_ws_size(const gsdlq_linear_job_t* job, size_t* bytes) {
+  if (!job || !bytes) return GSDLQ_ERR_INVALID;
+  HexmvParams P{};
+  P.job = *job;
+  const size_t b = hexmv_ws_bytes(P);
+  if (b == 0) return GSDLQ_ERR_INVALID;
+  *bytes = b;
+  return GSDLQ_OK;
+}
+
+extern "C" int gsdlq_linear(const gsdlq_linear_job_t* job, void* workspace, size_t workspace_bytes,
+                            gsdlq_stream_t stream) {
   if (!job) return GSDLQ_ERR_INVALID;
   HexmvParams P{};
   P.job = *job;
-  return hexmv_launch(P, static_cast<cudaStream_t>(stream));
+  return hexmv_launch(P, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int gsdlq_hex2d_matvec(const float* x, const uint8_t* codes, const uint16_t* scales, const float* xy_table,
@@ -573,8 +769,6 @@ extern "C" int gsdlq_hex2d_matvec(const float* x, const uint8_t* codes, const ui
   M.codes = codes;
   M.scales = scales;
   M.U = U;
-  M.S = nullptr;
-  M.Vt = nullptr;
   M.row_ptr = kink_row_ptr;
   M.kink_cols = kink_cols;
   M.kink_deltas = kink_deltas;
@@ -582,6 +776,9 @@ extern "C" int gsdlq_hex2d_matvec(const float* x, const uint8_t* codes, const ui
   M.cols = cols;
   M.k_dim = k_dim;
   M.radius = 8;  // unused when xy_table is given
+  // the drop-in signature carries no S/Vt: the low-rank term comes from the caller's tmp_k
+  M.S = nullptr;
+  M.Vt = nullptr;
   J.input_mode = GSDLQ_IN_PLAIN;
   J.x = x;
   J.epilogue = GSDLQ_EPI_STORE;
@@ -589,10 +786,22 @@ extern "C" int gsdlq_hex2d_matvec(const float* x, const uint8_t* codes, const ui
   P.xy_table = xy_table;
   P.n_pts = n_pts;
   P.tmp_k_ext = k_dim > 0 ? tmp_k : nullptr;
-  // the drop-in signature carries no S/Vt: the low-rank term comes from tmp_k
-  if (k_dim > 0) {
-    M.S = tmp_k;   // non-null placeholders so validation passes; never read when tmp_k_ext is set
-    M.Vt = U;
+  const size_t need = hexmv_ws_bytes(P);
+  if (need == 0) return GSDLQ_ERR_INVALID;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  if (dev < 0 || dev >= 64) return GSDLQ_ERR_UNSUPPORTED;
+  DropinWs& ws = g_mv_ws[dev];
+  if (ws.bytes < need) {
+    if (ws.p) cudaFree(ws.p);
+    ws.p = nullptr;
+    ws.bytes = 0;
+    e = cudaMalloc(&ws.p, need);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    e = cudaMemset(ws.p, 0, need);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    ws.bytes = need;
   }
-  return hexmv_launch(P, static_cast<cudaStream_t>(stream));
+  return hexmv_launch(P, ws.p, ws.bytes, static_cast<cudaStream_t>(stream));
 }

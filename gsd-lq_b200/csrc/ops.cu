@@ -123,151 +123,197 @@ __global__ void rope_store_kernel(float* q, const float* k, const float* v, uint
 }
 
 // ---------------------------------------------------------------------------------------
-// split-KV decode attention (flash-decoding).  CTA (kv head, split) folds the keys of
-// its token range into (max, sum, acc[hd]) for each query head of the group; the last
-// CTA of a kv head combines the splits.
-constexpr int AT_WARPS = 4;
+// split-KV decode attention (flash-decoding).  CTA (kv head, split) stages the K and V
+// rows of its token range in shared memory (row stride padded by 16 bytes so that a
+// 16-byte read per thread is conflict-free), computes the scores of all query heads of
+// the group, a per-head softmax of the tile and P.V, and writes (max, sum, acc[hd]); the
+// last CTA of a kv head combines the splits.  Rows of positions < pos come from earlier
+// steps, so they are loaded before the programmatic-dependent-launch wait; q and the
+// row at pos (written by the QKV kernel) after it.
+constexpr int AT_THREADS = 128;
 constexpr int AT_MAX_GQ = 8;
 constexpr int AT_MAX_SPLITS = 32;
+constexpr int AT_TPS_MAX = 64;  // tokens per CTA tile
 
 inline int attn_tokens_per_split(int max_seq) {
-  int t = 64;
-  while ((max_seq + t - 1) / t > AT_MAX_SPLITS) t *= 2;
+  int t = 16;
+  while ((max_seq + t - 1) / t > AT_MAX_SPLITS && t < AT_TPS_MAX) t *= 2;
   return t;
 }
 
+__device__ __forceinline__ void pdl_wait_ops() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger_ops() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 template <int HD>
-__global__ void __launch_bounds__(AT_WARPS * 32) attn_kernel(const __grid_constant__ gsdlq_attn_job_t J, int tps) {
-  constexpr int E = HD / 32;
+__global__ void __launch_bounds__(AT_THREADS) attn_kernel(const __grid_constant__ gsdlq_attn_job_t J, int tps) {
+  constexpr int ROWB = HD * 2 + 16;  // padded row bytes
+  constexpr int CH = HD / 8;         // 16-byte chunks per row
+  __shared__ __align__(16) uint8_t sk[AT_TPS_MAX * ROWB];
+  __shared__ __align__(16) uint8_t sv[AT_TPS_MAX * ROWB];
+  __shared__ float sq[AT_MAX_GQ * HD];
+  __shared__ float sp[AT_MAX_GQ][AT_TPS_MAX];
+  __shared__ float sm[AT_MAX_GQ], sl[AT_MAX_GQ];
+  __shared__ int s_last;
   const int kvh = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gq = J.n_heads / J.n_kv_heads;
   const int pos = J.pos_dev ? *J.pos_dev : J.pos_val;
-  __shared__ float s_m[AT_WARPS][AT_MAX_GQ], s_l[AT_WARPS][AT_MAX_GQ];
-  __shared__ float s_acc[AT_WARPS][AT_MAX_GQ][HD];
-  __shared__ int s_last;
   const bool pos_ok = pos >= 0 && pos < J.max_seq;
-  if (!pos_ok && threadIdx.x == 0 && kvh == 0 && split == 0) raise_flag(GSDLQ_FLAG_BAD_POS);
   const int len = pos_ok ? pos + 1 : 0;
   const int t0 = split * tps, t1 = min(len, t0 + tps);
-
-  float qv[AT_MAX_GQ][E];
-#pragma unroll
-  for (int g = 0; g < AT_MAX_GQ; ++g)
-#pragma unroll
-    for (int e = 0; e < E; ++e)
-      qv[g][e] = (g < gq) ? J.q[(size_t)(kvh * gq + g) * HD + lane * E + e] : 0.f;
-  float m[AT_MAX_GQ], l[AT_MAX_GQ], acc[AT_MAX_GQ][E];
-#pragma unroll
-  for (int g = 0; g < AT_MAX_GQ; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) acc[g][e] = 0.f;
-  }
+  const int nt = max(0, t1 - t0);
   const size_t tok_stride = (size_t)J.n_kv_heads * HD;
-  for (int t = t0 + warp; t < t1; t += AT_WARPS) {
-    size_t slot;
-    if (J.block_table) {
-      slot = (size_t)J.block_table[t / J.page_size] * J.page_size + (t % J.page_size);
-    } else {
-      slot = (size_t)J.layer * J.max_seq + t;
+  auto row_off = [&](int t) -> size_t {
+    const size_t slot = J.block_table ? (size_t)J.block_table[t / J.page_size] * J.page_size + (t % J.page_size)
+                                      : (size_t)J.layer * J.max_seq + t;
+    return slot * tok_stride + (size_t)kvh * HD;
+  };
+  // rows of earlier positions: independent of the producer kernel
+  for (int i = tid; i < nt * CH; i += AT_THREADS) {
+    const int j = i / CH, c = i - j * CH;
+    if (t0 + j < pos) {
+      const size_t off = row_off(t0 + j) + c * 8;
+      *reinterpret_cast<uint4*>(sk + j * ROWB + c * 16) = *reinterpret_cast<const uint4*>(J.k_cache + off);
+      *reinterpret_cast<uint4*>(sv + j * ROWB + c * 16) = *reinterpret_cast<const uint4*>(J.v_cache + off);
     }
-    const size_t off = slot * tok_stride + (size_t)kvh * HD + lane * E;
-    float kf[E], vf[E];
-    if constexpr (E == 4) {
-      const uint2 kr = *reinterpret_cast<const uint2*>(J.k_cache + off);
-      const uint2 vr = *reinterpret_cast<const uint2*>(J.v_cache + off);
-      kf[0] = h2f(kr.x & 0xffff); kf[1] = h2f(kr.x >> 16); kf[2] = h2f(kr.y & 0xffff); kf[3] = h2f(kr.y >> 16);
-      vf[0] = h2f(vr.x & 0xffff); vf[1] = h2f(vr.x >> 16); vf[2] = h2f(vr.y & 0xffff); vf[3] = h2f(vr.y >> 16);
-    } else {
+  }
+  pdl_wait_ops();
+  if (!pos_ok && tid == 0 && kvh == 0 && split == 0) raise_flag(GSDLQ_FLAG_BAD_POS);
+  for (int i = tid; i < nt * CH; i += AT_THREADS) {
+    const int j = i / CH, c = i - j * CH;
+    if (t0 + j == pos) {
+      const size_t off = row_off(t0 + j) + c * 8;
+      *reinterpret_cast<uint4*>(sk + j * ROWB + c * 16) = *reinterpret_cast<const uint4*>(J.k_cache + off);
+      *reinterpret_cast<uint4*>(sv + j * ROWB + c * 16) = *reinterpret_cast<const uint4*>(J.v_cache + off);
+    }
+  }
+  for (int i = tid; i < gq * HD; i += AT_THREADS) sq[i] = J.q[(size_t)kvh * gq * HD + i];
+  __syncthreads();
+  // scores: thread -> (token j, head subset); each reads its K row in 16-byte chunks
+  {
+    const int j = tid % AT_TPS_MAX, hset = tid / AT_TPS_MAX;  // 2 threads per token
+    if (j < nt) {
+      float acc[AT_MAX_GQ];
 #pragma unroll
-      for (int e = 0; e < E; ++e) { kf[e] = h2f(J.k_cache[off + e]); vf[e] = h2f(J.v_cache[off + e]); }
+      for (int h = 0; h < AT_MAX_GQ; ++h) acc[h] = 0.f;
+      for (int c = 0; c < CH; ++c) {
+        const uint4 kr = *reinterpret_cast<const uint4*>(sk + j * ROWB + c * 16);
+        const uint32_t kw[4] = {kr.x, kr.y, kr.z, kr.w};
+#pragma unroll
+        for (int h = 0; h < AT_MAX_GQ; ++h) {
+          if (h < gq && (h & 1) == hset) {
+            const float* qh = sq + h * HD + c * 8;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              acc[h] = fmaf(qh[2 * k], h2f(kw[k] & 0xffffu), acc[h]);
+              acc[h] = fmaf(qh[2 * k + 1], h2f(kw[k] >> 16), acc[h]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < AT_MAX_GQ; ++h)
+        if (h < gq && (h & 1) == hset) sp[h][j] = acc[h] * J.sm_scale;
+    }
+  }
+  __syncthreads();
+  // softmax of the tile per head (warp w handles heads w, w+4)
+  for (int h = warp; h < gq; h += AT_THREADS / 32) {
+    float mx = -INFINITY;
+    for (int j = lane; j < nt; j += 32) mx = fmaxf(mx, sp[h][j]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int j = lane; j < nt; j += 32) {
+      const float e = expf(sp[h][j] - mx);
+      sp[h][j] = e;
+      sum += e;
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) {
+      sm[h] = mx;
+      sl[h] = sum;
+    }
+  }
+  __syncthreads();
+  // P.V: thread -> (dimension d, head subset)
+  float* part = J.partial + ((size_t)kvh * nsplit + split) * (size_t)gq * (HD + 2);
+  {
+    constexpr int HSETS = AT_THREADS / HD;  // 1 (hd 128), 2 (hd 64), 4 (hd 32)
+    const int d = tid % HD, hs = tid / HD;
+    float acc[AT_MAX_GQ];
+#pragma unroll
+    for (int h = 0; h < AT_MAX_GQ; ++h) acc[h] = 0.f;
+    for (int j = 0; j < nt; ++j) {
+      const float vv = h2f(*reinterpret_cast<const uint16_t*>(sv + j * ROWB + d * 2));
+#pragma unroll
+      for (int h = 0; h < AT_MAX_GQ; ++h)
+        if (h < gq && h % HSETS == hs) acc[h] = fmaf(sp[h][j], vv, acc[h]);
     }
 #pragma unroll
-    for (int g = 0; g < AT_MAX_GQ; ++g) {
-      if (g < gq) {
-        float d = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) d = fmaf(qv[g][e], kf[e], d);
-        d = warp_sum(d);
-        const float s = d * J.sm_scale;
-        const float mn = fmaxf(m[g], s);
-        const float corr = expf(m[g] - mn);
-        const float p = expf(s - mn);
-        l[g] = l[g] * corr + p;
-#pragma unroll
-        for (int e = 0; e < E; ++e) acc[g][e] = fmaf(p, vf[e], acc[g][e] * corr);
-        m[g] = mn;
+    for (int h = 0; h < AT_MAX_GQ; ++h) {
+      if (h < gq && h % HSETS == hs) {
+        part[h * (HD + 2) + d] = acc[h];
+        if (d == 0) {
+          part[h * (HD + 2) + HD] = nt > 0 ? sm[h] : -INFINITY;
+          part[h * (HD + 2) + HD + 1] = nt > 0 ? sl[h] : 0.f;
+        }
       }
     }
   }
-  // combine the warps of this CTA
-#pragma unroll
-  for (int g = 0; g < AT_MAX_GQ; ++g) {
-    if (g < gq) {
-      if (lane == 0) { s_m[warp][g] = m[g]; s_l[warp][g] = l[g]; }
-#pragma unroll
-      for (int e = 0; e < E; ++e) s_acc[warp][g][lane * E + e] = acc[g][e];
-    }
-  }
-  __syncthreads();
-  float* part = J.partial + ((size_t)kvh * nsplit + split) * (size_t)gq * (HD + 2);
-  for (int i = threadIdx.x; i < gq * HD; i += blockDim.x) {
-    const int g = i / HD, d = i - g * HD;
-    float M = -INFINITY;
-    for (int w = 0; w < AT_WARPS; ++w) M = fmaxf(M, s_m[w][g]);
-    float a = 0.f, L = 0.f;
-    for (int w = 0; w < AT_WARPS; ++w) {
-      const float f = (s_m[w][g] == -INFINITY) ? 0.f : expf(s_m[w][g] - M);
-      a += s_acc[w][g][d] * f;
-      L += s_l[w][g] * f;
-    }
-    part[g * (HD + 2) + d] = a;
-    if (d == 0) { part[g * (HD + 2) + HD] = M; part[g * (HD + 2) + HD + 1] = L; }
-  }
-  // last CTA of this kv head combines all splits
+  pdl_trigger_ops();
+  // the last CTA of this kv head combines all splits
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(&J.workspace[kvh], 1u) == (unsigned)nsplit - 1);
+  if (tid == 0) s_last = (atomicAdd(&J.workspace[kvh], 1u) == (unsigned)nsplit - 1);
   __syncthreads();
   if (!s_last) return;
   __threadfence();
   const float* base = J.partial + (size_t)kvh * nsplit * gq * (HD + 2);
-  for (int i = threadIdx.x; i < gq * HD; i += blockDim.x) {
+  const int nact = min(nsplit, (len + tps - 1) / tps);
+  for (int i = tid; i < gq * HD; i += AT_THREADS) {
     const int g = i / HD, d = i - g * HD;
     float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, base[((size_t)s * gq + g) * (HD + 2) + HD]);
-    float a = 0.f, L = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float* ps = base + ((size_t)s * gq + g) * (HD + 2);
-      const float ms = ps[HD];
+    for (int sidx = 0; sidx < nact; ++sidx) M = fmaxf(M, __ldcg(base + ((size_t)sidx * gq + g) * (HD + 2) + HD));
+    float a = 0.f, Ls = 0.f;
+    for (int sidx = 0; sidx < nact; ++sidx) {
+      const float* ps = base + ((size_t)sidx * gq + g) * (HD + 2);
+      const float ms = __ldcg(ps + HD);
       if (ms == -INFINITY) continue;
       const float f = expf(ms - M);
-      a += ps[d] * f;
-      L += ps[HD + 1] * f;
+      a += __ldcg(ps + d) * f;
+      Ls += __ldcg(ps + HD + 1) * f;
     }
-    J.out[(size_t)(kvh * gq + g) * HD + d] = (L > 0.f) ? a / L : 0.f;
+    J.out[(size_t)(kvh * gq + g) * HD + d] = (Ls > 0.f) ? a / Ls : 0.f;
   }
-  if (threadIdx.x == 0) J.workspace[kvh] = 0u;
+  if (tid == 0) J.workspace[kvh] = 0u;
 }
 
 static int attention_launch(const gsdlq_attn_job_t& J, cudaStream_t s) {
   if (!J.q || !J.k_cache || !J.v_cache || !J.out || !J.partial || !J.workspace) return GSDLQ_ERR_INVALID;
-  // the kernel reads 4 fp16 of a key/value row per lane as one 8-byte load
-  if ((reinterpret_cast<uintptr_t>(J.k_cache) | reinterpret_cast<uintptr_t>(J.v_cache)) & 7u) return GSDLQ_ERR_INVALID;
+  // K/V rows are read in 16-byte chunks
+  if ((reinterpret_cast<uintptr_t>(J.k_cache) | reinterpret_cast<uintptr_t>(J.v_cache)) & 15u) return GSDLQ_ERR_INVALID;
   if (J.n_heads <= 0 || J.n_kv_heads <= 0 || J.n_heads % J.n_kv_heads) return GSDLQ_ERR_INVALID;
   if (J.n_heads / J.n_kv_heads > AT_MAX_GQ) return GSDLQ_ERR_UNSUPPORTED;
   if (J.max_seq <= 0 || J.layer < 0) return GSDLQ_ERR_INVALID;
   if (J.block_table && J.page_size <= 0) return GSDLQ_ERR_INVALID;
   if (!J.pos_dev && (J.pos_val < 0 || J.pos_val >= J.max_seq)) return GSDLQ_ERR_INVALID;
   const int tps = attn_tokens_per_split(J.max_seq);
-  dim3 grid(J.n_kv_heads, (J.max_seq + tps - 1) / tps);
-  if (J.head_dim == 128) attn_kernel<128><<<grid, AT_WARPS * 32, 0, s>>>(J, tps);
-  else if (J.head_dim == 64) attn_kernel<64><<<grid, AT_WARPS * 32, 0, s>>>(J, tps);
-  else if (J.head_dim == 32) attn_kernel<32><<<grid, AT_WARPS * 32, 0, s>>>(J, tps);
+  if ((J.max_seq + tps - 1) / tps > 65535) return GSDLQ_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(J.n_kv_heads, (J.max_seq + tps - 1) / tps);
+  cfg.blockDim = dim3(AT_THREADS);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
+  if (J.head_dim == 128) e = cudaLaunchKernelEx(&cfg, attn_kernel<128>, J, tps);
+  else if (J.head_dim == 64) e = cudaLaunchKernelEx(&cfg, attn_kernel<64>, J, tps);
+  else if (J.head_dim == 32) e = cudaLaunchKernelEx(&cfg, attn_kernel<32>, J, tps);
   else return GSDLQ_ERR_UNSUPPORTED;
-  GSDLQ_CUDA_CHECK_LAUNCH();
+  if (e != cudaSuccess) return record_cuda_error(e);
   return GSDLQ_OK;
 }
 
@@ -558,7 +604,7 @@ int gsdlq_gqa_attention(const float* q, const uint16_t* k_cache, const uint16_t*
                         int layer_idx, int pos, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
                         float sm_scale, gsdlq_stream_t stream) {
   if (n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads || max_seq_len <= 0) return GSDLQ_ERR_INVALID;
-  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 7u) return GSDLQ_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u) return GSDLQ_ERR_INVALID;
   size_t pb = 0, wb = 0;
   attention_ws(n_heads, n_kv_heads, head_dim, max_seq_len, &pb, &wb);
   int dev = 0;

@@ -145,8 +145,6 @@ class GSDLQModel:
         self.key = torch.zeros(2, dtype=torch.int64, device=dev)        # greedy argmax key (u64 bits)
         self.out_ids = torch.zeros(max(self.max_seq, 1), dtype=torch.int32, device=dev)
         self.rope_cs = torch.from_numpy(ops.rope_table(self.max_seq, hd, self.rope_theta)).to(dev)
-        n_sites = 4 * Lc + 1
-        self.ws = torch.zeros((n_sites, L.LINEAR_WS_WORDS), dtype=torch.int32, device=dev)
         pb, wb = ops.attention_ws_size(hl, kvl, hd, self.max_seq)
         self.attn_partial = torch.zeros(pb // 4 + 1, **f32)
         self.attn_ws = torch.zeros(wb // 4 + 1, dtype=torch.int32, device=dev)
@@ -168,7 +166,7 @@ class GSDLQModel:
         return n
 
     # ------------------------------------------------------------------ jobs
-    def _job(self, mats, site, input_mode, x=None, norm=None, epilogue=L.EPI_STORE, ys=(), resid=None, layer=0,
+    def _job(self, mats, input_mode, x=None, norm=None, epilogue=L.EPI_STORE, ys=(), resid=None, layer=0,
              argmax=False):
         j = L.LinearJob()
         for i, m in enumerate(mats):
@@ -194,7 +192,6 @@ class GSDLQModel:
         j.layer, j.max_seq, j.head_dim, j.interleaved = layer, self.max_seq, self.head_dim, 1
         j.argmax_key = self.key.data_ptr() if argmax else None
         j.argmax_index_base = self.tp.rank * self.vocab_local if (argmax and self.tp is not None) else 0
-        j.workspace = self.ws[site].data_ptr()
         return j
 
     def _build_jobs(self):
@@ -203,7 +200,7 @@ class GSDLQModel:
             p = f"blk.{l}."
             hx = lambda n: self.hex[p + n + ".weight"]  # noqa: E731
             an, fn = self.norms[p + "attn_norm.weight"], self.norms[p + "ffn_norm.weight"]
-            qkv = self._job([hx("attn_q"), hx("attn_k"), hx("attn_v")], 4 * l,
+            qkv = self._job([hx("attn_q"), hx("attn_k"), hx("attn_v")],
                             L.IN_EMBED if l == 0 else L.IN_RMSNORM, x=self.x, norm=an,
                             epilogue=L.EPI_ROPE_KV, ys=(self.q, None, None), layer=l)
             att = L.AttnJob(q=self.q.data_ptr(), k_cache=self.k_cache.data_ptr(), v_cache=self.v_cache.data_ptr(),
@@ -214,33 +211,48 @@ class GSDLQModel:
             # tensor parallel: rank 0 adds its partial to the residual, the other ranks store their bare
             # partials into x; the all-reduce(sum) that follows leaves x + sum of partials everywhere
             res_epi = L.EPI_RESID if (self.tp is None or self.tp.rank == 0) else L.EPI_STORE
-            o = self._job([hx("attn_output")], 4 * l + 1, L.IN_PLAIN, x=self.att, epilogue=res_epi,
+            o = self._job([hx("attn_output")], L.IN_PLAIN, x=self.att, epilogue=res_epi,
                           ys=(self.x,), resid=self.x)
-            gu = self._job([hx("ffn_gate"), hx("ffn_up")], 4 * l + 2, L.IN_RMSNORM, x=self.x, norm=fn,
+            gu = self._job([hx("ffn_gate"), hx("ffn_up")], L.IN_RMSNORM, x=self.x, norm=fn,
                            epilogue=L.EPI_SWIGLU, ys=(self.h,))
-            dn = self._job([hx("ffn_down")], 4 * l + 3, L.IN_PLAIN, x=self.h, epilogue=res_epi,
+            dn = self._job([hx("ffn_down")], L.IN_PLAIN, x=self.h, epilogue=res_epi,
                            ys=(self.x,), resid=self.x)
             self.layer_jobs.append((qkv, att, o, gu, dn))
-        self.head_job = self._job([self.hex["output.weight"]], 4 * self.n_layers, L.IN_RMSNORM, x=self.x,
+        self.head_job = self._job([self.hex["output.weight"]], L.IN_RMSNORM, x=self.x,
                                   norm=self.norms["output_norm.weight"], epilogue=L.EPI_STORE, ys=(self.logits,),
                                   argmax=True)
+        # Workspaces: consecutive fused-linear launches may overlap (programmatic dependent
+        # launch), so they alternate between two buffers; each launch leaves its own at zero.
+        jobs = [j for lj in self.layer_jobs for j in (lj[0], lj[2], lj[3], lj[4])] + [self.head_job]
+        need = max(ops.linear_ws_size(j) for j in jobs)
+        self.ws = [torch.zeros((need + 15) // 16 * 4, dtype=torch.int32, device=self.device) for _ in range(2)]
+        self.ws_of = {}
+        k = 0
+        for lj in self.layer_jobs:
+            for j in (lj[0], lj[2], lj[3], lj[4]):
+                self.ws_of[id(j)] = self.ws[k % 2]
+                k += 1
+        self.ws_of[id(self.head_job)] = self.ws[k % 2]
+
+    def linear(self, job):
+        ops.linear(job, self.ws_of[id(job)])
 
     # ------------------------------------------------------------------ step
     def _run_layers(self):
         allreduce = self.tp.allreduce if self.tp is not None else None
         for qkv, att, o, gu, dn in self.layer_jobs:
-            ops.linear(qkv)
+            self.linear(qkv)
             ops.attention(att)
-            ops.linear(o)
+            self.linear(o)
             if allreduce:
                 allreduce(self, "o")
-            ops.linear(gu)
-            ops.linear(dn)
+            self.linear(gu)
+            self.linear(dn)
             if allreduce:
                 allreduce(self, "down")
 
     def _run_head(self, advance: bool = True):
-        ops.linear(self.head_job)
+        self.linear(self.head_job)
         if self.tp is not None:
             self.tp.finish_head(self)
         if advance:
@@ -252,8 +264,15 @@ class GSDLQModel:
     def _graph(self, name, fn):
         g = self._graphs.get(name)
         if g is None:
-            fn()  # eager warm-up (sets kernel attributes outside capture)
+            # eager warm-up (sets kernel attributes and NCCL state outside capture); the step's
+            # device-side bookkeeping (token, pos, greedy key) is restored so that the warm-up
+            # leaves no trace and the replay that follows does the real work
+            saved = (self.state.clone(), self.key.clone(), self.out_ids.clone())
+            fn()
             torch.cuda.synchronize(self.device)
+            self.state.copy_(saved[0])
+            self.key.copy_(saved[1])
+            self.out_ids.copy_(saved[2])
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 fn()

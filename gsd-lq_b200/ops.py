@@ -173,8 +173,20 @@ def rope_table(max_seq: int, head_dim: int, theta: float) -> np.ndarray:
     return t
 
 
-def linear(job: L.LinearJob):
-    L.check(_lib().gsdlq_linear(ctypes.byref(job), stream_handle()), "gsdlq_linear")
+def linear_ws_size(job: L.LinearJob) -> int:
+    n = ctypes.c_size_t(0)
+    L.check(_lib().gsdlq_linear_ws_size(ctypes.byref(job), ctypes.byref(n)), "gsdlq_linear_ws_size")
+    return n.value
+
+
+def linear_workspace(job: L.LinearJob, device="cuda") -> torch.Tensor:
+    """A zeroed, 16-byte aligned device workspace large enough for ``job``."""
+    return torch.zeros((linear_ws_size(job) + 15) // 16 * 4, dtype=torch.int32, device=device)
+
+
+def linear(job: L.LinearJob, ws: torch.Tensor):
+    L.check(_lib().gsdlq_linear(ctypes.byref(job), ptr(ws), ws.numel() * ws.element_size(), stream_handle()),
+            "gsdlq_linear")
 
 
 def attention_ws_size(n_heads, n_kv, hd, max_seq) -> tuple[int, int]:

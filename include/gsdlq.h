@@ -151,8 +151,6 @@ typedef struct gsdlq_hexmat {
 #define GSDLQ_IN_EMBED 2    /* input = rmsnorm(f32(embed[*token])) * norm_w; CTA 0 writes the
                                raw row to x_out (the residual stream)                      */
 
-#define GSDLQ_LINEAR_WS_WORDS 64 /* workspace words per fused-linear call site */
-
 /* A fused packed-linear launch: up to three matrices that share one input,
  * the low-rank projection computed inside the same kernel, and an epilogue. */
 typedef struct gsdlq_linear_job {
@@ -178,12 +176,19 @@ typedef struct gsdlq_linear_job {
    * (value, ~index) key; the key must start at 0 */
   unsigned long long *argmax_key;
   int argmax_index_base;      /* added to the row index in the key (vocab-parallel LM head) */
-  unsigned int *workspace;    /* GSDLQ_LINEAR_WS_WORDS words, zero before first use;
-                                 each launch leaves it zero again */
 } gsdlq_linear_job_t;
 
-/* Launch a fused packed linear.  `job` is a HOST pointer (read during the call). */
-int gsdlq_linear(const gsdlq_linear_job_t *job, gsdlq_stream_t stream);
+/* Bytes of device workspace a gsdlq_linear launch of `job` needs (host pointers). */
+int gsdlq_linear_ws_size(const gsdlq_linear_job_t *job, size_t *bytes);
+
+/* Launch a fused packed linear.  `job` is a HOST pointer (read during the call).
+ * `workspace`: device memory of at least gsdlq_linear_ws_size bytes, 16-byte
+ * aligned, zero before its first use; every launch leaves its counters at zero
+ * again, so one workspace serves any number of launches that do not overlap
+ * (two launches that may overlap -- e.g. consecutive launches on a stream, which
+ * use programmatic dependent launch -- need distinct workspaces). */
+int gsdlq_linear(const gsdlq_linear_job_t *job, void *workspace, size_t workspace_bytes,
+                 gsdlq_stream_t stream);
 
 /* Split-KV decode attention.  q is already rotated.  pos is read from *pos_dev
  * when non-NULL (CUDA-graph friendly), else pos_val.  The cache layout is the

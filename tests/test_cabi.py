@@ -49,4 +49,4 @@ def test_argument_errors_before_launch():
     assert lib.gsdlq_rope_and_store_kv(None, None, None, None, None, 0, 0, 1, 1, 64, 16, 1e4, 1, None) == -1
     job = L.LinearJob()
     job.n_mat = 0
-    assert lib.gsdlq_linear(ctypes.byref(job), None) == -1
+    assert lib.gsdlq_linear(ctypes.byref(job), None, 0, None) == -1
