@@ -290,21 +290,28 @@ __device__ void finish_strip(const HexmvParams& P, int s, int lane) {
   const float* base = P.part + (size_t)s * (P.max_seg + 1) * width;
   float v = 0.f;
   if (lane < width) {
-    for (int k = 0; k < nseg; ++k) v += ld_cg_f32(base + (size_t)k * width + lane);
+    float* bw = const_cast<float*>(base);
+    for (int k = 0; k < nseg; ++k) {
+      v += ld_cg_f32(base + (size_t)k * width + lane);
+      bw[(size_t)k * width + lane] = 0.f;
+    }
     v += ld_cg_f32(base + (size_t)P.max_seg * width + lane);  // helper slot: kinks + low rank
+    bw[(size_t)P.max_seg * width + lane] = 0.f;
   }
-  if (lane == 0) P.cnt[s] = 0u;  // ready for the next launch
+  // every consumed slot and the counter go back to zero: the whole workspace is zero between
+  // launches, so launches of any geometry can share it
+  if (lane == 0) P.cnt[s] = 0u;
   strip_epilogue<EPI>(P, strip_info<NMAT>(P, s), v, lane);
 }
 
 // Count `units` toward strip s after this warp's slot writes; the warp completing the
 // strip (G streaming units + 1 helper unit) finishes it.
 template <int EPI, int NMAT>
-__device__ __forceinline__ void arrive(const HexmvParams& P, int s, unsigned units, int lane) {
+__device__ __forceinline__ void arrive(const HexmvParams& P, int s, unsigned units, int lane, bool fence = true) {
+  if (fence) __threadfence();  // every lane that wrote part of the slot orders its stores before the count
   __syncwarp();
   unsigned fin = 0;
   if (lane == 0) {
-    __threadfence();
     const unsigned old = atomicAdd(&P.cnt[s], units);
     fin = (old + units == (unsigned)P.G + 1u);
   }
@@ -332,16 +339,31 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
   const int sc_first = (int)(cta_it0 / G);
   const int sc_n = (cta_it1 > cta_it0) ? (int)((cta_it1 - 1) / G) - sc_first + 1 : 0;
   {
-    // raw fp16 bits: [local strip][mm][row][sc_stride]
-    const int per_strip = NMAT * 16 * G;
-    for (int i = tid; i < sc_n * per_strip; i += blockDim.x) {
-      const int ls = i / per_strip, rem = i - ls * per_strip;
-      const int mm = rem / (16 * G), rem2 = rem - mm * 16 * G;
-      const int rr = rem2 / G, gg = rem2 - rr * G;
-      const StripInfo si = strip_info<NMAT>(P, sc_first + ls);
-      const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
-      const int row = min(si.rbase + rr, M.rows - 1);
-      s_sc[((ls * NMAT + mm) * 16 + rr) * P.sc_stride + gg] = M.scales[(size_t)row * G + gg];
+    // raw fp16 bits: [local strip][mm][row][sc_stride], copied asynchronously (4-byte words when
+    // rows start 4-byte aligned, i.e. G even; 2-byte loads otherwise)
+    const int n_rows = sc_n * NMAT * 16;
+    if ((G & 1) == 0) {
+      const int wpr = G / 2;
+      for (int i = tid; i < n_rows * wpr; i += blockDim.x) {
+        const int rid = i / wpr, wi = i - rid * wpr;
+        const int ls = rid / (NMAT * 16), rem = rid - ls * NMAT * 16;
+        const int mm = rem >> 4, rr = rem & 15;
+        const StripInfo si = strip_info<NMAT>(P, sc_first + ls);
+        const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
+        const int row = min(si.rbase + rr, M.rows - 1);
+        cp_async_4(s_sc + (size_t)rid * P.sc_stride + 2 * wi, M.scales + (size_t)row * G + 2 * wi);
+      }
+      cp_async_commit();
+    } else {
+      for (int i = tid; i < n_rows * G; i += blockDim.x) {
+        const int rid = i / G, gg = i - rid * G;
+        const int ls = rid / (NMAT * 16), rem = rid - ls * NMAT * 16;
+        const int mm = rem >> 4, rr = rem & 15;
+        const StripInfo si = strip_info<NMAT>(P, sc_first + ls);
+        const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
+        const int row = min(si.rbase + rr, M.rows - 1);
+        s_sc[(size_t)rid * P.sc_stride + gg] = __ldg(M.scales + (size_t)row * G + gg);
+      }
     }
   }
   const int w = w_cta0 + warp;
@@ -399,32 +421,46 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
     __syncthreads();
     inv = misc[0];
   }
-  for (int p = tid; p < NP; p += blockDim.x) {
-    float x0, x1;
-    if (J.input_mode == GSDLQ_IN_EMBED) {
-      const uint32_t raw = *reinterpret_cast<const uint32_t*>(J.embed + (size_t)tok * C + 2 * p);
-      x0 = h2f(raw & 0xffffu);
-      x1 = h2f(raw >> 16);
-      if (blockIdx.x == 0 && J.x_out) {
-        J.x_out[2 * p] = x0;
-        J.x_out[2 * p + 1] = x1;
+  // loads of a batch are issued before any shared store, so they overlap (the generic input
+  // pointers could otherwise be assumed to alias shared memory and serialise)
+  constexpr int XB = 8;
+  for (int p0 = tid; p0 < NP; p0 += XB * HX_THREADS) {
+    float2 xv[XB], wv[XB];
+#pragma unroll
+    for (int k = 0; k < XB; ++k) {
+      const int p = p0 + k * HX_THREADS;
+      if (p < NP) {
+        if (J.input_mode == GSDLQ_IN_EMBED) {
+          const uint32_t raw = __ldg(reinterpret_cast<const unsigned int*>(J.embed + (size_t)tok * C) + p);
+          xv[k] = make_float2(h2f(raw & 0xffffu), h2f(raw >> 16));
+        } else {
+          xv[k] = __ldg(reinterpret_cast<const float2*>(J.x) + p);
+        }
+        wv[k] = (J.input_mode != GSDLQ_IN_PLAIN) ? __ldg(reinterpret_cast<const float2*>(J.norm_w) + p)
+                                                 : make_float2(1.f, 1.f);
       }
-    } else {
-      const float2 v = reinterpret_cast<const float2*>(J.x)[p];
-      x0 = v.x;
-      x1 = v.y;
     }
-    if (J.input_mode != GSDLQ_IN_PLAIN) {
-      x0 = __fmul_rn(__fmul_rn(x0, inv), J.norm_w[2 * p]);
-      x1 = __fmul_rn(__fmul_rn(x1, inv), J.norm_w[2 * p + 1]);
+#pragma unroll
+    for (int k = 0; k < XB; ++k) {
+      const int p = p0 + k * HX_THREADS;
+      if (p < NP) {
+        float x0 = xv[k].x, x1 = xv[k].y;
+        if (J.input_mode == GSDLQ_IN_EMBED && blockIdx.x == 0 && J.x_out)
+          reinterpret_cast<float2*>(J.x_out)[p] = make_float2(x0, x1);
+        if (J.input_mode != GSDLQ_IN_PLAIN) {
+          x0 = __fmul_rn(__fmul_rn(x0, inv), wv[k].x);
+          x1 = __fmul_rn(__fmul_rn(x1, inv), wv[k].y);
+        }
+        const float b = fmaf(0.8660254037844386f, x1, 0.5f * x0);
+        uint32_t h, l;
+        split_bf16x2(x0, b, h, l);
+        const int g = p >> 5, i = p & 31;
+        *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g) + 4 * i) = h;
+        *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g + 1) + 4 * i) = l;
+      }
     }
-    const float b = fmaf(0.8660254037844386f, x1, 0.5f * x0);
-    uint32_t h, l;
-    split_bf16x2(x0, b, h, l);
-    const int g = p >> 5, i = p & 31;
-    *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g) + 4 * i) = h;
-    *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g + 1) + 4 * i) = l;
   }
+  cp_async_wait_all();  // the staged scale window
   __syncthreads();
 
   if (warp >= HX_STREAM) {
@@ -518,7 +554,10 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
           slot[mm * 16 + gl + 8] = acc[mm][1];
         }
       }
-      arrive<EPI, NMAT>(P, s, (unsigned)(g1 - g0), lane);
+      // the count is deferred to the end of the range: a fence here would wait for the code
+      // prefetches in flight
+      (void)g0;
+      (void)g1;
     };
     for (long long base = it0; base < it1; base += HX_PF) {
 #pragma unroll
@@ -568,7 +607,17 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         }
       }
     }
-    if (it1 > it0) emit(seg_s, seg_g0, (cur_g == 0 && cur_s > seg_s) ? G : cur_g);
+    if (it1 > it0) {
+      emit(seg_s, seg_g0, (cur_g == 0 && cur_s > seg_s) ? G : cur_g);
+      // one fence for all of this warp's slot stores (no loads in flight any more), then one
+      // count per strip the range touched
+      __threadfence();
+      const int s_a = (int)(it0 / G), s_b = (int)((it1 - 1) / G);
+      for (int s = s_a; s <= s_b; ++s) {
+        const long long a = max(it0, (long long)s * G), b = min(it1, (long long)s * G + G);
+        arrive<EPI, NMAT>(P, s, (unsigned)(b - a), lane, false);
+      }
+    }
   }
 
   pdl_launch_dependents();

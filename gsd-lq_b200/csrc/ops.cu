@@ -168,26 +168,29 @@ __global__ void __launch_bounds__(AT_THREADS) attn_kernel(const __grid_constant_
                                       : (size_t)J.layer * J.max_seq + t;
     return slot * tok_stride + (size_t)kvh * HD;
   };
-  // rows of earlier positions: independent of the producer kernel
+  // rows of earlier positions: independent of the producer kernel (asynchronous copies)
   for (int i = tid; i < nt * CH; i += AT_THREADS) {
     const int j = i / CH, c = i - j * CH;
     if (t0 + j < pos) {
       const size_t off = row_off(t0 + j) + c * 8;
-      *reinterpret_cast<uint4*>(sk + j * ROWB + c * 16) = *reinterpret_cast<const uint4*>(J.k_cache + off);
-      *reinterpret_cast<uint4*>(sv + j * ROWB + c * 16) = *reinterpret_cast<const uint4*>(J.v_cache + off);
+      cp_async_16(sk + j * ROWB + c * 16, J.k_cache + off);
+      cp_async_16(sv + j * ROWB + c * 16, J.v_cache + off);
     }
   }
+  cp_async_commit();
   pdl_wait_ops();
   if (!pos_ok && tid == 0 && kvh == 0 && split == 0) raise_flag(GSDLQ_FLAG_BAD_POS);
   for (int i = tid; i < nt * CH; i += AT_THREADS) {
     const int j = i / CH, c = i - j * CH;
     if (t0 + j == pos) {
       const size_t off = row_off(t0 + j) + c * 8;
-      *reinterpret_cast<uint4*>(sk + j * ROWB + c * 16) = *reinterpret_cast<const uint4*>(J.k_cache + off);
-      *reinterpret_cast<uint4*>(sv + j * ROWB + c * 16) = *reinterpret_cast<const uint4*>(J.v_cache + off);
+      cp_async_16(sk + j * ROWB + c * 16, J.k_cache + off);
+      cp_async_16(sv + j * ROWB + c * 16, J.v_cache + off);
     }
   }
-  for (int i = tid; i < gq * HD; i += AT_THREADS) sq[i] = J.q[(size_t)kvh * gq * HD + i];
+  cp_async_commit();
+  for (int i = tid; i < gq * HD; i += AT_THREADS) sq[i] = __ldg(J.q + (size_t)kvh * gq * HD + i);
+  cp_async_wait_all();
   __syncthreads();
   // scores: thread -> (token j, head subset); each reads its K row in 16-byte chunks
   {

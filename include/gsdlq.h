@@ -183,10 +183,11 @@ int gsdlq_linear_ws_size(const gsdlq_linear_job_t *job, size_t *bytes);
 
 /* Launch a fused packed linear.  `job` is a HOST pointer (read during the call).
  * `workspace`: device memory of at least gsdlq_linear_ws_size bytes, 16-byte
- * aligned, zero before its first use; every launch leaves its counters at zero
- * again, so one workspace serves any number of launches that do not overlap
- * (two launches that may overlap -- e.g. consecutive launches on a stream, which
- * use programmatic dependent launch -- need distinct workspaces). */
+ * aligned, all zero before its first use.  Every launch leaves the bytes it used
+ * at zero again, so one workspace serves any number of launches, of any shape,
+ * that do not overlap in time.  Two launches that may overlap -- consecutive
+ * launches on one stream, which use programmatic dependent launch -- need
+ * distinct workspaces. */
 int gsdlq_linear(const gsdlq_linear_job_t *job, void *workspace, size_t workspace_bytes,
                  gsdlq_stream_t stream);
 
