@@ -50,7 +50,6 @@ namespace gsdlq {
 constexpr int HX_WARPS = 16;
 constexpr int HX_STREAM = 14;
 constexpr int HX_THREADS = HX_WARPS * kWarp;
-constexpr int HX_TAB_BYTES = 256 * 256;
 constexpr int HX_PF = 6;  // groups of codes kept in flight per streaming warp
 
 // control words at the start of the workspace
@@ -94,22 +93,35 @@ inline size_t hexmv_ws_bytes_for(int n_strips, int max_seg, int nmat) {
 }
 
 // ---- shared memory --------------------------------------------------------------------
+// The decode table sits at the absolute shared-window address 0x10000 so that one byte
+// permute builds a lookup address from a code byte (bits 8..15), the lane (bits 2..6) and
+// the constant 0x01 (bits 16..23).  Dynamic shared memory starts at a small offset B (the
+// system-reserved bytes); the buffers below the table use [0, 0x10000 - B):
+//   activation-split overflow chunks | staged scale window | misc
+// and the fp32 input xf follows the table.  The host sizes the allocation for B <= 4 KB;
+// the kernel checks B and raises GSDLQ_FLAG_UNSUPPORTED if the assumption fails.
+constexpr uint32_t HX_TAB_ABS = 0x10000u;
+constexpr int HX_BASE_MAX = 4096;
+
 struct HxLayout {
-  int sc_off, misc_off, total;
+  int sc_off, misc_off, low_end;
 };
 
 __host__ __device__ inline HxLayout hx_layout(int ovf_bytes, int sc_strips, int nmat, int sc_stride) {
   HxLayout L;
-  L.sc_off = HX_TAB_BYTES + ovf_bytes;
+  L.sc_off = ovf_bytes;
   const int sc_bytes = sc_strips * nmat * 16 * sc_stride * 2;
   L.misc_off = L.sc_off + ((sc_bytes + 15) & ~15);
-  L.total = L.misc_off + 64 * 4;
+  L.low_end = L.misc_off + 64 * 4;
   return L;
 }
 
-// byte offset of the 128-byte activation-split chunk `ch` (chunk 2g = hi words of group g, 2g+1 = lo)
-__device__ __forceinline__ uint32_t xs_chunk(int ch) {
-  return ch < 256 ? (uint32_t)ch * 256u + 128u : (uint32_t)HX_TAB_BYTES + (uint32_t)(ch - 256) * 128u;
+inline int hx_dyn_smem(int cols) { return (int)(2 * HX_TAB_ABS) + 4 * cols + 64; }
+
+// dynamic-smem offset of the 128-byte activation-split chunk `ch` (chunk 2g = hi words of
+// group g, 2g+1 = lo words); the first 256 chunks fill the free halves of the table rows
+__device__ __forceinline__ uint32_t xs_chunk(int ch, uint32_t tab_off) {
+  return ch < 256 ? tab_off + (uint32_t)ch * 256u + 128u : (uint32_t)(ch - 256) * 128u;
 }
 
 // (r0, r1) of code c in the radius-R enumeration (r0 outer, r1 inner, |r0+r1| <= R).
@@ -127,7 +139,7 @@ __device__ __forceinline__ bool lattice_of_code(int c, int R, int& r0, int& r1) 
   return false;
 }
 
-__device__ __forceinline__ void build_decode_table(uint8_t* smem, const HexmvParams& P) {
+__device__ __forceinline__ void build_decode_table(uint8_t* tab, const HexmvParams& P) {
   const int R = P.job.mat[0].radius;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) {
     int r0 = 0, r1 = 0;
@@ -152,32 +164,36 @@ __device__ __forceinline__ void build_decode_table(uint8_t* smem, const HexmvPar
     if (!ok) r0 = r1 = 0;
     const uint32_t e = pack_bf16x2((float)r0, (float)r1);
     const uint4 v = make_uint4(e, e, e, e);
-    uint4* row = reinterpret_cast<uint4*>(smem + i * 256);
+    uint4* row = reinterpret_cast<uint4*>(tab + i * 256);
 #pragma unroll
     for (int w = 0; w < 8; ++w) row[w] = v;
   }
 }
 
-__device__ __forceinline__ uint32_t tab_lookup(const uint8_t* smem, uint32_t word, uint32_t lane4, uint32_t sel) {
-  const uint32_t off = __byte_perm(word, lane4, sel);
-  return *reinterpret_cast<const uint32_t*>(smem + off);
+// Decode lookup: PRMT assembles the absolute shared address 0x10000 | code << 8 | lane << 2
+// (lane4x = lane*4 | 0x0100 supplies bytes 0 and 2), one 32-bit shared load reads the entry.
+__device__ __forceinline__ uint32_t tab_lookup(uint32_t word, uint32_t lane4x, uint32_t sel) {
+  const uint32_t addr = __byte_perm(word, lane4x, sel);
+  uint32_t r;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(r) : "r"(addr));
+  return r;
 }
 
 // one 64-column scale group of one 16-row strip: 4 MMAs; returns hi+lo sums for rows g, g+8
-__device__ __forceinline__ void group_mma(const uint8_t* smem, uint2 ca, uint2 cb, const uint32_t (&bq)[8],
-                                          uint32_t lane4, float& r_g, float& r_h) {
+__device__ __forceinline__ void group_mma(uint2 ca, uint2 cb, const uint32_t (&bq)[8], uint32_t lane4x, float& r_g,
+                                          float& r_h) {
   float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t wa = (j < 2) ? ca.x : ca.y;
     const uint32_t wb = (j < 2) ? cb.x : cb.y;
     const uint32_t k0 = 2 * (j & 1);
-    const uint32_t s0 = 0x5504u | (k0 << 4), s1 = 0x5504u | ((k0 + 1) << 4);
+    const uint32_t s0 = 0x6504u | (k0 << 4), s1 = 0x6504u | ((k0 + 1) << 4);
     uint32_t a[4];
-    a[0] = tab_lookup(smem, wa, lane4, s0);  // row g,   pair 8q+2j
-    a[1] = tab_lookup(smem, wb, lane4, s0);  // row g+8, pair 8q+2j
-    a[2] = tab_lookup(smem, wa, lane4, s1);  // row g,   pair 8q+2j+1
-    a[3] = tab_lookup(smem, wb, lane4, s1);  // row g+8, pair 8q+2j+1
+    a[0] = tab_lookup(wa, lane4x, s0);  // row g,   pair 8q+2j
+    a[1] = tab_lookup(wb, lane4x, s0);  // row g+8, pair 8q+2j
+    a[2] = tab_lookup(wa, lane4x, s1);  // row g,   pair 8q+2j+1
+    a[3] = tab_lookup(wb, lane4x, s1);  // row g+8, pair 8q+2j+1
     mma_bf16_16816(d, a, bq[2 * j], bq[2 * j + 1], d);
   }
   r_g = d[0] + d[1];
@@ -192,13 +208,6 @@ __device__ __forceinline__ float ld_cg_f32(const float* p) {
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
-
-// transformed input element c (after the RMSNorm / embedding prologue), from global memory
-__device__ __forceinline__ float input_at(const gsdlq_linear_job_t& J, int c, int tok, float inv) {
-  if (J.input_mode == GSDLQ_IN_PLAIN) return J.x[c];
-  const float raw = (J.input_mode == GSDLQ_IN_EMBED) ? h2f(J.embed[(size_t)tok * J.mat[0].cols + c]) : J.x[c];
-  return __fmul_rn(__fmul_rn(raw, inv), J.norm_w[c]);
-}
 
 struct StripInfo {
   int m0;     // matrix of the strip (the first of the pair in SwiGLU mode)
@@ -327,12 +336,20 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gl = lane >> 2, q = lane & 3;
   const int C = P.cols, G = P.G, NP = P.NP;
+  const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  if (sbase > (uint32_t)HX_BASE_MAX || (sbase & 15u)) {  // the layout's assumption on the reserved bytes
+    if (tid == 0) raise_flag(GSDLQ_FLAG_UNSUPPORTED);
+    return;
+  }
+  const uint32_t tab_off = HX_TAB_ABS - sbase;
+  uint8_t* tab = smem + tab_off;
+  float* xf = reinterpret_cast<float*>(smem + tab_off + HX_TAB_ABS);
   const HxLayout LY = hx_layout(P.ovf_bytes, P.sc_strips, NMAT, P.sc_stride);
   uint16_t* s_sc = reinterpret_cast<uint16_t*>(smem + LY.sc_off);
   float* misc = reinterpret_cast<float*>(smem + LY.misc_off);  // [0] 1/rms, [1..16] reduction
 
   // ---- 1. independent prologue: decode table, this CTA's scale window, first code prefetches
-  build_decode_table(smem, P);
+  build_decode_table(tab, P);
   const int w_cta0 = blockIdx.x * HX_STREAM;
   const long long cta_it0 = it_begin(min(w_cta0, P.W), P.T, P.W);
   const long long cta_it1 = it_begin(min(w_cta0 + HX_STREAM, P.W), P.T, P.W);
@@ -344,7 +361,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
     const int n_rows = sc_n * NMAT * 16;
     if ((G & 1) == 0) {
       const int wpr = G / 2;
-      for (int i = tid; i < n_rows * wpr; i += blockDim.x) {
+      for (int i = tid; i < n_rows * wpr; i += HX_THREADS) {
         const int rid = i / wpr, wi = i - rid * wpr;
         const int ls = rid / (NMAT * 16), rem = rid - ls * NMAT * 16;
         const int mm = rem >> 4, rr = rem & 15;
@@ -355,7 +372,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       }
       cp_async_commit();
     } else {
-      for (int i = tid; i < n_rows * G; i += blockDim.x) {
+      for (int i = tid; i < n_rows * G; i += HX_THREADS) {
         const int rid = i / G, gg = i - rid * G;
         const int ls = rid / (NMAT * 16), rem = rid - ls * NMAT * 16;
         const int mm = rem >> 4, rr = rem & 15;
@@ -371,29 +388,42 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
   const long long it0 = streamer ? it_begin(w, P.T, P.W) : 0;
   const long long it1 = streamer ? it_begin(w + 1, P.T, P.W) : 0;
   uint2 pf[NMAT][HX_PF][2];  // [matrix][ring][row g / row g+8]
-  // prefetch cursor: (strip, group) of the next iteration to prefetch
+  // prefetch cursor: pointers to this lane's 8 code bytes of the next iteration to prefetch
   int pf_s = (int)(it0 / G), pf_g = (int)(it0 - (long long)pf_s * G);
-  auto issue = [&](int slot_i) {
+  const uint8_t* pfa[NMAT];
+  const uint8_t* pfb[NMAT];
+  auto seek = [&]() {
     const StripInfo si = strip_info<NMAT>(P, pf_s);
 #pragma unroll
     for (int mm = 0; mm < NMAT; ++mm) {
       const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
       const int ra = min(si.rbase + gl, M.rows - 1), rb = min(si.rbase + gl + 8, M.rows - 1);
-      const uint8_t* pa = M.codes + (size_t)ra * NP + pf_g * 32 + q * 8;
-      const uint8_t* pb = M.codes + (size_t)rb * NP + pf_g * 32 + q * 8;
-      pf[mm][slot_i][0] = ldg_stream_u2(pa);
-      pf[mm][slot_i][1] = ldg_stream_u2(pb);
+      pfa[mm] = M.codes + (size_t)ra * NP + pf_g * 32 + q * 8;
+      pfb[mm] = M.codes + (size_t)rb * NP + pf_g * 32 + q * 8;
+    }
+  };
+  auto issue = [&](int slot_i) {
+#pragma unroll
+    for (int mm = 0; mm < NMAT; ++mm) {
+      pf[mm][slot_i][0] = ldg_stream_u2(pfa[mm]);
+      pf[mm][slot_i][1] = ldg_stream_u2(pfb[mm]);
+      pfa[mm] += 32;
+      pfb[mm] += 32;
     }
     if (++pf_g == G) {
       pf_g = 0;
       ++pf_s;
+      seek();
     }
   };
+  if (streamer) {
+    seek();
 #pragma unroll
-  for (int i = 0; i < HX_PF; ++i)
-    if (it0 + i < it1) issue(i);
+    for (int i = 0; i < HX_PF; ++i)
+      if (it0 + i < it1) issue(i);
+  }
 
-  // ---- 2. wait for the producer of x, then stage the input splits --------------------------
+  // ---- 2. wait for the producer of x, then stage the input (fp32 and bf16 splits) ----------
   pdl_wait();
   int tok = 0;
   if (J.input_mode == GSDLQ_IN_EMBED) {
@@ -406,8 +436,8 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
   float inv = 1.f;
   if (J.input_mode != GSDLQ_IN_PLAIN) {
     float ss = 0.f;
-    for (int c = tid; c < C; c += blockDim.x) {
-      const float v = (J.input_mode == GSDLQ_IN_EMBED) ? h2f(J.embed[(size_t)tok * C + c]) : J.x[c];
+    for (int c = tid; c < C; c += HX_THREADS) {
+      const float v = (J.input_mode == GSDLQ_IN_EMBED) ? h2f(__ldg(J.embed + (size_t)tok * C + c)) : __ldg(J.x + c);
       ss += v * v;
     }
     ss = warp_sum(ss);
@@ -451,12 +481,16 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
           x0 = __fmul_rn(__fmul_rn(x0, inv), wv[k].x);
           x1 = __fmul_rn(__fmul_rn(x1, inv), wv[k].y);
         }
+        reinterpret_cast<float2*>(xf)[p] = make_float2(x0, x1);
         const float b = fmaf(0.8660254037844386f, x1, 0.5f * x0);
         uint32_t h, l;
         split_bf16x2(x0, b, h, l);
+        // pair i of group g: hi word at i*4 of chunk 2g; lo word in chunk 2g+1 with the two
+        // 16-byte halves of each 32-byte lane segment swapped (see the B-fragment loads)
         const int g = p >> 5, i = p & 31;
-        *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g) + 4 * i) = h;
-        *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g + 1) + 4 * i) = l;
+        const int ilo = (i & ~7) | ((i + 4) & 7);
+        *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g, tab_off) + 4 * i) = h;
+        *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g + 1, tab_off) + 4 * ilo) = l;
       }
     }
   }
@@ -474,15 +508,21 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       int m = 0, j = (int)t;
       while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
       const gsdlq_hexmat_t& M = J.mat[m];
-      const uint16_t* vt = M.Vt + (size_t)j * C;
+      const uint4* vt = reinterpret_cast<const uint4*>(M.Vt + (size_t)j * C);
       float acc = 0.f;
-      for (int c = lane * 8; c < C; c += 256) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(vt + c);
-        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+      for (int c8 = lane; c8 < C / 8; c8 += 4 * 32) {
+        uint4 raw[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          acc += input_at(J, c + 2 * k, tok, inv) * h2f(wv[k] & 0xffffu);
-          acc += input_at(J, c + 2 * k + 1, tok, inv) * h2f(wv[k] >> 16);
+        for (int u = 0; u < 4; ++u) raw[u] = (c8 + 32 * u < C / 8) ? __ldg(vt + c8 + 32 * u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (c8 + 32 * u < C / 8) {
+            const float4* xp = reinterpret_cast<const float4*>(xf + 8 * (c8 + 32 * u));
+            const float4 a = xp[0], b = xp[1];
+            acc += a.x * h2f(raw[u].x & 0xffffu) + a.y * h2f(raw[u].x >> 16) + a.z * h2f(raw[u].y & 0xffffu) +
+                   a.w * h2f(raw[u].y >> 16) + b.x * h2f(raw[u].z & 0xffffu) + b.y * h2f(raw[u].z >> 16) +
+                   b.z * h2f(raw[u].w & 0xffffu) + b.w * h2f(raw[u].w >> 16);
+          }
         }
       }
       acc = warp_sum(acc);
@@ -510,20 +550,20 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       const int row = si.rbase + r;
       float v = 0.f;
       if (row < M.rows) {
-        const uint32_t e0 = M.row_ptr[row], e1 = M.row_ptr[row + 1];
+        const uint32_t e0 = __ldg(M.row_ptr + row), e1 = __ldg(M.row_ptr + row + 1);
         constexpr int step = (NMAT == 2) ? 1 : 2;
         for (uint32_t e = e0 + (NMAT == 2 ? 0 : hi); e < e1; e += step) {
-          const int col = M.kink_cols[e];
-          if (col < C) v += M.kink_deltas[e] * input_at(J, col, tok, inv);
+          const int col = __ldg(M.kink_cols + e);
+          if (col < C) v += __ldg(M.kink_deltas + e) * xf[col];
           else raise_flag(GSDLQ_FLAG_BAD_KINK);
         }
         if (M.k_dim > 0 && (NMAT == 2 || hi == 0)) {
           const uint16_t* ur = M.U + (size_t)row * M.k_dim;
           if (P.tmp_k_ext) {
-            for (int jj = 0; jj < M.k_dim; ++jj) v += h2f(ur[jj]) * P.tmp_k_ext[jj];
+            for (int jj = 0; jj < M.k_dim; ++jj) v += h2f(__ldg(ur + jj)) * __ldg(P.tmp_k_ext + jj);
           } else {
             const volatile float* tk = reinterpret_cast<volatile float*>(ctl) + CTL_TMPK + (si.m0 + mm) * 16;
-            for (int jj = 0; jj < M.k_dim; ++jj) v += h2f(ur[jj]) * tk[jj];
+            for (int jj = 0; jj < M.k_dim; ++jj) v += h2f(__ldg(ur + jj)) * tk[jj];
           }
         }
       }
@@ -534,16 +574,17 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
     }
   } else if (streamer) {
     // ---- streaming warps --------------------------------------------------------------
-    const uint32_t lane4 = (uint32_t)lane * 4u;
-    // B fragments: lanes gl == 0 read the hi chunk, gl == 1 the lo chunk; the two 16-byte
-    // halves are read in opposite orders so that the 8 active lanes hit 32 distinct banks
-    const int bsel = gl & 1;
+    const uint32_t lane4x = (uint32_t)lane * 4u | 0x0100u;
+    // B fragments: lane (gl, q), gl < 2, reads the hi (gl 0) or lo (gl 1) chunk of the group; the
+    // lo chunk stores each lane segment's halves swapped, so the 8 active lanes of each 16-byte
+    // load touch 32 distinct banks and both lane groups receive pairs 0-3 first
+    const uint32_t boff0 = (uint32_t)(q * 32 + 16 * gl), boff1 = (uint32_t)(q * 32 + 16 * (1 - gl));
     int cur_s = (int)(it0 / G), cur_g = (int)(it0 - (long long)cur_s * G);
-    int seg_s = cur_s, seg_g0 = cur_g;
+    int seg_s = cur_s;
     float acc[NMAT][2];
 #pragma unroll
     for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
-    auto emit = [&](int s, int g0, int g1) {
+    auto emit = [&](int s) {
       const int seg = w - warp_of((long long)s * G, P.T, P.W);
       constexpr int width = NMAT * 16;
       float* slot = P.part + ((size_t)s * (P.max_seg + 1) + seg) * width;
@@ -554,10 +595,6 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
           slot[mm * 16 + gl + 8] = acc[mm][1];
         }
       }
-      // the count is deferred to the end of the range: a fence here would wait for the code
-      // prefetches in flight
-      (void)g0;
-      (void)g1;
     };
     for (long long base = it0; base < it1; base += HX_PF) {
 #pragma unroll
@@ -565,9 +602,8 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         const long long it = base + i;
         if (it < it1) {
           if (cur_s != seg_s) {
-            emit(seg_s, seg_g0, G);
+            emit(seg_s);
             seg_s = cur_s;
-            seg_g0 = cur_g;
 #pragma unroll
             for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
           }
@@ -580,12 +616,11 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
           if (it + HX_PF < it1) issue(i);
           uint32_t bq[8];
           if (gl < 2) {
-            const uint8_t* src = smem + xs_chunk(2 * cur_g + bsel) + q * 32;
-            const uint4 v0 = *reinterpret_cast<const uint4*>(src + 16 * bsel);
-            const uint4 v1 = *reinterpret_cast<const uint4*>(src + 16 * (1 - bsel));
-            const uint4 lo4 = bsel ? v1 : v0, hi4 = bsel ? v0 : v1;
-            bq[0] = lo4.x; bq[1] = lo4.y; bq[2] = lo4.z; bq[3] = lo4.w;
-            bq[4] = hi4.x; bq[5] = hi4.y; bq[6] = hi4.z; bq[7] = hi4.w;
+            const uint8_t* src = smem + xs_chunk(2 * cur_g + gl, tab_off);
+            const uint4 v0 = *reinterpret_cast<const uint4*>(src + boff0);
+            const uint4 v1 = *reinterpret_cast<const uint4*>(src + boff1);
+            bq[0] = v0.x; bq[1] = v0.y; bq[2] = v0.z; bq[3] = v0.w;
+            bq[4] = v1.x; bq[5] = v1.y; bq[6] = v1.z; bq[7] = v1.w;
           } else {
 #pragma unroll
             for (int t = 0; t < 8; ++t) bq[t] = 0u;
@@ -596,7 +631,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
             const uint16_t* sr = s_sc + ((ls * NMAT + mm) * 16) * P.sc_stride + cur_g;
             const float sa = h2f(sr[gl * P.sc_stride]), sb = h2f(sr[(gl + 8) * P.sc_stride]);
             float rg, rh;
-            group_mma(smem, cur[mm][0], cur[mm][1], bq, lane4, rg, rh);
+            group_mma(cur[mm][0], cur[mm][1], bq, lane4x, rg, rh);
             acc[mm][0] = fmaf(sa, rg, acc[mm][0]);
             acc[mm][1] = fmaf(sb, rh, acc[mm][1]);
           }
@@ -608,9 +643,10 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       }
     }
     if (it1 > it0) {
-      emit(seg_s, seg_g0, (cur_g == 0 && cur_s > seg_s) ? G : cur_g);
-      // one fence for all of this warp's slot stores (no loads in flight any more), then one
-      // count per strip the range touched
+      emit(seg_s);
+      // the counts are deferred to the end of the range: a fence mid-range would wait for the code
+      // prefetches in flight.  One fence covers all of this warp's slot stores, then one count per
+      // strip the range touched.
       __threadfence();
       const int s_a = (int)(it0 / G), s_b = (int)((it1 - 1) / G);
       for (int s = s_a; s <= s_b; ++s) {
@@ -696,7 +732,8 @@ static int hexmv_plan(HexmvParams& P) {
 template <int EPI>
 static int hexmv_launch_t(const HexmvParams& P, cudaStream_t s) {
   const HxLayout LY = hx_layout(P.ovf_bytes, P.sc_strips, P.nmat, P.sc_stride);
-  if (LY.total > 227 * 1024) return GSDLQ_ERR_UNSUPPORTED;
+  const int dyn = hx_dyn_smem(P.cols);
+  if (LY.low_end > (int)HX_TAB_ABS - HX_BASE_MAX || dyn > 227 * 1024) return GSDLQ_ERR_UNSUPPORTED;
   static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
@@ -709,7 +746,7 @@ static int hexmv_launch_t(const HexmvParams& P, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(HX_THREADS);
-  cfg.dynamicSmemBytes = LY.total;
+  cfg.dynamicSmemBytes = dyn;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

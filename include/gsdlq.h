@@ -44,6 +44,7 @@ extern "C" {
 #define GSDLQ_FLAG_BAD_TABLE 0x8u  /* xy_table entry is not an A2 lattice point */
 #define GSDLQ_FLAG_TIMEOUT 0x10u   /* a bounded device-side wait gave up */
 #define GSDLQ_FLAG_BAD_TOKEN 0x20u /* token id >= vocab: embedding row skipped */
+#define GSDLQ_FLAG_UNSUPPORTED 0x40u /* a kernel found a device limit it was not built for and did nothing */
 
 typedef void *gsdlq_stream_t;
 
