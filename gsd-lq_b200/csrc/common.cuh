@@ -90,10 +90,11 @@ __device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gsrc) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// D = A(16x16 bf16, row) * B(16x8 bf16, col) + C, fp32 accumulate.
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + C, fp32 accumulate.  Not volatile: a pure
+// function of its operands, so the compiler may interleave independent MMAs and loads.
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
                                                const float (&c)[4]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%11,%12,%13};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])

@@ -172,32 +172,39 @@ __device__ __forceinline__ void build_decode_table(uint8_t* tab, const HexmvPara
 
 // Decode lookup: PRMT assembles the absolute shared address 0x10000 | code << 8 | lane << 2
 // (lane4x = lane*4 | 0x0100 supplies bytes 0 and 2), one 32-bit shared load reads the entry.
+// The load is not volatile (the table is constant after the prologue barrier), so lookups of
+// different k-steps and groups can be scheduled around the MMAs; lane4x is derived from a
+// shared-memory read made after that barrier, which keeps every lookup behind it.
 __device__ __forceinline__ uint32_t tab_lookup(uint32_t word, uint32_t lane4x, uint32_t sel) {
   const uint32_t addr = __byte_perm(word, lane4x, sel);
   uint32_t r;
-  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(r) : "r"(addr));
+  asm("ld.shared.b32 %0, [%1];" : "=r"(r) : "r"(addr));
   return r;
 }
 
 // one 64-column scale group of one 16-row strip: 4 MMAs; returns hi+lo sums for rows g, g+8
 __device__ __forceinline__ void group_mma(uint2 ca, uint2 cb, const uint32_t (&bq)[8], uint32_t lane4x, float& r_g,
                                           float& r_h) {
-  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  // two independent accumulator chains (k-steps 0,2 and 1,3) halve the MMA dependency depth
+  float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+  uint32_t a[4][4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t wa = (j < 2) ? ca.x : ca.y;
     const uint32_t wb = (j < 2) ? cb.x : cb.y;
     const uint32_t k0 = 2 * (j & 1);
     const uint32_t s0 = 0x6504u | (k0 << 4), s1 = 0x6504u | ((k0 + 1) << 4);
-    uint32_t a[4];
-    a[0] = tab_lookup(wa, lane4x, s0);  // row g,   pair 8q+2j
-    a[1] = tab_lookup(wb, lane4x, s0);  // row g+8, pair 8q+2j
-    a[2] = tab_lookup(wa, lane4x, s1);  // row g,   pair 8q+2j+1
-    a[3] = tab_lookup(wb, lane4x, s1);  // row g+8, pair 8q+2j+1
-    mma_bf16_16816(d, a, bq[2 * j], bq[2 * j + 1], d);
+    a[j][0] = tab_lookup(wa, lane4x, s0);  // row g,   pair 8q+2j
+    a[j][1] = tab_lookup(wb, lane4x, s0);  // row g+8, pair 8q+2j
+    a[j][2] = tab_lookup(wa, lane4x, s1);  // row g,   pair 8q+2j+1
+    a[j][3] = tab_lookup(wb, lane4x, s1);  // row g+8, pair 8q+2j+1
   }
-  r_g = d[0] + d[1];
-  r_h = d[2] + d[3];
+  mma_bf16_16816(d0, a[0], bq[0], bq[1], d0);
+  mma_bf16_16816(d1, a[1], bq[2], bq[3], d1);
+  mma_bf16_16816(d0, a[2], bq[4], bq[5], d0);
+  mma_bf16_16816(d1, a[3], bq[6], bq[7], d1);
+  r_g = (d0[0] + d1[0]) + (d0[1] + d1[1]);
+  r_h = (d0[2] + d1[2]) + (d0[3] + d1[3]);
 }
 
 __device__ __forceinline__ float ld_cg_f32(const float* p) {
@@ -358,30 +365,23 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
   {
     // raw fp16 bits: [local strip][mm][row][sc_stride], copied asynchronously (4-byte words when
     // rows start 4-byte aligned, i.e. G even; 2-byte loads otherwise)
+    // one warp per staged row, lanes over the row's words
     const int n_rows = sc_n * NMAT * 16;
-    if ((G & 1) == 0) {
-      const int wpr = G / 2;
-      for (int i = tid; i < n_rows * wpr; i += HX_THREADS) {
-        const int rid = i / wpr, wi = i - rid * wpr;
-        const int ls = rid / (NMAT * 16), rem = rid - ls * NMAT * 16;
-        const int mm = rem >> 4, rr = rem & 15;
-        const StripInfo si = strip_info<NMAT>(P, sc_first + ls);
-        const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
-        const int row = min(si.rbase + rr, M.rows - 1);
-        cp_async_4(s_sc + (size_t)rid * P.sc_stride + 2 * wi, M.scales + (size_t)row * G + 2 * wi);
-      }
-      cp_async_commit();
-    } else {
-      for (int i = tid; i < n_rows * G; i += HX_THREADS) {
-        const int rid = i / G, gg = i - rid * G;
-        const int ls = rid / (NMAT * 16), rem = rid - ls * NMAT * 16;
-        const int mm = rem >> 4, rr = rem & 15;
-        const StripInfo si = strip_info<NMAT>(P, sc_first + ls);
-        const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
-        const int row = min(si.rbase + rr, M.rows - 1);
-        s_sc[(size_t)rid * P.sc_stride + gg] = __ldg(M.scales + (size_t)row * G + gg);
+    for (int rid = warp; rid < n_rows; rid += HX_WARPS) {
+      const int ls = rid / (NMAT * 16), rem = rid - ls * NMAT * 16;
+      const int mm = rem >> 4, rr = rem & 15;
+      const StripInfo si = strip_info<NMAT>(P, sc_first + ls);
+      const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
+      const int row = min(si.rbase + rr, M.rows - 1);
+      const uint16_t* src = M.scales + (size_t)row * G;
+      uint16_t* dst = s_sc + (size_t)rid * P.sc_stride;
+      if ((G & 1) == 0) {
+        for (int wi = lane; wi < G / 2; wi += 32) cp_async_4(dst + 2 * wi, src + 2 * wi);
+      } else {
+        for (int gg = lane; gg < G; gg += 32) dst[gg] = __ldg(src + gg);
       }
     }
+    cp_async_commit();
   }
   const int w = w_cta0 + warp;
   const bool streamer = warp < HX_STREAM && w < P.W;
@@ -494,6 +494,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       }
     }
   }
+  if (tid == 0) reinterpret_cast<uint32_t*>(misc)[32] = 0x0100u;  // table address bits 16..23, read after the barrier
   cp_async_wait_all();  // the staged scale window
   __syncthreads();
 
@@ -550,20 +551,33 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       const int row = si.rbase + r;
       float v = 0.f;
       if (row < M.rows) {
-        const uint32_t e0 = __ldg(M.row_ptr + row), e1 = __ldg(M.row_ptr + row + 1);
-        constexpr int step = (NMAT == 2) ? 1 : 2;
-        for (uint32_t e = e0 + (NMAT == 2 ? 0 : hi); e < e1; e += step) {
-          const int col = __ldg(M.kink_cols + e);
-          if (col < C) v += __ldg(M.kink_deltas + e) * xf[col];
-          else raise_flag(GSDLQ_FLAG_BAD_KINK);
-        }
+        // low-rank term first: its U loads do not depend on row_ptr
         if (M.k_dim > 0 && (NMAT == 2 || hi == 0)) {
           const uint16_t* ur = M.U + (size_t)row * M.k_dim;
-          if (P.tmp_k_ext) {
-            for (int jj = 0; jj < M.k_dim; ++jj) v += h2f(__ldg(ur + jj)) * __ldg(P.tmp_k_ext + jj);
-          } else {
-            const volatile float* tk = reinterpret_cast<volatile float*>(ctl) + CTL_TMPK + (si.m0 + mm) * 16;
-            for (int jj = 0; jj < M.k_dim; ++jj) v += h2f(__ldg(ur + jj)) * tk[jj];
+          uint16_t uv[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) uv[jj] = jj < M.k_dim ? __ldg(ur + jj) : (uint16_t)0;
+          const float* tk = P.tmp_k_ext ? P.tmp_k_ext : reinterpret_cast<const float*>(ctl) + CTL_TMPK + (si.m0 + mm) * 16;
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj)
+            if (jj < M.k_dim) v += h2f(uv[jj]) * __ldcg(tk + jj);
+        }
+        const uint32_t e0 = __ldg(M.row_ptr + row), e1 = __ldg(M.row_ptr + row + 1);
+        constexpr int step = (NMAT == 2) ? 1 : 2;
+        // kinks in batches of 8: the batch's loads are issued together
+        for (uint32_t e = e0 + (NMAT == 2 ? 0 : hi); e < e1; e += 8 * step) {
+          int col[8];
+          float dl[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t eu = e + u * step;
+            col[u] = eu < e1 ? (int)__ldg(M.kink_cols + eu) : 0;
+            dl[u] = eu < e1 ? __ldg(M.kink_deltas + eu) : 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            if (col[u] < C) v += dl[u] * xf[col[u]];
+            else raise_flag(GSDLQ_FLAG_BAD_KINK);
           }
         }
       }
@@ -574,7 +588,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
     }
   } else if (streamer) {
     // ---- streaming warps --------------------------------------------------------------
-    const uint32_t lane4x = (uint32_t)lane * 4u | 0x0100u;
+    const uint32_t lane4x = (uint32_t)lane * 4u | reinterpret_cast<const volatile uint32_t*>(misc)[32];
     // B fragments: lane (gl, q), gl < 2, reads the hi (gl 0) or lo (gl 1) chunk of the group; the
     // lo chunk stores each lane segment's halves swapped, so the 8 active lanes of each 16-byte
     // load touch 32 distinct banks and both lane groups receive pairs 0-3 first
