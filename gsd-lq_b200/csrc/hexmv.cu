@@ -29,8 +29,9 @@
 // Work split: persistent stream-K.  One CTA per SM: 14 streaming warps and 2
 // helper warps.  The (16-row strip, 64-column group) iterations of the launch
 // are dealt to the streaming warps as equal contiguous ranges, so every warp
-// streams the same number of code bytes; codes are prefetched HX_PF groups
-// ahead in registers, across strip boundaries.  A warp's contribution to a
+// streams the same number of code bytes.  A unit is UG consecutive 64-column
+// groups of one strip; the next unit's codes are always in flight in registers,
+// across strip boundaries.  A warp's contribution to a
 // strip (a "segment") goes to a per-strip partial slot; a per-strip counter
 // tells the warp that completes a strip to sum the slots in slot order
 // (deterministic) and run the epilogue.  The helper warps compute the low-rank
@@ -50,7 +51,6 @@ namespace gsdlq {
 constexpr int HX_WARPS = 16;
 constexpr int HX_STREAM = 14;
 constexpr int HX_THREADS = HX_WARPS * kWarp;
-constexpr int HX_PF = 6;  // groups of codes kept in flight per streaming warp
 
 // control words at the start of the workspace
 constexpr int CTL_TK_TICKET = 0;    // low-rank job tickets
@@ -68,12 +68,12 @@ struct HexmvParams {
   int cols, G, NP;
   int n_strips, nmat;      // nmat: matrices per strip unit (2 in SwiGLU pair mode)
   int strip_begin[4];      // prefix of strips per matrix (non-pair modes)
-  long long T;             // iterations = n_strips * G
+  int UG, GU;              // groups per work unit, units per strip (G = UG * GU)
+  long long T;             // iterations (work units) = n_strips * GU
   int W;                   // streaming warps in the launch
   int max_seg;             // partial slots per strip for streaming segments (+1 helper slot)
   int n_lr_jobs;
   int sc_strips;           // capacity of the staged-scale window (strips)
-  int sc_stride;           // u16 stride of a staged scale row (odd number of words)
   int ovf_bytes;           // activation-split overflow region
   unsigned* ctl;
   unsigned* cnt;           // [n_strips]
@@ -107,10 +107,13 @@ struct HxLayout {
   int sc_off, misc_off, low_end;
 };
 
-__host__ __device__ inline HxLayout hx_layout(int ovf_bytes, int sc_strips, int nmat, int sc_stride) {
+// staged scales: per (local strip, matrix, group) eight 32-bit words; word r holds the fp16
+// scales of rows r (low half) and r+8 (high half), so lane (g, q) reads both of its rows'
+// scales with one conflict-free 32-bit load
+__host__ __device__ inline HxLayout hx_layout(int ovf_bytes, int sc_strips, int nmat, int G) {
   HxLayout L;
   L.sc_off = ovf_bytes;
-  const int sc_bytes = sc_strips * nmat * 16 * sc_stride * 2;
+  const int sc_bytes = sc_strips * nmat * G * 32;
   L.misc_off = L.sc_off + ((sc_bytes + 15) & ~15);
   L.low_end = L.misc_off + 64 * 4;
   return L;
@@ -298,9 +301,9 @@ __device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float 
 template <int EPI, int NMAT>
 __device__ void finish_strip(const HexmvParams& P, int s, int lane) {
   __threadfence();
-  const int G = P.G;
-  const int w_first = warp_of((long long)s * G, P.T, P.W);
-  const int w_last = warp_of((long long)s * G + G - 1, P.T, P.W);
+  const int GU = P.GU;
+  const int w_first = warp_of((long long)s * GU, P.T, P.W);
+  const int w_last = warp_of((long long)s * GU + GU - 1, P.T, P.W);
   const int nseg = w_last - w_first + 1;
   constexpr int width = NMAT * 16;
   const float* base = P.part + (size_t)s * (P.max_seg + 1) * width;
@@ -321,7 +324,7 @@ __device__ void finish_strip(const HexmvParams& P, int s, int lane) {
 }
 
 // Count `units` toward strip s after this warp's slot writes; the warp completing the
-// strip (G streaming units + 1 helper unit) finishes it.
+// strip (GU streaming units + 1 helper unit) finishes it.
 template <int EPI, int NMAT>
 __device__ __forceinline__ void arrive(const HexmvParams& P, int s, unsigned units, int lane, bool fence = true) {
   if (fence) __threadfence();  // every lane that wrote part of the slot orders its stores before the count
@@ -329,13 +332,13 @@ __device__ __forceinline__ void arrive(const HexmvParams& P, int s, unsigned uni
   unsigned fin = 0;
   if (lane == 0) {
     const unsigned old = atomicAdd(&P.cnt[s], units);
-    fin = (old + units == (unsigned)P.G + 1u);
+    fin = (old + units == (unsigned)P.GU + 1u);
   }
   fin = __shfl_sync(0xffffffffu, fin, 0);
   if (fin) finish_strip<EPI, NMAT>(P, s, lane);
 }
 
-template <int EPI>
+template <int EPI, int UG>
 __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_constant__ HexmvParams P) {
   constexpr int NMAT = (EPI == GSDLQ_EPI_SWIGLU) ? 2 : 1;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -351,21 +354,20 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
   const uint32_t tab_off = HX_TAB_ABS - sbase;
   uint8_t* tab = smem + tab_off;
   float* xf = reinterpret_cast<float*>(smem + tab_off + HX_TAB_ABS);
-  const HxLayout LY = hx_layout(P.ovf_bytes, P.sc_strips, NMAT, P.sc_stride);
-  uint16_t* s_sc = reinterpret_cast<uint16_t*>(smem + LY.sc_off);
+  const HxLayout LY = hx_layout(P.ovf_bytes, P.sc_strips, NMAT, G);
+  uint32_t* s_sc = reinterpret_cast<uint32_t*>(smem + LY.sc_off);
   float* misc = reinterpret_cast<float*>(smem + LY.misc_off);  // [0] 1/rms, [1..16] reduction
 
   // ---- 1. independent prologue: decode table, this CTA's scale window, first code prefetches
   build_decode_table(tab, P);
   const int w_cta0 = blockIdx.x * HX_STREAM;
-  const long long cta_it0 = it_begin(min(w_cta0, P.W), P.T, P.W);
-  const long long cta_it1 = it_begin(min(w_cta0 + HX_STREAM, P.W), P.T, P.W);
-  const int sc_first = (int)(cta_it0 / G);
-  const int sc_n = (cta_it1 > cta_it0) ? (int)((cta_it1 - 1) / G) - sc_first + 1 : 0;
+  const long long cta_u0 = it_begin(min(w_cta0, P.W), P.T, P.W);
+  const long long cta_u1 = it_begin(min(w_cta0 + HX_STREAM, P.W), P.T, P.W);
+  const int sc_first = (int)(cta_u0 / P.GU);
+  const int sc_n = (cta_u1 > cta_u0) ? (int)((cta_u1 - 1) / P.GU) - sc_first + 1 : 0;
   {
-    // raw fp16 bits: [local strip][mm][row][sc_stride], copied asynchronously (4-byte words when
-    // rows start 4-byte aligned, i.e. G even; 2-byte loads otherwise)
-    // one warp per staged row, lanes over the row's words
+    // one warp per staged row: the row's scales are loaded (coalesced, all before any store),
+    // then written as the row's half of the interleaved (row r, row r+8) words
     const int n_rows = sc_n * NMAT * 16;
     for (int rid = warp; rid < n_rows; rid += HX_WARPS) {
       const int ls = rid / (NMAT * 16), rem = rid - ls * NMAT * 16;
@@ -374,22 +376,23 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
       const int row = min(si.rbase + rr, M.rows - 1);
       const uint16_t* src = M.scales + (size_t)row * G;
-      uint16_t* dst = s_sc + (size_t)rid * P.sc_stride;
-      if ((G & 1) == 0) {
-        for (int wi = lane; wi < G / 2; wi += 32) cp_async_4(dst + 2 * wi, src + 2 * wi);
-      } else {
-        for (int gg = lane; gg < G; gg += 32) dst[gg] = __ldg(src + gg);
-      }
+      uint16_t v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = (lane + 32 * k < G) ? __ldg(src + lane + 32 * k) : (uint16_t)0;
+      uint16_t* dst = reinterpret_cast<uint16_t*>(s_sc + (size_t)(ls * NMAT + mm) * G * 8) + (rr & 7) * 2 + (rr >> 3);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (lane + 32 * k < G) dst[(size_t)(lane + 32 * k) * 16] = v[k];
     }
-    cp_async_commit();
   }
   const int w = w_cta0 + warp;
   const bool streamer = warp < HX_STREAM && w < P.W;
-  const long long it0 = streamer ? it_begin(w, P.T, P.W) : 0;
-  const long long it1 = streamer ? it_begin(w + 1, P.T, P.W) : 0;
-  uint2 pf[NMAT][HX_PF][2];  // [matrix][ring][row g / row g+8]
-  // prefetch cursor: pointers to this lane's 8 code bytes of the next iteration to prefetch
-  int pf_s = (int)(it0 / G), pf_g = (int)(it0 - (long long)pf_s * G);
+  const long long u0 = streamer ? it_begin(w, P.T, P.W) : 0;
+  const long long u1 = streamer ? it_begin(w + 1, P.T, P.W) : 0;
+  const int GU = P.GU;
+  uint2 pf[NMAT][UG][2];  // codes of the next unit: [matrix][group][row g / row g+8]
+  // prefetch cursor: unit (strip pf_s, unit-in-strip pf_u) and this lane's code pointers
+  int pf_s = (int)(u0 / GU), pf_u = (int)(u0 - (long long)pf_s * GU);
   const uint8_t* pfa[NMAT];
   const uint8_t* pfb[NMAT];
   auto seek = [&]() {
@@ -398,29 +401,30 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
     for (int mm = 0; mm < NMAT; ++mm) {
       const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
       const int ra = min(si.rbase + gl, M.rows - 1), rb = min(si.rbase + gl + 8, M.rows - 1);
-      pfa[mm] = M.codes + (size_t)ra * NP + pf_g * 32 + q * 8;
-      pfb[mm] = M.codes + (size_t)rb * NP + pf_g * 32 + q * 8;
+      pfa[mm] = M.codes + (size_t)ra * NP + pf_u * (UG * 32) + q * 8;
+      pfb[mm] = M.codes + (size_t)rb * NP + pf_u * (UG * 32) + q * 8;
     }
   };
-  auto issue = [&](int slot_i) {
+  auto issue = [&]() {
 #pragma unroll
     for (int mm = 0; mm < NMAT; ++mm) {
-      pf[mm][slot_i][0] = ldg_stream_u2(pfa[mm]);
-      pf[mm][slot_i][1] = ldg_stream_u2(pfb[mm]);
-      pfa[mm] += 32;
-      pfb[mm] += 32;
+#pragma unroll
+      for (int k = 0; k < UG; ++k) {
+        pf[mm][k][0] = ldg_stream_u2(pfa[mm] + 32 * k);
+        pf[mm][k][1] = ldg_stream_u2(pfb[mm] + 32 * k);
+      }
+      pfa[mm] += UG * 32;
+      pfb[mm] += UG * 32;
     }
-    if (++pf_g == G) {
-      pf_g = 0;
+    if (++pf_u == GU) {
+      pf_u = 0;
       ++pf_s;
       seek();
     }
   };
-  if (streamer) {
+  if (streamer && u1 > u0) {
     seek();
-#pragma unroll
-    for (int i = 0; i < HX_PF; ++i)
-      if (it0 + i < it1) issue(i);
+    issue();
   }
 
   // ---- 2. wait for the producer of x, then stage the input (fp32 and bf16 splits) ----------
@@ -495,6 +499,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
     }
   }
   if (tid == 0) reinterpret_cast<uint32_t*>(misc)[32] = 0x0100u;  // table address bits 16..23, read after the barrier
+  if (tid < 8) reinterpret_cast<uint32_t*>(misc)[40 + tid] = 0u;   // zero B fragments for lanes g >= 2
   cp_async_wait_all();  // the staged scale window
   __syncthreads();
 
@@ -591,15 +596,17 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
     const uint32_t lane4x = (uint32_t)lane * 4u | reinterpret_cast<const volatile uint32_t*>(misc)[32];
     // B fragments: lane (gl, q), gl < 2, reads the hi (gl 0) or lo (gl 1) chunk of the group; the
     // lo chunk stores each lane segment's halves swapped, so the 8 active lanes of each 16-byte
-    // load touch 32 distinct banks and both lane groups receive pairs 0-3 first
+    // load touch 32 distinct banks and both lane groups receive pairs 0-3 first.  Lanes gl >= 2
+    // read a zero block (broadcast), which keeps the loop free of divergent branches.
     const uint32_t boff0 = (uint32_t)(q * 32 + 16 * gl), boff1 = (uint32_t)(q * 32 + 16 * (1 - gl));
-    int cur_s = (int)(it0 / G), cur_g = (int)(it0 - (long long)cur_s * G);
+    const uint8_t* zero_blk = reinterpret_cast<const uint8_t*>(misc + 40);
+    int cur_s = (int)(u0 / GU), cur_u = (int)(u0 - (long long)cur_s * GU);
     int seg_s = cur_s;
     float acc[NMAT][2];
 #pragma unroll
     for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
     auto emit = [&](int s) {
-      const int seg = w - warp_of((long long)s * G, P.T, P.W);
+      const int seg = w - warp_of((long long)s * GU, P.T, P.W);
       constexpr int width = NMAT * 16;
       float* slot = P.part + ((size_t)s * (P.max_seg + 1) + seg) * width;
       if (q == 0) {
@@ -610,61 +617,54 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         }
       }
     };
-    for (long long base = it0; base < it1; base += HX_PF) {
+    for (long long u = u0; u < u1; ++u) {
+      if (cur_s != seg_s) {
+        emit(seg_s);
+        seg_s = cur_s;
 #pragma unroll
-      for (int i = 0; i < HX_PF; ++i) {
-        const long long it = base + i;
-        if (it < it1) {
-          if (cur_s != seg_s) {
-            emit(seg_s);
-            seg_s = cur_s;
+        for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
+      }
+      uint2 cur[NMAT][UG][2];
 #pragma unroll
-            for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
-          }
-          uint2 cur[NMAT][2];
+      for (int mm = 0; mm < NMAT; ++mm)
 #pragma unroll
-          for (int mm = 0; mm < NMAT; ++mm) {
-            cur[mm][0] = pf[mm][i][0];
-            cur[mm][1] = pf[mm][i][1];
-          }
-          if (it + HX_PF < it1) issue(i);
-          uint32_t bq[8];
-          if (gl < 2) {
-            const uint8_t* src = smem + xs_chunk(2 * cur_g + gl, tab_off);
-            const uint4 v0 = *reinterpret_cast<const uint4*>(src + boff0);
-            const uint4 v1 = *reinterpret_cast<const uint4*>(src + boff1);
-            bq[0] = v0.x; bq[1] = v0.y; bq[2] = v0.z; bq[3] = v0.w;
-            bq[4] = v1.x; bq[5] = v1.y; bq[6] = v1.z; bq[7] = v1.w;
-          } else {
+        for (int k = 0; k < UG; ++k) {
+          cur[mm][k][0] = pf[mm][k][0];
+          cur[mm][k][1] = pf[mm][k][1];
+        }
+      if (u + 1 < u1) issue();
+      const uint32_t* scw = s_sc + (size_t)((cur_s - sc_first) * NMAT) * G * 8 + gl;
 #pragma unroll
-            for (int t = 0; t < 8; ++t) bq[t] = 0u;
-          }
-          const int ls = cur_s - sc_first;
+      for (int k = 0; k < UG; ++k) {
+        const int g = cur_u * UG + k;
+        const uint8_t* src = (gl < 2) ? smem + xs_chunk(2 * g + gl, tab_off) : zero_blk;
+        const uint4 v0 = *reinterpret_cast<const uint4*>(src + ((gl < 2) ? boff0 : 0u));
+        const uint4 v1 = *reinterpret_cast<const uint4*>(src + ((gl < 2) ? boff1 : 16u));
+        const uint32_t bq[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
-          for (int mm = 0; mm < NMAT; ++mm) {
-            const uint16_t* sr = s_sc + ((ls * NMAT + mm) * 16) * P.sc_stride + cur_g;
-            const float sa = h2f(sr[gl * P.sc_stride]), sb = h2f(sr[(gl + 8) * P.sc_stride]);
-            float rg, rh;
-            group_mma(cur[mm][0], cur[mm][1], bq, lane4x, rg, rh);
-            acc[mm][0] = fmaf(sa, rg, acc[mm][0]);
-            acc[mm][1] = fmaf(sb, rh, acc[mm][1]);
-          }
-          if (++cur_g == G) {
-            cur_g = 0;
-            ++cur_s;
-          }
+        for (int mm = 0; mm < NMAT; ++mm) {
+          const uint32_t sw = scw[(size_t)(mm * G + g) * 8];
+          const float2 sab = __half22float2(*reinterpret_cast<const __half2*>(&sw));
+          float rg, rh;
+          group_mma(cur[mm][k][0], cur[mm][k][1], bq, lane4x, rg, rh);
+          acc[mm][0] = fmaf(sab.x, rg, acc[mm][0]);
+          acc[mm][1] = fmaf(sab.y, rh, acc[mm][1]);
         }
       }
+      if (++cur_u == GU) {
+        cur_u = 0;
+        ++cur_s;
+      }
     }
-    if (it1 > it0) {
+    if (u1 > u0) {
       emit(seg_s);
       // the counts are deferred to the end of the range: a fence mid-range would wait for the code
       // prefetches in flight.  One fence covers all of this warp's slot stores, then one count per
       // strip the range touched.
       __threadfence();
-      const int s_a = (int)(it0 / G), s_b = (int)((it1 - 1) / G);
+      const int s_a = (int)(u0 / GU), s_b = (int)((u1 - 1) / GU);
       for (int s = s_a; s <= s_b; ++s) {
-        const long long a = max(it0, (long long)s * G), b = min(it1, (long long)s * G + G);
+        const long long a = max(u0, (long long)s * GU), b = min(u1, (long long)s * GU + GU);
         arrive<EPI, NMAT>(P, s, (unsigned)(b - a), lane, false);
       }
     }
@@ -719,11 +719,15 @@ static int hexmv_plan(HexmvParams& P) {
     for (int m = 0; m < J.n_mat; ++m) P.strip_begin[m + 1] = P.strip_begin[m] + (J.mat[m].rows + 15) / 16;
     P.n_strips = P.strip_begin[J.n_mat];
   }
-  P.T = (long long)P.n_strips * P.G;
+  // work unit: UG consecutive groups of one strip (4, or 2 in pair mode, when G allows)
+  const int ug_max = (P.nmat == 2) ? 2 : 4;
+  P.UG = (P.G % ug_max == 0) ? ug_max : ((P.G % 2 == 0) ? 2 : 1);
+  P.GU = P.G / P.UG;
+  P.T = (long long)P.n_strips * P.GU;
   const int max_w = num_sms() * HX_STREAM;
   P.W = (int)std::min<long long>(max_w, P.T);
   const long long lmin = P.T / P.W;
-  P.max_seg = (int)((P.G - 1 + lmin - 1) / lmin) + 1;
+  P.max_seg = (int)((P.GU - 1 + lmin - 1) / lmin) + 1;
   int lr = 0;
   for (int m = 0; m < J.n_mat; ++m) lr += J.mat[m].k_dim;
   P.n_lr_jobs = P.tmp_k_ext ? 0 : lr;
@@ -733,26 +737,23 @@ static int hexmv_plan(HexmvParams& P) {
   for (int c = 0; c < grid; ++c) {
     const long long a = it_begin(std::min(c * HX_STREAM, P.W), P.T, P.W);
     const long long b = it_begin(std::min((c + 1) * HX_STREAM, P.W), P.T, P.W);
-    if (b > a) sc = std::max(sc, (int)((b - 1) / P.G - a / P.G + 1));
+    if (b > a) sc = std::max(sc, (int)((b - 1) / P.GU - a / P.GU + 1));
   }
   P.sc_strips = sc;
-  int words = (P.G + 1) / 2;
-  if ((words & 1) == 0) ++words;
-  P.sc_stride = 2 * words;
   P.ovf_bytes = std::max(0, 2 * P.G - 256) * 128;
   return GSDLQ_OK;
 }
 
-template <int EPI>
+template <int EPI, int UG>
 static int hexmv_launch_t(const HexmvParams& P, cudaStream_t s) {
-  const HxLayout LY = hx_layout(P.ovf_bytes, P.sc_strips, P.nmat, P.sc_stride);
+  const HxLayout LY = hx_layout(P.ovf_bytes, P.sc_strips, P.nmat, P.G);
   const int dyn = hx_dyn_smem(P.cols);
   if (LY.low_end > (int)HX_TAB_ABS - HX_BASE_MAX || dyn > 227 * 1024) return GSDLQ_ERR_UNSUPPORTED;
   static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(hexmv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(hexmv_kernel<EPI, UG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return record_cuda_error(e);
     configured[dev] = true;
   }
@@ -767,7 +768,7 @@ static int hexmv_launch_t(const HexmvParams& P, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, hexmv_kernel<EPI>, P);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, hexmv_kernel<EPI, UG>, P);
   if (e != cudaSuccess) return record_cuda_error(e);
   return GSDLQ_OK;
 }
@@ -801,6 +802,24 @@ static int hexmv_check_io(const HexmvParams& P) {
   }
 }
 
+template <int EPI>
+static int hexmv_dispatch_ug(const HexmvParams& P, cudaStream_t s) {
+  if constexpr (EPI != GSDLQ_EPI_SWIGLU) {  // pair mode never uses 4-group units
+    if (P.UG == 4) return hexmv_launch_t<EPI, 4>(P, s);
+  }
+  if (P.UG == 2) return hexmv_launch_t<EPI, 2>(P, s);
+  return hexmv_launch_t<EPI, 1>(P, s);
+}
+
+static int hexmv_dispatch(const HexmvParams& P, cudaStream_t s) {
+  switch (P.job.epilogue) {
+    case GSDLQ_EPI_STORE: return hexmv_dispatch_ug<GSDLQ_EPI_STORE>(P, s);
+    case GSDLQ_EPI_RESID: return hexmv_dispatch_ug<GSDLQ_EPI_RESID>(P, s);
+    case GSDLQ_EPI_SWIGLU: return hexmv_dispatch_ug<GSDLQ_EPI_SWIGLU>(P, s);
+    default: return hexmv_dispatch_ug<GSDLQ_EPI_ROPE_KV>(P, s);
+  }
+}
+
 int hexmv_launch(HexmvParams& P, void* workspace, size_t ws_bytes, cudaStream_t s) {
   int st = hexmv_plan(P);
   if (st != GSDLQ_OK) return st;
@@ -812,12 +831,7 @@ int hexmv_launch(HexmvParams& P, void* workspace, size_t ws_bytes, cudaStream_t 
   P.cnt = P.ctl + CTL_WORDS;
   const uintptr_t pb = reinterpret_cast<uintptr_t>(P.cnt + P.n_strips);
   P.part = reinterpret_cast<float*>((pb + 15) & ~uintptr_t(15));
-  switch (P.job.epilogue) {
-    case GSDLQ_EPI_STORE: return hexmv_launch_t<GSDLQ_EPI_STORE>(P, s);
-    case GSDLQ_EPI_RESID: return hexmv_launch_t<GSDLQ_EPI_RESID>(P, s);
-    case GSDLQ_EPI_SWIGLU: return hexmv_launch_t<GSDLQ_EPI_SWIGLU>(P, s);
-    default: return hexmv_launch_t<GSDLQ_EPI_ROPE_KV>(P, s);
-  }
+  return hexmv_dispatch(P, s);
 }
 
 size_t hexmv_ws_bytes(HexmvParams& P) {
