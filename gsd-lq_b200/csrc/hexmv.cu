@@ -107,13 +107,15 @@ struct HxLayout {
   int sc_off, misc_off, low_end;
 };
 
-// staged scales: per (local strip, matrix, group) eight 32-bit words; word r holds the fp16
-// scales of rows r (low half) and r+8 (high half), so lane (g, q) reads both of its rows'
-// scales with one conflict-free 32-bit load
+// staged scales: row-major fp16 rows of the CTA's strips, [local strip][matrix][row][sc_words]
+// 32-bit words, sc_words = an odd number >= ceil(G/2) so that the 8 rows a warp reads at the
+// same column sit in 8 different banks; one 32-bit load gives a row's scales of two groups
+__host__ __device__ inline int hx_sc_words(int G) { return ((G + 1) / 2) | 1; }
+
 __host__ __device__ inline HxLayout hx_layout(int ovf_bytes, int sc_strips, int nmat, int G) {
   HxLayout L;
   L.sc_off = ovf_bytes;
-  const int sc_bytes = sc_strips * nmat * G * 32;
+  const int sc_bytes = sc_strips * nmat * 16 * hx_sc_words(G) * 4;
   L.misc_off = L.sc_off + ((sc_bytes + 15) & ~15);
   L.low_end = L.misc_off + 64 * 4;
   return L;
@@ -365,9 +367,10 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
   const long long cta_u1 = it_begin(min(w_cta0 + HX_STREAM, P.W), P.T, P.W);
   const int sc_first = (int)(cta_u0 / P.GU);
   const int sc_n = (cta_u1 > cta_u0) ? (int)((cta_u1 - 1) / P.GU) - sc_first + 1 : 0;
+  const int scw_n = hx_sc_words(G);
   {
-    // one warp per staged row: the row's scales are loaded (coalesced, all before any store),
-    // then written as the row's half of the interleaved (row r, row r+8) words
+    // asynchronous 4-byte copies of whole rows (2-byte loads when G is odd and rows are not
+    // 4-byte aligned)
     const int n_rows = sc_n * NMAT * 16;
     for (int rid = warp; rid < n_rows; rid += HX_WARPS) {
       const int ls = rid / (NMAT * 16), rem = rid - ls * NMAT * 16;
@@ -376,14 +379,14 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
       const int row = min(si.rbase + rr, M.rows - 1);
       const uint16_t* src = M.scales + (size_t)row * G;
-      uint16_t v[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = (lane + 32 * k < G) ? __ldg(src + lane + 32 * k) : (uint16_t)0;
-      uint16_t* dst = reinterpret_cast<uint16_t*>(s_sc + (size_t)(ls * NMAT + mm) * G * 8) + (rr & 7) * 2 + (rr >> 3);
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (lane + 32 * k < G) dst[(size_t)(lane + 32 * k) * 16] = v[k];
+      uint32_t* dst = s_sc + (size_t)rid * scw_n;
+      if ((G & 1) == 0) {
+        for (int wi = lane; wi < G / 2; wi += 32) cp_async_4(dst + wi, src + 2 * wi);
+      } else {
+        for (int gg = lane; gg < G; gg += 32) reinterpret_cast<uint16_t*>(dst)[gg] = __ldg(src + gg);
+      }
     }
+    cp_async_commit();
   }
   const int w = w_cta0 + warp;
   const bool streamer = warp < HX_STREAM && w < P.W;
@@ -499,7 +502,6 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
     }
   }
   if (tid == 0) reinterpret_cast<uint32_t*>(misc)[32] = 0x0100u;  // table address bits 16..23, read after the barrier
-  if (tid < 8) reinterpret_cast<uint32_t*>(misc)[40 + tid] = 0u;   // zero B fragments for lanes g >= 2
   cp_async_wait_all();  // the staged scale window
   __syncthreads();
 
@@ -569,21 +571,24 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         }
         const uint32_t e0 = __ldg(M.row_ptr + row), e1 = __ldg(M.row_ptr + row + 1);
         constexpr int step = (NMAT == 2) ? 1 : 2;
-        // kinks in batches of 8: the batch's loads are issued together
-        for (uint32_t e = e0 + (NMAT == 2 ? 0 : hi); e < e1; e += 8 * step) {
-          int col[8];
-          float dl[8];
+        // kinks in batches of 16: the batch's loads are issued together
+        for (uint32_t e = e0 + (NMAT == 2 ? 0 : hi); e < e1; e += 16 * step) {
+          int col[16];
+          float dl[16];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
+          for (int u = 0; u < 16; ++u) {
             const uint32_t eu = e + u * step;
             col[u] = eu < e1 ? (int)__ldg(M.kink_cols + eu) : 0;
             dl[u] = eu < e1 ? __ldg(M.kink_deltas + eu) : 0.f;
           }
+          bool bad = false;
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            if (col[u] < C) v += dl[u] * xf[col[u]];
-            else raise_flag(GSDLQ_FLAG_BAD_KINK);
+          for (int u = 0; u < 16; ++u) {
+            const bool ok = col[u] < C;
+            v += ok ? dl[u] * xf[ok ? col[u] : 0] : 0.f;
+            bad |= !ok;
           }
+          if (bad) raise_flag(GSDLQ_FLAG_BAD_KINK);
         }
       }
       if (NMAT == 1) v += __shfl_xor_sync(0xffffffffu, v, 16);
@@ -594,12 +599,13 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
   } else if (streamer) {
     // ---- streaming warps --------------------------------------------------------------
     const uint32_t lane4x = (uint32_t)lane * 4u | reinterpret_cast<const volatile uint32_t*>(misc)[32];
-    // B fragments: lane (gl, q), gl < 2, reads the hi (gl 0) or lo (gl 1) chunk of the group; the
-    // lo chunk stores each lane segment's halves swapped, so the 8 active lanes of each 16-byte
-    // load touch 32 distinct banks and both lane groups receive pairs 0-3 first.  Lanes gl >= 2
-    // read a zero block (broadcast), which keeps the loop free of divergent branches.
-    const uint32_t boff0 = (uint32_t)(q * 32 + 16 * gl), boff1 = (uint32_t)(q * 32 + 16 * (1 - gl));
-    const uint8_t* zero_blk = reinterpret_cast<const uint8_t*>(misc + 40);
+    // B fragments: lane (gl, q) supplies column n = gl of B.  Column 0 is the hi split, column 1
+    // the lo split; the lo chunk stores each lane segment's halves swapped, so the 8 lanes of
+    // columns 0-1 touch 32 distinct banks per 16-byte load and all receive pairs 0-3 first.
+    // Columns 2-7 only feed D columns 2-7, which are never read, so lanes gl >= 2 simply load the
+    // same addresses as lanes gl & 1 (a broadcast: no extra wavefronts, no divergent branch).
+    const int gb = gl & 1;
+    const uint32_t boff0 = (uint32_t)(q * 32 + 16 * gb), boff1 = (uint32_t)(q * 32 + 16 * (1 - gb));
     int cur_s = (int)(u0 / GU), cur_u = (int)(u0 - (long long)cur_s * GU);
     int seg_s = cur_s;
     float acc[NMAT][2];
@@ -633,22 +639,23 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
           cur[mm][k][1] = pf[mm][k][1];
         }
       if (u + 1 < u1) issue();
-      const uint32_t* scw = s_sc + (size_t)((cur_s - sc_first) * NMAT) * G * 8 + gl;
+      // this lane's staged scale rows (gl and gl + 8) of the unit's strip
+      const uint16_t* sra = reinterpret_cast<const uint16_t*>(s_sc + ((size_t)((cur_s - sc_first) * NMAT) * 16 + gl) * scw_n);
 #pragma unroll
       for (int k = 0; k < UG; ++k) {
         const int g = cur_u * UG + k;
-        const uint8_t* src = (gl < 2) ? smem + xs_chunk(2 * g + gl, tab_off) : zero_blk;
-        const uint4 v0 = *reinterpret_cast<const uint4*>(src + ((gl < 2) ? boff0 : 0u));
-        const uint4 v1 = *reinterpret_cast<const uint4*>(src + ((gl < 2) ? boff1 : 16u));
+        const uint8_t* src = smem + xs_chunk(2 * g + gb, tab_off);
+        const uint4 v0 = *reinterpret_cast<const uint4*>(src + boff0);
+        const uint4 v1 = *reinterpret_cast<const uint4*>(src + boff1);
         const uint32_t bq[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
         for (int mm = 0; mm < NMAT; ++mm) {
-          const uint32_t sw = scw[(size_t)(mm * G + g) * 8];
-          const float2 sab = __half22float2(*reinterpret_cast<const __half2*>(&sw));
+          const uint16_t* sr = sra + (size_t)mm * 16 * scw_n * 2;
+          const float sa = h2f(sr[g]), sb = h2f(sr[8 * scw_n * 2 + g]);
           float rg, rh;
           group_mma(cur[mm][k][0], cur[mm][k][1], bq, lane4x, rg, rh);
-          acc[mm][0] = fmaf(sab.x, rg, acc[mm][0]);
-          acc[mm][1] = fmaf(sab.y, rh, acc[mm][1]);
+          acc[mm][0] = fmaf(sa, rg, acc[mm][0]);
+          acc[mm][1] = fmaf(sb, rh, acc[mm][1]);
         }
       }
       if (++cur_u == GU) {
