@@ -21,7 +21,7 @@ GSDLQ_OK = 0
 EPI_STORE, EPI_RESID, EPI_SWIGLU, EPI_ROPE_KV = 0, 1, 2, 3
 IN_PLAIN, IN_RMSNORM, IN_EMBED = 0, 1, 2
 FLAG_NAMES = {0x1: "bad_code", 0x2: "bad_kink", 0x4: "bad_pos", 0x8: "bad_table", 0x10: "timeout",
-              0x20: "bad_token", 0x40: "unsupported"}
+              0x20: "bad_token", 0x40: "unsupported", 0x80: "range"}
 
 
 class HexMat(ctypes.Structure):

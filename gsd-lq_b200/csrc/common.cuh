@@ -5,7 +5,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#include "../../include/gsdlq.h"
+#include "gsdlq.h"  // include/ is on the include path
 
 namespace gsdlq {
 
@@ -102,16 +102,18 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
         "f"(c[3]));
 }
 
-// Bounded spin on a global counter: returns false (and raises a flag) when the
-// producer did not arrive within ~`max_ns` nanoseconds of %globaltimer.
-__device__ __forceinline__ bool wait_counter_geq(const unsigned int* ctr, unsigned int target,
-                                                 unsigned long long max_ns) {
+// Bounded spin on a global counter until it EQUALS `target`: returns false (and raises a
+// flag) when that did not happen within ~`max_ns` nanoseconds of %globaltimer.  Equality
+// rather than >= makes a counter that did not start at zero (a dirty workspace) show up as
+// a timeout instead of an early, silent read.
+__device__ __forceinline__ bool wait_counter_eq(const unsigned int* ctr, unsigned int target,
+                                                unsigned long long max_ns) {
   unsigned long long t0;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   while (true) {
     unsigned int v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr));
-    if (v >= target) return true;
+    if (v == target) return true;
     unsigned long long t1;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
     if (t1 - t0 > max_ns) {

@@ -14,33 +14,47 @@
 // integers r0, r1, so
 //     xy . (x0, x1) = r0 * x0 + r1 * (x0/2 + sqrt3/2 * x1) = r0 * a + r1 * b.
 // (r0, r1) are exact in bf16; (a, b) is split into bf16 hi + lo parts (about 16
-// mantissa bits together).  One warp-level mma.sync m16n8k16 then computes, for
-// 16 rows x 8 code pairs, the hi and lo dot products in B columns 0 and 1 with
-// fp32 accumulation.  The tensor core only does the multiply-adds; the kernel
-// is HBM-bound on the code stream (0.53 B/weight).
+// mantissa bits together).  Warp-level mma.sync m16n8k16 (bf16 in, fp32
+// accumulate) does the multiply-adds; the kernel is HBM-bound on the code
+// stream (0.53 B/weight).
+//
+// Code stream.  A work unit is 16 rows x 256 code bytes (512 columns, 8 scale
+// groups) of one matrix.  Lane (g, q) of a warp loads 16 contiguous bytes of rows
+// g and g+8 at byte 64*s + 16*q of the unit (segment s = 0..3), so every load
+// instruction reads 64 contiguous bytes per row and a unit reads 256 contiguous
+// bytes per row -- the shape that streams HBM at full rate.  The unit's 8 fp16
+// scales per row are one 16-byte load.  The next unit's loads are in flight
+// while the current one is computed (segment by segment, in registers).
 //
 // Decode.  A code byte becomes its bf16x2 (r0, r1) through one byte-permute
 // (PRMT: code -> bits 8..15, lane*4 -> bits 0..7) and one 32-bit shared load
 // from a 256-entry table replicated once per lane in the lane's own bank
 // (entry c of lane l at byte c*256 + l*4), so the 32 lookups of a warp never
-// conflict.  The other half of every 256-byte table row holds 128 bytes of the
-// staged activation splits.
+// conflict.  The other half of every 256-byte table row holds staged
+// activation splits.
+//
+// MMA shape.  Within a 64-byte segment, lanes q = 0,1 hold scale group A and
+// lanes q = 2,3 hold group B.  One m16n8k16 per pair of k-steps takes A = decoded
+// codes (16 rows x 8 code pairs, two from each lane) and a block-diagonal B:
+// column 0/1 = hi/lo splits of group A's activations (zero on group B's k rows),
+// column 2/3 = hi/lo of group B (zero on group A's k rows), columns 4-7 zero.
+// Lane q = 0 then holds group A's dot products for rows g, g+8 and lane q = 1
+// group B's, so each applies its own group's scale.
 //
 // Work split: persistent stream-K.  One CTA per SM: 14 streaming warps and 2
-// helper warps.  The (16-row strip, 64-column group) iterations of the launch
-// are dealt to the streaming warps as equal contiguous ranges, so every warp
-// streams the same number of code bytes.  A unit is UG consecutive 64-column
-// groups of one strip; the next unit's codes are always in flight in registers,
-// across strip boundaries.  A warp's contribution to a
-// strip (a "segment") goes to a per-strip partial slot; a per-strip counter
-// tells the warp that completes a strip to sum the slots in slot order
-// (deterministic) and run the epilogue.  The helper warps compute the low-rank
-// projections (one tmp_k value per ticket) and then each strip's kink and
-// low-rank terms into one more slot, off the streaming warps' critical path.
+// helper warps.  The (strip, matrix, unit) iterations of the launch are dealt to
+// the streaming warps as equal contiguous ranges.  A warp's contribution to a
+// 16-row strip (a "segment") goes to a per-strip partial slot; a per-strip
+// counter tells the warp that completes a strip to sum the slots in slot order
+// (deterministic), add the low-rank term and run the epilogue.  The helper
+// warps project a column slice of every Vt row (fixed-point 64-bit atomics, so
+// the sum is order-independent and deterministic) and compute the kink sums of
+// statically assigned strips into one more slot.
 //
-// Launch order (programmatic dependent launch): decode table, staged scales
-// and the first code prefetches are issued BEFORE griddepcontrol.wait, so they
-// overlap the previous kernel; the input x is read only after it.
+// Launch order (programmatic dependent launch): decode table, the first unit's
+// code and scale loads and L2 prefetches of the helpers' Vt slices are issued
+// BEFORE griddepcontrol.wait, so they overlap the previous kernel; the input x is
+// read only after it.
 #include <algorithm>
 #include <cstdio>
 
@@ -50,15 +64,17 @@ namespace gsdlq {
 
 constexpr int HX_WARPS = 16;
 constexpr int HX_STREAM = 14;
+constexpr int HX_HELP = HX_WARPS - HX_STREAM;
 constexpr int HX_THREADS = HX_WARPS * kWarp;
+constexpr int HX_UB = 256;  // code bytes of one row in a work unit (8 scale groups, 512 columns)
 
 // control words at the start of the workspace
-constexpr int CTL_TK_TICKET = 0;    // low-rank job tickets
-constexpr int CTL_TK_DONE = 1;      // low-rank jobs published
-constexpr int CTL_KINK_TICKET = 2;  // helper strip tickets
-constexpr int CTL_DONE = 3;         // CTAs finished
-constexpr int CTL_TMPK = 16;        // 48 floats: tmp_k[m][j]
-constexpr int CTL_WORDS = 64;
+constexpr int CTL_LR_DONE = 0;  // helper warps that have added their low-rank slice
+constexpr int CTL_DONE = 1;     // CTAs finished
+constexpr int CTL_TMPK = 16;    // 48 x u64 fixed-point low-rank accumulators (words 16..111)
+constexpr int CTL_WORDS = 128;
+constexpr float LR_FIX = 4294967296.f;  // 2^32: fixed-point scale of the low-rank partials
+constexpr float LR_MAX = 4194304.f;     // 2^22: largest partial magnitude (keeps 296 partials in 63 bits)
 
 struct HexmvParams {
   gsdlq_linear_job_t job;
@@ -66,14 +82,16 @@ struct HexmvParams {
   const float* tmp_k_ext;  // drop-in path: caller-computed tmp_k for mat[0]
   int n_pts;
   int cols, G, NP;
-  int n_strips, nmat;      // nmat: matrices per strip unit (2 in SwiGLU pair mode)
+  int n_strips, nmat;      // nmat: matrices per strip (2 in SwiGLU pair mode)
   int strip_begin[4];      // prefix of strips per matrix (non-pair modes)
-  int UG, GU;              // groups per work unit, units per strip (G = UG * GU)
-  long long T;             // iterations (work units) = n_strips * GU
+  int GU;                  // units per row: ceil(G / 8)
+  int UPS;                 // units per strip: nmat * GU
+  long long T;             // units in the launch: n_strips * UPS
   int W;                   // streaming warps in the launch
   int max_seg;             // partial slots per strip for streaming segments (+1 helper slot)
-  int n_lr_jobs;
-  int sc_strips;           // capacity of the staged-scale window (strips)
+  int n_lr;                // low-rank rows projected in the kernel (0 with tmp_k_ext)
+  int lr_off[4];           // prefix of k_dim over the matrices
+  int lr_chunks;           // 8-column chunks of every Vt row per helper warp
   int ovf_bytes;           // activation-split overflow region
   unsigned* ctl;
   unsigned* cnt;           // [n_strips]
@@ -97,34 +115,31 @@ inline size_t hexmv_ws_bytes_for(int n_strips, int max_seg, int nmat) {
 // permute builds a lookup address from a code byte (bits 8..15), the lane (bits 2..6) and
 // the constant 0x01 (bits 16..23).  Dynamic shared memory starts at a small offset B (the
 // system-reserved bytes); the buffers below the table use [0, 0x10000 - B):
-//   activation-split overflow chunks | staged scale window | misc
+//   activation-split overflow chunks | decode entries | reduction words
 // and the fp32 input xf follows the table.  The host sizes the allocation for B <= 4 KB;
 // the kernel checks B and raises GSDLQ_FLAG_UNSUPPORTED if the assumption fails.
 constexpr uint32_t HX_TAB_ABS = 0x10000u;
 constexpr int HX_BASE_MAX = 4096;
 
 struct HxLayout {
-  int sc_off, misc_off, low_end;
+  int ent_off, red_off, low_end;
 };
 
-// staged scales: row-major fp16 rows of the CTA's strips, [local strip][matrix][row][sc_words]
-// 32-bit words, sc_words = an odd number >= ceil(G/2) so that the 8 rows a warp reads at the
-// same column sit in 8 different banks; one 32-bit load gives a row's scales of two groups
-__host__ __device__ inline int hx_sc_words(int G) { return ((G + 1) / 2) | 1; }
-
-__host__ __device__ inline HxLayout hx_layout(int ovf_bytes, int sc_strips, int nmat, int G) {
+__host__ __device__ inline HxLayout hx_layout(int ovf_bytes) {
   HxLayout L;
-  L.sc_off = ovf_bytes;
-  const int sc_bytes = sc_strips * nmat * 16 * hx_sc_words(G) * 4;
-  L.misc_off = L.sc_off + ((sc_bytes + 15) & ~15);
-  L.low_end = L.misc_off + 64 * 4;
+  L.ent_off = ovf_bytes;         // 256 decode entries (bf16x2)
+  L.red_off = L.ent_off + 1024;  // [0] 1/rms, [1..16] warp sums, [32] table address bits, [33] zero
+  L.low_end = L.red_off + 256;
   return L;
 }
 
 inline int hx_dyn_smem(int cols) { return (int)(2 * HX_TAB_ABS) + 4 * cols + 64; }
 
-// dynamic-smem offset of the 128-byte activation-split chunk `ch` (chunk 2g = hi words of
-// group g, 2g+1 = lo words); the first 256 chunks fill the free halves of the table rows
+// Activation splits.  For pair p (columns 2p, 2p+1) with a = x[2p], b = x[2p]/2 + sqrt3/2 x[2p+1],
+// the hi word (bf16 a_hi | b_hi << 16) and the lo word live in 128-byte chunk
+// ch = (p / 64) * 4 + (p % 16) / 4 at byte ((p % 64) / 16) * 32 + (p % 4) * 4 (+16 for lo).
+// One chunk is exactly what the 32 lanes of a warp read with one 16-byte load per k-step
+// pair, conflict-free.  The first 256 chunks fill the free halves of the table rows.
 __device__ __forceinline__ uint32_t xs_chunk(int ch, uint32_t tab_off) {
   return ch < 256 ? tab_off + (uint32_t)ch * 256u + 128u : (uint32_t)(ch - 256) * 128u;
 }
@@ -144,42 +159,36 @@ __device__ __forceinline__ bool lattice_of_code(int c, int R, int& r0, int& r1) 
   return false;
 }
 
-__device__ __forceinline__ void build_decode_table(uint8_t* tab, const HexmvParams& P) {
-  const int R = P.job.mat[0].radius;
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-    int r0 = 0, r1 = 0;
-    bool ok;
-    if (P.xy_table != nullptr) {
-      ok = i < P.n_pts;
-      if (ok) {
-        const float x = P.xy_table[2 * i], y = P.xy_table[2 * i + 1];
-        const float rf1 = rintf(y * 1.1547005383792515f);
-        const float rf0 = x - 0.5f * rf1;
-        r0 = (int)rf0;
-        r1 = (int)rf1;
-        const float yy = (float)((double)r1 * 0.8660254037844386);
-        if ((float)r0 != rf0 || yy != y || fabsf(rf0) > 16.f || fabsf(rf1) > 16.f) {
-          raise_flag(GSDLQ_FLAG_BAD_TABLE);
-          r0 = r1 = 0;
-        }
+// bf16x2 (r0, r1) decode entry of code i (0 for codes past the table)
+__device__ __forceinline__ uint32_t decode_entry(int i, const HexmvParams& P) {
+  int r0 = 0, r1 = 0;
+  bool ok;
+  if (P.xy_table != nullptr) {
+    ok = i < P.n_pts;
+    if (ok) {
+      const float x = P.xy_table[2 * i], y = P.xy_table[2 * i + 1];
+      const float rf1 = rintf(y * 1.1547005383792515f);
+      const float rf0 = x - 0.5f * rf1;
+      r0 = (int)rf0;
+      r1 = (int)rf1;
+      const float yy = (float)((double)r1 * 0.8660254037844386);
+      if ((float)r0 != rf0 || yy != y || fabsf(rf0) > 16.f || fabsf(rf1) > 16.f) {
+        raise_flag(GSDLQ_FLAG_BAD_TABLE);
+        r0 = r1 = 0;
       }
-    } else {
-      ok = lattice_of_code(i, R, r0, r1);
     }
-    if (!ok) r0 = r1 = 0;
-    const uint32_t e = pack_bf16x2((float)r0, (float)r1);
-    const uint4 v = make_uint4(e, e, e, e);
-    uint4* row = reinterpret_cast<uint4*>(tab + i * 256);
-#pragma unroll
-    for (int w = 0; w < 8; ++w) row[w] = v;
+  } else {
+    ok = lattice_of_code(i, P.job.mat[0].radius, r0, r1);
   }
+  if (!ok) r0 = r1 = 0;
+  return pack_bf16x2((float)r0, (float)r1);
 }
 
 // Decode lookup: PRMT assembles the absolute shared address 0x10000 | code << 8 | lane << 2
 // (lane4x = lane*4 | 0x0100 supplies bytes 0 and 2), one 32-bit shared load reads the entry.
-// The load is not volatile (the table is constant after the prologue barrier), so lookups of
-// different k-steps and groups can be scheduled around the MMAs; lane4x is derived from a
-// shared-memory read made after that barrier, which keeps every lookup behind it.
+// The load is not volatile (the table is constant after the prologue barrier), so lookups can
+// be scheduled around the MMAs; lane4x is derived from a shared-memory read made after that
+// barrier, which keeps every lookup behind it.
 __device__ __forceinline__ uint32_t tab_lookup(uint32_t word, uint32_t lane4x, uint32_t sel) {
   const uint32_t addr = __byte_perm(word, lane4x, sel);
   uint32_t r;
@@ -187,34 +196,49 @@ __device__ __forceinline__ uint32_t tab_lookup(uint32_t word, uint32_t lane4x, u
   return r;
 }
 
-// one 64-column scale group of one 16-row strip: 4 MMAs; returns hi+lo sums for rows g, g+8
-__device__ __forceinline__ void group_mma(uint2 ca, uint2 cb, const uint32_t (&bq)[8], uint32_t lane4x, float& r_g,
-                                          float& r_h) {
-  // two independent accumulator chains (k-steps 0,2 and 1,3) halve the MMA dependency depth
+__device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
+  uint4 r;
+  asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
+  return r;
+}
+
+// One 64-byte segment of a unit (16 rows x 64 code pairs = scale groups A and B): 8 MMAs in
+// two independent accumulator chains.  ca / cb: this lane's 16 code bytes of rows g and g+8;
+// baddr: this lane's 16-byte B slice in the segment's first chunk (chunks bstride apart).
+// Returns the dot products of this lane's group (q = 0: A, q = 1: B; 0 for q = 2, 3).
+__device__ __forceinline__ void segment_mma(const uint4& ca, const uint4& cb, uint32_t baddr, uint32_t bstride,
+                                            uint32_t bmask, uint32_t lane4x, float& r_g, float& r_h) {
   float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-  uint32_t a[4][4];
+  const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w};
+  const uint32_t wb[4] = {cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t wa = (j < 2) ? ca.x : ca.y;
-    const uint32_t wb = (j < 2) ? cb.x : cb.y;
-    const uint32_t k0 = 2 * (j & 1);
-    const uint32_t s0 = 0x6504u | (k0 << 4), s1 = 0x6504u | ((k0 + 1) << 4);
-    a[j][0] = tab_lookup(wa, lane4x, s0);  // row g,   pair 8q+2j
-    a[j][1] = tab_lookup(wb, lane4x, s0);  // row g+8, pair 8q+2j
-    a[j][2] = tab_lookup(wa, lane4x, s1);  // row g,   pair 8q+2j+1
-    a[j][3] = tab_lookup(wb, lane4x, s1);  // row g+8, pair 8q+2j+1
+  for (int m = 0; m < 4; ++m) {
+    // k-steps 2m (code bytes 0, 1 of word m) and 2m+1 (bytes 2, 3)
+    const uint4 bv = lds_u4(baddr + (uint32_t)m * bstride);
+    uint32_t a0[4], a1[4];
+    a0[0] = tab_lookup(wa[m], lane4x, 0x6504u);  // row g,   pair 2t
+    a0[1] = tab_lookup(wb[m], lane4x, 0x6504u);  // row g+8, pair 2t
+    a0[2] = tab_lookup(wa[m], lane4x, 0x6514u);  // row g,   pair 2t+1
+    a0[3] = tab_lookup(wb[m], lane4x, 0x6514u);  // row g+8, pair 2t+1
+    a1[0] = tab_lookup(wa[m], lane4x, 0x6524u);
+    a1[1] = tab_lookup(wb[m], lane4x, 0x6524u);
+    a1[2] = tab_lookup(wa[m], lane4x, 0x6534u);
+    a1[3] = tab_lookup(wb[m], lane4x, 0x6534u);
+    mma_bf16_16816(d0, a0, bv.x & bmask, bv.y & bmask, d0);
+    mma_bf16_16816(d1, a1, bv.z & bmask, bv.w & bmask, d1);
   }
-  mma_bf16_16816(d0, a[0], bq[0], bq[1], d0);
-  mma_bf16_16816(d1, a[1], bq[2], bq[3], d1);
-  mma_bf16_16816(d0, a[2], bq[4], bq[5], d0);
-  mma_bf16_16816(d1, a[3], bq[6], bq[7], d1);
-  r_g = (d0[0] + d1[0]) + (d0[1] + d1[1]);
-  r_h = (d0[2] + d1[2]) + (d0[3] + d1[3]);
+  r_g = (d0[0] + d0[1]) + (d1[0] + d1[1]);
+  r_h = (d0[2] + d0[3]) + (d1[2] + d1[3]);
 }
 
 __device__ __forceinline__ float ld_cg_f32(const float* p) {
   float v;
   asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_cg_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(v) : "l"(p));
   return v;
 }
 
@@ -299,34 +323,71 @@ __device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float 
   }
 }
 
-// Sum a completed strip's slots in slot order and run its epilogue (one warp).
+// Sum a completed strip's slots in slot order, add the low-rank term and run the epilogue
+// (one warp).
 template <int EPI, int NMAT>
 __device__ void finish_strip(const HexmvParams& P, int s, int lane) {
   __threadfence();
-  const int GU = P.GU;
-  const int w_first = warp_of((long long)s * GU, P.T, P.W);
-  const int w_last = warp_of((long long)s * GU + GU - 1, P.T, P.W);
+  const int UPS = P.UPS;
+  const int w_first = warp_of((long long)s * UPS, P.T, P.W);
+  const int w_last = warp_of((long long)s * UPS + UPS - 1, P.T, P.W);
   const int nseg = w_last - w_first + 1;
   constexpr int width = NMAT * 16;
-  const float* base = P.part + (size_t)s * (P.max_seg + 1) * width;
+  const StripInfo si = strip_info<NMAT>(P, s);
+  const int mm = (NMAT == 2) ? (lane >> 4) : 0;
+  const gsdlq_hexmat_t& M = P.job.mat[si.m0 + mm];
+  const int row = si.rbase + (lane & 15);
+  const bool active = lane < width && row < M.rows;
+  // low-rank operands first: their loads do not depend on the slots
+  const int kd = active ? M.k_dim : 0;
+  uint16_t uv[16];
+  float sv[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    uv[j] = j < kd ? __ldg(M.U + (size_t)row * kd + j) : (uint16_t)0;
+    sv[j] = (j < kd && P.tmp_k_ext == nullptr) ? __ldg(M.S + j) : 0.f;
+  }
+  float* base = P.part + (size_t)s * (P.max_seg + 1) * width;
   float v = 0.f;
   if (lane < width) {
-    float* bw = const_cast<float*>(base);
     for (int k = 0; k < nseg; ++k) {
       v += ld_cg_f32(base + (size_t)k * width + lane);
-      bw[(size_t)k * width + lane] = 0.f;
+      base[(size_t)k * width + lane] = 0.f;
     }
-    v += ld_cg_f32(base + (size_t)P.max_seg * width + lane);  // helper slot: kinks + low rank
-    bw[(size_t)P.max_seg * width + lane] = 0.f;
+    v += ld_cg_f32(base + (size_t)P.max_seg * width + lane);  // helper slot: kinks
+    base[(size_t)P.max_seg * width + lane] = 0.f;
   }
   // every consumed slot and the counter go back to zero: the whole workspace is zero between
   // launches, so launches of any geometry can share it
   if (lane == 0) P.cnt[s] = 0u;
-  strip_epilogue<EPI>(P, strip_info<NMAT>(P, s), v, lane);
+  const bool any_lr = __any_sync(0xffffffffu, kd > 0);
+  if (any_lr) {
+    float lr = 0.f;
+    if (P.tmp_k_ext != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < kd) lr += h2f(uv[j]) * __ldg(P.tmp_k_ext + j);
+    } else {
+      if (lane == 0) wait_counter_eq(&P.ctl[CTL_LR_DONE], gridDim.x * HX_HELP, 1000000000ull);  // 1 s bound
+      __syncwarp();
+      __threadfence();
+      const unsigned long long* acc = reinterpret_cast<const unsigned long long*>(P.ctl + CTL_TMPK) +
+                                      P.lr_off[si.m0 + mm];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j < kd) {
+          const double d = (double)(long long)ld_cg_u64(acc + j) * (1.0 / 4294967296.0);
+          lr += h2f(uv[j]) * ((float)d * sv[j]);
+        }
+      }
+    }
+    v += lr;
+  }
+  strip_epilogue<EPI>(P, si, v, lane);
 }
 
 // Count `units` toward strip s after this warp's slot writes; the warp completing the
-// strip (GU streaming units + 1 helper unit) finishes it.
+// strip (UPS streaming units + 1 helper unit) finishes it.
 template <int EPI, int NMAT>
 __device__ __forceinline__ void arrive(const HexmvParams& P, int s, unsigned units, int lane, bool fence = true) {
   if (fence) __threadfence();  // every lane that wrote part of the slot orders its stores before the count
@@ -334,13 +395,13 @@ __device__ __forceinline__ void arrive(const HexmvParams& P, int s, unsigned uni
   unsigned fin = 0;
   if (lane == 0) {
     const unsigned old = atomicAdd(&P.cnt[s], units);
-    fin = (old + units == (unsigned)P.GU + 1u);
+    fin = (old + units == (unsigned)P.UPS + 1u);
   }
   fin = __shfl_sync(0xffffffffu, fin, 0);
   if (fin) finish_strip<EPI, NMAT>(P, s, lane);
 }
 
-template <int EPI, int UG>
+template <int EPI, bool FULL>
 __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_constant__ HexmvParams P) {
   constexpr int NMAT = (EPI == GSDLQ_EPI_SWIGLU) ? 2 : 1;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -356,79 +417,103 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
   const uint32_t tab_off = HX_TAB_ABS - sbase;
   uint8_t* tab = smem + tab_off;
   float* xf = reinterpret_cast<float*>(smem + tab_off + HX_TAB_ABS);
-  const HxLayout LY = hx_layout(P.ovf_bytes, P.sc_strips, NMAT, G);
-  uint32_t* s_sc = reinterpret_cast<uint32_t*>(smem + LY.sc_off);
-  float* misc = reinterpret_cast<float*>(smem + LY.misc_off);  // [0] 1/rms, [1..16] reduction
+  const HxLayout LY = hx_layout(P.ovf_bytes);
+  uint32_t* ent = reinterpret_cast<uint32_t*>(smem + LY.ent_off);
+  float* red = reinterpret_cast<float*>(smem + LY.red_off);
 
-  // ---- 1. independent prologue: decode table, this CTA's scale window, first code prefetches
-  build_decode_table(tab, P);
-  const int w_cta0 = blockIdx.x * HX_STREAM;
-  const long long cta_u0 = it_begin(min(w_cta0, P.W), P.T, P.W);
-  const long long cta_u1 = it_begin(min(w_cta0 + HX_STREAM, P.W), P.T, P.W);
-  const int sc_first = (int)(cta_u0 / P.GU);
-  const int sc_n = (cta_u1 > cta_u0) ? (int)((cta_u1 - 1) / P.GU) - sc_first + 1 : 0;
-  const int scw_n = hx_sc_words(G);
-  {
-    // asynchronous 4-byte copies of whole rows (2-byte loads when G is odd and rows are not
-    // 4-byte aligned)
-    const int n_rows = sc_n * NMAT * 16;
-    for (int rid = warp; rid < n_rows; rid += HX_WARPS) {
-      const int ls = rid / (NMAT * 16), rem = rid - ls * NMAT * 16;
-      const int mm = rem >> 4, rr = rem & 15;
-      const StripInfo si = strip_info<NMAT>(P, sc_first + ls);
-      const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
-      const int row = min(si.rbase + rr, M.rows - 1);
-      const uint16_t* src = M.scales + (size_t)row * G;
-      uint32_t* dst = s_sc + (size_t)rid * scw_n;
-      if ((G & 1) == 0) {
-        for (int wi = lane; wi < G / 2; wi += 32) cp_async_4(dst + wi, src + 2 * wi);
-      } else {
-        for (int gg = lane; gg < G; gg += 32) reinterpret_cast<uint16_t*>(dst)[gg] = __ldg(src + gg);
-      }
-    }
-    cp_async_commit();
+  // ---- 1. independent prologue: decode entries, first unit's loads, helper Vt slices -------
+  if (tid < 256) ent[tid] = decode_entry(tid, P);
+  if (tid == 0) {
+    reinterpret_cast<uint32_t*>(red)[32] = 0x0100u;  // table address bits 16..23, read after a barrier
+    reinterpret_cast<uint32_t*>(red)[33] = 0u;
   }
-  const int w = w_cta0 + warp;
+
+  const int w = blockIdx.x * HX_STREAM + warp;
   const bool streamer = warp < HX_STREAM && w < P.W;
   const long long u0 = streamer ? it_begin(w, P.T, P.W) : 0;
   const long long u1 = streamer ? it_begin(w + 1, P.T, P.W) : 0;
-  const int GU = P.GU;
-  uint2 pf[NMAT][UG][2];  // codes of the next unit: [matrix][group][row g / row g+8]
-  // prefetch cursor: unit (strip pf_s, unit-in-strip pf_u) and this lane's code pointers
-  int pf_s = (int)(u0 / GU), pf_u = (int)(u0 - (long long)pf_s * GU);
-  const uint8_t* pfa[NMAT];
-  const uint8_t* pfb[NMAT];
+  // cursor (strip, matrix in strip, unit column) of the next unit to load, and its pointers
+  int ns = 0, nm = 0, nc = 0;
+  {
+    const long long s_ = u0 / P.UPS;
+    const int r_ = (int)(u0 - s_ * P.UPS);
+    ns = (int)s_;
+    nm = r_ / P.GU;
+    nc = r_ - nm * P.GU;
+  }
+  const uint8_t* pa = nullptr;
+  const uint8_t* pb = nullptr;
+  const uint16_t* qa = nullptr;
+  const uint16_t* qb = nullptr;
   auto seek = [&]() {
-    const StripInfo si = strip_info<NMAT>(P, pf_s);
-#pragma unroll
-    for (int mm = 0; mm < NMAT; ++mm) {
-      const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
-      const int ra = min(si.rbase + gl, M.rows - 1), rb = min(si.rbase + gl + 8, M.rows - 1);
-      pfa[mm] = M.codes + (size_t)ra * NP + pf_u * (UG * 32) + q * 8;
-      pfb[mm] = M.codes + (size_t)rb * NP + pf_u * (UG * 32) + q * 8;
+    const StripInfo si = strip_info<NMAT>(P, ns);
+    const gsdlq_hexmat_t& M = J.mat[si.m0 + nm];
+    const int ra = min(si.rbase + gl, M.rows - 1), rb = min(si.rbase + gl + 8, M.rows - 1);
+    pa = M.codes + (size_t)ra * NP + nc * HX_UB + q * 16;
+    pb = M.codes + (size_t)rb * NP + nc * HX_UB + q * 16;
+    qa = M.scales + (size_t)ra * G + nc * 8;
+    qb = M.scales + (size_t)rb * G + nc * 8;
+  };
+  auto advance = [&]() {
+    if (++nc == P.GU) {
+      nc = 0;
+      if (++nm == NMAT) {
+        nm = 0;
+        ++ns;
+      }
     }
   };
-  auto issue = [&]() {
-#pragma unroll
-    for (int mm = 0; mm < NMAT; ++mm) {
-#pragma unroll
-      for (int k = 0; k < UG; ++k) {
-        pf[mm][k][0] = ldg_stream_u2(pfa[mm] + 32 * k);
-        pf[mm][k][1] = ldg_stream_u2(pfb[mm] + 32 * k);
-      }
-      pfa[mm] += UG * 32;
-      pfb[mm] += UG * 32;
+  // the FULL path shifts the lane's fp16 scale out of a word holding two groups
+  const int sh = FULL ? 16 * (q & 1) : 0;
+  uint4 cw[4][2];      // code bytes of the unit being consumed / refilled: [segment][row g, g+8]
+  uint32_t sa[4], sb[4];  // the next unit's scale words: [segment]
+  auto load_codes = [&](int s) {
+    if (FULL || nc * HX_UB + 64 * s + 16 * q < NP) {
+      cw[s][0] = ldg_stream_u4(pa + 64 * s);
+      cw[s][1] = ldg_stream_u4(pb + 64 * s);
+    } else {
+      cw[s][0] = make_uint4(0u, 0u, 0u, 0u);  // past the row: its activations are staged as zero
+      cw[s][1] = make_uint4(0u, 0u, 0u, 0u);
     }
-    if (++pf_u == GU) {
-      pf_u = 0;
-      ++pf_s;
-      seek();
+  };
+  auto load_scales = [&]() {
+    if (FULL) {
+      const uint4 x = ldg_stream_u4(qa), y = ldg_stream_u4(qb);
+      sa[0] = x.x, sa[1] = x.y, sa[2] = x.z, sa[3] = x.w;
+      sb[0] = y.x, sb[1] = y.y, sb[2] = y.z, sb[3] = y.w;
+    } else {
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const int gi = 2 * s + (q & 1);
+        const bool ok = nc * 8 + gi < G;
+        sa[s] = ok ? (uint32_t)__ldg(qa + gi) : 0u;
+        sb[s] = ok ? (uint32_t)__ldg(qb + gi) : 0u;
+      }
     }
   };
   if (streamer && u1 > u0) {
     seek();
-    issue();
+    load_scales();
+#pragma unroll
+    for (int s = 0; s < 4; ++s) load_codes(s);
   }
+
+  // helper warps: pull this warp's column slice of every Vt row into L2 (no registers held)
+  const int hw = blockIdx.x * HX_HELP + (warp - HX_STREAM);
+  const int c8_0 = hw * P.lr_chunks;
+  const int c8_1 = min(c8_0 + P.lr_chunks, C / 8);
+  if (warp >= HX_STREAM) {
+    for (int jl = lane; jl < P.n_lr; jl += 32) {
+      int m = 0, j = jl;
+      while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
+      const uint8_t* vt = reinterpret_cast<const uint8_t*>(J.mat[m].Vt + (size_t)j * C);
+      for (int b = (c8_0 * 16) & ~127; b < c8_1 * 16; b += 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(vt + b));
+    }
+  }
+
+  __syncthreads();  // decode entries
+  for (int i = warp; i < 256; i += HX_WARPS) *reinterpret_cast<uint32_t*>(tab + i * 256 + lane * 4) = ent[i];
 
   // ---- 2. wait for the producer of x, then stage the input (fp32 and bf16 splits) ----------
   pdl_wait();
@@ -440,186 +525,183 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       tok = 0;
     }
   }
-  float inv = 1.f;
-  if (J.input_mode != GSDLQ_IN_PLAIN) {
-    float ss = 0.f;
-    for (int c = tid; c < C; c += HX_THREADS) {
-      const float v = (J.input_mode == GSDLQ_IN_EMBED) ? h2f(__ldg(J.embed + (size_t)tok * C + c)) : __ldg(J.x + c);
-      ss += v * v;
+  const bool normed = J.input_mode != GSDLQ_IN_PLAIN;
+  auto load_x = [&](int p) -> float2 {
+    if (J.input_mode == GSDLQ_IN_EMBED) {
+      const uint32_t raw = __ldg(reinterpret_cast<const unsigned int*>(J.embed + (size_t)tok * C) + p);
+      return make_float2(h2f(raw & 0xffffu), h2f(raw >> 16));
+    }
+    return __ldg(reinterpret_cast<const float2*>(J.x) + p);
+  };
+  auto stage = [&](int p, float x0, float x1, float2 wv) {
+    if (J.input_mode == GSDLQ_IN_EMBED && blockIdx.x == 0 && J.x_out)
+      reinterpret_cast<float2*>(J.x_out)[p] = make_float2(x0, x1);
+    if (normed) {
+      const float inv = red[0];
+      x0 = __fmul_rn(__fmul_rn(x0, inv), wv.x);
+      x1 = __fmul_rn(__fmul_rn(x1, inv), wv.y);
+    }
+    reinterpret_cast<float2*>(xf)[p] = make_float2(x0, x1);
+    const float b = fmaf(0.8660254037844386f, x1, 0.5f * x0);
+    uint32_t h, l;
+    split_bf16x2(x0, b, h, l);
+    const int j = p & 63, r = j & 15;
+    const uint32_t off = xs_chunk((p >> 6) * 4 + (r >> 2), tab_off) + (uint32_t)((j >> 4) * 32 + (r & 3) * 4);
+    *reinterpret_cast<uint32_t*>(smem + off) = h;
+    *reinterpret_cast<uint32_t*>(smem + off + 16) = l;
+  };
+  // pass 1: the first XR pairs of each thread stay in registers; sum of squares
+  constexpr int XR = 4;
+  float2 xv[XR], wv[XR];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < XR; ++k) {
+    const int p = tid + k * HX_THREADS;
+    if (p < NP) {
+      xv[k] = load_x(p);
+      wv[k] = normed ? __ldg(reinterpret_cast<const float2*>(J.norm_w) + p) : make_float2(1.f, 1.f);
+    }
+  }
+  if (normed) {
+#pragma unroll
+    for (int k = 0; k < XR; ++k)
+      if (tid + k * HX_THREADS < NP) ss += xv[k].x * xv[k].x + xv[k].y * xv[k].y;
+    for (int p = tid + XR * HX_THREADS; p < NP; p += HX_THREADS) {
+      const float2 v = load_x(p);
+      ss += v.x * v.x + v.y * v.y;
     }
     ss = warp_sum(ss);
-    if (lane == 0) misc[1 + warp] = ss;
+    if (lane == 0) red[1 + warp] = ss;
     __syncthreads();
     if (tid == 0) {
       float t = 0.f;
-      for (int k = 0; k < HX_WARPS; ++k) t += misc[1 + k];
-      misc[0] = 1.0f / sqrtf(t / (float)C + J.eps);  // gsd_lq_cpu_engine.c:78
+      for (int k = 0; k < HX_WARPS; ++k) t += red[1 + k];
+      red[0] = 1.0f / sqrtf(t / (float)C + J.eps);  // gsd_lq_cpu_engine.c:78
     }
     __syncthreads();
-    inv = misc[0];
   }
-  // loads of a batch are issued before any shared store, so they overlap (the generic input
-  // pointers could otherwise be assumed to alias shared memory and serialise)
-  constexpr int XB = 8;
-  for (int p0 = tid; p0 < NP; p0 += XB * HX_THREADS) {
-    float2 xv[XB], wv[XB];
 #pragma unroll
-    for (int k = 0; k < XB; ++k) {
-      const int p = p0 + k * HX_THREADS;
-      if (p < NP) {
-        if (J.input_mode == GSDLQ_IN_EMBED) {
-          const uint32_t raw = __ldg(reinterpret_cast<const unsigned int*>(J.embed + (size_t)tok * C) + p);
-          xv[k] = make_float2(h2f(raw & 0xffffu), h2f(raw >> 16));
-        } else {
-          xv[k] = __ldg(reinterpret_cast<const float2*>(J.x) + p);
-        }
-        wv[k] = (J.input_mode != GSDLQ_IN_PLAIN) ? __ldg(reinterpret_cast<const float2*>(J.norm_w) + p)
-                                                 : make_float2(1.f, 1.f);
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < XB; ++k) {
-      const int p = p0 + k * HX_THREADS;
-      if (p < NP) {
-        float x0 = xv[k].x, x1 = xv[k].y;
-        if (J.input_mode == GSDLQ_IN_EMBED && blockIdx.x == 0 && J.x_out)
-          reinterpret_cast<float2*>(J.x_out)[p] = make_float2(x0, x1);
-        if (J.input_mode != GSDLQ_IN_PLAIN) {
-          x0 = __fmul_rn(__fmul_rn(x0, inv), wv[k].x);
-          x1 = __fmul_rn(__fmul_rn(x1, inv), wv[k].y);
-        }
-        reinterpret_cast<float2*>(xf)[p] = make_float2(x0, x1);
-        const float b = fmaf(0.8660254037844386f, x1, 0.5f * x0);
-        uint32_t h, l;
-        split_bf16x2(x0, b, h, l);
-        // pair i of group g: hi word at i*4 of chunk 2g; lo word in chunk 2g+1 with the two
-        // 16-byte halves of each 32-byte lane segment swapped (see the B-fragment loads)
-        const int g = p >> 5, i = p & 31;
-        const int ilo = (i & ~7) | ((i + 4) & 7);
-        *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g, tab_off) + 4 * i) = h;
-        *reinterpret_cast<uint32_t*>(smem + xs_chunk(2 * g + 1, tab_off) + 4 * ilo) = l;
-      }
-    }
+  for (int k = 0; k < XR; ++k) {
+    const int p = tid + k * HX_THREADS;
+    if (p < NP) stage(p, xv[k].x, xv[k].y, wv[k]);
   }
-  if (tid == 0) reinterpret_cast<uint32_t*>(misc)[32] = 0x0100u;  // table address bits 16..23, read after the barrier
-  cp_async_wait_all();  // the staged scale window
+  for (int p = tid + XR * HX_THREADS; p < NP; p += HX_THREADS) {
+    const float2 v = load_x(p);
+    stage(p, v.x, v.y, normed ? __ldg(reinterpret_cast<const float2*>(J.norm_w) + p) : make_float2(1.f, 1.f));
+  }
+  // pairs past the row end of the last unit read zero activations
+  for (int p = NP + tid; p < P.GU * (HX_UB); p += HX_THREADS) {
+    const int j = p & 63, r = j & 15;
+    const uint32_t off = xs_chunk((p >> 6) * 4 + (r >> 2), tab_off) + (uint32_t)((j >> 4) * 32 + (r & 3) * 4);
+    *reinterpret_cast<uint32_t*>(smem + off) = 0u;
+    *reinterpret_cast<uint32_t*>(smem + off + 16) = 0u;
+  }
   __syncthreads();
 
   if (warp >= HX_STREAM) {
-    // ---- helper warps: low-rank projections, then per-strip kink + low-rank slots --------
-    unsigned* ctl = P.ctl;
-    while (true) {
-      unsigned t = 0;
-      if (lane == 0) t = atomicAdd(&ctl[CTL_TK_TICKET], 1u);
-      t = __shfl_sync(0xffffffffu, t, 0);
-      if ((int)t >= P.n_lr_jobs) break;
-      int m = 0, j = (int)t;
-      while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
-      const gsdlq_hexmat_t& M = J.mat[m];
-      const uint4* vt = reinterpret_cast<const uint4*>(M.Vt + (size_t)j * C);
-      float acc = 0.f;
-      for (int c8 = lane; c8 < C / 8; c8 += 4 * 32) {
-        uint4 raw[4];
+    // ---- helper warps: low-rank slice partials, then kink slots of their strips -----------
+    const int H = gridDim.x * HX_HELP;
+    if (P.n_lr > 0) {
+      for (int jl = lane; jl < P.n_lr; jl += 32) {
+        int m = 0, j = jl;
+        while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
+        const uint4* vt = reinterpret_cast<const uint4*>(J.mat[m].Vt + (size_t)j * C);
+        float acc = 0.f;
+        for (int cb = c8_0; cb < c8_1; cb += 8) {
+          uint4 raw[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) raw[u] = (c8 + 32 * u < C / 8) ? __ldg(vt + c8 + 32 * u) : make_uint4(0, 0, 0, 0);
+          for (int k = 0; k < 8; ++k) raw[k] = (cb + k < c8_1) ? __ldg(vt + cb + k) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (c8 + 32 * u < C / 8) {
-            const float4* xp = reinterpret_cast<const float4*>(xf + 8 * (c8 + 32 * u));
-            const float4 a = xp[0], b = xp[1];
-            acc += a.x * h2f(raw[u].x & 0xffffu) + a.y * h2f(raw[u].x >> 16) + a.z * h2f(raw[u].y & 0xffffu) +
-                   a.w * h2f(raw[u].y >> 16) + b.x * h2f(raw[u].z & 0xffffu) + b.y * h2f(raw[u].z >> 16) +
-                   b.z * h2f(raw[u].w & 0xffffu) + b.w * h2f(raw[u].w >> 16);
+          for (int k = 0; k < 8; ++k) {
+            if (cb + k < c8_1) {
+              const float4* xp = reinterpret_cast<const float4*>(xf + 8 * (cb + k));
+              const float4 a = xp[0], b = xp[1];
+              acc += a.x * h2f(raw[k].x & 0xffffu) + a.y * h2f(raw[k].x >> 16) + a.z * h2f(raw[k].y & 0xffffu) +
+                     a.w * h2f(raw[k].y >> 16) + b.x * h2f(raw[k].z & 0xffffu) + b.y * h2f(raw[k].z >> 16) +
+                     b.z * h2f(raw[k].w & 0xffffu) + b.w * h2f(raw[k].w >> 16);
+            }
           }
         }
+        if (!(fabsf(acc) < LR_MAX)) {
+          raise_flag(GSDLQ_FLAG_RANGE);
+          acc = (acc != acc) ? 0.f : copysignf(LR_MAX, acc);
+        }
+        const long long fx = __float2ll_rn(acc * LR_FIX);
+        atomicAdd(reinterpret_cast<unsigned long long*>(P.ctl + CTL_TMPK) + jl, (unsigned long long)fx);
       }
-      acc = warp_sum(acc);
-      if (lane == 0) {
-        reinterpret_cast<volatile float*>(ctl)[CTL_TMPK + m * 16 + j] = acc * M.S[j];
-        __threadfence();
-        atomicAdd(&ctl[CTL_TK_DONE], 1u);
-      }
-    }
-    if (P.n_lr_jobs > 0) {
-      if (lane == 0) wait_counter_geq(&ctl[CTL_TK_DONE], (unsigned)P.n_lr_jobs, 1000000000ull);  // 1 s bound
-      __syncwarp();
       __threadfence();
+      __syncwarp();
+      if (lane == 0) atomicAdd(&P.ctl[CTL_LR_DONE], 1u);
     }
+    // kinks: lane = row.  Pair mode: one 32-row strip per pass; otherwise two 16-row strips
+    constexpr int SPP = (NMAT == 2) ? 1 : 2;
     constexpr int width = NMAT * 16;
-    while (true) {
-      unsigned s = 0;
-      if (lane == 0) s = atomicAdd(&ctl[CTL_KINK_TICKET], 1u);
-      s = __shfl_sync(0xffffffffu, s, 0);
-      if ((int)s >= P.n_strips) break;
-      const StripInfo si = strip_info<NMAT>(P, (int)s);
-      const int r = lane & 15, hi = lane >> 4;
-      const int mm = (NMAT == 2) ? hi : 0;
+    for (int s0 = hw; s0 < P.n_strips; s0 += SPP * H) {
+      const int s = (NMAT == 2) ? s0 : s0 + (lane >> 4) * H;
+      const bool sv = s < P.n_strips;
+      const StripInfo si = strip_info<NMAT>(P, sv ? s : s0);
+      const int mm = (NMAT == 2) ? (lane >> 4) : 0;
       const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
-      const int row = si.rbase + r;
-      float v = 0.f;
-      if (row < M.rows) {
-        // low-rank term first: its U loads do not depend on row_ptr
-        if (M.k_dim > 0 && (NMAT == 2 || hi == 0)) {
-          const uint16_t* ur = M.U + (size_t)row * M.k_dim;
-          uint16_t uv[16];
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) uv[jj] = jj < M.k_dim ? __ldg(ur + jj) : (uint16_t)0;
-          const float* tk = P.tmp_k_ext ? P.tmp_k_ext : reinterpret_cast<const float*>(ctl) + CTL_TMPK + (si.m0 + mm) * 16;
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj)
-            if (jj < M.k_dim) v += h2f(uv[jj]) * __ldcg(tk + jj);
-        }
-        const uint32_t e0 = __ldg(M.row_ptr + row), e1 = __ldg(M.row_ptr + row + 1);
-        constexpr int step = (NMAT == 2) ? 1 : 2;
-        // kinks in batches of 16: the batch's loads are issued together
-        for (uint32_t e = e0 + (NMAT == 2 ? 0 : hi); e < e1; e += 16 * step) {
-          int col[16];
-          float dl[16];
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const uint32_t eu = e + u * step;
-            col[u] = eu < e1 ? (int)__ldg(M.kink_cols + eu) : 0;
-            dl[u] = eu < e1 ? __ldg(M.kink_deltas + eu) : 0.f;
-          }
-          bool bad = false;
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const bool ok = col[u] < C;
-            v += ok ? dl[u] * xf[ok ? col[u] : 0] : 0.f;
-            bad |= !ok;
-          }
-          if (bad) raise_flag(GSDLQ_FLAG_BAD_KINK);
-        }
+      const int row = si.rbase + (lane & 15);
+      uint32_t e = 0u, e1 = 0u;
+      if (sv && row < M.rows) {
+        e = __ldg(M.row_ptr + row);
+        e1 = __ldg(M.row_ptr + row + 1);
       }
-      if (NMAT == 1) v += __shfl_xor_sync(0xffffffffu, v, 16);
-      float* slot = P.part + ((size_t)s * (P.max_seg + 1) + P.max_seg) * width;
-      if (lane < width) slot[lane] = v;
-      arrive<EPI, NMAT>(P, (int)s, 1u, lane);
+      float v = 0.f;
+      bool bad = false;
+      while (__any_sync(0xffffffffu, e < e1)) {
+        int col[8];
+        float dl[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint32_t eu = e + u;
+          col[u] = eu < e1 ? (int)__ldg(M.kink_cols + eu) : 0;
+          dl[u] = eu < e1 ? __ldg(M.kink_deltas + eu) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const bool ok = col[u] < C;
+          v += ok ? dl[u] * xf[ok ? col[u] : 0] : 0.f;
+          bad |= !ok;
+        }
+        e += 8u;
+      }
+      if (bad) raise_flag(GSDLQ_FLAG_BAD_KINK);
+      if (sv) P.part[((size_t)s * (P.max_seg + 1) + P.max_seg) * width + (lane & (width - 1))] = v;
+      arrive<EPI, NMAT>(P, s0, 1u, lane);
+      if (SPP == 2 && s0 + H < P.n_strips) arrive<EPI, NMAT>(P, s0 + H, 1u, lane, false);
     }
   } else if (streamer) {
     // ---- streaming warps --------------------------------------------------------------
-    const uint32_t lane4x = (uint32_t)lane * 4u | reinterpret_cast<const volatile uint32_t*>(misc)[32];
-    // B fragments: lane (gl, q) supplies column n = gl of B.  Column 0 is the hi split, column 1
-    // the lo split; the lo chunk stores each lane segment's halves swapped, so the 8 lanes of
-    // columns 0-1 touch 32 distinct banks per 16-byte load and all receive pairs 0-3 first.
-    // Columns 2-7 only feed D columns 2-7, which are never read, so lanes gl >= 2 simply load the
-    // same addresses as lanes gl & 1 (a broadcast: no extra wavefronts, no divergent branch).
-    const int gb = gl & 1;
-    const uint32_t boff0 = (uint32_t)(q * 32 + 16 * gb), boff1 = (uint32_t)(q * 32 + 16 * (1 - gb));
-    int cur_s = (int)(u0 / GU), cur_u = (int)(u0 - (long long)cur_s * GU);
+    const uint32_t lane4x = (uint32_t)lane * 4u | reinterpret_cast<const volatile uint32_t*>(red)[32];
+    const uint32_t dep = reinterpret_cast<const volatile uint32_t*>(red)[33];  // zero, read after the barrier
+    // B operand: lane (g, q) supplies column g.  Columns 0/1 (hi/lo of group A) are nonzero only
+    // on the k rows of lanes q = 0, 1, columns 2/3 (group B) only on those of q = 2, 3, columns
+    // 4-7 are zero.  Every lane loads the slice of a lane that has real data in its column (so
+    // a warp reads 8 distinct 16-byte slices = one conflict-free 128-byte chunk) and masks.
+    const int g3 = gl & 3;
+    const bool same = (g3 >> 1) == (q >> 1);
+    const uint32_t boff = (uint32_t)((same ? q : (q ^ 2)) * 32 + (gl & 1) * 16);
+    const uint32_t bmask = (gl < 4 && same) ? 0xffffffffu : 0u;
+    int cur_s = ns, cur_m = nm, cur_c = nc;
+    advance();
+    seek();
     int seg_s = cur_s;
     float acc[NMAT][2];
 #pragma unroll
     for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
     auto emit = [&](int s) {
-      const int seg = w - warp_of((long long)s * GU, P.T, P.W);
+      const int seg = w - warp_of((long long)s * P.UPS, P.T, P.W);
       constexpr int width = NMAT * 16;
       float* slot = P.part + ((size_t)s * (P.max_seg + 1) + seg) * width;
-      if (q == 0) {
 #pragma unroll
-        for (int mm = 0; mm < NMAT; ++mm) {
-          slot[mm * 16 + gl] = acc[mm][0];
-          slot[mm * 16 + gl + 8] = acc[mm][1];
+      for (int mm = 0; mm < NMAT; ++mm) {
+        const float vg = acc[mm][0] + __shfl_xor_sync(0xffffffffu, acc[mm][0], 1);
+        const float vh = acc[mm][1] + __shfl_xor_sync(0xffffffffu, acc[mm][1], 1);
+        if (q == 0) {
+          slot[mm * 16 + gl] = vg;
+          slot[mm * 16 + gl + 8] = vh;
         }
       }
     };
@@ -630,48 +712,46 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
 #pragma unroll
         for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
       }
-      uint2 cur[NMAT][UG][2];
+      const bool more = u + 1 < u1;
+      // this unit's scales; the next unit's scales go into flight
+      uint32_t swa[4], swb[4];
 #pragma unroll
-      for (int mm = 0; mm < NMAT; ++mm)
+      for (int s = 0; s < 4; ++s) swa[s] = sa[s], swb[s] = sb[s];
+      if (more) load_scales();
+      const int ch0 = cur_c * 16;
+      const uint32_t bstride = ch0 < 256 ? 256u : 128u;
+      const uint32_t bbase = sbase + xs_chunk(ch0, tab_off) + dep + boff;  // absolute shared address
+      float rg_sum = 0.f, rh_sum = 0.f;
 #pragma unroll
-        for (int k = 0; k < UG; ++k) {
-          cur[mm][k][0] = pf[mm][k][0];
-          cur[mm][k][1] = pf[mm][k][1];
-        }
-      if (u + 1 < u1) issue();
-      // this lane's staged scale rows (gl and gl + 8) of the unit's strip
-      const uint16_t* sra = reinterpret_cast<const uint16_t*>(s_sc + ((size_t)((cur_s - sc_first) * NMAT) * 16 + gl) * scw_n);
-#pragma unroll
-      for (int k = 0; k < UG; ++k) {
-        const int g = cur_u * UG + k;
-        const uint8_t* src = smem + xs_chunk(2 * g + gb, tab_off);
-        const uint4 v0 = *reinterpret_cast<const uint4*>(src + boff0);
-        const uint4 v1 = *reinterpret_cast<const uint4*>(src + boff1);
-        const uint32_t bq[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-        for (int mm = 0; mm < NMAT; ++mm) {
-          const uint16_t* sr = sra + (size_t)mm * 16 * scw_n * 2;
-          const float sa = h2f(sr[g]), sb = h2f(sr[8 * scw_n * 2 + g]);
-          float rg, rh;
-          group_mma(cur[mm][k][0], cur[mm][k][1], bq, lane4x, rg, rh);
-          acc[mm][0] = fmaf(sa, rg, acc[mm][0]);
-          acc[mm][1] = fmaf(sb, rh, acc[mm][1]);
-        }
+      for (int s = 0; s < 4; ++s) {
+        float rg, rh;
+        segment_mma(cw[s][0], cw[s][1], bbase + (uint32_t)s * 4u * bstride, bstride, bmask, lane4x, rg, rh);
+        if (more) load_codes(s);  // refill this segment's registers with the next unit
+        rg_sum = fmaf(h2f((uint16_t)(swa[s] >> sh)), rg, rg_sum);
+        rh_sum = fmaf(h2f((uint16_t)(swb[s] >> sh)), rh, rh_sum);
       }
-      if (++cur_u == GU) {
-        cur_u = 0;
-        ++cur_s;
+      if (NMAT == 1 || cur_m == 0) {
+        acc[0][0] += rg_sum;
+        acc[0][1] += rh_sum;
+      } else {
+        acc[NMAT - 1][0] += rg_sum;
+        acc[NMAT - 1][1] += rh_sum;
+      }
+      cur_s = ns, cur_m = nm, cur_c = nc;
+      if (more) {
+        advance();
+        seek();
       }
     }
     if (u1 > u0) {
       emit(seg_s);
       // the counts are deferred to the end of the range: a fence mid-range would wait for the code
-      // prefetches in flight.  One fence covers all of this warp's slot stores, then one count per
+      // loads in flight.  One fence covers all of this warp's slot stores, then one count per
       // strip the range touched.
       __threadfence();
-      const int s_a = (int)(u0 / GU), s_b = (int)((u1 - 1) / GU);
+      const int s_a = (int)(u0 / P.UPS), s_b = (int)((u1 - 1) / P.UPS);
       for (int s = s_a; s <= s_b; ++s) {
-        const long long a = max(u0, (long long)s * GU), b = min(u1, (long long)s * GU + GU);
+        const long long a = max(u0, (long long)s * P.UPS), b = min(u1, (long long)s * P.UPS + P.UPS);
         arrive<EPI, NMAT>(P, s, (unsigned)(b - a), lane, false);
       }
     }
@@ -692,8 +772,9 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
 // ---- host side ------------------------------------------------------------------------
 static int hexmv_validate_mat(const gsdlq_hexmat_t& M, int cols, bool own_lowrank) {
   if (!M.codes || !M.scales || !M.row_ptr) return GSDLQ_ERR_INVALID;
-  // codes are read 8 bytes at a time from row starts (cols/2 is a multiple of 32)
-  if (reinterpret_cast<uintptr_t>(M.codes) & 7u) return GSDLQ_ERR_INVALID;
+  // codes are read 16 bytes at a time from row starts (cols/2 is a multiple of 32)
+  if (reinterpret_cast<uintptr_t>(M.codes) & 15u) return GSDLQ_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(M.scales) & 1u) return GSDLQ_ERR_INVALID;
   if (M.rows <= 0 || M.cols != cols || cols <= 0 || cols % 64 != 0) return GSDLQ_ERR_INVALID;
   if (M.k_dim < 0 || M.k_dim > 16) return GSDLQ_ERR_INVALID;
   if (M.k_dim > 0 && !M.U) return GSDLQ_ERR_INVALID;
@@ -716,7 +797,6 @@ static int hexmv_plan(HexmvParams& P) {
   P.cols = C;
   P.G = C / 64;
   P.NP = C / 2;
-  if (C > 65535) return GSDLQ_ERR_UNSUPPORTED;  // u16 kink columns
   P.nmat = (J.epilogue == GSDLQ_EPI_SWIGLU) ? 2 : 1;
   if (P.nmat == 2) {
     if (J.n_mat != 2) return GSDLQ_ERR_INVALID;
@@ -726,41 +806,46 @@ static int hexmv_plan(HexmvParams& P) {
     for (int m = 0; m < J.n_mat; ++m) P.strip_begin[m + 1] = P.strip_begin[m] + (J.mat[m].rows + 15) / 16;
     P.n_strips = P.strip_begin[J.n_mat];
   }
-  // work unit: UG consecutive groups of one strip (4, or 2 in pair mode, when G allows)
-  const int ug_max = (P.nmat == 2) ? 2 : 4;
-  P.UG = (P.G % ug_max == 0) ? ug_max : ((P.G % 2 == 0) ? 2 : 1);
-  P.GU = P.G / P.UG;
-  P.T = (long long)P.n_strips * P.GU;
+  P.GU = (P.G + 7) / 8;
+  P.UPS = P.nmat * P.GU;
+  P.T = (long long)P.n_strips * P.UPS;
   const int max_w = num_sms() * HX_STREAM;
   P.W = (int)std::min<long long>(max_w, P.T);
   const long long lmin = P.T / P.W;
-  P.max_seg = (int)((P.GU - 1 + lmin - 1) / lmin) + 1;
-  int lr = 0;
-  for (int m = 0; m < J.n_mat; ++m) lr += J.mat[m].k_dim;
-  P.n_lr_jobs = P.tmp_k_ext ? 0 : lr;
-  // staged-scale window: the most strips one CTA's 14 warps touch
+  P.max_seg = (int)((P.UPS - 1 + lmin - 1) / lmin) + 1;
   const int grid = (P.W + HX_STREAM - 1) / HX_STREAM;
-  int sc = 1;
-  for (int c = 0; c < grid; ++c) {
-    const long long a = it_begin(std::min(c * HX_STREAM, P.W), P.T, P.W);
-    const long long b = it_begin(std::min((c + 1) * HX_STREAM, P.W), P.T, P.W);
-    if (b > a) sc = std::max(sc, (int)((b - 1) / P.GU - a / P.GU + 1));
+  int lr = 0;
+  for (int m = 0; m < 4; ++m) P.lr_off[m] = 0;
+  for (int m = 0; m < J.n_mat; ++m) {
+    P.lr_off[m] = lr;
+    lr += J.mat[m].k_dim;
   }
-  P.sc_strips = sc;
-  P.ovf_bytes = std::max(0, 2 * P.G - 256) * 128;
+  P.n_lr = P.tmp_k_ext ? 0 : lr;
+  const int helpers = grid * HX_HELP;
+  P.lr_chunks = (C / 8 + helpers - 1) / helpers;
+  P.ovf_bytes = std::max(0, P.GU * 16 - 256) * 128;
+  // shared-memory limits: overflow chunks below the table, xf above it
+  if (hx_layout(P.ovf_bytes).low_end > (int)HX_TAB_ABS - HX_BASE_MAX || hx_dyn_smem(C) > 227 * 1024)
+    return GSDLQ_ERR_UNSUPPORTED;
   return GSDLQ_OK;
 }
 
-template <int EPI, int UG>
+// 16-byte scale loads: every row's scales start 16-byte aligned and no unit is partial
+static bool hexmv_full(const HexmvParams& P) {
+  if (P.G % 8 != 0) return false;
+  for (int m = 0; m < P.job.n_mat; ++m)
+    if (reinterpret_cast<uintptr_t>(P.job.mat[m].scales) & 15u) return false;
+  return true;
+}
+
+template <int EPI, bool FULL>
 static int hexmv_launch_t(const HexmvParams& P, cudaStream_t s) {
-  const HxLayout LY = hx_layout(P.ovf_bytes, P.sc_strips, P.nmat, P.G);
   const int dyn = hx_dyn_smem(P.cols);
-  if (LY.low_end > (int)HX_TAB_ABS - HX_BASE_MAX || dyn > 227 * 1024) return GSDLQ_ERR_UNSUPPORTED;
   static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(hexmv_kernel<EPI, UG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(hexmv_kernel<EPI, FULL>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return record_cuda_error(e);
     configured[dev] = true;
   }
@@ -775,7 +860,7 @@ static int hexmv_launch_t(const HexmvParams& P, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, hexmv_kernel<EPI, UG>, P);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, hexmv_kernel<EPI, FULL>, P);
   if (e != cudaSuccess) return record_cuda_error(e);
   return GSDLQ_OK;
 }
@@ -787,6 +872,7 @@ static int hexmv_check_io(const HexmvParams& P) {
   if (J.input_mode == GSDLQ_IN_RMSNORM && (!J.x || !J.norm_w)) return GSDLQ_ERR_INVALID;
   if (J.input_mode == GSDLQ_IN_EMBED && (!J.embed || !J.token || !J.norm_w || J.vocab <= 0)) return GSDLQ_ERR_INVALID;
   if (J.input_mode != GSDLQ_IN_EMBED && (reinterpret_cast<uintptr_t>(J.x) & 7u)) return GSDLQ_ERR_INVALID;
+  if (J.input_mode != GSDLQ_IN_PLAIN && (reinterpret_cast<uintptr_t>(J.norm_w) & 7u)) return GSDLQ_ERR_INVALID;
   if (J.input_mode == GSDLQ_IN_EMBED && (reinterpret_cast<uintptr_t>(J.embed) & 3u)) return GSDLQ_ERR_INVALID;
   switch (J.epilogue) {
     case GSDLQ_EPI_STORE:
@@ -810,20 +896,17 @@ static int hexmv_check_io(const HexmvParams& P) {
 }
 
 template <int EPI>
-static int hexmv_dispatch_ug(const HexmvParams& P, cudaStream_t s) {
-  if constexpr (EPI != GSDLQ_EPI_SWIGLU) {  // pair mode never uses 4-group units
-    if (P.UG == 4) return hexmv_launch_t<EPI, 4>(P, s);
-  }
-  if (P.UG == 2) return hexmv_launch_t<EPI, 2>(P, s);
-  return hexmv_launch_t<EPI, 1>(P, s);
+static int hexmv_dispatch_full(const HexmvParams& P, cudaStream_t s) {
+  if (hexmv_full(P)) return hexmv_launch_t<EPI, true>(P, s);
+  return hexmv_launch_t<EPI, false>(P, s);
 }
 
 static int hexmv_dispatch(const HexmvParams& P, cudaStream_t s) {
   switch (P.job.epilogue) {
-    case GSDLQ_EPI_STORE: return hexmv_dispatch_ug<GSDLQ_EPI_STORE>(P, s);
-    case GSDLQ_EPI_RESID: return hexmv_dispatch_ug<GSDLQ_EPI_RESID>(P, s);
-    case GSDLQ_EPI_SWIGLU: return hexmv_dispatch_ug<GSDLQ_EPI_SWIGLU>(P, s);
-    default: return hexmv_dispatch_ug<GSDLQ_EPI_ROPE_KV>(P, s);
+    case GSDLQ_EPI_STORE: return hexmv_dispatch_full<GSDLQ_EPI_STORE>(P, s);
+    case GSDLQ_EPI_RESID: return hexmv_dispatch_full<GSDLQ_EPI_RESID>(P, s);
+    case GSDLQ_EPI_SWIGLU: return hexmv_dispatch_full<GSDLQ_EPI_SWIGLU>(P, s);
+    default: return hexmv_dispatch_full<GSDLQ_EPI_ROPE_KV>(P, s);
   }
 }
 

@@ -45,6 +45,7 @@ extern "C" {
 #define GSDLQ_FLAG_TIMEOUT 0x10u   /* a bounded device-side wait gave up */
 #define GSDLQ_FLAG_BAD_TOKEN 0x20u /* token id >= vocab: embedding row skipped */
 #define GSDLQ_FLAG_UNSUPPORTED 0x40u /* a kernel found a device limit it was not built for and did nothing */
+#define GSDLQ_FLAG_RANGE 0x80u     /* a low-rank partial sum left the +-2^22 fixed-point range (clamped) */
 
 typedef void *gsdlq_stream_t;
 

@@ -196,15 +196,16 @@ def test_flags_bad_kink_and_bad_pos(env, restated, rng):
 
 
 def test_bounded_wait_times_out_without_hanging(env, rng):
-    """The low-rank counter never reaches its target (every ticket pre-taken in the workspace, so
-    nobody produces tmp_k): the helpers' bounded wait gives up after ~1 s and raises a flag."""
+    """The low-rank completion counter starts dirty in the workspace, so it never equals the
+    number of helper warps: the finishing warps' bounded wait gives up after ~1 s and raises a
+    flag instead of reading a half-built tmp_k."""
     ops, L = env
     t = rand_hex(rng, 64, 256, k=4, nnz=0)
     x = rng.standard_normal(256).astype(np.float32)
     y = torch.zeros(64, device="cuda")
     j = make_job(L, [ops.DeviceHex(t)], L.IN_PLAIN, x=dev(x), epilogue=L.EPI_STORE, ys=(y,))
     ws = ops.linear_workspace(j)
-    ws[0] = 1 << 20  # low-rank ticket counter
+    ws[0] = 1 << 20  # low-rank completion counter
     ops.linear(j, ws)
     torch.cuda.synchronize()
     flags = L.device_flags()
