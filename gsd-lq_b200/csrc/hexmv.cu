@@ -1009,3 +1009,63 @@ extern "C" int gsdlq_hex2d_matvec(const float* x, const uint8_t* codes, const ui
   }
   return hexmv_launch(P, ws.p, ws.bytes, static_cast<cudaStream_t>(stream));
 }
+
+// ---- allocation-free matvec ------------------------------------------------------------
+// Scratch for gsdlq_hex2d_matvec_noalloc: a fixed array in the library's device image, so a
+// call never allocates.  Host code must not pass `g_noalloc_ws` itself to a kernel (on the
+// host it names a stand-in, not device memory); the device address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+namespace gsdlq {
+static __device__ __align__(256) unsigned char g_noalloc_ws[GSDLQ_NOALLOC_WS_BYTES];
+static void* g_noalloc_addr[64];
+}  // namespace gsdlq
+
+extern "C" int gsdlq_hex2d_matvec_noalloc(const float* x, const uint8_t* codes, const uint16_t* scales,
+                                          const float* xy_table, const uint16_t* U, const float* tmp_k,
+                                          const uint32_t* kink_row_ptr, const uint16_t* kink_cols,
+                                          const float* kink_deltas, float* y, int rows, int cols, int k_dim,
+                                          int n_pts, gsdlq_stream_t stream) {
+  if (!x || !codes || !scales || !xy_table || !kink_row_ptr || !y) return GSDLQ_ERR_INVALID;
+  if (n_pts <= 0 || n_pts > 256) return GSDLQ_ERR_INVALID;
+  if (k_dim > 0 && (!U || !tmp_k)) return GSDLQ_ERR_INVALID;
+  HexmvParams P{};
+  gsdlq_linear_job_t& J = P.job;
+  J.n_mat = 1;
+  gsdlq_hexmat_t& M = J.mat[0];
+  M.codes = codes;
+  M.scales = scales;
+  M.U = U;
+  M.row_ptr = kink_row_ptr;
+  M.kink_cols = kink_cols;
+  M.kink_deltas = kink_deltas;
+  M.rows = rows;
+  M.cols = cols;
+  M.k_dim = k_dim;
+  M.radius = 8;  // unused when xy_table is given
+  J.input_mode = GSDLQ_IN_PLAIN;
+  J.x = x;
+  J.epilogue = GSDLQ_EPI_STORE;
+  J.y[0] = y;
+  P.xy_table = xy_table;
+  P.n_pts = n_pts;
+  P.tmp_k_ext = k_dim > 0 ? tmp_k : nullptr;
+  const size_t need = hexmv_ws_bytes(P);
+  if (need == 0) return GSDLQ_ERR_INVALID;
+  if (need > (size_t)GSDLQ_NOALLOC_WS_BYTES) return GSDLQ_ERR_UNSUPPORTED;  // beyond the fixed scratch
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  if (dev < 0 || dev >= 64) return GSDLQ_ERR_UNSUPPORTED;
+  if (g_noalloc_addr[dev] == nullptr) {  // set-up, once per device (this device is current)
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_ws);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    g_noalloc_addr[dev] = p;
+  }
+  void* ws = g_noalloc_addr[dev];
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the array keeps whatever the previous call left: clear the bytes this launch needs at zero
+  e = cudaMemsetAsync(ws, 0, need, s);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  return hexmv_launch(P, ws, (size_t)GSDLQ_NOALLOC_WS_BYTES, s);
+}

@@ -193,6 +193,36 @@ int gsdlq_linear_ws_size(const gsdlq_linear_job_t *job, size_t *bytes);
 int gsdlq_linear(const gsdlq_linear_job_t *job, void *workspace, size_t workspace_bytes,
                  gsdlq_stream_t stream);
 
+/* Size of the library's fixed device scratch array used by gsdlq_hex2d_matvec_noalloc. */
+#define GSDLQ_NOALLOC_WS_BYTES (4u << 20)
+
+/* gsdlq_hex2d_matvec without any device allocation.  No counterpart in the reference:
+ * the reference's matvec runs on the host and needs no scratch.
+ *
+ * Who it is for: gsdlq_hex2d_matvec keeps the reference signature, which has no
+ * workspace argument, so on first use it allocates its scratch with cudaMalloc.
+ * Some callers cannot allow that: a host that has handed all device memory to its own
+ * allocator or to a fixed budget, and latency-critical loops where cudaMalloc/cudaFree
+ * may synchronise the device.  This variant takes the same arguments and gives the same
+ * result.  Its scratch is a file-scope device array of GSDLQ_NOALLOC_WS_BYTES (4 MiB) that
+ * every GPU loading this library holds until the process exits.
+ *
+ * - The first call on a device looks up the array's device address (cudaGetSymbolAddress,
+ *   with that device current) and keeps it.  Make that first call before any stream
+ *   capture begins.
+ * - Each call clears the scratch bytes it needs with cudaMemsetAsync on `stream`, then
+ *   launches.  It calls no cudaMalloc, cudaFree or other allocating routine.
+ * - All calls share the one array.  Calls that may overlap on the GPU (different streams,
+ *   or different host threads without ordering) race on it and give wrong results.
+ * - A launch whose scratch need exceeds GSDLQ_NOALLOC_WS_BYTES returns
+ *   GSDLQ_ERR_UNSUPPORTED before touching the device.  About 16 000 row strips of 16 rows
+ *   fit; use gsdlq_hex2d_matvec or gsdlq_linear beyond that. */
+int gsdlq_hex2d_matvec_noalloc(const float *x, const uint8_t *codes, const uint16_t *scales,
+                               const float *xy_table, const uint16_t *U, const float *tmp_k,
+                               const uint32_t *kink_row_ptr, const uint16_t *kink_cols,
+                               const float *kink_deltas, float *y, int rows, int cols, int k_dim,
+                               int n_pts, gsdlq_stream_t stream);
+
 /* Split-KV decode attention.  q is already rotated.  pos is read from *pos_dev
  * when non-NULL (CUDA-graph friendly), else pos_val.  The cache layout is the
  * reference's [layer][max_seq][n_kv][head_dim] fp16 when block_table is NULL,
