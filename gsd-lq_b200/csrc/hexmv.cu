@@ -88,6 +88,8 @@ struct HexmvParams {
   int UPS;                 // units per strip: nmat * GU
   long long T;             // units in the launch: n_strips * UPS
   int W;                   // streaming warps in the launch
+  long long TW;            // total partition weight of the W streaming warps
+  float w_per_unit;        // W / T
   int max_seg;             // partial slots per strip for streaming segments (+1 helper slot)
   int n_lr;                // low-rank rows projected in the kernel (0 with tmp_k_ext)
   int lr_off[4];           // prefix of k_dim over the matrices
@@ -98,12 +100,29 @@ struct HexmvParams {
   float* part;             // [n_strips][max_seg + 1][nmat * 16]
 };
 
-// ---- partition helpers (identical on host and device) --------------------------------
-__host__ __device__ __forceinline__ long long it_begin(int w, long long T, int W) { return (long long)w * T / W; }
-// warp whose range contains iteration i: the largest w with it_begin(w) <= i
-__host__ __device__ __forceinline__ int warp_of(long long i, long long T, int W) {
-  return (int)(((i + 1) * (long long)W - 1) / T);
+// ---- partition (identical on host and device) ---------------------------------------
+// Warps are spread over the SM's four schedulers by warp index mod 4, so schedulers 0 and 1 run
+// four streaming warps and schedulers 2 and 3 run three streaming warps plus one helper warp.
+// The units are dealt in proportion 3 : 4 to warps on the first and the second pair, so every
+// scheduler streams the same share.  lp(l) = sum of the weights of local warps 0 .. l-1.
+__host__ __device__ __forceinline__ int hx_lp(int l) { return 4 * l - 2 * (l / 4) - ((l % 4) < 2 ? (l % 4) : 2); }
+__host__ __device__ __forceinline__ long long hx_cumw(int w) {
+  return (long long)hx_lp(HX_STREAM) * (w / HX_STREAM) + hx_lp(w % HX_STREAM);
 }
+// first unit of streaming warp w
+__host__ __device__ __forceinline__ int hx_unit_begin(long long T, long long TW, int w) {
+  return (int)(T * hx_cumw(w) / TW);
+}
+__device__ __forceinline__ int unit_begin(const HexmvParams& P, int w) { return hx_unit_begin(P.T, P.TW, w); }
+// warp whose range contains unit i: the largest w with unit_begin(w) <= i (estimate, then exact steps)
+__host__ __device__ __forceinline__ int hx_warp_of(long long T, long long TW, int W, float w_per_unit, int i) {
+  int w = (int)(((float)i + 0.5f) * w_per_unit);
+  w = w < 0 ? 0 : (w > W - 1 ? W - 1 : w);
+  while (w + 1 < W && hx_unit_begin(T, TW, w + 1) <= i) ++w;
+  while (w > 0 && hx_unit_begin(T, TW, w) > i) --w;
+  return w;
+}
+__device__ __forceinline__ int warp_of_unit(const HexmvParams& P, int i) { return hx_warp_of(P.T, P.TW, P.W, P.w_per_unit, i); }
 
 inline size_t hexmv_ws_bytes_for(int n_strips, int max_seg, int nmat) {
   return sizeof(unsigned) * (CTL_WORDS + (size_t)n_strips) +
@@ -111,29 +130,23 @@ inline size_t hexmv_ws_bytes_for(int n_strips, int max_seg, int nmat) {
 }
 
 // ---- shared memory --------------------------------------------------------------------
-// The decode table sits at the absolute shared-window address 0x10000 so that one byte
-// permute builds a lookup address from a code byte (bits 8..15), the lane (bits 2..6) and
-// the constant 0x01 (bits 16..23).  Dynamic shared memory starts at a small offset B (the
-// system-reserved bytes); the buffers below the table use [0, 0x10000 - B):
-//   activation-split overflow chunks | decode entries | reduction words
-// and the fp32 input xf follows the table.  The host sizes the allocation for B <= 4 KB;
-// the kernel checks B and raises GSDLQ_FLAG_UNSUPPORTED if the assumption fails.
-constexpr uint32_t HX_TAB_ABS = 0x10000u;
-constexpr int HX_BASE_MAX = 4096;
+// The decode table sits at the fixed shared-window address HX_TAB_ABS: one byte permute builds
+// (code << 8 | lane << 2) from a code byte and the lane, and the lookup's load adds HX_TAB_ABS as
+// its immediate offset.  Dynamic shared memory starts at a small offset B (the system-reserved
+// bytes) below it:
+//   [B, HX_TAB_ABS)                          reduction words (the last 256 bytes)
+//   [HX_TAB_ABS, HX_TAB_ABS + 64 KB)         256 table rows of 256 bytes: 32 lanes x 4-byte
+//                                            entries, then a free 128-byte half
+//   [HX_TAB_ABS + 64 KB, ...)                activation-split overflow chunks
+// The whole footprint stays small (68 KB for rows of up to 8192 columns) because shared memory
+// taken from the unified L1 leaves less room for the code loads in flight.  The host sizes the
+// allocation for B = 0; the kernel checks B and raises GSDLQ_FLAG_UNSUPPORTED if its reduction
+// words would not fit below the table.
+constexpr uint32_t HX_TAB_ABS = 0x1000u;
+constexpr int HX_RED_BYTES = 512;
+constexpr int HX_LR_FLAG = 60;  // index (in the shared tmp_k area) of its ready flag
 
-struct HxLayout {
-  int ent_off, red_off, low_end;
-};
-
-__host__ __device__ inline HxLayout hx_layout(int ovf_bytes) {
-  HxLayout L;
-  L.ent_off = ovf_bytes;         // 256 decode entries (bf16x2)
-  L.red_off = L.ent_off + 1024;  // [0] 1/rms, [1..16] warp sums, [32] table address bits, [33] zero
-  L.low_end = L.red_off + 256;
-  return L;
-}
-
-inline int hx_dyn_smem(int cols) { return (int)(2 * HX_TAB_ABS) + 4 * cols + 64; }
+inline int hx_dyn_smem(int ovf_bytes) { return (int)HX_TAB_ABS + 0x10000 + ovf_bytes; }
 
 // Activation splits.  For pair p (columns 2p, 2p+1) with a = x[2p], b = x[2p]/2 + sqrt3/2 x[2p+1],
 // the hi word (bf16 a_hi | b_hi << 16) and the lo word live in 128-byte chunk
@@ -141,10 +154,11 @@ inline int hx_dyn_smem(int cols) { return (int)(2 * HX_TAB_ABS) + 4 * cols + 64;
 // One chunk is exactly what the 32 lanes of a warp read with one 16-byte load per k-step
 // pair, conflict-free.  The first 256 chunks fill the free halves of the table rows.
 __device__ __forceinline__ uint32_t xs_chunk(int ch, uint32_t tab_off) {
-  return ch < 256 ? tab_off + (uint32_t)ch * 256u + 128u : (uint32_t)(ch - 256) * 128u;
+  return ch < 256 ? tab_off + (uint32_t)ch * 256u + 128u : tab_off + 0x10000u + (uint32_t)(ch - 256) * 128u;
 }
 
-// (r0, r1) of code c in the radius-R enumeration (r0 outer, r1 inner, |r0+r1| <= R).
+// ---- decode table ----------------------------------------------------------------------
+// (r0, r1) of code c in the radius-R enumeration (r0 outer, r1 inner, |r0+r1| <= R)
 __device__ __forceinline__ bool lattice_of_code(int c, int R, int& r0, int& r1) {
   for (int a = -R; a <= R; ++a) {
     const int lo = max(-R, -R - a), hi = min(R, R - a);
@@ -159,40 +173,30 @@ __device__ __forceinline__ bool lattice_of_code(int c, int R, int& r0, int& r1) 
   return false;
 }
 
-// bf16x2 (r0, r1) decode entry of code i (0 for codes past the table)
-__device__ __forceinline__ uint32_t decode_entry(int i, const HexmvParams& P) {
-  int r0 = 0, r1 = 0;
-  bool ok;
-  if (P.xy_table != nullptr) {
-    ok = i < P.n_pts;
-    if (ok) {
-      const float x = P.xy_table[2 * i], y = P.xy_table[2 * i + 1];
-      const float rf1 = rintf(y * 1.1547005383792515f);
-      const float rf0 = x - 0.5f * rf1;
-      r0 = (int)rf0;
-      r1 = (int)rf1;
-      const float yy = (float)((double)r1 * 0.8660254037844386);
-      if ((float)r0 != rf0 || yy != y || fabsf(rf0) > 16.f || fabsf(rf1) > 16.f) {
-        raise_flag(GSDLQ_FLAG_BAD_TABLE);
-        r0 = r1 = 0;
-      }
-    }
-  } else {
-    ok = lattice_of_code(i, P.job.mat[0].radius, r0, r1);
+// decode entry of code i from a caller's float xy table (the drop-in path); the table must be
+// the A2 lattice, which is checked
+__device__ __forceinline__ uint32_t entry_from_xy(const float* xy, int n_pts, int i) {
+  if (i >= n_pts) return 0u;
+  const float x = xy[2 * i], y = xy[2 * i + 1];
+  const float rf1 = rintf(y * 1.1547005383792515f);
+  const float rf0 = x - 0.5f * rf1;
+  const float yy = (float)((double)rf1 * 0.8660254037844386);
+  if (rf0 != rintf(rf0) || yy != y || fabsf(rf0) > 16.f || fabsf(rf1) > 16.f) {
+    raise_flag(GSDLQ_FLAG_BAD_TABLE);
+    return 0u;
   }
-  if (!ok) r0 = r1 = 0;
-  return pack_bf16x2((float)r0, (float)r1);
+  return pack_bf16x2(rf0, rf1);
 }
 
-// Decode lookup: PRMT assembles the absolute shared address 0x10000 | code << 8 | lane << 2
-// (lane4x = lane*4 | 0x0100 supplies bytes 0 and 2), one 32-bit shared load reads the entry.
+// Decode lookup: PRMT assembles code << 8 | lane << 2 (lane4x = lane*4 supplies byte 0 and the
+// zero bytes 2, 3), and one 32-bit shared load at that address + HX_TAB_ABS reads the entry.
 // The load is not volatile (the table is constant after the prologue barrier), so lookups can
 // be scheduled around the MMAs; lane4x is derived from a shared-memory read made after that
 // barrier, which keeps every lookup behind it.
 __device__ __forceinline__ uint32_t tab_lookup(uint32_t word, uint32_t lane4x, uint32_t sel) {
   const uint32_t addr = __byte_perm(word, lane4x, sel);
   uint32_t r;
-  asm("ld.shared.b32 %0, [%1];" : "=r"(r) : "r"(addr));
+  asm("ld.shared.b32 %0, [%1+%2];" : "=r"(r) : "r"(addr), "n"(HX_TAB_ABS));
   return r;
 }
 
@@ -205,16 +209,18 @@ __device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
 // One 64-byte segment of a unit (16 rows x 64 code pairs = scale groups A and B): 8 MMAs in
 // two independent accumulator chains.  ca / cb: this lane's 16 code bytes of rows g and g+8;
 // baddr: this lane's 16-byte B slice in the segment's first chunk (chunks bstride apart).
+// Only the 8 lanes whose B column has data on their own k rows load (bld); the B registers of
+// the others were zeroed once and are never written, so the block-diagonal zeros cost nothing.
 // Returns the dot products of this lane's group (q = 0: A, q = 1: B; 0 for q = 2, 3).
 __device__ __forceinline__ void segment_mma(const uint4& ca, const uint4& cb, uint32_t baddr, uint32_t bstride,
-                                            uint32_t bmask, uint32_t lane4x, float& r_g, float& r_h) {
+                                            bool bld, uint4 (&bv)[2], uint32_t lane4x, float& r_g, float& r_h) {
   float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
   const uint32_t wa[4] = {ca.x, ca.y, ca.z, ca.w};
   const uint32_t wb[4] = {cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
     // k-steps 2m (code bytes 0, 1 of word m) and 2m+1 (bytes 2, 3)
-    const uint4 bv = lds_u4(baddr + (uint32_t)m * bstride);
+    if (bld) bv[m & 1] = lds_u4(baddr + (uint32_t)m * bstride);
     uint32_t a0[4], a1[4];
     a0[0] = tab_lookup(wa[m], lane4x, 0x6504u);  // row g,   pair 2t
     a0[1] = tab_lookup(wb[m], lane4x, 0x6504u);  // row g+8, pair 2t
@@ -224,24 +230,31 @@ __device__ __forceinline__ void segment_mma(const uint4& ca, const uint4& cb, ui
     a1[1] = tab_lookup(wb[m], lane4x, 0x6524u);
     a1[2] = tab_lookup(wa[m], lane4x, 0x6534u);
     a1[3] = tab_lookup(wb[m], lane4x, 0x6534u);
-    mma_bf16_16816(d0, a0, bv.x & bmask, bv.y & bmask, d0);
-    mma_bf16_16816(d1, a1, bv.z & bmask, bv.w & bmask, d1);
+    mma_bf16_16816(d0, a0, bv[m & 1].x, bv[m & 1].y, d0);
+    mma_bf16_16816(d1, a1, bv[m & 1].z, bv[m & 1].w, d1);
   }
   r_g = (d0[0] + d0[1]) + (d1[0] + d1[1]);
   r_h = (d0[2] + d0[3]) + (d1[2] + d1[3]);
 }
 
-__device__ __forceinline__ float ld_cg_f32(const float* p) {
-  float v;
-  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
-  return v;
-}
 __device__ __forceinline__ unsigned long long ld_cg_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(v) : "l"(p));
   return v;
 }
 
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
@@ -265,10 +278,35 @@ __device__ __forceinline__ StripInfo strip_info(const HexmvParams& P, int s) {
   return si;
 }
 
+// Operands of a strip's epilogue that do not depend on its result, loaded before the slot sum
+// so that their latency overlaps it.
+struct EpiPre {
+  float resid;  // RESID
+  float2 cs;    // ROPE_KV: (cos, sin) of this row's pair at the current position
+};
+
+template <int EPI>
+__device__ __forceinline__ EpiPre epilogue_pre(const HexmvParams& P, const StripInfo& si, int lane, int pos) {
+  const gsdlq_linear_job_t& J = P.job;
+  EpiPre e{0.f, make_float2(1.f, 0.f)};
+  const int row = si.rbase + (lane & 15);
+  const bool ok = lane < 16 && row < J.mat[si.m0].rows;
+  if constexpr (EPI == GSDLQ_EPI_RESID) {
+    if (ok) e.resid = __ldcg(J.resid + row);
+  } else if constexpr (EPI == GSDLQ_EPI_ROPE_KV) {
+    if (ok && si.m0 != 2 && pos >= 0 && pos < J.max_seq) {
+      const int hd = J.head_dim;
+      e.cs = __ldg(reinterpret_cast<const float2*>(J.rope_cs) + (size_t)pos * (hd / 2) + ((row % hd) >> 1));
+    }
+  }
+  return e;
+}
+
 // Epilogue of a completed strip.  Lane j holds the finished value of row (j & 15) of
 // matrix m0 + (j >> 4) (lanes >= 16 only carry data in pair mode).
 template <int EPI>
-__device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float v, int lane) {
+__device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float v, int lane, const EpiPre& pre,
+                               int pos) {
   const gsdlq_linear_job_t& J = P.job;
   const int r = lane & 15;
   const gsdlq_hexmat_t& M = J.mat[si.m0];
@@ -289,7 +327,7 @@ __device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float 
       if (lane == 0 && key) atomicMax(J.argmax_key, key);
     }
   } else if constexpr (EPI == GSDLQ_EPI_RESID) {
-    if (lane < 16 && ok) J.y[0][row] = J.resid[row] + v;
+    if (lane < 16 && ok) J.y[0][row] = pre.resid + v;
   } else if constexpr (EPI == GSDLQ_EPI_SWIGLU) {
     const float u = __shfl_down_sync(0xffffffffu, v, 16);
     if (lane < 16 && ok) J.y[0][row] = (v / (1.0f + expf(-v))) * u;
@@ -299,17 +337,13 @@ __device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float 
     if (lane < 16 && ok) {
       const bool even = (r & 1) == 0;
       const float v0 = even ? v : other, v1 = even ? other : v;
-      const int pos = *J.pos;
-      const int hd = J.head_dim;
       const bool pos_ok = pos >= 0 && pos < J.max_seq;
       if (!pos_ok && lane == 0) raise_flag(GSDLQ_FLAG_BAD_POS);
       if (si.m0 == 2) {  // V: stored unrotated
         if (J.y[2]) J.y[2][row] = v;
         if (pos_ok) J.v_cache[((size_t)J.layer * J.max_seq + pos) * M.rows + row] = f2h(v);
       } else {
-        const int i = (row % hd) >> 1;
-        const float2 cs = pos_ok ? reinterpret_cast<const float2*>(J.rope_cs)[(size_t)pos * (hd / 2) + i]
-                                 : make_float2(1.f, 0.f);
+        const float2 cs = pre.cs;
         const float o = even ? __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y))
                              : __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
         if (si.m0 == 0) {
@@ -324,13 +358,16 @@ __device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float 
 }
 
 // Sum a completed strip's slots in slot order, add the low-rank term and run the epilogue
-// (one warp).
+// (one warp).  Once the projection is complete, every load (slots, U row, S, tmp_k, epilogue
+// operands) is issued in one batch; the U rows were pulled into L2 by the helper warps.
 template <int EPI, int NMAT>
-__device__ void finish_strip(const HexmvParams& P, int s, int lane) {
-  __threadfence();
+__device__ void finish_strip(const HexmvParams& P, int s, int lane, int pos, const volatile float* s_lr) {
+  // the arriving lane's acq_rel count was the acquire; the warp barrier orders the other lanes'
+  // reads after it
+  __syncwarp();
   const int UPS = P.UPS;
-  const int w_first = warp_of((long long)s * UPS, P.T, P.W);
-  const int w_last = warp_of((long long)s * UPS + UPS - 1, P.T, P.W);
+  const int w_first = warp_of_unit(P, s * UPS);
+  const int w_last = warp_of_unit(P, s * UPS + UPS - 1);
   const int nseg = w_last - w_first + 1;
   constexpr int width = NMAT * 16;
   const StripInfo si = strip_info<NMAT>(P, s);
@@ -338,362 +375,494 @@ __device__ void finish_strip(const HexmvParams& P, int s, int lane) {
   const gsdlq_hexmat_t& M = P.job.mat[si.m0 + mm];
   const int row = si.rbase + (lane & 15);
   const bool active = lane < width && row < M.rows;
-  // low-rank operands first: their loads do not depend on the slots
   const int kd = active ? M.k_dim : 0;
-  uint16_t uv[16];
-  float sv[16];
+  // loads that do not need the projection: epilogue operands, U row, S, the partial slots
+  const EpiPre pre = epilogue_pre<EPI>(P, si, lane, pos);
+  float uu[16];
+  {
+    const uint16_t* ur = M.U + (size_t)(active ? row : 0) * kd;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    uv[j] = j < kd ? __ldg(M.U + (size_t)row * kd + j) : (uint16_t)0;
-    sv[j] = (j < kd && P.tmp_k_ext == nullptr) ? __ldg(M.S + j) : 0.f;
+    for (int j = 0; j < 16; ++j) uu[j] = j < kd ? h2f(__ldcg(ur + j)) : 0.f;
   }
   float* base = P.part + (size_t)s * (P.max_seg + 1) * width;
   float v = 0.f;
   if (lane < width) {
-    for (int k = 0; k < nseg; ++k) {
-      v += ld_cg_f32(base + (size_t)k * width + lane);
-      base[(size_t)k * width + lane] = 0.f;
-    }
-    v += ld_cg_f32(base + (size_t)P.max_seg * width + lane);  // helper slot: kinks
+    constexpr int B = 12;
+    float pv[B];
+#pragma unroll
+    for (int k = 0; k < B; ++k) pv[k] = k < nseg ? __ldcg(base + (size_t)k * width + lane) : 0.f;
+    const float hv = __ldcg(base + (size_t)P.max_seg * width + lane);  // helper slot: kinks
+#pragma unroll
+    for (int k = 0; k < B; ++k) v += pv[k];
+    for (int k = B; k < nseg; ++k) v += __ldcg(base + (size_t)k * width + lane);
+    v += hv;
+    // every consumed slot and the counter go back to zero: the whole workspace is zero between
+    // launches, so launches of any geometry can share it
+    for (int k = 0; k < nseg; ++k) base[(size_t)k * width + lane] = 0.f;
     base[(size_t)P.max_seg * width + lane] = 0.f;
   }
-  // every consumed slot and the counter go back to zero: the whole workspace is zero between
-  // launches, so launches of any geometry can share it
   if (lane == 0) P.cnt[s] = 0u;
-  const bool any_lr = __any_sync(0xffffffffu, kd > 0);
-  if (any_lr) {
-    float lr = 0.f;
+  float lr = 0.f;
+  if (__any_sync(0xffffffffu, kd > 0)) {
     if (P.tmp_k_ext != nullptr) {
 #pragma unroll
       for (int j = 0; j < 16; ++j)
-        if (j < kd) lr += h2f(uv[j]) * __ldg(P.tmp_k_ext + j);
+        if (j < kd) lr += uu[j] * __ldg(P.tmp_k_ext + j);
     } else {
-      if (lane == 0) wait_counter_eq(&P.ctl[CTL_LR_DONE], gridDim.x * HX_HELP, 1000000000ull);  // 1 s bound
-      __syncwarp();
-      __threadfence();
-      const unsigned long long* acc = reinterpret_cast<const unsigned long long*>(P.ctl + CTL_TMPK) +
-                                      P.lr_off[si.m0 + mm];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        if (j < kd) {
-          const double d = (double)(long long)ld_cg_u64(acc + j) * (1.0 / 4294967296.0);
-          lr += h2f(uv[j]) * ((float)d * sv[j]);
+      // tmp_k was published in shared memory by this CTA's last helper warp (bounded wait, 1 s)
+      if (s_lr[HX_LR_FLAG] == 0.f) {
+        unsigned long long t0, t1;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        while (s_lr[HX_LR_FLAG] == 0.f) {
+          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+          if (t1 - t0 > 1000000000ull) {
+            if (lane == 0) raise_flag(GSDLQ_FLAG_TIMEOUT);
+            break;
+          }
+          __nanosleep(64);
         }
       }
+      const volatile float* tk = s_lr + P.lr_off[si.m0 + mm];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < kd) lr += uu[j] * tk[j];
     }
-    v += lr;
   }
-  strip_epilogue<EPI>(P, si, v, lane);
-}
-
-// Count `units` toward strip s after this warp's slot writes; the warp completing the
-// strip (UPS streaming units + 1 helper unit) finishes it.
-template <int EPI, int NMAT>
-__device__ __forceinline__ void arrive(const HexmvParams& P, int s, unsigned units, int lane, bool fence = true) {
-  if (fence) __threadfence();  // every lane that wrote part of the slot orders its stores before the count
-  __syncwarp();
-  unsigned fin = 0;
-  if (lane == 0) {
-    const unsigned old = atomicAdd(&P.cnt[s], units);
-    fin = (old + units == (unsigned)P.UPS + 1u);
-  }
-  fin = __shfl_sync(0xffffffffu, fin, 0);
-  if (fin) finish_strip<EPI, NMAT>(P, s, lane);
+  strip_epilogue<EPI>(P, si, v + lr, lane, pre, pos);
 }
 
 template <int EPI, bool FULL>
 __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_constant__ HexmvParams P) {
   constexpr int NMAT = (EPI == GSDLQ_EPI_SWIGLU) ? 2 : 1;
+  constexpr int width = NMAT * 16;
   extern __shared__ __align__(1024) uint8_t smem[];
   const gsdlq_linear_job_t& J = P.job;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gl = lane >> 2, q = lane & 3;
   const int C = P.cols, G = P.G, NP = P.NP;
   const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-  if (sbase > (uint32_t)HX_BASE_MAX || (sbase & 15u)) {  // the layout's assumption on the reserved bytes
+  if (sbase + HX_RED_BYTES > HX_TAB_ABS || (sbase & 15u)) {  // the layout's assumption on the reserved bytes
     if (tid == 0) raise_flag(GSDLQ_FLAG_UNSUPPORTED);
     return;
   }
   const uint32_t tab_off = HX_TAB_ABS - sbase;
   uint8_t* tab = smem + tab_off;
-  float* xf = reinterpret_cast<float*>(smem + tab_off + HX_TAB_ABS);
-  const HxLayout LY = hx_layout(P.ovf_bytes);
-  uint32_t* ent = reinterpret_cast<uint32_t*>(smem + LY.ent_off);
-  float* red = reinterpret_cast<float*>(smem + LY.red_off);
+  float* red = reinterpret_cast<float*>(smem + tab_off - HX_RED_BYTES);
+  // [1..16] warp sums, [32] [33] zero words, [34] position; s_lr: [0..48) tmp_k, [HX_LR_FLAG] ready
+  volatile float* s_lr = red + 64;
+  uint32_t* redu = reinterpret_cast<uint32_t*>(red);
 
-  // ---- 1. independent prologue: decode entries, first unit's loads, helper Vt slices -------
-  if (tid < 256) ent[tid] = decode_entry(tid, P);
-  if (tid == 0) {
-    reinterpret_cast<uint32_t*>(red)[32] = 0x0100u;  // table address bits 16..23, read after a barrier
-    reinterpret_cast<uint32_t*>(red)[33] = 0u;
-  }
+  // Barriers: 0 = the whole CTA (end only); 1 = the 14 streaming warps; 2 = streaming warps
+  // arrive once the input is staged, helper warps wait on it only when they need the input.
+  const bool helper = warp >= HX_STREAM;
+  constexpr int NST = HX_STREAM * kWarp;  // streaming (and staging) threads
 
-  const int w = blockIdx.x * HX_STREAM + warp;
-  const bool streamer = warp < HX_STREAM && w < P.W;
-  const long long u0 = streamer ? it_begin(w, P.T, P.W) : 0;
-  const long long u1 = streamer ? it_begin(w + 1, P.T, P.W) : 0;
-  // cursor (strip, matrix in strip, unit column) of the next unit to load, and its pointers
-  int ns = 0, nm = 0, nc = 0;
-  {
-    const long long s_ = u0 / P.UPS;
-    const int r_ = (int)(u0 - s_ * P.UPS);
-    ns = (int)s_;
-    nm = r_ / P.GU;
-    nc = r_ - nm * P.GU;
-  }
-  const uint8_t* pa = nullptr;
-  const uint8_t* pb = nullptr;
-  const uint16_t* qa = nullptr;
-  const uint16_t* qb = nullptr;
-  auto seek = [&]() {
-    const StripInfo si = strip_info<NMAT>(P, ns);
-    const gsdlq_hexmat_t& M = J.mat[si.m0 + nm];
-    const int ra = min(si.rbase + gl, M.rows - 1), rb = min(si.rbase + gl + 8, M.rows - 1);
-    pa = M.codes + (size_t)ra * NP + nc * HX_UB + q * 16;
-    pb = M.codes + (size_t)rb * NP + nc * HX_UB + q * 16;
-    qa = M.scales + (size_t)ra * G + nc * 8;
-    qb = M.scales + (size_t)rb * G + nc * 8;
-  };
-  auto advance = [&]() {
-    if (++nc == P.GU) {
-      nc = 0;
-      if (++nm == NMAT) {
-        nm = 0;
-        ++ns;
-      }
-    }
-  };
-  // the FULL path shifts the lane's fp16 scale out of a word holding two groups
-  const int sh = FULL ? 16 * (q & 1) : 0;
-  uint4 cw[4][2];      // code bytes of the unit being consumed / refilled: [segment][row g, g+8]
-  uint32_t sa[4], sb[4];  // the next unit's scale words: [segment]
-  auto load_codes = [&](int s) {
-    if (FULL || nc * HX_UB + 64 * s + 16 * q < NP) {
-      cw[s][0] = ldg_stream_u4(pa + 64 * s);
-      cw[s][1] = ldg_stream_u4(pb + 64 * s);
-    } else {
-      cw[s][0] = make_uint4(0u, 0u, 0u, 0u);  // past the row: its activations are staged as zero
-      cw[s][1] = make_uint4(0u, 0u, 0u, 0u);
-    }
-  };
-  auto load_scales = [&]() {
-    if (FULL) {
-      const uint4 x = ldg_stream_u4(qa), y = ldg_stream_u4(qb);
-      sa[0] = x.x, sa[1] = x.y, sa[2] = x.z, sa[3] = x.w;
-      sb[0] = y.x, sb[1] = y.y, sb[2] = y.z, sb[3] = y.w;
-    } else {
-#pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const int gi = 2 * s + (q & 1);
-        const bool ok = nc * 8 + gi < G;
-        sa[s] = ok ? (uint32_t)__ldg(qa + gi) : 0u;
-        sb[s] = ok ? (uint32_t)__ldg(qb + gi) : 0u;
-      }
-    }
-  };
-  if (streamer && u1 > u0) {
-    seek();
-    load_scales();
-#pragma unroll
-    for (int s = 0; s < 4; ++s) load_codes(s);
-  }
-
-  // helper warps: pull this warp's column slice of every Vt row into L2 (no registers held)
-  const int hw = blockIdx.x * HX_HELP + (warp - HX_STREAM);
-  const int c8_0 = hw * P.lr_chunks;
-  const int c8_1 = min(c8_0 + P.lr_chunks, C / 8);
-  if (warp >= HX_STREAM) {
-    for (int jl = lane; jl < P.n_lr; jl += 32) {
-      int m = 0, j = jl;
-      while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
-      const uint8_t* vt = reinterpret_cast<const uint8_t*>(J.mat[m].Vt + (size_t)j * C);
-      for (int b = (c8_0 * 16) & ~127; b < c8_1 * 16; b += 128)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(vt + b));
-    }
-  }
-
-  __syncthreads();  // decode entries
-  for (int i = warp; i < 256; i += HX_WARPS) *reinterpret_cast<uint32_t*>(tab + i * 256 + lane * 4) = ent[i];
-
-  // ---- 2. wait for the producer of x, then stage the input (fp32 and bf16 splits) ----------
-  pdl_wait();
-  int tok = 0;
-  if (J.input_mode == GSDLQ_IN_EMBED) {
-    tok = *J.token;
-    if (tok < 0 || tok >= J.vocab) {
-      if (tid == 0) raise_flag(GSDLQ_FLAG_BAD_TOKEN);
-      tok = 0;
-    }
-  }
-  const bool normed = J.input_mode != GSDLQ_IN_PLAIN;
-  auto load_x = [&](int p) -> float2 {
-    if (J.input_mode == GSDLQ_IN_EMBED) {
-      const uint32_t raw = __ldg(reinterpret_cast<const unsigned int*>(J.embed + (size_t)tok * C) + p);
-      return make_float2(h2f(raw & 0xffffu), h2f(raw >> 16));
-    }
-    return __ldg(reinterpret_cast<const float2*>(J.x) + p);
-  };
-  auto stage = [&](int p, float x0, float x1, float2 wv) {
-    if (J.input_mode == GSDLQ_IN_EMBED && blockIdx.x == 0 && J.x_out)
-      reinterpret_cast<float2*>(J.x_out)[p] = make_float2(x0, x1);
-    if (normed) {
-      const float inv = red[0];
-      x0 = __fmul_rn(__fmul_rn(x0, inv), wv.x);
-      x1 = __fmul_rn(__fmul_rn(x1, inv), wv.y);
-    }
-    reinterpret_cast<float2*>(xf)[p] = make_float2(x0, x1);
-    const float b = fmaf(0.8660254037844386f, x1, 0.5f * x0);
-    uint32_t h, l;
-    split_bf16x2(x0, b, h, l);
-    const int j = p & 63, r = j & 15;
-    const uint32_t off = xs_chunk((p >> 6) * 4 + (r >> 2), tab_off) + (uint32_t)((j >> 4) * 32 + (r & 3) * 4);
-    *reinterpret_cast<uint32_t*>(smem + off) = h;
-    *reinterpret_cast<uint32_t*>(smem + off + 16) = l;
-  };
-  // pass 1: the first XR pairs of each thread stay in registers; sum of squares
-  constexpr int XR = 4;
-  float2 xv[XR], wv[XR];
-  float ss = 0.f;
-#pragma unroll
-  for (int k = 0; k < XR; ++k) {
-    const int p = tid + k * HX_THREADS;
-    if (p < NP) {
-      xv[k] = load_x(p);
-      wv[k] = normed ? __ldg(reinterpret_cast<const float2*>(J.norm_w) + p) : make_float2(1.f, 1.f);
-    }
-  }
-  if (normed) {
-#pragma unroll
-    for (int k = 0; k < XR; ++k)
-      if (tid + k * HX_THREADS < NP) ss += xv[k].x * xv[k].x + xv[k].y * xv[k].y;
-    for (int p = tid + XR * HX_THREADS; p < NP; p += HX_THREADS) {
-      const float2 v = load_x(p);
-      ss += v.x * v.x + v.y * v.y;
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) red[1 + warp] = ss;
-    __syncthreads();
-    if (tid == 0) {
-      float t = 0.f;
-      for (int k = 0; k < HX_WARPS; ++k) t += red[1 + k];
-      red[0] = 1.0f / sqrtf(t / (float)C + J.eps);  // gsd_lq_cpu_engine.c:78
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int k = 0; k < XR; ++k) {
-    const int p = tid + k * HX_THREADS;
-    if (p < NP) stage(p, xv[k].x, xv[k].y, wv[k]);
-  }
-  for (int p = tid + XR * HX_THREADS; p < NP; p += HX_THREADS) {
-    const float2 v = load_x(p);
-    stage(p, v.x, v.y, normed ? __ldg(reinterpret_cast<const float2*>(J.norm_w) + p) : make_float2(1.f, 1.f));
-  }
-  // pairs past the row end of the last unit read zero activations
-  for (int p = NP + tid; p < P.GU * (HX_UB); p += HX_THREADS) {
-    const int j = p & 63, r = j & 15;
-    const uint32_t off = xs_chunk((p >> 6) * 4 + (r >> 2), tab_off) + (uint32_t)((j >> 4) * 32 + (r & 3) * 4);
-    *reinterpret_cast<uint32_t*>(smem + off) = 0u;
-    *reinterpret_cast<uint32_t*>(smem + off + 16) = 0u;
-  }
-  __syncthreads();
-
-  if (warp >= HX_STREAM) {
-    // ---- helper warps: low-rank slice partials, then kink slots of their strips -----------
+  if (helper) {
+    // ==== helper warps: low-rank slice partials, kink slots, deferred strip arrivals ==========
+    const int hw = blockIdx.x * HX_HELP + (warp - HX_STREAM);
     const int H = gridDim.x * HX_HELP;
-    if (P.n_lr > 0) {
-      for (int jl = lane; jl < P.n_lr; jl += 32) {
+    const int c8_0 = hw * P.lr_chunks;
+    const int c8_1 = min(c8_0 + P.lr_chunks, C / 8);
+    constexpr int SPP = (NMAT == 2) ? 1 : 2;  // strips per kink pass
+    // pass p covers strip hw + p*SPP*H (+ H for lanes 16-31 when SPP == 2); lane = row
+    auto pass_strip = [&](int p) { return hw + p * SPP * H + ((NMAT == 2) ? 0 : (lane >> 4) * H); };
+    const int npass = hw < P.n_strips ? (P.n_strips - hw + SPP * H - 1) / (SPP * H) : 0;
+    struct KRow {
+      const uint16_t* cols;
+      const float* del;
+      uint32_t e0, e1;
+      int km, row;  // matrix and row of this lane (row -1: none)
+    };
+    // row offsets and kink arrays of this lane's row in pass p (copied out of the parameters)
+    auto krow = [&](int p) -> KRow {
+      KRow k{nullptr, nullptr, 0u, 0u, 0, -1};
+      const int s = pass_strip(p);
+      if (p < npass && s < P.n_strips) {
+        const StripInfo si = strip_info<NMAT>(P, s);
+        const int km = si.m0 + ((NMAT == 2) ? (lane >> 4) : 0);
+        k.km = km;
+        k.cols = J.mat[km].kink_cols;
+        k.del = J.mat[km].kink_deltas;
+        const int row = si.rbase + (lane & 15);
+        if (row < J.mat[km].rows) {
+          k.row = row;
+          const uint32_t* rp = J.mat[km].row_ptr;
+          k.e0 = __ldg(rp + row);
+          k.e1 = __ldg(rp + row + 1);
+        }
+      }
+      return k;
+    };
+    constexpr int KB = 16;  // kinks per lane per batch
+    int col[KB];
+    float dl[KB];
+    auto load_batch = [&](const KRow& k, uint32_t e) {
+#pragma unroll
+      for (int u = 0; u < KB; ++u) {
+        const uint32_t eu = e + u;
+        col[u] = eu < k.e1 ? (int)__ldg(k.cols + eu) : 0;
+        dl[u] = eu < k.e1 ? __ldg(k.del + eu) : 0.f;
+      }
+    };
+    // ---- before the wait: everything that does not depend on x -----------------------------
+    KRow kcur = krow(0), knext = krow(1);
+    load_batch(kcur, kcur.e0);
+    // the finishing warps read the U rows of these strips: pull them into L2 now (one 32-byte row
+    // per lane per pass)
+    for (int p = 0; p < npass; ++p) {
+      const int s = pass_strip(p);
+      if (s < P.n_strips) {
+        const StripInfo si = strip_info<NMAT>(P, s);
+        const int km = si.m0 + ((NMAT == 2) ? (lane >> 4) : 0);
+        const int row = si.rbase + (lane & 15);
+        const int kd = J.mat[km].k_dim;
+        if (kd > 0 && row < J.mat[km].rows)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(J.mat[km].U + (size_t)row * kd));
+      }
+    }
+    constexpr int LRC = 4;  // Vt chunks per row held in registers; the rest of the slice via L2
+    uint4 vr[2][LRC];
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int jl = lane + 32 * jj;
+      if (jl < P.n_lr) {
         int m = 0, j = jl;
         while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
         const uint4* vt = reinterpret_cast<const uint4*>(J.mat[m].Vt + (size_t)j * C);
-        float acc = 0.f;
-        for (int cb = c8_0; cb < c8_1; cb += 8) {
-          uint4 raw[8];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) raw[k] = (cb + k < c8_1) ? __ldg(vt + cb + k) : make_uint4(0u, 0u, 0u, 0u);
+        for (int k = 0; k < LRC; ++k) vr[jj][k] = (c8_0 + k < c8_1) ? __ldg(vt + c8_0 + k) : make_uint4(0u, 0u, 0u, 0u);
+        const uint8_t* vb = reinterpret_cast<const uint8_t*>(vt);
+        for (int b = ((c8_0 + LRC) * 16) & ~127; b < c8_1 * 16; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(vb + b));
+      }
+    }
+    // ---- the staged input, and the previous kernel's outputs, are ready after these ------------
+    named_bar_sync(2, HX_THREADS);
+    pdl_wait();
+    const int pos = reinterpret_cast<const int*>(redu)[34];
+    // the input values come back from the staged splits (hi + lo: about 16 significant bits),
+    // so no fp32 copy of x occupies shared memory and no gather waits on L2
+    auto xs_pair = [&](int p) -> float2 {
+      const int j = p & 63, r = j & 15;
+      const uint32_t off = xs_chunk((p >> 6) * 4 + (r >> 2), tab_off) + (uint32_t)((j >> 4) * 32 + (r & 3) * 4);
+      const uint32_t h = *reinterpret_cast<const uint32_t*>(smem + off);
+      const uint32_t l = *reinterpret_cast<const uint32_t*>(smem + off + 16);
+      const float x0 = bf16lo_to_f(h) + bf16lo_to_f(l);
+      const float b = bf16hi_to_f(h) + bf16hi_to_f(l);
+      return make_float2(x0, (b - 0.5f * x0) * 1.1547005383792515f);
+    };
+    auto dot8 = [&](const uint4& raw, int c8) {  // 8 columns of one Vt row against x
+      const float2 a0 = xs_pair(4 * c8), a1 = xs_pair(4 * c8 + 1), a2 = xs_pair(4 * c8 + 2), a3 = xs_pair(4 * c8 + 3);
+      return a0.x * h2f(raw.x & 0xffffu) + a0.y * h2f(raw.x >> 16) + a1.x * h2f(raw.y & 0xffffu) +
+             a1.y * h2f(raw.y >> 16) + a2.x * h2f(raw.z & 0xffffu) + a2.y * h2f(raw.z >> 16) +
+             a3.x * h2f(raw.w & 0xffffu) + a3.y * h2f(raw.w >> 16);
+    };
+    if (P.n_lr > 0) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            if (cb + k < c8_1) {
-              const float4* xp = reinterpret_cast<const float4*>(xf + 8 * (cb + k));
-              const float4 a = xp[0], b = xp[1];
-              acc += a.x * h2f(raw[k].x & 0xffffu) + a.y * h2f(raw[k].x >> 16) + a.z * h2f(raw[k].y & 0xffffu) +
-                     a.w * h2f(raw[k].y >> 16) + b.x * h2f(raw[k].z & 0xffffu) + b.y * h2f(raw[k].z >> 16) +
-                     b.z * h2f(raw[k].w & 0xffffu) + b.w * h2f(raw[k].w >> 16);
-            }
+      for (int jj = 0; jj < 2; ++jj) {
+        const int jl = lane + 32 * jj;
+        if (jl < P.n_lr) {
+          int m = 0, j = jl;
+          while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
+          const uint4* vt = reinterpret_cast<const uint4*>(J.mat[m].Vt + (size_t)j * C);
+          float acc = 0.f;
+#pragma unroll
+          for (int k = 0; k < LRC; ++k)
+            if (c8_0 + k < c8_1) acc += dot8(vr[jj][k], c8_0 + k);
+          for (int cb = c8_0 + LRC; cb < c8_1; cb += 4) {
+            uint4 raw[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) raw[k] = (cb + k < c8_1) ? __ldg(vt + cb + k) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (cb + k < c8_1) acc += dot8(raw[k], cb + k);
           }
+          if (!(fabsf(acc) < LR_MAX)) {
+            raise_flag(GSDLQ_FLAG_RANGE);
+            acc = (acc != acc) ? 0.f : copysignf(LR_MAX, acc);
+          }
+          const long long fx = __float2ll_rn(acc * LR_FIX);
+          atomicAdd(reinterpret_cast<unsigned long long*>(P.ctl + CTL_TMPK) + jl, (unsigned long long)fx);
         }
-        if (!(fabsf(acc) < LR_MAX)) {
-          raise_flag(GSDLQ_FLAG_RANGE);
-          acc = (acc != acc) ? 0.f : copysignf(LR_MAX, acc);
-        }
-        const long long fx = __float2ll_rn(acc * LR_FIX);
-        atomicAdd(reinterpret_cast<unsigned long long*>(P.ctl + CTL_TMPK) + jl, (unsigned long long)fx);
       }
       __threadfence();
       __syncwarp();
       if (lane == 0) atomicAdd(&P.ctl[CTL_LR_DONE], 1u);
+      if (warp == HX_WARPS - 1) {
+        // once every slice is in, publish S * projection to this CTA's finishing warps
+        if (lane == 0) wait_counter_eq(&P.ctl[CTL_LR_DONE], gridDim.x * HX_HELP, 1000000000ull);  // 1 s bound
+        __syncwarp();  // lane 0's acquire load orders the accumulator reads of the warp
+        const unsigned long long* acc = reinterpret_cast<const unsigned long long*>(P.ctl + CTL_TMPK);
+        for (int jl = lane; jl < P.n_lr; jl += 32) {
+          int m = 0, j = jl;
+          while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
+          const double d = (double)(long long)__ldcg(acc + jl) * (1.0 / 4294967296.0);
+          s_lr[jl] = (float)d * __ldg(J.mat[m].S + j);
+        }
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) s_lr[HX_LR_FLAG] = 1.f;
+      }
     }
-    // kinks: lane = row.  Pair mode: one 32-row strip per pass; otherwise two 16-row strips
-    constexpr int SPP = (NMAT == 2) ? 1 : 2;
-    constexpr int width = NMAT * 16;
-    for (int s0 = hw; s0 < P.n_strips; s0 += SPP * H) {
-      const int s = (NMAT == 2) ? s0 : s0 + (lane >> 4) * H;
-      const bool sv = s < P.n_strips;
-      const StripInfo si = strip_info<NMAT>(P, sv ? s : s0);
-      const int mm = (NMAT == 2) ? (lane >> 4) : 0;
-      const gsdlq_hexmat_t& M = J.mat[si.m0 + mm];
-      const int row = si.rbase + (lane & 15);
-      uint32_t e = 0u, e1 = 0u;
-      if (sv && row < M.rows) {
-        e = __ldg(M.row_ptr + row);
-        e1 = __ldg(M.row_ptr + row + 1);
+    // ---- kink passes: one slot per strip; the counts are made together at the end -------------
+    bool bad = false;
+    for (int p = 0; p < npass; ++p) {
+      if (p > 0) {
+        kcur = knext;
+        knext = krow(p + 1);  // in flight during this pass
+        load_batch(kcur, kcur.e0);
       }
       float v = 0.f;
-      bool bad = false;
-      while (__any_sync(0xffffffffu, e < e1)) {
-        int col[8];
-        float dl[8];
+      for (uint32_t e = kcur.e0;;) {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint32_t eu = e + u;
-          col[u] = eu < e1 ? (int)__ldg(M.kink_cols + eu) : 0;
-          dl[u] = eu < e1 ? __ldg(M.kink_deltas + eu) : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < KB; ++u) {
+          const bool in = e + u < kcur.e1;
           const bool ok = col[u] < C;
-          v += ok ? dl[u] * xf[ok ? col[u] : 0] : 0.f;
-          bad |= !ok;
+          if (in && ok) {
+            const float2 xp = xs_pair(col[u] >> 1);
+            v += dl[u] * ((col[u] & 1) ? xp.y : xp.x);
+          }
+          bad |= in && !ok;
         }
-        e += 8u;
+        e += KB;
+        if (!__any_sync(0xffffffffu, e < kcur.e1)) break;
+        load_batch(kcur, e);
       }
-      if (bad) raise_flag(GSDLQ_FLAG_BAD_KINK);
-      if (sv) P.part[((size_t)s * (P.max_seg + 1) + P.max_seg) * width + (lane & (width - 1))] = v;
-      arrive<EPI, NMAT>(P, s0, 1u, lane);
-      if (SPP == 2 && s0 + H < P.n_strips) arrive<EPI, NMAT>(P, s0 + H, 1u, lane, false);
+      const int s = pass_strip(p);
+      if (s < P.n_strips) P.part[((size_t)s * (P.max_seg + 1) + P.max_seg) * width + (lane & (width - 1))] = v;
     }
-  } else if (streamer) {
+    if (bad) raise_flag(GSDLQ_FLAG_BAD_KINK);
+    __threadfence();
+    __syncwarp();
+    // arrival i of this warp: pass i / SPP, half i % SPP
+    const int n_arr = npass * SPP;
+    for (int b0 = 0; b0 < n_arr; b0 += 32) {
+      const int i = b0 + lane;
+      const int s = hw + (i / SPP) * SPP * H + (i % SPP) * H;
+      unsigned fin = 0u;
+      if (i < n_arr && s < P.n_strips) fin = (atom_add_acq_rel(&P.cnt[s], 1u) + 1u == (unsigned)P.UPS + 1u) ? 1u : 0u;
+      unsigned fm = __ballot_sync(0xffffffffu, fin);
+      while (fm) {
+        const int k = b0 + __ffs(fm) - 1;
+        fm &= fm - 1u;
+        finish_strip<EPI, NMAT>(P, hw + (k / SPP) * SPP * H + (k % SPP) * H, lane, pos, s_lr);
+      }
+    }
+  } else {
+    // ==== streaming warps ===================================================================
+    // decode table: lanes 0-15 compute the entries of 16 rows, then every lane writes 16-byte
+    // quarters of four of them (no table memory is read)
+    for (int rb = warp * 16; rb < 256; rb += HX_STREAM * 16) {
+      const int myrow = rb + (lane & 15);
+      uint32_t e = 0u;
+      if (P.xy_table != nullptr) {
+        e = entry_from_xy(P.xy_table, P.n_pts, myrow);
+      } else {
+        int r0 = 0, r1 = 0;
+        if (lattice_of_code(myrow, J.mat[0].radius, r0, r1)) e = pack_bf16x2((float)r0, (float)r1);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t ek = __shfl_sync(0xffffffffu, e, 4 * k + (lane >> 3));
+        const int row = rb + 4 * k + (lane >> 3);
+        *reinterpret_cast<uint4*>(tab + row * 256 + (lane & 7) * 16) = make_uint4(ek, ek, ek, ek);
+      }
+    }
+    if (tid == 0) {
+      redu[32] = 0u;  // zero bits for the lookup addresses, read after a barrier
+      redu[33] = 0u;
+      s_lr[HX_LR_FLAG] = 0.f;
+    }
+    const int w = blockIdx.x * HX_STREAM + warp;
+    const bool streamer = w < P.W;
+    const int u0 = streamer ? unit_begin(P, w) : 0;
+    const int u1 = streamer ? unit_begin(P, w + 1) : 0;
+    // cursor (strip, matrix in strip, unit column) of the next unit to load, and its pointers
+    int ns = u0 / P.UPS;
+    int nm = (u0 - ns * P.UPS) / P.GU;
+    int nc = u0 - ns * P.UPS - nm * P.GU;
+    const uint8_t* pa = nullptr;
+    const uint8_t* pb = nullptr;
+    const uint16_t* qa = nullptr;
+    const uint16_t* qb = nullptr;
+    auto seek = [&]() {
+      const StripInfo si = strip_info<NMAT>(P, ns);
+      const gsdlq_hexmat_t& M = J.mat[si.m0 + nm];
+      const int ra = min(si.rbase + gl, M.rows - 1), rb = min(si.rbase + gl + 8, M.rows - 1);
+      pa = M.codes + (size_t)ra * NP + nc * HX_UB + q * 16;
+      pb = M.codes + (size_t)rb * NP + nc * HX_UB + q * 16;
+      qa = M.scales + (size_t)ra * G + nc * 8;
+      qb = M.scales + (size_t)rb * G + nc * 8;
+    };
+    auto step_next = [&]() {  // the next unit: along the row, or the start of the next row block
+      if (++nc == P.GU) {
+        nc = 0;
+        if (++nm == NMAT) {
+          nm = 0;
+          ++ns;
+        }
+        seek();
+      } else {
+        pa += HX_UB;
+        pb += HX_UB;
+        qa += 8;
+        qb += 8;
+      }
+    };
+    // the FULL path shifts the lane's fp16 scale out of a word holding two groups
+    const int sh = FULL ? 16 * (q & 1) : 0;
+    uint4 cw[4][2];         // code bytes of the unit being consumed / refilled: [segment][row g, g+8]
+    uint32_t sa[4], sb[4];  // the next unit's scale words: [segment]
+    auto load_codes = [&](int s) {
+      if (FULL || nc * HX_UB + 64 * s + 16 * q < NP) {
+        cw[s][0] = ldg_stream_u4(pa + 64 * s);
+        cw[s][1] = ldg_stream_u4(pb + 64 * s);
+      } else {
+        cw[s][0] = make_uint4(0u, 0u, 0u, 0u);  // past the row: its activations are staged as zero
+        cw[s][1] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    };
+    auto load_scales = [&]() {
+      if (FULL) {
+        const uint4 x = ldg_stream_u4(qa), y = ldg_stream_u4(qb);
+        sa[0] = x.x, sa[1] = x.y, sa[2] = x.z, sa[3] = x.w;
+        sb[0] = y.x, sb[1] = y.y, sb[2] = y.z, sb[3] = y.w;
+      } else {
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const int gi = 2 * s + (q & 1);
+          const bool ok = nc * 8 + gi < G;
+          sa[s] = ok ? (uint32_t)__ldg(qa + gi) : 0u;
+          sb[s] = ok ? (uint32_t)__ldg(qb + gi) : 0u;
+        }
+      }
+    };
+    if (streamer && u1 > u0) {
+      seek();
+      load_scales();
+#pragma unroll
+      for (int s = 0; s < 4; ++s) load_codes(s);
+    }
+
+    // ---- wait for the producer of x, then stage the input ---------------------------------
+    pdl_wait();
+    if (tid == 0) {
+      int pv = -1;
+      if (EPI == GSDLQ_EPI_ROPE_KV) pv = *J.pos;
+      reinterpret_cast<int*>(redu)[34] = pv;
+    }
+    int tok = 0;
+    if (J.input_mode == GSDLQ_IN_EMBED) {
+      tok = *J.token;
+      if (tok < 0 || tok >= J.vocab) {
+        if (tid == 0) raise_flag(GSDLQ_FLAG_BAD_TOKEN);
+        tok = 0;
+      }
+    }
+    const bool normed = J.input_mode != GSDLQ_IN_PLAIN;
+    auto load_x = [&](int p) -> float2 {
+      if (J.input_mode == GSDLQ_IN_EMBED) {
+        const uint32_t raw = __ldg(reinterpret_cast<const unsigned int*>(J.embed + (size_t)tok * C) + p);
+        return make_float2(h2f(raw & 0xffffu), h2f(raw >> 16));
+      }
+      return __ldg(reinterpret_cast<const float2*>(J.x) + p);
+    };
+    auto load_w = [&](int p) -> float2 {
+      return normed ? __ldg(reinterpret_cast<const float2*>(J.norm_w) + p) : make_float2(1.f, 1.f);
+    };
+    auto stage = [&](int p, float x0, float x1, float2 wv, float inv) {
+      if (J.input_mode == GSDLQ_IN_EMBED && blockIdx.x == 0 && J.x_out)
+        reinterpret_cast<float2*>(J.x_out)[p] = make_float2(x0, x1);
+      if (normed) {
+        x0 = __fmul_rn(__fmul_rn(x0, inv), wv.x);
+        x1 = __fmul_rn(__fmul_rn(x1, inv), wv.y);
+      }
+      const float b = fmaf(0.8660254037844386f, x1, 0.5f * x0);
+      uint32_t h, l;
+      split_bf16x2(x0, b, h, l);
+      const int j = p & 63, r = j & 15;
+      const uint32_t off = xs_chunk((p >> 6) * 4 + (r >> 2), tab_off) + (uint32_t)((j >> 4) * 32 + (r & 3) * 4);
+      *reinterpret_cast<uint32_t*>(smem + off) = h;
+      *reinterpret_cast<uint32_t*>(smem + off + 16) = l;
+    };
+    // the first XR pairs of each staging thread are loaded in one batch and stay in registers
+    constexpr int XR = 8;
+    float2 xv[XR], wv[XR];
+#pragma unroll
+    for (int k = 0; k < XR; ++k) {
+      const int p = tid + k * NST;
+      if (p < NP) {
+        xv[k] = load_x(p);
+        wv[k] = load_w(p);
+      }
+    }
+    float inv = 1.f;
+    if (normed) {
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < XR; ++k)
+        if (tid + k * NST < NP) ss += xv[k].x * xv[k].x + xv[k].y * xv[k].y;
+      for (int p0 = tid + XR * NST; p0 < NP; p0 += XR * NST) {
+        float2 t[XR];
+#pragma unroll
+        for (int k = 0; k < XR; ++k) t[k] = (p0 + k * NST < NP) ? load_x(p0 + k * NST) : make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < XR; ++k) ss += t[k].x * t[k].x + t[k].y * t[k].y;
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) red[1 + warp] = ss;
+      named_bar_sync(1, NST);
+      float t = 0.f;
+      for (int k = 0; k < HX_STREAM; ++k) t += red[1 + k];  // every thread: no second barrier
+      inv = 1.0f / sqrtf(t / (float)C + J.eps);             // gsd_lq_cpu_engine.c:78
+    }
+#pragma unroll
+    for (int k = 0; k < XR; ++k) {
+      const int p = tid + k * NST;
+      if (p < NP) stage(p, xv[k].x, xv[k].y, wv[k], inv);
+    }
+    for (int p0 = tid + XR * NST; p0 < NP; p0 += XR * NST) {
+#pragma unroll
+      for (int k = 0; k < XR; ++k) {
+        const int p = p0 + k * NST;
+        if (p < NP) {
+          xv[k] = load_x(p);
+          wv[k] = load_w(p);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < XR; ++k) {
+        const int p = p0 + k * NST;
+        if (p < NP) stage(p, xv[k].x, xv[k].y, wv[k], inv);
+      }
+    }
+    // pairs past the row end of the last unit read zero activations
+    for (int p = NP + tid; p < P.GU * HX_UB; p += NST) {
+      const int j = p & 63, r = j & 15;
+      const uint32_t off = xs_chunk((p >> 6) * 4 + (r >> 2), tab_off) + (uint32_t)((j >> 4) * 32 + (r & 3) * 4);
+      *reinterpret_cast<uint32_t*>(smem + off) = 0u;
+      *reinterpret_cast<uint32_t*>(smem + off + 16) = 0u;
+    }
+    named_bar_sync(1, NST);             // table and splits complete for the streaming warps
+    named_bar_arrive(2, HX_THREADS);    // ... and released to the helper warps
+    const int pos = reinterpret_cast<const int*>(redu)[34];
+    if (streamer) {
     // ---- streaming warps --------------------------------------------------------------
-    const uint32_t lane4x = (uint32_t)lane * 4u | reinterpret_cast<const volatile uint32_t*>(red)[32];
-    const uint32_t dep = reinterpret_cast<const volatile uint32_t*>(red)[33];  // zero, read after the barrier
+    const uint32_t lane4x = (uint32_t)lane * 4u | reinterpret_cast<const volatile uint32_t*>(redu)[32];
+    const uint32_t dep = reinterpret_cast<const volatile uint32_t*>(redu)[33];  // zero, read after the barrier
     // B operand: lane (g, q) supplies column g.  Columns 0/1 (hi/lo of group A) are nonzero only
     // on the k rows of lanes q = 0, 1, columns 2/3 (group B) only on those of q = 2, 3, columns
-    // 4-7 are zero.  Every lane loads the slice of a lane that has real data in its column (so
-    // a warp reads 8 distinct 16-byte slices = one conflict-free 128-byte chunk) and masks.
-    const int g3 = gl & 3;
-    const bool same = (g3 >> 1) == (q >> 1);
-    const uint32_t boff = (uint32_t)((same ? q : (q ^ 2)) * 32 + (gl & 1) * 16);
-    const uint32_t bmask = (gl < 4 && same) ? 0xffffffffu : 0u;
+    // 4-7 are zero.  The 8 lanes with data read one conflict-free 128-byte chunk per load.
+    const bool bld = gl < 4 && ((gl >> 1) == (q >> 1));
+    const uint32_t boff = (uint32_t)(q * 32 + (gl & 1) * 16);
+    uint4 bv[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
     int cur_s = ns, cur_m = nm, cur_c = nc;
-    advance();
-    seek();
+    if (u1 > u0 + 1) step_next();
     int seg_s = cur_s;
     float acc[NMAT][2];
 #pragma unroll
     for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
     auto emit = [&](int s) {
-      const int seg = w - warp_of((long long)s * P.UPS, P.T, P.W);
-      constexpr int width = NMAT * 16;
+      const int seg = w - warp_of_unit(P, s * P.UPS);
       float* slot = P.part + ((size_t)s * (P.max_seg + 1) + seg) * width;
 #pragma unroll
       for (int mm = 0; mm < NMAT; ++mm) {
@@ -705,7 +874,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         }
       }
     };
-    for (long long u = u0; u < u1; ++u) {
+    for (int u = u0; u < u1; ++u) {
       if (cur_s != seg_s) {
         emit(seg_s);
         seg_s = cur_s;
@@ -725,7 +894,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         float rg, rh;
-        segment_mma(cw[s][0], cw[s][1], bbase + (uint32_t)s * 4u * bstride, bstride, bmask, lane4x, rg, rh);
+        segment_mma(cw[s][0], cw[s][1], bbase + (uint32_t)s * 4u * bstride, bstride, bld, bv, lane4x, rg, rh);
         if (more) load_codes(s);  // refill this segment's registers with the next unit
         rg_sum = fmaf(h2f((uint16_t)(swa[s] >> sh)), rg, rg_sum);
         rh_sum = fmaf(h2f((uint16_t)(swb[s] >> sh)), rh, rh_sum);
@@ -738,23 +907,33 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         acc[NMAT - 1][1] += rh_sum;
       }
       cur_s = ns, cur_m = nm, cur_c = nc;
-      if (more) {
-        advance();
-        seek();
-      }
+      if (u + 2 < u1) step_next();
     }
     if (u1 > u0) {
       emit(seg_s);
       // the counts are deferred to the end of the range: a fence mid-range would wait for the code
-      // loads in flight.  One fence covers all of this warp's slot stores, then one count per
-      // strip the range touched.
+      // loads in flight.  One fence covers all of this warp's slot stores; lane i then counts this
+      // warp's units of the i-th strip the range touched.
       __threadfence();
-      const int s_a = (int)(u0 / P.UPS), s_b = (int)((u1 - 1) / P.UPS);
-      for (int s = s_a; s <= s_b; ++s) {
-        const long long a = max(u0, (long long)s * P.UPS), b = min(u1, (long long)s * P.UPS + P.UPS);
-        arrive<EPI, NMAT>(P, s, (unsigned)(b - a), lane, false);
+      __syncwarp();
+      const int s_a = u0 / P.UPS, s_b = (u1 - 1) / P.UPS;
+      for (int b0 = s_a; b0 <= s_b; b0 += 32) {
+        const int s = b0 + lane;
+        unsigned fin = 0u;
+        if (s <= s_b) {
+          const int a = max(u0, s * P.UPS), b = min(u1, s * P.UPS + P.UPS);
+          const unsigned units = (unsigned)(b - a);
+          fin = (atom_add_acq_rel(&P.cnt[s], units) + units == (unsigned)P.UPS + 1u) ? 1u : 0u;
+        }
+        unsigned fm = __ballot_sync(0xffffffffu, fin);
+        while (fm) {
+          const int i = __ffs(fm) - 1;
+          fm &= fm - 1u;
+          finish_strip<EPI, NMAT>(P, b0 + i, lane, pos, s_lr);
+        }
       }
     }
+      }
   }
 
   pdl_launch_dependents();
@@ -809,10 +988,14 @@ static int hexmv_plan(HexmvParams& P) {
   P.GU = (P.G + 7) / 8;
   P.UPS = P.nmat * P.GU;
   P.T = (long long)P.n_strips * P.UPS;
+  if (P.T >= (1LL << 31)) return GSDLQ_ERR_UNSUPPORTED;  // unit indices are 32-bit in the kernel
   const int max_w = num_sms() * HX_STREAM;
   P.W = (int)std::min<long long>(max_w, P.T);
-  const long long lmin = P.T / P.W;
-  P.max_seg = (int)((P.UPS - 1 + lmin - 1) / lmin) + 1;
+  P.TW = hx_cumw(P.W);
+  P.w_per_unit = (float)P.W / (float)P.T;
+  // partial slots per strip: consecutive warps' first units are at least 3T/TW apart, so a strip
+  // of UPS units meets at most ceil(UPS * TW / 3T) + 2 warps (empty ranges in between included)
+  P.max_seg = (int)((P.UPS * P.TW + 3 * P.T - 1) / (3 * P.T)) + 2;
   const int grid = (P.W + HX_STREAM - 1) / HX_STREAM;
   int lr = 0;
   for (int m = 0; m < 4; ++m) P.lr_off[m] = 0;
@@ -824,8 +1007,8 @@ static int hexmv_plan(HexmvParams& P) {
   const int helpers = grid * HX_HELP;
   P.lr_chunks = (C / 8 + helpers - 1) / helpers;
   P.ovf_bytes = std::max(0, P.GU * 16 - 256) * 128;
-  // shared-memory limits: overflow chunks below the table, xf above it
-  if (hx_layout(P.ovf_bytes).low_end > (int)HX_TAB_ABS - HX_BASE_MAX || hx_dyn_smem(C) > 227 * 1024)
+  // shared-memory limit: the table region plus the activation-split overflow chunks
+  if (hx_dyn_smem(P.ovf_bytes) > 227 * 1024)
     return GSDLQ_ERR_UNSUPPORTED;
   return GSDLQ_OK;
 }
@@ -840,7 +1023,7 @@ static bool hexmv_full(const HexmvParams& P) {
 
 template <int EPI, bool FULL>
 static int hexmv_launch_t(const HexmvParams& P, cudaStream_t s) {
-  const int dyn = hx_dyn_smem(P.cols);
+  const int dyn = hx_dyn_smem(P.ovf_bytes);
   static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
