@@ -114,13 +114,19 @@ __host__ __device__ __forceinline__ int hx_unit_begin(long long T, long long TW,
   return (int)(T * hx_cumw(w) / TW);
 }
 __device__ __forceinline__ int unit_begin(const HexmvParams& P, int w) { return hx_unit_begin(P.T, P.TW, w); }
-// warp whose range contains unit i: the largest w with unit_begin(w) <= i (estimate, then exact steps)
+// warp whose range contains unit i: the largest w with unit_begin(w) <= i, i.e. with
+// cumw(w) <= c = floor(((i + 1) * TW - 1) / T); cumw is a whole number of CTA cycles plus a local
+// prefix, so w follows from one division and a scan of the 14 local prefixes.
 __host__ __device__ __forceinline__ int hx_warp_of(long long T, long long TW, int W, float w_per_unit, int i) {
-  int w = (int)(((float)i + 0.5f) * w_per_unit);
-  w = w < 0 ? 0 : (w > W - 1 ? W - 1 : w);
-  while (w + 1 < W && hx_unit_begin(T, TW, w + 1) <= i) ++w;
-  while (w > 0 && hx_unit_begin(T, TW, w) > i) --w;
-  return w;
+  (void)w_per_unit;
+  const long long c = ((long long)(i + 1) * TW - 1) / T;
+  const int cyc = hx_lp(HX_STREAM);
+  const long long q = c / cyc;
+  const int r = (int)(c - q * cyc);
+  int l = 0;
+  while (l + 1 < HX_STREAM && hx_lp(l + 1) <= r) ++l;
+  const long long w = q * HX_STREAM + l;
+  return (int)(w < W - 1 ? w : W - 1);
 }
 __device__ __forceinline__ int warp_of_unit(const HexmvParams& P, int i) { return hx_warp_of(P.T, P.TW, P.W, P.w_per_unit, i); }
 
@@ -249,6 +255,22 @@ __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
   return old;
 }
 
+// bounded spin (1 s of %globaltimer) until a shared-memory flag set by another warp of the CTA is
+// nonzero; on timeout the flag is raised and the caller continues
+__device__ __forceinline__ void wait_shared_flag(const volatile float* flag, int lane) {
+  if (*flag != 0.f) return;
+  unsigned long long t0, t1;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (*flag == 0.f) {
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (t1 - t0 > 1000000000ull) {
+      if (lane == 0) raise_flag(GSDLQ_FLAG_TIMEOUT);
+      return;
+    }
+    __nanosleep(64);
+  }
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -357,11 +379,10 @@ __device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float 
   }
 }
 
-// Sum a completed strip's slots in slot order, add the low-rank term and run the epilogue
-// (one warp).  Once the projection is complete, every load (slots, U row, S, tmp_k, epilogue
-// operands) is issued in one batch; the U rows were pulled into L2 by the helper warps.
+// Sum a completed strip's slots in slot order and run the epilogue (one warp).  The helper slot
+// already holds the kink and low-rank terms; the slot and epilogue loads go out in one batch.
 template <int EPI, int NMAT>
-__device__ void finish_strip(const HexmvParams& P, int s, int lane, int pos, const volatile float* s_lr) {
+__device__ void finish_strip(const HexmvParams& P, int s, int lane, int pos) {
   // the arriving lane's acq_rel count was the acquire; the warp barrier orders the other lanes'
   // reads after it
   __syncwarp();
@@ -371,19 +392,7 @@ __device__ void finish_strip(const HexmvParams& P, int s, int lane, int pos, con
   const int nseg = w_last - w_first + 1;
   constexpr int width = NMAT * 16;
   const StripInfo si = strip_info<NMAT>(P, s);
-  const int mm = (NMAT == 2) ? (lane >> 4) : 0;
-  const gsdlq_hexmat_t& M = P.job.mat[si.m0 + mm];
-  const int row = si.rbase + (lane & 15);
-  const bool active = lane < width && row < M.rows;
-  const int kd = active ? M.k_dim : 0;
-  // loads that do not need the projection: epilogue operands, U row, S, the partial slots
   const EpiPre pre = epilogue_pre<EPI>(P, si, lane, pos);
-  float uu[16];
-  {
-    const uint16_t* ur = M.U + (size_t)(active ? row : 0) * kd;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) uu[j] = j < kd ? h2f(__ldcg(ur + j)) : 0.f;
-  }
   float* base = P.part + (size_t)s * (P.max_seg + 1) * width;
   float v = 0.f;
   if (lane < width) {
@@ -391,7 +400,7 @@ __device__ void finish_strip(const HexmvParams& P, int s, int lane, int pos, con
     float pv[B];
 #pragma unroll
     for (int k = 0; k < B; ++k) pv[k] = k < nseg ? __ldcg(base + (size_t)k * width + lane) : 0.f;
-    const float hv = __ldcg(base + (size_t)P.max_seg * width + lane);  // helper slot: kinks
+    const float hv = __ldcg(base + (size_t)P.max_seg * width + lane);  // helper slot: kinks + low rank
 #pragma unroll
     for (int k = 0; k < B; ++k) v += pv[k];
     for (int k = B; k < nseg; ++k) v += __ldcg(base + (size_t)k * width + lane);
@@ -402,33 +411,7 @@ __device__ void finish_strip(const HexmvParams& P, int s, int lane, int pos, con
     base[(size_t)P.max_seg * width + lane] = 0.f;
   }
   if (lane == 0) P.cnt[s] = 0u;
-  float lr = 0.f;
-  if (__any_sync(0xffffffffu, kd > 0)) {
-    if (P.tmp_k_ext != nullptr) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (j < kd) lr += uu[j] * __ldg(P.tmp_k_ext + j);
-    } else {
-      // tmp_k was published in shared memory by this CTA's last helper warp (bounded wait, 1 s)
-      if (s_lr[HX_LR_FLAG] == 0.f) {
-        unsigned long long t0, t1;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-        while (s_lr[HX_LR_FLAG] == 0.f) {
-          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-          if (t1 - t0 > 1000000000ull) {
-            if (lane == 0) raise_flag(GSDLQ_FLAG_TIMEOUT);
-            break;
-          }
-          __nanosleep(64);
-        }
-      }
-      const volatile float* tk = s_lr + P.lr_off[si.m0 + mm];
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (j < kd) lr += uu[j] * tk[j];
-    }
-  }
-  strip_epilogue<EPI>(P, si, v + lr, lane, pre, pos);
+  strip_epilogue<EPI>(P, si, v, lane, pre, pos);
 }
 
 template <int EPI, bool FULL>
@@ -504,22 +487,18 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         dl[u] = eu < k.e1 ? __ldg(k.del + eu) : 0.f;
       }
     };
+    // the U row of this lane's row in the pass (raw fp16 bits), loaded with the pass's first batch
+    uint16_t ur[16];
+    auto load_u = [&](const KRow& k) {
+      const int kd = k.row >= 0 ? J.mat[k.km].k_dim : 0;
+      const uint16_t* up = J.mat[k.km].U + (size_t)(k.row < 0 ? 0 : k.row) * kd;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) ur[j] = j < kd ? __ldg(up + j) : (uint16_t)0;
+    };
     // ---- before the wait: everything that does not depend on x -----------------------------
     KRow kcur = krow(0), knext = krow(1);
     load_batch(kcur, kcur.e0);
-    // the finishing warps read the U rows of these strips: pull them into L2 now (one 32-byte row
-    // per lane per pass)
-    for (int p = 0; p < npass; ++p) {
-      const int s = pass_strip(p);
-      if (s < P.n_strips) {
-        const StripInfo si = strip_info<NMAT>(P, s);
-        const int km = si.m0 + ((NMAT == 2) ? (lane >> 4) : 0);
-        const int row = si.rbase + (lane & 15);
-        const int kd = J.mat[km].k_dim;
-        if (kd > 0 && row < J.mat[km].rows)
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(J.mat[km].U + (size_t)row * kd));
-      }
-    }
+    load_u(kcur);
     constexpr int LRC = 4;  // Vt chunks per row held in registers; the rest of the slice via L2
     uint4 vr[2][LRC];
 #pragma unroll
@@ -610,6 +589,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         kcur = knext;
         knext = krow(p + 1);  // in flight during this pass
         load_batch(kcur, kcur.e0);
+        load_u(kcur);
       }
       float v = 0.f;
       for (uint32_t e = kcur.e0;;) {
@@ -626,6 +606,23 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         e += KB;
         if (!__any_sync(0xffffffffu, e < kcur.e1)) break;
         load_batch(kcur, e);
+      }
+      // the low-rank term: U row . tmp_k, tmp_k from this CTA's shared copy (or the caller's)
+      const int kd = kcur.row >= 0 ? J.mat[kcur.km].k_dim : 0;
+      if (__any_sync(0xffffffffu, kd > 0)) {
+        float lr = 0.f;
+        if (P.tmp_k_ext != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (j < kd) lr += h2f(ur[j]) * __ldg(P.tmp_k_ext + j);
+        } else {
+          wait_shared_flag(s_lr + HX_LR_FLAG, lane);
+          const volatile float* tk = s_lr + P.lr_off[kcur.km];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (j < kd) lr += h2f(ur[j]) * tk[j];
+        }
+        v += lr;
       }
       const int s = pass_strip(p);
       if (s < P.n_strips) P.part[((size_t)s * (P.max_seg + 1) + P.max_seg) * width + (lane & (width - 1))] = v;
@@ -644,7 +641,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       while (fm) {
         const int k = b0 + __ffs(fm) - 1;
         fm &= fm - 1u;
-        finish_strip<EPI, NMAT>(P, hw + (k / SPP) * SPP * H + (k % SPP) * H, lane, pos, s_lr);
+        finish_strip<EPI, NMAT>(P, hw + (k / SPP) * SPP * H + (k % SPP) * H, lane, pos);
       }
     }
   } else {
@@ -929,7 +926,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         while (fm) {
           const int i = __ffs(fm) - 1;
           fm &= fm - 1u;
-          finish_strip<EPI, NMAT>(P, b0 + i, lane, pos, s_lr);
+          finish_strip<EPI, NMAT>(P, b0 + i, lane, pos);
         }
       }
     }

@@ -12,6 +12,8 @@
 #include <mutex>
 #include <vector>
 
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace gsdlq {
@@ -123,145 +125,209 @@ __global__ void rope_store_kernel(float* q, const float* k, const float* v, uint
 }
 
 // ---------------------------------------------------------------------------------------
-// split-KV decode attention (flash-decoding).  CTA (kv head, split) stages the K and V
-// rows of its token range in shared memory (row stride padded by 16 bytes so that a
-// 16-byte read per thread is conflict-free), computes the scores of all query heads of
-// the group, a per-head softmax of the tile and P.V, and writes (max, sum, acc[hd]); the
-// last CTA of a kv head combines the splits.  Rows of positions < pos come from earlier
-// steps, so they are loaded before the programmatic-dependent-launch wait; q and the
-// row at pos (written by the QKV kernel) after it.
-constexpr int AT_THREADS = 128;
+// split-KV decode attention (flash-decoding).  CTA (kv head, split) processes its token range
+// in tiles of AT_TILE rows: the K and V rows are staged in shared memory (row stride padded by
+// 16 bytes so that 16-byte reads are conflict-free), four threads compute one token's scores
+// for all GQ query heads of the group, a warp per head keeps the running softmax of the
+// split, and each thread accumulates P.V for one dimension pair of one (or two) heads.  The
+// split writes (max, sum, acc[hd]) per head; the last CTA of a kv head combines the splits
+// (one batch of loads per output), or the only split writes the output itself.  Rows of
+// positions < pos come from earlier steps, so the first tile's rows are loaded before the
+// programmatic-dependent-launch wait; q and the row at pos (written by the QKV kernel) after.
+constexpr int AT_THREADS = 256;
+constexpr int AT_TILE = 64;       // tokens per tile
 constexpr int AT_MAX_GQ = 8;
 constexpr int AT_MAX_SPLITS = 32;
-constexpr int AT_TPS_MAX = 64;  // tokens per CTA tile
 
+// tokens per split: a multiple of the tile with at most AT_MAX_SPLITS splits
 inline int attn_tokens_per_split(int max_seq) {
-  int t = 16;
-  while ((max_seq + t - 1) / t > AT_MAX_SPLITS && t < AT_TPS_MAX) t *= 2;
-  return t;
+  const int span = AT_TILE * AT_MAX_SPLITS;
+  return AT_TILE * std::max(1, (max_seq + span - 1) / span);
 }
 
 __device__ __forceinline__ void pdl_wait_ops() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger_ops() { asm volatile("griddepcontrol.launch_dependents;"); }
 
-template <int HD>
+template <int HD, int GQ>
 __global__ void __launch_bounds__(AT_THREADS) attn_kernel(const __grid_constant__ gsdlq_attn_job_t J, int tps) {
-  constexpr int ROWB = HD * 2 + 16;  // padded row bytes
-  constexpr int CH = HD / 8;         // 16-byte chunks per row
-  __shared__ __align__(16) uint8_t sk[AT_TPS_MAX * ROWB];
-  __shared__ __align__(16) uint8_t sv[AT_TPS_MAX * ROWB];
-  __shared__ float sq[AT_MAX_GQ * HD];
-  __shared__ float sp[AT_MAX_GQ][AT_TPS_MAX];
-  __shared__ float sm[AT_MAX_GQ], sl[AT_MAX_GQ];
+  constexpr int ROWB = HD * 2 + 16;         // padded row bytes
+  constexpr int CH = HD / 8;                // 16-byte chunks per row
+  constexpr int DP = HD / 2;                // dimension pairs
+  constexpr int HS = AT_THREADS / DP;       // token groups of the P.V mapping
+  constexpr int NO = (GQ * HD + AT_THREADS - 1) / AT_THREADS;  // outputs per thread
+  __shared__ __align__(16) uint8_t skv[2 * AT_TILE * ROWB];
+  uint8_t* sk = skv;
+  uint8_t* sv = skv + AT_TILE * ROWB;
+  __shared__ __align__(16) float sq[GQ * HD];
+  __shared__ float sp[GQ][AT_TILE];
+  __shared__ float s_m[GQ], s_l[GQ], s_f[GQ];
   __shared__ int s_last;
   const int kvh = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int gq = J.n_heads / J.n_kv_heads;
   const int pos = J.pos_dev ? *J.pos_dev : J.pos_val;
   const bool pos_ok = pos >= 0 && pos < J.max_seq;
   const int len = pos_ok ? pos + 1 : 0;
   const int t0 = split * tps, t1 = min(len, t0 + tps);
-  const int nt = max(0, t1 - t0);
   const size_t tok_stride = (size_t)J.n_kv_heads * HD;
   auto row_off = [&](int t) -> size_t {
     const size_t slot = J.block_table ? (size_t)J.block_table[t / J.page_size] * J.page_size + (t % J.page_size)
                                       : (size_t)J.layer * J.max_seq + t;
     return slot * tok_stride + (size_t)kvh * HD;
   };
-  // rows of earlier positions: independent of the producer kernel (asynchronous copies)
-  for (int i = tid; i < nt * CH; i += AT_THREADS) {
-    const int j = i / CH, c = i - j * CH;
-    if (t0 + j < pos) {
-      const size_t off = row_off(t0 + j) + c * 8;
-      cp_async_16(sk + j * ROWB + c * 16, J.k_cache + off);
-      cp_async_16(sv + j * ROWB + c * 16, J.v_cache + off);
+  // asynchronous copies of the rows of [tb, tb + nt) selected by `which` (0: < pos, 1: == pos, 2: all)
+  auto issue = [&](int tb, int nt, int which) {
+    for (int i = tid; i < nt * CH; i += AT_THREADS) {
+      const int j = i / CH, c = i - j * CH, t = tb + j;
+      if (which == 2 || (which == 0 ? t < pos : t == pos)) {
+        const size_t off = row_off(t) + c * 8;
+        cp_async_16(sk + j * ROWB + c * 16, J.k_cache + off);
+        cp_async_16(sv + j * ROWB + c * 16, J.v_cache + off);
+      }
     }
-  }
-  cp_async_commit();
+    cp_async_commit();
+  };
+  if (t1 > t0) issue(t0, min(AT_TILE, t1 - t0), 0);
   pdl_wait_ops();
   if (!pos_ok && tid == 0 && kvh == 0 && split == 0) raise_flag(GSDLQ_FLAG_BAD_POS);
-  for (int i = tid; i < nt * CH; i += AT_THREADS) {
-    const int j = i / CH, c = i - j * CH;
-    if (t0 + j == pos) {
-      const size_t off = row_off(t0 + j) + c * 8;
-      cp_async_16(sk + j * ROWB + c * 16, J.k_cache + off);
-      cp_async_16(sv + j * ROWB + c * 16, J.v_cache + off);
-    }
+  if (t1 > t0) issue(t0, min(AT_TILE, t1 - t0), 1);
+  for (int i = tid; i < GQ * HD; i += AT_THREADS) sq[i] = __ldg(J.q + (size_t)kvh * GQ * HD + i);
+  if (tid < GQ) {
+    s_m[tid] = -INFINITY;
+    s_l[tid] = 0.f;
   }
-  cp_async_commit();
-  for (int i = tid; i < gq * HD; i += AT_THREADS) sq[i] = __ldg(J.q + (size_t)kvh * gq * HD + i);
-  cp_async_wait_all();
-  __syncthreads();
-  // scores: thread -> (token j, head subset); each reads its K row in 16-byte chunks
-  {
-    const int j = tid % AT_TPS_MAX, hset = tid / AT_TPS_MAX;  // 2 threads per token
-    if (j < nt) {
-      float acc[AT_MAX_GQ];
+  // P.V state: thread -> dimension pair dp, tokens j = tg (mod HS), every head; each V element is
+  // converted once
+  const int dp = tid % DP, tg = tid / DP;
+  float acc[GQ][2];
 #pragma unroll
-      for (int h = 0; h < AT_MAX_GQ; ++h) acc[h] = 0.f;
-      for (int c = 0; c < CH; ++c) {
-        const uint4 kr = *reinterpret_cast<const uint4*>(sk + j * ROWB + c * 16);
-        const uint32_t kw[4] = {kr.x, kr.y, kr.z, kr.w};
+  for (int h = 0; h < GQ; ++h) acc[h][0] = acc[h][1] = 0.f;
+  for (int tb = t0; tb < t1; tb += AT_TILE) {
+    const int nt = min(AT_TILE, t1 - tb);
+    cp_async_wait_all();
+    __syncthreads();
+    // scores: four threads per token, each a quarter of the dimensions, all heads
+    {
+      const int j = tid >> 2, qd = tid & 3;
+      float s[GQ];
 #pragma unroll
-        for (int h = 0; h < AT_MAX_GQ; ++h) {
-          if (h < gq && (h & 1) == hset) {
-            const float* qh = sq + h * HD + c * 8;
+      for (int h = 0; h < GQ; ++h) s[h] = 0.f;
+      if (j < nt) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              acc[h] = fmaf(qh[2 * k], h2f(kw[k] & 0xffffu), acc[h]);
-              acc[h] = fmaf(qh[2 * k + 1], h2f(kw[k] >> 16), acc[h]);
-            }
+        for (int c = qd * (CH / 4); c < (qd + 1) * (CH / 4); ++c) {
+          const uint4 kr = *reinterpret_cast<const uint4*>(sk + j * ROWB + c * 16);
+          const float k0 = h2f(kr.x & 0xffffu), k1 = h2f(kr.x >> 16), k2 = h2f(kr.y & 0xffffu), k3 = h2f(kr.y >> 16);
+          const float k4 = h2f(kr.z & 0xffffu), k5 = h2f(kr.z >> 16), k6 = h2f(kr.w & 0xffffu), k7 = h2f(kr.w >> 16);
+#pragma unroll
+          for (int h = 0; h < GQ; ++h) {
+            const float4 qa = *reinterpret_cast<const float4*>(sq + h * HD + c * 8);
+            const float4 qb = *reinterpret_cast<const float4*>(sq + h * HD + c * 8 + 4);
+            s[h] = fmaf(qa.x, k0, s[h]);
+            s[h] = fmaf(qa.y, k1, s[h]);
+            s[h] = fmaf(qa.z, k2, s[h]);
+            s[h] = fmaf(qa.w, k3, s[h]);
+            s[h] = fmaf(qb.x, k4, s[h]);
+            s[h] = fmaf(qb.y, k5, s[h]);
+            s[h] = fmaf(qb.z, k6, s[h]);
+            s[h] = fmaf(qb.w, k7, s[h]);
           }
         }
       }
 #pragma unroll
-      for (int h = 0; h < AT_MAX_GQ; ++h)
-        if (h < gq && (h & 1) == hset) sp[h][j] = acc[h] * J.sm_scale;
+      for (int h = 0; h < GQ; ++h) {
+        s[h] += __shfl_xor_sync(0xffffffffu, s[h], 1);
+        s[h] += __shfl_xor_sync(0xffffffffu, s[h], 2);
+        if (qd == 0 && j < nt) sp[h][j] = s[h] * J.sm_scale;
+      }
+    }
+    __syncthreads();
+    // running softmax of the split: warp h handles head h (and h + 8 ... none: GQ <= 8)
+    if (warp < GQ) {
+      const int h = warp;
+      const float a = lane < nt ? sp[h][lane] : -INFINITY;
+      const float b = lane + 32 < nt ? sp[h][lane + 32] : -INFINITY;
+      const float mt = warp_max(fmaxf(a, b));
+      const float m_old = s_m[h];
+      const float m = fmaxf(m_old, mt);
+      const float ea = lane < nt ? expf(a - m) : 0.f;
+      const float eb = lane + 32 < nt ? expf(b - m) : 0.f;
+      if (lane < nt) sp[h][lane] = ea;
+      if (lane + 32 < nt) sp[h][lane + 32] = eb;
+      const float sum = warp_sum(ea + eb);
+      if (lane == 0) {
+        const float f = (m_old == -INFINITY) ? 0.f : expf(m_old - m);
+        s_f[h] = f;
+        s_m[h] = m;
+        s_l[h] = s_l[h] * f + sum;
+      }
+    }
+    __syncthreads();
+    // P.V
+#pragma unroll
+    for (int h = 0; h < GQ; ++h) {
+      const float f = s_f[h];
+      acc[h][0] *= f;
+      acc[h][1] *= f;
+    }
+    for (int j = tg; j < nt; j += HS) {
+      const uint32_t v2 = *reinterpret_cast<const uint32_t*>(sv + j * ROWB + dp * 4);
+      const float v0 = h2f(v2 & 0xffffu), v1 = h2f(v2 >> 16);
+#pragma unroll
+      for (int h = 0; h < GQ; ++h) {
+        const float p = sp[h][j];
+        acc[h][0] = fmaf(p, v0, acc[h][0]);
+        acc[h][1] = fmaf(p, v1, acc[h][1]);
+      }
+    }
+    if (tb + AT_TILE < t1) {
+      __syncthreads();  // every read of this tile is done before the next one is copied in
+      issue(tb + AT_TILE, min(AT_TILE, t1 - tb - AT_TILE), 2);
     }
   }
+  // sum the token groups (the staging buffers are free now): red[(tg * GQ + h) * HD + d]
   __syncthreads();
-  // softmax of the tile per head (warp w handles heads w, w+4)
-  for (int h = warp; h < gq; h += AT_THREADS / 32) {
-    float mx = -INFINITY;
-    for (int j = lane; j < nt; j += 32) mx = fmaxf(mx, sp[h][j]);
-    mx = warp_max(mx);
-    float sum = 0.f;
-    for (int j = lane; j < nt; j += 32) {
-      const float e = expf(sp[h][j] - mx);
-      sp[h][j] = e;
-      sum += e;
-    }
-    sum = warp_sum(sum);
-    if (lane == 0) {
-      sm[h] = mx;
-      sl[h] = sum;
-    }
+  float* red = reinterpret_cast<float*>(skv);
+#pragma unroll
+  for (int h = 0; h < GQ; ++h) {
+    red[(tg * GQ + h) * HD + 2 * dp] = acc[h][0];
+    red[(tg * GQ + h) * HD + 2 * dp + 1] = acc[h][1];
   }
   __syncthreads();
-  // P.V: thread -> (dimension d, head subset)
-  float* part = J.partial + ((size_t)kvh * nsplit + split) * (size_t)gq * (HD + 2);
-  {
-    constexpr int HSETS = AT_THREADS / HD;  // 1 (hd 128), 2 (hd 64), 4 (hd 32)
-    const int d = tid % HD, hs = tid / HD;
-    float acc[AT_MAX_GQ];
+  float res[NO];
 #pragma unroll
-    for (int h = 0; h < AT_MAX_GQ; ++h) acc[h] = 0.f;
-    for (int j = 0; j < nt; ++j) {
-      const float vv = h2f(*reinterpret_cast<const uint16_t*>(sv + j * ROWB + d * 2));
-#pragma unroll
-      for (int h = 0; h < AT_MAX_GQ; ++h)
-        if (h < gq && h % HSETS == hs) acc[h] = fmaf(sp[h][j], vv, acc[h]);
+  for (int k = 0; k < NO; ++k) {
+    const int o = tid + k * AT_THREADS;
+    res[k] = 0.f;
+    if (o < GQ * HD) {
+      const int h = o / HD, d = o - h * HD;
+      for (int g = 0; g < HS; ++g) res[k] += red[(g * GQ + h) * HD + d];
     }
+  }
+  const int nact = min(nsplit, (len + tps - 1) / tps);
+  if (nact == 1) {
+    // a single split holds the whole sequence: write the output directly
+    if (split == 0) {
 #pragma unroll
-    for (int h = 0; h < AT_MAX_GQ; ++h) {
-      if (h < gq && h % HSETS == hs) {
-        part[h * (HD + 2) + d] = acc[h];
-        if (d == 0) {
-          part[h * (HD + 2) + HD] = nt > 0 ? sm[h] : -INFINITY;
-          part[h * (HD + 2) + HD + 1] = nt > 0 ? sl[h] : 0.f;
+      for (int k = 0; k < NO; ++k) {
+        const int o = tid + k * AT_THREADS;
+        if (o < GQ * HD) {
+          const float l = s_l[o / HD];
+          J.out[(size_t)kvh * GQ * HD + o] = l > 0.f ? res[k] / l : 0.f;
         }
       }
     }
+    pdl_trigger_ops();
+    return;
+  }
+  float* part = J.partial + ((size_t)kvh * nsplit + split) * (size_t)GQ * (HD + 2);
+#pragma unroll
+  for (int k = 0; k < NO; ++k) {
+    const int o = tid + k * AT_THREADS;
+    if (o < GQ * HD) part[(o / HD) * (HD + 2) + (o % HD)] = res[k];
+  }
+  if (tid < GQ) {
+    const bool any = t1 > t0;
+    part[tid * (HD + 2) + HD] = any ? s_m[tid] : -INFINITY;
+    part[tid * (HD + 2) + HD + 1] = any ? s_l[tid] : 0.f;
   }
   pdl_trigger_ops();
   // the last CTA of this kv head combines all splits
@@ -271,39 +337,108 @@ __global__ void __launch_bounds__(AT_THREADS) attn_kernel(const __grid_constant_
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const float* base = J.partial + (size_t)kvh * nsplit * gq * (HD + 2);
-  const int nact = min(nsplit, (len + tps - 1) / tps);
-  for (int i = tid; i < gq * HD; i += AT_THREADS) {
-    const int g = i / HD, d = i - g * HD;
-    float M = -INFINITY;
-    for (int sidx = 0; sidx < nact; ++sidx) M = fmaxf(M, __ldcg(base + ((size_t)sidx * gq + g) * (HD + 2) + HD));
-    float a = 0.f, Ls = 0.f;
-    for (int sidx = 0; sidx < nact; ++sidx) {
-      const float* ps = base + ((size_t)sidx * gq + g) * (HD + 2);
-      const float ms = __ldcg(ps + HD);
-      if (ms == -INFINITY) continue;
-      const float f = expf(ms - M);
-      a += __ldcg(ps + d) * f;
-      Ls += __ldcg(ps + HD + 1) * f;
+  const float* base = J.partial + (size_t)kvh * nsplit * GQ * (HD + 2);
+  // one batch of loads: every split's (max, sum) and this thread's partial values
+  __shared__ float cw[GQ][AT_MAX_SPLITS], cl[GQ][AT_MAX_SPLITS], cL[GQ];
+  float mv = -INFINITY, lv = 0.f;
+  const int gi = tid / nact, si = tid - gi * nact;
+  if (tid < GQ * nact) {
+    const float* ps = base + ((size_t)si * GQ + gi) * (HD + 2);
+    mv = __ldcg(ps + HD);
+    lv = __ldcg(ps + HD + 1);
+  }
+  constexpr int NB = NO < 2 ? NO : 2;  // outputs whose partials are loaded with the maxima
+  float pv[NB][AT_MAX_SPLITS];
+  auto load_pv = [&](int k0) {
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      const int o = tid + (k0 + k) * AT_THREADS;
+      const int g = o / HD, d = o - g * HD;
+#pragma unroll
+      for (int sidx = 0; sidx < AT_MAX_SPLITS; ++sidx)
+        pv[k][sidx] = (k0 + k < NO && o < GQ * HD && sidx < nact) ? __ldcg(base + ((size_t)sidx * GQ + g) * (HD + 2) + d) : 0.f;
     }
-    J.out[(size_t)(kvh * gq + g) * HD + d] = (Ls > 0.f) ? a / Ls : 0.f;
+  };
+  load_pv(0);
+  if (tid < GQ * nact) {
+    cw[gi][si] = mv;
+    cl[gi][si] = lv;
+  }
+  __syncthreads();
+  if (tid < GQ) {
+    float M = -INFINITY;
+    for (int sidx = 0; sidx < nact; ++sidx) M = fmaxf(M, cw[tid][sidx]);
+    float L = 0.f;
+    for (int sidx = 0; sidx < nact; ++sidx) {
+      const float ms = cw[tid][sidx];
+      const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
+      cw[tid][sidx] = f;
+      L += cl[tid][sidx] * f;
+    }
+    cL[tid] = L;
+  }
+  __syncthreads();
+  for (int k0 = 0; k0 < NO; k0 += NB) {
+    if (k0 > 0) load_pv(k0);
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      const int o = tid + (k0 + k) * AT_THREADS;
+      if (k0 + k < NO && o < GQ * HD) {
+        const int g = o / HD;
+        float a = 0.f;
+#pragma unroll
+        for (int sidx = 0; sidx < AT_MAX_SPLITS; ++sidx)
+          if (sidx < nact) a += pv[k][sidx] * cw[g][sidx];
+        const float L = cL[g];
+        J.out[(size_t)kvh * GQ * HD + o] = (L > 0.f) ? a / L : 0.f;
+      }
+    }
   }
   if (tid == 0) J.workspace[kvh] = 0u;
+}
+
+// the P.V token-group reduction reuses the K/V staging buffers; shapes where it does not fit are
+// not instantiated (head_dim 32 with more than 5 query heads per kv head)
+template <int HD, int GQ>
+constexpr bool attn_fits() {
+  return (AT_THREADS / (HD / 2)) * GQ * HD * 4 <= 2 * AT_TILE * (HD * 2 + 16);
+}
+
+template <int HD, int GQ>
+static cudaError_t attention_launch_t(const cudaLaunchConfig_t& cfg, const gsdlq_attn_job_t& J, int tps) {
+  if constexpr (attn_fits<HD, GQ>()) return cudaLaunchKernelEx(&cfg, attn_kernel<HD, GQ>, J, tps);
+  return cudaErrorNotSupported;
+}
+
+template <int HD>
+static cudaError_t attention_launch_hd(const cudaLaunchConfig_t& cfg, const gsdlq_attn_job_t& J, int tps, int gq) {
+  switch (gq) {
+    case 1: return attention_launch_t<HD, 1>(cfg, J, tps);
+    case 2: return attention_launch_t<HD, 2>(cfg, J, tps);
+    case 3: return attention_launch_t<HD, 3>(cfg, J, tps);
+    case 4: return attention_launch_t<HD, 4>(cfg, J, tps);
+    case 5: return attention_launch_t<HD, 5>(cfg, J, tps);
+    case 6: return attention_launch_t<HD, 6>(cfg, J, tps);
+    case 7: return attention_launch_t<HD, 7>(cfg, J, tps);
+    default: return attention_launch_t<HD, 8>(cfg, J, tps);
+  }
 }
 
 static int attention_launch(const gsdlq_attn_job_t& J, cudaStream_t s) {
   if (!J.q || !J.k_cache || !J.v_cache || !J.out || !J.partial || !J.workspace) return GSDLQ_ERR_INVALID;
   // K/V rows are read in 16-byte chunks
   if ((reinterpret_cast<uintptr_t>(J.k_cache) | reinterpret_cast<uintptr_t>(J.v_cache)) & 15u) return GSDLQ_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(J.q) & 3u) return GSDLQ_ERR_INVALID;
   if (J.n_heads <= 0 || J.n_kv_heads <= 0 || J.n_heads % J.n_kv_heads) return GSDLQ_ERR_INVALID;
-  if (J.n_heads / J.n_kv_heads > AT_MAX_GQ) return GSDLQ_ERR_UNSUPPORTED;
+  const int gq = J.n_heads / J.n_kv_heads;
+  if (gq > AT_MAX_GQ) return GSDLQ_ERR_UNSUPPORTED;
   if (J.max_seq <= 0 || J.layer < 0) return GSDLQ_ERR_INVALID;
   if (J.block_table && J.page_size <= 0) return GSDLQ_ERR_INVALID;
   if (!J.pos_dev && (J.pos_val < 0 || J.pos_val >= J.max_seq)) return GSDLQ_ERR_INVALID;
   const int tps = attn_tokens_per_split(J.max_seq);
-  if ((J.max_seq + tps - 1) / tps > 65535) return GSDLQ_ERR_UNSUPPORTED;
+  const int nsplit = (J.max_seq + tps - 1) / tps;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(J.n_kv_heads, (J.max_seq + tps - 1) / tps);
+  cfg.gridDim = dim3(J.n_kv_heads, nsplit);
   cfg.blockDim = dim3(AT_THREADS);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -312,10 +447,11 @@ static int attention_launch(const gsdlq_attn_job_t& J, cudaStream_t s) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e;
-  if (J.head_dim == 128) e = cudaLaunchKernelEx(&cfg, attn_kernel<128>, J, tps);
-  else if (J.head_dim == 64) e = cudaLaunchKernelEx(&cfg, attn_kernel<64>, J, tps);
-  else if (J.head_dim == 32) e = cudaLaunchKernelEx(&cfg, attn_kernel<32>, J, tps);
+  if (J.head_dim == 128) e = attention_launch_hd<128>(cfg, J, tps, gq);
+  else if (J.head_dim == 64) e = attention_launch_hd<64>(cfg, J, tps, gq);
+  else if (J.head_dim == 32) e = attention_launch_hd<32>(cfg, J, tps, gq);
   else return GSDLQ_ERR_UNSUPPORTED;
+  if (e == cudaErrorNotSupported) return GSDLQ_ERR_UNSUPPORTED;
   if (e != cudaSuccess) return record_cuda_error(e);
   return GSDLQ_OK;
 }
