@@ -27,7 +27,7 @@ FLAG_NAMES = {0x1: "bad_code", 0x2: "bad_kink", 0x4: "bad_pos", 0x8: "bad_table"
 class HexMat(ctypes.Structure):
     _fields_ = [("codes", vp), ("scales", vp), ("U", vp), ("S", vp), ("Vt", vp), ("row_ptr", vp),
                 ("kink_cols", vp), ("kink_deltas", vp), ("rows", i32), ("cols", i32), ("k_dim", i32),
-                ("radius", i32)]
+                ("radius", i32), ("unit_kink_off", vp), ("unit_kinks", vp)]
 
 
 class LinearJob(ctypes.Structure):
@@ -67,6 +67,7 @@ SIGNATURES = {
     "gsdlq_attention": ([ctypes.POINTER(AttnJob), vp], i32),
     "gsdlq_rope_table": ([vp, i32, i32, f32], i32),
     "gsdlq_greedy_advance": ([vp, vp, vp, vp, vp, i32, vp], i32),
+    "gsdlq_unit_kinks": ([vp, vp, vp, i32, i32, vp, vp, vp], i32),
 }
 
 

@@ -95,6 +95,7 @@ struct HexmvParams {
   int lr_off[4];           // prefix of k_dim over the matrices
   int lr_chunks;           // 8-column chunks of every Vt row per helper warp
   int ovf_bytes;           // activation-split overflow region
+  int ukink;               // every matrix has per-unit kink lists: the streaming warps apply them
   unsigned* ctl;
   unsigned* cnt;           // [n_strips]
   float* part;             // [n_strips][max_seg + 1][nmat * 16]
@@ -149,7 +150,7 @@ inline size_t hexmv_ws_bytes_for(int n_strips, int max_seg, int nmat) {
 // allocation for B = 0; the kernel checks B and raises GSDLQ_FLAG_UNSUPPORTED if its reduction
 // words would not fit below the table.
 constexpr uint32_t HX_TAB_ABS = 0x1000u;
-constexpr int HX_RED_BYTES = 512;
+constexpr int HX_RED_BYTES = 2048;
 constexpr int HX_LR_FLAG = 60;  // index (in the shared tmp_k area) of its ready flag
 
 inline int hx_dyn_smem(int ovf_bytes) { return (int)HX_TAB_ABS + 0x10000 + ovf_bytes; }
@@ -431,8 +432,20 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
   const uint32_t tab_off = HX_TAB_ABS - sbase;
   uint8_t* tab = smem + tab_off;
   float* red = reinterpret_cast<float*>(smem + tab_off - HX_RED_BYTES);
-  // [1..16] warp sums, [32] [33] zero words, [34] position; s_lr: [0..48) tmp_k, [HX_LR_FLAG] ready
+  // [1..16] warp sums, [32] [33] zero words, [34] position; s_lr: [0..48) tmp_k, [HX_LR_FLAG] ready;
+  // then 16 kink row sums per streaming warp
   volatile float* s_lr = red + 64;
+  float* s_ks = red + 128 + 16 * warp;
+  // (x[2p], x[2p+1]) recovered from the staged splits (hi + lo: about 16 significant bits)
+  auto xs_pair = [&](int p) -> float2 {
+    const int j = p & 63, r = j & 15;
+    const uint32_t off = xs_chunk((p >> 6) * 4 + (r >> 2), tab_off) + (uint32_t)((j >> 4) * 32 + (r & 3) * 4);
+    const uint32_t h = *reinterpret_cast<const uint32_t*>(smem + off);
+    const uint32_t l = *reinterpret_cast<const uint32_t*>(smem + off + 16);
+    const float x0 = bf16lo_to_f(h) + bf16lo_to_f(l);
+    const float b = bf16hi_to_f(h) + bf16hi_to_f(l);
+    return make_float2(x0, (b - 0.5f * x0) * 1.1547005383792515f);
+  };
   uint32_t* redu = reinterpret_cast<uint32_t*>(red);
 
   // Barriers: 0 = the whole CTA (end only); 1 = the 14 streaming warps; 2 = streaming warps
@@ -469,9 +482,11 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         const int row = si.rbase + (lane & 15);
         if (row < J.mat[km].rows) {
           k.row = row;
-          const uint32_t* rp = J.mat[km].row_ptr;
-          k.e0 = __ldg(rp + row);
-          k.e1 = __ldg(rp + row + 1);
+          if (!P.ukink) {  // otherwise the streaming warps apply the kinks
+            const uint32_t* rp = J.mat[km].row_ptr;
+            k.e0 = __ldg(rp + row);
+            k.e1 = __ldg(rp + row + 1);
+          }
         }
       }
       return k;
@@ -518,17 +533,8 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
     named_bar_sync(2, HX_THREADS);
     pdl_wait();
     const int pos = reinterpret_cast<const int*>(redu)[34];
-    // the input values come back from the staged splits (hi + lo: about 16 significant bits),
-    // so no fp32 copy of x occupies shared memory and no gather waits on L2
-    auto xs_pair = [&](int p) -> float2 {
-      const int j = p & 63, r = j & 15;
-      const uint32_t off = xs_chunk((p >> 6) * 4 + (r >> 2), tab_off) + (uint32_t)((j >> 4) * 32 + (r & 3) * 4);
-      const uint32_t h = *reinterpret_cast<const uint32_t*>(smem + off);
-      const uint32_t l = *reinterpret_cast<const uint32_t*>(smem + off + 16);
-      const float x0 = bf16lo_to_f(h) + bf16lo_to_f(l);
-      const float b = bf16hi_to_f(h) + bf16hi_to_f(l);
-      return make_float2(x0, (b - 0.5f * x0) * 1.1547005383792515f);
-    };
+    // the input values come back from the staged splits (xs_pair), so no fp32 copy of x occupies
+    // shared memory and no gather waits on L2
     auto dot8 = [&](const uint4& raw, int c8) {  // 8 columns of one Vt row against x
       const float2 a0 = xs_pair(4 * c8), a1 = xs_pair(4 * c8 + 1), a2 = xs_pair(4 * c8 + 2), a3 = xs_pair(4 * c8 + 3);
       return a0.x * h2f(raw.x & 0xffffu) + a0.y * h2f(raw.x >> 16) + a1.x * h2f(raw.y & 0xffffu) +
@@ -669,6 +675,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       redu[33] = 0u;
       s_lr[HX_LR_FLAG] = 0.f;
     }
+    if (lane < 16) s_ks[lane] = 0.f;
     const int w = blockIdx.x * HX_STREAM + warp;
     const bool streamer = w < P.W;
     const int u0 = streamer ? unit_begin(P, w) : 0;
@@ -709,6 +716,7 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
     const int sh = FULL ? 16 * (q & 1) : 0;
     uint4 cw[4][2];         // code bytes of the unit being consumed / refilled: [segment][row g, g+8]
     uint32_t sa[4], sb[4];  // the next unit's scale words: [segment]
+    uint32_t nko0 = 0u, nko1 = 0u;  // the next unit's kink range
     auto load_codes = [&](int s) {
       if (FULL || nc * HX_UB + 64 * s + 16 * q < NP) {
         cw[s][0] = ldg_stream_u4(pa + 64 * s);
@@ -719,6 +727,12 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
       }
     };
     auto load_scales = [&]() {
+      if (P.ukink) {
+        const StripInfo si = strip_info<NMAT>(P, ns);
+        const uint32_t* kof = J.mat[si.m0 + nm].unit_kink_off + (size_t)(si.rbase / 16) * P.GU + nc;
+        nko0 = __ldg(kof);
+        nko1 = __ldg(kof + 1);
+      }
       if (FULL) {
         const uint4 x = ldg_stream_u4(qa), y = ldg_stream_u4(qb);
         sa[0] = x.x, sa[1] = x.y, sa[2] = x.z, sa[3] = x.w;
@@ -879,6 +893,15 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
       }
       const bool more = u + 1 < u1;
+      // this unit's kink entries (range known since the previous unit) go into flight
+      const uint32_t ko0 = nko0, ko1 = nko1;
+      uint2 ke0 = make_uint2(0u, 0u), ke1 = make_uint2(0u, 0u);
+      if (P.ukink && ko0 + lane < ko1) {
+        const int km = (NMAT == 2) ? cur_m : strip_info<NMAT>(P, cur_s).m0;
+        const uint2* kent = reinterpret_cast<const uint2*>(J.mat[km].unit_kinks) + ko0 + lane;
+        ke0 = __ldg(kent);
+        if (ko0 + 32u + lane < ko1) ke1 = __ldg(kent + 32);
+      }
       // this unit's scales; the next unit's scales go into flight
       uint32_t swa[4], swb[4];
 #pragma unroll
@@ -895,6 +918,49 @@ __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_const
         if (more) load_codes(s);  // refill this segment's registers with the next unit
         rg_sum = fmaf(h2f((uint16_t)(swa[s] >> sh)), rg, rg_sum);
         rh_sum = fmaf(h2f((uint16_t)(swb[s] >> sh)), rh, rh_sum);
+      }
+      if (P.ukink) {
+        // the unit's kinks, sorted by row: a segmented scan per row, one writer per row
+        auto kink_set = [&](uint2 e, bool valid) {
+          const int col = (int)(e.x & 0xffffu), row = (int)(e.x >> 16) & 15;
+          const bool ok = valid && col < C;
+          float v = 0.f;
+          if (ok) {
+            const float2 xp = xs_pair(col >> 1);
+            v = __uint_as_float(e.y) * ((col & 1) ? xp.y : xp.x);
+          }
+          if (valid && !ok) raise_flag(GSDLQ_FLAG_BAD_KINK);
+          const int key = valid ? row : 64 + lane;
+#pragma unroll
+          for (int d = 1; d < 32; d <<= 1) {
+            const float vu = __shfl_up_sync(0xffffffffu, v, d);
+            const int ku = __shfl_up_sync(0xffffffffu, key, d);
+            if (lane >= d && ku == key) v += vu;
+          }
+          const int kn = __shfl_down_sync(0xffffffffu, key, 1);
+          if (valid && (lane == 31 || kn != key)) s_ks[row] += v;
+          __syncwarp();
+        };
+        const uint32_t n = ko1 - ko0;
+        if (n > 0u) {
+          kink_set(ke0, lane < n);
+          if (n > 32u) kink_set(ke1, lane + 32u < n);
+          if (n > 64u) {  // rare: units with more than 64 kinks load the rest here
+            const int km = (NMAT == 2) ? cur_m : strip_info<NMAT>(P, cur_s).m0;
+            const uint2* kent = reinterpret_cast<const uint2*>(J.mat[km].unit_kinks) + ko0;
+            for (uint32_t b0 = 64u; b0 < n; b0 += 32u) {
+              const bool valid = b0 + lane < n;
+              kink_set(valid ? __ldg(kent + b0 + lane) : make_uint2(0u, 0u), valid);
+            }
+          }
+          if (q == 0) {
+            rg_sum += s_ks[gl];
+            rh_sum += s_ks[gl + 8];
+          }
+          __syncwarp();
+          if (lane < 16) s_ks[lane] = 0.f;
+          __syncwarp();
+        }
       }
       if (NMAT == 1 || cur_m == 0) {
         acc[0][0] += rg_sum;
@@ -1004,6 +1070,12 @@ static int hexmv_plan(HexmvParams& P) {
   const int helpers = grid * HX_HELP;
   P.lr_chunks = (C / 8 + helpers - 1) / helpers;
   P.ovf_bytes = std::max(0, P.GU * 16 - 256) * 128;
+  // per-unit kink lists are used when every matrix has them (8-byte entries)
+  P.ukink = 1;
+  for (int m = 0; m < J.n_mat; ++m) {
+    const gsdlq_hexmat_t& M = J.mat[m];
+    if (!M.unit_kink_off || !M.unit_kinks || (reinterpret_cast<uintptr_t>(M.unit_kinks) & 7u)) P.ukink = 0;
+  }
   // shared-memory limit: the table region plus the activation-split overflow chunks
   if (hx_dyn_smem(P.ovf_bytes) > 227 * 1024)
     return GSDLQ_ERR_UNSUPPORTED;
@@ -1188,6 +1260,112 @@ extern "C" int gsdlq_hex2d_matvec(const float* x, const uint8_t* codes, const ui
     ws.bytes = need;
   }
   return hexmv_launch(P, ws.p, ws.bytes, static_cast<cudaStream_t>(stream));
+}
+
+// ---- per-unit kink lists ------------------------------------------------------------------
+// Unit (strip s, column block c) holds the kinks of rows 16s .. 16s+15 with columns in
+// [512c, 512c + 512), rows then columns ascending (the CSR order within each row); a column
+// past the last block (an invalid kink) is kept in the last block, where the kernel flags it.
+namespace gsdlq {
+__device__ __forceinline__ void unit_row_range(const uint32_t* rp, const uint16_t* kc, int row, int c, int GU,
+                                               uint32_t& a, uint32_t& b) {
+  const uint32_t e0 = rp[row], e1 = max(rp[row + 1], e0);
+  // first kink with col >= 512c, and with col >= 512(c+1) (the last block takes the rest)
+  auto lower = [&](uint32_t v) {
+    uint32_t lo = e0, hi = e1;
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if ((uint32_t)kc[mid] < v) lo = mid + 1;
+      else hi = mid;
+    }
+    return lo;
+  };
+  a = c == 0 ? e0 : lower((uint32_t)c * HX_UB * 2);
+  b = c == GU - 1 ? e1 : lower((uint32_t)(c + 1) * HX_UB * 2);
+}
+
+__global__ void unit_kink_count(const uint32_t* rp, const uint16_t* kc, int rows, int GU, int n_units, uint32_t* cnt) {
+  const int u = blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= n_units) return;
+  const int s = u / GU, c = u - s * GU;
+  uint32_t n = 0u;
+  for (int r = s * 16; r < min(rows, s * 16 + 16); ++r) {
+    uint32_t a, b;
+    unit_row_range(rp, kc, r, c, GU, a, b);
+    n += b > a ? b - a : 0u;
+  }
+  cnt[u] = n;
+}
+
+// exclusive prefix sum of cnt[0..n) into off[0..n] (one CTA; load-time only)
+__global__ void unit_kink_scan(const uint32_t* cnt, int n, uint32_t* off) {
+  __shared__ uint32_t carry;
+  __shared__ uint32_t wsum[32];
+  if (threadIdx.x == 0) carry = 0u;
+  __syncthreads();
+  for (int base = 0; base < n; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    uint32_t v = i < n ? cnt[i] : 0u;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t x = v;
+    for (int d = 1; d < 32; d <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, d);
+      if (lane >= d) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t t = lane < (int)(blockDim.x >> 5) ? wsum[lane] : 0u;
+      for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, t, d);
+        if (lane >= d) t += y;
+      }
+      wsum[lane] = t;
+    }
+    __syncthreads();
+    const uint32_t pre = carry + (warp > 0 ? wsum[warp - 1] : 0u) + x - v;
+    if (i < n) off[i] = pre;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = pre + v;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) off[n] = carry;
+}
+
+__global__ void unit_kink_fill(const uint32_t* rp, const uint16_t* kc, const float* kd, int rows, int GU, int n_units,
+                               const uint32_t* off, uint2* ent) {
+  const int u = blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= n_units) return;
+  const int s = u / GU, c = u - s * GU;
+  uint32_t o = off[u];
+  for (int r = s * 16; r < min(rows, s * 16 + 16); ++r) {
+    uint32_t a, b;
+    unit_row_range(rp, kc, r, c, GU, a, b);
+    for (uint32_t e = a; e < b; ++e) ent[o++] = make_uint2((uint32_t)kc[e] | ((uint32_t)(r - s * 16) << 16), __float_as_uint(kd[e]));
+  }
+}
+}  // namespace gsdlq
+
+extern "C" int gsdlq_unit_kinks(const uint32_t* row_ptr, const uint16_t* kink_cols, const float* kink_deltas, int rows,
+                                int cols, uint32_t* unit_kink_off, uint32_t* unit_kinks, gsdlq_stream_t stream) {
+  if (!row_ptr || !unit_kink_off || rows <= 0 || cols <= 0 || cols % 64 != 0) return GSDLQ_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(unit_kinks) & 7u) return GSDLQ_ERR_INVALID;
+  const int GU = (cols / 64 + 7) / 8;
+  const int n_units = ((rows + 15) / 16) * GU;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the counts go to unit_kink_off + 1 .. n (shifted), then the scan writes offsets in place
+  uint32_t* cnt = unit_kink_off + 1;
+  const int tb = 256, nb = (n_units + tb - 1) / tb;
+  unit_kink_count<<<nb, tb, 0, s>>>(row_ptr, kink_cols, rows, GU, n_units, cnt);
+  GSDLQ_CUDA_CHECK_LAUNCH();
+  unit_kink_scan<<<1, 1024, 0, s>>>(cnt, n_units, unit_kink_off);
+  GSDLQ_CUDA_CHECK_LAUNCH();
+  if (unit_kinks && kink_cols && kink_deltas) {
+    unit_kink_fill<<<nb, tb, 0, s>>>(row_ptr, kink_cols, kink_deltas, rows, GU, n_units, unit_kink_off,
+                                     reinterpret_cast<uint2*>(unit_kinks));
+    GSDLQ_CUDA_CHECK_LAUNCH();
+  }
+  return GSDLQ_OK;
 }
 
 // ---- allocation-free matvec ------------------------------------------------------------

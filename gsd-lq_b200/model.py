@@ -75,7 +75,7 @@ class DevicePacked:
 
 class GSDLQModel:
     def __init__(self, source, rope_interleaved: int = 1, device=None, max_seq: int = MAX_SEQ_LEN,
-                 use_graph: bool = True, verbose: bool = False, tp=None):
+                 use_graph: bool = True, verbose: bool = False, tp=None, unit_kinks: bool = False):
         t0 = time.time()
         if not torch.cuda.is_available():
             raise RuntimeError("GSDLQModel needs a CUDA device (there is no CPU path)")
@@ -90,6 +90,7 @@ class GSDLQModel:
         self.max_seq = max_seq
         self.use_graph = use_graph
         self.tp = tp
+        self.unit_kinks = unit_kinks
         if isinstance(source, str):
             source = read_gsd2(source)
         self._load(source)
@@ -131,6 +132,10 @@ class GSDLQModel:
             self.embed = torch.from_numpy(np.ascontiguousarray(src.dense["token_embd.weight"])).to(dev)
             self.norms = {k: torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32)).to(dev)
                           for k, v in src.dense.items() if k != "token_embd.weight"}
+        if self.unit_kinks:
+            # kinks regrouped per work unit: the fused linear applies them in its streaming loop
+            for h in self.hex.values():
+                h.build_unit_kinks()
         H, Lc = self.hidden, self.n_layers
         hd, kvl, hl = self.head_dim, self.n_kv_local, self.n_heads_local
         f32 = dict(dtype=torch.float32, device=dev)

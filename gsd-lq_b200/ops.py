@@ -64,8 +64,25 @@ class DeviceHex:
                 n += v.numel() * v.element_size()
         return n
 
+    def build_unit_kinks(self):
+        """Regroup the CSR kinks per 16-row x 512-column work unit (gsdlq_unit_kinks); the fused
+        linear then applies them in its streaming loop.  Keeps the CSR arrays (the drop-in path)."""
+        gu = (self.cols // 64 + 7) // 8
+        n_units = ((self.rows + 15) // 16) * gu
+        dev = self.codes.device
+        self.unit_kink_off = torch.zeros(n_units + 1, dtype=torch.int32, device=dev)
+        self.unit_kinks = torch.zeros(max(1, 2 * self.nnz), dtype=torch.int32, device=dev)
+        L.check(_lib().gsdlq_unit_kinks(ptr(self.row_ptr), ptr(self.kink_cols), ptr(self.kink_deltas), self.rows,
+                                        self.cols, ptr(self.unit_kink_off), ptr(self.unit_kinks), stream_handle()),
+                "gsdlq_unit_kinks")
+        return self
+
     def desc(self) -> L.HexMat:
-        return L.HexMat(codes=self.codes.data_ptr(), scales=self.scales.data_ptr(),
+        uko = getattr(self, "unit_kink_off", None)
+        uk = getattr(self, "unit_kinks", None)
+        return L.HexMat(unit_kink_off=uko.data_ptr() if uko is not None else None,
+                        unit_kinks=uk.data_ptr() if uk is not None else None,
+                        codes=self.codes.data_ptr(), scales=self.scales.data_ptr(),
                         U=self.U.data_ptr() if self.U is not None else None,
                         S=self.S.data_ptr() if self.S is not None else None,
                         Vt=self.Vt.data_ptr() if self.Vt is not None else None,

@@ -141,6 +141,12 @@ typedef struct gsdlq_hexmat {
   const uint16_t *kink_cols;  /* [nnz]                                  */
   const float *kink_deltas;   /* [nnz]                                  */
   int rows, cols, k_dim, radius;
+  /* Optional (gsdlq_linear only; NULL = use the CSR arrays above): the same kinks regrouped
+   * per work unit of 16 rows x 512 columns, built by gsdlq_unit_kinks.  unit_kink_off has
+   * ceil(rows/16) * ceil(cols/512) + 1 offsets; entry i of unit_kinks is two words
+   * (col | row_in_strip << 16, fp32 delta bits), rows then columns ascending within a unit. */
+  const uint32_t *unit_kink_off;
+  const uint32_t *unit_kinks;
 } gsdlq_hexmat_t;
 
 #define GSDLQ_EPI_STORE 0   /* y[m][r] = W_m x                                            */
@@ -192,6 +198,14 @@ int gsdlq_linear_ws_size(const gsdlq_linear_job_t *job, size_t *bytes);
  * distinct workspaces. */
 int gsdlq_linear(const gsdlq_linear_job_t *job, void *workspace, size_t workspace_bytes,
                  gsdlq_stream_t stream);
+
+/* Regroup a packed linear's CSR kinks into the per-unit lists of gsdlq_hexmat_t (device
+ * pointers).  unit_kink_off: ceil(rows/16) * ceil(cols/512) + 1 words; unit_kinks: 2 * nnz words.
+ * Engine layout with no reference counterpart: the fused linear then applies the kinks of each
+ * 16 x 512 work unit in the streaming loop instead of in separate per-row passes. */
+int gsdlq_unit_kinks(const uint32_t *row_ptr, const uint16_t *kink_cols, const float *kink_deltas,
+                     int rows, int cols, uint32_t *unit_kink_off, uint32_t *unit_kinks,
+                     gsdlq_stream_t stream);
 
 /* Size of the library's fixed device scratch array used by gsdlq_hex2d_matvec_noalloc. */
 #define GSDLQ_NOALLOC_WS_BYTES (4u << 20)

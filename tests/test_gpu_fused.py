@@ -53,11 +53,21 @@ def rms(restated, x, w, eps=1e-5):
     return o
 
 
+def hexes(ops, ts, uk):
+    """Device copies of packed linears; uk: with per-unit kink lists (the engine layout)."""
+    hs = [ops.DeviceHex(t) for t in ts]
+    if uk:
+        for h in hs:
+            h.build_unit_kinks()
+    return hs
+
+
+@pytest.mark.parametrize("uk", [False, True])
 @pytest.mark.parametrize("rows,cols", [(512, 1024), (32768, 4096), (151936, 1536)])
-def test_rmsnorm_store_argmax(env, restated, oracle_mod, rng, rows, cols):
+def test_rmsnorm_store_argmax(env, restated, oracle_mod, rng, rows, cols, uk):
     ops, L = env
     t = rand_hex(rng, rows, cols, k=16, nnz=4)
-    h = ops.DeviceHex(t)
+    h, = hexes(ops, [t], uk)
     x = rng.standard_normal(cols).astype(np.float32)
     w = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
     y = torch.zeros(rows, device="cuda")
@@ -90,14 +100,15 @@ def test_plain_resid(env, restated, rng):
     assert rel_err(res.cpu().numpy(), yr) < MATVEC_TOL
 
 
+@pytest.mark.parametrize("uk", [False, True])
 @pytest.mark.parametrize("rows,cols", [(14336, 4096), (8960, 1536), (512, 256)])
-def test_rmsnorm_swiglu(env, restated, rng, rows, cols):
+def test_rmsnorm_swiglu(env, restated, rng, rows, cols, uk):
     ops, L = env
     tg, tu = rand_hex(rng, rows, cols, k=16, nnz=4), rand_hex(rng, rows, cols, k=16, nnz=4)
     x = rng.standard_normal(cols).astype(np.float32)
     w = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
     hout = torch.zeros(rows, device="cuda")
-    j = make_job(L, [ops.DeviceHex(tg), ops.DeviceHex(tu)], L.IN_RMSNORM, x=dev(x), norm=dev(w),
+    j = make_job(L, hexes(ops, [tg, tu], uk), L.IN_RMSNORM, x=dev(x), norm=dev(w),
                  epilogue=L.EPI_SWIGLU, ys=(hout,))
     ws = ops.linear_workspace(j)
     ops.linear(j, ws)
@@ -110,8 +121,9 @@ def test_rmsnorm_swiglu(env, restated, rng, rows, cols):
     assert int(ws.abs().sum().item()) == 0
 
 
+@pytest.mark.parametrize("uk", [False, True])
 @pytest.mark.parametrize("nh,nkv,hd,H", [(32, 8, 128, 4096), (12, 2, 128, 1536), (32, 32, 64, 2048)])
-def test_embed_qkv_rope_kv(env, restated, rng, nh, nkv, hd, H):
+def test_embed_qkv_rope_kv(env, restated, rng, nh, nkv, hd, H, uk):
     ops, L = env
     V, S, layer = 1000, 128, 1
     tq = rand_hex(rng, nh * hd, H, k=16, nnz=4)
@@ -127,7 +139,7 @@ def test_embed_qkv_rope_kv(env, restated, rng, nh, nkv, hd, H):
     state = torch.tensor([777, 0], dtype=torch.int32, device="cuda")
     cs = torch.from_numpy(ops.rope_table(S, hd, 1e6)).cuda()
     embd = dev(emb.view(np.int16))
-    j = make_job(L, [ops.DeviceHex(tq), ops.DeviceHex(tk), ops.DeviceHex(tv)], L.IN_EMBED, norm=dev(w),
+    j = make_job(L, hexes(ops, [tq, tk, tv], uk), L.IN_EMBED, norm=dev(w),
                  epilogue=L.EPI_ROPE_KV, ys=(q, kout, vout), embed=embd.data_ptr(), token=state.data_ptr(),
                  vocab=V, x_out=xo.data_ptr(), k_cache=kd.data_ptr(), v_cache=vd.data_ptr(),
                  pos=state.data_ptr() + 4, rope_cs=cs.data_ptr(), layer=layer, max_seq=S, head_dim=hd,
@@ -158,23 +170,26 @@ def test_flags_bad_kink_and_bad_pos(env, restated, rng):
     """Host-made bad inputs: the kernels skip the access and raise a flag instead of faulting."""
     ops, L = env
     t = rand_hex(rng, 64, 256, k=0, nnz=2)
-    h = ops.DeviceHex(t)
-    bad = t.kink_cols.copy()
-    bad[3] = 300  # column >= cols
-    h.kink_cols = dev(bad.view(np.int16))
     x = rng.standard_normal(256).astype(np.float32)
-    y = torch.zeros(64, device="cuda")
-    j = make_job(L, [h], L.IN_PLAIN, x=dev(x), epilogue=L.EPI_STORE, ys=(y,))
-    ops.linear(j, ops.linear_workspace(j))
-    flags = L.device_flags()
-    assert flags & 0x2, L.flag_names(flags)
     t2 = rand_hex(np.random.default_rng(0), 64, 256, k=0, nnz=2)
     t2.kink_cols[:] = t.kink_cols
     t2.codes[:] = t.codes
     t2.scales[:] = t.scales
     t2.kink_deltas[:] = t.kink_deltas
     t2.kink_deltas[3] = 0.0  # the skipped kink contributes nothing
-    assert rel_err(y.cpu().numpy(), oracle_matvec(restated, x, t2)) < MATVEC_TOL
+    for uk in (False, True):  # CSR kinks (helper warps) and per-unit lists (streaming warps)
+        h = ops.DeviceHex(t)
+        bad = t.kink_cols.copy()
+        bad[3] = 300  # column >= cols
+        h.kink_cols = dev(bad.view(np.int16))
+        if uk:
+            h.build_unit_kinks()
+        y = torch.zeros(64, device="cuda")
+        j = make_job(L, [h], L.IN_PLAIN, x=dev(x), epilogue=L.EPI_STORE, ys=(y,))
+        ops.linear(j, ops.linear_workspace(j))
+        flags = L.device_flags()
+        assert flags & 0x2, L.flag_names(flags)
+        assert rel_err(y.cpu().numpy(), oracle_matvec(restated, x, t2)) < MATVEC_TOL
     # pos >= max_seq read from device memory: no KV store, flag raised
     tq = rand_hex(rng, 128, 128, k=0, nnz=0)
     tk = rand_hex(rng, 64, 128, k=0, nnz=0)

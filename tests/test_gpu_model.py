@@ -21,12 +21,13 @@ LOGIT_TOL = 1e-2
 
 
 @pytest.mark.parametrize("mode", ["precision", "turbo"])
-@pytest.mark.parametrize("use_graph", [True, False])
-def test_golden_tiny(cuda_lib, mode, use_graph):
+@pytest.mark.parametrize("use_graph,unit_kinks", [(True, False), (False, False), (True, True)])
+def test_golden_tiny(cuda_lib, mode, use_graph, unit_kinks):
     from gsdlq_b200.model import GSDLQModel
     import gsdlq_b200._lib as L
     g = np.load(os.path.join(GOLDEN, f"tiny_{mode}_ref.npz"))
-    m = GSDLQModel(os.path.join(GOLDEN, f"tiny_{mode}.gsd2"), max_seq=64, use_graph=use_graph)
+    m = GSDLQModel(os.path.join(GOLDEN, f"tiny_{mode}.gsd2"), max_seq=64, use_graph=use_graph,
+                   unit_kinks=unit_kinks)
     for pos, tok in enumerate(g["tokens"]):
         lg = m.forward_token(int(tok), pos)
         err = float(np.max(np.abs(lg - g["logits"][pos])))
