@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override n_layers (debug only; not a bench number)")
+    ap.add_argument("--step", choices=["fused", "per-op"], default="per-op",
+                    help="one persistent launch per token (fused) or the per-operation launches in CUDA graphs")
     return ap.parse_args()
 
 
@@ -230,7 +232,7 @@ def run_ours(args):
         from gsdlq_b200.tp import TensorParallel
         tp = TensorParallel(rank, world)
     cfg, dm, pack_s = build_model(args, world, rank, device)
-    model = GSDLQModel(dm, device=device, tp=tp)
+    model = GSDLQModel(dm, device=device, tp=tp, fused_step=args.step == "fused")
     host_model = None
     if rank == 0 and not args.no_cpu_baseline and world == 1:
         import gsdlq_b200.packer as P
@@ -323,7 +325,9 @@ def run_ours(args):
         kv = (model.k_cache.cpu().numpy().view(np.uint16), model.v_cache.cpu().numpy().view(np.uint16))
         cpu = cpu_reference_sample(host_model, kv=kv, pos=P0)
 
-    launches_per_step = 5 * model.n_layers + 2 + (2 * model.n_layers + 1 if world > 1 else 0)
+    # one persistent launch per step when the decode kernel covers the shape, else the per-op launches
+    launches_per_step = (1 if model.fused_step else
+                         5 * model.n_layers + 2 + (2 * model.n_layers + 1 if world > 1 else 0))
     if rank == 0:
         line = {
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -334,6 +338,7 @@ def run_ours(args):
                                    f"{P0}..{model.max_seq - 1} (wrapping), random-init N(0,0.02^2) packed on the GPU",
                        "model": args.model, "mode": args.mode, "prompt": P0, "global_batch": 1,
                        "parallelism": f"tp{world}", "avg_bpw": round(model.avg_bpw, 4),
+                       "step": "fused" if model.fused_step else "per-op",
                        "l2": "inputs larger than L2: every step streams all packed weights "
                              f"({bytes_tok / 1e9:.2f} GB)",
                        "n_layers": model.n_layers},

@@ -44,6 +44,15 @@ class AttnJob(ctypes.Structure):
                 ("sm_scale", f32), ("block_table", vp), ("page_size", i32), ("partial", vp), ("workspace", vp)]
 
 
+class DecodeLayer(ctypes.Structure):
+    _fields_ = [("qkv", LinearJob), ("attn", AttnJob), ("o", LinearJob), ("gate_up", LinearJob), ("down", LinearJob)]
+
+
+class DecodeDesc(ctypes.Structure):
+    _fields_ = [("n_layers", i32), ("layers", ctypes.POINTER(DecodeLayer)), ("head", LinearJob),
+                ("argmax_key", vp), ("token", vp), ("pos", vp), ("step", vp), ("out_ids", vp), ("max_out", i32)]
+
+
 SIGNATURES = {
     "gsdlq_status_string": ([i32], ctypes.c_char_p),
     "gsdlq_last_cuda_error": ([], i32),
@@ -68,6 +77,9 @@ SIGNATURES = {
     "gsdlq_rope_table": ([vp, i32, i32, f32], i32),
     "gsdlq_greedy_advance": ([vp, vp, vp, vp, vp, i32, vp], i32),
     "gsdlq_unit_kinks": ([vp, vp, vp, i32, i32, vp, vp, vp], i32),
+    "gsdlq_decode_plan_create": ([ctypes.POINTER(DecodeDesc), ctypes.POINTER(vp)], i32),
+    "gsdlq_decode_step": ([vp, vp], i32),
+    "gsdlq_decode_plan_destroy": ([vp], i32),
 }
 
 

@@ -124,6 +124,107 @@ __device__ __forceinline__ bool wait_counter_eq(const unsigned int* ctr, unsigne
   }
 }
 
+__device__ __forceinline__ void red_add_release(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded spin until *ctr >= target (acquire), for the persistent decode kernel's phase
+// dependencies.  Gives up after 1 s of %globaltimer, or at once when *abort is set: on giving
+// up it raises GSDLQ_FLAG_TIMEOUT and sets *abort, so that every later wait of the launch
+// returns at once and the kernel ends with the flag raised instead of hanging.
+__device__ __forceinline__ void wait_geq_abort(const unsigned* ctr, unsigned target, unsigned* abort) {
+  unsigned long long t0 = 0ull;
+  for (int it = 0;; ++it) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return;
+    if (*reinterpret_cast<volatile unsigned*>(abort) != 0u) return;
+    unsigned long long t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (it == 0) t0 = t1;
+    if (t1 - t0 > 1000000000ull) {
+      raise_flag(GSDLQ_FLAG_TIMEOUT);
+      atomicExch(abort, 1u);
+      return;
+    }
+    __nanosleep(20);
+  }
+}
+
+// wait_counter_eq (1 s bound) that also returns at once when *abort (if given) is set, and sets it
+// when it gives up
+__device__ __forceinline__ void wait_eq_abort(const unsigned* ctr, unsigned target, unsigned* abort) {
+  if (abort == nullptr) {
+    wait_counter_eq(ctr, target, 1000000000ull);
+    return;
+  }
+  unsigned long long t0 = 0ull;
+  for (int it = 0;; ++it) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v == target) return;
+    if (*reinterpret_cast<volatile unsigned*>(abort) != 0u) return;
+    unsigned long long t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (it == 0) t0 = t1;
+    if (t1 - t0 > 1000000000ull) {
+      raise_flag(GSDLQ_FLAG_TIMEOUT);
+      atomicExch(abort, 1u);
+      return;
+    }
+    __nanosleep(64);
+  }
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+// ---- mbarrier + TMA (bulk tensor copies into this CTA's shared memory; no multicast) ----------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+// make initialised barriers visible to the asynchronous (TMA) proxy
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+// arrive once and add `bytes` to the transaction count of the current phase
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0u;
+}
+// Bounded wait for the phase of `bar` with the given parity: false (flag raised) after 1 s.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  unsigned long long t0, t1;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (!mbar_try_wait(bar, parity)) {
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (t1 - t0 > 1000000000ull) {
+      raise_flag(GSDLQ_FLAG_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+// 2-D tiled copy of one box at element coordinates (x, y) of `tmap` (a tensor map in parameter,
+// constant or global memory) into shared memory at `dst`, completing on `bar`.  x * element size
+// must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
 // Monotone float -> uint32 map (larger float -> larger key).
 __device__ __forceinline__ uint32_t ordered_key(float v) {
   const uint32_t b = __float_as_uint(v);

@@ -23,6 +23,7 @@ position are read from device memory, so replays need no re-capture.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 import time
 
@@ -75,7 +76,8 @@ class DevicePacked:
 
 class GSDLQModel:
     def __init__(self, source, rope_interleaved: int = 1, device=None, max_seq: int = MAX_SEQ_LEN,
-                 use_graph: bool = True, verbose: bool = False, tp=None, unit_kinks: bool = False):
+                 use_graph: bool = True, verbose: bool = False, tp=None, unit_kinks: bool = False,
+                 fused_step: bool = False):
         t0 = time.time()
         if not torch.cuda.is_available():
             raise RuntimeError("GSDLQModel needs a CUDA device (there is no CPU path)")
@@ -91,6 +93,8 @@ class GSDLQModel:
         self.use_graph = use_graph
         self.tp = tp
         self.unit_kinks = unit_kinks
+        self._want_fused = fused_step and tp is None
+        self._plans: dict = {}
         if isinstance(source, str):
             source = read_gsd2(source)
         self._load(source)
@@ -154,6 +158,8 @@ class GSDLQModel:
         self.attn_partial = torch.zeros(pb // 4 + 1, **f32)
         self.attn_ws = torch.zeros(wb // 4 + 1, dtype=torch.int32, device=dev)
         self._build_jobs()
+        if self._want_fused:
+            self._build_plans()
         torch.cuda.synchronize(dev)
         self.vram_used_mb = self._bytes_resident() / (1024 * 1024)
 
@@ -242,6 +248,38 @@ class GSDLQModel:
     def linear(self, job):
         ops.linear(job, self.ws_of[id(job)])
 
+    def _build_plans(self):
+        """The whole step as one persistent launch (gsdlq_decode_step), with and without the head.
+
+        Shapes the decode kernel is not built for keep the per-operation launches."""
+        lib = L.load()
+        layers = (L.DecodeLayer * self.n_layers)()
+        for i, (qkv, att, o, gu, dn) in enumerate(self.layer_jobs):
+            layers[i] = L.DecodeLayer(qkv=qkv, attn=att, o=o, gate_up=gu, down=dn)
+        st = self.state.data_ptr()
+        for name, head in (("full", self.head_job), ("layers", L.LinearJob())):
+            d = L.DecodeDesc(n_layers=self.n_layers, layers=layers, head=head,
+                             argmax_key=self.key.data_ptr(), token=st, pos=st + 4, step=st + 8,
+                             out_ids=self.out_ids.data_ptr(), max_out=self.out_ids.numel())
+            plan = ctypes.c_void_p()
+            status = lib.gsdlq_decode_plan_create(ctypes.byref(d), ctypes.byref(plan))
+            if status == -3:  # GSDLQ_ERR_UNSUPPORTED: keep the per-operation launches
+                self._destroy_plans()
+                return
+            L.check(status, "gsdlq_decode_plan_create")
+            self._plans[name] = plan
+
+    def _destroy_plans(self):
+        lib = L.load()
+        for plan in self._plans.values():
+            lib.gsdlq_decode_plan_destroy(plan)
+        self._plans = {}
+
+    @property
+    def fused_step(self) -> bool:
+        """True when each step runs as one persistent launch (gsdlq_decode_step)."""
+        return bool(self._plans)
+
     # ------------------------------------------------------------------ step
     def _run_layers(self):
         allreduce = self.tp.allreduce if self.tp is not None else None
@@ -286,6 +324,10 @@ class GSDLQModel:
 
     def step(self, with_head: bool = True):
         """One decode step on the device (token/pos taken from self.state)."""
+        if self._plans:
+            plan = self._plans["full" if with_head else "layers"]
+            L.check(L.load().gsdlq_decode_step(plan, ops.stream_handle()), "gsdlq_decode_step")
+            return
         if self.use_graph:
             self._graph("layers", self._run_layers).replay()
             if with_head:
@@ -356,6 +398,7 @@ class GSDLQModel:
 
     def release(self):
         self._graphs.clear()
+        self._destroy_plans()
         for k in ("hex", "embed", "norms", "k_cache", "v_cache", "_arena"):
             if hasattr(self, k):
                 delattr(self, k)

@@ -273,6 +273,50 @@ int gsdlq_greedy_advance(unsigned long long *argmax_key, int *token, int *pos, i
  * (gsd_lq_cpu_engine.c:215-218) so that rotations match it bit for bit. */
 int gsdlq_rope_table(float *table, int max_seq, int head_dim, float rope_theta);
 
+/* ---- The whole decode step in one launch ----------------------------------------------------
+ * Engine-level entry point with no single reference counterpart: the reference's
+ * Model.forward_token (run_gpu_native_chat.py:921-984) walks the layers on the host, one kernel
+ * per operation; this runs the same sequence -- per layer QKV (+RoPE, KV append), attention, O
+ * (+residual), gate/up (+SwiGLU), down (+residual), then the LM head with the greedy argmax and
+ * the greedy bookkeeping of gsdlq_greedy_advance -- as one cooperative launch of one CTA per SM
+ * whose phases wait on one another through device counters.
+ *
+ * The jobs are the ones gsdlq_linear / gsdlq_attention take (their workspace fields are ignored:
+ * the plan owns its scratch).  Requirements: every linear has the same stream shape (all with
+ * cols a multiple of 512 and 16-byte aligned scales, or none), the attention shape (head_dim,
+ * n_heads / n_kv_heads) is one the library is built for (128/4, 128/8, 64/4, 32/2), contiguous
+ * KV cache (no block table); otherwise gsdlq_decode_plan_create returns GSDLQ_ERR_UNSUPPORTED and
+ * the caller runs the per-operation launches.  Results equal the per-operation launches' to float
+ * rounding (the attention splits the sequence differently).  Each step first copies the plan's
+ * parameter block into the library's constant memory on `stream`, so the steps of all plans of
+ * one device must not overlap on the GPU (use one stream, or ordered streams). */
+typedef struct gsdlq_decode_layer {
+  gsdlq_linear_job_t qkv;      /* epilogue GSDLQ_EPI_ROPE_KV */
+  gsdlq_attn_job_t attn;
+  gsdlq_linear_job_t o;        /* GSDLQ_EPI_RESID */
+  gsdlq_linear_job_t gate_up;  /* GSDLQ_EPI_SWIGLU */
+  gsdlq_linear_job_t down;     /* GSDLQ_EPI_RESID */
+} gsdlq_decode_layer_t;
+
+typedef struct gsdlq_decode_desc {
+  int n_layers;
+  const gsdlq_decode_layer_t *layers;  /* host array of n_layers */
+  gsdlq_linear_job_t head;             /* GSDLQ_EPI_STORE with argmax_key; n_mat 0: no head
+                                          (a prefill step: layers only, no greedy bookkeeping) */
+  /* greedy bookkeeping after the head (as gsdlq_greedy_advance); argmax_key NULL: none */
+  unsigned long long *argmax_key;
+  int *token, *pos, *step, *out_ids;
+  int max_out;
+} gsdlq_decode_desc_t;
+
+typedef struct gsdlq_decode_plan gsdlq_decode_plan_t;  /* opaque */
+
+/* Plan the step (validates every job, allocates the plan's device scratch). */
+int gsdlq_decode_plan_create(const gsdlq_decode_desc_t *desc, gsdlq_decode_plan_t **plan);
+/* One decode token: a single launch on `stream`. */
+int gsdlq_decode_step(gsdlq_decode_plan_t *plan, gsdlq_stream_t stream);
+int gsdlq_decode_plan_destroy(gsdlq_decode_plan_t *plan);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,13 +21,16 @@ LOGIT_TOL = 1e-2
 
 
 @pytest.mark.parametrize("mode", ["precision", "turbo"])
-@pytest.mark.parametrize("use_graph,unit_kinks", [(True, False), (False, False), (True, True)])
-def test_golden_tiny(cuda_lib, mode, use_graph, unit_kinks):
+@pytest.mark.parametrize("use_graph,unit_kinks,fused", [(True, False, False), (False, False, False),
+                                                        (True, True, False), (True, False, True),
+                                                        (True, True, True)])
+def test_golden_tiny(cuda_lib, mode, use_graph, unit_kinks, fused):
     from gsdlq_b200.model import GSDLQModel
     import gsdlq_b200._lib as L
     g = np.load(os.path.join(GOLDEN, f"tiny_{mode}_ref.npz"))
     m = GSDLQModel(os.path.join(GOLDEN, f"tiny_{mode}.gsd2"), max_seq=64, use_graph=use_graph,
-                   unit_kinks=unit_kinks)
+                   unit_kinks=unit_kinks, fused_step=fused)
+    assert m.fused_step == fused  # the tiny shape (head_dim 32, 2 query heads per kv head) has a decode kernel
     for pos, tok in enumerate(g["tokens"]):
         lg = m.forward_token(int(tok), pos)
         err = float(np.max(np.abs(lg - g["logits"][pos])))
@@ -110,3 +113,38 @@ def test_baseline_shapes_vs_oracle(cuda_lib, name, over, mode, steps, prompt):
     cfg = P.make_config(name, **over)
     worst, ties = _parity(cfg, mode, steps, prompt)
     print(f"{name}: max|dlogit| {worst:.2e}, near-ties {ties}")
+
+
+@pytest.mark.parametrize("name,over,mode", [
+    ("mistral-7b", dict(n_layers=2), "precision"),
+    ("tiny", dict(hidden_size=512, n_heads=8, n_kv_heads=2, head_dim=64, ffn_size=1024), "turbo"),
+])
+def test_fused_step_matches_per_op_launches(cuda_lib, name, over, mode):
+    """The persistent decode kernel (gsdlq_decode_step) against the per-operation launches on the
+    same packed weights: the linears and the KV cache are computed by the same code, only the
+    attention's split of the sequence differs, so logits agree to float rounding and every greedy
+    pick is the same.  Positions run past one attention tile and past one split."""
+    import gsdlq_b200.packer as P
+    import gsdlq_b200._lib as L
+    from gsdlq_b200.model import GSDLQModel
+    cfg = P.make_config(name, **over)
+    dm = P.random_model_cuda(cfg, mode, seed=3, norm_jitter=0.1)
+    a = GSDLQModel(dm, max_seq=256, fused_step=True)
+    b = GSDLQModel(dm, max_seq=256, fused_step=False)
+    assert a.fused_step and not b.fused_step
+    rng = np.random.default_rng(4)
+    toks = rng.integers(0, cfg["vocab_size"], 150).tolist()
+    worst = 0.0
+    for pos, t in enumerate(toks):
+        last = pos % 37 == 0 or pos == len(toks) - 1
+        la = a.forward_token(t, pos, return_logits=last)
+        lb = b.forward_token(t, pos, return_logits=last)
+        if last:
+            worst = max(worst, float(np.max(np.abs(la - lb))))
+            assert int(np.argmax(la)) == int(np.argmax(lb)), pos
+    assert worst < 1e-3, worst
+    # the device-side greedy loop: same generated ids
+    ga = a.generate(toks[:20], 12)
+    gb = b.generate(toks[:20], 12)
+    assert ga == gb
+    assert L.device_flags() == 0
