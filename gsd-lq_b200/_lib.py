@@ -35,13 +35,15 @@ class LinearJob(ctypes.Structure):
                 ("eps", f32), ("embed", vp), ("token", vp), ("vocab", i32), ("x_out", vp), ("epilogue", i32),
                 ("y", vp * 3), ("resid", vp), ("k_cache", vp), ("v_cache", vp), ("pos", vp), ("rope_cs", vp),
                 ("layer", i32), ("max_seq", i32), ("head_dim", i32), ("interleaved", i32),
-                ("argmax_key", vp), ("argmax_index_base", i32)]
+                ("argmax_key", vp), ("argmax_index_base", i32), ("fwd_vt", vp * 3), ("fwd_k", i32 * 3),
+                ("fwd_norm_w", vp), ("fwd_acc", vp), ("lr_forwarded", i32)]
 
 
 class AttnJob(ctypes.Structure):
     _fields_ = [("q", vp), ("k_cache", vp), ("v_cache", vp), ("out", vp), ("pos_dev", vp), ("pos_val", i32),
                 ("layer", i32), ("n_heads", i32), ("n_kv_heads", i32), ("head_dim", i32), ("max_seq", i32),
-                ("sm_scale", f32), ("block_table", vp), ("page_size", i32), ("partial", vp), ("workspace", vp)]
+                ("sm_scale", f32), ("block_table", vp), ("page_size", i32), ("partial", vp), ("workspace", vp),
+                ("fwd_vt", vp), ("fwd_k", i32), ("fwd_acc", vp)]
 
 
 class DecodeLayer(ctypes.Structure):

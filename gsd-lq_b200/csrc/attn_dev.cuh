@@ -216,18 +216,63 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
       for (int g = 0; g < HS; ++g) res[k] += red[(g * GQ + h) * HD + d];
     }
   }
+  // Low-rank forwarding into the next linear (J.fwd_acc): this head group's GQ*HD outputs (ov[k] =
+  // output tid + k * AT_THREADS) against columns kvh*GQ*HD + o of the next Vt rows, summed over
+  // the group into one fixed-point atomic per row.  The K/V buffers are free by then.
+  auto forward = [&](const float (&ov)[NO]) {
+    if (J.fwd_acc == nullptr) return;  // uniform
+    float* fr = reinterpret_cast<float*>(skv);  // [AT_THREADS / 32][fwd_k]
+    const int nk = J.fwd_k;
+    const int n_in = J.n_heads * HD;  // the next linear's columns
+    for (int j0 = 0; j0 < nk; j0 += 16) {
+      float pj[16];
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        float a = 0.f;
+        if (j0 + jj < nk) {
+          const uint16_t* vt = J.fwd_vt + (size_t)(j0 + jj) * n_in + (size_t)kvh * GQ * HD;
+#pragma unroll
+          for (int k = 0; k < NO; ++k) {
+            const int o = tid + k * AT_THREADS;
+            if (o < GQ * HD) a = fmaf(h2f(__ldg(vt + o)), ov[k], a);
+          }
+        }
+        pj[jj] = warp_sum(a);
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) fr[warp * 16 + jj] = pj[jj];
+      }
+      attn_sync<BAR>();
+      if (tid < 16 && j0 + tid < nk) {
+        float a = 0.f;
+        for (int w = 0; w < AT_THREADS / 32; ++w) a += fr[w * 16 + tid];
+        if (!(fabsf(a) < 4194304.f)) {
+          raise_flag(GSDLQ_FLAG_RANGE);
+          a = (a != a) ? 0.f : copysignf(4194304.f, a);
+        }
+        atomicAdd(J.fwd_acc + j0 + tid, (unsigned long long)__float2ll_rn(a * 4294967296.f));
+      }
+      attn_sync<BAR>();
+    }
+  };
   const int nact = min(nsplit, (len + tps - 1) / tps);
   if (nact == 1) {
     // a single split holds the whole sequence: write the output directly
     if (split == 0) {
+      float ov[NO];
 #pragma unroll
       for (int k = 0; k < NO; ++k) {
         const int o = tid + k * AT_THREADS;
+        ov[k] = 0.f;
         if (o < GQ * HD) {
           const float l = s_l[o / HD];
-          J.out[(size_t)kvh * GQ * HD + o] = l > 0.f ? res[k] / l : 0.f;
+          ov[k] = l > 0.f ? res[k] / l : 0.f;
+          J.out[(size_t)kvh * GQ * HD + o] = ov[k];
         }
       }
+      attn_sync<BAR>();  // (the K/V buffers held the token-group reduction until here)
+      forward(ov);
     }
     if (MEGA) {
       if (split == 0) {  // publish the head to the next phase
@@ -302,6 +347,9 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
     cL[tid] = L;
   }
   attn_sync<BAR>();
+  float ov[NO];
+#pragma unroll
+  for (int k = 0; k < NO; ++k) ov[k] = 0.f;
   for (int k0 = 0; k0 < NO; k0 += NB) {
     if (k0 > 0) load_pv(k0);
 #pragma unroll
@@ -314,10 +362,15 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
         for (int sidx = 0; sidx < AT_MAX_SPLITS; ++sidx)
           if (sidx < nact) a += pv[k][sidx] * cw[g][sidx];
         const float L = cL[g];
-        J.out[(size_t)kvh * GQ * HD + o] = (L > 0.f) ? a / L : 0.f;
+        const float r = (L > 0.f) ? a / L : 0.f;
+        J.out[(size_t)kvh * GQ * HD + o] = r;
+#pragma unroll
+        for (int kk = 0; kk < NO; ++kk)
+          if (kk == k0 + k) ov[kk] = r;
       }
     }
   }
+  forward(ov);
   if (tid == 0) J.workspace[kvh] = 0u;
   if (MEGA) {  // publish the head to the next phase
     __threadfence();

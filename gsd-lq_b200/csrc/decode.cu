@@ -45,7 +45,7 @@ struct MkLayer {
 
 struct MkParams {
   HexmvParams lin[MK_KINDS];  // shape records (the layer-specific fields come from layers[])
-  int part_off[MK_KINDS];     // byte offset of the partial slots in a strip workspace
+  int gacc_off[MK_KINDS];     // byte offset of the shared strips' fixed-point sums in a strip workspace
   gsdlq_attn_job_t attn;      // attention (its layer field is replaced per layer)
   int n_layers;
   int with_head;
@@ -109,8 +109,8 @@ struct MkPtrs {
   __device__ __forceinline__ unsigned* cnt() const {
     return reinterpret_cast<unsigned*>(K.ws[(KIND == MK_O || KIND == MK_DN) ? 1 : 0]);
   }
-  __device__ __forceinline__ float* part() const {
-    return reinterpret_cast<float*>(K.ws[(KIND == MK_O || KIND == MK_DN) ? 1 : 0] + K.part_off[KIND]);
+  __device__ __forceinline__ unsigned long long* gacc() const {
+    return reinterpret_cast<unsigned long long*>(K.ws[(KIND == MK_O || KIND == MK_DN) ? 1 : 0] + K.gacc_off[KIND]);
   }
   __device__ __forceinline__ const unsigned* dep() const { return p > 0 ? K.sync + MK_SYNC_PHASE + p - 1 : nullptr; }
   __device__ __forceinline__ unsigned dep_target() const { return dep_t; }
@@ -315,23 +315,27 @@ extern "C" int gsdlq_decode_plan_create(const gsdlq_decode_desc_t* d, gsdlq_deco
   const int epi[MK_KINDS] = {GSDLQ_EPI_ROPE_KV, GSDLQ_EPI_RESID, GSDLQ_EPI_SWIGLU, GSDLQ_EPI_RESID, GSDLQ_EPI_STORE};
   int full = -1, st = GSDLQ_OK;
   size_t ws_need = 0;
-  int ovf_max = 0;
+  int ovf_max = 0, lacc_max = 0;
   for (int k = 0; k < MK_KINDS && st == GSDLQ_OK; ++k) {
     if (k == MK_HEAD && !with_head) break;
     HexmvParams& H = K.lin[k];
     H.job = *tmpl[k];
+    // the decode kernel projects every linear's input itself (no forwarding between phases)
+    H.job.fwd_acc = nullptr;
+    H.job.lr_forwarded = 0;
     if (H.job.epilogue != epi[k]) st = GSDLQ_ERR_INVALID;
     if (st == GSDLQ_OK) st = hexmv_plan(H);
     if (st == GSDLQ_OK) st = hexmv_check_io(H);
     if (st != GSDLQ_OK) break;
-    if ((H.W + HX_STREAM - 1) / HX_STREAM > grid) st = GSDLQ_ERR_UNSUPPORTED;
+    if (H.n_cta > grid) st = GSDLQ_ERR_UNSUPPORTED;
     // the stream mode of every linear must agree: 2 the TMA ring (opt-in), 1 16-byte loads, 0 any
     const int f = hexmv_full(H) ? (hexmv_tma_ok(H) ? 2 : 1) : 0;
     if (full < 0) full = f;
     if (f != full) st = GSDLQ_ERR_UNSUPPORTED;  // one kernel per stream shape
-    ws_need = std::max(ws_need, hexmv_ws_bytes_for(H.n_strips, H.max_seg, H.nmat));
+    ws_need = std::max(ws_need, hexmv_ws_bytes_for(H.n_strips, H.nmat));
     ovf_max = std::max(ovf_max, H.ovf_bytes);
-    K.part_off[k] = (int)((sizeof(unsigned) * (size_t)H.n_strips + 15) & ~size_t(15));
+    lacc_max = std::max(lacc_max, hx_lacc_bytes(H));
+    K.gacc_off[k] = (int)((sizeof(unsigned) * (size_t)H.n_strips + 15) & ~size_t(15));
   }
   if (st == GSDLQ_OK && with_head && d->head.input_mode != GSDLQ_IN_RMSNORM) st = GSDLQ_ERR_UNSUPPORTED;
   if (st == GSDLQ_OK && (l0.o.input_mode != GSDLQ_IN_PLAIN || l0.down.input_mode != GSDLQ_IN_PLAIN ||
@@ -355,6 +359,8 @@ extern "C" int gsdlq_decode_plan_create(const gsdlq_decode_desc_t* d, gsdlq_deco
     for (int j = 0; j < 4 && st == GSDLQ_OK; ++j) {
       HexmvParams H{};
       H.job = *js[j];
+      H.job.fwd_acc = nullptr;
+      H.job.lr_forwarded = 0;
       st = hexmv_plan(H);
       if (st == GSDLQ_OK) st = hexmv_check_io(H);
     }
@@ -407,8 +413,10 @@ extern "C" int gsdlq_decode_plan_create(const gsdlq_decode_desc_t* d, gsdlq_deco
   // dynamic shared memory: the table region, then max(activation overflow, attention groups) (the
   // host sizes for a zero reserved offset, as the stand-alone launch does)
   const size_t attn_b = mk_attn_bytes(hd, gq);
+  // every linear phase's accumulator sits after the largest overflow region (and the ring)
   const size_t ring_b = full == 2 ? (size_t)ovf_max + HX_RING_BYTES : (size_t)ovf_max;
-  P->dyn_smem = hx_dyn_smem(0) + (int)std::max<size_t>(ring_b, attn_b);
+  for (int k = 0; k < MK_KINDS; ++k) K.lin[k].lacc_off = 0x10000 + (int)ring_b;
+  P->dyn_smem = hx_dyn_smem(0) + (int)std::max<size_t>(ring_b + lacc_max, attn_b);
   if (e == cudaSuccess && P->dyn_smem > 227 * 1024) e = cudaErrorInvalidValue;
   if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, P->dyn_smem);
   int per_sm = 0;
@@ -428,6 +436,7 @@ extern "C" int gsdlq_decode_plan_create(const gsdlq_decode_desc_t* d, gsdlq_deco
   K.ws[0] = base + sync_b + ctl_b;
   K.ws[1] = base + sync_b + ctl_b + ws_b;
   K.attn = A0;
+  K.attn.fwd_acc = nullptr;
   K.attn.partial = reinterpret_cast<float*>(base + sync_b + ctl_b + 2 * ws_b);
   K.attn.workspace = reinterpret_cast<unsigned*>(base + sync_b + ctl_b + 2 * ws_b + part_b);
   K.n_layers = L;

@@ -95,14 +95,12 @@ int hexmv_plan(HexmvParams& P) {
   P.UPS = P.nmat * P.GU;
   P.T = (long long)P.n_strips * P.UPS;
   if (P.T >= (1LL << 31)) return GSDLQ_ERR_UNSUPPORTED;  // unit indices are 32-bit in the kernel
-  const int max_w = num_sms() * HX_STREAM;
-  P.W = (int)std::min<long long>(max_w, P.T);
-  P.TW = hx_cumw(P.W);
-  P.w_per_unit = (float)P.W / (float)P.T;
-  // partial slots per strip: consecutive warps' first units are at least 3T/TW apart, so a strip
-  // of UPS units meets at most ceil(UPS * TW / 3T) + 2 warps (empty ranges in between included)
-  P.max_seg = (int)((P.UPS * P.TW + 3 * P.T - 1) / (3 * P.T)) + 2;
-  const int grid = (P.W + HX_STREAM - 1) / HX_STREAM;
+  // one CTA per SM (fewer when there are fewer units); a range of ceil(T / n_cta) units touches at
+  // most ceil(that / UPS) + 1 strips, the rows of each CTA's shared-memory accumulator
+  P.n_cta = (int)std::min<long long>(num_sms(), P.T);
+  const long long upc = (P.T + P.n_cta - 1) / P.n_cta;
+  P.n_local = (int)((upc + P.UPS - 1) / P.UPS) + 1;
+  const int grid = P.n_cta;
   int lr = 0;
   for (int m = 0; m < 4; ++m) P.lr_off[m] = 0;
   for (int m = 0; m < J.n_mat; ++m) {
@@ -119,9 +117,11 @@ int hexmv_plan(HexmvParams& P) {
     const gsdlq_hexmat_t& M = J.mat[m];
     if (!M.unit_kink_off || !M.unit_kinks || (reinterpret_cast<uintptr_t>(M.unit_kinks) & 7u)) P.ukink = 0;
   }
-  // shared-memory limit: the table region plus the activation-split overflow chunks
-  if (hx_dyn_smem(P.ovf_bytes) > 227 * 1024)
+  // shared-memory limits: the accumulator (16 KB), and the table region, the activation-split
+  // overflow chunks and the accumulator together
+  if (hx_lacc_bytes(P) > 16 * 1024 || hx_dyn_smem(P.ovf_bytes) + hx_lacc_bytes(P) > 227 * 1024)
     return GSDLQ_ERR_UNSUPPORTED;
+  P.lacc_off = 0x10000 + P.ovf_bytes;  // (after the TMA ring when a launch uses it)
   return GSDLQ_OK;
 }
 
@@ -135,7 +135,7 @@ bool hexmv_full(const HexmvParams& P) {
 
 template <int EPI, bool FULL, bool TMA>
 static int hexmv_launch_t(const HexmvParams& P, const HxMaps& T, cudaStream_t s) {
-  const int dyn = TMA ? hx_dyn_smem_tma(P.ovf_bytes) : hx_dyn_smem(P.ovf_bytes);
+  const int dyn = (TMA ? hx_dyn_smem_tma(P.ovf_bytes) : hx_dyn_smem(P.ovf_bytes)) + hx_lacc_bytes(P);
   static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
@@ -145,7 +145,7 @@ static int hexmv_launch_t(const HexmvParams& P, const HxMaps& T, cudaStream_t s)
     if (e != cudaSuccess) return record_cuda_error(e);
     configured[dev] = true;
   }
-  const int grid = (P.W + HX_STREAM - 1) / HX_STREAM;
+  const int grid = P.n_cta;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(HX_THREADS);
@@ -161,8 +161,28 @@ static int hexmv_launch_t(const HexmvParams& P, const HxMaps& T, cudaStream_t s)
   return GSDLQ_OK;
 }
 
+// low-rank forwarding: a single-output epilogue, whole strips, at most 48 accumulators (the
+// control block's), aligned Vt rows of the next linear
+static int hexmv_check_fwd(const HexmvParams& P) {
+  const gsdlq_linear_job_t& J = P.job;
+  if (J.lr_forwarded && P.tmp_k_ext != nullptr) return GSDLQ_ERR_INVALID;
+  if (J.fwd_acc == nullptr) return GSDLQ_OK;
+  if (reinterpret_cast<uintptr_t>(J.fwd_acc) & 7u) return GSDLQ_ERR_INVALID;
+  const bool single = J.epilogue == GSDLQ_EPI_RESID || J.epilogue == GSDLQ_EPI_SWIGLU ||
+                      (J.epilogue == GSDLQ_EPI_STORE && J.n_mat == 1);
+  if (!single || J.mat[0].rows % 16 != 0) return GSDLQ_ERR_INVALID;
+  int nk = 0;
+  for (int m = 0; m < 3; ++m) {
+    if (J.fwd_k[m] < 0 || J.fwd_k[m] > 16) return GSDLQ_ERR_INVALID;
+    if (J.fwd_k[m] > 0 && (!J.fwd_vt[m] || (reinterpret_cast<uintptr_t>(J.fwd_vt[m]) & 15u))) return GSDLQ_ERR_INVALID;
+    nk += J.fwd_k[m];
+  }
+  return nk > 0 ? GSDLQ_OK : GSDLQ_ERR_INVALID;
+}
+
 int hexmv_check_io(const HexmvParams& P) {
   const gsdlq_linear_job_t& J = P.job;
+  if (hexmv_check_fwd(P) != GSDLQ_OK) return GSDLQ_ERR_INVALID;
   if (J.input_mode < 0 || J.input_mode > 2) return GSDLQ_ERR_INVALID;
   if (J.input_mode == GSDLQ_IN_PLAIN && !J.x) return GSDLQ_ERR_INVALID;
   if (J.input_mode == GSDLQ_IN_RMSNORM && (!J.x || !J.norm_w)) return GSDLQ_ERR_INVALID;
@@ -202,7 +222,7 @@ bool hexmv_tma_enabled() {
   return on;
 }
 bool hexmv_tma_ok(const HexmvParams& P) {
-  return hexmv_tma_enabled() && hexmv_full(P) && hx_dyn_smem_tma(P.ovf_bytes) <= 227 * 1024 &&
+  return hexmv_tma_enabled() && hexmv_full(P) && hx_dyn_smem_tma(P.ovf_bytes) + hx_lacc_bytes(P) <= 227 * 1024 &&
          tmap_encoder() != nullptr;
 }
 
@@ -213,7 +233,11 @@ static int hexmv_dispatch_full(const HexmvParams& P, cudaStream_t s) {
   if (hexmv_tma_ok(P)) {
     bool ok = true;
     for (int m = 0; m < P.job.n_mat && ok; ++m) ok = hexmv_encode_maps(P.job.mat[m], &T.codes[m], &T.scales[m]) == GSDLQ_OK;
-    if (ok) return hexmv_launch_t<EPI, true, true>(P, T, s);
+    if (ok) {
+      HexmvParams Q = P;
+      Q.lacc_off = 0x10000 + P.ovf_bytes + HX_RING_BYTES;  // the accumulator after the ring
+      return hexmv_launch_t<EPI, true, true>(Q, T, s);
+    }
   }
   if (hexmv_full(P)) return hexmv_launch_t<EPI, true, false>(P, T, s);
   return hexmv_launch_t<EPI, false, false>(P, T, s);
@@ -233,18 +257,18 @@ int hexmv_launch(HexmvParams& P, void* workspace, size_t ws_bytes, cudaStream_t 
   if (st != GSDLQ_OK) return st;
   st = hexmv_check_io(P);
   if (st != GSDLQ_OK) return st;
-  const size_t need = hexmv_ws_bytes_for(P.n_strips, P.max_seg, P.nmat);
+  const size_t need = hexmv_ws_bytes_for(P.n_strips, P.nmat);
   if (!workspace || ws_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u)) return GSDLQ_ERR_INVALID;
   P.ctl = static_cast<unsigned*>(workspace);
   P.cnt = P.ctl + CTL_WORDS;
   const uintptr_t pb = reinterpret_cast<uintptr_t>(P.cnt + P.n_strips);
-  P.part = reinterpret_cast<float*>((pb + 15) & ~uintptr_t(15));
+  P.gacc = reinterpret_cast<unsigned long long*>((pb + 15) & ~uintptr_t(15));
   return hexmv_dispatch(P, s);
 }
 
 size_t hexmv_ws_bytes(HexmvParams& P) {
   if (hexmv_plan(P) != GSDLQ_OK) return 0;
-  return hexmv_ws_bytes_for(P.n_strips, P.max_seg, P.nmat);
+  return hexmv_ws_bytes_for(P.n_strips, P.nmat);
 }
 
 // Workspace of the drop-in gsdlq_hex2d_matvec, whose signature carries none: one buffer
@@ -308,8 +332,9 @@ extern "C" int gsdlq_hex2d_matvec(const float* x, const uint8_t* codes, const ui
   P.xy_table = xy_table;
   P.n_pts = n_pts;
   P.tmp_k_ext = k_dim > 0 ? tmp_k : nullptr;
-  const size_t need = hexmv_ws_bytes(P);
-  if (need == 0) return GSDLQ_ERR_INVALID;
+  const int st = hexmv_plan(P);
+  if (st != GSDLQ_OK) return st;
+  const size_t need = hexmv_ws_bytes_for(P.n_strips, P.nmat);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return record_cuda_error(e);
@@ -473,8 +498,9 @@ extern "C" int gsdlq_hex2d_matvec_noalloc(const float* x, const uint8_t* codes, 
   P.xy_table = xy_table;
   P.n_pts = n_pts;
   P.tmp_k_ext = k_dim > 0 ? tmp_k : nullptr;
-  const size_t need = hexmv_ws_bytes(P);
-  if (need == 0) return GSDLQ_ERR_INVALID;
+  const int st = hexmv_plan(P);
+  if (st != GSDLQ_OK) return st;
+  const size_t need = hexmv_ws_bytes_for(P.n_strips, P.nmat);
   if (need > (size_t)GSDLQ_NOALLOC_WS_BYTES) return GSDLQ_ERR_UNSUPPORTED;  // beyond the fixed scratch
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -90,20 +90,19 @@ struct HexmvParams {
   int GU;                  // units per row: ceil(G / 8)
   int UPS;                 // units per strip: nmat * GU
   long long T;             // units in the launch: n_strips * UPS
-  int W;                   // streaming warps in the launch
-  long long TW;            // total partition weight of the W streaming warps
-  float w_per_unit;        // W / T
-  int max_seg;             // partial slots per strip for streaming segments (+1 helper slot)
+  int n_cta;               // CTAs that carry units (the launch may have more)
+  int n_local;             // strips one CTA's unit range can touch (rows of its accumulator)
+  int lacc_off;            // its accumulator in shared memory, bytes after the decode table
   int n_lr;                // low-rank rows projected in the kernel (0 with tmp_k_ext)
   int lr_off[4];           // prefix of k_dim over the matrices
   int lr_chunks;           // 8-column chunks of every Vt row per helper warp
   int ovf_bytes;           // activation-split overflow region
   int ukink;               // every matrix has per-unit kink lists: the streaming warps apply them
   unsigned* ctl;
-  unsigned* cnt;           // [n_strips]
-  float* part;             // [n_strips][max_seg + 1][nmat * 16]
+  unsigned* cnt;                // [n_strips] arrivals of CTAs at strips shared with other CTAs
+  unsigned long long* gacc;     // [n_strips][nmat * 16] fixed-point sums of those strips
   // Inside the persistent decode kernel (null in a stand-alone launch): the input is ready once
-  // *dep >= dep_target; every finished strip and every CTA's completed staging add 1 to *done;
+  // *dep >= dep_target; every finished strip and every CTA of the launch add 1 to *done;
   // *abort is set when a bounded wait gives up, after which every later wait returns at once.
   const unsigned* dep;
   unsigned dep_target;
@@ -133,7 +132,7 @@ struct HxPtrs {
   __device__ __forceinline__ int layer() const { return P.job.layer; }
   __device__ __forceinline__ unsigned* ctl() const { return P.ctl; }
   __device__ __forceinline__ unsigned* cnt() const { return P.cnt; }
-  __device__ __forceinline__ float* part() const { return P.part; }
+  __device__ __forceinline__ unsigned long long* gacc() const { return P.gacc; }
   __device__ __forceinline__ const unsigned* dep() const { return P.dep; }
   __device__ __forceinline__ unsigned dep_target() const { return P.dep_target; }
   __device__ __forceinline__ unsigned* done() const { return P.done; }
@@ -142,38 +141,37 @@ struct HxPtrs {
 };
 
 // ---- partition (identical on host and device) ---------------------------------------
-// Warps are spread over the SM's four schedulers by warp index mod 4, so schedulers 0 and 1 run
-// four streaming warps and schedulers 2 and 3 run three streaming warps plus one helper warp.
-// The units are dealt in proportion 3 : 4 to warps on the first and the second pair, so every
-// scheduler streams the same share.  lp(l) = sum of the weights of local warps 0 .. l-1.
+// The (strip, matrix, unit) iterations are dealt to the CTAs as equal contiguous ranges, and a
+// CTA's range to its 14 streaming warps as contiguous ranges weighted by scheduler: warps are
+// spread over the SM's four schedulers by warp index mod 4, so schedulers 0 and 1 run four
+// streaming warps and schedulers 2 and 3 run three plus one helper warp; the units are dealt in
+// proportion 3 : 4 to warps on the first and the second pair, so every scheduler streams the same
+// share.  lp(l) = sum of the weights of local warps 0 .. l-1.
 __host__ __device__ __forceinline__ int hx_lp(int l) { return 4 * l - 2 * (l / 4) - ((l % 4) < 2 ? (l % 4) : 2); }
-__host__ __device__ __forceinline__ long long hx_cumw(int w) {
-  return (long long)hx_lp(HX_STREAM) * (w / HX_STREAM) + hx_lp(w % HX_STREAM);
+__host__ __device__ __forceinline__ long long hx_cta_begin(long long T, int n_cta, int c) {
+  return c >= n_cta ? T : T * c / n_cta;
 }
-// first unit of streaming warp w
-__host__ __device__ __forceinline__ int hx_unit_begin(long long T, long long TW, int w) {
-  return (int)(T * hx_cumw(w) / TW);
+// the CTA whose range holds unit u: the largest c with cta_begin(c) <= u
+__host__ __device__ __forceinline__ int hx_cta_of(long long T, int n_cta, long long u) {
+  return (int)(((u + 1) * n_cta - 1) / T);
 }
-__device__ __forceinline__ int unit_begin(const HexmvParams& P, int w) { return hx_unit_begin(P.T, P.TW, w); }
-// warp whose range contains unit i: the largest w with unit_begin(w) <= i, i.e. with
-// cumw(w) <= c = floor(((i + 1) * TW - 1) / T); cumw is a whole number of CTA cycles plus a local
-// prefix, so w follows from one division and a scan of the 14 local prefixes.
-__host__ __device__ __forceinline__ int hx_warp_of(long long T, long long TW, int W, float w_per_unit, int i) {
-  (void)w_per_unit;
-  const long long c = ((long long)(i + 1) * TW - 1) / T;
-  const int cyc = hx_lp(HX_STREAM);
-  const long long q = c / cyc;
-  const int r = (int)(c - q * cyc);
-  int l = 0;
-  while (l + 1 < HX_STREAM && hx_lp(l + 1) <= r) ++l;
-  const long long w = q * HX_STREAM + l;
-  return (int)(w < W - 1 ? w : W - 1);
-}
-__device__ __forceinline__ int warp_of_unit(const HexmvParams& P, int i) { return hx_warp_of(P.T, P.TW, P.W, P.w_per_unit, i); }
 
-inline size_t hexmv_ws_bytes_for(int n_strips, int max_seg, int nmat) {
-  return sizeof(unsigned) * (CTL_WORDS + (size_t)n_strips) +
-         sizeof(float) * (size_t)n_strips * (max_seg + 1) * nmat * 16 + 256;
+// Fixed-point strip sums: exact integer additions make the result independent of the order in
+// which warps and CTAs contribute (deterministic), at 2^-32 resolution and +-2^22 range.
+__device__ __forceinline__ unsigned long long hx_fix(float v) {
+  if (!(fabsf(v) < LR_MAX)) {
+    raise_flag(GSDLQ_FLAG_RANGE);
+    v = (v != v) ? 0.f : copysignf(LR_MAX, v);
+  }
+  return (unsigned long long)__float2ll_rn(v * LR_FIX);
+}
+__device__ __forceinline__ float hx_unfix(unsigned long long a) {
+  return (float)((double)(long long)a * (1.0 / 4294967296.0));
+}
+
+inline size_t hexmv_ws_bytes_for(int n_strips, int nmat) {
+  return ((sizeof(unsigned) * (CTL_WORDS + (size_t)n_strips) + 15) & ~size_t(15)) +
+         sizeof(unsigned long long) * (size_t)n_strips * nmat * 16 + 256;
 }
 
 // ---- shared memory --------------------------------------------------------------------
@@ -205,6 +203,8 @@ constexpr int HX_RING_BYTES = HX_STREAM * 2 * HX_SLOT;
 constexpr int HX_MBAR_OFF = 1536;  // byte offset in the reduction words: 2 x 8 bytes per warp
 constexpr int HX_PH_OFF = 1792;    // byte offset: one parity word per warp
 inline int hx_dyn_smem_tma(int ovf_bytes) { return hx_dyn_smem(ovf_bytes) + HX_RING_BYTES; }
+// the CTA's strip accumulator (placed at lacc_off, after the overflow chunks / the ring)
+inline int hx_lacc_bytes(const HexmvParams& P) { return P.n_local * P.nmat * 16 * 8; }
 
 // Activation splits.  For pair p (columns 2p, 2p+1) with a = x[2p], b = x[2p]/2 + sqrt3/2 x[2p+1],
 // the hi word (bf16 a_hi | b_hi << 16) and the lo word live in 128-byte chunk
@@ -371,19 +371,22 @@ __device__ __forceinline__ EpiPre epilogue_pre(const HexmvParams& P, const Strip
 }
 
 // Epilogue of a completed strip.  Lane j holds the finished value of row (j & 15) of
-// matrix m0 + (j >> 4) (lanes >= 16 only carry data in pair mode).
+// matrix m0 + (j >> 4) (lanes >= 16 only carry data in pair mode).  Returns, in lanes 0-15, the
+// value written for the row (the next linear's input; 0 for ROPE_KV and rows past the end).
 template <int EPI>
-__device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float v, int lane, const EpiPre& pre,
-                               int pos, int layer) {
+__device__ float strip_epilogue(const HexmvParams& P, const StripInfo& si, float v, int lane, const EpiPre& pre,
+                                int pos, int layer) {
   const gsdlq_linear_job_t& J = P.job;
   const int r = lane & 15;
   const gsdlq_hexmat_t& M = J.mat[si.m0];
   const int row = si.rbase + r;
   const bool ok = row < M.rows;
+  float out = 0.f;
   if constexpr (EPI == GSDLQ_EPI_STORE) {
     unsigned long long key = 0ull;
     if (lane < 16 && ok) {
       J.y[si.m0][row] = v;
+      out = v;
       if (J.argmax_key) key = argmax_key(v, (uint32_t)(row + J.argmax_index_base));
     }
     if (J.argmax_key) {
@@ -395,10 +398,16 @@ __device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float 
       if (lane == 0 && key) atomicMax(J.argmax_key, key);
     }
   } else if constexpr (EPI == GSDLQ_EPI_RESID) {
-    if (lane < 16 && ok) J.y[0][row] = pre.resid + v;
+    if (lane < 16 && ok) {
+      out = pre.resid + v;
+      J.y[0][row] = out;
+    }
   } else if constexpr (EPI == GSDLQ_EPI_SWIGLU) {
     const float u = __shfl_down_sync(0xffffffffu, v, 16);
-    if (lane < 16 && ok) J.y[0][row] = (v / (1.0f + expf(-v))) * u;
+    if (lane < 16 && ok) {
+      out = (v / (1.0f + expf(-v))) * u;
+      J.y[0][row] = out;
+    }
   } else if constexpr (EPI == GSDLQ_EPI_ROPE_KV) {
     // rows (2i, 2i+1) of a head form one interleaved RoPE pair
     const float other = __shfl_xor_sync(0xffffffffu, v, 1);
@@ -423,46 +432,81 @@ __device__ void strip_epilogue(const HexmvParams& P, const StripInfo& si, float 
       }
     }
   }
+  return out;
 }
 
-// Sum a completed strip's slots in slot order and run the epilogue (one warp).  The helper slot
-// already holds the kink and low-rank terms; the slot and epilogue loads go out in one batch.
+// Low-rank forwarding (job.fwd_acc): this strip's 16 output rows r contribute
+// sum_r Vt_next[j][rbase + r] * w[rbase + r] * out_r to the next linear's accumulator j.  Lane l
+// handles accumulators l and l + 32; their Vt slices (16 fp16 each) are loaded before the strip's
+// slot sum so that the loads overlap it.
+struct FwdSlice {
+  uint4 a[2], b[2];
+};
+__device__ __forceinline__ int fwd_total(const gsdlq_linear_job_t& J) { return J.fwd_k[0] + J.fwd_k[1] + J.fwd_k[2]; }
+__device__ __forceinline__ const uint16_t* fwd_row(const gsdlq_linear_job_t& J, int jl, int n_out) {
+  int m = 0, j = jl;
+  while (m < 2 && j >= J.fwd_k[m]) j -= J.fwd_k[m], ++m;
+  return J.fwd_vt[m] + (size_t)j * n_out;
+}
+__device__ __forceinline__ FwdSlice fwd_load(const gsdlq_linear_job_t& J, int rbase, int n_out, int lane) {
+  FwdSlice f;
+  const int nk = fwd_total(J);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int jl = lane + 32 * h;
+    const bool whole = rbase + 16 <= n_out;  // (n_out is a multiple of 64: strips never straddle it)
+    if (jl < nk && whole) {
+      const uint4* v = reinterpret_cast<const uint4*>(fwd_row(J, jl, n_out) + rbase);
+      f.a[h] = __ldg(v);
+      f.b[h] = __ldg(v + 1);
+    } else {
+      f.a[h] = make_uint4(0u, 0u, 0u, 0u);
+      f.b[h] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  return f;
+}
+__device__ __forceinline__ float fwd_dot16(const uint4& a, const uint4& b, float o, int lane) {
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  float acc = 0.f;
+#pragma unroll
+  for (int r = 0; r < 16; ++r) acc = fmaf(h2f((uint16_t)(w[r >> 1] >> (16 * (r & 1)))), __shfl_sync(0xffffffffu, o, r), acc);
+  (void)lane;
+  return acc;
+}
+__device__ __forceinline__ void fwd_apply(const gsdlq_linear_job_t& J, const FwdSlice& f, int rbase, int n_out, float out,
+                                          int lane) {
+  const int row = rbase + (lane & 15);
+  float o = (lane < 16 && row < n_out) ? out : 0.f;
+  if (J.fwd_norm_w != nullptr && lane < 16 && row < n_out) o *= __ldg(J.fwd_norm_w + row);
+  const int nk = fwd_total(J);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (32 * h >= nk) break;  // uniform
+    float acc = fwd_dot16(f.a[h], f.b[h], o, lane);
+    const int jl = lane + 32 * h;
+    if (jl < nk) {
+      if (!(fabsf(acc) < LR_MAX)) {
+        raise_flag(GSDLQ_FLAG_RANGE);
+        acc = (acc != acc) ? 0.f : copysignf(LR_MAX, acc);
+      }
+      atomicAdd(J.fwd_acc + jl, (unsigned long long)__float2ll_rn(acc * LR_FIX));
+    }
+  }
+}
+
+// Epilogue of a completed strip whose final sum v lane j holds (row j & 15 of matrix
+// m0 + (j >> 4)), with low-rank forwarding (one warp).
 template <int EPI, int NMAT, class PTR>
-__device__ void finish_strip(const HexmvParams& P, const PTR& mp, int s, int lane, int pos) {
-  // the arriving lane's acq_rel count was the acquire; the warp barrier orders the other lanes'
-  // reads after it
-  __syncwarp();
-  const int UPS = P.UPS;
-  const int w_first = warp_of_unit(P, s * UPS);
-  const int w_last = warp_of_unit(P, s * UPS + UPS - 1);
-  const int nseg = w_last - w_first + 1;
-  constexpr int width = NMAT * 16;
-  const StripInfo si = strip_info<NMAT>(P, s);
+__device__ __forceinline__ void finish_value(const HexmvParams& P, const PTR& mp, const StripInfo& si, float v, int lane,
+                                             int pos) {
   const EpiPre pre = epilogue_pre<EPI>(P, si, lane, pos);
-  float* base = mp.part() + (size_t)s * (P.max_seg + 1) * width;
-  float v = 0.f;
-  if (lane < width) {
-    constexpr int B = 12;
-    float pv[B];
-#pragma unroll
-    for (int k = 0; k < B; ++k) pv[k] = k < nseg ? __ldcg(base + (size_t)k * width + lane) : 0.f;
-    const float hv = __ldcg(base + (size_t)P.max_seg * width + lane);  // helper slot: kinks + low rank
-#pragma unroll
-    for (int k = 0; k < B; ++k) v += pv[k];
-    for (int k = B; k < nseg; ++k) v += __ldcg(base + (size_t)k * width + lane);
-    v += hv;
-    // every consumed slot and the counter go back to zero: the whole workspace is zero between
-    // launches, so launches of any geometry can share it
-    for (int k = 0; k < nseg; ++k) base[(size_t)k * width + lane] = 0.f;
-    base[(size_t)P.max_seg * width + lane] = 0.f;
-  }
-  if (lane == 0) mp.cnt()[s] = 0u;
-  strip_epilogue<EPI>(P, si, v, lane, pre, pos, mp.layer());
-  if (mp.done() != nullptr) {  // persistent decode kernel: publish the strip to the next phase
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) red_add_release(mp.done(), 1u);
-  }
+  const bool fwd = P.job.fwd_acc != nullptr;
+  const int n_out = P.job.mat[si.m0].rows;
+  FwdSlice fs;
+  if (fwd) fs = fwd_load(P.job, si.rbase, n_out, lane);
+  const float out = strip_epilogue<EPI>(P, si, v, lane, pre, pos, mp.layer());
+  if (fwd) fwd_apply(P.job, fs, si.rbase, n_out, out, lane);
 }
 
 // The whole fused linear for one CTA.  MEGA = false: a stand-alone launch (programmatic dependent
@@ -507,6 +551,10 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
     return make_float2(x0, (b - 0.5f * x0) * 1.1547005383792515f);
   };
   uint32_t* redu = reinterpret_cast<uint32_t*>(red);
+  // this CTA's unit range, the strips it touches [s_lo, s_hi] and their fixed-point sums
+  const long long cb0 = hx_cta_begin(P.T, P.n_cta, blockIdx.x), cb1 = hx_cta_begin(P.T, P.n_cta, blockIdx.x + 1);
+  const int s_lo = (int)(cb0 / P.UPS), s_hi = cb1 > cb0 ? (int)((cb1 - 1) / P.UPS) : s_lo - 1;
+  unsigned long long* lacc = reinterpret_cast<unsigned long long*>(smem + tab_off + P.lacc_off);
 
   // Barriers: 0 = the whole CTA (end only); 1 = the 14 streaming warps; 2 = streaming warps
   // arrive once the input is staged, helper warps wait on it only when they need the input.
@@ -520,9 +568,15 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
     const int c8_0 = hw * P.lr_chunks;
     const int c8_1 = min(c8_0 + P.lr_chunks, C / 8);
     constexpr int SPP = (NMAT == 2) ? 1 : 2;  // strips per kink pass
-    // pass p covers strip hw + p*SPP*H (+ H for lanes 16-31 when SPP == 2); lane = row
-    auto pass_strip = [&](int p) { return hw + p * SPP * H + ((NMAT == 2) ? 0 : (lane >> 4) * H); };
-    const int npass = hw < P.n_strips ? (P.n_strips - hw + SPP * H - 1) / (SPP * H) : 0;
+    // The kink and low-rank terms of the strips this CTA owns (those whose first unit is in its
+    // range) go into its accumulator; pass p of helper warp hl covers strip
+    // o_lo + (p * HX_HELP + hl) * SPP (+ 1 for lanes 16-31 when SPP == 2); lane = row.
+    const int hl = warp - HX_STREAM;
+    const int o_lo = cb1 > cb0 ? (int)((cb0 + P.UPS - 1) / P.UPS) : 0;
+    const int o_hi = cb1 > cb0 ? (int)((cb1 + P.UPS - 1) / P.UPS) : 0;
+    auto pass_strip = [&](int p) { return o_lo + (p * HX_HELP + hl) * SPP + ((NMAT == 2) ? 0 : (lane >> 4)); };
+    const int npass = o_hi > o_lo + hl * SPP ? (o_hi - o_lo - hl * SPP + HX_HELP * SPP - 1) / (HX_HELP * SPP) : 0;
+    (void)H;
     struct KRow {
       const uint16_t* cols;
       const float* del;
@@ -533,7 +587,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
     auto krow = [&](int p) -> KRow {
       KRow k{nullptr, nullptr, 0u, 0u, 0, -1};
       const int s = pass_strip(p);
-      if (p < npass && s < P.n_strips) {
+      if (p < npass && s < o_hi) {
         const StripInfo si = strip_info<NMAT>(P, s);
         const int km = si.m0 + ((NMAT == 2) ? (lane >> 4) : 0);
         k.km = km;
@@ -581,8 +635,9 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
       return reinterpret_cast<const uint4*>(mp.mat(m).Vt + (size_t)j * C);
     };
+    const bool lr_here = P.n_lr > 0 && !J.lr_forwarded;  // else the previous launch forwarded it
 #pragma unroll 1
-    for (int jl = lane; jl < P.n_lr; jl += 32) {
+    for (int jl = lane; lr_here && jl < P.n_lr; jl += 32) {
       const uint4* vt = vt_row(jl);
       if (jl == lane) {
 #pragma unroll
@@ -604,7 +659,22 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
              a1.y * h2f(raw.y >> 16) + a2.x * h2f(raw.z & 0xffffu) + a2.y * h2f(raw.z >> 16) +
              a3.x * h2f(raw.w & 0xffffu) + a3.y * h2f(raw.w >> 16);
     };
-    if (P.n_lr > 0) {
+    if (P.n_lr > 0 && J.lr_forwarded) {
+      // the previous launch added every row's term: scale by this launch's 1/rms and S
+      if (warp == HX_WARPS - 1) {
+        const float sc = (mp.input_mode() != GSDLQ_IN_PLAIN) ? red[37] : 1.f;
+        const unsigned long long* acc = reinterpret_cast<const unsigned long long*>(mp.ctl() + CTL_TMPK);
+        for (int jl = lane; jl < P.n_lr; jl += 32) {
+          int m = 0, j = jl;
+          while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
+          const double d = (double)(long long)__ldcg(acc + jl) * (1.0 / 4294967296.0);
+          s_lr[jl] = (float)d * sc * __ldg(mp.mat(m).S + j);
+        }
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) s_lr[HX_LR_FLAG] = 1.f;
+      }
+    } else if (P.n_lr > 0) {
 #pragma unroll 1
       for (int jl = lane; jl - lane < P.n_lr; jl += 32) {  // uniform trip count: all lanes reach the fence
         if (jl < P.n_lr) {
@@ -692,25 +762,9 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
         v += lr;
       }
       const int s = pass_strip(p);
-      if (s < P.n_strips) mp.part()[((size_t)s * (P.max_seg + 1) + P.max_seg) * width + (lane & (width - 1))] = v;
+      if (s < o_hi) atomicAdd(lacc + (size_t)(s - s_lo) * width + (lane & (width - 1)), hx_fix(v));
     }
     if (bad) raise_flag(GSDLQ_FLAG_BAD_KINK);
-    __threadfence();
-    __syncwarp();
-    // arrival i of this warp: pass i / SPP, half i % SPP
-    const int n_arr = npass * SPP;
-    for (int b0 = 0; b0 < n_arr; b0 += 32) {
-      const int i = b0 + lane;
-      const int s = hw + (i / SPP) * SPP * H + (i % SPP) * H;
-      unsigned fin = 0u;
-      if (i < n_arr && s < P.n_strips) fin = (atom_add_acq_rel(&mp.cnt()[s], 1u) + 1u == (unsigned)P.UPS + 1u) ? 1u : 0u;
-      unsigned fm = __ballot_sync(0xffffffffu, fin);
-      while (fm) {
-        const int k = b0 + __ffs(fm) - 1;
-        fm &= fm - 1u;
-        finish_strip<EPI, NMAT>(P, mp, hw + (k / SPP) * SPP * H + (k % SPP) * H, lane, pos);
-      }
-    }
   } else {
     // ==== streaming warps ===================================================================
     // decode table: lanes 0-15 compute the entries of 16 rows, then every lane writes 16-byte
@@ -739,10 +793,10 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       s_lr[HX_LR_FLAG] = 0.f;
     }
     if (lane < 16) s_ks[lane] = 0.f;
-    const int w = blockIdx.x * HX_STREAM + warp;
-    const bool streamer = w < P.W;
-    const int u0 = streamer ? unit_begin(P, w) : 0;
-    const int u1 = streamer ? unit_begin(P, w + 1) : 0;
+    const bool streamer = cb1 > cb0;
+    const long long n_c = cb1 - cb0;
+    const int u0 = (int)(cb0 + n_c * hx_lp(warp) / hx_lp(HX_STREAM));
+    const int u1 = (int)(cb0 + n_c * hx_lp(warp + 1) / hx_lp(HX_STREAM));
     // cursor (strip, matrix in strip, unit column) of the next unit to load, and its pointers
     int ns = u0 / P.UPS;
     int nm = (u0 - ns * P.UPS) / P.GU;
@@ -944,6 +998,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       for (int k = 0; k < HX_STREAM; ++k) t += red[1 + k];  // every thread: no second barrier
       inv = 1.0f / sqrtf(t / (float)C + J.eps);             // gsd_lq_cpu_engine.c:78
     }
+    if (tid == 0) red[37] = inv;  // for a forwarded projection's scale (read after barrier 2)
 #pragma unroll
     for (int k = 0; k < XR; ++k) {
       const int p = tid + k * NST;
@@ -971,12 +1026,11 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       *reinterpret_cast<uint32_t*>(smem + off) = 0u;
       *reinterpret_cast<uint32_t*>(smem + off + 16) = 0u;
     }
-    named_bar_sync(1, NST);             // table and splits complete for the streaming warps
+    for (int i = tid; i < P.n_local * width; i += NST) lacc[i] = 0ull;
+    if (tid == 0) redu[38] = 0u;        // strips this CTA finished (decode kernel)
+    named_bar_sync(1, NST);             // table, splits and accumulator ready for the streaming warps
     named_bar_arrive(2, HX_THREADS);    // ... and released to the helper warps
-    if (MEGA && tid == 0) {
-      reinterpret_cast<int*>(redu)[35] = J.mat[0].radius;  // every streaming warp has read the old value
-      red_add_release(mp.done(), 1u);  // this CTA no longer reads the phase's input from global memory
-    }
+    if (MEGA && tid == 0) reinterpret_cast<int*>(redu)[35] = J.mat[0].radius;  // every streaming warp has read the old value
     const int pos = reinterpret_cast<const int*>(redu)[34];
     if (streamer) {
     // ---- streaming warps --------------------------------------------------------------
@@ -994,16 +1048,15 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
     float acc[NMAT][2];
 #pragma unroll
     for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
-    auto emit = [&](int s) {
-      const int seg = w - warp_of_unit(P, s * P.UPS);
-      float* slot = mp.part() + ((size_t)s * (P.max_seg + 1) + seg) * width;
+    auto emit = [&](int s) {  // this warp's part of strip s into the CTA's accumulator
+      unsigned long long* la = lacc + (size_t)(s - s_lo) * width;
 #pragma unroll
       for (int mm = 0; mm < NMAT; ++mm) {
         const float vg = acc[mm][0] + __shfl_xor_sync(0xffffffffu, acc[mm][0], 1);
         const float vh = acc[mm][1] + __shfl_xor_sync(0xffffffffu, acc[mm][1], 1);
         if (q == 0) {
-          slot[mm * 16 + gl] = vg;
-          slot[mm * 16 + gl + 8] = vh;
+          atomicAdd(la + mm * 16 + gl, hx_fix(vg));
+          atomicAdd(la + mm * 16 + gl + 8, hx_fix(vh));
         }
       }
     };
@@ -1124,33 +1177,56 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       if (u + 2 < u1) step_next();
     }
     if (TMA && MEGA && lane == 0) *ph_word = ph;  // the slots' parities carry over to the next phase
-    if (u1 > u0) {
-      emit(seg_s);
-      // the counts are deferred to the end of the range: a fence mid-range would wait for the code
-      // loads in flight.  One fence covers all of this warp's slot stores; lane i then counts this
-      // warp's units of the i-th strip the range touched.
-      __threadfence();
-      __syncwarp();
-      const int s_a = u0 / P.UPS, s_b = (u1 - 1) / P.UPS;
-      for (int b0 = s_a; b0 <= s_b; b0 += 32) {
-        const int s = b0 + lane;
-        unsigned fin = 0u;
-        if (s <= s_b) {
-          const int a = max(u0, s * P.UPS), b = min(u1, s * P.UPS + P.UPS);
-          const unsigned units = (unsigned)(b - a);
-          fin = (atom_add_acq_rel(&mp.cnt()[s], units) + units == (unsigned)P.UPS + 1u) ? 1u : 0u;
-        }
-        unsigned fm = __ballot_sync(0xffffffffu, fin);
-        while (fm) {
-          const int i = __ffs(fm) - 1;
-          fm &= fm - 1u;
-          finish_strip<EPI, NMAT>(P, mp, b0 + i, lane, pos);
-        }
-      }
-    }
+    if (u1 > u0) emit(seg_s);
       }
   }
 
+  // ---- finish this CTA's strips ------------------------------------------------------------
+  // After one barrier every warp and helper term is in the accumulator.  Warp w takes strips
+  // s_lo + w, s_lo + w + 16, ...: a strip inside this CTA's range is finished from the
+  // accumulator; one shared with other CTAs adds its part to the strip's global fixed-point sum,
+  // and the last CTA to arrive (acq_rel count) finishes it and leaves the sum and count at zero.
+  __syncthreads();
+  {
+    const int pos = reinterpret_cast<const int*>(redu)[34];
+    unsigned nfin = 0u;
+    for (int s = s_lo + warp; s <= s_hi; s += HX_WARPS) {
+      const long long first = (long long)s * P.UPS;
+      const int cf = hx_cta_of(P.T, P.n_cta, first), cl = hx_cta_of(P.T, P.n_cta, first + P.UPS - 1);
+      unsigned long long a = lane < width ? lacc[(size_t)(s - s_lo) * width + lane] : 0ull;
+      bool mine = true;
+      if (cf != cl) {
+        unsigned long long* g = mp.gacc() + (size_t)s * width;
+        if (lane < width) atomicAdd(g + lane, a);
+        __threadfence();
+        __syncwarp();
+        unsigned last = 0u;
+        if (lane == 0) last = atom_add_acq_rel(&mp.cnt()[s], 1u) + 1u == (unsigned)(cl - cf + 1) ? 1u : 0u;
+        mine = __shfl_sync(0xffffffffu, last, 0) != 0u;
+        if (mine) {
+          __syncwarp();  // lane 0's acquire orders the other lanes' reads
+          if (lane < width) {
+            a = __ldcg(g + lane);
+            g[lane] = 0ull;
+          }
+          if (lane == 0) mp.cnt()[s] = 0u;
+        }
+      }
+      if (mine) {
+        finish_value<EPI, NMAT>(P, mp, strip_info<NMAT>(P, s), hx_unfix(a), lane, pos);
+        ++nfin;
+      }
+    }
+    if (MEGA) {
+      // one release per CTA: its finished strips and 1 for the CTA (it has read its input)
+      if (lane == 0 && nfin) atomicAdd(&redu[38], nfin);
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence();
+        red_add_release(mp.done(), redu[38] + 1u);
+      }
+    }
+  }
   if (MEGA) return;  // the decode kernel zeroes every phase's control words at the end of the step
   pdl_launch_dependents();
   // ---- the last CTA leaves the control words at zero for the next launch ---------------

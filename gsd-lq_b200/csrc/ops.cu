@@ -156,6 +156,8 @@ static int attention_launch(const gsdlq_attn_job_t& J, cudaStream_t s) {
   if (J.max_seq <= 0 || J.layer < 0) return GSDLQ_ERR_INVALID;
   if (J.block_table && J.page_size <= 0) return GSDLQ_ERR_INVALID;
   if (!J.pos_dev && (J.pos_val < 0 || J.pos_val >= J.max_seq)) return GSDLQ_ERR_INVALID;
+  if (J.fwd_acc && (J.fwd_k <= 0 || J.fwd_k > 48 || !J.fwd_vt || (reinterpret_cast<uintptr_t>(J.fwd_acc) & 7u)))
+    return GSDLQ_ERR_INVALID;
   const int tps = attn_tokens_per_split(J.max_seq);
   const int nsplit = (J.max_seq + tps - 1) / tps;
   cudaLaunchConfig_t cfg = {};

@@ -77,7 +77,7 @@ class DevicePacked:
 class GSDLQModel:
     def __init__(self, source, rope_interleaved: int = 1, device=None, max_seq: int = MAX_SEQ_LEN,
                  use_graph: bool = True, verbose: bool = False, tp=None, unit_kinks: bool = False,
-                 fused_step: bool = False):
+                 fused_step: bool = False, lr_forward: bool = True):
         t0 = time.time()
         if not torch.cuda.is_available():
             raise RuntimeError("GSDLQModel needs a CUDA device (there is no CPU path)")
@@ -94,6 +94,7 @@ class GSDLQModel:
         self.tp = tp
         self.unit_kinks = unit_kinks
         self._want_fused = fused_step and tp is None
+        self.lr_forward = lr_forward
         self._plans: dict = {}
         if isinstance(source, str):
             source = read_gsd2(source)
@@ -244,6 +245,40 @@ class GSDLQModel:
                 self.ws_of[id(j)] = self.ws[k % 2]
                 k += 1
         self.ws_of[id(self.head_job)] = self.ws[k % 2]
+        if self.tp is None and self.lr_forward:
+            self._wire_forwarding()
+
+    def _wire_forwarding(self):
+        """Low-rank forwarding: every op whose output is the next linear's input adds that linear's
+        projection of it (strip by strip, fixed point) to the next launch's workspace, which then
+        skips its own grid-wide projection.  (Tensor parallelism keeps the in-kernel projection:
+        there the epilogues see partial sums.)"""
+        def acc(job):
+            return self.ws_of[id(job)].data_ptr() + 64  # the workspace's accumulator words
+
+        def into(src, dst, mats, norm):
+            if sum(m.k_dim for m in mats) == 0:
+                return  # no low-rank term to forward
+            for i in range(3):
+                src.fwd_vt[i] = mats[i].desc().Vt if i < len(mats) and mats[i].k_dim > 0 else None
+                src.fwd_k[i] = mats[i].k_dim if i < len(mats) else 0
+            src.fwd_norm_w = norm.data_ptr() if norm is not None else None
+            src.fwd_acc = acc(dst)
+            dst.lr_forwarded = 1
+
+        hx = lambda l, n: self.hex[f"blk.{l}.{n}.weight"]  # noqa: E731
+        for l, (qkv, att, o, gu, dn) in enumerate(self.layer_jobs):
+            ho = hx(l, "attn_output")
+            if ho.k_dim > 0:
+                att.fwd_vt, att.fwd_k, att.fwd_acc = ho.desc().Vt, ho.k_dim, acc(o)
+                o.lr_forwarded = 1
+            into(o, gu, [hx(l, "ffn_gate"), hx(l, "ffn_up")], self.norms[f"blk.{l}.ffn_norm.weight"])
+            into(gu, dn, [hx(l, "ffn_down")], None)
+            # (not into the LM head: prefill steps and graph warm-ups run the layers without it, and a
+            # forwarded sum must always be consumed by the launch it was made for)
+            if l + 1 < self.n_layers:
+                into(dn, self.layer_jobs[l + 1][0], [hx(l + 1, n) for n in ("attn_q", "attn_k", "attn_v")],
+                     self.norms[f"blk.{l + 1}.attn_norm.weight"])
 
     def linear(self, job):
         ops.linear(job, self.ws_of[id(job)])

@@ -184,6 +184,20 @@ typedef struct gsdlq_linear_job {
    * (value, ~index) key; the key must start at 0 */
   unsigned long long *argmax_key;
   int argmax_index_base;      /* added to the row index in the key (vocab-parallel LM head) */
+  /* Low-rank forwarding (optional; engine use).  A launch whose output is the NEXT linear's input
+   * adds that linear's projection of it, strip by strip, to the next launch's accumulators:
+   * fwd_acc[lr_off(m) + j] += round(2^32 * sum_r Vt_m[j][r] * w[r] * out[r]) (two's-complement
+   * 64-bit), over the rows r it finished, for the next linear's matrices m (fwd_vt[m], fwd_k[m]
+   * rows of [cols] fp16) and w = fwd_norm_w (1 when NULL).  out is the epilogue's output (the new
+   * residual for RESID, the SwiGLU product for SWIGLU, y for STORE).  fwd_acc is the next launch's
+   * workspace + 64 bytes (its accumulator words), so the next launch's workspace must be zero at
+   * this launch's start.  The next launch sets lr_forwarded = 1: it skips its own projection and
+   * scales the accumulators by its 1/rms (RMSNORM input) and S. */
+  const uint16_t *fwd_vt[3];
+  int fwd_k[3];
+  const float *fwd_norm_w;
+  unsigned long long *fwd_acc;
+  int lr_forwarded;
 } gsdlq_linear_job_t;
 
 /* Bytes of device workspace a gsdlq_linear launch of `job` needs (host pointers). */
@@ -254,6 +268,11 @@ typedef struct gsdlq_attn_job {
   int page_size;
   float *partial;
   unsigned int *workspace;
+  /* low-rank forwarding into the next linear (the O projection; see gsdlq_linear_job_t): each
+   * combined kv head adds fwd_vt[j][c] * out[c] over its head columns c to fwd_acc[j], j < fwd_k */
+  const uint16_t *fwd_vt;
+  int fwd_k;
+  unsigned long long *fwd_acc;
 } gsdlq_attn_job_t;
 
 /* Bytes of `partial` (floats) and `workspace` (uints) a gsdlq_attention call needs. */
