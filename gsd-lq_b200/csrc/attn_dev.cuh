@@ -72,6 +72,7 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
   float* s_l = S.s_l;
   float* s_f = S.s_f;
   const int lane = tid & 31, warp = tid >> 5;
+  if (!MEGA) pdl_trigger_ops();  // the next launch may be scheduled at once (its wait covers this grid)
   const int pos = J.pos_dev ? *J.pos_dev : J.pos_val;
   const bool pos_ok = pos >= 0 && pos < J.max_seq;
   const int len = pos_ok ? pos + 1 : 0;
@@ -274,14 +275,10 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
       attn_sync<BAR>();  // (the K/V buffers held the token-group reduction until here)
       forward(ov);
     }
-    if (MEGA) {
-      if (split == 0) {  // publish the head to the next phase
-        __threadfence();
-        attn_sync<BAR>();
-        if (tid == 0) red_add_release(done, 1u);
-      }
-    } else {
-      pdl_trigger_ops();
+    if (MEGA && split == 0) {  // publish the head to the next phase
+      __threadfence();
+      attn_sync<BAR>();
+      if (tid == 0) red_add_release(done, 1u);
     }
     return;
   }
@@ -296,7 +293,6 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
     part[tid * (HD + 2) + HD] = any ? s_m[tid] : -INFINITY;
     part[tid * (HD + 2) + HD + 1] = any ? s_l[tid] : 0.f;
   }
-  if (!MEGA) pdl_trigger_ops();
   // the last CTA of this kv head combines all splits
   __threadfence();
   attn_sync<BAR>();

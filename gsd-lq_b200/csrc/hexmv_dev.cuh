@@ -497,16 +497,35 @@ __device__ __forceinline__ void fwd_apply(const gsdlq_linear_job_t& J, const Fwd
 
 // Epilogue of a completed strip whose final sum v lane j holds (row j & 15 of matrix
 // m0 + (j >> 4)), with low-rank forwarding (one warp).
+// The operands of a strip's epilogue that do not depend on its sum (loaded ahead of it).
+struct StripPre {
+  EpiPre e;
+  FwdSlice f;
+};
+template <int EPI>
+__device__ __forceinline__ StripPre strip_pre(const HexmvParams& P, const StripInfo& si, int lane, int pos) {
+  StripPre sp;
+  sp.e = epilogue_pre<EPI>(P, si, lane, pos);
+  if (P.job.fwd_acc != nullptr) sp.f = fwd_load(P.job, si.rbase, P.job.mat[si.m0].rows, lane);
+  return sp;
+}
 template <int EPI, int NMAT, class PTR>
 __device__ __forceinline__ void finish_value(const HexmvParams& P, const PTR& mp, const StripInfo& si, float v, int lane,
-                                             int pos) {
-  const EpiPre pre = epilogue_pre<EPI>(P, si, lane, pos);
-  const bool fwd = P.job.fwd_acc != nullptr;
+                                             int pos, const StripPre& sp) {
   const int n_out = P.job.mat[si.m0].rows;
-  FwdSlice fs;
-  if (fwd) fs = fwd_load(P.job, si.rbase, n_out, lane);
-  const float out = strip_epilogue<EPI>(P, si, v, lane, pre, pos, mp.layer());
-  if (fwd) fwd_apply(P.job, fs, si.rbase, n_out, out, lane);
+  const float out = strip_epilogue<EPI>(P, si, v, lane, sp.e, pos, mp.layer());
+  if (P.job.fwd_acc != nullptr) fwd_apply(P.job, sp.f, si.rbase, n_out, out, lane);
+}
+
+// After a CTA's last helper warp has read the low-rank accumulators: count it; the last CTA of
+// the launch leaves every control word at zero for the workspace's next user (its acquire
+// orders the zeroing after every CTA's reads, which precede their releases of the count).
+__device__ __forceinline__ void ctl_release_last(unsigned* ctl, int lane) {
+  unsigned last = 0u;
+  if (lane == 0) last = atom_add_acq_rel(&ctl[CTL_DONE], 1u) == gridDim.x - 1 ? 1u : 0u;
+  if (__shfl_sync(0xffffffffu, last, 0)) {
+    for (int i = lane; i < CTL_WORDS; i += 32) ctl[i] = 0u;
+  }
 }
 
 // The whole fused linear for one CTA.  MEGA = false: a stand-alone launch (programmatic dependent
@@ -533,6 +552,9 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
     }
     return;
   }
+  // the next launch may be scheduled at once: its CTAs take an SM as soon as one of ours leaves it,
+  // and its griddepcontrol.wait still waits for this whole grid
+  if (!MEGA) pdl_launch_dependents();
   const uint32_t tab_off = HX_TAB_ABS - sbase;
   uint8_t* tab = smem + tab_off;
   float* red = reinterpret_cast<float*>(smem + tab_off - HX_RED_BYTES);
@@ -673,6 +695,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
         __threadfence_block();
         __syncwarp();
         if (lane == 0) s_lr[HX_LR_FLAG] = 1.f;
+        ctl_release_last(mp.ctl(), lane);
       }
     } else if (P.n_lr > 0) {
 #pragma unroll 1
@@ -717,6 +740,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
         __threadfence_block();
         __syncwarp();
         if (lane == 0) s_lr[HX_LR_FLAG] = 1.f;
+        ctl_release_last(mp.ctl(), lane);
       }
     }
     // ---- kink passes: one slot per strip; the counts are made together at the end -------------
@@ -1186,19 +1210,24 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
   // s_lo + w, s_lo + w + 16, ...: a strip inside this CTA's range is finished from the
   // accumulator; one shared with other CTAs adds its part to the strip's global fixed-point sum,
   // and the last CTA to arrive (acq_rel count) finishes it and leaves the sum and count at zero.
-  __syncthreads();
   {
-    const int pos = reinterpret_cast<const int*>(redu)[34];
+    // (the operands of this warp's first strip's epilogue are loaded before the barrier)
+    const int pos = reinterpret_cast<const volatile int*>(redu)[34];
+    StripPre sp0;
+    if (s_lo + warp <= s_hi) sp0 = strip_pre<EPI>(P, strip_info<NMAT>(P, s_lo + warp), lane, pos);
+    __syncthreads();
     unsigned nfin = 0u;
     for (int s = s_lo + warp; s <= s_hi; s += HX_WARPS) {
       const long long first = (long long)s * P.UPS;
       const int cf = hx_cta_of(P.T, P.n_cta, first), cl = hx_cta_of(P.T, P.n_cta, first + P.UPS - 1);
+      const StripInfo si = strip_info<NMAT>(P, s);
+      const StripPre sp = s == s_lo + warp ? sp0 : strip_pre<EPI>(P, si, lane, pos);
       unsigned long long a = lane < width ? lacc[(size_t)(s - s_lo) * width + lane] : 0ull;
       bool mine = true;
       if (cf != cl) {
+        // the acq_rel count releases every lane's addition (ordered before it by the warp barrier)
         unsigned long long* g = mp.gacc() + (size_t)s * width;
         if (lane < width) atomicAdd(g + lane, a);
-        __threadfence();
         __syncwarp();
         unsigned last = 0u;
         if (lane == 0) last = atom_add_acq_rel(&mp.cnt()[s], 1u) + 1u == (unsigned)(cl - cf + 1) ? 1u : 0u;
@@ -1213,7 +1242,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
         }
       }
       if (mine) {
-        finish_value<EPI, NMAT>(P, mp, strip_info<NMAT>(P, s), hx_unfix(a), lane, pos);
+        finish_value<EPI, NMAT>(P, mp, si, hx_unfix(a), lane, pos, sp);
         ++nfin;
       }
     }
@@ -1225,17 +1254,6 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
         __threadfence();
         red_add_release(mp.done(), redu[38] + 1u);
       }
-    }
-  }
-  if (MEGA) return;  // the decode kernel zeroes every phase's control words at the end of the step
-  pdl_launch_dependents();
-  // ---- the last CTA leaves the control words at zero for the next launch ---------------
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    if (atomicAdd(&mp.ctl()[CTL_DONE], 1u) == gridDim.x - 1) {
-      for (int i = 0; i < CTL_WORDS; ++i) mp.ctl()[i] = 0u;
-      __threadfence();
     }
   }
 }
