@@ -96,6 +96,16 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
     cp_async_commit();
   };
   if (t1 > t0) issue(t0, min(AT_TILE, t1 - t0), 0);
+  if (J.fwd_acc != nullptr) {
+    // the next linear's Vt columns of this head group, for the combining CTA: each split prefetches
+    // its share of the 128-byte lines into L2 (rows of fwd_k, GQ*HD fp16 columns from kvh*GQ*HD)
+    const int lines_per_row = GQ * HD * 2 / 128, n_lines = J.fwd_k * lines_per_row;
+    for (int i = split * AT_THREADS + tid; i < n_lines; i += nsplit * AT_THREADS) {
+      const int j = i / lines_per_row, c = i - j * lines_per_row;
+      const uint8_t* a = reinterpret_cast<const uint8_t*>(J.fwd_vt + (size_t)j * J.n_heads * HD + (size_t)kvh * GQ * HD) + c * 128;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+    }
+  }
   if (MEGA) {
     if (tid == 0 && dep != nullptr) wait_geq_abort(dep, dep_target, abort);
     attn_sync<BAR>();
@@ -226,18 +236,22 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
     const int nk = J.fwd_k;
     const int n_in = J.n_heads * HD;  // the next linear's columns
     for (int j0 = 0; j0 < nk; j0 += 16) {
+      uint16_t vv[16][NO];  // every load of the block in flight at once
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const uint16_t* vt = J.fwd_vt + (size_t)(j0 + jj) * n_in + (size_t)kvh * GQ * HD;
+#pragma unroll
+        for (int k = 0; k < NO; ++k) {
+          const int o = tid + k * AT_THREADS;
+          vv[jj][k] = (j0 + jj < nk && o < GQ * HD) ? __ldg(vt + o) : (uint16_t)0;
+        }
+      }
       float pj[16];
 #pragma unroll
       for (int jj = 0; jj < 16; ++jj) {
         float a = 0.f;
-        if (j0 + jj < nk) {
-          const uint16_t* vt = J.fwd_vt + (size_t)(j0 + jj) * n_in + (size_t)kvh * GQ * HD;
 #pragma unroll
-          for (int k = 0; k < NO; ++k) {
-            const int o = tid + k * AT_THREADS;
-            if (o < GQ * HD) a = fmaf(h2f(__ldg(vt + o)), ov[k], a);
-          }
-        }
+        for (int k = 0; k < NO; ++k) a = fmaf(h2f(vv[jj][k]), ov[k], a);
         pj[jj] = warp_sum(a);
       }
       if (lane == 0) {
@@ -330,17 +344,14 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
     cl[gi][si] = lv;
   }
   attn_sync<BAR>();
-  if (tid < GQ) {
-    float M = -INFINITY;
-    for (int sidx = 0; sidx < nact; ++sidx) M = fmaxf(M, cw[tid][sidx]);
-    float L = 0.f;
-    for (int sidx = 0; sidx < nact; ++sidx) {
-      const float ms = cw[tid][sidx];
-      const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
-      cw[tid][sidx] = f;
-      L += cl[tid][sidx] * f;
-    }
-    cL[tid] = L;
+  if (warp < GQ) {  // warp g: head g, lane = split (AT_MAX_SPLITS <= 32)
+    const int g = warp;
+    const float ms = lane < nact ? cw[g][lane] : -INFINITY;
+    const float M = warp_max(ms);
+    const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
+    const float L = warp_sum(lane < nact ? cl[g][lane] * f : 0.f);
+    if (lane < nact) cw[g][lane] = f;
+    if (lane == 0) cL[g] = L;
   }
   attn_sync<BAR>();
   float ov[NO];
@@ -384,7 +395,7 @@ constexpr bool attn_fits() {
 
 
 template <int HD, int GQ>
-__global__ void __launch_bounds__(AT_THREADS) attn_kernel(const __grid_constant__ gsdlq_attn_job_t J, int tps) {
+__global__ void __launch_bounds__(AT_THREADS, 2) attn_kernel(const __grid_constant__ gsdlq_attn_job_t J, int tps) {
   __shared__ AttnSmem<HD, GQ> S;
   attn_body<HD, GQ, false, 0>(J, J.layer, blockIdx.x, blockIdx.y, gridDim.y, tps, threadIdx.x, S, nullptr, 0u,
                               nullptr, nullptr);
