@@ -41,20 +41,25 @@
 // Lane q = 0 then holds group A's dot products for rows g, g+8 and lane q = 1
 // group B's, so each applies its own group's scale.
 //
-// Work split: persistent stream-K.  One CTA per SM: 14 streaming warps and 2
-// helper warps.  The (strip, matrix, unit) iterations of the launch are dealt to
-// the streaming warps as equal contiguous ranges.  A warp's contribution to a
-// 16-row strip (a "segment") goes to a per-strip partial slot; a per-strip
-// counter tells the warp that completes a strip to sum the slots in slot order
-// (deterministic), add the low-rank term and run the epilogue.  The helper
-// warps project a column slice of every Vt row (fixed-point 64-bit atomics, so
-// the sum is order-independent and deterministic) and compute the kink sums of
-// statically assigned strips into one more slot.
+// Work split: persistent stream-K with a CTA-local reduction.  One CTA per SM:
+// 14 streaming warps and 2 helper warps.  The (strip, matrix, unit) iterations
+// of the launch are dealt to the CTAs as equal contiguous ranges and, inside a
+// CTA, to the streaming warps in proportion to their issue share.  Every
+// contribution to a 16-row strip is added in 2^-32 fixed point (64-bit integer
+// sums, so the result does not depend on the order of the additions) into a
+// shared-memory accumulator of the CTA.  The helper warps add the kink sums
+// and the low-rank term of the strips whose first unit lies in their CTA: the
+// low-rank projection tmp_k = S * (Vt . x) is computed once per launch in
+// column slices by all helpers of the grid, or forwarded by the kernel that
+// produced x.  After one CTA barrier a strip inside the CTA's range is
+// finished from shared memory; a strip shared with other CTAs adds its part to
+// a global fixed-point sum and the last CTA to arrive (acq_rel counter)
+// finishes it and leaves the sum and the counter at zero.
 //
-// Launch order (programmatic dependent launch): decode table, the first unit's
-// code and scale loads and L2 prefetches of the helpers' Vt slices are issued
-// BEFORE griddepcontrol.wait, so they overlap the previous kernel; the input x is
-// read only after it.
+// Launch order (programmatic dependent launch): the next launch is released at
+// once; decode table, the first unit's code and scale loads and L2 prefetches
+// of the helpers' Vt slices are issued BEFORE griddepcontrol.wait, so they
+// overlap the previous kernel; the input x is read only after it.
 #pragma once
 #include <cuda.h>  // CUtensorMap
 

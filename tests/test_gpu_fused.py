@@ -248,3 +248,22 @@ def test_workspace_shared_across_shapes(env, restated, rng):
             torch.cuda.synchronize()
             assert rel_err(y.cpu().numpy(), yr) < MATVEC_TOL
             assert int(ws.abs().sum().item()) == 0
+
+
+@pytest.mark.skipif(__import__("os").environ.get("GSDLQ_TMA") == "1", reason="already running under the TMA ring")
+def test_tma_ring_parity_in_subprocess(cuda_lib):
+    """The opt-in TMA-ring streaming (GSDLQ_TMA=1, read once per process) passes the fused-linear
+    parity cases that take full units, and the persistent decode step in its TMA mode matches
+    per-operation decode."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, GSDLQ_TMA="1")
+    cmd = [sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+           os.path.join(here, "test_gpu_fused.py") + "::test_rmsnorm_swiglu",
+           os.path.join(here, "test_gpu_fused.py") + "::test_embed_qkv_rope_kv",
+           os.path.join(here, "test_gpu_fused.py") + "::test_workspace_shared_across_shapes",
+           os.path.join(here, "test_gpu_model.py") + "::test_fused_step_matches_per_op_launches"]
+    r = subprocess.run(cmd, env=env, cwd=os.path.dirname(here), capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
