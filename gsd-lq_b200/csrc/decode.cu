@@ -328,10 +328,10 @@ extern "C" int gsdlq_decode_plan_create(const gsdlq_decode_desc_t* d, gsdlq_deco
     if (st == GSDLQ_OK) st = hexmv_check_io(H);
     if (st != GSDLQ_OK) break;
     if (H.n_cta > grid) st = GSDLQ_ERR_UNSUPPORTED;
-    // the stream mode of every linear must agree: 2 the TMA ring (opt-in), 1 16-byte loads, 0 any
+    // one stream mode serves every linear: 2 the TMA ring (opt-in), 1 16-byte loads (full units),
+    // 0 any shape; the kernel takes the lowest mode any linear needs
     const int f = hexmv_full(H) ? (hexmv_tma_ok(H) ? 2 : 1) : 0;
-    if (full < 0) full = f;
-    if (f != full) st = GSDLQ_ERR_UNSUPPORTED;  // one kernel per stream shape
+    full = full < 0 ? f : std::min(full, f);
     ws_need = std::max(ws_need, hexmv_ws_bytes_for(H.n_strips, H.nmat));
     ovf_max = std::max(ovf_max, H.ovf_bytes);
     lacc_max = std::max(lacc_max, hx_lacc_bytes(H));
@@ -376,6 +376,9 @@ extern "C" int gsdlq_decode_plan_create(const gsdlq_decode_desc_t* d, gsdlq_deco
   if (st == GSDLQ_OK && (!A0.q || !A0.k_cache || !A0.v_cache || !A0.out || !A0.pos_dev || A0.max_seq <= 0 ||
                          ((reinterpret_cast<uintptr_t>(A0.k_cache) | reinterpret_cast<uintptr_t>(A0.v_cache)) & 15u)))
     st = GSDLQ_ERR_INVALID;
+  // not every attention shape has every stream mode built (the TMA ring only the most common
+  // one): take the next lower mode that is
+  while (st == GSDLQ_OK && full > 0 && mk_kernel(hd, gq, full) == nullptr) --full;
   const KernelFn fn = st == GSDLQ_OK ? mk_kernel(hd, gq, full) : nullptr;
   if (st == GSDLQ_OK && fn == nullptr) st = GSDLQ_ERR_UNSUPPORTED;
   if (st != GSDLQ_OK) {
