@@ -63,6 +63,16 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
   constexpr int DP = HD / 2;                // dimension pairs
   constexpr int HS = AT_THREADS / DP;       // token groups of the P.V mapping
   constexpr int NO = (GQ * HD + AT_THREADS - 1) / AT_THREADS;  // outputs per thread
+  constexpr int CQ = CH / 4;                // 16-byte chunks of a K row per score thread
+  // Chunk of a K row that score thread quarter qd reads at step cc.  The 8 threads of a
+  // quarter-warp phase are two tokens (rows 16 bytes apart modulo 128) x four quarters; this
+  // order puts the four quarters 32 bytes apart, so the 8 reads cover 8 different 16-byte bank
+  // groups (no conflict).  Every quarter still covers CQ distinct chunks and all quarters all CH.
+  auto kchunk = [](int qd, int cc) -> int {
+    if constexpr (CQ == 4) return 2 * qd + 8 * (cc & 1) + (cc >> 1);
+    else if constexpr (CQ == 2) return 2 * qd + cc;
+    else return qd * CQ + cc;
+  };
   uint8_t* skv = S.skv;
   uint8_t* sk = skv;
   uint8_t* sv = skv + AT_TILE * ROWB;
@@ -114,8 +124,13 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
   }
   if (!pos_ok && tid == 0 && kvh == 0 && split == 0) raise_flag(GSDLQ_FLAG_BAD_POS);
   if (t1 > t0) issue(t0, min(AT_TILE, t1 - t0), 1);
-  // .cg: in the decode kernel q was written earlier in the same launch
-  for (int i = tid; i < GQ * HD; i += AT_THREADS) sq[i] = __ldcg(J.q + (size_t)kvh * GQ * HD + i);
+  // q is staged with its 8-float chunks permuted: slot 4 * cc + qd holds the chunk that score
+  // thread quarter qd takes at step cc (kchunk), so the four quarters' reads of one step fall in
+  // four different bank groups.  (.cg: in the decode kernel q was written earlier in the launch.)
+  for (int i = tid; i < GQ * HD; i += AT_THREADS) {
+    const int h = i / HD, r = i - h * HD, slot = r >> 3;
+    sq[i] = __ldcg(J.q + (size_t)kvh * GQ * HD + h * HD + kchunk(slot & 3, slot >> 2) * 8 + (r & 7));
+  }
   if (tid < GQ) {
     s_m[tid] = -INFINITY;
     s_l[tid] = 0.f;
@@ -138,14 +153,15 @@ __device__ __forceinline__ void attn_body(const gsdlq_attn_job_t& J, int layer, 
       for (int h = 0; h < GQ; ++h) s[h] = 0.f;
       if (j < nt) {
 #pragma unroll
-        for (int c = qd * (CH / 4); c < (qd + 1) * (CH / 4); ++c) {
+        for (int cc = 0; cc < CQ; ++cc) {
+          const int c = kchunk(qd, cc);
           const uint4 kr = *reinterpret_cast<const uint4*>(sk + j * ROWB + c * 16);
           const float k0 = h2f(kr.x & 0xffffu), k1 = h2f(kr.x >> 16), k2 = h2f(kr.y & 0xffffu), k3 = h2f(kr.y >> 16);
           const float k4 = h2f(kr.z & 0xffffu), k5 = h2f(kr.z >> 16), k6 = h2f(kr.w & 0xffffu), k7 = h2f(kr.w >> 16);
 #pragma unroll
           for (int h = 0; h < GQ; ++h) {
-            const float4 qa = *reinterpret_cast<const float4*>(sq + h * HD + c * 8);
-            const float4 qb = *reinterpret_cast<const float4*>(sq + h * HD + c * 8 + 4);
+            const float4 qa = *reinterpret_cast<const float4*>(sq + h * HD + (4 * cc + qd) * 8);
+            const float4 qb = *reinterpret_cast<const float4*>(sq + h * HD + (4 * cc + qd) * 8 + 4);
             s[h] = fmaf(qa.x, k0, s[h]);
             s[h] = fmaf(qa.y, k1, s[h]);
             s[h] = fmaf(qa.z, k2, s[h]);

@@ -8,6 +8,7 @@
 //   pack_lattice                                the packer's lattice step (no reference counterpart)
 #include <cmath>
 #include <cstdio>
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 #include <vector>
@@ -16,6 +17,7 @@
 
 #include "common.cuh"
 #include "attn_dev.cuh"
+#include "attn_cluster.cuh"
 
 namespace gsdlq {
 
@@ -145,6 +147,64 @@ static cudaError_t attention_launch_hd(const cudaLaunchConfig_t& cfg, const gsdl
   }
 }
 
+// The cluster kernel (attn_cluster.cuh) serves every stand-alone launch unless GSDLQ_ATTN_CLUSTER=0
+// (read once per process) selects the split/counter kernel (attn_kernel).
+static bool attn_cluster_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("GSDLQ_ATTN_CLUSTER");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+template <int HD, int GQ>
+static cudaError_t attention_cluster_launch_t(const gsdlq_attn_job_t& J, cudaStream_t s) {
+  using Lo = AcLayout<HD, GQ>;
+  if constexpr (Lo::BYTES > 227 * 1024) {
+    return cudaErrorNotSupported;
+  } else {
+    static std::atomic<bool> smem_set[64];  // per device: the dynamic shared-memory opt-in is done
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 64) return cudaErrorNotSupported;
+    if (!smem_set[dev].load(std::memory_order_acquire)) {
+      e = cudaFuncSetAttribute(attn_cluster_kernel<HD, GQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lo::BYTES);
+      if (e != cudaSuccess) return e;
+      smem_set[dev].store(true, std::memory_order_release);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(AC_CL, J.n_kv_heads);
+    cfg.blockDim = dim3(AC_THREADS);
+    cfg.dynamicSmemBytes = Lo::BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = AC_CL;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<HD, GQ>, J);
+  }
+}
+
+template <int HD>
+static cudaError_t attention_cluster_launch_hd(const gsdlq_attn_job_t& J, cudaStream_t s, int gq) {
+  switch (gq) {
+    case 1: return attention_cluster_launch_t<HD, 1>(J, s);
+    case 2: return attention_cluster_launch_t<HD, 2>(J, s);
+    case 3: return attention_cluster_launch_t<HD, 3>(J, s);
+    case 4: return attention_cluster_launch_t<HD, 4>(J, s);
+    case 5: return attention_cluster_launch_t<HD, 5>(J, s);
+    case 6: return attention_cluster_launch_t<HD, 6>(J, s);
+    case 7: return attention_cluster_launch_t<HD, 7>(J, s);
+    default: return attention_cluster_launch_t<HD, 8>(J, s);
+  }
+}
+
 static int attention_launch(const gsdlq_attn_job_t& J, cudaStream_t s) {
   if (!J.q || !J.k_cache || !J.v_cache || !J.out || !J.partial || !J.workspace) return GSDLQ_ERR_INVALID;
   // K/V rows are read in 16-byte chunks
@@ -158,6 +218,16 @@ static int attention_launch(const gsdlq_attn_job_t& J, cudaStream_t s) {
   if (!J.pos_dev && (J.pos_val < 0 || J.pos_val >= J.max_seq)) return GSDLQ_ERR_INVALID;
   if (J.fwd_acc && (J.fwd_k <= 0 || J.fwd_k > 48 || !J.fwd_vt || (reinterpret_cast<uintptr_t>(J.fwd_acc) & 7u)))
     return GSDLQ_ERR_INVALID;
+  if (J.head_dim != 128 && J.head_dim != 64 && J.head_dim != 32) return GSDLQ_ERR_UNSUPPORTED;
+  // the cluster kernel copies the forwarded Vt slice in 4-byte pieces
+  if (attn_cluster_enabled() && !(J.fwd_acc && (reinterpret_cast<uintptr_t>(J.fwd_vt) & 3u))) {
+    cudaError_t e;
+    if (J.head_dim == 128) e = attention_cluster_launch_hd<128>(J, s, gq);
+    else if (J.head_dim == 64) e = attention_cluster_launch_hd<64>(J, s, gq);
+    else e = attention_cluster_launch_hd<32>(J, s, gq);
+    if (e == cudaSuccess) return GSDLQ_OK;
+    if (e != cudaErrorNotSupported) return record_cuda_error(e);
+  }
   const int tps = attn_tokens_per_split(J.max_seq);
   const int nsplit = (J.max_seq + tps - 1) / tps;
   cudaLaunchConfig_t cfg = {};

@@ -175,7 +175,8 @@ def test_rope_store_bitexact(env, restated, rng, interleaved, nh, nkv, hd):
     assert np.array_equal(vd.cpu().numpy().view(np.uint16), vc)
 
 
-@pytest.mark.parametrize("nh,nkv,hd,S", [(32, 8, 128, 2048), (12, 2, 128, 2048), (32, 32, 64, 256), (4, 4, 128, 100)])
+@pytest.mark.parametrize("nh,nkv,hd,S", [(32, 8, 128, 2048), (12, 2, 128, 2048), (32, 32, 64, 256), (4, 4, 128, 100),
+                                         (64, 8, 128, 4096), (8, 4, 32, 300), (16, 2, 64, 1000)])
 def test_gqa_attention(env, restated, rng, nh, nkv, hd, S):
     ops, L = env
     Lc = 2
@@ -189,6 +190,51 @@ def test_gqa_attention(env, restated, rng, nh, nkv, hd, S):
         r = np.zeros(nh * hd, np.float32)
         restated.gqa_attention(_p(q), _p(kc), _p(vc), _p(r), 1, pos, nh, nkv, hd, S, 1 / math.sqrt(hd))
         assert rel_err(o.cpu().numpy(), r) < 1e-5, pos
+
+
+@pytest.mark.parametrize("nh,nkv,hd,S,page,fk", [(32, 8, 128, 2048, 16, 16), (12, 2, 128, 700, 64, 40),
+                                                  (16, 16, 64, 512, 32, 0)])
+def test_attention_job_paged_and_forward(env, restated, rng, nh, nkv, hd, S, page, fk):
+    """gsdlq_attention over a paged cache (shuffled block table) against the oracle on the same rows
+    laid out contiguously, and the low-rank forward sum_c Vt[j][c] * out[c] it adds (2^-32 fixed point)."""
+    ops, L = env
+    kc = (rng.standard_normal((1, S, nkv, hd)) * 2).astype(np.float16).view(np.uint16)
+    vc = rng.standard_normal((1, S, nkv, hd)).astype(np.float16).view(np.uint16)
+    n_pages = (S + page - 1) // page
+    perm = rng.permutation(n_pages + 3)[:n_pages].astype(np.int32)
+    pool_k = np.zeros((n_pages + 3, page, nkv, hd), np.uint16)
+    pool_v = np.zeros_like(pool_k)
+    for t in range(S):
+        pool_k[perm[t // page], t % page] = kc[0, t]
+        pool_v[perm[t // page], t % page] = vc[0, t]
+    pk, pv = dev(pool_k.view(np.int16)), dev(pool_v.view(np.int16))
+    bt = dev(perm)
+    pb, wb = ops.attention_ws_size(nh, nkv, hd, S)
+    part = torch.zeros(pb // 4 + 1, device="cuda")
+    wsp = torch.zeros(wb // 4 + 1, dtype=torch.int32, device="cuda")
+    vt = (rng.standard_normal((max(fk, 1), nh * hd)) * 0.05).astype(np.float16)
+    vtd = dev(vt.view(np.int16))
+    for pos in sorted({0, 5, page - 1, page, S // 3, S - 1}):
+        q = rng.standard_normal(nh * hd).astype(np.float32)
+        qd = dev(q)
+        o = torch.zeros(nh * hd, device="cuda")
+        acc = torch.zeros(max(fk, 1), dtype=torch.int64, device="cuda")
+        j = L.AttnJob(q=qd.data_ptr(), k_cache=pk.data_ptr(), v_cache=pv.data_ptr(), out=o.data_ptr(), pos_dev=None,
+                      pos_val=pos, layer=0, n_heads=nh, n_kv_heads=nkv, head_dim=hd, max_seq=S,
+                      sm_scale=1 / math.sqrt(hd), block_table=bt.data_ptr(), page_size=page,
+                      partial=part.data_ptr(), workspace=wsp.data_ptr(),
+                      fwd_vt=vtd.data_ptr() if fk else None, fwd_k=fk, fwd_acc=acc.data_ptr() if fk else None)
+        ops.attention(j)
+        torch.cuda.synchronize()
+        r = np.zeros(nh * hd, np.float32)
+        restated.gqa_attention(_p(q), _p(kc), _p(vc), _p(r), 0, pos, nh, nkv, hd, S, 1 / math.sqrt(hd))
+        got = o.cpu().numpy()
+        assert rel_err(got, r) < 1e-5, pos
+        if fk:
+            want = vt.astype(np.float64) @ r.astype(np.float64)
+            fwd = acc.cpu().numpy().astype(np.float64) / 2.0 ** 32
+            assert np.max(np.abs(fwd - want)) < 1e-4 * (np.max(np.abs(want)) + 1e-3), pos
+        assert int(wsp.abs().sum().item()) == 0
 
 
 def test_argmax_rules(env, oracle_mod):
@@ -221,3 +267,21 @@ def test_pack_lattice_bitexact_vs_numpy(env, radius):
     assert np.array_equal(c.cpu().numpy(), codes)
     assert np.array_equal(s.cpu().numpy().view(np.uint16), sb)
     assert np.array_equal(r.cpu().numpy(), e)
+
+
+@pytest.mark.skipif(__import__("os").environ.get("GSDLQ_ATTN_CLUSTER") == "0",
+                    reason="already running the split/counter attention kernel")
+def test_split_counter_attention_in_subprocess(cuda_lib):
+    """GSDLQ_ATTN_CLUSTER=0 (read once per process) selects the split/counter attention kernel
+    instead of the cluster kernel; the attention parity cases and the golden model pass with it."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, GSDLQ_ATTN_CLUSTER="0")
+    cmd = [sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+           os.path.join(here, "test_gpu_kernels.py") + "::test_gqa_attention",
+           os.path.join(here, "test_gpu_kernels.py") + "::test_attention_job_paged_and_forward",
+           os.path.join(here, "test_gpu_model.py") + "::test_golden_tiny"]
+    r = subprocess.run(cmd, env=env, cwd=os.path.dirname(here), capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
