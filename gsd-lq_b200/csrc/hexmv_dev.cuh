@@ -446,6 +446,7 @@ __device__ float strip_epilogue(const HexmvParams& P, const StripInfo& si, float
 // slot sum so that the loads overlap it.
 struct FwdSlice {
   uint4 a[2], b[2];
+  float w;  // lanes 0-15: the next linear's norm weight of row rbase + lane (1 without one)
 };
 __device__ __forceinline__ int fwd_total(const gsdlq_linear_job_t& J) { return J.fwd_k[0] + J.fwd_k[1] + J.fwd_k[2]; }
 __device__ __forceinline__ const uint16_t* fwd_row(const gsdlq_linear_job_t& J, int jl, int n_out) {
@@ -456,6 +457,8 @@ __device__ __forceinline__ const uint16_t* fwd_row(const gsdlq_linear_job_t& J, 
 __device__ __forceinline__ FwdSlice fwd_load(const gsdlq_linear_job_t& J, int rbase, int n_out, int lane) {
   FwdSlice f;
   const int nk = fwd_total(J);
+  const int row = rbase + (lane & 15);
+  f.w = (J.fwd_norm_w != nullptr && lane < 16 && row < n_out) ? __ldg(J.fwd_norm_w + row) : 1.f;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int jl = lane + 32 * h;
@@ -482,8 +485,7 @@ __device__ __forceinline__ float fwd_dot16(const uint4& a, const uint4& b, float
 __device__ __forceinline__ void fwd_apply(const gsdlq_linear_job_t& J, const FwdSlice& f, int rbase, int n_out, float out,
                                           int lane) {
   const int row = rbase + (lane & 15);
-  float o = (lane < 16 && row < n_out) ? out : 0.f;
-  if (J.fwd_norm_w != nullptr && lane < 16 && row < n_out) o *= __ldg(J.fwd_norm_w + row);
+  const float o = (lane < 16 && row < n_out) ? out * f.w : 0.f;
   const int nk = fwd_total(J);
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -996,19 +998,30 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       *reinterpret_cast<uint32_t*>(smem + off) = h;
       *reinterpret_cast<uint32_t*>(smem + off + 16) = l;
     };
-    // the first XR pairs of each staging thread are loaded in one batch and stay in registers
     constexpr int XR = 8;
-    float2 xv[XR], wv[XR];
+    if (!normed) {
+      // a plain input: batches of 2 XR pairs, so the 14336-wide down-projection input is staged
+      // with one round of loads
+      for (int p0 = tid; p0 < NP; p0 += 2 * XR * NST) {
+        float2 t[2 * XR];
 #pragma unroll
-    for (int k = 0; k < XR; ++k) {
-      const int p = tid + k * NST;
-      if (p < NP) {
-        xv[k] = load_x(p);
-        wv[k] = load_w(p);
+        for (int k = 0; k < 2 * XR; ++k) t[k] = (p0 + k * NST < NP) ? load_x(p0 + k * NST) : make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 2 * XR; ++k)
+          if (p0 + k * NST < NP) stage(p0 + k * NST, t[k].x, t[k].y, make_float2(1.f, 1.f), 1.f);
       }
-    }
-    float inv = 1.f;
-    if (normed) {
+      if (tid == 0) red[37] = 1.f;
+    } else {
+      // the first XR pairs of each staging thread are loaded in one batch and stay in registers
+      float2 xv[XR], wv[XR];
+#pragma unroll
+      for (int k = 0; k < XR; ++k) {
+        const int p = tid + k * NST;
+        if (p < NP) {
+          xv[k] = load_x(p);
+          wv[k] = load_w(p);
+        }
+      }
       float ss = 0.f;
 #pragma unroll
       for (int k = 0; k < XR; ++k)
@@ -1023,29 +1036,29 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       ss = warp_sum(ss);
       if (lane == 0) red[1 + warp] = ss;
       named_bar_sync(1, NST);
-      float t = 0.f;
-      for (int k = 0; k < HX_STREAM; ++k) t += red[1 + k];  // every thread: no second barrier
-      inv = 1.0f / sqrtf(t / (float)C + J.eps);             // gsd_lq_cpu_engine.c:78
-    }
-    if (tid == 0) red[37] = inv;  // for a forwarded projection's scale (read after barrier 2)
-#pragma unroll
-    for (int k = 0; k < XR; ++k) {
-      const int p = tid + k * NST;
-      if (p < NP) stage(p, xv[k].x, xv[k].y, wv[k], inv);
-    }
-    for (int p0 = tid + XR * NST; p0 < NP; p0 += XR * NST) {
+      float tot = 0.f;
+      for (int k = 0; k < HX_STREAM; ++k) tot += red[1 + k];  // every thread: no second barrier
+      const float inv = 1.0f / sqrtf(tot / (float)C + J.eps);  // gsd_lq_cpu_engine.c:78
+      if (tid == 0) red[37] = inv;  // for a forwarded projection's scale (read after barrier 2)
 #pragma unroll
       for (int k = 0; k < XR; ++k) {
-        const int p = p0 + k * NST;
-        if (p < NP) {
-          xv[k] = load_x(p);
-          wv[k] = load_w(p);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < XR; ++k) {
-        const int p = p0 + k * NST;
+        const int p = tid + k * NST;
         if (p < NP) stage(p, xv[k].x, xv[k].y, wv[k], inv);
+      }
+      for (int p0 = tid + XR * NST; p0 < NP; p0 += XR * NST) {
+#pragma unroll
+        for (int k = 0; k < XR; ++k) {
+          const int p = p0 + k * NST;
+          if (p < NP) {
+            xv[k] = load_x(p);
+            wv[k] = load_w(p);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < XR; ++k) {
+          const int p = p0 + k * NST;
+          if (p < NP) stage(p, xv[k].x, xv[k].y, wv[k], inv);
+        }
       }
     }
     // pairs past the row end of the last unit read zero activations
