@@ -97,7 +97,10 @@ int hexmv_plan(HexmvParams& P) {
   if (P.T >= (1LL << 31)) return GSDLQ_ERR_UNSUPPORTED;  // unit indices are 32-bit in the kernel
   // one CTA per SM (fewer when there are fewer units); a range of ceil(T / n_cta) units touches at
   // most ceil(that / UPS) + 1 strips, the rows of each CTA's shared-memory accumulator
-  P.n_cta = (int)std::min<long long>(num_sms(), P.T);
+  // at least ceil(UPS / 6) units a CTA, so that a strip spans at most 7 CTAs (the shared-strip
+  // words count up to 7 contributions)
+  const long long upc_min = (P.UPS + 5) / 6;
+  P.n_cta = (int)std::max<long long>(1, std::min<long long>(num_sms(), P.T / upc_min));
   const long long upc = (P.T + P.n_cta - 1) / P.n_cta;
   P.n_local = (int)((upc + P.UPS - 1) / P.UPS) + 1;
   const int grid = P.n_cta;

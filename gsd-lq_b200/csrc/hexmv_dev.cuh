@@ -174,6 +174,15 @@ __device__ __forceinline__ float hx_unfix(unsigned long long a) {
   return (float)((double)(long long)a * (1.0 / 4294967296.0));
 }
 
+// Strips shared between CTAs.  Every CTA holding units of such a strip adds its fixed-point part
+// plus HX_SH_ONE to the strip's global word of each row with one returning atomic per word.  A word
+// thus carries the number of contributions in its top bits (at most 7, which the planner
+// guarantees) and their sum below (|sum| < 2^59, far beyond the +-2^22 value range): the CTA whose
+// addition completes word 0 finishes the strip, from the values its own atomics returned, without
+// a separate counter or a second round trip.
+constexpr unsigned long long HX_SH_ONE = 1ull << 60;
+__device__ __forceinline__ unsigned hx_sh_count(unsigned long long w) { return (unsigned)((w + (HX_SH_ONE >> 1)) >> 60); }
+
 inline size_t hexmv_ws_bytes_for(int n_strips, int nmat) {
   return ((sizeof(unsigned) * (CTL_WORDS + (size_t)n_strips) + 15) & ~size_t(15)) +
          sizeof(unsigned long long) * (size_t)n_strips * nmat * 16 + 256;
@@ -565,8 +574,9 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
   const uint32_t tab_off = HX_TAB_ABS - sbase;
   uint8_t* tab = smem + tab_off;
   float* red = reinterpret_cast<float*>(smem + tab_off - HX_RED_BYTES);
-  // [1..16] warp sums, [32] [33] zero words, [34] position; s_lr: [0..48) tmp_k, [HX_LR_FLAG] ready;
-  // then 16 kink row sums per streaming warp
+  // [1..16] warp sums, [32] [33] zero words, [34] position, [35] radius (decode kernel), [37] 1/rms,
+  // [38] finished strips; s_lr: [0..48) tmp_k, [HX_LR_FLAG] ready; then 16 kink row sums per
+  // streaming warp
   volatile float* s_lr = red + 64;
   float* s_ks = red + 128 + 16 * warp;
   // (x[2p], x[2p+1]) recovered from the staged splits (hi + lo: about 16 significant bits)
@@ -826,8 +836,9 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
     if (lane < 16) s_ks[lane] = 0.f;
     const bool streamer = cb1 > cb0;
     const long long n_c = cb1 - cb0;
-    const int u0 = (int)(cb0 + n_c * hx_lp(warp) / hx_lp(HX_STREAM));
-    const int u1 = (int)(cb0 + n_c * hx_lp(warp + 1) / hx_lp(HX_STREAM));
+    // (unit indices and a CTA's range fit 32 bits: the planner keeps T below 2^31)
+    const int u0 = (int)cb0 + (int)n_c * hx_lp(warp) / hx_lp(HX_STREAM);
+    const int u1 = (int)cb0 + (int)n_c * hx_lp(warp + 1) / hx_lp(HX_STREAM);
     // cursor (strip, matrix in strip, unit column) of the next unit to load, and its pointers
     int ns = u0 / P.UPS;
     int nm = (u0 - ns * P.UPS) / P.GU;
@@ -1069,7 +1080,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       *reinterpret_cast<uint32_t*>(smem + off + 16) = 0u;
     }
     for (int i = tid; i < P.n_local * width; i += NST) lacc[i] = 0ull;
-    if (tid == 0) redu[38] = 0u;        // strips this CTA finished (decode kernel)
+    if (tid == 0) redu[38] = 0u;  // strips this CTA finished (decode kernel)
     named_bar_sync(1, NST);             // table, splits and accumulator ready for the streaming warps
     named_bar_arrive(2, HX_THREADS);    // ... and released to the helper warps
     if (MEGA && tid == 0) reinterpret_cast<int*>(redu)[35] = J.mat[0].radius;  // every streaming warp has read the old value
@@ -1241,28 +1252,32 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       const StripInfo si = strip_info<NMAT>(P, s);
       const StripPre sp = s == s_lo + warp ? sp0 : strip_pre<EPI>(P, si, lane, pos);
       unsigned long long a = lane < width ? lacc[(size_t)(s - s_lo) * width + lane] : 0ull;
-      bool mine = true;
       if (cf != cl) {
-        // the acq_rel count releases every lane's addition (ordered before it by the warp barrier)
-        unsigned long long* g = mp.gacc() + (size_t)s * width;
-        if (lane < width) atomicAdd(g + lane, a);
-        __syncwarp();
-        unsigned last = 0u;
-        if (lane == 0) last = atom_add_acq_rel(&mp.cnt()[s], 1u) + 1u == (unsigned)(cl - cf + 1) ? 1u : 0u;
-        mine = __shfl_sync(0xffffffffu, last, 0) != 0u;
-        if (mine) {
-          __syncwarp();  // lane 0's acquire orders the other lanes' reads
-          if (lane < width) {
-            a = __ldcg(g + lane);
-            g[lane] = 0ull;
+        unsigned long long* g = mp.gacc() + (size_t)s * width + lane;
+        const unsigned total = (unsigned)(cl - cf + 1);
+        unsigned long long w = 0ull;
+        if (lane < width) w = atomicAdd(g, a + HX_SH_ONE) + a + HX_SH_ONE;  // the word after this addition
+        if (__shfl_sync(0xffffffffu, hx_sh_count(w), 0) != total) continue;  // another CTA completes it
+        if (lane < width) {
+          // the other CTAs' additions to this lane's word were issued with their word-0 additions:
+          // wait (bounded) for any still in flight
+          unsigned long long t0 = 0ull;
+          for (int it = 0; hx_sh_count(w) < total; ++it) {
+            asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(g) : "memory");
+            unsigned long long t1;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+            if (it == 0) t0 = t1;
+            if (t1 - t0 > 1000000000ull) {
+              raise_flag(GSDLQ_FLAG_TIMEOUT);
+              break;
+            }
           }
-          if (lane == 0) mp.cnt()[s] = 0u;
+          a = w - (unsigned long long)total * HX_SH_ONE;
+          *g = 0ull;  // the workspace is zero again for its next launch
         }
       }
-      if (mine) {
-        finish_value<EPI, NMAT>(P, mp, si, hx_unfix(a), lane, pos, sp);
-        ++nfin;
-      }
+      finish_value<EPI, NMAT>(P, mp, si, hx_unfix(a), lane, pos, sp);
+      ++nfin;
     }
     if (MEGA) {
       // one release per CTA: its finished strips and 1 for the CTA (it has read its input)
