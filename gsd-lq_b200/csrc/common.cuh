@@ -182,7 +182,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
 __device__ __forceinline__ void named_bar_arrive(int id, int threads) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
-// ---- mbarrier + TMA (bulk tensor copies into this CTA's shared memory; no multicast) ----------
+// ---- mbarrier + TMA (bulk tensor copies into this CTA's own shared memory) -------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
