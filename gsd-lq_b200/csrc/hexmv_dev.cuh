@@ -699,15 +699,15 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
              a3.x * h2f(raw.w & 0xffffu) + a3.y * h2f(raw.w >> 16);
     };
     if (P.n_lr > 0 && J.lr_forwarded) {
-      // the previous launch added every row's term: scale by this launch's 1/rms and S
+      // the previous launch added every row's term: scale by S (the 1/rms of a normed input is applied
+      // to the finished strip values)
       if (warp == HX_WARPS - 1) {
-        const float sc = (mp.input_mode() != GSDLQ_IN_PLAIN) ? red[37] : 1.f;
         const unsigned long long* acc = reinterpret_cast<const unsigned long long*>(mp.ctl() + CTL_TMPK);
         for (int jl = lane; jl < P.n_lr; jl += 32) {
           int m = 0, j = jl;
           while (m < J.n_mat - 1 && j >= J.mat[m].k_dim) j -= J.mat[m].k_dim, ++m;
           const double d = (double)(long long)__ldcg(acc + jl) * (1.0 / 4294967296.0);
-          s_lr[jl] = (float)d * sc * __ldg(mp.mat(m).S + j);
+          s_lr[jl] = (float)d * __ldg(mp.mat(m).S + j);
         }
         __threadfence_block();
         __syncwarp();
@@ -1021,56 +1021,24 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
         for (int k = 0; k < 2 * XR; ++k)
           if (p0 + k * NST < NP) stage(p0 + k * NST, t[k].x, t[k].y, make_float2(1.f, 1.f), 1.f);
       }
-      if (tid == 0) red[37] = 1.f;
     } else {
-      // the first XR pairs of each staging thread are loaded in one batch and stay in registers
-      float2 xv[XR], wv[XR];
-#pragma unroll
-      for (int k = 0; k < XR; ++k) {
-        const int p = tid + k * NST;
-        if (p < NP) {
-          xv[k] = load_x(p);
-          wv[k] = load_w(p);
-        }
-      }
+      // RMSNorm is linear in its scale: the splits of w * x are staged at once and the finished strip
+      // values (lattice, kink and low-rank terms alike) are multiplied by 1/rms, so the sum of squares
+      // stays off the staging path; its per-warp parts are summed after the staging barrier
       float ss = 0.f;
-#pragma unroll
-      for (int k = 0; k < XR; ++k)
-        if (tid + k * NST < NP) ss += xv[k].x * xv[k].x + xv[k].y * xv[k].y;
-      for (int p0 = tid + XR * NST; p0 < NP; p0 += XR * NST) {
-        float2 t[XR];
-#pragma unroll
-        for (int k = 0; k < XR; ++k) t[k] = (p0 + k * NST < NP) ? load_x(p0 + k * NST) : make_float2(0.f, 0.f);
-#pragma unroll
-        for (int k = 0; k < XR; ++k) ss += t[k].x * t[k].x + t[k].y * t[k].y;
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) red[1 + warp] = ss;
-      named_bar_sync(1, NST);
-      float tot = 0.f;
-      for (int k = 0; k < HX_STREAM; ++k) tot += red[1 + k];  // every thread: no second barrier
-      const float inv = 1.0f / sqrtf(tot / (float)C + J.eps);  // gsd_lq_cpu_engine.c:78
-      if (tid == 0) red[37] = inv;  // for a forwarded projection's scale (read after barrier 2)
-#pragma unroll
-      for (int k = 0; k < XR; ++k) {
-        const int p = tid + k * NST;
-        if (p < NP) stage(p, xv[k].x, xv[k].y, wv[k], inv);
-      }
-      for (int p0 = tid + XR * NST; p0 < NP; p0 += XR * NST) {
+      for (int p0 = tid; p0 < NP; p0 += XR * NST) {
 #pragma unroll
         for (int k = 0; k < XR; ++k) {
           const int p = p0 + k * NST;
           if (p < NP) {
-            xv[k] = load_x(p);
-            wv[k] = load_w(p);
+            const float2 xv = load_x(p), wv = load_w(p);
+            ss = fmaf(xv.x, xv.x, fmaf(xv.y, xv.y, ss));
+            stage(p, xv.x, xv.y, wv, 1.f);
           }
         }
-#pragma unroll
-        for (int k = 0; k < XR; ++k) {
-          const int p = p0 + k * NST;
-          if (p < NP) stage(p, xv[k].x, xv[k].y, wv[k], inv);
-        }
       }
+      ss = warp_sum(ss);
+      if (lane == 0) red[1 + warp] = ss;
     }
     // pairs past the row end of the last unit read zero activations
     for (int p = NP + tid; p < P.GU * HX_UB; p += NST) {
@@ -1083,6 +1051,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
     if (tid == 0) redu[38] = 0u;  // strips this CTA finished (decode kernel)
     named_bar_sync(1, NST);             // table, splits and accumulator ready for the streaming warps
     named_bar_arrive(2, HX_THREADS);    // ... and released to the helper warps
+
     if (MEGA && tid == 0) reinterpret_cast<int*>(redu)[35] = J.mat[0].radius;  // every streaming warp has read the old value
     const int pos = reinterpret_cast<const int*>(redu)[34];
     if (streamer) {
@@ -1245,6 +1214,14 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
     StripPre sp0;
     if (s_lo + warp <= s_hi) sp0 = strip_pre<EPI>(P, strip_info<NMAT>(P, s_lo + warp), lane, pos);
     __syncthreads();
+    // the scale of the finished strip values: 1/rms of a normed input (the staging threads' sums of
+    // squares are in the reduction words since the staging barrier), else 1
+    float v_scale = 1.f;
+    if (mp.input_mode() != GSDLQ_IN_PLAIN) {
+      float tot = 0.f;
+      for (int k = 0; k < HX_STREAM; ++k) tot += red[1 + k];
+      v_scale = 1.0f / sqrtf(tot / (float)C + J.eps);  // gsd_lq_cpu_engine.c:78
+    }
     unsigned nfin = 0u;
     for (int s = s_lo + warp; s <= s_hi; s += HX_WARPS) {
       const long long first = (long long)s * P.UPS;
@@ -1276,7 +1253,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
           *g = 0ull;  // the workspace is zero again for its next launch
         }
       }
-      finish_value<EPI, NMAT>(P, mp, si, hx_unfix(a), lane, pos, sp);
+      finish_value<EPI, NMAT>(P, mp, si, hx_unfix(a) * v_scale, lane, pos, sp);
       ++nfin;
     }
     if (MEGA) {
