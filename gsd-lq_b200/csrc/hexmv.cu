@@ -136,14 +136,14 @@ bool hexmv_full(const HexmvParams& P) {
   return true;
 }
 
-template <int EPI, bool FULL, bool TMA>
+template <int EPI, bool FULL, bool TMA, bool UK>
 static int hexmv_launch_t(const HexmvParams& P, const HxMaps& T, cudaStream_t s) {
   const int dyn = (TMA ? hx_dyn_smem_tma(P.ovf_bytes) : hx_dyn_smem(P.ovf_bytes)) + hx_lacc_bytes(P);
   static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(hexmv_kernel<EPI, FULL, TMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(hexmv_kernel<EPI, FULL, TMA, UK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          227 * 1024);
     if (e != cudaSuccess) return record_cuda_error(e);
     configured[dev] = true;
@@ -159,7 +159,7 @@ static int hexmv_launch_t(const HexmvParams& P, const HxMaps& T, cudaStream_t s)
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, hexmv_kernel<EPI, FULL, TMA>, P, T);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, hexmv_kernel<EPI, FULL, TMA, UK>, P, T);
   if (e != cudaSuccess) return record_cuda_error(e);
   return GSDLQ_OK;
 }
@@ -239,11 +239,11 @@ static int hexmv_dispatch_full(const HexmvParams& P, cudaStream_t s) {
     if (ok) {
       HexmvParams Q = P;
       Q.lacc_off = 0x10000 + P.ovf_bytes + HX_RING_BYTES;  // the accumulator after the ring
-      return hexmv_launch_t<EPI, true, true>(Q, T, s);
+      return hexmv_launch_t<EPI, true, true, false>(Q, T, s);
     }
   }
-  if (hexmv_full(P)) return hexmv_launch_t<EPI, true, false>(P, T, s);
-  return hexmv_launch_t<EPI, false, false>(P, T, s);
+  if (hexmv_full(P)) return P.ukink ? hexmv_launch_t<EPI, true, false, true>(P, T, s) : hexmv_launch_t<EPI, true, false, false>(P, T, s);
+  return P.ukink ? hexmv_launch_t<EPI, false, false, true>(P, T, s) : hexmv_launch_t<EPI, false, false, false>(P, T, s);
 }
 
 static int hexmv_dispatch(const HexmvParams& P, cudaStream_t s) {

@@ -548,12 +548,13 @@ __device__ __forceinline__ void ctl_release_last(unsigned* ctl, int lane) {
 // launch, the decode table built here, the control words reset by the last CTA).  MEGA = true: one
 // phase of the persistent decode kernel, which built the table once (s_radius in the reduction
 // words holds its radius) and orders the phases through the accessor's dep / done counters.
-template <int EPI, bool FULL, bool MEGA, bool TMA, class PTR>
+template <int EPI, bool FULL, bool MEGA, bool TMA, class PTR, bool UK = true>
 __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, uint8_t* smem) {
   static_assert(!TMA || FULL, "the TMA ring streams whole units only");
   // per-unit kink lists are applied by the streaming warps of the per-lane-load paths only; the host
   // never picks the TMA ring for a launch that has them
-  const bool ukink = !TMA && P.ukink;
+  // UK = false compiles the per-unit kink path out (it costs the streaming loop registers and code)
+  const bool ukink = UK && !TMA && P.ukink;
   constexpr int NMAT = (EPI == GSDLQ_EPI_SWIGLU) ? 2 : 1;
   constexpr int width = NMAT * 16;
   const gsdlq_linear_job_t& J = P.job;
@@ -1268,11 +1269,12 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
   }
 }
 
-template <int EPI, bool FULL, bool TMA>
+// UK: launches whose matrices carry per-unit kink lists (the streaming warps apply the kinks)
+template <int EPI, bool FULL, bool TMA, bool UK>
 __global__ void __launch_bounds__(HX_THREADS, 1) hexmv_kernel(const __grid_constant__ HexmvParams P,
                                                               const __grid_constant__ HxMaps T) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  hexmv_body<EPI, FULL, false, TMA>(P, HxPtrs{P, T}, smem);
+  hexmv_body<EPI, FULL, false, TMA, HxPtrs, UK>(P, HxPtrs{P, T}, smem);
 }
 
 }  // namespace gsdlq
