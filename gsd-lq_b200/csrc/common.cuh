@@ -59,9 +59,11 @@ __device__ __forceinline__ uint2 ldg_stream_u2(const void* p) {
   return r;
 }
 
+// 16-byte streaming load; the L2 fetches the whole 256-byte sector group around it (a unit reads
+// 256 contiguous bytes of a row in four steps)
 __device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
   uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
   return r;
 }
