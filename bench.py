@@ -35,6 +35,7 @@ METRIC = "decode tok/s batch1 Mistral-7B-shape Precision; unpack-matvec HBM GB/s
 PUBLISHED_TOKS = 6.5  # Mistral-7B Precision decode, AMD RX 5600 XT (README.md:32)
 # DRAM bytes (read + write) of one gate/up launch of a Mistral-7B layer, from one ncu capture on a B200
 GU_TRAFFIC = 66_798_848 + 873_216
+GU_ALGO = 66_527_368  # the algorithmic bytes of that launch (a tensor-parallel rank's launch scales both)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
@@ -317,8 +318,29 @@ def run_ours(args):
         e_ms = s.elapsed_time(e) / n
         e2e = {"value": 1e3 / e_ms, "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4 * V,
                "api": "GSDLQModel.forward_token(token_id, pos) -> np.float32[vocab]"}
-    elif world > 1:
-        e2e = None
+    elif world > 1 and args.e2e_steps > 0:
+        # every rank runs the same public calls (set_state: H2D of token and position; step; the greedy
+        # token read back), so the ranks' collectives stay in step; device time, max over ranks
+        import torch.distributed as dist
+        n = min(args.e2e_steps, model.max_seq - P0)
+        tok = prompt[-1]
+        model.set_state(tok, P0 - 1)
+        model.step(with_head=True)
+        tok = int(model.state[0].item())
+        dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(n):
+            model.set_state(tok, P0 + i)
+            model.step(with_head=True)
+            tok = int(model.state[0].item())
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e) / n], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e = {"value": 1e3 / float(t.item()), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4,
+               "api": "GSDLQModel.set_state(token_id, pos) + step() + the greedy token read from the device"}
 
     cpu = None
     if host_model is not None:
@@ -347,9 +369,11 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "kernel": "hexmv_kernel<SWIGLU> (fused gate/up linear)",
                          "achieved": gu_gbs, "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm,
                          "peak_source": f"{pk_src} hbm_gbs", "bytes_per_launch": gu_bytes,
-                         "launch_ms": gu_ms, "traffic": GU_TRAFFIC if args.model == "mistral-7b" else None,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
-                                           "(profiles/hexmv_swiglu_gate_up_mistral7b.md)"},
+                         "launch_ms": gu_ms,
+                         "traffic": GU_TRAFFIC * gu_bytes / GU_ALGO if args.model == "mistral-7b" else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full launch "
+                                           "(profiles/hexmv_swiglu_gate_up_mistral7b.md), scaled by this "
+                                           "launch's share of its bytes (1 on one GPU)"},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks, "pack_s": round(pack_s, 2), "prefill_s": round(prefill_s, 2),
         }

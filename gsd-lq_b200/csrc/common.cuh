@@ -134,13 +134,15 @@ __device__ __forceinline__ void red_add_release(unsigned* p, unsigned v) {
 // dependencies.  Gives up after 1 s of %globaltimer, or at once when *abort is set: on giving
 // up it raises GSDLQ_FLAG_TIMEOUT and sets *abort, so that every later wait of the launch
 // returns at once and the kernel ends with the flag raised instead of hanging.
+// Each poll is one load: the abort word is read only every 32nd poll (it matters only once some
+// wait has already given up), and there is no sleep between polls.
 __device__ __forceinline__ void wait_geq_abort(const unsigned* ctr, unsigned target, unsigned* abort) {
   unsigned long long t0 = 0ull;
   for (int it = 0;; ++it) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
     if (v >= target) return;
-    if (*reinterpret_cast<volatile unsigned*>(abort) != 0u) return;
+    if ((it & 31) == 31 && *reinterpret_cast<volatile unsigned*>(abort) != 0u) return;
     unsigned long long t1;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
     if (it == 0) t0 = t1;
@@ -149,7 +151,6 @@ __device__ __forceinline__ void wait_geq_abort(const unsigned* ctr, unsigned tar
       atomicExch(abort, 1u);
       return;
     }
-    __nanosleep(20);
   }
 }
 
