@@ -11,8 +11,10 @@
 //   scores S[t][h] = K[t] . q_h: mma.sync m16n8k16 with A = K rows (fp16, exact) and B = q split
 //     into fp16 hi + lo (after scaling by a power of two that puts max|q| in [2^14, 2^15), so
 //     both parts stay normal); S = (A.B_hi + A.B_lo) * sm_scale / scale;
-//   online softmax per head (one warp per head), P = exp(S - m) scaled by 2^11 and split into
-//     fp16 hi (A rows 0..7) + lo (A rows 8..15);
+//   softmax per head (one warp per head), P = exp(S - m) scaled by 2^11 and split into fp16 hi
+//     (A rows 0..7) + lo (A rows 8..15): one pass over all of the CTA's tokens when its tiles fit
+//     the AC_NBUF buffers (the common case: 8 warps take the score tiles, then one softmax and one
+//     P.V sweep), else tile by tile with an online softmax;
 //   O[h][d] += P . V: mma.sync with A = P rows, B = V rows read transposed by ldmatrix; rows g
 //     (hi) and g + 8 (lo) of the accumulator are the same head, so their sum is the output.
 // Combine: each CTA leaves (m_h, l_h, O_h) in its shared memory; after a cluster barrier CTA r
@@ -37,13 +39,14 @@ struct AcLayout {
   static constexpr int ROWB = HD * 2 + 16;          // K/V row bytes, padded (conflict-free fragments)
   static constexpr int TILEB = 2 * AT_TILE * ROWB;  // K rows, then V rows
   static constexpr int QROW = HD + 8;               // halves per q row (padded)
-  static constexpr int PROW = AT_TILE + 8;          // halves per P row (padded)
+  static constexpr int SPW = AC_NBUF * AT_TILE;     // score columns: every buffered token
+  static constexpr int PROW = SPW + 8;              // halves per P row (padded)
   static constexpr int OPC = GQ * HD / AC_CL;       // outputs each CTA combines
   static constexpr int KV = 0;
   static constexpr int QS = KV + AC_NBUF * TILEB;   // fp16 [16][QROW]: q hi (rows 0..7), lo (8..15)
   static constexpr int PS = QS + 16 * QROW * 2;     // fp16 [16][PROW]: P hi (rows 0..7), lo (8..15)
-  static constexpr int SP = PS + 16 * PROW * 2;     // fp32 [GQ][AT_TILE]: scaled scores of a tile
-  static constexpr int ACC = SP + GQ * AT_TILE * 4; // fp32 [GQ * HD]: this CTA's output x 2^11
+  static constexpr int SP = PS + 16 * PROW * 2;     // fp32 [GQ][SPW]: scaled scores
+  static constexpr int ACC = SP + GQ * SPW * 4;     // fp32 [GQ * HD]: this CTA's output x 2^11
   static constexpr int ST = ACC + GQ * HD * 4;      // fp32: m[8], l[8], f[8], reduction[8]
   static constexpr int VT = ST + 32 * 4;            // fp16 [AC_MAXK][OPC]: forwarded Vt slice
   static constexpr int FR = VT + AC_MAXK * OPC * 2; // fp32 [8 warps][16]: forward partial sums
@@ -105,6 +108,7 @@ template <int HD, int GQ>
 __global__ void __launch_bounds__(AC_THREADS, 1) attn_cluster_kernel(const __grid_constant__ gsdlq_attn_job_t J) {
   using Lo = AcLayout<HD, GQ>;
   constexpr int ROWB = Lo::ROWB, CH = HD / 8, KS = HD / 16, QROW = Lo::QROW, PROW = Lo::PROW, OPC = Lo::OPC;
+  constexpr int SPW = Lo::SPW;
   constexpr int NTALL = HD / 8;              // 8-dimension column tiles of the output
   constexpr int NTW = (NTALL + 7) / 8;       // column tiles per warp in P.V
   constexpr int NQ = (GQ * HD + AC_THREADS - 1) / AC_THREADS;
@@ -217,71 +221,133 @@ __global__ void __launch_bounds__(AC_THREADS, 1) attn_cluster_kernel(const __gri
   float acc[NTW][4];
 #pragma unroll
   for (int n = 0; n < NTW; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-  for (int i = 0; i < ntiles; ++i) {
-    const int nt = min(AT_TILE, t1 - (t0 + i * AT_TILE));
-    const uint8_t* kb = tile_k(i);
-    const uint8_t* vb = kb + AT_TILE * ROWB;
+  // scores of the 16 tokens from row rb of tile buffer kb against both q splits, into score
+  // columns c0 .. c0+15; lane (g, q4) holds heads 2q4, 2q4+1 of tokens c0+g (c[0], c[1]) and
+  // c0+g+8 (c[2], c[3])
+  auto scores16 = [&](const uint8_t* kb, int rb, int c0) {
+    float ch[4] = {0.f, 0.f, 0.f, 0.f}, cl[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint8_t* r0 = kb + (rb + g) * ROWB + 4 * q4;
+    const uint8_t* r1 = r0 + 8 * ROWB;
+    const uint16_t* qh = qs + g * QROW + 2 * q4;
+    const uint16_t* ql = qh + 8 * QROW;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      uint32_t a[4];
+      a[0] = *reinterpret_cast<const uint32_t*>(r0 + kk * 32);
+      a[1] = *reinterpret_cast<const uint32_t*>(r1 + kk * 32);
+      a[2] = *reinterpret_cast<const uint32_t*>(r0 + kk * 32 + 16);
+      a[3] = *reinterpret_cast<const uint32_t*>(r1 + kk * 32 + 16);
+      mma_f16_16816(ch, a, *reinterpret_cast<const uint32_t*>(qh + kk * 16),
+                    *reinterpret_cast<const uint32_t*>(qh + kk * 16 + 8));
+      mma_f16_16816(cl, a, *reinterpret_cast<const uint32_t*>(ql + kk * 16),
+                    *reinterpret_cast<const uint32_t*>(ql + kk * 16 + 8));
+    }
+    const int h0 = 2 * q4, ta = c0 + g;
+    if (h0 < GQ) {
+      sp[h0 * SPW + ta] = (ch[0] + cl[0]) * sscale;
+      sp[h0 * SPW + ta + 8] = (ch[2] + cl[2]) * sscale;
+    }
+    if (h0 + 1 < GQ) {
+      sp[(h0 + 1) * SPW + ta] = (ch[1] + cl[1]) * sscale;
+      sp[(h0 + 1) * SPW + ta + 8] = (ch[3] + cl[3]) * sscale;
+    }
+  };
+  // P.V over the first nk 16-token k-steps of the P columns; vrows(kk) is the first V row of
+  // k-step kk.  Warp w takes output column tiles w*NTW .. w*NTW+NTW-1; accumulator rows g (P hi)
+  // and g + 8 (P lo) both belong to head g.
+  auto pv = [&](int nk, auto vrows) {
+    if (warp * NTW < NTALL) {
+      const uint16_t* p0 = ps + g * PROW + 2 * q4;
+      const uint16_t* p1 = p0 + 8 * PROW;
+#pragma unroll 4
+      for (int kk = 0; kk < nk; ++kk) {
+        uint32_t a[4];
+        a[0] = *reinterpret_cast<const uint32_t*>(p0 + kk * 16);
+        a[1] = *reinterpret_cast<const uint32_t*>(p1 + kk * 16);
+        a[2] = *reinterpret_cast<const uint32_t*>(p0 + kk * 16 + 8);
+        a[3] = *reinterpret_cast<const uint32_t*>(p1 + kk * 16 + 8);
+        const uint8_t* vr = vrows(kk) + (lane & 15) * ROWB;
+#pragma unroll
+        for (int n = 0; n < NTW; ++n) {
+          uint32_t b0, b1;
+          ldsm_x2_trans(smem_u32(vr + (warp * NTW + n) * 16), b0, b1);
+          mma_f16_16816(acc[n], a, b0, b1);
+        }
+      }
+    }
+  };
+  if (ntiles > 0 && ntiles <= AC_NBUF) {
+    // every tile is buffered: scores of all of them, one softmax per head, one P.V sweep
+    const int ntot = t1 - t0;
     cp_async_wait_all();
     __syncthreads();
-    // scores: warp w < 4 takes tokens 16w..16w+15 against both q splits
-    if (warp < 4) {
-      float ch[4] = {0.f, 0.f, 0.f, 0.f}, cl[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint8_t* r0 = kb + (16 * warp + g) * ROWB + 4 * q4;
-      const uint8_t* r1 = r0 + 8 * ROWB;
-      const uint16_t* qh = qs + g * QROW + 2 * q4;
-      const uint16_t* ql = qh + 8 * QROW;
-#pragma unroll
-      for (int kk = 0; kk < KS; ++kk) {
-        uint32_t a[4];
-        a[0] = *reinterpret_cast<const uint32_t*>(r0 + kk * 32);
-        a[1] = *reinterpret_cast<const uint32_t*>(r1 + kk * 32);
-        a[2] = *reinterpret_cast<const uint32_t*>(r0 + kk * 32 + 16);
-        a[3] = *reinterpret_cast<const uint32_t*>(r1 + kk * 32 + 16);
-        mma_f16_16816(ch, a, *reinterpret_cast<const uint32_t*>(qh + kk * 16),
-                      *reinterpret_cast<const uint32_t*>(qh + kk * 16 + 8));
-        mma_f16_16816(cl, a, *reinterpret_cast<const uint32_t*>(ql + kk * 16),
-                      *reinterpret_cast<const uint32_t*>(ql + kk * 16 + 8));
-      }
-      // lane (g, q4): heads 2q4 and 2q4+1 of tokens 16w+g (c[0], c[1]) and 16w+g+8 (c[2], c[3])
-      const int h0 = 2 * q4, ta = 16 * warp + g;
-      if (h0 < GQ) {
-        sp[h0 * AT_TILE + ta] = (ch[0] + cl[0]) * sscale;
-        sp[h0 * AT_TILE + ta + 8] = (ch[2] + cl[2]) * sscale;
-      }
-      if (h0 + 1 < GQ) {
-        sp[(h0 + 1) * AT_TILE + ta] = (ch[1] + cl[1]) * sscale;
-        sp[(h0 + 1) * AT_TILE + ta + 8] = (ch[3] + cl[3]) * sscale;
-      }
-    }
+    for (int mt = warp; mt < 4 * ntiles; mt += 8) scores16(tile_k(mt >> 2), (mt & 3) * 16, mt * 16);
     __syncthreads();
-    // online softmax: warp h takes head h
-    if (warp < GQ) {
+    if (warp < GQ) {  // warp h: head h, token lane + 32 j
       const int h = warp;
-      const float a = lane < nt ? sp[h * AT_TILE + lane] : -INFINITY;
-      const float b = lane + 32 < nt ? sp[h * AT_TILE + lane + 32] : -INFINITY;
-      const float m_old = s_m[h];
-      const float m = fmaxf(m_old, warp_max(fmaxf(a, b)));
-      const float ea = lane < nt ? expf(a - m) : 0.f;
-      const float eb = lane + 32 < nt ? expf(b - m) : 0.f;
-      const float xa = ea * AC_PSCALE, xb = eb * AC_PSCALE;
-      const uint16_t ha = f2h(xa), hb = f2h(xb);
-      ps[h * PROW + lane] = ha;
-      ps[h * PROW + lane + 32] = hb;
-      ps[(8 + h) * PROW + lane] = f2h(xa - h2f(ha));
-      ps[(8 + h) * PROW + lane + 32] = f2h(xb - h2f(hb));
-      const float sum = warp_sum(ea + eb);
+      float v[SPW / 32];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < SPW / 32; ++j) {
+        const int t = lane + 32 * j;
+        v[j] = t < ntot ? sp[h * SPW + t] : -INFINITY;
+        mx = fmaxf(mx, v[j]);
+      }
+      const float m = warp_max(mx);
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < SPW / 32; ++j) {
+        const int t = lane + 32 * j;
+        const float e = t < ntot ? expf(v[j] - m) : 0.f;
+        sum += e;
+        const float x = e * AC_PSCALE;
+        const uint16_t hi = f2h(x);
+        ps[h * PROW + t] = hi;
+        ps[(8 + h) * PROW + t] = f2h(x - h2f(hi));
+      }
+      sum = warp_sum(sum);
       if (lane == 0) {
-        const float f = (m_old == -INFINITY) ? 0.f : expf(m_old - m);
-        s_f[h] = f;
         s_m[h] = m;
-        s_l[h] = s_l[h] * f + sum;
+        s_l[h] = sum;
       }
     }
     __syncthreads();
-    // P.V: warp w takes output column tiles w*NTW .. w*NTW+NTW-1; accumulator rows g (P hi) and
-    // g + 8 (P lo) both belong to head g
-    {
-      const float f = g < GQ ? s_f[g] : 0.f;
+    pv(4 * ntiles, [&](int kk) { return tile_k(kk >> 2) + AT_TILE * ROWB + (kk & 3) * 16 * ROWB; });
+  } else {
+    // more tiles than buffers: tile by tile with an online softmax, refilling each buffer after use
+    for (int i = 0; i < ntiles; ++i) {
+      const int nt = min(AT_TILE, t1 - (t0 + i * AT_TILE));
+      const uint8_t* kb = tile_k(i);
+      const uint8_t* vb = kb + AT_TILE * ROWB;
+      cp_async_wait_all();
+      __syncthreads();
+      if (warp < 4) scores16(kb, 16 * warp, 16 * warp);
+      __syncthreads();
+      // online softmax: warp h takes head h
+      if (warp < GQ) {
+        const int h = warp;
+        const float a = lane < nt ? sp[h * SPW + lane] : -INFINITY;
+        const float b = lane + 32 < nt ? sp[h * SPW + lane + 32] : -INFINITY;
+        const float m_old = s_m[h];
+        const float m = fmaxf(m_old, warp_max(fmaxf(a, b)));
+        const float ea = lane < nt ? expf(a - m) : 0.f;
+        const float eb = lane + 32 < nt ? expf(b - m) : 0.f;
+        const float xa = ea * AC_PSCALE, xb = eb * AC_PSCALE;
+        const uint16_t ha = f2h(xa), hb = f2h(xb);
+        ps[h * PROW + lane] = ha;
+        ps[h * PROW + lane + 32] = hb;
+        ps[(8 + h) * PROW + lane] = f2h(xa - h2f(ha));
+        ps[(8 + h) * PROW + lane + 32] = f2h(xb - h2f(hb));
+        const float sum = warp_sum(ea + eb);
+        if (lane == 0) {
+          const float f = (m_old == -INFINITY) ? 0.f : expf(m_old - m);
+          s_f[h] = f;
+          s_m[h] = m;
+          s_l[h] = s_l[h] * f + sum;
+        }
+      }
+      __syncthreads();
+      const float f = g < GQ ? s_f[g] : 0.f;  // rescale the running output by this tile's factor
 #pragma unroll
       for (int n = 0; n < NTW; ++n) {
         acc[n][0] *= f;
@@ -289,29 +355,11 @@ __global__ void __launch_bounds__(AC_THREADS, 1) attn_cluster_kernel(const __gri
         acc[n][2] *= f;
         acc[n][3] *= f;
       }
-      if (warp * NTW < NTALL) {
-        const uint16_t* p0 = ps + g * PROW + 2 * q4;
-        const uint16_t* p1 = p0 + 8 * PROW;
-#pragma unroll
-        for (int kk = 0; kk < AT_TILE / 16; ++kk) {
-          uint32_t a[4];
-          a[0] = *reinterpret_cast<const uint32_t*>(p0 + kk * 16);
-          a[1] = *reinterpret_cast<const uint32_t*>(p1 + kk * 16);
-          a[2] = *reinterpret_cast<const uint32_t*>(p0 + kk * 16 + 8);
-          a[3] = *reinterpret_cast<const uint32_t*>(p1 + kk * 16 + 8);
-#pragma unroll
-          for (int n = 0; n < NTW; ++n) {
-            const int n0 = (warp * NTW + n) * 8;
-            uint32_t b0, b1;
-            ldsm_x2_trans(smem_u32(vb + (kk * 16 + (lane & 15)) * ROWB + n0 * 2), b0, b1);
-            mma_f16_16816(acc[n], a, b0, b1);
-          }
-        }
+      pv(AT_TILE / 16, [&](int kk) { return vb + kk * 16 * ROWB; });
+      if (i + AC_NBUF < ntiles) {
+        __syncthreads();  // every read of this buffer is done before it is refilled
+        issue(i + AC_NBUF, 2);
       }
-    }
-    if (i + AC_NBUF < ntiles) {
-      __syncthreads();  // every read of this buffer is done before it is refilled
-      issue(i + AC_NBUF, 2);
     }
   }
   // this CTA's output (x 2^11) for the combine; m = -inf, l = 0, O = 0 without tokens
