@@ -52,9 +52,11 @@
 // low-rank projection tmp_k = S * (Vt . x) is computed once per launch in
 // column slices by all helpers of the grid, or forwarded by the kernel that
 // produced x.  After one CTA barrier a strip inside the CTA's range is
-// finished from shared memory; a strip shared with other CTAs adds its part to
-// a global fixed-point sum and the last CTA to arrive (acq_rel counter)
-// finishes it and leaves the sum and the counter at zero.
+// finished from shared memory; for a strip shared with other CTAs every sharer
+// adds its part, plus a count unit, to one global word per row with a returning
+// atomic, and the CTA whose addition completes the count finishes the strip and
+// leaves the words at zero.  An RMSNorm input is staged as w * x and the finished
+// values are multiplied by 1/rms.
 //
 // Launch order (programmatic dependent launch): the next launch is released at
 // once; decode table, the first unit's code and scale loads and L2 prefetches
@@ -104,7 +106,7 @@ struct HexmvParams {
   int ovf_bytes;           // activation-split overflow region
   int ukink;               // every matrix has per-unit kink lists: the streaming warps apply them
   unsigned* ctl;
-  unsigned* cnt;                // [n_strips] arrivals of CTAs at strips shared with other CTAs
+  unsigned* cnt;                // [n_strips] reserved (zero; the shared-strip words count their own contributions)
   unsigned long long* gacc;     // [n_strips][nmat * 16] fixed-point sums of those strips
   // Inside the persistent decode kernel (null in a stand-alone launch): the input is ready once
   // *dep >= dep_target; every finished strip and every CTA of the launch add 1 to *done;
@@ -360,7 +362,7 @@ __device__ __forceinline__ StripInfo strip_info(const HexmvParams& P, int s) {
   return si;
 }
 
-// Operands of a strip's epilogue that do not depend on its result, loaded before the slot sum
+// Operands of a strip's epilogue that do not depend on its result, loaded before the CTA barrier
 // so that their latency overlaps it.
 struct EpiPre {
   float resid;  // RESID
@@ -452,7 +454,7 @@ __device__ float strip_epilogue(const HexmvParams& P, const StripInfo& si, float
 // Low-rank forwarding (job.fwd_acc): this strip's 16 output rows r contribute
 // sum_r Vt_next[j][rbase + r] * w[rbase + r] * out_r to the next linear's accumulator j.  Lane l
 // handles accumulators l and l + 32; their Vt slices (16 fp16 each) are loaded before the strip's
-// slot sum so that the loads overlap it.
+// CTA barrier so that the loads overlap it.
 struct FwdSlice {
   uint4 a[2], b[2];
   float w;  // lanes 0-15: the next linear's norm weight of row rbase + lane (1 without one)
@@ -602,7 +604,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
   constexpr int NST = HX_STREAM * kWarp;  // streaming (and staging) threads
 
   if (helper) {
-    // ==== helper warps: low-rank slice partials, kink slots, deferred strip arrivals ==========
+    // ==== helper warps: low-rank slice partials and the kink sums of the strips this CTA owns ===
     const int hw = blockIdx.x * HX_HELP + (warp - HX_STREAM);
     const int H = gridDim.x * HX_HELP;
     const int c8_0 = hw * P.lr_chunks;
@@ -1207,8 +1209,8 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
   // ---- finish this CTA's strips ------------------------------------------------------------
   // After one barrier every warp and helper term is in the accumulator.  Warp w takes strips
   // s_lo + w, s_lo + w + 16, ...: a strip inside this CTA's range is finished from the
-  // accumulator; one shared with other CTAs adds its part to the strip's global fixed-point sum,
-  // and the last CTA to arrive (acq_rel count) finishes it and leaves the sum and count at zero.
+  // accumulator; one shared with other CTAs adds its part to the strip's counted global words
+  // (HX_SH_ONE), and the CTA that completes them finishes it and leaves them at zero.
   {
     // (the operands of this warp's first strip's epilogue are loaded before the barrier)
     const int pos = reinterpret_cast<const volatile int*>(redu)[34];
