@@ -647,6 +647,16 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       }
       return k;
     };
+    // L2 prefetch of the kink columns and deltas of a pass's rows, so that the pass's batches hit L2
+    // instead of queueing behind the streaming warps' HBM loads
+    auto pf_kinks = [&](const KRow& k) {
+      if (k.row >= 0 && k.e1 > k.e0) {
+        const uint8_t* c = reinterpret_cast<const uint8_t*>(k.cols + k.e0);
+        const uint8_t* d = reinterpret_cast<const uint8_t*>(k.del + k.e0);
+        for (uint32_t b = 0; b < (k.e1 - k.e0) * 2u + 127u; b += 128u) asm volatile("prefetch.global.L2 [%0];" ::"l"(c + b));
+        for (uint32_t b = 0; b < (k.e1 - k.e0) * 4u + 127u; b += 128u) asm volatile("prefetch.global.L2 [%0];" ::"l"(d + b));
+      }
+    };
     constexpr int KB = 8;  // kinks per lane per batch
     int col[KB];
     float dl[KB];
@@ -670,6 +680,8 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
     KRow kcur = krow(0), knext = krow(1);
     load_batch(kcur, kcur.e0);
     load_u(kcur);
+    pf_kinks(kcur);
+    pf_kinks(knext);
     constexpr int LRC = 4;  // Vt chunks of this lane's first row held in registers; the rest via L2
     uint4 vr[LRC];
     auto vt_row = [&](int jl) {  // Vt row jl of the launch's concatenated low-rank rows
@@ -771,6 +783,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
         knext = krow(p + 1);  // in flight during this pass
         load_batch(kcur, kcur.e0);
         load_u(kcur);
+        pf_kinks(knext);  // waits for its row offsets, which overlaps this pass's first batch
       }
       float v = 0.f;
       for (uint32_t e = kcur.e0;;) {
