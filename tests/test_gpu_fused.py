@@ -166,6 +166,26 @@ def test_embed_qkv_rope_kv(env, restated, rng, nh, nkv, hd, H, uk):
     assert L.device_flags() == 0
 
 
+@pytest.mark.parametrize("rows,cols", [(64, 14336), (48, 8192), (32, 5120), (160, 14336)])
+def test_strips_shared_by_many_ctas(env, restated, rng, rows, cols):
+    """Few strips with many units each: a strip's units spread over up to 7 CTAs, whose parts meet in
+    the counted global words (the finishing CTA is whichever completes them); the workspace is left
+    zero and the result matches the oracle."""
+    ops, L = env
+    t = rand_hex(rng, rows, cols, k=16, nnz=cols // 256)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = torch.zeros(rows, device="cuda")
+    j = make_job(L, [ops.DeviceHex(t)], L.IN_PLAIN, x=dev(x), epilogue=L.EPI_STORE, ys=(y,))
+    ws = ops.linear_workspace(j)
+    yr = oracle_matvec(restated, x, t)
+    for _ in range(2):
+        y.zero_()
+        ops.linear(j, ws)
+        torch.cuda.synchronize()
+        assert rel_err(y.cpu().numpy(), yr) < MATVEC_TOL
+        assert int(ws.view(torch.int32).abs().sum().item()) == 0
+
+
 def test_flags_bad_kink_and_bad_pos(env, restated, rng):
     """Host-made bad inputs: the kernels skip the access and raise a flag instead of faulting."""
     ops, L = env
