@@ -149,6 +149,14 @@ def hex2d_matvec(x, h: DeviceHex, xy_table, tmp_k, y):
                                       h.k_dim, h.n_pts, stream_handle()), "hex2d_matvec")
 
 
+def hex2d_matmul(x, h: DeviceHex, xy_table, y, work):
+    """y[b] = the packed linear of x[b] for every row b of x ([batch][cols] -> [batch][rows]); work: 1088+ floats."""
+    L.check(_lib().gsdlq_hex2d_matmul(ptr(x), x.shape[0], ptr(h.codes), ptr(h.scales), ptr(xy_table), ptr(h.U),
+                                      ptr(h.S), ptr(h.Vt), ptr(h.row_ptr), ptr(h.kink_cols), ptr(h.kink_deltas),
+                                      ptr(y), ptr(work), h.rows, h.cols, h.k_dim, h.n_pts, stream_handle()),
+            "hex2d_matmul")
+
+
 def rope_and_store_kv(q, k, v, k_cache, v_cache, layer, pos, n_heads, n_kv, hd, max_seq, theta, interleaved=1):
     L.check(_lib().gsdlq_rope_and_store_kv(ptr(q), ptr(k), ptr(v), ptr(k_cache), ptr(v_cache), layer, pos, n_heads,
                                            n_kv, hd, max_seq, theta, interleaved, stream_handle()),
