@@ -14,7 +14,8 @@
 //     power of two that puts max|x_b| in [2^14, 2^15), so both halves stay normal);
 //   - mma.sync m16n8k16 (fp16 in, fp32 accumulate): warp w takes rows 16w..16w+15; per 8-token n-tile
 //     and k-step three MMAs, W_hi x_hi + W_hi x_lo + W_lo x_hi (the lo * lo term is below fp32 rounding);
-//   - the next block's codes, scale and activations are loaded into registers while this one is computed.
+//   - the codes and scales of the block two ahead and the activations of the next block are loaded into
+//     registers while this one is computed.
 // The partial sums are added into y (zeroed by the entry point) with fp32 atomics, so the summation
 // order over the k-runs is not fixed; the kink and low-rank terms are added once per (row, token) by the
 // CTA of the run with the token's index modulo the number of runs.
@@ -39,18 +40,21 @@ __device__ __forceinline__ void mm_f16_16816(float (&d)[4], const uint32_t (&a)[
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Per token b: xsc[b], the power of two that puts max|x_b| in [2^14, 2^15), and
-// tmp[16 b + j] = S[j] * (Vt[j] . x_b) for j < k (gsd_cpu_lowrank_proj, in a tree order).
+// Per token b and chunk of MM_PREP columns: the chunk's max|x_b| into amax[b] (as ordered bits) and its
+// part of S[j] * (Vt[j] . x_b) into tmp[16 b + j] (gsd_cpu_lowrank_proj; fp32 atomics, so the summation
+// order is not fixed).  Both start at zero.
+constexpr int MM_PREP = 1024;
 __global__ void __launch_bounds__(256) hexmm_prep(const float* __restrict__ x, int C, const uint16_t* __restrict__ Vt,
-                                                  const float* __restrict__ S, int k, float* __restrict__ xsc,
+                                                  const float* __restrict__ S, int k, unsigned* __restrict__ amax_bits,
                                                   float* __restrict__ tmp) {
   __shared__ float red[8][17];
   const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* xb = x + (size_t)b * C;
+  const int c1 = min(C, (int)(blockIdx.y + 1) * MM_PREP);
   float amax = 0.f, acc[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-  for (int c = threadIdx.x; c < C; c += 256) {
+  for (int c = blockIdx.y * MM_PREP + threadIdx.x; c < c1; c += 256) {
     const float v = xb[c];
     amax = fmaxf(amax, fabsf(v));
 #pragma unroll
@@ -69,16 +73,22 @@ __global__ void __launch_bounds__(256) hexmm_prep(const float* __restrict__ x, i
   if (threadIdx.x < 16 && threadIdx.x < k) {
     float t = 0.f;
     for (int w = 0; w < 8; ++w) t += red[w][threadIdx.x];
-    tmp[(size_t)b * 16 + threadIdx.x] = S[threadIdx.x] * t;
+    atomicAdd(tmp + (size_t)b * 16 + threadIdx.x, S[threadIdx.x] * t);
   }
   if (threadIdx.x == 32) {
     float m = 0.f;
     for (int w = 0; w < 8; ++w) m = fmaxf(m, red[w][16]);
-    int e = 0;
-    frexpf(m, &e);  // m < 2^e
-    e = max(e, -100);
-    xsc[b] = (m > 0.f && m <= 3.0e38f) ? ldexpf(1.f, 15 - e) : 1.f;
+    atomicMax(amax_bits + b, __float_as_uint(m));  // non-negative floats order as their bits
   }
+}
+
+// the power of two that puts max|x_b| in [2^14, 2^15), so both fp16 halves of x_b stay normal
+__device__ __forceinline__ float hexmm_xscale(unsigned amax_bits) {
+  const float m = __uint_as_float(amax_bits);
+  int e = 0;
+  frexpf(m, &e);  // m < 2^e
+  e = max(e, -100);
+  return (m > 0.f && m <= 3.0e38f) ? ldexpf(1.f, 15 - e) : 1.f;
 }
 
 // NB: 8-token n-tiles (tokens padded to 8 NB with zero activations).
@@ -91,7 +101,7 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
                                                            const uint32_t* __restrict__ row_ptr,
                                                            const uint16_t* __restrict__ kcols,
                                                            const float* __restrict__ kdel, float* __restrict__ y,
-                                                           int R, int C, int nsplit, const float* __restrict__ xsc,
+                                                           int R, int C, int nsplit, const unsigned* __restrict__ amax_bits,
                                                            const float* __restrict__ tmp) {
   constexpr int BP = NB * 8;                        // padded tokens
   constexpr int XE = BP * MM_KB / MM_THREADS;       // activations of a k-block per thread
@@ -107,7 +117,7 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
   const int NP = C / 2, G = C / 64, nkb = C / MM_KB;
   const int kb0 = (int)((long long)nkb * split / nsplit), kb1 = (int)((long long)nkb * (split + 1) / nsplit);
   for (int i = tid; i < 256; i += MM_THREADS) tab[i] = i < n_pts ? make_float2(xy[2 * i], xy[2 * i + 1]) : make_float2(0.f, 0.f);
-  for (int i = tid; i < BP; i += MM_THREADS) s_xsc[i] = i < B ? xsc[i] : 0.f;
+  for (int i = tid; i < BP; i += MM_THREADS) s_xsc[i] = i < B ? hexmm_xscale(amax_bits[i]) : 0.f;
   __syncthreads();
 
   // this thread's share of a k-block: 16 code bytes (32 weights) of row drow, and XE activations
@@ -122,13 +132,18 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
       xr[i] = b < B ? x[(size_t)b * C + kb * MM_KB + c] * s_xsc[b] : 0.f;
     }
   };
-  uint4 cw = make_uint4(0u, 0u, 0u, 0u);
-  uint16_t sc = 0;
+  // codes and scales two k-blocks ahead (HBM), activations one ahead (L2)
+  uint4 cw = make_uint4(0u, 0u, 0u, 0u), cw2 = make_uint4(0u, 0u, 0u, 0u);
+  uint16_t sc = 0, sc2 = 0;
   float xr[XE];
   if (kb1 > kb0) {
     if (rok) {
       cw = *reinterpret_cast<const uint4*>(cp + kb0 * 32);
       sc = scp[kb0];
+      if (kb0 + 1 < kb1) {
+        cw2 = *reinterpret_cast<const uint4*>(cp + (kb0 + 1) * 32);
+        sc2 = scp[kb0 + 1];
+      }
     }
     load_x(kb0, xr);
   }
@@ -159,13 +174,13 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
       xl[b * MM_XROW + c] = f2h(xr[i] - h2f(hi));
     }
     // ---- the next block's operands into registers while this one is multiplied ----
-    if (kb + 1 < kb1) {
-      if (rok) {
-        cw = *reinterpret_cast<const uint4*>(cp + (kb + 1) * 32);
-        sc = scp[kb + 1];
-      }
-      load_x(kb + 1, xr);
+    cw = cw2;
+    sc = sc2;
+    if (rok && kb + 2 < kb1) {
+      cw2 = *reinterpret_cast<const uint4*>(cp + (kb + 2) * 32);
+      sc2 = scp[kb + 2];
     }
+    if (kb + 1 < kb1) load_x(kb + 1, xr);
     __syncthreads();
     const int ao = (16 * warp + g) * MM_XROW + 2 * q4;
 #pragma unroll
@@ -226,8 +241,8 @@ template <int NB>
 static cudaError_t hexmm_launch_nb(dim3 grid, cudaStream_t s, const float* x, int B, const uint8_t* codes,
                                    const uint16_t* scales, const float* xy, int n_pts, const uint16_t* U, int k,
                                    const uint32_t* rp, const uint16_t* kc, const float* kd, float* y, int R, int C,
-                                   int nsplit, const float* xsc, const float* tmp) {
-  hexmm_kernel<NB><<<grid, MM_THREADS, 0, s>>>(x, B, codes, scales, xy, n_pts, U, k, rp, kc, kd, y, R, C, nsplit, xsc, tmp);
+                                   int nsplit, const unsigned* amax, const float* tmp) {
+  hexmm_kernel<NB><<<grid, MM_THREADS, 0, s>>>(x, B, codes, scales, xy, n_pts, U, k, rp, kc, kd, y, R, C, nsplit, amax, tmp);
   return cudaGetLastError();
 }
 
@@ -252,27 +267,30 @@ extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* code
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(work)) & 3u)
     return GSDLQ_ERR_INVALID;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  float* xsc = work;
+  unsigned* amax = reinterpret_cast<unsigned*>(work);  // per-token max|x| (bits)
   float* tmp = work + MM_MAXB;
   cudaError_t e = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)batch * rows, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(work, 0, sizeof(float) * 17 * MM_MAXB, s);
   if (e != cudaSuccess) return record_cuda_error(e);
-  hexmm_prep<<<batch, 256, 0, s>>>(x, cols, Vt, S, k_dim, xsc, tmp);
+  hexmm_prep<<<dim3(batch, (cols + MM_PREP - 1) / MM_PREP), 256, 0, s>>>(x, cols, Vt, S, k_dim, amax, tmp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return record_cuda_error(e);
-  // k-runs per row tile: about four CTAs per SM in all, at least one k-block each
+  // k-runs per row tile: about eight CTAs per SM in all up to 16 tokens (shorter load chains per CTA),
+  // four above (the wide-batch kernels hold more registers), at least one k-block each
   const int tiles = (rows + MM_ROWS - 1) / MM_ROWS, nkb = cols / MM_KB;
-  const int nsplit = std::max(1, std::min(nkb, (4 * num_sms() + tiles - 1) / tiles));
+  const int per_sm = batch <= 16 ? 8 : 4;
+  const int nsplit = std::max(1, std::min(nkb, (per_sm * num_sms() + tiles - 1) / tiles));
   const dim3 grid(tiles, nsplit);
   const float* kd = kink_deltas;
   switch ((batch + 7) / 8) {
-    case 1: e = hexmm_launch_nb<1>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, xsc, tmp); break;
-    case 2: e = hexmm_launch_nb<2>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, xsc, tmp); break;
-    case 3: e = hexmm_launch_nb<3>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, xsc, tmp); break;
-    case 4: e = hexmm_launch_nb<4>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, xsc, tmp); break;
-    case 5: e = hexmm_launch_nb<5>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, xsc, tmp); break;
-    case 6: e = hexmm_launch_nb<6>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, xsc, tmp); break;
-    case 7: e = hexmm_launch_nb<7>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, xsc, tmp); break;
-    default: e = hexmm_launch_nb<8>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, xsc, tmp); break;
+    case 1: e = hexmm_launch_nb<1>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
+    case 2: e = hexmm_launch_nb<2>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
+    case 3: e = hexmm_launch_nb<3>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
+    case 4: e = hexmm_launch_nb<4>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
+    case 5: e = hexmm_launch_nb<5>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
+    case 6: e = hexmm_launch_nb<6>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
+    case 7: e = hexmm_launch_nb<7>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
+    default: e = hexmm_launch_nb<8>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
   }
   if (e != cudaSuccess) return record_cuda_error(e);
   return GSDLQ_OK;

@@ -296,7 +296,7 @@ int gsdlq_rope_table(float *table, int max_seq, int head_dim, float rope_theta);
  * y[b] = gsd_cpu_hex2d_matvec(gsd_cpu_lowrank_proj(x[b])) for b < batch (gsd_lq_cpu_engine.c:111-183
  * applied to each token), as one dequant-GEMM on the tensor cores: the codes are decoded once per
  * launch for all tokens.  x: [batch][cols] fp32, y: [batch][rows] fp32 (zeroed here, then
- * accumulated), work: at least 17 * 64 floats of device scratch (per-token scales and low-rank
+ * accumulated), work: at least 17 * 64 floats of device scratch (per-token maxima and low-rank
  * projections).  1 <= batch <= 64, cols a multiple of 64 and at most 65535, k_dim <= 16, n_pts <= 256,
  * codes 16-byte aligned.  Results match the per-token matvec to about 1e-6 relative; the
  * partial sums are added with atomics, so the last bits may differ between runs. */
