@@ -32,7 +32,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s batch1 Mistral-7B-shape Precision; unpack-matvec HBM GB/s % peak"
-PUBLISHED_TOKS = 6.5  # Mistral-7B Precision decode, AMD RX 5600 XT (README.md:32)
+PUBLISHED_TOKS = 6.5  # the reference's published Mistral-7B Precision decode rate, AMD RX 5600 XT (README.md:32)
 # DRAM bytes (read + write) of one gate/up launch of a Mistral-7B layer, from one ncu capture on a B200
 GU_TRAFFIC = 66_794_752 + 727_296
 GU_ALGO = 66_527_368  # the algorithmic bytes of that launch (a tensor-parallel rank's launch scales both)
