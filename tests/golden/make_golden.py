@@ -4,7 +4,8 @@ Run in a container that holds the reference tree (default location taken from
 $GSDLQ_REFERENCE, else the standard mount); the fixtures are committed so the
 tests never need the reference at run time:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py            # everything
+    python tests/golden/make_golden.py sampling   # only sampling_ref.npz
 
 What it records (all produced by the reference's own code):
   codebook.npz     _get_turbo_codebook(6|8) from both reference copies
@@ -16,6 +17,8 @@ What it records (all produced by the reference's own code):
                      - _matvec_cpu(x, layer0.q) and (k_dim = 0 path) _matvec_cpu(x, layer0.k of a turbo file)
                      - the NumPy-fallback dequantised weight W of layer0.q (the W definition)
                        and its fallback matvec
+  sampling_ref.npz the reference's sample_token picks (temperature + top-p) on fixed logits
+                   under fixed np.random seeds
 """
 from __future__ import annotations
 
@@ -84,5 +87,46 @@ def main():
         print(mode, "picks", picks)
 
 
+# (temperature, top_p) pairs of the sampling fixture: greedy, the chat default, a tight nucleus, top_p = 1.0
+# (the cumulative sum may never exceed it, so the reference keeps only the top token) and a tiny temperature
+SAMPLING_CASES = [(0.0, 0.9), (0.7, 0.9), (1.0, 0.5), (1.3, 1.0), (1e-6, 0.9), (0.9, 0.99)]
+SAMPLING_SEEDS = range(8)
+
+
+def sampling_logits():
+    """Logit vectors of the sampling fixture: random, with NaN/+-inf entries, with a tie at the maximum."""
+    rng = np.random.default_rng(11)
+    out = [rng.standard_normal(320).astype(np.float32) * 3.0, rng.standard_normal(320).astype(np.float32) * 0.7]
+    z = rng.standard_normal(320).astype(np.float32)
+    z[[5, 77, 200]] = [np.nan, np.inf, -np.inf]
+    out.append(z)
+    z = rng.standard_normal(320).astype(np.float32)
+    z[[10, 250]] = 9.0  # a tie: the first index wins the greedy pick
+    out.append(z)
+    out.append(np.full(320, -3.0, np.float32))  # flat: every token equally likely
+    return np.stack(out)
+
+
+def sampling_main():
+    """sampling_ref.npz: the reference's sample_token (gsd_lq_cpu_runtime.py:422-443) under np.random.seed(s)."""
+    sys.path.insert(0, os.path.join(REF, "gsd_lq_v2"))
+    import gsd_lq_cpu_runtime as R
+
+    logits = sampling_logits()
+    picks = np.zeros((len(logits), len(SAMPLING_CASES), len(SAMPLING_SEEDS)), np.int64)
+    for i, lg in enumerate(logits):
+        for j, (t, p) in enumerate(SAMPLING_CASES):
+            for k, seed in enumerate(SAMPLING_SEEDS):
+                np.random.seed(seed)
+                picks[i, j, k] = R.CPUMistralV2Model.sample_token(None, lg.copy(), temperature=t, top_p=p)
+    np.savez(os.path.join(HERE, "sampling_ref.npz"), logits=logits, cases=np.array(SAMPLING_CASES),
+             seeds=np.array(list(SAMPLING_SEEDS)), picks=picks)
+    print("sampling picks", picks.shape)
+
+
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["sampling"]:
+        sampling_main()
+    else:
+        main()
+        sampling_main()
