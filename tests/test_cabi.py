@@ -50,3 +50,26 @@ def test_argument_errors_before_launch():
     job = L.LinearJob()
     job.n_mat = 0
     assert lib.gsdlq_linear(ctypes.byref(job), None, 0, None) == -1
+
+
+def test_batched_and_noalloc_argument_errors_before_launch():
+    """The batched linear and the no-allocation matvec refuse bad shapes and alignments on the host,
+    before any CUDA call (the stand-in addresses below are never dereferenced)."""
+    lib = L.load()
+    A = ctypes.c_void_p(0x100000)        # a 256-byte-aligned stand-in address
+    odd = ctypes.c_void_p(0x100001)
+
+    def mm(x=A, batch=4, codes=A, y=A, work=A, rows=64, cols=128, k=0, n_pts=217, U=None, S=None, Vt=None):
+        return lib.gsdlq_hex2d_matmul(x, batch, codes, A, A, U, S, Vt, A, A, A, y, work, rows, cols, k, n_pts, None)
+
+    for kw in (dict(batch=0), dict(batch=65), dict(cols=100), dict(cols=65536), dict(cols=0), dict(rows=0),
+               dict(k=17), dict(k=4), dict(n_pts=0), dict(n_pts=257), dict(codes=odd), dict(y=odd),
+               dict(work=odd), dict(x=None), dict(codes=None)):
+        assert mm(**kw) == -1, kw
+
+    def mv(x=A, codes=A, y=A, rows=64, cols=128, k=0, n_pts=217, U=None, tmp=None):
+        return lib.gsdlq_hex2d_matvec_noalloc(x, codes, A, A, U, tmp, A, A, A, y, rows, cols, k, n_pts, None)
+
+    for kw in (dict(n_pts=0), dict(n_pts=257), dict(k=4), dict(k=17, U=A, tmp=A), dict(cols=100), dict(rows=0),
+               dict(codes=odd), dict(x=None), dict(y=None)):
+        assert mv(**kw) == -1, kw
