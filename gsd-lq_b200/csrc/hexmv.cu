@@ -2,6 +2,7 @@
 // its C-ABI entry points.
 #include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -281,6 +282,7 @@ struct DropinWs {
   size_t bytes = 0;
 };
 static DropinWs g_mv_ws[64];
+static std::mutex g_mv_mu;  // guards g_mv_ws: the grow (free + malloc) and the launch that reads it
 
 }  // namespace gsdlq
 
@@ -342,6 +344,7 @@ extern "C" int gsdlq_hex2d_matvec(const float* x, const uint8_t* codes, const ui
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return record_cuda_error(e);
   if (dev < 0 || dev >= 64) return GSDLQ_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_mv_mu);
   DropinWs& ws = g_mv_ws[dev];
   if (ws.bytes < need) {
     if (ws.p) cudaFree(ws.p);
@@ -469,7 +472,7 @@ extern "C" int gsdlq_unit_kinks(const uint32_t* row_ptr, const uint16_t* kink_co
 // cudaGetSymbolAddress, looked up once per device with that device current.
 namespace gsdlq {
 static __device__ __align__(256) unsigned char g_noalloc_ws[GSDLQ_NOALLOC_WS_BYTES];
-static void* g_noalloc_addr[64];
+static std::atomic<void*> g_noalloc_addr[64];  // per device; racing set-ups store the same address
 }  // namespace gsdlq
 
 extern "C" int gsdlq_hex2d_matvec_noalloc(const float* x, const uint8_t* codes, const uint16_t* scales,
@@ -509,13 +512,12 @@ extern "C" int gsdlq_hex2d_matvec_noalloc(const float* x, const uint8_t* codes, 
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return record_cuda_error(e);
   if (dev < 0 || dev >= 64) return GSDLQ_ERR_UNSUPPORTED;
-  if (g_noalloc_addr[dev] == nullptr) {  // set-up, once per device (this device is current)
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_ws);
+  void* ws = g_noalloc_addr[dev].load(std::memory_order_acquire);
+  if (ws == nullptr) {  // set-up, once per device (this device is current)
+    e = cudaGetSymbolAddress(&ws, g_noalloc_ws);
     if (e != cudaSuccess) return record_cuda_error(e);
-    g_noalloc_addr[dev] = p;
+    g_noalloc_addr[dev].store(ws, std::memory_order_release);
   }
-  void* ws = g_noalloc_addr[dev];
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // the array keeps whatever the previous call left: clear the bytes this launch needs at zero
   e = cudaMemsetAsync(ws, 0, need, s);

@@ -82,7 +82,11 @@ int gsdlq_lowrank_proj(const float *x, const uint16_t *Vt, const float *S, float
  * with c = codes[(r*cols)/2 + p].  cols % 64 == 0, k_dim <= 16, n_pts <= 256 and
  * xy_table an A2 lattice table (the reference's _get_turbo_codebook).
  * Replaces gsd_cpu_hex2d_matvec, gsd_lq_cpu_engine.c:130-183
- * (OpenCL twin: gsd_hex2d_matvec_fused, run_gpu_native_chat.py:196-267). */
+ * (OpenCL twin: gsd_hex2d_matvec_fused, run_gpu_native_chat.py:196-267).
+ * The library keeps one scratch area per device for this call (grown with cudaMalloc when a
+ * larger matrix comes).  Back-to-back calls on one stream may share it; calls on DIFFERENT
+ * streams of one device must not run at the same time (the reference's function is synchronous).
+ * Callers with several streams use gsdlq_linear with a workspace per stream. */
 int gsdlq_hex2d_matvec(const float *x, const uint8_t *codes, const uint16_t *scales,
                        const float *xy_table, const uint16_t *U, const float *tmp_k,
                        const uint32_t *kink_row_ptr, const uint16_t *kink_cols,
