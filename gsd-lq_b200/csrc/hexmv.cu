@@ -140,14 +140,14 @@ bool hexmv_full(const HexmvParams& P) {
 template <int EPI, bool FULL, bool TMA, bool UK>
 static int hexmv_launch_t(const HexmvParams& P, const HxMaps& T, cudaStream_t s) {
   const int dyn = (TMA ? hx_dyn_smem_tma(P.ovf_bytes) : hx_dyn_smem(P.ovf_bytes)) + hx_lacc_bytes(P);
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device: the dynamic shared-memory opt-in is done
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  if (!configured[dev]) {
+  if (!configured[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(hexmv_kernel<EPI, FULL, TMA, UK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          227 * 1024);
     if (e != cudaSuccess) return record_cuda_error(e);
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   const int grid = P.n_cta;
   cudaLaunchConfig_t cfg = {};
