@@ -160,3 +160,31 @@ def test_peer_death_is_detected():
     for p in procs:
         p.join(timeout=30)
     assert msg != "no-error"
+
+
+def test_tp4_matches_unsharded(oracle_mod, restated, tmp_path):
+    """Four gloo ranks on a model that shards four ways: 2 of 8 query heads and 1 of 4 KV heads per
+    rank, O and down cut into 64- and 128-column slices, an 80-row vocabulary slice each."""
+    import torch.multiprocessing as mp
+    import gsdlq_b200.gsd2 as G
+    import gsdlq_b200.packer as P
+    cfg = P.make_config("tiny", n_layers=2, hidden_size=256, n_heads=8, n_kv_heads=4, head_dim=32,
+                        ffn_size=512, vocab_size=320)
+    path = str(tmp_path / "tp4_precision.gsd2")
+    G.write_gsd2(path, P.random_model(cfg, "precision", seed=5, norm_jitter=0.1))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 4, port, path, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=180)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    om = oracle_mod.OracleModel(oracle_mod.read_gsd2(path), restated, max_seq=64)
+    for pos, tok in enumerate(TOKENS):
+        full = om.forward_token(tok, pos)
+        lg, pick = res[pos]
+        assert np.allclose(lg, full, rtol=1e-4, atol=1e-5), float(np.max(np.abs(lg - full)))
+        assert pick == oracle_mod.argmax(full)
