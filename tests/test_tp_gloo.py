@@ -188,3 +188,46 @@ def test_tp4_matches_unsharded(oracle_mod, restated, tmp_path):
         lg, pick = res[pos]
         assert np.allclose(lg, full, rtol=1e-4, atol=1e-5), float(np.max(np.abs(lg - full)))
         assert pick == oracle_mod.argmax(full)
+
+
+def _typed_device_hex(t):
+    """A DeviceHex on CPU tensors with the GPU packer's dtypes (pack_matrix_cuda)."""
+    import torch
+    from gsdlq_b200.ops import DeviceHex
+
+    def T(a, dt):
+        return torch.from_numpy(np.ascontiguousarray(a).reshape(-1).view(dt).copy())
+    k, nz = t.k_dim, t.nnz
+    return DeviceHex(None, rows=t.rows, cols=t.cols, k_dim=k, radius=t.radius, codes=T(t.codes, np.uint8),
+                     scales=T(t.scales, np.int16), row_ptr=T(t.row_ptr, np.int32),
+                     kink_cols=T(t.kink_cols, np.int16) if nz else None,
+                     kink_deltas=T(t.kink_deltas, np.float32) if nz else None,
+                     U=T(t.U, np.int16) if k else None, S=T(t.S, np.float32) if k else None,
+                     Vt=T(t.Vt, np.int16) if k else None, nnz=nz)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("mode", ["precision", "turbo"])
+def test_device_shards_equal_host_shards(world, mode):
+    """tp.shard_device (the slicer of GPU-packed models that bench.py and GSDLQModel(tp=...) use) gives
+    the same bytes as the host shard_packed checked above, on CPU tensors: codes and scales per row,
+    kinks filtered and re-based by column range, Vt sliced by columns, U / S kept whole."""
+    import gsdlq_b200.packer as P
+    import gsdlq_b200.tp as TP
+    from gsdlq_b200.model import DevicePacked
+    cfg = P.make_config("tiny", n_layers=1, hidden_size=256, n_heads=8, n_kv_heads=4, head_dim=32,
+                        ffn_size=512, vocab_size=320)
+    pm = P.random_model(cfg, mode, seed=9)
+    dm = DevicePacked(config=cfg, hexes={n: _typed_device_hex(t) for n, t in pm.hex.items()}, dense=pm.dense,
+                      avg_bpw=pm.avg_bpw, mode=mode)
+    for rank in range(world):
+        host = TP.shard_packed(pm, rank, world)
+        dev = TP.shard_device(dm, rank, world)
+        assert dev.config == host.config
+        for name, t in host.hex.items():
+            d = P.device_hex_to_host(dev.hexes[name])
+            assert (d.rows, d.cols, d.k_dim, d.radius, d.nnz) == (t.rows, t.cols, t.k_dim, t.radius, t.nnz), name
+            for key, arr in t.blobs().items():
+                got = np.ascontiguousarray(d.blobs()[key]).reshape(-1).view(np.uint8)
+                want = np.ascontiguousarray(arr).reshape(-1).view(np.uint8)
+                assert np.array_equal(got, want), (name, key, rank)
