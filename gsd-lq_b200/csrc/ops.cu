@@ -544,8 +544,9 @@ int gsdlq_gqa_attention(const float* q, const uint16_t* k_cache, const uint16_t*
   if (e != cudaSuccess) return record_cuda_error(e);
   if (dev < 0 || dev >= 64) return GSDLQ_ERR_UNSUPPORTED;
   DropinScratch* sc = &g_scratch[dev];
+  // held through the launch: another thread's grow frees the buffers this launch is given
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
   {
-    std::lock_guard<std::mutex> lk(g_scratch_mu);
     if (sc->pbytes < pb) {
       if (sc->partial) cudaFree(sc->partial);
       sc->partial = nullptr;
