@@ -132,9 +132,15 @@ def lowrank_kinks(e: np.ndarray, k_dim: int, kinks_per_row: int, rng: np.random.
             qm, _ = np.linalg.qr(y)
             ub, s, vt = np.linalg.svd(qm.T @ e.astype(np.float64), full_matrices=False)
             u = qm @ ub
-        Uh = u[:, :k_dim].astype(np.float16)
-        Sf = s[:k_dim].astype(np.float32)
-        Vh = vt[:k_dim].astype(np.float16)
+        # a matrix smaller than k in either dimension has fewer components: the rest are zero, so the
+        # factors keep the declared k_dim (the format's U/S/Vt sizes)
+        kk = min(k_dim, u.shape[1])
+        Uh = np.zeros((r, k_dim), np.float16)
+        Uh[:, :kk] = u[:, :kk].astype(np.float16)
+        Sf = np.zeros(k_dim, np.float32)
+        Sf[:kk] = s[:kk].astype(np.float32)
+        Vh = np.zeros((k_dim, c), np.float16)
+        Vh[:kk] = vt[:kk].astype(np.float16)
         e2 = e - (Uh.astype(np.float32) * Sf[None, :]) @ Vh.astype(np.float32)
         U, S, Vt = Uh.view(np.uint16).reshape(-1), Sf, Vh.view(np.uint16).reshape(-1)
     if kinks_per_row > 0:
@@ -249,6 +255,23 @@ __all__ = ["pack_matrix", "quantize_lattice", "dequant", "random_model", "make_c
 # CUDA packer: the same lattice step on the GPU (bit-identical codes/scales/residual,
 # gsdlq_pack_lattice), low-rank factors and kinks with torch linear algebra.  Used for
 # the large benchmark shapes, where the NumPy packer would take minutes.
+def lowrank_factors_torch(resid, K: int):
+    """Rank-K factors of a float32 [rows, cols] tensor by torch.svd_lowrank (q = K + 8, two power
+    iterations): U fp16 [rows, K], S fp32 [K], Vt fp16 [K, cols].  A matrix with fewer than K
+    components gets zero columns / entries / rows for the rest, so the sizes match the declared k_dim."""
+    import torch
+    rows, cols = resid.shape
+    u, s, v = torch.svd_lowrank(resid, q=min(K + 8, rows, cols), niter=2)
+    kk = min(K, u.shape[1])
+    Uh = resid.new_zeros((rows, K), dtype=torch.float16)
+    Uh[:, :kk] = u[:, :kk].half()
+    S = resid.new_zeros(K, dtype=torch.float32)
+    S[:kk] = s[:kk].float()
+    Vh = resid.new_zeros((K, cols), dtype=torch.float16)
+    Vh[:kk] = v[:, :kk].T.half()
+    return Uh, S, Vh
+
+
 def pack_matrix_cuda(w, mode: str = "precision", radius: int | None = None, k_dim: int | None = None,
                      kinks_per_row: int | None = None, seed: int = 0):
     """Pack a float32 [rows, cols] CUDA tensor; returns an ``ops.DeviceHex``."""
@@ -268,11 +291,8 @@ def pack_matrix_cuda(w, mode: str = "precision", radius: int | None = None, k_di
     if K > 0:
         gen_state = torch.cuda.get_rng_state(dev)
         torch.manual_seed(seed)
-        u, s, v = torch.svd_lowrank(resid, q=K + 8, niter=2)
+        Uh, S, Vh = lowrank_factors_torch(resid, K)
         torch.cuda.set_rng_state(gen_state, dev)
-        Uh = u[:, :K].contiguous().half()
-        S = s[:K].contiguous().float()
-        Vh = v[:, :K].T.contiguous().half()
         resid -= (Uh.float() * S[None, :]) @ Vh.float()
         U, Vt = Uh.view(torch.int16).reshape(-1), Vh.view(torch.int16).reshape(-1)
     if KN > 0:

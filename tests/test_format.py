@@ -202,3 +202,75 @@ def test_shard_slices_sum_to_whole():
     assert np.array_equal(rows, full)
     cols = sum(eng.matvec(x[a:a + 128], rec(t.col_slice(a, a + 128))) for a in (0, 128))
     assert np.allclose(cols, full, rtol=1e-5, atol=1e-6)
+
+
+def test_slices_compose_and_sum_property():
+    """Property check of the shard slicers over random shapes and cut points: every slice validates,
+    slices of slices equal direct slices, and column slices at any 64-column cuts sum to the whole."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+    import oracle
+    eng = oracle.CEngine.restatement()
+    tabs = {r: oracle.codebook(r) for r in (6, 8)}
+
+    def rec(h):
+        return oracle.hex_record({"radius": h.radius, "k_dim": h.k_dim, "rows": h.rows, "cols": h.cols},
+                                 {k: v.tobytes() for k, v in h.blobs().items()}, tabs)
+
+    def same(a, b):
+        return all(np.array_equal(x, y) for x, y in zip(a.blobs().values(), b.blobs().values())) and \
+            (a.rows, a.cols, a.nnz) == (b.rows, b.cols, b.nnz)
+
+    @hyp.settings(max_examples=25, deadline=None, derandomize=True)
+    @hyp.given(rows=st.integers(1, 40), g=st.integers(2, 6), mode=st.sampled_from(["precision", "turbo"]),
+               data=st.data())
+    def check(rows, g, mode, data):
+        cols = 64 * g
+        rng = np.random.default_rng(rows * 131 + g)
+        t = P.pack_matrix((rng.standard_normal((rows, cols)) * 0.02).astype(np.float32), mode)
+        a = data.draw(st.integers(0, rows - 1))
+        b = data.draw(st.integers(a + 1, rows))
+        c = data.draw(st.integers(0, b - a - 1))
+        d = data.draw(st.integers(c + 1, b - a))
+        rs = t.row_slice(a, b)
+        rs.validate()
+        assert same(rs.row_slice(c, d), t.row_slice(a + c, a + d))
+        cuts = sorted(set([0, cols] + [64 * data.draw(st.integers(1, g - 1)) for _ in range(2)]))
+        parts = [t.col_slice(lo, hi) for lo, hi in zip(cuts, cuts[1:])]
+        for p in parts:
+            p.validate()
+        assert sum(p.nnz for p in parts) == t.nnz
+        x = rng.standard_normal(cols).astype(np.float32)
+        full = eng.matvec(x, rec(t))
+        tot = sum(eng.matvec(x[lo:hi].copy(), rec(p)) for (lo, hi), p in zip(zip(cuts, cuts[1:]), parts))
+        assert np.allclose(tot, full, rtol=1e-5, atol=1e-5)
+
+    check()
+
+
+def test_lowrank_factors_torch_pad_and_match():
+    """The GPU packer's factor step on CPU tensors: full-rank shapes equal torch.svd_lowrank's leading K
+    components; a matrix with fewer than K components gets zero padding up to k_dim."""
+    torch = pytest.importorskip("torch")
+    g = torch.Generator().manual_seed(4)
+    a = torch.randn(64, 128, generator=g) * 0.02
+    torch.manual_seed(1)
+    Uh, S, Vh = P.lowrank_factors_torch(a, 16)
+    torch.manual_seed(1)
+    u, s, v = torch.svd_lowrank(a, q=24, niter=2)
+    assert torch.equal(Uh, u[:, :16].half()) and torch.equal(S, s[:16].float()) and torch.equal(Vh, v[:, :16].T.half())
+    small = torch.randn(5, 128, generator=g)
+    Uh, S, Vh = P.lowrank_factors_torch(small, 16)
+    assert Uh.shape == (5, 16) and S.shape == (16,) and Vh.shape == (16, 128)
+    assert not Uh[:, 5:].any() and not S[5:].any() and not Vh[5:].any()
+    rec = (Uh.float() * S[None, :]) @ Vh.float()
+    assert torch.allclose(rec, small, atol=2e-2 * float(small.abs().max()))
+
+
+def test_packer_small_matrix_keeps_k_dim():
+    """A Precision matrix with fewer rows than k keeps k_dim = 16 with zero-padded factors."""
+    w = (np.random.default_rng(2).standard_normal((3, 128)) * 0.02).astype(np.float32)
+    t = P.pack_matrix(w, "precision")
+    t.validate()
+    assert t.k_dim == 16 and t.U.size == 3 * 16 and t.Vt.size == 16 * 128
+    assert not t.S[3:].any()
