@@ -274,3 +274,42 @@ def test_packer_small_matrix_keeps_k_dim():
     t.validate()
     assert t.k_dim == 16 and t.U.size == 3 * 16 and t.Vt.size == 16 * 128
     assert not t.S[3:].any()
+
+
+def test_gsd2_roundtrip_property(tmp_path):
+    """Random small configurations (GQA ratios, head sizes, FFN and vocabulary sizes, both modes) survive
+    write -> read byte for byte, and the oracle's own reader (a restatement of the reference's) agrees."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+    import oracle
+    counter = iter(range(10 ** 6))
+    seen = []
+
+    @hyp.settings(max_examples=12, deadline=None, derandomize=True)
+    @hyp.given(hd=st.sampled_from([32, 64]), nkv=st.integers(1, 3), grp=st.integers(1, 3), fg=st.integers(1, 4),
+               vocab=st.integers(40, 200), mode=st.sampled_from(["precision", "turbo"]), layers=st.integers(1, 2))
+    def check(hd, nkv, grp, fg, vocab, mode, layers):
+        nh = nkv * grp
+        if (nh * hd) % 64:
+            hd = 64  # hidden = n_heads * head_dim is the column count of q/k/v/gate/up: a multiple of 64
+        cfg = P.make_config("tiny", n_layers=layers, hidden_size=nh * hd, n_heads=nh, n_kv_heads=nkv, head_dim=hd,
+                            ffn_size=64 * fg, vocab_size=vocab)
+        seen.append((nh, nkv, hd, 64 * fg, vocab, mode, layers))
+        m = P.random_model(cfg, mode, seed=next(counter))
+        p = str(tmp_path / f"r{next(counter)}.gsd2")
+        G.write_gsd2(p, m)
+        r = G.read_gsd2(p)
+        assert r.config["n_layers"] == layers and r.mode == m.mode
+        for n, t in m.hex.items():
+            for k, a in t.blobs().items():
+                assert np.array_equal(a, getattr(r.hex[n], k)), (n, k)
+        for n, a in m.dense.items():
+            assert np.array_equal(np.asarray(a), np.asarray(r.dense[n])), n
+        o = oracle.read_gsd2(p)
+        lay = o["layers"][layers - 1]["down"]
+        t = m.hex[f"blk.{layers - 1}.ffn_down.weight"]
+        for k in ("codes", "scales", "row_ptr", "kink_cols", "kink_deltas"):
+            assert np.array_equal(getattr(t, k), lay[k]), k
+
+    check()
+    assert len(set(seen)) >= 8, seen
