@@ -43,6 +43,35 @@ def test_matvec_restatement_bitexact_vs_reference(restated, reference_engine, rn
     assert np.array_equal(y1, y2)
 
 
+def test_matvec_restatement_bitexact_property(restated, reference_engine):
+    """Random shapes, both radii, k in [0, 16] and ragged kink rows (unsorted and repeated columns, empty
+    rows): the restatement equals the reference engine bit for bit."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+    import gsdlq_b200.codebook as cb
+
+    @hyp.settings(max_examples=30, deadline=None, derandomize=True)
+    @hyp.given(rows=st.integers(1, 160), g=st.integers(1, 24), k=st.integers(0, 16), radius=st.sampled_from([6, 8]),
+               seed=st.integers(0, 2 ** 31 - 1))
+    def check(rows, g, k, radius, seed):
+        rng = np.random.default_rng(seed)
+        cols = 64 * g
+        rec = _rand_hex(rng, rows, cols, k, 0, radius=radius)
+        counts = rng.integers(0, 5, rows)
+        rec["row_ptr"] = np.concatenate([[0], np.cumsum(counts)]).astype(np.uint32)
+        nnz = int(counts.sum())
+        kc = rng.integers(0, cols, nnz)
+        if nnz > 1:
+            kc[-1] = kc[0]  # a repeated column
+        rec["kink_cols"] = kc.astype(np.uint16)
+        rec["kink_deltas"] = (rng.standard_normal(nnz) * 0.01).astype(np.float32)
+        assert rec["n_pts"] == cb.num_points(radius)
+        x = rng.standard_normal(cols).astype(np.float32)
+        assert np.array_equal(restated.matvec(x, rec), reference_engine.matvec(x, rec))
+
+    check()
+
+
 def test_elementwise_bitexact_vs_reference(restated, reference_engine, rng):
     n = 1000
     x = rng.standard_normal(n).astype(np.float32)
