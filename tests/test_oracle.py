@@ -117,6 +117,37 @@ def test_rope_attention_bitexact_vs_reference(restated, reference_engine, rng, i
         assert np.array_equal(q1, q2) and np.array_equal(o1, o2)
 
 
+def test_rope_attention_bitexact_property(restated, reference_engine):
+    """RoPE + fp16 KV store and GQA attention over random head sizes, GQA ratios, cache lengths, positions,
+    theta and both rotation layouts, on a randomly pre-filled cache: restatement == reference, bit for bit."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+
+    @hyp.settings(max_examples=25, deadline=None, derandomize=True)
+    @hyp.given(hd=st.sampled_from([32, 64, 128]), nkv=st.sampled_from([1, 2, 4]), grp=st.integers(1, 4),
+               S=st.sampled_from([16, 64, 200]), data=st.data(), theta=st.sampled_from([1e4, 5e5, 1e6]),
+               interleaved=st.sampled_from([0, 1]), seed=st.integers(0, 2 ** 31 - 1))
+    def check(hd, nkv, grp, S, data, theta, interleaved, seed):
+        nh, L = nkv * grp, 2
+        pos = data.draw(st.integers(0, S - 1))
+        r = np.random.default_rng(seed)
+        cache0 = r.standard_normal((2, L, S, nkv, hd)).astype(np.float16).view(np.uint16)
+        q0 = r.standard_normal(nh * hd).astype(np.float32)
+        k = r.standard_normal(nkv * hd).astype(np.float32)
+        v = r.standard_normal(nkv * hd).astype(np.float32)
+        res = []
+        for e in (restated, reference_engine):
+            kc, vc, q = cache0[0].copy(), cache0[1].copy(), q0.copy()
+            e.rope_and_store_kv(_p(q), _p(k), _p(v), _p(kc), _p(vc), 1, pos, nh, nkv, hd, S, theta, interleaved)
+            o = np.zeros(nh * hd, np.float32)
+            e.gqa_attention(_p(q), _p(kc), _p(vc), _p(o), 1, pos, nh, nkv, hd, S, 1 / np.sqrt(hd))
+            res.append((q, kc, vc, o))
+        for a, b in zip(*res):
+            assert np.array_equal(a, b)
+
+    check()
+
+
 @pytest.mark.parametrize("mode", ["precision", "turbo"])
 def test_oracle_model_matches_golden(oracle_mod, restated, mode):
     """Our restated reader + decoder step reproduce the reference runtime's logits bit for bit."""
