@@ -93,6 +93,41 @@ def test_elementwise_bitexact_vs_reference(restated, reference_engine, rng):
         assert np.array_equal(a, b)
 
 
+def test_elementwise_bitexact_property(restated, reference_engine):
+    """RMSNorm, add, SwiGLU (also in place, out aliasing gate as the reference's caller does) and the
+    low-rank projection over random lengths, eps, k and input scales (large gates saturate the sigmoid):
+    restatement == reference, bit for bit."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+
+    @hyp.settings(max_examples=30, deadline=None, derandomize=True)
+    @hyp.given(n=st.integers(1, 5000), k=st.integers(1, 16), eps=st.sampled_from([1e-5, 1e-6, 1e-3]),
+               scale=st.sampled_from([1e-3, 1.0, 40.0]), seed=st.integers(0, 2 ** 31 - 1))
+    def check(n, k, eps, scale, seed):
+        r = np.random.default_rng(seed)
+        x = (r.standard_normal(n) * scale).astype(np.float32)
+        w = r.standard_normal(n).astype(np.float32)
+        vt = r.standard_normal(k * n).astype(np.float16).view(np.uint16)
+        sv = r.random(k, dtype=np.float32)
+        outs = []
+        for e in (restated, reference_engine):
+            o1 = np.zeros(n, np.float32)
+            e.rmsnorm(_p(x), _p(w), _p(o1), n, eps)
+            o2 = np.zeros(n, np.float32)
+            e.vec_add(_p(o2), _p(x), _p(w), n)
+            o3 = np.zeros(n, np.float32)
+            e.swiglu(_p(x), _p(w), _p(o3), n)
+            g = x.copy()
+            e.swiglu(_p(g), _p(w), _p(g), n)
+            tk = np.zeros(16, np.float32)
+            e.lowrank_proj(_p(x), _p(vt), _p(sv), _p(tk), k, n)
+            outs.append((o1, o2, o3, g, tk))
+        for a, b in zip(*outs):
+            assert np.array_equal(a, b, equal_nan=True)
+
+    check()
+
+
 @pytest.mark.parametrize("interleaved", [1, 0])
 def test_rope_attention_bitexact_vs_reference(restated, reference_engine, rng, interleaved):
     L, S, nh, nkv, hd = 2, 64, 8, 2, 32
