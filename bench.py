@@ -49,17 +49,18 @@ def peaks():
 
 
 def parse():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=512)
-    ap.add_argument("--warmup", type=int, default=8)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--model", default="mistral-7b")
-    ap.add_argument("--mode", default="precision", choices=["precision", "turbo"])
-    ap.add_argument("--prompt", type=int, default=1536)
-    ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--e2e-steps", type=int, default=64)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap = argparse.ArgumentParser(description="Batch-1 greedy decode throughput (one JSON line on rank 0).")
+    ap.add_argument("--gpus", type=int, default=1, help="GPUs of this node (N > 1: tensor parallelism, via torchrun)")
+    ap.add_argument("--steps", type=int, default=512, help="timed decode tokens")
+    ap.add_argument("--warmup", type=int, default=8, help="untimed decode tokens before them (at least 3)")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours",
+                    help="this engine, or the reference's C engine on the host cores")
+    ap.add_argument("--model", default="mistral-7b", help="model shape (random-init weights of that architecture)")
+    ap.add_argument("--mode", default="precision", choices=["precision", "turbo"], help="packing mode")
+    ap.add_argument("--prompt", type=int, default=1536, help="KV length at the first timed token")
+    ap.add_argument("--seed", type=int, default=0, help="seed of the weights and inputs")
+    ap.add_argument("--e2e-steps", type=int, default=64, help="tokens timed through the host-facing forward_token")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the reference CPU sample (cpu_baseline)")
     ap.add_argument("--layers", type=int, default=0, help="override n_layers (debug only; not a bench number)")
     ap.add_argument("--step", choices=["fused", "per-op"], default="per-op",
                     help="one persistent launch per token (fused) or the per-operation launches in CUDA graphs")
