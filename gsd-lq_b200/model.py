@@ -33,6 +33,7 @@ import torch
 from . import _lib as L
 from . import ops
 from .gsd2 import PackedModel, read_gsd2, HexTensor
+from .tokenizer import from_config as tokenizer_from_config
 
 MAX_SEQ_LEN = 2048  # the reference's compile-time cache length (run_gpu_native_chat.py:99)
 
@@ -48,23 +49,6 @@ class _DeviceInfo:
 
     def release_all(self):
         self._m.release()
-
-
-class SimpleTokenizer:
-    """Minimal tokenizer over the header's vocabulary (decode only; prompts are token ids)."""
-
-    def __init__(self, cfg: dict):
-        self.tokens = cfg.get("tokens", [])
-        self.bos_id = cfg.get("bos_id", 1)
-        self.eos_id = cfg.get("eos_id", 2)
-
-    def decode(self, ids) -> str:
-        out = []
-        for t in ids:
-            if t in (self.bos_id, self.eos_id) or t >= len(self.tokens):
-                continue
-            out.append(self.tokens[t].replace("▁", " "))
-        return "".join(out)
 
 
 class DevicePacked:
@@ -100,7 +84,7 @@ class GSDLQModel:
             source = read_gsd2(source)
         self._load(source)
         self.cl = _DeviceInfo(self)
-        self.tokenizer = SimpleTokenizer(self.cfg)
+        self.tokenizer = tokenizer_from_config(self.cfg)  # SentencePiece BPE over the header's vocabulary
         self._graphs: dict = {}
         self.load_seconds = time.time() - t0
         if verbose:

@@ -6,6 +6,7 @@ tests never need the reference at run time:
 
     python tests/golden/make_golden.py            # everything
     python tests/golden/make_golden.py sampling   # only sampling_ref.npz
+    python tests/golden/make_golden.py tokenizer  # only tokenizer_ref.json
 
 What it records (all produced by the reference's own code):
   codebook.npz     _get_turbo_codebook(6|8) from both reference copies
@@ -19,6 +20,7 @@ What it records (all produced by the reference's own code):
                        and its fallback matvec
   sampling_ref.npz the reference's sample_token picks (temperature + top-p) on fixed logits
                    under fixed np.random seeds
+  tokenizer_ref.json the reference's SentencePiece-BPE encode/decode on a test vocabulary
 """
 from __future__ import annotations
 
@@ -124,9 +126,68 @@ def sampling_main():
     print("sampling picks", picks.shape)
 
 
+def tokenizer_vocab():
+    """A SentencePiece-style test vocabulary: control tokens, the 256 byte tokens, single characters and
+    merged pieces with seeded scores, including equal scores (leftmost-merge ties), a NaN and a -inf score
+    (never merged) and one string listed twice (its last id wins)."""
+    rng = np.random.default_rng(21)
+    toks = ["<unk>", "<s>", "</s>", "[INST]", "[/INST]", "<<SYS>>"]
+    types = [2, 3, 3, 3, 3, 3]
+    toks += [f"<0x{b:02X}>" for b in range(256)]
+    types += [6] * 256
+    chars = list("\u2581abcdefghijklmnopqrstuvwxyzABCDEFGHIJKLMNOPQRSTUVWXYZ0123456789.,!?'-:()é")
+    toks += chars
+    types += [1] * len(chars)
+    pieces = ["\u2581t", "th", "\u2581th", "he", "\u2581the", "in", "ing", "\u2581a", "an", "\u2581an", "nd",
+              "\u2581and", "er", "re", "on", "\u2581o", "\u2581of", "ll", "\u2581he", "\u2581hel", "\u2581hell",
+              "\u2581hello", "lo", "llo", "wor", "\u2581w", "\u2581wor", "\u2581world", "or", "ld", "aa", "aaa",
+              "\u2581\u2581", "\u2581\u2581\u2581\u2581", "es", "est", "\u2581t\u00e9", "\u00e9s", "ab", "bc",
+              "abc", "ab", "IN", "ST", "\u2581[", "12", "123", "\u25811"]
+    scores = [0.0] * len(toks)
+    psc = list(np.round(rng.uniform(-12.0, -1.0, len(pieces)), 1))
+    psc[pieces.index("th")] = psc[pieces.index("he")]    # a tie between overlapping pairs
+    psc[pieces.index("bc")] = float("nan")               # never merged
+    psc[pieces.index("ld")] = float("-inf")              # never merged
+    toks += pieces
+    types += [1] * len(pieces)
+    scores += [float(x) for x in psc]
+    return {"tokens": toks, "scores": scores, "token_types": types, "bos_id": 1, "eos_id": 2}
+
+
+TOKENIZER_TEXTS = [
+    "hello world", " hello world", "Hello World!", "the thing and the other", "  two  spaces", "",
+    " ", "aaaaaaa", "abcabc abc", "[INST] hello [/INST] the end", "<s>the</s>", "[INST][/INST]",
+    "t\u00e9s est", "price: 12\u20ac (123)", "emoji \U0001F600 ok", "tab\there\nnewline", "<<SYS>>of<<SYS>>",
+    "inging ing in", "x" * 40, "\u2581already marked",
+]
+
+
+def tokenizer_main():
+    """tokenizer_ref.json: the reference's MistralSentencePieceTokenizer (run_gpu_native_chat.py:660-729)
+    on tokenizer_vocab(): encode of each text (with and without BOS) and decode of fixed id lists."""
+    import json
+    sys.path.insert(0, os.path.join(REF, "gsd_lq_v2"))
+    import run_gpu_native_chat as RG
+
+    v = tokenizer_vocab()
+    tk = RG.MistralSentencePieceTokenizer(v["tokens"], v["scores"], v["token_types"], v["bos_id"], v["eos_id"])
+    enc = [[t, tk.encode(t), tk.encode(t, add_bos=False)] for t in TOKENIZER_TEXTS]
+    rng = np.random.default_rng(5)
+    id_lists = [e[1] for e in enc]
+    id_lists += [[int(i) for i in rng.integers(0, len(v["tokens"]), 12)] for _ in range(6)]
+    id_lists += [[1, 6 + 0xE2, 6 + 0x82, 6 + 0xAC, 2], [6 + 0xE2, 6 + 0x82], [6 + 0xC3, 6 + 0xA9, 270, 2]]
+    dec = [[ids, tk.decode(ids)] for ids in id_lists]
+    with open(os.path.join(HERE, "tokenizer_ref.json"), "w", encoding="utf-8") as f:
+        json.dump({"vocab": v, "encode": enc, "decode": dec}, f, ensure_ascii=False)
+    print("tokenizer cases", len(enc), len(dec))
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["sampling"]:
         sampling_main()
+    elif sys.argv[1:] == ["tokenizer"]:
+        tokenizer_main()
     else:
         main()
         sampling_main()
+        tokenizer_main()
