@@ -313,3 +313,29 @@ def test_gsd2_roundtrip_property(tmp_path):
 
     check()
     assert len(set(seen)) >= 8, seen
+
+
+def test_arena_alignment_and_upload_from_mmap(tmp_path):
+    """The device arena (here on CPU tensors) takes every blob of a memory-mapped .gsd2 straight from the
+    mapped pages, each at a 256-byte-aligned address, byte for byte; overflow is an error, not a wrap."""
+    import warnings
+    import torch
+    from gsdlq_b200.ops import Arena
+    cfg = P.make_config("tiny", n_layers=1, hidden_size=128, n_heads=2, n_kv_heads=1, head_dim=64,
+                        ffn_size=192, vocab_size=64)
+    p = str(tmp_path / "m.gsd2")
+    G.write_gsd2(p, P.random_model(cfg, "precision", seed=4))
+    r = G.read_gsd2(p, mmap=True)
+    blobs = [a for t in r.hex.values() for a in t.blobs().values()]
+    assert any(isinstance(a, np.memmap) or isinstance(getattr(a, "base", None), np.memmap) for a in blobs)
+    ar = Arena(Arena.bytes_needed(blobs), device="cpu")
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", UserWarning)  # torch notes that mapped pages are read-only
+        outs = [ar.put(a) for a in blobs]
+    for a, d in zip(blobs, outs):
+        if a.nbytes:
+            assert d.data_ptr() % Arena.ALIGN == 0
+        assert np.array_equal(d.numpy(), np.ascontiguousarray(a).reshape(-1).view(np.uint8))
+    with pytest.raises(MemoryError):
+        ar.put(np.zeros(Arena.ALIGN + 1, np.uint8))
+    assert torch.is_tensor(outs[0])
