@@ -1,5 +1,6 @@
 """The C-ABI library loads without a GPU and exports every symbol include/gsdlq.h declares."""
 import ctypes
+import os
 
 import numpy as np
 import pytest
@@ -73,3 +74,38 @@ def test_batched_and_noalloc_argument_errors_before_launch():
     for kw in (dict(n_pts=0), dict(n_pts=257), dict(k=4), dict(k=17, U=A, tmp=A), dict(cols=100), dict(rows=0),
                dict(codes=odd), dict(x=None), dict(y=None)):
         assert mv(**kw) == -1, kw
+
+
+def test_header_is_c99_and_links_from_c(tmp_path):
+    """include/gsdlq.h compiles as pedantic C99, and a C program links libgsdlq_cuda.so and calls its
+    host-only entry points (version, status strings, codebook, RoPE table) without a GPU."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    inc, libdir = os.path.join(root, "include"), os.path.dirname(L.load()._name)
+    src = tmp_path / "use_gsdlq.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include "gsdlq.h"
+int main(void) {
+  float xy[2 * 256];
+  float rope[4 * 8 * 2];
+  int n6 = gsdlq_codebook(6, xy, 256), n8 = gsdlq_codebook(8, xy, 256);
+  int st = gsdlq_rope_table(rope, 4, 16, 10000.0f);
+  printf("%s|%s|%d|%d|%d|%d\n", gsdlq_version(), gsdlq_status_string(GSDLQ_ERR_INVALID), n6, n8, st,
+         gsdlq_hex2d_matvec(0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 16, 64, 0, 217, 0));
+  return 0;
+}
+''')
+    exe = tmp_path / "use_gsdlq"
+    r = subprocess.run([cc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", inc, str(src), "-o", str(exe),
+                        "-L", libdir, "-lgsdlq_cuda", "-Wl,-rpath," + libdir], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, out.stderr
+    ver, msg, n6, n8, st, bad = out.stdout.strip().split("|")
+    assert ver.startswith("0.") and msg == "invalid argument"
+    assert (int(n6), int(n8), int(st), int(bad)) == (127, 217, 0, -1)
