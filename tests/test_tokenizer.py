@@ -75,3 +75,18 @@ def test_round_trip(golden):
         assert ids[0] == 1 and tk.decode(ids + [2]) == " " + text
     # only the first text part gets the marker: text after a control token keeps its own start
     assert tk.decode(tk.encode("a[INST]b")) == " a[INST]b"
+
+
+def test_from_gsd2_header():
+    """The tokenizer the model object builds from a .gsd2 header (the golden tiny model's synthetic
+    vocabulary: control tokens, 256 byte tokens and "▁w<i>" words, no single characters): text falls back
+    to byte tokens, which decode to the marked text, and word ids decode to their words."""
+    import gsdlq_b200.gsd2 as G
+    cfg = G.read_gsd2(os.path.join(GOLDEN, "tiny_precision.gsd2")).config
+    tk = from_config(cfg)
+    assert (tk.bos_id, tk.eos_id) == (cfg["bos_id"], cfg["eos_id"])
+    ids = tk.encode("w300 Zé")
+    assert ids[0] == cfg["bos_id"] and all(tk.token_types[i] == 6 for i in ids[1:])
+    assert len(ids) - 1 == len("▁w300▁Zé".encode("utf-8"))
+    assert tk.decode(ids) == "▁w300▁Zé"  # byte tokens keep the marker, as the reference's decode does
+    assert tk.decode([tk.vocab["▁w300"], tk.vocab["▁w301"]]) == " w300 w301"
