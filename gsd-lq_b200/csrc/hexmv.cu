@@ -473,6 +473,8 @@ extern "C" int gsdlq_unit_kinks(const uint32_t* row_ptr, const uint16_t* kink_co
 namespace gsdlq {
 static __device__ __align__(256) unsigned char g_noalloc_ws[GSDLQ_NOALLOC_WS_BYTES];
 static std::atomic<void*> g_noalloc_addr[64];  // per device; racing set-ups store the same address
+static_assert(sizeof(unsigned) * CTL_WORDS + 256 + 132ull * GSDLQ_NOALLOC_MAX_STRIPS + 16 <= GSDLQ_NOALLOC_WS_BYTES,
+              "GSDLQ_NOALLOC_MAX_STRIPS strips must fit the fixed scratch");
 }  // namespace gsdlq
 
 extern "C" int gsdlq_hex2d_matvec_noalloc(const float* x, const uint8_t* codes, const uint16_t* scales,
@@ -504,7 +506,9 @@ extern "C" int gsdlq_hex2d_matvec_noalloc(const float* x, const uint8_t* codes, 
   P.xy_table = xy_table;
   P.n_pts = n_pts;
   P.tmp_k_ext = k_dim > 0 ? tmp_k : nullptr;
-  const int st = hexmv_plan(P);
+  int st = hexmv_plan(P);
+  if (st != GSDLQ_OK) return st;
+  st = hexmv_check_io(P);  // every argument error is returned before the set-up and the memset
   if (st != GSDLQ_OK) return st;
   const size_t need = hexmv_ws_bytes_for(P.n_strips, P.nmat);
   if (need > (size_t)GSDLQ_NOALLOC_WS_BYTES) return GSDLQ_ERR_UNSUPPORTED;  // beyond the fixed scratch

@@ -247,8 +247,68 @@ def random_model(cfg: dict, mode: str = "precision", seed: int = 0, std: float =
                        extra={"packer": {"name": "gsdlq_b200.packer", "seed": seed, "std": std}})
 
 
-__all__ = ["pack_matrix", "quantize_lattice", "dequant", "random_model", "make_config", "CONFIGS",
-           "MODES", "LINEAR_NAMES", "linear_shapes"]
+def random_packed_model(cfg: dict, mode: str = "precision", seed: int = 0) -> PackedModel:
+    """Format-valid packed tensors of a whole decoder, drawn directly with NumPy (no quantisation).
+
+    Codes are uniform over the radius-8 lattice, scales are the fp16 value the packer gives a
+    N(0, 0.02^2) group, U/Vt are small fp16 values, S is positive, and every row carries the mode's
+    kink count at distinct ascending columns.  The decode engines do the same work on these bytes
+    as on packed weights (no step depends on the values), so this stands in for ``random_model`` at
+    shapes where quantising and factorising with NumPy would take many minutes.  Uses no GPU."""
+    rng = np.random.default_rng(seed)
+    shapes = linear_shapes(cfg)
+    hexes: dict[str, HexTensor] = {}
+    R, K, _ = mode_params(mode, 64)
+    n_pts = codebook.num_points(R)
+    scale = np.float16(0.02 * 3.0 / (R * float(FIT))).view(np.uint16)
+    # codes: slices of one 64 MiB pool of uniform codes at random offsets (drawing gigabytes one by one
+    # with NumPy's generator would take most of a minute)
+    pool = rng.integers(0, n_pts, 1 << 26, dtype=np.uint8)
+
+    def draw(n):
+        out, i, off = np.empty(n, np.uint8), 0, int(rng.integers(0, pool.size))
+        while i < n:
+            m = min(n - i, pool.size - off)
+            out[i:i + m] = pool[off:off + m]
+            i, off = i + m, 0
+        return out
+    for name in hex_names(cfg["n_layers"]):
+        key = name.split(".")[-2]
+        r, c = shapes[key] if key in shapes else (cfg["vocab_size"], cfg["hidden_size"])
+        _, k, kn = mode_params(mode, c)
+        codes = draw(r * c // 2)
+        scales = np.full(r * c // 64, scale, np.uint16)
+        if kn:
+            kn = min(kn, c)
+            # distinct ascending columns per row: one random offset inside each of kn equal bins
+            bins = (np.arange(kn, dtype=np.int64) * c) // kn
+            width = np.diff(np.append(bins, c))
+            cols = (bins[None, :] + (rng.random((r, kn)) * width[None, :]).astype(np.int64)).astype(np.uint16)
+            deltas = (rng.standard_normal(r * kn, dtype=np.float32) * np.float32(0.002))
+            row_ptr = (np.arange(r + 1, dtype=np.uint64) * kn).astype(np.uint32)
+            kc = cols.reshape(-1)
+        else:
+            kc, deltas, row_ptr = np.zeros(0, np.uint16), np.zeros(0, np.float32), np.zeros(r + 1, np.uint32)
+        U = S = Vt = None
+        if k:
+            U = (rng.standard_normal(r * k, dtype=np.float32) * np.float32(0.05)).astype(np.float16).view(np.uint16)
+            S = np.sort(rng.random(k, dtype=np.float32))[::-1].copy() * np.float32(0.5)
+            Vt = (rng.standard_normal(k * c, dtype=np.float32) * np.float32(0.05)).astype(np.float16).view(np.uint16)
+        hexes[name] = HexTensor(rows=r, cols=c, radius=R, k_dim=k, codes=codes, scales=scales, row_ptr=row_ptr,
+                                kink_cols=kc, kink_deltas=deltas, U=U, S=S, Vt=Vt)
+    H = cfg["hidden_size"]
+    dense = {"token_embd.weight":
+             (rng.standard_normal((cfg["vocab_size"], H), dtype=np.float32) * np.float32(0.02)).astype(np.float16),
+             "output_norm.weight": np.ones(H, np.float32)}
+    for l in range(cfg["n_layers"]):
+        dense[f"blk.{l}.attn_norm.weight"] = np.ones(H, np.float32)
+        dense[f"blk.{l}.ffn_norm.weight"] = np.ones(H, np.float32)
+    return PackedModel(config=cfg, hex=hexes, dense=dense, avg_bpw=compute_avg_bpw(hexes), mode=mode,
+                       extra={"packer": {"name": "gsdlq_b200.packer.random_packed_model", "seed": seed}})
+
+
+__all__ = ["pack_matrix", "quantize_lattice", "dequant", "random_model", "random_packed_model", "make_config",
+           "CONFIGS", "MODES", "LINEAR_NAMES", "linear_shapes"]
 
 
 # ---------------------------------------------------------------------------------------

@@ -159,8 +159,12 @@ class TensorParallel:
 
     # called inside the captured layer step
     def allreduce(self, model, which: str):
+        self.allreduce_buf(model.x)
+
+    def allreduce_buf(self, buf):
+        """Sum of ``buf`` over the ranks, in place (the residual exchange of one O or down projection)."""
         import torch.distributed as dist
-        dist.all_reduce(model.x, op=dist.ReduceOp.SUM, group=self.group)
+        dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group)
 
     def finish_head(self, model):
         """Global greedy pick: all-reduce MAX of the 64-bit keys (MSB flipped so signed order = unsigned)."""

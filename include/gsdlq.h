@@ -225,8 +225,12 @@ int gsdlq_unit_kinks(const uint32_t *row_ptr, const uint16_t *kink_cols, const f
                      int rows, int cols, uint32_t *unit_kink_off, uint32_t *unit_kinks,
                      gsdlq_stream_t stream);
 
-/* Size of the library's fixed device scratch array used by gsdlq_hex2d_matvec_noalloc. */
+/* Size of the library's fixed device scratch array used by gsdlq_hex2d_matvec_noalloc, and the
+ * most 16-row strips a call may have: a launch needs 768 + 132 * strips bytes of it (control
+ * words, one count and sixteen 8-byte partial sums per strip), so at most
+ * (GSDLQ_NOALLOC_WS_BYTES - 768) / 132 = 31 769 strips, i.e. rows <= 508 304. */
 #define GSDLQ_NOALLOC_WS_BYTES (4u << 20)
+#define GSDLQ_NOALLOC_MAX_STRIPS 31769u
 
 /* gsdlq_hex2d_matvec without any device allocation.  No counterpart in the reference:
  * the reference's matvec runs on the host and needs no scratch.
@@ -246,9 +250,9 @@ int gsdlq_unit_kinks(const uint32_t *row_ptr, const uint16_t *kink_cols, const f
  *   launches.  It calls no cudaMalloc, cudaFree or other allocating routine.
  * - All calls share the one array.  Calls that may overlap on the GPU (different streams,
  *   or different host threads without ordering) race on it and give wrong results.
- * - A launch whose scratch need exceeds GSDLQ_NOALLOC_WS_BYTES returns
- *   GSDLQ_ERR_UNSUPPORTED before touching the device.  About 16 000 row strips of 16 rows
- *   fit; use gsdlq_hex2d_matvec or gsdlq_linear beyond that. */
+ * - Argument errors and a matrix of more than GSDLQ_NOALLOC_MAX_STRIPS strips of 16 rows
+ *   (rows > 508 304) return GSDLQ_ERR_INVALID or GSDLQ_ERR_UNSUPPORTED before anything
+ *   touches the device; use gsdlq_hex2d_matvec or gsdlq_linear for larger matrices. */
 int gsdlq_hex2d_matvec_noalloc(const float *x, const uint8_t *codes, const uint16_t *scales,
                                const float *xy_table, const uint16_t *U, const float *tmp_k,
                                const uint32_t *kink_row_ptr, const uint16_t *kink_cols,

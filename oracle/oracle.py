@@ -38,9 +38,24 @@ REF_LIB = os.path.join(HERE, "_ref", "libgsd_cpu.so")
 MAX_SEQ_LEN = 2048  # gsd_lq_cpu_runtime.py:22
 
 
+def reference_dir() -> str | None:
+    """Where the reference source tree is: $GSDLQ_REFERENCE, else the `reference_path` that the
+    repository's BASELINE.json records; None when neither names an existing directory."""
+    d = os.environ.get("GSDLQ_REFERENCE")
+    if not d:
+        try:
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                d = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            d = None
+    return d if d and os.path.isdir(d) else None
+
+
 def build(quiet: bool = True) -> None:
     """Build the restatement (and, where the reference tree exists, the reference) with make."""
-    out = subprocess.run(["make", "-C", HERE, "all"], capture_output=True, text=True)
+    ref = reference_dir()
+    cmd = ["make", "-C", HERE, "all"] + ([f"REF_DIR={ref}"] if ref else [])
+    out = subprocess.run(cmd, capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
     if not quiet:

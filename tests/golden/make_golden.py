@@ -1,8 +1,8 @@
 """Generate the golden fixtures in this directory from the REFERENCE implementation.
 
-Run in a container that holds the reference tree (default location taken from
-$GSDLQ_REFERENCE, else the standard mount); the fixtures are committed so the
-tests never need the reference at run time:
+Run in a container that holds the reference tree (its location taken from
+$GSDLQ_REFERENCE, else from BASELINE.json's reference_path); the fixtures are
+committed so the tests never need the reference at run time:
 
     python tests/golden/make_golden.py            # everything
     python tests/golden/make_golden.py sampling   # only sampling_ref.npz
@@ -34,8 +34,15 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
-REF = os.environ.get("GSDLQ_REFERENCE", "/root/reference")
 TOKENS = [1, 17, 300, 42, 255, 7, 299, 100]
+
+
+def reference_tree() -> str:
+    import oracle as O
+    ref = O.reference_dir()  # $GSDLQ_REFERENCE, else BASELINE.json's reference_path
+    if ref is None:
+        raise SystemExit("the reference source tree is needed: set GSDLQ_REFERENCE")
+    return ref
 
 
 def main():
@@ -44,7 +51,7 @@ def main():
     import oracle as O  # only to locate/build the reference .so
 
     O.build()
-    sys.path.insert(0, os.path.join(REF, "gsd_lq_v2"))
+    sys.path.insert(0, os.path.join(reference_tree(), "gsd_lq_v2"))
     import gsd_lq_cpu_runtime as R
     import run_gpu_native_chat as RG
 
@@ -111,7 +118,7 @@ def sampling_logits():
 
 def sampling_main():
     """sampling_ref.npz: the reference's sample_token (gsd_lq_cpu_runtime.py:422-443) under np.random.seed(s)."""
-    sys.path.insert(0, os.path.join(REF, "gsd_lq_v2"))
+    sys.path.insert(0, os.path.join(reference_tree(), "gsd_lq_v2"))
     import gsd_lq_cpu_runtime as R
 
     logits = sampling_logits()
@@ -166,7 +173,7 @@ def tokenizer_main():
     """tokenizer_ref.json: the reference's MistralSentencePieceTokenizer (run_gpu_native_chat.py:660-729)
     on tokenizer_vocab(): encode of each text (with and without BOS) and decode of fixed id lists."""
     import json
-    sys.path.insert(0, os.path.join(REF, "gsd_lq_v2"))
+    sys.path.insert(0, os.path.join(reference_tree(), "gsd_lq_v2"))
     import run_gpu_native_chat as RG
 
     v = tokenizer_vocab()

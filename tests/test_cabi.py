@@ -72,8 +72,10 @@ def test_batched_and_noalloc_argument_errors_before_launch():
         return lib.gsdlq_hex2d_matvec_noalloc(x, codes, A, A, U, tmp, A, A, A, y, rows, cols, k, n_pts, None)
 
     for kw in (dict(n_pts=0), dict(n_pts=257), dict(k=4), dict(k=17, U=A, tmp=A), dict(cols=100), dict(rows=0),
-               dict(codes=odd), dict(x=None), dict(y=None)):
+               dict(codes=odd), dict(x=None), dict(y=None), dict(x=odd)):
         assert mv(**kw) == -1, kw
+    # one strip more than the fixed scratch holds: refused as unsupported, still before any CUDA call
+    assert mv(rows=16 * (31769 + 1), cols=64) == -3
 
 
 def test_header_is_c99_and_links_from_c(tmp_path):

@@ -18,9 +18,25 @@ MATVEC_TOL = 1e-3
 
 
 def rel_err(y, yr):
+    """Mixed error: max |y - yr| / (|yr| + rms(yr)) -- relative for large entries, absolute (in units of
+    the rms) for entries near zero, where a plain relative error is undefined."""
     y, yr = np.asarray(y, np.float64), np.asarray(yr, np.float64)
     scale = np.abs(yr) + np.sqrt(np.mean(yr ** 2)) + 1e-30
     return float(np.max(np.abs(y - yr) / scale))
+
+
+def plain_rel_err(y, yr):
+    """Plain relative error max |y - yr| / |yr| over the entries with |yr| above the rms of yr."""
+    y, yr = np.asarray(y, np.float64), np.asarray(yr, np.float64)
+    big = np.abs(yr) > np.sqrt(np.mean(yr ** 2))
+    if not big.any():
+        return 0.0
+    return float(np.max(np.abs(y[big] - yr[big]) / np.abs(yr[big])))
+
+
+def matvec_err(y, yr):
+    """The matvec bar: both the mixed error and the plain relative error of the large entries."""
+    return max(rel_err(y, yr), plain_rel_err(y, yr))
 
 
 def _p(a):
@@ -112,7 +128,7 @@ def test_hex2d_matvec_dropin(env, restated, rng, rows, cols, k, nnz, radius):
     torch.cuda.synchronize()
     if k:
         assert rel_err(tk.cpu().numpy()[:k], tk_host[:k]) < 1e-5
-    assert rel_err(y.cpu().numpy(), yr) < MATVEC_TOL
+    assert matvec_err(y.cpu().numpy(), yr) < MATVEC_TOL
     assert L.device_flags() == 0
 
 

@@ -18,7 +18,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
-from test_gpu_kernels import rand_hex, rel_err, dev, MATVEC_TOL  # noqa: E402
+from test_gpu_kernels import rand_hex, oracle_rec, matvec_err, dev, MATVEC_TOL  # noqa: E402
 
 
 def _vp(t):
@@ -37,7 +37,37 @@ def test_noalloc_matches_allocating_dropin(cuda_lib, rng, rows, cols, k, nnz):
     import gsdlq_b200._lib as L
     lib = cuda_lib
     L.device_flags()  # start from a clear flag word
+    import oracle
     t = rand_hex(rng, rows, cols, k=k, nnz=nnz, radius=8)
+    h = ops.DeviceHex(t)
+    xy = dev(cb.xy_table(8))
+    x = rng.standard_normal(cols).astype(np.float32)
+    xd = dev(x)
+    tk = torch.zeros(16, device="cuda")
+    ops.lowrank_proj(xd, h, tk)
+    y_ref = torch.zeros(rows, device="cuda")
+    assert _matvec(lib.gsdlq_hex2d_matvec, xd, h, xy, tk, y_ref) == 0
+    torch.cuda.synchronize()
+    ref = y_ref.cpu().numpy()
+    # the allocating entry point itself against the CPU oracle of the reference's matvec
+    assert matvec_err(ref, oracle.CEngine.restatement().matvec(x, oracle_rec(t))) < MATVEC_TOL
+    for call in range(2):  # the shared scratch must serve a second call after the first
+        y = torch.full((rows,), float("nan"), device="cuda")
+        assert _matvec(lib.gsdlq_hex2d_matvec_noalloc, xd, h, xy, tk, y) == 0
+        torch.cuda.synchronize()
+        assert matvec_err(y.cpu().numpy(), ref) < MATVEC_TOL, f"call {call}"
+    assert L.device_flags() == 0
+
+
+def test_noalloc_at_the_strip_limit(cuda_lib, rng):
+    """The tallest matrix the fixed scratch holds (GSDLQ_NOALLOC_MAX_STRIPS strips of 16 rows, 64
+    columns) against the allocating drop-in, twice; one strip more is refused."""
+    import gsdlq_b200.codebook as cb
+    import gsdlq_b200.ops as ops
+    lib = cuda_lib
+    max_strips = 31769
+    rows, cols = 16 * max_strips, 64
+    t = rand_hex(rng, rows, cols, k=4, nnz=1, radius=8)
     h = ops.DeviceHex(t)
     xy = dev(cb.xy_table(8))
     xd = dev(rng.standard_normal(cols).astype(np.float32))
@@ -47,12 +77,14 @@ def test_noalloc_matches_allocating_dropin(cuda_lib, rng, rows, cols, k, nnz):
     assert _matvec(lib.gsdlq_hex2d_matvec, xd, h, xy, tk, y_ref) == 0
     torch.cuda.synchronize()
     ref = y_ref.cpu().numpy()
-    for call in range(2):  # the shared scratch must serve a second call after the first
+    for call in range(2):
         y = torch.full((rows,), float("nan"), device="cuda")
         assert _matvec(lib.gsdlq_hex2d_matvec_noalloc, xd, h, xy, tk, y) == 0
         torch.cuda.synchronize()
-        assert rel_err(y.cpu().numpy(), ref) < MATVEC_TOL, f"call {call}"
-    assert L.device_flags() == 0
+        assert matvec_err(y.cpu().numpy(), ref) < MATVEC_TOL, f"call {call}"
+    h.rows = rows + 16  # claimed height only: refused before any buffer is read
+    y = torch.zeros(16, device="cuda")
+    assert _matvec(lib.gsdlq_hex2d_matvec_noalloc, xd, h, xy, tk, y) == -3
 
 
 def test_noalloc_rejects_oversized_launch(cuda_lib, rng):
