@@ -283,8 +283,9 @@ def cpu_reference_sample(host_model, P0, seed):
 # ---- our engine ------------------------------------------------------------------------------
 def kind_times(model, world):
     """Device time of each launch kind of a step, each kind as one CUDA graph of its launches over all
-    layers back to back (distinct weights per layer, so the weights stream from HBM), with the kind's
-    algorithmic bytes per launch.  Consecutive launches alternate between the two workspaces."""
+    layers back to back (distinct weights per layer, so the weights stream from HBM; no L2 prefetch),
+    with the kind's algorithmic bytes per launch.  Consecutive launches alternate between the two
+    workspaces."""
     import torch
     from gsdlq_b200 import ops
     kinds = {"qkv": 0, "attn": 1, "o": 2, "gate_up": 3, "down": 4}
@@ -304,8 +305,13 @@ def kind_times(model, world):
            "down": nb("ffn_down") + 4 * model.ffn_local + 8 * H,
            "head": model.hex["output.weight"].nbytes() + 8 * H + 4 * model.vocab_local}
     rep = 5
+
+    def alone(j):  # a copy without the L2 prefetch of the next launch's weights (nothing would read them)
+        c = type(j).from_buffer_copy(j)
+        c.prefetch.n = 0
+        return c
     for name, idx in list(kinds.items()) + [("head", None)]:
-        jobs = [lj[idx] for lj in model.layer_jobs] if idx is not None else [model.head_job] * 2
+        jobs = [alone(lj[idx]) for lj in model.layer_jobs] if idx is not None else [alone(model.head_job)] * 2
 
         def run_all():
             for i, j in enumerate(jobs):
@@ -479,8 +485,6 @@ def run_ours(args):
     launches_per_step = 1 if model.fused_step else 5 * model.n_layers + 2
     if rank == 0:
         conf = workload_config(args, world)
-        conf.update({"avg_bpw": round(model.avg_bpw, 4), "step": "fused" if model.fused_step else "per-op",
-                     "n_layers": model.n_layers, "bytes_per_step_gb": round(bytes_tok / 1e9, 3)})
         line = {
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -500,6 +504,8 @@ def run_ours(args):
             "ids_head": ids[:8].tolist(),
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks, "pack_s": round(pack_s, 2), "prefill_s": round(prefill_s, 2),
+            "avg_bpw": round(model.avg_bpw, 4), "step": "fused" if model.fused_step else "per-op",
+            "n_layers": model.n_layers, "l2_prefetch": model.prefetch,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -530,14 +536,14 @@ def run_reference(args):
               f"argmax) after {max(1, args.warmup)} warm-up tokens, OpenMP threads = {cores}; packed bytes of the "
               f"same shapes drawn with NumPy (random_packed_model)")
     conf = workload_config(args, world)
-    conf.update({"avg_bpw": round(host.avg_bpw, 4), "parallelism": "host cores"})
     line = {"metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": n,
             "warmup": max(1, args.warmup), "ms_per_step": 1e3 * secs / n, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": vs_published(args, tok_s), "dtype": "f32",
             "data": "synthetic", "impl": "reference", "config": conf,
             "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
             "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "token_ms": [round(1e3 * t, 1) for t in ts[:8]], "pack_s": round(pack_s, 2)}
+            "token_ms": [round(1e3 * t, 1) for t in ts[:8]], "pack_s": round(pack_s, 2),
+            "avg_bpw": round(host.avg_bpw, 4), "runs_on": f"host cores ({cores} OpenMP threads), no GPU"}
     print(json.dumps(line), flush=True)
 
 

@@ -30,20 +30,27 @@ class HexMat(ctypes.Structure):
                 ("radius", i32), ("unit_kink_off", vp), ("unit_kinks", vp)]
 
 
+MAX_PREFETCH = 16
+
+
+class Prefetch(ctypes.Structure):
+    _fields_ = [("ptr", vp * MAX_PREFETCH), ("bytes", ctypes.c_uint64 * MAX_PREFETCH), ("n", i32)]
+
+
 class LinearJob(ctypes.Structure):
     _fields_ = [("mat", HexMat * 3), ("n_mat", i32), ("input_mode", i32), ("x", vp), ("norm_w", vp),
                 ("eps", f32), ("embed", vp), ("token", vp), ("vocab", i32), ("x_out", vp), ("epilogue", i32),
                 ("y", vp * 3), ("resid", vp), ("k_cache", vp), ("v_cache", vp), ("pos", vp), ("rope_cs", vp),
                 ("layer", i32), ("max_seq", i32), ("head_dim", i32), ("interleaved", i32),
                 ("argmax_key", vp), ("argmax_index_base", i32), ("fwd_vt", vp * 3), ("fwd_k", i32 * 3),
-                ("fwd_norm_w", vp), ("fwd_acc", vp), ("lr_forwarded", i32)]
+                ("fwd_norm_w", vp), ("fwd_acc", vp), ("lr_forwarded", i32), ("prefetch", Prefetch)]
 
 
 class AttnJob(ctypes.Structure):
     _fields_ = [("q", vp), ("k_cache", vp), ("v_cache", vp), ("out", vp), ("pos_dev", vp), ("pos_val", i32),
                 ("layer", i32), ("n_heads", i32), ("n_kv_heads", i32), ("head_dim", i32), ("max_seq", i32),
                 ("sm_scale", f32), ("block_table", vp), ("page_size", i32), ("partial", vp), ("workspace", vp),
-                ("fwd_vt", vp), ("fwd_k", i32), ("fwd_acc", vp)]
+                ("fwd_vt", vp), ("fwd_k", i32), ("fwd_acc", vp), ("prefetch", Prefetch)]
 
 
 class DecodeLayer(ctypes.Structure):

@@ -171,6 +171,8 @@ __global__ void __launch_bounds__(AC_THREADS, 1) attn_cluster_kernel(const __gri
     s_f[tid] = 0.f;
   }
   for (int i = 0; i < min(ntiles, AC_NBUF); ++i) issue(i, 0);
+  // the later launches' weights go into L2 while attention runs (it reads little from HBM)
+  if (warp == AC_THREADS / 32 - 1) issue_prefetch(J.prefetch, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y, lane);
   const int fk = J.fwd_acc != nullptr ? J.fwd_k : 0;
   const int col0 = kvh * GQ * HD + rank * OPC;  // this CTA's first output column of the O linear
   {

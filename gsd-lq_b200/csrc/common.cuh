@@ -228,6 +228,38 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
+// Bulk prefetch of `bytes` (a multiple of 16) at a 16-byte aligned global address into the L2 cache.
+__device__ __forceinline__ void l2_prefetch_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// CTA `cta` of `n_cta` issues its share of a launch's L2 prefetch list with the 32 lanes of one
+// warp: range r is cut into n_cta equal 16-byte-aligned slices and this CTA's slice into 16 KB bulk
+// prefetches dealt round-robin to the lanes.  (The host checked the alignment and n <= 16.)
+__device__ __forceinline__ void issue_prefetch(const gsdlq_prefetch_t& pf, unsigned cta, unsigned n_cta, int lane) {
+  const int n = pf.n < GSDLQ_MAX_PREFETCH ? pf.n : GSDLQ_MAX_PREFETCH;
+  constexpr unsigned long long CHUNK = 1024;  // 16-byte units per bulk prefetch
+  for (int r = 0; r < n; ++r) {
+    const unsigned long long units = pf.bytes[r] >> 4;
+    const unsigned long long u0 = units * cta / n_cta, u1 = units * (cta + 1) / n_cta;
+    const char* base = static_cast<const char*>(pf.ptr[r]);
+    for (unsigned long long u = u0 + (unsigned long long)lane * CHUNK; u < u1; u += 32 * CHUNK) {
+      const unsigned long long e = u + CHUNK < u1 ? u + CHUNK : u1;
+      l2_prefetch_bulk(base + u * 16, (uint32_t)((e - u) * 16));
+    }
+  }
+}
+
+// Host check of a prefetch list: n in [0, GSDLQ_MAX_PREFETCH], 16-byte aligned ranges.
+inline bool prefetch_ok(const gsdlq_prefetch_t& pf) {
+  if (pf.n < 0 || pf.n > GSDLQ_MAX_PREFETCH) return false;
+  for (int r = 0; r < pf.n; ++r) {
+    if ((pf.bytes[r] & 15u) != 0u) return false;
+    if (pf.bytes[r] != 0u && (pf.ptr[r] == nullptr || (reinterpret_cast<uintptr_t>(pf.ptr[r]) & 15u) != 0u)) return false;
+  }
+  return true;
+}
+
 // Monotone float -> uint32 map (larger float -> larger key).
 __device__ __forceinline__ uint32_t ordered_key(float v) {
   const uint32_t b = __float_as_uint(v);

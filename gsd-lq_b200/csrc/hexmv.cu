@@ -187,6 +187,7 @@ static int hexmv_check_fwd(const HexmvParams& P) {
 int hexmv_check_io(const HexmvParams& P) {
   const gsdlq_linear_job_t& J = P.job;
   if (hexmv_check_fwd(P) != GSDLQ_OK) return GSDLQ_ERR_INVALID;
+  if (!prefetch_ok(J.prefetch)) return GSDLQ_ERR_INVALID;
   if (J.input_mode < 0 || J.input_mode > 2) return GSDLQ_ERR_INVALID;
   if (J.input_mode == GSDLQ_IN_PLAIN && !J.x) return GSDLQ_ERR_INVALID;
   if (J.input_mode == GSDLQ_IN_RMSNORM && (!J.x || !J.norm_w)) return GSDLQ_ERR_INVALID;

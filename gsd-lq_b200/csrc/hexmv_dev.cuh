@@ -605,6 +605,8 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
 
   if (helper) {
     // ==== helper warps: low-rank slice partials and the kink sums of the strips this CTA owns ===
+    // the later launches' weights go into L2 first, while this launch waits for its input
+    if (!MEGA && warp == HX_STREAM) issue_prefetch(J.prefetch, blockIdx.x, gridDim.x, lane);
     const int hw = blockIdx.x * HX_HELP + (warp - HX_STREAM);
     const int H = gridDim.x * HX_HELP;
     const int c8_0 = hw * P.lr_chunks;

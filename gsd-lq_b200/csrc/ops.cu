@@ -219,6 +219,7 @@ static int attention_launch(const gsdlq_attn_job_t& J, cudaStream_t s) {
   if (J.fwd_acc && (J.fwd_k <= 0 || J.fwd_k > 48 || !J.fwd_vt || (reinterpret_cast<uintptr_t>(J.fwd_acc) & 7u)))
     return GSDLQ_ERR_INVALID;
   if (J.head_dim != 128 && J.head_dim != 64 && J.head_dim != 32) return GSDLQ_ERR_UNSUPPORTED;
+  if (!prefetch_ok(J.prefetch)) return GSDLQ_ERR_INVALID;  // (only the cluster kernel issues it)
   // the cluster kernel copies the forwarded Vt slice in 4-byte pieces
   if (attn_cluster_enabled() && !(J.fwd_acc && (reinterpret_cast<uintptr_t>(J.fwd_vt) & 3u))) {
     cudaError_t e;

@@ -25,6 +25,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 import time
 
 import numpy as np
@@ -61,7 +62,7 @@ class DevicePacked:
 class GSDLQModel:
     def __init__(self, source, rope_interleaved: int = 1, device=None, max_seq: int = MAX_SEQ_LEN,
                  use_graph: bool = True, verbose: bool = False, tp=None, unit_kinks: bool = False,
-                 fused_step: bool = False, lr_forward: bool = True):
+                 fused_step: bool = False, lr_forward: bool = True, prefetch: int | None = None):
         t0 = time.time()
         if not torch.cuda.is_available():
             raise RuntimeError("GSDLQModel needs a CUDA device (there is no CPU path)")
@@ -79,6 +80,8 @@ class GSDLQModel:
         self.unit_kinks = unit_kinks
         self._want_fused = fused_step and tp is None
         self.lr_forward = lr_forward
+        # L2 prefetch policy of the launches (see _wire_prefetch); GSDLQ_PREFETCH overrides the default
+        self.prefetch = int(os.environ.get("GSDLQ_PREFETCH", "1")) if prefetch is None else int(prefetch)
         self._plans: dict = {}
         if isinstance(source, str):
             source = read_gsd2(source)
@@ -231,6 +234,7 @@ class GSDLQModel:
         self.ws_of[id(self.head_job)] = self.ws[k % 2]
         if self.tp is None and self.lr_forward:
             self._wire_forwarding()
+        self._wire_prefetch(self.prefetch)
 
     def _wire_forwarding(self):
         """Low-rank forwarding: every op whose output is the next linear's input adds that linear's
@@ -263,6 +267,51 @@ class GSDLQModel:
             if l + 1 < self.n_layers:
                 into(dn, self.layer_jobs[l + 1][0], [hx(l + 1, n) for n in ("attn_q", "attn_k", "attn_v")],
                      self.norms[f"blk.{l + 1}.attn_norm.weight"])
+
+    @staticmethod
+    def _ranges(mats) -> list[tuple[int, int]]:
+        """(address, bytes) of the packed blobs of ``mats`` that a launch streams: codes, scales,
+        kink columns and deltas, U and Vt (16-byte aligned starts; lengths cut to multiples of 16)."""
+        out = []
+        for h in mats:
+            for t in (h.codes, h.scales, h.kink_cols, h.kink_deltas, h.U, h.Vt):
+                if t is None or t.numel() == 0:
+                    continue
+                p, n = t.data_ptr(), t.numel() * t.element_size()
+                n -= n % 16
+                if p % 16 == 0 and n > 0:
+                    out.append((p, n))
+        return out
+
+    @staticmethod
+    def _set_prefetch(job, ranges):
+        ranges = ranges[:L.MAX_PREFETCH]
+        job.prefetch.n = len(ranges)
+        for i, (p, n) in enumerate(ranges):
+            job.prefetch.ptr[i] = p
+            job.prefetch.bytes[i] = n
+
+    def _wire_prefetch(self, policy: int):
+        """L2 prefetch of later launches' weights (gsdlq_prefetch_t): a launch fetches into L2 the
+        packed weights that the next launches will stream, so that HBM keeps working while the
+        dependent launches wait for one another.  policy 0: none; 1: every launch prefetches the
+        next linear launch's weights (attention those of gate/up, the head the first QKV of the next
+        step)."""
+        jobs = [j for lj in self.layer_jobs for j in lj] + [self.head_job]
+        for j in jobs:
+            j.prefetch.n = 0
+        if policy == 0:
+            return
+        hx = lambda l, n: self.hex[f"blk.{l}.{n}.weight"]  # noqa: E731
+        qkv_w = lambda l: [hx(l, n) for n in ("attn_q", "attn_k", "attn_v")]  # noqa: E731
+        for l, (qkv, att, o, gu, dn) in enumerate(self.layer_jobs):
+            self._set_prefetch(qkv, self._ranges([hx(l, "attn_output")]))
+            self._set_prefetch(att, self._ranges([hx(l, "ffn_gate"), hx(l, "ffn_up")]))
+            self._set_prefetch(o, self._ranges([hx(l, "ffn_gate"), hx(l, "ffn_up")]))
+            self._set_prefetch(gu, self._ranges([hx(l, "ffn_down")]))
+            nxt = qkv_w(l + 1) if l + 1 < self.n_layers else [self.hex["output.weight"]]
+            self._set_prefetch(dn, self._ranges(nxt))
+        self._set_prefetch(self.head_job, self._ranges(qkv_w(0)))
 
     def linear(self, job):
         ops.linear(job, self.ws_of[id(job)])

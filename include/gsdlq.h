@@ -163,6 +163,19 @@ typedef struct gsdlq_hexmat {
 #define GSDLQ_IN_EMBED 2    /* input = rmsnorm(f32(embed[*token])) * norm_w; CTA 0 writes the
                                raw row to x_out (the residual stream)                      */
 
+/* L2 prefetch list of a launch (engine use; no counterpart in the reference): byte ranges of
+ * device memory that a LATER launch will read -- the next linears' packed weights -- fetched into
+ * the L2 cache while this launch runs, so that HBM keeps streaming across the gaps between
+ * dependent launches.  Each range must start 16-byte aligned and span a multiple of 16 bytes; the
+ * ranges are split evenly over the launch's CTAs and issued as bulk L2 prefetches at their start.
+ * n = 0: none.  Prefetches change no result. */
+#define GSDLQ_MAX_PREFETCH 16
+typedef struct gsdlq_prefetch {
+  const void *ptr[GSDLQ_MAX_PREFETCH];
+  uint64_t bytes[GSDLQ_MAX_PREFETCH];
+  int n;
+} gsdlq_prefetch_t;
+
 /* A fused packed-linear launch: up to three matrices that share one input,
  * the low-rank projection computed inside the same kernel, and an epilogue. */
 typedef struct gsdlq_linear_job {
@@ -202,6 +215,7 @@ typedef struct gsdlq_linear_job {
   const float *fwd_norm_w;
   unsigned long long *fwd_acc;
   int lr_forwarded;
+  gsdlq_prefetch_t prefetch;  /* optional L2 prefetch of later launches' weights */
 } gsdlq_linear_job_t;
 
 /* Bytes of device workspace a gsdlq_linear launch of `job` needs (host pointers). */
@@ -252,7 +266,9 @@ int gsdlq_unit_kinks(const uint32_t *row_ptr, const uint16_t *kink_cols, const f
  *   or different host threads without ordering) race on it and give wrong results.
  * - Argument errors and a matrix of more than GSDLQ_NOALLOC_MAX_STRIPS strips of 16 rows
  *   (rows > 508 304) return GSDLQ_ERR_INVALID or GSDLQ_ERR_UNSUPPORTED before anything
- *   touches the device; use gsdlq_hex2d_matvec or gsdlq_linear for larger matrices. */
+ *   touches the device.  (The planner of every packed-linear entry point has a lower limit
+ *   of its own, 127 strips per SM -- 18 796 strips, 300 736 rows, on a 148-SM B200 -- and
+ *   returns GSDLQ_ERR_UNSUPPORTED above it, so the scratch is never the binding limit there.) */
 int gsdlq_hex2d_matvec_noalloc(const float *x, const uint8_t *codes, const uint16_t *scales,
                                const float *xy_table, const uint16_t *U, const float *tmp_k,
                                const uint32_t *kink_row_ptr, const uint16_t *kink_cols,
@@ -281,6 +297,7 @@ typedef struct gsdlq_attn_job {
   const uint16_t *fwd_vt;
   int fwd_k;
   unsigned long long *fwd_acc;
+  gsdlq_prefetch_t prefetch;  /* optional L2 prefetch of later launches' weights */
 } gsdlq_attn_job_t;
 
 /* Bytes of `partial` (floats) and `workspace` (uints) a gsdlq_attention call needs. */

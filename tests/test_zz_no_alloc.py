@@ -60,12 +60,14 @@ def test_noalloc_matches_allocating_dropin(cuda_lib, rng, rows, cols, k, nnz):
 
 
 def test_noalloc_at_the_strip_limit(cuda_lib, rng):
-    """The tallest matrix the fixed scratch holds (GSDLQ_NOALLOC_MAX_STRIPS strips of 16 rows, 64
-    columns) against the allocating drop-in, twice; one strip more is refused."""
+    """The tallest matrix the packed linear's planner takes (127 strips of 16 rows per SM: its CTAs'
+    shared-memory accumulators hold 128 strips), 64 columns, against the allocating drop-in, twice;
+    its scratch fills most of the fixed array.  One strip more is refused (GSDLQ_ERR_UNSUPPORTED)."""
     import gsdlq_b200.codebook as cb
     import gsdlq_b200.ops as ops
     lib = cuda_lib
-    max_strips = 31769
+    max_strips = 127 * torch.cuda.get_device_properties(0).multi_processor_count
+    assert 768 + 132 * max_strips <= 4 << 20  # the scratch this launch needs fits the fixed array
     rows, cols = 16 * max_strips, 64
     t = rand_hex(rng, rows, cols, k=4, nnz=1, radius=8)
     h = ops.DeviceHex(t)
