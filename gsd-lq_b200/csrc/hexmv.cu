@@ -70,6 +70,16 @@ static int hexmv_validate_mat(const gsdlq_hexmat_t& M, int cols, bool own_lowran
   return GSDLQ_OK;
 }
 
+// In-loop L2 prefetch distance of the streaming warps, in units (GSDLQ_PF_AHEAD, default 0).
+static int hexmv_pf_ahead() {
+  static const int d = [] {
+    const char* e = std::getenv("GSDLQ_PF_AHEAD");
+    const int v = e ? std::atoi(e) : 0;
+    return v < 0 ? 0 : (v > 16 ? 16 : v);
+  }();
+  return d;
+}
+
 // Geometry of a launch (everything but the workspace pointers).
 int hexmv_plan(HexmvParams& P) {
   const gsdlq_linear_job_t& J = P.job;
@@ -116,6 +126,7 @@ int hexmv_plan(HexmvParams& P) {
   P.lr_chunks = (C / 8 + helpers - 1) / helpers;
   P.ovf_bytes = std::max(0, P.GU * 16 - 256) * 128;
   // per-unit kink lists are used when every matrix has them (8-byte entries)
+  P.pf_ahead = hexmv_pf_ahead();
   P.ukink = 1;
   for (int m = 0; m < J.n_mat; ++m) {
     const gsdlq_hexmat_t& M = J.mat[m];

@@ -105,6 +105,8 @@ struct HexmvParams {
   int lr_chunks;           // 8-column chunks of every Vt row per helper warp
   int ovf_bytes;           // activation-split overflow region
   int ukink;               // every matrix has per-unit kink lists: the streaming warps apply them
+  int pf_ahead;            // FULL streams: each warp prefetches into L2 the unit this many units past the
+                           // one it is loading, within the same row block (0: none)
   unsigned* ctl;
   unsigned* cnt;                // [n_strips] reserved (zero; the shared-strip words count their own contributions)
   unsigned long long* gacc;     // [n_strips][nmat * 16] fixed-point sums of those strips
@@ -1108,6 +1110,13 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
         for (int mm = 0; mm < NMAT; ++mm) acc[mm][0] = acc[mm][1] = 0.f;
       }
       const bool more = u + 1 < u1;
+      // (pa, pb and the cursor point at unit u + 1 here) the unit pf_ahead past it goes into L2, so
+      // that its register loads, issued one unit ahead, find it there; lane (g, q) takes one 128-byte
+      // line: row g (q < 2) or g + 8, half q & 1
+      if (FULL && !TMA && P.pf_ahead > 0 && more && nc + P.pf_ahead < P.GU) {
+        const uint8_t* rowp = ((q >> 1) ? pb : pa) - q * 16 + P.pf_ahead * HX_UB + (q & 1) * 128;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(rowp));
+      }
       // this unit's kink entries (range known since the previous unit) go into flight
       const uint32_t ko0 = nko0, ko1 = nko1;
       uint2 ke0 = make_uint2(0u, 0u), ke1 = make_uint2(0u, 0u);

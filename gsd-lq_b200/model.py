@@ -81,7 +81,7 @@ class GSDLQModel:
         self._want_fused = fused_step and tp is None
         self.lr_forward = lr_forward
         # L2 prefetch policy of the launches (see _wire_prefetch); GSDLQ_PREFETCH overrides the default
-        self.prefetch = int(os.environ.get("GSDLQ_PREFETCH", "1")) if prefetch is None else int(prefetch)
+        self.prefetch = int(os.environ.get("GSDLQ_PREFETCH", "0")) if prefetch is None else int(prefetch)
         self._plans: dict = {}
         if isinstance(source, str):
             source = read_gsd2(source)
@@ -291,12 +291,15 @@ class GSDLQModel:
             job.prefetch.ptr[i] = p
             job.prefetch.bytes[i] = n
 
+    # links of the L2 prefetch policy (bits of GSDLQ_PREFETCH / the prefetch argument)
+    PF_QKV_O, PF_ATTN_GU, PF_O_GU, PF_GU_DOWN, PF_DOWN_NEXT, PF_HEAD_QKV = 1, 2, 4, 8, 16, 32
+
     def _wire_prefetch(self, policy: int):
         """L2 prefetch of later launches' weights (gsdlq_prefetch_t): a launch fetches into L2 the
-        packed weights that the next launches will stream, so that HBM keeps working while the
-        dependent launches wait for one another.  policy 0: none; 1: every launch prefetches the
-        next linear launch's weights (attention those of gate/up, the head the first QKV of the next
-        step)."""
+        packed weights that a later launch will stream, so that HBM keeps working while the dependent
+        launches wait for one another.  ``policy`` is a bit set of links: QKV -> O (1), attention ->
+        gate/up (2), O -> gate/up (4), gate/up -> down (8), down -> the next layer's QKV or the head
+        (16), head -> the first QKV of the next step (32); 0 = none."""
         jobs = [j for lj in self.layer_jobs for j in lj] + [self.head_job]
         for j in jobs:
             j.prefetch.n = 0
@@ -305,13 +308,19 @@ class GSDLQModel:
         hx = lambda l, n: self.hex[f"blk.{l}.{n}.weight"]  # noqa: E731
         qkv_w = lambda l: [hx(l, n) for n in ("attn_q", "attn_k", "attn_v")]  # noqa: E731
         for l, (qkv, att, o, gu, dn) in enumerate(self.layer_jobs):
-            self._set_prefetch(qkv, self._ranges([hx(l, "attn_output")]))
-            self._set_prefetch(att, self._ranges([hx(l, "ffn_gate"), hx(l, "ffn_up")]))
-            self._set_prefetch(o, self._ranges([hx(l, "ffn_gate"), hx(l, "ffn_up")]))
-            self._set_prefetch(gu, self._ranges([hx(l, "ffn_down")]))
-            nxt = qkv_w(l + 1) if l + 1 < self.n_layers else [self.hex["output.weight"]]
-            self._set_prefetch(dn, self._ranges(nxt))
-        self._set_prefetch(self.head_job, self._ranges(qkv_w(0)))
+            if policy & self.PF_QKV_O:
+                self._set_prefetch(qkv, self._ranges([hx(l, "attn_output")]))
+            if policy & self.PF_ATTN_GU:
+                self._set_prefetch(att, self._ranges([hx(l, "ffn_gate"), hx(l, "ffn_up")]))
+            if policy & self.PF_O_GU:
+                self._set_prefetch(o, self._ranges([hx(l, "ffn_gate"), hx(l, "ffn_up")]))
+            if policy & self.PF_GU_DOWN:
+                self._set_prefetch(gu, self._ranges([hx(l, "ffn_down")]))
+            if policy & self.PF_DOWN_NEXT:
+                nxt = qkv_w(l + 1) if l + 1 < self.n_layers else [self.hex["output.weight"]]
+                self._set_prefetch(dn, self._ranges(nxt))
+        if policy & self.PF_HEAD_QKV:
+            self._set_prefetch(self.head_job, self._ranges(qkv_w(0)))
 
     def linear(self, job):
         ops.linear(job, self.ws_of[id(job)])
