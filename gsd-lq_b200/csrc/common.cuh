@@ -260,6 +260,39 @@ inline bool prefetch_ok(const gsdlq_prefetch_t& pf) {
   return true;
 }
 
+// ---- phase trace (compiled in only with -DGSDLQ_TRACE; a diagnostic build, not the product) ----
+// Each CTA of a stand-alone fused-linear launch stamps %globaltimer at fixed points of its run into
+// g_trace[launch][cta][point]; launch = how many launches this CTA index has started since the last
+// reset.  Read back with gsdlq_trace_read (defined in trace builds only).
+#ifdef GSDLQ_TRACE
+constexpr int TR_CTAS = 160, TR_LAUNCHES = 192, TR_POINTS = 32;
+extern __device__ unsigned long long g_trace[TR_LAUNCHES * TR_CTAS * TR_POINTS];
+extern __device__ unsigned g_trace_cnt[TR_CTAS];
+__device__ __forceinline__ unsigned long long tr_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned long long* tr_rec(unsigned slot) {
+  return g_trace + ((size_t)slot * TR_CTAS + blockIdx.x) * TR_POINTS;
+}
+#define GSDLQ_TR_SET(slot, pt, v)                                               \
+  do {                                                                          \
+    if ((slot) < (unsigned)TR_LAUNCHES && blockIdx.x < (unsigned)TR_CTAS) tr_rec(slot)[pt] = (v); \
+  } while (0)
+#define GSDLQ_TR_MAX(slot, pt)                                                  \
+  do {                                                                          \
+    if ((slot) < (unsigned)TR_LAUNCHES && blockIdx.x < (unsigned)TR_CTAS) atomicMax(tr_rec(slot) + (pt), tr_now()); \
+  } while (0)
+#else
+#define GSDLQ_TR_SET(slot, pt, v) \
+  do {                            \
+  } while (0)
+#define GSDLQ_TR_MAX(slot, pt) \
+  do {                         \
+  } while (0)
+#endif
+
 // Monotone float -> uint32 map (larger float -> larger key).
 __device__ __forceinline__ uint32_t ordered_key(float v) {
   const uint32_t b = __float_as_uint(v);

@@ -116,6 +116,7 @@ struct MkPtrs {
   __device__ __forceinline__ unsigned dep_target() const { return dep_t; }
   __device__ __forceinline__ unsigned* done() const { return K.sync + MK_SYNC_PHASE + p; }
   __device__ __forceinline__ unsigned* abort() const { return K.sync + MK_SYNC_ABORT; }
+  __device__ __forceinline__ unsigned trace_slot() const { return (unsigned)p; }
 };
 
 // completion count of a linear phase of kind KIND: its strips plus one per CTA (staging done)

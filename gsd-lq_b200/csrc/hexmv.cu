@@ -477,6 +477,26 @@ extern "C" int gsdlq_unit_kinks(const uint32_t* row_ptr, const uint16_t* kink_co
   return GSDLQ_OK;
 }
 
+// ---- phase trace read-back (trace builds only) -------------------------------------------------
+#ifdef GSDLQ_TRACE
+namespace gsdlq {
+__device__ unsigned long long g_trace[TR_LAUNCHES * TR_CTAS * TR_POINTS];
+__device__ unsigned g_trace_cnt[TR_CTAS];
+}  // namespace gsdlq
+extern "C" int gsdlq_trace_reset(void) {
+  static unsigned long long zero_t[TR_LAUNCHES * TR_CTAS * TR_POINTS];
+  static unsigned zero_c[TR_CTAS];
+  cudaError_t e = cudaMemcpyToSymbol(g_trace, zero_t, sizeof(zero_t));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_trace_cnt, zero_c, sizeof(zero_c));
+  return e == cudaSuccess ? GSDLQ_OK : record_cuda_error(e);
+}
+extern "C" int gsdlq_trace_read(unsigned long long* out, size_t n) {
+  if (n < (size_t)TR_LAUNCHES * TR_CTAS * TR_POINTS) return GSDLQ_ERR_INVALID;
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_trace, sizeof(unsigned long long) * TR_LAUNCHES * TR_CTAS * TR_POINTS);
+  return e == cudaSuccess ? GSDLQ_OK : record_cuda_error(e);
+}
+#endif
+
 // ---- allocation-free matvec ------------------------------------------------------------
 // Scratch for gsdlq_hex2d_matvec_noalloc: a fixed array in the library's device image, so a
 // call never allocates.  Host code must not pass `g_noalloc_ws` itself to a kernel (on the

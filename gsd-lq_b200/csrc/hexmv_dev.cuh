@@ -153,10 +153,14 @@ struct HxPtrs {
 // The (strip, matrix, unit) iterations are dealt to the CTAs as equal contiguous ranges, and a
 // CTA's range to its 14 streaming warps as contiguous ranges weighted by scheduler: warps are
 // spread over the SM's four schedulers by warp index mod 4, so schedulers 0 and 1 run four
-// streaming warps and schedulers 2 and 3 run three plus one helper warp; the units are dealt in
-// proportion 3 : 4 to warps on the first and the second pair, so every scheduler streams the same
-// share.  lp(l) = sum of the weights of local warps 0 .. l-1.
-__host__ __device__ __forceinline__ int hx_lp(int l) { return 4 * l - 2 * (l / 4) - ((l % 4) < 2 ? (l % 4) : 2); }
+// streaming warps and schedulers 2 and 3 run three plus one helper warp.  A warp on the second pair
+// streams faster (its scheduler is shared by fewer streaming warps), but not 4/3 faster: a phase
+// trace of the gate/up launch measured a per-unit rate ratio of 1.14, so the units are dealt in
+// proportion 7 : 8.  lp(l) = sum of the weights of local warps 0 .. l-1.
+__host__ __device__ __forceinline__ int hx_lp(int l) {
+  const int r = l % 4;
+  return 30 * (l / 4) + 7 * (r < 2 ? r : 2) + 8 * (r > 2 ? r - 2 : 0);
+}
 __host__ __device__ __forceinline__ long long hx_cta_begin(long long T, int n_cta, int c) {
   return c >= n_cta ? T : T * c / n_cta;
 }
@@ -234,20 +238,33 @@ __device__ __forceinline__ uint32_t xs_chunk(int ch, uint32_t tab_off) {
 }
 
 // ---- decode table ----------------------------------------------------------------------
-// (r0, r1) of code c in the radius-R enumeration (r0 outer, r1 inner, |r0+r1| <= R)
-__device__ __forceinline__ bool lattice_of_code(int c, int R, int& r0, int& r1) {
-  for (int a = -R; a <= R; ++a) {
-    const int lo = max(-R, -R - a), hi = min(R, R - a);
-    const int n = hi - lo + 1;
-    if (c < n) {
-      r0 = a;
-      r1 = lo + c;
-      return true;
-    }
-    c -= n;
-  }
-  return false;
+// bf16 bits of a small integer (|v| <= 255: exact)
+constexpr uint32_t bf16_of_int(int v) {
+  if (v == 0) return 0u;
+  const uint32_t sign = v < 0 ? 0x8000u : 0u;
+  const int a = v < 0 ? -v : v;
+  int e = 0;
+  while ((a >> (e + 1)) != 0) ++e;  // floor(log2 a) <= 7
+  return sign | ((uint32_t)(127 + e) << 7) | (((uint32_t)a << (7 - e)) & 0x7fu);
 }
+// The decode-table entries of both radii, made at compile time: entry c of radius R is the bf16x2
+// (r0 low, r1 high) of the c-th point of the reference's enumeration (r0 outer, r1 inner,
+// |r0 + r1| <= R; gsd_lq_cpu_runtime.py:111-118); codes past the last point decode to (0, 0).
+struct LatticeEntries {
+  uint32_t e[2][256];  // [0]: radius 6, [1]: radius 8
+};
+constexpr LatticeEntries make_lattice_entries() {
+  LatticeEntries t{};
+  for (int ri = 0; ri < 2; ++ri) {
+    const int R = ri ? 8 : 6;
+    int c = 0;
+    for (int a = -R; a <= R; ++a)
+      for (int b = -R; b <= R; ++b)
+        if (a + b <= R && a + b >= -R) t.e[ri][c++] = bf16_of_int(a) | (bf16_of_int(b) << 16);
+  }
+  return t;
+}
+__device__ const LatticeEntries g_lattice_entries = make_lattice_entries();
 
 // decode entry of code i from a caller's float xy table (the drop-in path); the table must be
 // the A2 lattice, which is checked
@@ -576,6 +593,19 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
   // the next launch may be scheduled at once: its CTAs take an SM as soon as one of ours leaves it,
   // and its griddepcontrol.wait still waits for this whole grid
   if (!MEGA) pdl_launch_dependents();
+#ifdef GSDLQ_TRACE
+  if (tid == 0) {
+    unsigned slot;
+    if constexpr (MEGA) slot = mp.trace_slot();  // the phase index inside the persistent step
+    else slot = atomicAdd(&g_trace_cnt[blockIdx.x], 1u);
+    reinterpret_cast<uint32_t*>(smem + (HX_TAB_ABS - sbase) - HX_RED_BYTES)[40] = slot;
+    GSDLQ_TR_SET(slot, 0, tr_now());
+    GSDLQ_TR_SET(slot, 9, ((unsigned long long)P.job.layer << 8) | (unsigned)P.job.epilogue);
+  }
+#define HX_SLOT_NOW (reinterpret_cast<const volatile uint32_t*>(smem + (HX_TAB_ABS - sbase) - HX_RED_BYTES)[40])
+#else
+#define HX_SLOT_NOW 0u
+#endif
   const uint32_t tab_off = HX_TAB_ABS - sbase;
   uint8_t* tab = smem + tab_off;
   float* red = reinterpret_cast<float*>(smem + tab_off - HX_RED_BYTES);
@@ -777,6 +807,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
         __syncwarp();
         if (lane == 0) s_lr[HX_LR_FLAG] = 1.f;
         ctl_release_last(mp.ctl(), lane);
+        if (lane == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 14, tr_now());
       }
     }
     // ---- kink passes: one slot per strip; the counts are made together at the end -------------
@@ -826,33 +857,9 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       if (s < o_hi) atomicAdd(lacc + (size_t)(s - s_lo) * width + (lane & (width - 1)), hx_fix(v));
     }
     if (bad) raise_flag(GSDLQ_FLAG_BAD_KINK);
+    if (lane == 0) GSDLQ_TR_MAX(HX_SLOT_NOW, 8);
   } else {
     // ==== streaming warps ===================================================================
-    // decode table: lanes 0-15 compute the entries of 16 rows, then every lane writes 16-byte
-    // quarters of four of them (no table memory is read).  The decode kernel keeps the table of
-    // the previous phase when the lattice radius is the same.
-    const bool build_table = !MEGA || reinterpret_cast<const volatile int*>(redu)[35] != J.mat[0].radius;
-    for (int rb = warp * 16; build_table && rb < 256; rb += HX_STREAM * 16) {
-      const int myrow = rb + (lane & 15);
-      uint32_t e = 0u;
-      if (P.xy_table != nullptr) {
-        e = entry_from_xy(P.xy_table, P.n_pts, myrow);
-      } else {
-        int r0 = 0, r1 = 0;
-        if (lattice_of_code(myrow, J.mat[0].radius, r0, r1)) e = pack_bf16x2((float)r0, (float)r1);
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t ek = __shfl_sync(0xffffffffu, e, 4 * k + (lane >> 3));
-        const int row = rb + 4 * k + (lane >> 3);
-        *reinterpret_cast<uint4*>(tab + row * 256 + (lane & 7) * 16) = make_uint4(ek, ek, ek, ek);
-      }
-    }
-    if (tid == 0) {
-      redu[32] = 0u;  // zero bits for the lookup addresses, read after a barrier
-      redu[33] = 0u;
-      s_lr[HX_LR_FLAG] = 0.f;
-    }
     if (lane < 16) s_ks[lane] = 0.f;
     const bool streamer = cb1 > cb0;
     const long long n_c = cb1 - cb0;
@@ -963,6 +970,10 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       if (MEGA) ph = *ph_word;
       __syncwarp();
     }
+    // this thread's decode-table entry is loaded before the weight loads, so it does not queue behind them
+    const bool build_table = !MEGA || reinterpret_cast<const volatile int*>(redu)[35] != J.mat[0].radius;
+    const uint32_t tab_e = (build_table && tid < 256 && P.xy_table == nullptr)
+                               ? __ldg(&g_lattice_entries.e[J.mat[0].radius == 8 ? 1 : 0][tid]) : 0u;
     if (streamer && u1 > u0) {
       if (TMA) {
         if (lane == 0) {
@@ -982,12 +993,51 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       }
     }
 
+    // decode table (after the first unit's loads are in flight: it does not depend on them).  The
+    // decode kernel keeps the table of the previous phase when the lattice radius is the same.
+    if (build_table && P.xy_table != nullptr) {
+      // the drop-in path: entries derived from the caller's float table (checked to be the lattice)
+      for (int rb = warp * 16; rb < 256; rb += HX_STREAM * 16) {
+        const uint32_t e = entry_from_xy(P.xy_table, P.n_pts, rb + (lane & 15));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t ek = __shfl_sync(0xffffffffu, e, 4 * k + (lane >> 3));
+          const int row = rb + 4 * k + (lane >> 3);
+          *reinterpret_cast<uint4*>(tab + row * 256 + (lane & 7) * 16) = make_uint4(ek, ek, ek, ek);
+        }
+      }
+    } else if (build_table && tid < 256) {
+      // thread t fills row t (the 32 per-lane copies of entry t) from the compile-time entries; its
+      // 16-byte stores rotate through the row so that a warp's stores spread over all banks
+      const uint4 v = make_uint4(tab_e, tab_e, tab_e, tab_e);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(tab + tid * 256 + ((j + tid) & 7) * 16) = v;
+    }
+    if (tid == 0) {
+      redu[32] = 0u;  // zero bits for the lookup addresses, read after a barrier
+      redu[33] = 0u;
+      s_lr[HX_LR_FLAG] = 0.f;
+    }
+    if (tid == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 10, tr_now());
+    // the norm weights of this thread's first staging pairs do not depend on the producer: load them now
+    constexpr int XR = 8;
+    const bool normed = mp.input_mode() != GSDLQ_IN_PLAIN;
+    float2 wpre[XR];
+#pragma unroll
+    for (int k = 0; k < XR; ++k) {
+      const int p = tid + k * NST;
+      wpre[k] = (normed && p < NP) ? __ldg(reinterpret_cast<const float2*>(mp.norm_w()) + p) : make_float2(1.f, 1.f);
+    }
     // ---- wait for the producer of x, then stage the input ---------------------------------
     if (MEGA) {
+      if (tid == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 1, tr_now());
       if (tid == 0 && mp.dep() != nullptr) wait_geq_abort(mp.dep(), mp.dep_target(), mp.abort());
+      if (tid == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 2, tr_now());
       named_bar_sync(1, NST);
     } else {
+      if (tid == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 1, tr_now());
       pdl_wait();
+      if (tid == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 2, tr_now());
     }
     if (tid == 0) {
       int pv = -1;
@@ -1002,7 +1052,6 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
         tok = 0;
       }
     }
-    const bool normed = mp.input_mode() != GSDLQ_IN_PLAIN;
     auto load_x = [&](int p) -> float2 {
       if (mp.input_mode() == GSDLQ_IN_EMBED) {
         const uint32_t raw = __ldg(reinterpret_cast<const unsigned int*>(J.embed + (size_t)tok * C) + p);
@@ -1029,7 +1078,6 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       *reinterpret_cast<uint32_t*>(smem + off) = h;
       *reinterpret_cast<uint32_t*>(smem + off + 16) = l;
     };
-    constexpr int XR = 8;
     if (!normed) {
       // a plain input: batches of 2 XR pairs, so the 14336-wide down-projection input is staged
       // with one round of loads
@@ -1046,7 +1094,20 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       // values (lattice, kink and low-rank terms alike) are multiplied by 1/rms, so the sum of squares
       // stays off the staging path; its per-warp parts are summed after the staging barrier
       float ss = 0.f;
-      for (int p0 = tid; p0 < NP; p0 += XR * NST) {
+      {  // the first XR pairs of this thread: all inputs in one batch of loads, weights loaded before the wait
+        float2 xv[XR];
+#pragma unroll
+        for (int k = 0; k < XR; ++k) xv[k] = (tid + k * NST < NP) ? load_x(tid + k * NST) : make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < XR; ++k) {
+          const int p = tid + k * NST;
+          if (p < NP) {
+            ss = fmaf(xv[k].x, xv[k].x, fmaf(xv[k].y, xv[k].y, ss));
+            stage(p, xv[k].x, xv[k].y, wpre[k], 1.f);
+          }
+        }
+      }
+      for (int p0 = tid + XR * NST; p0 < NP; p0 += XR * NST) {
 #pragma unroll
         for (int k = 0; k < XR; ++k) {
           const int p = p0 + k * NST;
@@ -1057,9 +1118,11 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
           }
         }
       }
+      if (tid == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 11, tr_now());
       ss = warp_sum(ss);
       if (lane == 0) red[1 + warp] = ss;
     }
+    if (tid == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 12, tr_now());
     // pairs past the row end of the last unit read zero activations
     for (int p = NP + tid; p < P.GU * HX_UB; p += NST) {
       const int j = p & 63, r = j & 15;
@@ -1071,6 +1134,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
     if (tid == 0) redu[38] = 0u;  // strips this CTA finished (decode kernel)
     named_bar_sync(1, NST);             // table, splits and accumulator ready for the streaming warps
     named_bar_arrive(2, HX_THREADS);    // ... and released to the helper warps
+    if (tid == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 3, tr_now());
 
     if (MEGA && tid == 0) reinterpret_cast<int*>(redu)[35] = J.mat[0].radius;  // every streaming warp has read the old value
     const int pos = reinterpret_cast<const int*>(redu)[34];
@@ -1224,8 +1288,12 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       }
       cur_s = ns, cur_m = nm, cur_c = nc;
       if (u + 2 < u1) step_next();
+      if (tid == 0 && u == u0) GSDLQ_TR_SET(HX_SLOT_NOW, 13, tr_now());
     }
+    if (lane == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 16 + warp, tr_now());
     if (TMA && MEGA && lane == 0) *ph_word = ph;  // the slots' parities carry over to the next phase
+    if (tid == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 4, tr_now());
+    if (lane == 0) GSDLQ_TR_MAX(HX_SLOT_NOW, 5);
     if (u1 > u0) emit(seg_s);
       }
   }
@@ -1241,6 +1309,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
     StripPre sp0;
     if (s_lo + warp <= s_hi) sp0 = strip_pre<EPI>(P, strip_info<NMAT>(P, s_lo + warp), lane, pos);
     __syncthreads();
+    if (tid == 0) GSDLQ_TR_SET(HX_SLOT_NOW, 6, tr_now());
     // the scale of the finished strip values: 1/rms of a normed input (the staging threads' sums of
     // squares are in the reduction words since the staging barrier), else 1
     float v_scale = 1.f;
@@ -1283,6 +1352,7 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       finish_value<EPI, NMAT>(P, mp, si, hx_unfix(a) * v_scale, lane, pos, sp);
       ++nfin;
     }
+    if (lane == 0) GSDLQ_TR_MAX(HX_SLOT_NOW, 7);
     if (MEGA) {
       // one release per CTA: its finished strips and 1 for the CTA (it has read its input)
       if (lane == 0 && nfin) atomicAdd(&redu[38], nfin);
