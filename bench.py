@@ -344,7 +344,6 @@ def comm_time(model, world):
     """Device time per step of the step's collectives alone (2 all-reduces of the hidden vector per layer
     and the argmax MAX), as one CUDA graph, on scratch buffers; max over ranks."""
     import torch
-    import torch.distributed as dist
     buf = torch.zeros(model.hidden, dtype=torch.float32, device=model.device)
     key = torch.zeros(1, dtype=torch.int64, device=model.device)
 
@@ -352,7 +351,7 @@ def comm_time(model, world):
         for _ in range(model.n_layers):
             model.tp.allreduce_buf(buf)
             model.tp.allreduce_buf(buf)
-        dist.all_reduce(key, op=dist.ReduceOp.MAX, group=model.tp.group)
+        model.tp.key_max(key)
     coll()
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
@@ -506,6 +505,7 @@ def run_ours(args):
             "clocks": clocks, "pack_s": round(pack_s, 2), "prefill_s": round(prefill_s, 2),
             "avg_bpw": round(model.avg_bpw, 4), "step": "fused" if model.fused_step else "per-op",
             "n_layers": model.n_layers, "l2_prefetch": model.prefetch,
+            "tp_exchange": model.tp.exchange if model.tp is not None else None,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -90,7 +90,13 @@ SIGNATURES = {
     "gsdlq_decode_plan_create": ([ctypes.POINTER(DecodeDesc), ctypes.POINTER(vp)], i32),
     "gsdlq_decode_step": ([vp, vp], i32),
     "gsdlq_decode_plan_destroy": ([vp], i32),
+    "gsdlq_comm_create": ([i32, i32, i32, ctypes.POINTER(vp), vp], i32),
+    "gsdlq_comm_connect": ([vp, vp], i32),
+    "gsdlq_comm_allreduce_sum": ([vp, vp, i32, vp], i32),
+    "gsdlq_comm_allreduce_max_u64": ([vp, vp, vp], i32),
+    "gsdlq_comm_destroy": ([vp], i32),
 }
+IPC_HANDLE_BYTES = 64
 
 
 class GsdlqError(RuntimeError):

@@ -86,6 +86,8 @@ class GSDLQModel:
         if isinstance(source, str):
             source = read_gsd2(source)
         self._load(source)
+        if self.tp is not None:
+            self.tp.setup(self)  # the residual exchange among the ranks (collective: every rank calls it)
         self.cl = _DeviceInfo(self)
         self.tokenizer = tokenizer_from_config(self.cfg)  # SentencePiece BPE over the header's vocabulary
         self._graphs: dict = {}
@@ -476,6 +478,9 @@ class GSDLQModel:
     def release(self):
         self._graphs.clear()
         self._destroy_plans()
+        if self.tp is not None:
+            torch.cuda.synchronize(self.device)
+            self.tp.close()
         for k in ("hex", "embed", "norms", "k_cache", "v_cache", "_arena"):
             if hasattr(self, k):
                 delattr(self, k)

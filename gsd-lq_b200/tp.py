@@ -15,7 +15,9 @@ Sharding (Megatron style; the reference has no multi-device code at all):
 Per layer there are two all-reduces of the hidden-size fp32 residual: rank 0's
 O/down epilogue adds its partial to the residual, the other ranks store their bare
 partials into the same buffer, and one all-reduce(sum) leaves x + sum_r partial_r
-on every rank.
+on every rank.  The all-reduce is the library's one-shot exchange over peer memory
+(gsdlq_comm_allreduce_sum; rank-ordered sums, so every rank holds the same bits), or
+NCCL's with exchange="nccl".
 """
 from __future__ import annotations
 
@@ -143,10 +145,48 @@ def shard_device(dm, rank: int, world: int):
 
 
 class TensorParallel:
-    """Collective plumbing for GSDLQModel(tp=...) over an initialised torch.distributed group."""
+    """Collective plumbing for GSDLQModel(tp=...) over an initialised torch.distributed group.
 
-    def __init__(self, rank: int, world: int, group=None):
+    ``exchange`` picks the path of the per-layer residual all-reduce and of the greedy-key maximum:
+    "p2p" (default; GSDLQ_TP_EXCHANGE overrides) is the library's one-shot exchange over CUDA-IPC
+    mapped peer buffers (gsdlq_comm_*), "nccl" is torch.distributed.all_reduce.  torch.distributed
+    is used in both cases for the rendezvous (the IPC handles are all-gathered over it)."""
+
+    def __init__(self, rank: int, world: int, group=None, exchange: str | None = None):
+        import os
         self.rank, self.world, self.group = rank, world, group
+        self.exchange = exchange or os.environ.get("GSDLQ_TP_EXCHANGE", "p2p")
+        if self.exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange {self.exchange!r}: use 'p2p' or 'nccl'")
+        self.comm = None
+
+    def setup(self, model):
+        """Create and connect this rank's exchange buffer (p2p), sized for the hidden vector."""
+        if self.exchange != "p2p" or self.comm is not None:
+            return
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        from . import _lib as L
+        lib = L.load()
+        comm = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * L.IPC_HANDLE_BYTES)()
+        L.check(lib.gsdlq_comm_create(self.world, self.rank, model.hidden, ctypes.byref(comm), handle),
+                "gsdlq_comm_create")
+        mine = torch.tensor(bytearray(handle), dtype=torch.uint8, device=model.device)
+        every = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(every, mine, group=self.group)
+        handles = bytes(torch.cat(every).cpu().numpy().tobytes())
+        buf = (ctypes.c_uint8 * len(handles)).from_buffer_copy(handles)
+        L.check(lib.gsdlq_comm_connect(comm, buf), "gsdlq_comm_connect")
+        self.comm = comm
+        dist.barrier(group=self.group)
+
+    def close(self):
+        if self.comm is not None:
+            from . import _lib as L
+            L.check(L.load().gsdlq_comm_destroy(self.comm), "gsdlq_comm_destroy")
+            self.comm = None
 
     def shard(self, src):
         from .model import DevicePacked
@@ -163,16 +203,32 @@ class TensorParallel:
 
     def allreduce_buf(self, buf):
         """Sum of ``buf`` over the ranks, in place (the residual exchange of one O or down projection)."""
+        if self.comm is not None:
+            from . import _lib as L
+            from .ops import stream_handle
+            L.check(L.load().gsdlq_comm_allreduce_sum(self.comm, buf.data_ptr(), buf.numel(), stream_handle()),
+                    "gsdlq_comm_allreduce_sum")
+            return
         import torch.distributed as dist
         dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group)
 
-    def finish_head(self, model):
-        """Global greedy pick: all-reduce MAX of the 64-bit keys (MSB flipped so signed order = unsigned)."""
+    def key_max(self, key):
+        """Maximum over the ranks of the unsigned 64-bit key ``key[0]``, in place."""
+        if self.comm is not None:
+            from . import _lib as L
+            from .ops import stream_handle
+            L.check(L.load().gsdlq_comm_allreduce_max_u64(self.comm, key.data_ptr(), stream_handle()),
+                    "gsdlq_comm_allreduce_max_u64")
+            return
         import torch.distributed as dist
-        k = model.key[:1]
-        k.bitwise_xor_(-(1 << 63))
+        k = key[:1]
+        k.bitwise_xor_(-(1 << 63))  # MSB flipped so that signed order = unsigned order
         dist.all_reduce(k, op=dist.ReduceOp.MAX, group=self.group)
         k.bitwise_xor_(-(1 << 63))
+
+    def finish_head(self, model):
+        """Global greedy pick: the maximum over ranks of the 64-bit (value, ~global index) keys."""
+        self.key_max(model.key)
 
     def gather_logits(self, model) -> np.ndarray:
         import torch

@@ -347,6 +347,28 @@ int gsdlq_hex2d_matmul(const float *x, int batch, const uint8_t *codes, const ui
  * rounding (the attention splits the sequence differently).  Each step first copies the plan's
  * parameter block into the library's constant memory on `stream`, so the steps of all plans of
  * one device must not overlap on the GPU (use one stream, or ordered streams). */
+/* ---- Tensor-parallel exchange (engine use) -----------------------------------------------------
+ * No counterpart in the reference, which runs on one device.  A one-shot all-reduce among the W
+ * ranks (one process per GPU) of one node, through each rank's exchange buffer mapped into every
+ * peer with CUDA IPC: every rank stores its values into every peer's receive slots over NVLink,
+ * raises a flag there, waits (bounded: 1 s, then GSDLQ_FLAG_TIMEOUT) for every peer's flag and sums
+ * the slots in rank order, so all ranks hold the same bits.  Every rank must make the same calls in
+ * the same order.  No TMA and no multicast are used.
+ *   create:  allocates this rank's buffer (for vectors of up to n_max floats) and writes its
+ *            GSDLQ_IPC_HANDLE_BYTES-byte IPC handle to ipc_handle;
+ *   connect: handles = the W ranks' handles, rank-major; opens the peers' buffers;
+ *   allreduce_sum: x[n] (16-byte aligned, device) := the sum over ranks, in place;
+ *   allreduce_max_u64: *key := the maximum over ranks (the vocab-parallel greedy argmax key).
+ * Both are stream-ordered kernels (capturable into a CUDA graph) that read their input after the
+ * previous kernel on the stream has completed. */
+#define GSDLQ_IPC_HANDLE_BYTES 64
+typedef struct gsdlq_comm gsdlq_comm_t;  /* opaque */
+int gsdlq_comm_create(int world, int rank, int n_max, gsdlq_comm_t **comm, void *ipc_handle);
+int gsdlq_comm_connect(gsdlq_comm_t *comm, const void *handles);
+int gsdlq_comm_allreduce_sum(gsdlq_comm_t *comm, float *x, int n, gsdlq_stream_t stream);
+int gsdlq_comm_allreduce_max_u64(gsdlq_comm_t *comm, unsigned long long *key, gsdlq_stream_t stream);
+int gsdlq_comm_destroy(gsdlq_comm_t *comm);
+
 typedef struct gsdlq_decode_layer {
   gsdlq_linear_job_t qkv;      /* epilogue GSDLQ_EPI_ROPE_KV */
   gsdlq_attn_job_t attn;
