@@ -43,7 +43,8 @@ class LinearJob(ctypes.Structure):
                 ("y", vp * 3), ("resid", vp), ("k_cache", vp), ("v_cache", vp), ("pos", vp), ("rope_cs", vp),
                 ("layer", i32), ("max_seq", i32), ("head_dim", i32), ("interleaved", i32),
                 ("argmax_key", vp), ("argmax_index_base", i32), ("fwd_vt", vp * 3), ("fwd_k", i32 * 3),
-                ("fwd_norm_w", vp), ("fwd_acc", vp), ("lr_forwarded", i32), ("prefetch", Prefetch)]
+                ("fwd_norm_w", vp), ("fwd_acc", vp), ("lr_forwarded", i32), ("prefetch", Prefetch),
+                ("exchange", vp)]
 
 
 class AttnJob(ctypes.Structure):

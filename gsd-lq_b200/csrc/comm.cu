@@ -25,19 +25,9 @@
 // No TMA, no multicast: plain stores to peer memory and volatile loads of this rank's own memory.
 #include <cstring>
 
-#include "common.cuh"
+#include "comm.cuh"
 
 namespace gsdlq {
-
-constexpr int CM_CHUNK = 1024;    // elements per CTA
-constexpr int CM_THREADS = 256;   // 4 elements per thread
-constexpr int CM_MAX_WORLD = 8;
-
-struct CommDesc {
-  uint8_t* base[CM_MAX_WORLD];  // every rank's exchange buffer (this rank's own at [rank])
-  int world, rank, n_max, n_chunks;
-  size_t off_keys, off_count;
-};
 
 struct gsdlq_comm_impl {  // behind the opaque gsdlq_comm_t
   CommDesc d;
@@ -53,18 +43,12 @@ static void cm_layout(CommDesc& d) {
   const size_t data = sizeof(unsigned long long) * 2 * (size_t)d.world * (size_t)d.n_chunks * CM_CHUNK;
   d.off_keys = cm_align(data);
   d.off_count = cm_align(d.off_keys + sizeof(unsigned long long) * 2 * 2 * d.world);
+  d.off_excount = cm_align(d.off_count + sizeof(unsigned) * (d.n_chunks + 1));
+  d.off_exdata = cm_align(d.off_excount + 2 * sizeof(unsigned));
 }
 
-static size_t cm_bytes(const CommDesc& d) { return cm_align(d.off_count + sizeof(unsigned) * (d.n_chunks + 1)); }
-
-__device__ __forceinline__ void st_vol_v2(unsigned long long* p, unsigned long long a, unsigned long long b) {
-  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
-}
-__device__ __forceinline__ void ld_vol_v2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
-  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
-}
-__device__ __forceinline__ unsigned long long ll_pack(float v, unsigned k) {
-  return (unsigned long long)__float_as_uint(v) | ((unsigned long long)k << 32);
+static size_t cm_bytes(const CommDesc& d) {
+  return cm_align(d.off_exdata + sizeof(unsigned long long) * 2 * (size_t)d.world * (size_t)d.n_max);
 }
 
 // Poll the two slots at p (this rank's memory) until both carry call number k; bounded by `deadline`
@@ -225,6 +209,17 @@ extern "C" int gsdlq_comm_connect(gsdlq_comm_t* comm, const void* handles) {
   }
   return GSDLQ_OK;
 }
+
+namespace gsdlq {
+int comm_desc(const gsdlq_comm_t* comm, CommDesc* out) {
+  const gsdlq_comm_impl* c = reinterpret_cast<const gsdlq_comm_impl*>(comm);
+  if (!c || !out) return GSDLQ_ERR_INVALID;
+  for (int r = 0; r < c->d.world; ++r)
+    if (c->d.base[r] == nullptr) return GSDLQ_ERR_INVALID;
+  *out = c->d;
+  return GSDLQ_OK;
+}
+}  // namespace gsdlq
 
 static bool cm_ready(const gsdlq_comm_impl* c) {
   for (int r = 0; r < c->d.world; ++r)

@@ -284,6 +284,7 @@ static bool same_shape(const gsdlq_hexmat_t& a, const gsdlq_hexmat_t& b) {
 // keeps one record per phase kind and only the matrices, the norm weight and the layer differ.
 static bool same_job(const gsdlq_linear_job_t& a, const gsdlq_linear_job_t& b, bool input_may_differ) {
   if (a.n_mat != b.n_mat || a.epilogue != b.epilogue || a.x != b.x || a.eps != b.eps) return false;
+  if (a.exchange || b.exchange) return false;  // (the persistent step has no tensor-parallel exchange)
   if (!input_may_differ && a.input_mode != b.input_mode) return false;
   for (int m = 0; m < a.n_mat; ++m) {
     if (!same_shape(a.mat[m], b.mat[m]) || a.y[m] != b.y[m]) return false;

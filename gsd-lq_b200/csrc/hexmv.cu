@@ -199,6 +199,11 @@ int hexmv_check_io(const HexmvParams& P) {
   const gsdlq_linear_job_t& J = P.job;
   if (hexmv_check_fwd(P) != GSDLQ_OK) return GSDLQ_ERR_INVALID;
   if (!prefetch_ok(J.prefetch)) return GSDLQ_ERR_INVALID;
+  if (J.exchange) {  // the fused tensor-parallel sum: a RESID launch of one matrix
+    CommDesc d;
+    if (J.epilogue != GSDLQ_EPI_RESID || J.n_mat != 1) return GSDLQ_ERR_INVALID;
+    if (comm_desc(J.exchange, &d) != GSDLQ_OK || J.mat[0].rows > d.n_max) return GSDLQ_ERR_INVALID;
+  }
   if (J.input_mode < 0 || J.input_mode > 2) return GSDLQ_ERR_INVALID;
   if (J.input_mode == GSDLQ_IN_PLAIN && !J.x) return GSDLQ_ERR_INVALID;
   if (J.input_mode == GSDLQ_IN_RMSNORM && (!J.x || !J.norm_w)) return GSDLQ_ERR_INVALID;
@@ -277,6 +282,11 @@ int hexmv_launch(HexmvParams& P, void* workspace, size_t ws_bytes, cudaStream_t 
   if (!workspace || ws_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u)) return GSDLQ_ERR_INVALID;
   P.ctl = static_cast<unsigned*>(workspace);
   P.cnt = P.ctl + CTL_WORDS;
+  if (P.job.exchange) {
+    st = comm_desc(P.job.exchange, &P.ex);
+    if (st != GSDLQ_OK) return st;
+    P.ex_on = 1;
+  }
   const uintptr_t pb = reinterpret_cast<uintptr_t>(P.cnt + P.n_strips);
   P.gacc = reinterpret_cast<unsigned long long*>((pb + 15) & ~uintptr_t(15));
   return hexmv_dispatch(P, s);

@@ -68,6 +68,7 @@
 #include <algorithm>
 #include <cstdio>
 
+#include "comm.cuh"
 #include "common.cuh"
 
 namespace gsdlq {
@@ -117,6 +118,9 @@ struct HexmvParams {
   unsigned dep_target;
   unsigned* done;
   unsigned* abort;
+  // tensor parallelism (stand-alone RESID launches): the exchange the epilogue sums the ranks' strips through
+  CommDesc ex;
+  int ex_on;
 };
 
 // The fields of a fused linear that differ between the layers of a model: the matrices' data,
@@ -1043,6 +1047,8 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       int pv = -1;
       if (EPI == GSDLQ_EPI_ROPE_KV) pv = *J.pos;
       reinterpret_cast<int*>(redu)[34] = pv;
+      // the call number of this launch's exchange (read by every CTA before the last one advances it)
+      if (EPI == GSDLQ_EPI_RESID && !MEGA && P.ex_on) redu[41] = *reinterpret_cast<volatile unsigned*>(ex_words(P.ex)) + 1u;
     }
     int tok = 0;
     if (mp.input_mode() == GSDLQ_IN_EMBED) {
@@ -1319,7 +1325,13 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
       v_scale = 1.0f / sqrtf(tot / (float)C + J.eps);  // gsd_lq_cpu_engine.c:78
     }
     unsigned nfin = 0u;
+    // tensor parallelism: finished strips are posted to the peers here and summed after the loop
+    const bool exch = EPI == GSDLQ_EPI_RESID && !MEGA && P.ex_on;
+    const unsigned ex_k = exch ? redu[41] : 0u;
+    unsigned ex_mask = 0u;  // loop iterations of this warp whose strip it posted
+    int iter = -1;
     for (int s = s_lo + warp; s <= s_hi; s += HX_WARPS) {
+      ++iter;
       const long long first = (long long)s * P.UPS;
       const int cf = hx_cta_of(P.T, P.n_cta, first), cl = hx_cta_of(P.T, P.n_cta, first + P.UPS - 1);
       const StripInfo si = strip_info<NMAT>(P, s);
@@ -1349,8 +1361,59 @@ __device__ __forceinline__ void hexmv_body(const HexmvParams& P, const PTR& mp, 
           *g = 0ull;  // the workspace is zero again for its next launch
         }
       }
+      if (exch) {
+        // this rank's partial of the strip's rows into every other rank's slots (value | call << 32);
+        // kept in the accumulator word for the sum below
+        const float pv = hx_unfix(a) * v_scale;
+        const int row = si.rbase + (lane & 15);
+        if (lane < 16 && row < J.mat[0].rows) {
+          const unsigned long long w = ll_pack(pv, ex_k);
+          for (int r = 0; r < P.ex.world; ++r)
+            if (r != P.ex.rank) st_vol_u64(ex_slot(P.ex, r, ex_k, P.ex.rank, row), w);
+          reinterpret_cast<float*>(lacc + (size_t)(s - s_lo) * width + lane)[0] = pv;
+        }
+        ex_mask |= 1u << iter;
+        ++nfin;
+        continue;
+      }
       finish_value<EPI, NMAT>(P, mp, si, hx_unfix(a) * v_scale, lane, pos, sp);
       ++nfin;
+    }
+    if (exch) {
+      // y = ((resid + p_0) + p_1) + ... in rank order (the peers' partials from this rank's slots,
+      // bounded waits), the same bits on every rank
+      unsigned long long deadline = 0ull;
+      bool gave_up = false;
+      for (int i = 0; i < 32 && (ex_mask >> i) != 0u; ++i) {
+        if (((ex_mask >> i) & 1u) == 0u) continue;
+        const int s = s_lo + warp + i * HX_WARPS;
+        const StripInfo si = strip_info<NMAT>(P, s);
+        const int row = si.rbase + (lane & 15);
+        float out = 0.f;
+        // one lane waits for each peer's strip (a peer posts a strip's 16 rows together), then the
+        // others read their rows
+        if (lane == 0)
+          for (int r = 0; r < P.ex.world; ++r)
+            if (r != P.ex.rank) (void)ex_wait(P.ex, ex_k, r, si.rbase, deadline, gave_up);
+        __syncwarp();
+        if (lane < 16 && row < J.mat[0].rows) {
+          const float own = reinterpret_cast<const float*>(lacc + (size_t)(s - s_lo) * width + lane)[0];
+          out = __ldcg(J.resid + row);
+          for (int r = 0; r < P.ex.world; ++r) out += r == P.ex.rank ? own : ex_wait(P.ex, ex_k, r, row, deadline, gave_up);
+          J.y[0][row] = out;
+        }
+        // low-rank forwarding of the summed rows into the next launch (the whole warp: shuffles)
+        if (J.fwd_acc != nullptr) fwd_apply(J, fwd_load(J, si.rbase, J.mat[0].rows, lane), si.rbase, J.mat[0].rows, out, lane);
+      }
+      // the last CTA to get here advances the exchange's call number for the next such launch
+      __syncthreads();
+      if (tid == 0) {
+        unsigned* w = ex_words(P.ex);
+        if (atomicAdd(w + 1, 1u) == gridDim.x - 1) {
+          w[1] = 0u;
+          w[0] = ex_k;
+        }
+      }
     }
     if (lane == 0) GSDLQ_TR_MAX(HX_SLOT_NOW, 7);
     if (MEGA) {

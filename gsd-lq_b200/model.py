@@ -88,6 +88,7 @@ class GSDLQModel:
         self._load(source)
         if self.tp is not None:
             self.tp.setup(self)  # the residual exchange among the ranks (collective: every rank calls it)
+            self._wire_exchange()
         self.cl = _DeviceInfo(self)
         self.tokenizer = tokenizer_from_config(self.cfg)  # SentencePiece BPE over the header's vocabulary
         self._graphs: dict = {}
@@ -241,8 +242,9 @@ class GSDLQModel:
     def _wire_forwarding(self):
         """Low-rank forwarding: every op whose output is the next linear's input adds that linear's
         projection of it (strip by strip, fixed point) to the next launch's workspace, which then
-        skips its own grid-wide projection.  (Tensor parallelism keeps the in-kernel projection:
-        there the epilogues see partial sums.)"""
+        skips its own grid-wide projection.  (Tensor parallelism forwards only with the fused
+        exchange, whose O and down epilogues hold the summed residual; with separate all-reduce
+        launches they see partial sums and every launch keeps its in-kernel projection.)"""
         def acc(job):
             return self.ws_of[id(job)].data_ptr() + 64  # the workspace's accumulator words
 
@@ -324,6 +326,23 @@ class GSDLQModel:
         if policy & self.PF_HEAD_QKV:
             self._set_prefetch(self.head_job, self._ranges(qkv_w(0)))
 
+    def _wire_exchange(self):
+        """Tensor parallelism with the fused exchange: the O and down launches of every rank sum the
+        ranks' partial outputs in their epilogue (gsdlq_linear_job_t.exchange), so the step has no
+        separate all-reduce launches."""
+        if not self.tp.fused_epilogue:
+            return
+        for (qkv, att, o, gu, dn) in self.layer_jobs:
+            for j in (o, dn):
+                j.epilogue = L.EPI_RESID
+                j.resid = self.x.data_ptr()
+                j.exchange = self.tp.comm
+        # every rank holds the summed residual in the O and down epilogues, so low-rank forwarding works
+        # as on one GPU: row-parallel consumers (O, down) receive their rank's partial projection, whose
+        # U S term the exchange sums with the rest of the partial output
+        if self.lr_forward:
+            self._wire_forwarding()
+
     def linear(self, job):
         ops.linear(job, self.ws_of[id(job)])
 
@@ -361,7 +380,7 @@ class GSDLQModel:
 
     # ------------------------------------------------------------------ step
     def _run_layers(self):
-        allreduce = self.tp.allreduce if self.tp is not None else None
+        allreduce = self.tp.allreduce if (self.tp is not None and not self.tp.fused_epilogue) else None
         for qkv, att, o, gu, dn in self.layer_jobs:
             self.linear(qkv)
             ops.attention(att)

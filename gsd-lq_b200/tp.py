@@ -160,6 +160,13 @@ class TensorParallel:
             raise ValueError(f"exchange {self.exchange!r}: use 'p2p' or 'nccl'")
         self.comm = None
 
+    @property
+    def fused_epilogue(self) -> bool:
+        """True when the O and down launches sum the ranks' partials themselves (p2p exchange, unless
+        GSDLQ_TP_FUSED=0 asks for separate all-reduce launches)."""
+        import os
+        return self.comm is not None and os.environ.get("GSDLQ_TP_FUSED", "1") != "0"
+
     def setup(self, model):
         """Create and connect this rank's exchange buffer (p2p), sized for the hidden vector."""
         if self.exchange != "p2p" or self.comm is not None:

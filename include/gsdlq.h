@@ -163,6 +163,10 @@ typedef struct gsdlq_hexmat {
 #define GSDLQ_IN_EMBED 2    /* input = rmsnorm(f32(embed[*token])) * norm_w; CTA 0 writes the
                                raw row to x_out (the residual stream)                      */
 
+/* A tensor-parallel exchange among the ranks of one node (gsdlq_comm_create; see that section). */
+#define GSDLQ_IPC_HANDLE_BYTES 64
+typedef struct gsdlq_comm gsdlq_comm_t;  /* opaque */
+
 /* L2 prefetch list of a launch (engine use; no counterpart in the reference): byte ranges of
  * device memory that a LATER launch will read -- the next linears' packed weights -- fetched into
  * the L2 cache while this launch runs, so that HBM keeps streaming across the gaps between
@@ -216,6 +220,14 @@ typedef struct gsdlq_linear_job {
   unsigned long long *fwd_acc;
   int lr_forwarded;
   gsdlq_prefetch_t prefetch;  /* optional L2 prefetch of later launches' weights */
+  /* Tensor parallelism (optional; RESID epilogue of one matrix): a connected exchange (host
+   * handle).  Every rank then finishes each strip as
+   *   y[r] = ((resid[r] + p_0[r]) + p_1[r]) + ... + p_{W-1}[r],
+   * p_w = rank w's partial W x, exchanged through the peers' buffers strip by strip -- the
+   * all-reduce of the row-parallel O and down projections fused into their epilogue, the same bits
+   * on every rank; low-rank forwarding (fwd_acc) is applied to the summed y.  Every rank must
+   * launch the same sequence of such jobs. */
+  gsdlq_comm_t *exchange;
 } gsdlq_linear_job_t;
 
 /* Bytes of device workspace a gsdlq_linear launch of `job` needs (host pointers). */
@@ -361,8 +373,6 @@ int gsdlq_hex2d_matmul(const float *x, int batch, const uint8_t *codes, const ui
  *   allreduce_max_u64: *key := the maximum over ranks (the vocab-parallel greedy argmax key).
  * Both are stream-ordered kernels (capturable into a CUDA graph) that read their input after the
  * previous kernel on the stream has completed. */
-#define GSDLQ_IPC_HANDLE_BYTES 64
-typedef struct gsdlq_comm gsdlq_comm_t;  /* opaque */
 int gsdlq_comm_create(int world, int rank, int n_max, gsdlq_comm_t **comm, void *ipc_handle);
 int gsdlq_comm_connect(gsdlq_comm_t *comm, const void *handles);
 int gsdlq_comm_allreduce_sum(gsdlq_comm_t *comm, float *x, int n, gsdlq_stream_t stream);
