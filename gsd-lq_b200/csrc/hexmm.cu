@@ -1,24 +1,29 @@
-// hexmm.cu -- the batched packed linear: B <= 64 tokens through one GSD-LQ matrix as a dequant-GEMM on
-// the tensor cores (the batch-B counterpart of gsd_cpu_lowrank_proj + gsd_cpu_hex2d_matvec,
-// gsd_lq_cpu_engine.c:111-183, applied to each token).
+// hexmm.cu -- the batched packed linear: B <= 128 tokens through one GSD-LQ matrix as a dequant-GEMM on
+// the 5th-generation tensor cores (tcgen05, accumulators in tensor memory) -- the batch-B counterpart of
+// gsd_cpu_lowrank_proj + gsd_cpu_hex2d_matvec (gsd_lq_cpu_engine.c:111-183) applied to each token, used
+// for batched decode and for chunked prefill.
 //
 //   y[b][r] = sum_c W[r][c] x[b][c] + sum_{kinks of r} delta * x[b][col] + sum_j U[r][j] tmp[b][j],
 //   W[r][2p + i] = xy[code(r, p)][i] * scale(r, p / 32),  tmp[b][j] = S[j] * (Vt[j] . x[b]).
 //
-// Layout of the work.  A CTA of 4 warps owns 64 weight rows and a contiguous run of 64-column k-blocks
-// (split-K over CTAs, so that enough loads are in flight on every SM).  Per k-block:
-//   - each thread decodes 16 code bytes of one row (32 weights, one scale group) through a 256-entry
-//     float2 table into fp32 weights, W = xy * scale as the reference's dequant defines them, and writes
-//     each as an fp16 hi + lo pair into two shared W tiles (about 22 significant bits together);
-//   - the block's activations of every token are written as fp16 hi + lo splits (x scaled per token by a
-//     power of two that puts max|x_b| in [2^14, 2^15), so both halves stay normal);
-//   - mma.sync m16n8k16 (fp16 in, fp32 accumulate): warp w takes rows 16w..16w+15; per 8-token n-tile
-//     and k-step three MMAs, W_hi x_hi + W_hi x_lo + W_lo x_hi (the lo * lo term is below fp32 rounding);
-//   - the codes and scales of the block two ahead and the activations of the next block are loaded into
-//     registers while this one is computed.
-// The partial sums are added into y (zeroed by the entry point) with fp32 atomics, so the summation
-// order over the k-runs is not fixed; the kink and low-rank terms are added once per (row, token) by the
-// CTA of the run with the token's index modulo the number of runs.
+// Layout of the work.  A CTA of 4 warps owns a tile of 128 weight rows and a contiguous run of 64-column
+// k-blocks (split-K over CTAs, so that every SM streams weights).  Per k-block, through two shared-memory
+// stages:
+//   - thread t decodes the 32 code bytes of row t (one scale group) through a 256-entry float2 table into
+//     fp32 weights, W = xy * scale as the reference's dequant defines them, splits them into fp16 hi + lo
+//     parts (about 22 significant bits together) and writes them as two A operands: K-major core matrices
+//     of 8 rows x 16 bytes, no swizzle (LBO 128 B between the two 8-column halves of a 16-column k-step,
+//     SBO 1024 B between 8-row groups);
+//   - the block's activations of every token are written as the B operand in the same layout, token b as
+//     two rows: 2b = fp16 hi, 2b + 1 = fp16 lo of x_b scaled by a power of two that puts max|x_b| in
+//     [2^14, 2^15) (so both halves stay normal; about 22 significant bits together);
+//   - one thread issues eight tcgen05.mma (W hi and W lo for each 16-column k-step; M = 128, N = 2 x tokens
+//     padded to 8, fp16 in, fp32 accumulate in tensor memory) and commits them to the stage's mbarrier,
+//     which releases the stage for the block two ahead; the next block's codes are loaded meanwhile.
+// At the end each warp reads its 32 tensor-memory lanes (its rows) with tcgen05.ld, adds each token's hi
+// and lo columns, unscales, and adds the partial sums into y (zeroed by the entry point) with fp32 atomics,
+// so the summation order over the k-runs is not fixed.  The kink and low-rank terms are added once per
+// (row, token) by the CTA whose run index equals the token index modulo the number of runs.
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -27,18 +32,14 @@
 
 namespace gsdlq {
 
-constexpr int MM_ROWS = 64;        // weight rows per CTA
-constexpr int MM_KB = 64;          // columns per k-block: one scale group
-constexpr int MM_THREADS = 128;    // 4 warps, 16 rows each
-constexpr int MM_MAXB = 64;        // tokens per call
-constexpr int MM_XROW = MM_KB + 8; // halves per shared row (padded: conflict-free fragment loads)
-
-__device__ __forceinline__ void mm_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
+constexpr int MM_ROWS = 128;      // weight rows per CTA (tensor-memory lanes)
+constexpr int MM_KB = 64;         // columns per k-block: one scale group
+constexpr int MM_THREADS = 128;   // thread t decodes row t and reads lane t of the accumulator
+constexpr int MM_MAXB = GSDLQ_MATMUL_MAX_BATCH;  // tokens per call (N = 2 * 128 = 256, the largest MMA N)
+static_assert(GSDLQ_MATMUL_WORK_FLOATS >= 17 * MM_MAXB, "work: maxima and low-rank projections of every token");
+constexpr int MM_AHALF = MM_ROWS * MM_KB * 2;  // bytes of one fp16 A tile (16 KB): the weights' hi or lo parts
+constexpr int MM_ATILE = 2 * MM_AHALF;         // one stage's A tiles (hi, then lo)
+constexpr int MM_HDR = 4096;                   // table, barriers, tensor-memory slot, token scales
 
 // Per token b and chunk of MM_PREP columns: the chunk's max|x_b| into amax[b] (as ordered bits) and its
 // part of S[j] * (Vt[j] . x_b) into tmp[16 b + j] (gsd_cpu_lowrank_proj; fp32 atomics, so the summation
@@ -82,6 +83,7 @@ __global__ void __launch_bounds__(256) hexmm_prep(const float* __restrict__ x, i
   }
 }
 
+
 // the power of two that puts max|x_b| in [2^14, 2^15), so both fp16 halves of x_b stay normal
 __device__ __forceinline__ float hexmm_xscale(unsigned amax_bits) {
   const float m = __uint_as_float(amax_bits);
@@ -91,7 +93,62 @@ __device__ __forceinline__ float hexmm_xscale(unsigned amax_bits) {
   return (m > 0.f && m <= 3.0e38f) ? ldexpf(1.f, 15 - e) : 1.f;
 }
 
-// NB: 8-token n-tiles (tokens padded to 8 NB with zero activations).
+// ---- tcgen05 helpers (cta_group::1) -----------------------------------------------------------
+// shared-memory matrix descriptor: K-major, no swizzle, LBO 128 B, SBO 1024 B, descriptor version 1
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128u >> 4) << 16) | ((uint64_t)(1024u >> 4) << 32) |
+         (1ull << 46);
+}
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 16 consecutive 32-bit columns of this thread's tensor-memory lane
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);  // a in the low half
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <int NB>
+constexpr int mm_tcols() {  // tensor-memory columns of the accumulator: a power of two >= 32
+  return 16 * NB <= 32 ? 32 : 16 * NB <= 64 ? 64 : 16 * NB <= 128 ? 128 : 256;
+}
+template <int NB>
+constexpr int mm_smem() {
+  // header + two A stages + two B stages (16 NB rows of 128 bytes); with 256 accumulator columns at
+  // least 80 KB, so that no more than two CTAs share an SM's 512 tensor-memory columns (a third
+  // would wait in tcgen05.alloc)
+  constexpr int need = MM_HDR + 2 * MM_ATILE + 2 * 16 * NB * 128;  // (at least 80 KB whenever NB > 8)
+  return (mm_tcols<NB>() == 256 && need < 80 * 1024) ? 80 * 1024 : need;
+}
+static_assert(mm_smem<3>() * 9 > 227 * 1024 && mm_smem<5>() * 5 > 227 * 1024 && mm_smem<9>() * 3 > 227 * 1024,
+              "at most 512 tensor-memory columns of resident CTAs per SM");
+
+// NB: groups of 8 tokens (tokens padded to 8 NB with zero activations); N = 16 NB accumulator columns.
 template <int NB>
 __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restrict__ x, int B,
                                                            const uint8_t* __restrict__ codes,
@@ -103,146 +160,180 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
                                                            const float* __restrict__ kdel, float* __restrict__ y,
                                                            int R, int C, int nsplit, const unsigned* __restrict__ amax_bits,
                                                            const float* __restrict__ tmp) {
-  constexpr int BP = NB * 8;                        // padded tokens
-  constexpr int XE = BP * MM_KB / MM_THREADS;       // activations of a k-block per thread
-  __shared__ __align__(16) uint16_t wh[MM_ROWS * MM_XROW];
-  __shared__ __align__(16) uint16_t wl[MM_ROWS * MM_XROW];
-  __shared__ __align__(16) uint16_t xh[BP * MM_XROW];
-  __shared__ __align__(16) uint16_t xl[BP * MM_XROW];
-  __shared__ float2 tab[256];
-  __shared__ float s_xsc[MM_MAXB];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, q4 = lane & 3;
-  const int r0 = blockIdx.x * MM_ROWS;
-  const int split = blockIdx.y;
+  constexpr int N = 16 * NB, BP = 8 * NB;
+  constexpr uint32_t TCOLS = (uint32_t)mm_tcols<NB>();
+  constexpr int BTILE = N * 128;
+  extern __shared__ __align__(1024) uint8_t sm[];
+  float2* tab = reinterpret_cast<float2*>(sm);                    // [0, 2048)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + 2064);       // tensor-memory address
+  float* xsc = reinterpret_cast<float*>(sm + 2080);               // [MM_MAXB] token scales
+  const uint32_t sbase = smem_u32(sm);
+  const uint32_t bar0 = sbase + 2048;                             // two mbarriers (8 bytes each)
+  const uint32_t a_base = sbase + MM_HDR, b_base = sbase + MM_HDR + 2 * MM_ATILE;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int r0 = blockIdx.x * MM_ROWS, split = blockIdx.y;
   const int NP = C / 2, G = C / 64, nkb = C / MM_KB;
   const int kb0 = (int)((long long)nkb * split / nsplit), kb1 = (int)((long long)nkb * (split + 1) / nsplit);
-  for (int i = tid; i < 256; i += MM_THREADS) tab[i] = i < n_pts ? make_float2(xy[2 * i], xy[2 * i + 1]) : make_float2(0.f, 0.f);
-  for (int i = tid; i < BP; i += MM_THREADS) s_xsc[i] = i < B ? hexmm_xscale(amax_bits[i]) : 0.f;
-  __syncthreads();
+  const int nk = kb1 - kb0;
 
-  // this thread's share of a k-block: 16 code bytes (32 weights) of row drow, and XE activations
-  const int drow = tid >> 1, dhalf = tid & 1;
-  const bool rok = r0 + drow < R;
-  const uint8_t* cp = codes + (size_t)(rok ? r0 + drow : 0) * NP + dhalf * 16;
-  const uint16_t* scp = scales + (size_t)(rok ? r0 + drow : 0) * G;
-  auto load_x = [&](int kb, float (&xr)[XE]) {
-#pragma unroll
-    for (int i = 0; i < XE; ++i) {
-      const int e = tid + i * MM_THREADS, b = e / MM_KB, c = e - b * MM_KB;
-      xr[i] = b < B ? x[(size_t)b * C + kb * MM_KB + c] * s_xsc[b] : 0.f;
-    }
-  };
-  // codes and scales two k-blocks ahead (HBM), activations one ahead (L2)
-  uint4 cw = make_uint4(0u, 0u, 0u, 0u), cw2 = make_uint4(0u, 0u, 0u, 0u);
-  uint16_t sc = 0, sc2 = 0;
-  float xr[XE];
-  if (kb1 > kb0) {
-    if (rok) {
-      cw = *reinterpret_cast<const uint4*>(cp + kb0 * 32);
-      sc = scp[kb0];
-      if (kb0 + 1 < kb1) {
-        cw2 = *reinterpret_cast<const uint4*>(cp + (kb0 + 1) * 32);
-        sc2 = scp[kb0 + 1];
-      }
-    }
-    load_x(kb0, xr);
+  for (int i = tid; i < 256; i += MM_THREADS) tab[i] = i < n_pts ? make_float2(xy[2 * i], xy[2 * i + 1]) : make_float2(0.f, 0.f);
+  for (int i = tid; i < BP; i += MM_THREADS) xsc[i] = i < B ? hexmm_xscale(amax_bits[i]) : 0.f;
+  if (tid == 0) {
+    mbar_init(bar0, 1u);
+    mbar_init(bar0 + 8u, 1u);
+    mbar_fence_init();
   }
-  float acc[NB][4];
-#pragma unroll
-  for (int n = 0; n < NB; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  if (warp == 0) tmem_alloc(smem_u32(tslot), TCOLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot);
+
+  const int row = r0 + tid;
+  const bool rok = row < R;
+  const uint8_t* cp = codes + (size_t)(rok ? row : 0) * NP;
+  const uint16_t* scp = scales + (size_t)(rok ? row : 0) * G;
+  uint4 c0 = make_uint4(0u, 0u, 0u, 0u), c1 = make_uint4(0u, 0u, 0u, 0u);
+  uint16_t sc = 0;
+  if (rok && nk > 0) {
+    c0 = *reinterpret_cast<const uint4*>(cp + kb0 * 32);
+    c1 = *reinterpret_cast<const uint4*>(cp + kb0 * 32 + 16);
+    sc = scp[kb0];
+  }
+  // instruction descriptor: D fp32, A and B fp16, both K-major, N, M = 128
+  const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(MM_ROWS >> 4) << 24);
   bool bad = false;
   for (int kb = kb0; kb < kb1; ++kb) {
-    // ---- stage block kb: W rows as fp16, activations as fp16 hi + lo ----
+    const int i = kb - kb0, st = i & 1;
+    // the MMAs of two blocks ago read this stage: wait for their commit (bounded)
+    if (i >= 2) mbar_wait_bounded(bar0 + 8u * st, (uint32_t)(((i >> 1) - 1) & 1));
+    // ---- A: row tid's 64 weights, chunk j = weights 8j .. 8j+7 = code bytes 4j .. 4j+3 ----
     const float s = h2f(sc);
-    const uint32_t cv[4] = {cw.x, cw.y, cw.z, cw.w};
+    const uint32_t cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    uint8_t* arow = sm + MM_HDR + st * MM_ATILE + (tid >> 3) * 1024 + (tid & 7) * 16;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int code = (int)((cv[i >> 2] >> (8 * (i & 3))) & 0xffu);
-      bad |= rok && code >= n_pts;
-      const float2 p = tab[code];
-      const float w0 = p.x * s, w1 = p.y * s;  // a3 dequant: one fp32 multiply per weight
-      const uint16_t h0 = f2h(w0), h1 = f2h(w1);
-      const int o = drow * MM_XROW + dhalf * 32 + 2 * i;
-      *reinterpret_cast<uint32_t*>(wh + o) = (uint32_t)h0 | ((uint32_t)h1 << 16);
-      *reinterpret_cast<uint32_t*>(wl + o) = (uint32_t)f2h(w0 - h2f(h0)) | ((uint32_t)f2h(w1 - h2f(h1)) << 16);
-    }
+    for (int j = 0; j < 8; ++j) {
+      uint32_t h[4], l[4];
 #pragma unroll
-    for (int i = 0; i < XE; ++i) {
-      const int e = tid + i * MM_THREADS, b = e / MM_KB, c = e - b * MM_KB;
-      const uint16_t hi = f2h(xr[i]);
-      xh[b * MM_XROW + c] = hi;
-      xl[b * MM_XROW + c] = f2h(xr[i] - h2f(hi));
-    }
-    // ---- the next block's operands into registers while this one is multiplied ----
-    cw = cw2;
-    sc = sc2;
-    if (rok && kb + 2 < kb1) {
-      cw2 = *reinterpret_cast<const uint4*>(cp + (kb + 2) * 32);
-      sc2 = scp[kb + 2];
-    }
-    if (kb + 1 < kb1) load_x(kb + 1, xr);
-    __syncthreads();
-    const int ao = (16 * warp + g) * MM_XROW + 2 * q4;
-#pragma unroll
-    for (int kk = 0; kk < MM_KB / 16; ++kk) {
-      uint32_t ah[4], al[4];
-      const int o = ao + kk * 16;
-      ah[0] = *reinterpret_cast<const uint32_t*>(wh + o);
-      ah[1] = *reinterpret_cast<const uint32_t*>(wh + o + 8 * MM_XROW);
-      ah[2] = *reinterpret_cast<const uint32_t*>(wh + o + 8);
-      ah[3] = *reinterpret_cast<const uint32_t*>(wh + o + 8 * MM_XROW + 8);
-      al[0] = *reinterpret_cast<const uint32_t*>(wl + o);
-      al[1] = *reinterpret_cast<const uint32_t*>(wl + o + 8 * MM_XROW);
-      al[2] = *reinterpret_cast<const uint32_t*>(wl + o + 8);
-      al[3] = *reinterpret_cast<const uint32_t*>(wl + o + 8 * MM_XROW + 8);
-#pragma unroll
-      for (int n = 0; n < NB; ++n) {
-        const uint16_t* bh = xh + (n * 8 + g) * MM_XROW + kk * 16 + 2 * q4;
-        const uint16_t* bl = xl + (n * 8 + g) * MM_XROW + kk * 16 + 2 * q4;
-        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(bh), bh1 = *reinterpret_cast<const uint32_t*>(bh + 8);
-        mm_f16_16816(acc[n], ah, bh0, bh1);
-        mm_f16_16816(acc[n], ah, *reinterpret_cast<const uint32_t*>(bl), *reinterpret_cast<const uint32_t*>(bl + 8));
-        mm_f16_16816(acc[n], al, bh0, bh1);
+      for (int q = 0; q < 4; ++q) {
+        const int code = (int)((cv[j] >> (8 * q)) & 0xffu);
+        bad |= rok && code >= n_pts;
+        const float2 p = tab[code];
+        const float w0 = p.x * s, w1 = p.y * s;  // a3 dequant: one fp32 multiply per weight
+        const __half2 hh = __floats2half2_rn(w0, w1);
+        h[q] = *reinterpret_cast<const uint32_t*>(&hh);
+        l[q] = pack_h2(w0 - __low2float(hh), w1 - __high2float(hh));  // fp16 hi + lo: about 22 bits
       }
+      *reinterpret_cast<uint4*>(arow + j * 128) = make_uint4(h[0], h[1], h[2], h[3]);
+      *reinterpret_cast<uint4*>(arow + MM_AHALF + j * 128) = make_uint4(l[0], l[1], l[2], l[3]);
     }
-    __syncthreads();  // every read of the tiles is done before the next block is staged
+    // the next block's codes into registers while this one is staged and multiplied
+    if (rok && kb + 1 < kb1) {
+      c0 = *reinterpret_cast<const uint4*>(cp + (kb + 1) * 32);
+      c1 = *reinterpret_cast<const uint4*>(cp + (kb + 1) * 32 + 16);
+      sc = scp[kb + 1];
+    }
+    // ---- B: token b, chunk j -> rows 2b (hi) and 2b + 1 (lo) ----
+    uint8_t* bt = sm + MM_HDR + 2 * MM_ATILE + st * BTILE;
+    for (int e = tid; e < BP * 8; e += MM_THREADS) {
+      const int b = e >> 3, j = e & 7;
+      float v[8];
+      if (b < B) {
+        const float4* xp = reinterpret_cast<const float4*>(x + (size_t)b * C + kb * MM_KB + 8 * j);
+        const float4 u0 = xp[0], u1 = xp[1];
+        const float f = xsc[b];
+        v[0] = u0.x * f, v[1] = u0.y * f, v[2] = u0.z * f, v[3] = u0.w * f;
+        v[4] = u1.x * f, v[5] = u1.y * f, v[6] = u1.z * f, v[7] = u1.w * f;
+      } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[t] = 0.f;
+      }
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const __half2 hh = __floats2half2_rn(v[2 * t], v[2 * t + 1]);
+        hi[t] = *reinterpret_cast<const uint32_t*>(&hh);
+        lo[t] = pack_h2(v[2 * t] - __low2float(hh), v[2 * t + 1] - __high2float(hh));
+      }
+      const int rh = 2 * b, rl = 2 * b + 1;
+      *reinterpret_cast<uint4*>(bt + (rh >> 3) * 1024 + j * 128 + (rh & 7) * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(bt + (rl >> 3) * 1024 + j * 128 + (rl & 7) * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    fence_proxy_async_smem();  // the tiles' generic stores, visible to the tensor core's reads
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < MM_KB / 16; ++kk) {
+        const uint64_t bd = umma_desc(b_base + st * BTILE + kk * 256);
+        umma_f16(tmem, umma_desc(a_base + st * MM_ATILE + kk * 256), bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        umma_f16(tmem, umma_desc(a_base + st * MM_ATILE + MM_AHALF + kk * 256), bd, idesc, 1u);
+      }
+      umma_commit(bar0 + 8u * st);  // arrives when every MMA issued so far has completed
+    }
   }
   if (bad) raise_flag(GSDLQ_FLAG_BAD_CODE);
-  // ---- this run's partial sums into y (unscaled): lane (g, q4) holds rows g, g+8, tokens 2q4, 2q4+1 ----
-  if (kb1 > kb0) {
+  // ---- the run's partial sums: lane tid = row tid; columns 2b, 2b + 1 = token b's hi and lo parts ----
+  if (nk > 0) {
+    mbar_wait_bounded(bar0 + 8u * ((nk - 1) & 1), (uint32_t)(((nk - 1) >> 1) & 1));
+    tc_fence_after();
+#pragma unroll 1
+    for (int cb = 0; cb < N / 16; ++cb) {
+      uint32_t v[16];
+      tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(cb * 16), v);
 #pragma unroll
-    for (int n = 0; n < NB; ++n) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = r0 + 16 * warp + g + (e >= 2 ? 8 : 0), b = n * 8 + 2 * q4 + (e & 1);
-        if (r < R && b < B) atomicAdd(y + (size_t)b * R + r, acc[n][e] / s_xsc[b]);
+      for (int t = 0; t < 8; ++t) {
+        const int b = cb * 8 + t;
+        if (rok && b < B)
+          atomicAdd(y + (size_t)b * R + row, (__uint_as_float(v[2 * t]) + __uint_as_float(v[2 * t + 1])) / xsc[b]);
       }
     }
   }
   // ---- kinks and the low-rank term, once per (row, token): tokens b = split (mod nsplit) ----
   bool badk = false;
-  for (int i = tid; i < MM_ROWS * BP; i += MM_THREADS) {
-    const int rr = i / BP, b = i - rr * BP, r = r0 + rr;
-    if (r >= R || b >= B || b % nsplit != split) continue;
-    float v = 0.f;
-    for (int j = 0; j < k; ++j) v = fmaf(h2f(U[(size_t)r * k + j]), tmp[(size_t)b * 16 + j], v);
-    const float* xb = x + (size_t)b * C;
-    for (uint32_t e = row_ptr[r]; e < row_ptr[r + 1]; ++e) {
-      const int col = kcols[e];
-      if (col < C) v = fmaf(kdel[e], xb[col], v);
-      else badk = true;
+  if (rok) {
+    for (int b = split; b < B; b += nsplit) {
+      float v = 0.f;
+      for (int j = 0; j < k; ++j) v = fmaf(h2f(U[(size_t)row * k + j]), tmp[(size_t)b * 16 + j], v);
+      const float* xb = x + (size_t)b * C;
+      for (uint32_t e = row_ptr[row]; e < row_ptr[row + 1]; ++e) {
+        const int col = kcols[e];
+        if (col < C) v = fmaf(kdel[e], xb[col], v);
+        else badk = true;
+      }
+      atomicAdd(y + (size_t)b * R + row, v);
     }
-    atomicAdd(y + (size_t)b * R + r, v);
   }
   if (badk) raise_flag(GSDLQ_FLAG_BAD_KINK);
+  // ---- release the tensor memory (every warp's loads are complete) ----
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TCOLS);
+  }
 }
 
 template <int NB>
-static cudaError_t hexmm_launch_nb(dim3 grid, cudaStream_t s, const float* x, int B, const uint8_t* codes,
+static cudaError_t hexmm_launch_nb(int tiles, int nkb, cudaStream_t s, const float* x, int B, const uint8_t* codes,
                                    const uint16_t* scales, const float* xy, int n_pts, const uint16_t* U, int k,
                                    const uint32_t* rp, const uint16_t* kc, const float* kd, float* y, int R, int C,
-                                   int nsplit, const unsigned* amax, const float* tmp) {
-  hexmm_kernel<NB><<<grid, MM_THREADS, 0, s>>>(x, B, codes, scales, xy, n_pts, U, k, rp, kc, kd, y, R, C, nsplit, amax, tmp);
+                                   const unsigned* amax, const float* tmp) {
+  constexpr int smem = mm_smem<NB>();
+  static bool configured[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (!configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(hexmm_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  // k-runs per row tile: the CTAs that fit an SM at once (shared memory) on every SM, at least one
+  // k-block each
+  const int per_sm = std::max(1, std::min(8, (227 * 1024) / smem));
+  const int nsplit = std::max(1, std::min(nkb, (per_sm * num_sms() + tiles - 1) / tiles));
+  hexmm_kernel<NB><<<dim3(tiles, nsplit), MM_THREADS, smem, s>>>(x, B, codes, scales, xy, n_pts, U, k, rp, kc, kd, y, R,
+                                                                 C, nsplit, amax, tmp);
   return cudaGetLastError();
 }
 
@@ -264,8 +355,8 @@ extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* code
   if (reinterpret_cast<uintptr_t>(codes) & 15u) return GSDLQ_ERR_INVALID;  // 16-byte code loads
   if ((reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(U) | reinterpret_cast<uintptr_t>(Vt)) & 1u)
     return GSDLQ_ERR_INVALID;
-  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(work)) & 3u)
-    return GSDLQ_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(x) & 15u) return GSDLQ_ERR_INVALID;  // 16-byte activation loads
+  if ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(work)) & 3u) return GSDLQ_ERR_INVALID;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   unsigned* amax = reinterpret_cast<unsigned*>(work);  // per-token max|x| (bits)
   float* tmp = work + MM_MAXB;
@@ -275,23 +366,19 @@ extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* code
   hexmm_prep<<<dim3(batch, (cols + MM_PREP - 1) / MM_PREP), 256, 0, s>>>(x, cols, Vt, S, k_dim, amax, tmp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return record_cuda_error(e);
-  // k-runs per row tile: about eight CTAs per SM in all up to 16 tokens (shorter load chains per CTA),
-  // four above (the wide-batch kernels hold more registers), at least one k-block each
   const int tiles = (rows + MM_ROWS - 1) / MM_ROWS, nkb = cols / MM_KB;
-  const int per_sm = batch <= 16 ? 8 : 4;
-  const int nsplit = std::max(1, std::min(nkb, (per_sm * num_sms() + tiles - 1) / tiles));
-  const dim3 grid(tiles, nsplit);
   const float* kd = kink_deltas;
+#define GSDLQ_MM_CASE(nb)                                                                                               \
+  case nb:                                                                                                              \
+    e = hexmm_launch_nb<nb>(tiles, nkb, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, \
+                            kd, y, rows, cols, amax, tmp);                                                              \
+    break;
   switch ((batch + 7) / 8) {
-    case 1: e = hexmm_launch_nb<1>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
-    case 2: e = hexmm_launch_nb<2>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
-    case 3: e = hexmm_launch_nb<3>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
-    case 4: e = hexmm_launch_nb<4>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
-    case 5: e = hexmm_launch_nb<5>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
-    case 6: e = hexmm_launch_nb<6>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
-    case 7: e = hexmm_launch_nb<7>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
-    default: e = hexmm_launch_nb<8>(grid, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, kd, y, rows, cols, nsplit, amax, tmp); break;
+    GSDLQ_MM_CASE(1) GSDLQ_MM_CASE(2) GSDLQ_MM_CASE(3) GSDLQ_MM_CASE(4) GSDLQ_MM_CASE(5) GSDLQ_MM_CASE(6)
+    GSDLQ_MM_CASE(7) GSDLQ_MM_CASE(8) GSDLQ_MM_CASE(9) GSDLQ_MM_CASE(10) GSDLQ_MM_CASE(11) GSDLQ_MM_CASE(12)
+    GSDLQ_MM_CASE(13) GSDLQ_MM_CASE(14) GSDLQ_MM_CASE(15) default: GSDLQ_MM_CASE(16)
   }
+#undef GSDLQ_MM_CASE
   if (e != cudaSuccess) return record_cuda_error(e);
   return GSDLQ_OK;
 }

@@ -149,8 +149,13 @@ def hex2d_matvec(x, h: DeviceHex, xy_table, tmp_k, y):
                                       h.k_dim, h.n_pts, stream_handle()), "hex2d_matvec")
 
 
+MATMUL_MAX_BATCH = 128         # GSDLQ_MATMUL_MAX_BATCH
+MATMUL_WORK_FLOATS = 17 * 128  # GSDLQ_MATMUL_WORK_FLOATS
+
+
 def hex2d_matmul(x, h: DeviceHex, xy_table, y, work):
-    """y[b] = the packed linear of x[b] for every row b of x ([batch][cols] -> [batch][rows]); work: 1088+ floats."""
+    """y[b] = the packed linear of x[b] for every row b of x ([batch][cols] -> [batch][rows]); work:
+    MATMUL_WORK_FLOATS floats of device scratch."""
     L.check(_lib().gsdlq_hex2d_matmul(ptr(x), x.shape[0], ptr(h.codes), ptr(h.scales), ptr(xy_table), ptr(h.U),
                                       ptr(h.S), ptr(h.Vt), ptr(h.row_ptr), ptr(h.kink_cols), ptr(h.kink_deltas),
                                       ptr(y), ptr(work), h.rows, h.cols, h.k_dim, h.n_pts, stream_handle()),

@@ -63,9 +63,9 @@ def test_batched_and_noalloc_argument_errors_before_launch():
     def mm(x=A, batch=4, codes=A, y=A, work=A, rows=64, cols=128, k=0, n_pts=217, U=None, S=None, Vt=None):
         return lib.gsdlq_hex2d_matmul(x, batch, codes, A, A, U, S, Vt, A, A, A, y, work, rows, cols, k, n_pts, None)
 
-    for kw in (dict(batch=0), dict(batch=65), dict(cols=100), dict(cols=65536), dict(cols=0), dict(rows=0),
+    for kw in (dict(batch=0), dict(batch=129), dict(cols=100), dict(cols=65536), dict(cols=0), dict(rows=0),
                dict(k=17), dict(k=4), dict(n_pts=0), dict(n_pts=257), dict(codes=odd), dict(y=odd),
-               dict(work=odd), dict(x=None), dict(codes=None)):
+               dict(work=odd), dict(x=None), dict(codes=None), dict(x=ctypes.c_void_p(0x100008))):
         assert mm(**kw) == -1, kw
 
     def mv(x=A, codes=A, y=A, rows=64, cols=128, k=0, n_pts=217, U=None, tmp=None):

@@ -19,7 +19,7 @@ def env(cuda_lib):
 
 @pytest.mark.parametrize("rows,cols,k,nnz,radius", [
     (16, 64, 0, 0, 8), (100, 512, 16, 2, 8), (1024, 4096, 16, 16, 8), (4096, 4096, 8, 16, 6), (700, 14336, 16, 56, 8)])
-@pytest.mark.parametrize("batch", [1, 3, 16, 64])
+@pytest.mark.parametrize("batch", [1, 3, 16, 64, 128])
 def test_matmul_vs_oracle(env, restated, rng, rows, cols, k, nnz, radius, batch):
     ops, L = env
     import gsdlq_b200.codebook as cb
@@ -29,7 +29,7 @@ def test_matmul_vs_oracle(env, restated, rng, rows, cols, k, nnz, radius, batch)
     x[batch // 2] *= 40.0  # tokens of very different magnitude share the launch
     h = ops.DeviceHex(t)
     y = torch.full((batch, rows), 7.0, device="cuda")  # the entry point zeroes it
-    work = torch.zeros(17 * 64, device="cuda")
+    work = torch.zeros(ops.MATMUL_WORK_FLOATS, device="cuda")
     xy = dev(cb.xy_table(radius))
     for rep in range(2):
         ops.hex2d_matmul(dev(x), h, xy, y, work)
@@ -51,7 +51,7 @@ def test_matmul_batch1_matches_matvec(env, rng):
     y1, tk = torch.zeros(4096, device="cuda"), torch.zeros(16, device="cuda")
     ops.lowrank_proj(xd[0], h, tk)
     ops.hex2d_matvec(xd[0], h, xy, tk, y1)
-    y2, work = torch.zeros((1, 4096), device="cuda"), torch.zeros(17 * 64, device="cuda")
+    y2, work = torch.zeros((1, 4096), device="cuda"), torch.zeros(ops.MATMUL_WORK_FLOATS, device="cuda")
     ops.hex2d_matmul(xd, h, xy, y2, work)
     torch.cuda.synchronize()
     assert matvec_err(y2.cpu().numpy()[0], y1.cpu().numpy()) < MATVEC_TOL
@@ -62,8 +62,8 @@ def test_matmul_rejects_bad_arguments(env, rng):
     import gsdlq_b200.codebook as cb
     t = rand_hex(rng, 64, 128, k=0, nnz=0, radius=8)
     h = ops.DeviceHex(t)
-    xy, work = dev(cb.xy_table(8)), torch.zeros(17 * 64, device="cuda")
-    for batch in (0, 65):
+    xy, work = dev(cb.xy_table(8)), torch.zeros(ops.MATMUL_WORK_FLOATS, device="cuda")
+    for batch in (0, ops.MATMUL_MAX_BATCH + 1):
         x = torch.zeros((max(batch, 1), 128), device="cuda")
         y = torch.zeros((max(batch, 1), 64), device="cuda")
         st = L.load().gsdlq_hex2d_matmul(ops.ptr(x), batch, ops.ptr(h.codes), ops.ptr(h.scales), ops.ptr(xy), None,
