@@ -389,10 +389,18 @@ def run_ours(args):
     V, P0 = cfg["vocab_size"], args.prompt
     rng = np.random.default_rng(args.seed + 1)
     prompt = rng.integers(0, V, P0).tolist()
+    # prefill time of the prompt with chunked tensor-core prefill (one GPU), then the KV state of the timed
+    # steps from token-by-token prefill at every N, so that the greedy ids compare across N
+    prefill_s = prefill_token_s = None
+    if world == 1:
+        t0 = time.time()
+        model.prefill(prompt[:-1], batched=True)
+        torch.cuda.synchronize()
+        prefill_s = time.time() - t0
     t0 = time.time()
-    model.prefill(prompt[:-1])
+    model.prefill(prompt[:-1], batched=False)
     torch.cuda.synchronize()
-    prefill_s = time.time() - t0
+    prefill_token_s = time.time() - t0
     span = model.max_seq - (P0 - 1)
 
     state = {"pos": P0 - 1}
@@ -502,7 +510,10 @@ def run_ours(args):
             "kinds": kinds, "kinds_pos": kinds_pos, "comm_us_per_step": comm_us, "ids_sha": ids_sha,
             "ids_head": ids[:8].tolist(),
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
-            "clocks": clocks, "pack_s": round(pack_s, 2), "prefill_s": round(prefill_s, 2),
+            "clocks": clocks, "pack_s": round(pack_s, 2),
+            "prefill_s": round(prefill_s, 3) if prefill_s is not None else None,
+            "prefill_tok_s": round((P0 - 1) / prefill_s, 1) if prefill_s else None,
+            "prefill_token_by_token_s": round(prefill_token_s, 3),
             "avg_bpw": round(model.avg_bpw, 4), "step": "fused" if model.fused_step else "per-op",
             "n_layers": model.n_layers, "l2_prefetch": model.prefetch,
             "tp_exchange": model.tp.exchange if model.tp is not None else None,

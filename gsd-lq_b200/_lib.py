@@ -96,6 +96,10 @@ SIGNATURES = {
     "gsdlq_comm_allreduce_sum": ([vp, vp, i32, vp], i32),
     "gsdlq_comm_allreduce_max_u64": ([vp, vp, vp], i32),
     "gsdlq_comm_destroy": ([vp], i32),
+    "gsdlq_embed_rows": ([vp, vp, i32, i32, i32, vp, vp], i32),
+    "gsdlq_rmsnorm_rows": ([vp, vp, vp, i32, i32, f32, vp], i32),
+    "gsdlq_rope_kv_rows": ([vp] * 6 + [i32] * 7 + [vp], i32),
+    "gsdlq_attention_rows": ([vp] * 4 + [i32] * 7 + [f32, vp], i32),
 }
 IPC_HANDLE_BYTES = 64
 

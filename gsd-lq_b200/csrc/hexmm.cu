@@ -11,9 +11,9 @@
 // stages:
 //   - thread t decodes the 32 code bytes of row t (one scale group) through a 256-entry float2 table into
 //     fp32 weights, W = xy * scale as the reference's dequant defines them, splits them into fp16 hi + lo
-//     parts (about 22 significant bits together) and writes them as two A operands: K-major core matrices
-//     of 8 rows x 16 bytes, no swizzle (LBO 128 B between the two 8-column halves of a 16-column k-step,
-//     SBO 1024 B between 8-row groups);
+//     parts (about 22 significant bits together) and writes them as two A operands in the K-major
+//     128-byte-swizzle layout (a row's 64 columns are 128 bytes, 8 rows form a 1024-byte atom, 16-byte
+//     chunk j of row r sits at chunk j ^ (r % 8), so the tensor core's reads spread over all banks);
 //   - the block's activations of every token are written as the B operand in the same layout, token b as
 //     two rows: 2b = fp16 hi, 2b + 1 = fp16 lo of x_b scaled by a power of two that puts max|x_b| in
 //     [2^14, 2^15) (so both halves stay normal; about 22 significant bits together);
@@ -94,11 +94,15 @@ __device__ __forceinline__ float hexmm_xscale(unsigned amax_bits) {
 }
 
 // ---- tcgen05 helpers (cta_group::1) -----------------------------------------------------------
-// shared-memory matrix descriptor: K-major, no swizzle, LBO 128 B, SBO 1024 B, descriptor version 1
+// shared-memory matrix descriptor: K-major, 128-byte swizzle (8-row x 128-byte atoms, SBO 1024 B
+// between atoms; LBO unused for swizzled K-major), descriptor version 1.  The start address of k-step
+// kk inside a 64-column block is the atom base + 32 kk bytes.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128u >> 4) << 16) | ((uint64_t)(1024u >> 4) << 32) |
-         (1ull << 46);
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) | (1ull << 46) |
+         (2ull << 61);
 }
+// byte offset of 16-byte chunk j (columns 8j .. 8j+7) of row r in a swizzled 64-column tile
+__device__ __forceinline__ int sw128(int r, int j) { return (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4); }
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
@@ -142,7 +146,7 @@ constexpr int mm_smem() {
   // header + two A stages + two B stages (16 NB rows of 128 bytes); with 256 accumulator columns at
   // least 80 KB, so that no more than two CTAs share an SM's 512 tensor-memory columns (a third
   // would wait in tcgen05.alloc)
-  constexpr int need = MM_HDR + 2 * MM_ATILE + 2 * 16 * NB * 128;  // (at least 80 KB whenever NB > 8)
+  constexpr int need = MM_HDR + 1024 + 2 * MM_ATILE + 2 * 16 * NB * 128;  // (+1 KB: the tiles' alignment)
   return (mm_tcols<NB>() == 256 && need < 80 * 1024) ? 80 * 1024 : need;
 }
 static_assert(mm_smem<3>() * 9 > 227 * 1024 && mm_smem<5>() * 5 > 227 * 1024 && mm_smem<9>() * 3 > 227 * 1024,
@@ -169,7 +173,8 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
   float* xsc = reinterpret_cast<float*>(sm + 2080);               // [MM_MAXB] token scales
   const uint32_t sbase = smem_u32(sm);
   const uint32_t bar0 = sbase + 2048;                             // two mbarriers (8 bytes each)
-  const uint32_t a_base = sbase + MM_HDR, b_base = sbase + MM_HDR + 2 * MM_ATILE;
+  // the operand tiles start on a 1024-byte boundary of the shared window (the swizzle atoms' alignment)
+  const uint32_t a_base = (sbase + MM_HDR + 1023u) & ~1023u, b_base = a_base + 2 * MM_ATILE;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int r0 = blockIdx.x * MM_ROWS, split = blockIdx.y;
   const int NP = C / 2, G = C / 64, nkb = C / MM_KB;
@@ -210,7 +215,7 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
     // ---- A: row tid's 64 weights, chunk j = weights 8j .. 8j+7 = code bytes 4j .. 4j+3 ----
     const float s = h2f(sc);
     const uint32_t cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-    uint8_t* arow = sm + MM_HDR + st * MM_ATILE + (tid >> 3) * 1024 + (tid & 7) * 16;
+    uint8_t* atile = sm + (a_base - sbase) + st * MM_ATILE;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       uint32_t h[4], l[4];
@@ -224,8 +229,8 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
         h[q] = *reinterpret_cast<const uint32_t*>(&hh);
         l[q] = pack_h2(w0 - __low2float(hh), w1 - __high2float(hh));  // fp16 hi + lo: about 22 bits
       }
-      *reinterpret_cast<uint4*>(arow + j * 128) = make_uint4(h[0], h[1], h[2], h[3]);
-      *reinterpret_cast<uint4*>(arow + MM_AHALF + j * 128) = make_uint4(l[0], l[1], l[2], l[3]);
+      *reinterpret_cast<uint4*>(atile + sw128(tid, j)) = make_uint4(h[0], h[1], h[2], h[3]);
+      *reinterpret_cast<uint4*>(atile + MM_AHALF + sw128(tid, j)) = make_uint4(l[0], l[1], l[2], l[3]);
     }
     // the next block's codes into registers while this one is staged and multiplied
     if (rok && kb + 1 < kb1) {
@@ -234,7 +239,7 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
       sc = scp[kb + 1];
     }
     // ---- B: token b, chunk j -> rows 2b (hi) and 2b + 1 (lo) ----
-    uint8_t* bt = sm + MM_HDR + 2 * MM_ATILE + st * BTILE;
+    uint8_t* bt = sm + (b_base - sbase) + st * BTILE;
     for (int e = tid; e < BP * 8; e += MM_THREADS) {
       const int b = e >> 3, j = e & 7;
       float v[8];
@@ -256,8 +261,8 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
         lo[t] = pack_h2(v[2 * t] - __low2float(hh), v[2 * t + 1] - __high2float(hh));
       }
       const int rh = 2 * b, rl = 2 * b + 1;
-      *reinterpret_cast<uint4*>(bt + (rh >> 3) * 1024 + j * 128 + (rh & 7) * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      *reinterpret_cast<uint4*>(bt + (rl >> 3) * 1024 + j * 128 + (rl & 7) * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      *reinterpret_cast<uint4*>(bt + sw128(rh, j)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(bt + sw128(rl, j)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
     fence_proxy_async_smem();  // the tiles' generic stores, visible to the tensor core's reads
     __syncthreads();
@@ -265,9 +270,9 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
       tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < MM_KB / 16; ++kk) {
-        const uint64_t bd = umma_desc(b_base + st * BTILE + kk * 256);
-        umma_f16(tmem, umma_desc(a_base + st * MM_ATILE + kk * 256), bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-        umma_f16(tmem, umma_desc(a_base + st * MM_ATILE + MM_AHALF + kk * 256), bd, idesc, 1u);
+        const uint64_t bd = umma_desc(b_base + st * BTILE + kk * 32);
+        umma_f16(tmem, umma_desc(a_base + st * MM_ATILE + kk * 32), bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        umma_f16(tmem, umma_desc(a_base + st * MM_ATILE + MM_AHALF + kk * 32), bd, idesc, 1u);
       }
       umma_commit(bar0 + 8u * st);  // arrives when every MMA issued so far has completed
     }

@@ -474,11 +474,85 @@ class GSDLQModel:
         pt = pt / pt.sum()
         return int(np.random.choice(top, p=pt))
 
-    def prefill(self, ids, start_pos: int = 0):
-        """Token-by-token prefill as the reference does (run_gpu_native_chat.py:1128-1131); no logits."""
-        for i, t in enumerate(ids):
-            self.set_state(int(t), start_pos + i)
-            self.step(with_head=False)
+    PREFILL_CHUNK = 128  # tokens per chunk of batched prefill (the dequant-GEMM's largest batch)
+
+    def prefill(self, ids, start_pos: int = 0, batched: bool | None = None):
+        """Fill the KV cache for ``ids`` at positions start_pos.. (no logits).
+
+        Batched (default on one GPU): chunks of up to 128 tokens, every packed linear as one tensor-core
+        dequant-GEMM over the chunk, causal attention over the chunk's rows.  Token by token (as the
+        reference does, run_gpu_native_chat.py:1128-1131) with batched=False, under tensor parallelism,
+        or with GSDLQ_PREFILL=token."""
+        ids = [int(t) for t in ids]
+        if batched is None:
+            batched = self.tp is None and os.environ.get("GSDLQ_PREFILL", "batched") != "token"
+        if not batched:
+            for i, t in enumerate(ids):
+                self.set_state(t, start_pos + i)
+                self.step(with_head=False)
+            return
+        if start_pos + len(ids) > self.max_seq:
+            raise ValueError("prefill past max_seq")
+        for c in range(0, len(ids), self.PREFILL_CHUNK):
+            self._prefill_chunk(ids[c:c + self.PREFILL_CHUNK], start_pos + c)
+
+    def _prefill_bufs(self):
+        b = getattr(self, "_pf", None)
+        if b is None:
+            T, dev = self.PREFILL_CHUNK, self.device
+            f32 = dict(dtype=torch.float32, device=dev)
+            qd, kvd = self.n_heads_local * self.head_dim, self.n_kv_local * self.head_dim
+            b = {"x": torch.zeros((T, self.hidden), **f32), "xn": torch.zeros((T, self.hidden), **f32),
+                 "q": torch.zeros((T, qd), **f32), "k": torch.zeros((T, kvd), **f32), "v": torch.zeros((T, kvd), **f32),
+                 "att": torch.zeros((T, qd), **f32), "o": torch.zeros((T, self.hidden), **f32),
+                 "g": torch.zeros((T, self.ffn_local), **f32), "u": torch.zeros((T, self.ffn_local), **f32),
+                 "work": torch.zeros(ops.MATMUL_WORK_FLOATS, **f32),
+                 "ids": torch.zeros(T, dtype=torch.int32, device=dev),
+                 "xy": {r: torch.from_numpy(ops.codebook(r)).to(dev) for r in (6, 8)}}
+            self._pf = b
+        return b
+
+    def _prefill_chunk(self, ids, pos0: int):
+        lib, sh = L.load(), ops.stream_handle()
+        b = self._prefill_bufs()
+        n, H, F = len(ids), self.hidden, self.ffn_local
+        b["ids"][:n].copy_(torch.tensor(ids, dtype=torch.int32))
+
+        def mm(xin, name, yout):
+            h = self.hex[name]
+            L.check(lib.gsdlq_hex2d_matmul(xin.data_ptr(), n, ops.ptr(h.codes), ops.ptr(h.scales),
+                                           b["xy"][h.radius].data_ptr(), ops.ptr(h.U), ops.ptr(h.S), ops.ptr(h.Vt),
+                                           ops.ptr(h.row_ptr), ops.ptr(h.kink_cols), ops.ptr(h.kink_deltas),
+                                           yout.data_ptr(), b["work"].data_ptr(), h.rows, h.cols, h.k_dim,
+                                           h.n_pts, sh), "gsdlq_hex2d_matmul")
+        x, xn = b["x"], b["xn"]
+        L.check(lib.gsdlq_embed_rows(self.embed.data_ptr(), b["ids"].data_ptr(), n, self.vocab_size, H,
+                                     x.data_ptr(), sh), "gsdlq_embed_rows")
+        sm = 1.0 / math.sqrt(self.head_dim)
+        for l in range(self.n_layers):
+            p = f"blk.{l}."
+            L.check(lib.gsdlq_rmsnorm_rows(x.data_ptr(), self.norms[p + "attn_norm.weight"].data_ptr(), xn.data_ptr(),
+                                           n, H, self.rms_eps, sh), "gsdlq_rmsnorm_rows")
+            mm(xn, p + "attn_q.weight", b["q"])
+            mm(xn, p + "attn_k.weight", b["k"])
+            mm(xn, p + "attn_v.weight", b["v"])
+            L.check(lib.gsdlq_rope_kv_rows(b["q"].data_ptr(), b["k"].data_ptr(), b["v"].data_ptr(),
+                                           self.k_cache.data_ptr(), self.v_cache.data_ptr(), self.rope_cs.data_ptr(),
+                                           l, pos0, n, self.n_heads_local, self.n_kv_local, self.head_dim,
+                                           self.max_seq, sh), "gsdlq_rope_kv_rows")
+            L.check(lib.gsdlq_attention_rows(b["q"].data_ptr(), self.k_cache.data_ptr(), self.v_cache.data_ptr(),
+                                             b["att"].data_ptr(), l, pos0, n, self.n_heads_local, self.n_kv_local,
+                                             self.head_dim, self.max_seq, sm, sh), "gsdlq_attention_rows")
+            mm(b["att"], p + "attn_output.weight", b["o"])
+            L.check(lib.gsdlq_vec_add(x.data_ptr(), x.data_ptr(), b["o"].data_ptr(), n * H, sh), "gsdlq_vec_add")
+            L.check(lib.gsdlq_rmsnorm_rows(x.data_ptr(), self.norms[p + "ffn_norm.weight"].data_ptr(), xn.data_ptr(),
+                                           n, H, self.rms_eps, sh), "gsdlq_rmsnorm_rows")
+            mm(xn, p + "ffn_gate.weight", b["g"])
+            mm(xn, p + "ffn_up.weight", b["u"])
+            L.check(lib.gsdlq_swiglu(b["g"].data_ptr(), b["u"].data_ptr(), b["g"].data_ptr(), n * F, sh),
+                    "gsdlq_swiglu")
+            mm(b["g"], p + "ffn_down.weight", b["o"])
+            L.check(lib.gsdlq_vec_add(x.data_ptr(), x.data_ptr(), b["o"].data_ptr(), n * H, sh), "gsdlq_vec_add")
 
     def generate(self, prompt_ids, max_new_tokens: int) -> list[int]:
         """Greedy generation with the loop on the device: one graph replay per token, one D2H at the end.

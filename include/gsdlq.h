@@ -346,6 +346,26 @@ int gsdlq_hex2d_matmul(const float *x, int batch, const uint8_t *codes, const ui
                        const uint32_t *kink_row_ptr, const uint16_t *kink_cols, const float *kink_deltas,
                        float *y, float *work, int rows, int cols, int k_dim, int n_pts, gsdlq_stream_t stream);
 
+/* ---- Chunked prefill: the per-token operations over the n rows of a chunk ---------------------
+ * No counterpart in the reference, whose prefill runs forward_token once per prompt token
+ * (run_gpu_native_chat.py:1128-1131): each of these applies the reference's per-token operation to
+ * every row of a chunk of n tokens at positions pos0 .. pos0 + n - 1 ([n][dim] fp32 rows, device).
+ *   embed_rows:     out[t] = f32(embed[ids[t]]) (ids: device int32)
+ *   rmsnorm_rows:   gsd_cpu_rmsnorm of every row (gsd_lq_cpu_engine.c:67-82)
+ *   rope_kv_rows:   gsd_cpu_rope_and_store_kv of every row, interleaved pairs, angles from the
+ *                   gsdlq_rope_table table rope_cs [max_seq][head_dim/2] (gsd_lq_cpu_engine.c:186-262)
+ *   attention_rows: gsd_cpu_gqa_attention of row t at position pos0 + t: causal over the cache
+ *                   (gsd_lq_cpu_engine.c:265-330); head_dim <= 128, n_heads / n_kv_heads <= 8 */
+int gsdlq_embed_rows(const uint16_t *embed, const int *ids, int n, int vocab, int dim, float *out,
+                     gsdlq_stream_t stream);
+int gsdlq_rmsnorm_rows(const float *x, const float *w, float *out, int n, int dim, float eps, gsdlq_stream_t stream);
+int gsdlq_rope_kv_rows(float *q, const float *k, const float *v, uint16_t *k_cache, uint16_t *v_cache,
+                       const float *rope_cs, int layer, int pos0, int n, int n_heads, int n_kv_heads, int head_dim,
+                       int max_seq, gsdlq_stream_t stream);
+int gsdlq_attention_rows(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, float *out, int layer,
+                         int pos0, int n, int n_heads, int n_kv_heads, int head_dim, int max_seq, float sm_scale,
+                         gsdlq_stream_t stream);
+
 /* ---- The whole decode step in one launch ----------------------------------------------------
  * Engine-level entry point with no single reference counterpart: the reference's
  * Model.forward_token (run_gpu_native_chat.py:921-984) walks the layers on the host, one kernel

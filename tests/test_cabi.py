@@ -18,6 +18,18 @@ def test_library_exports_header_symbols():
     assert set(names) == set(L.SIGNATURES), set(names) ^ set(L.SIGNATURES)
 
 
+def test_bindings_match_header_arity():
+    """Every ctypes binding takes as many arguments as its declaration in include/gsdlq.h."""
+    import re
+    txt = re.sub(r"/\*.*?\*/", "", open(L.HEADER).read(), flags=re.S)
+    for name, (args, _) in L.SIGNATURES.items():
+        m = re.search(r"\b" + name + r"\s*\(([^)]*)\)\s*;", txt)
+        assert m, name
+        params = m.group(1).strip()
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert n == len(args), (name, n, len(args))
+
+
 def test_host_functions_without_gpu(oracle_mod):
     lib = L.load()
     assert lib.gsdlq_version().startswith(b"0.")
