@@ -74,7 +74,8 @@ SIGNATURES = {
     "gsdlq_lowrank_proj": ([vp, vp, vp, vp, i32, i32, vp], i32),
     "gsdlq_hex2d_matvec": ([vp] * 10 + [i32] * 4 + [vp], i32),
     "gsdlq_hex2d_matvec_noalloc": ([vp] * 10 + [i32] * 4 + [vp], i32),
-    "gsdlq_hex2d_matmul": ([vp, i32] + [vp] * 11 + [i32] * 4 + [vp], i32),
+    "gsdlq_hex2d_matmul": ([vp, i32] + [vp] * 11 + [ctypes.c_size_t] + [i32] * 4 + [vp], i32),
+    "gsdlq_hex2d_matmul_work_size": ([i32, i32, szp], i32),
     "gsdlq_rope_and_store_kv": ([vp] * 5 + [i32] * 6 + [f32, i32, vp], i32),
     "gsdlq_gqa_attention": ([vp] * 4 + [i32] * 6 + [f32, vp], i32),
     "gsdlq_codebook": ([i32, vp, i32], i32),

@@ -34,12 +34,11 @@ namespace gsdlq {
 
 constexpr int MM_ROWS = 128;      // weight rows per CTA (tensor-memory lanes)
 constexpr int MM_KB = 64;         // columns per k-block: one scale group
-constexpr int MM_THREADS = 128;   // thread t decodes row t and reads lane t of the accumulator
+constexpr int MM_THREADS = 256;   // two threads per weight row (its two 32-column halves of a block)
 constexpr int MM_MAXB = GSDLQ_MATMUL_MAX_BATCH;  // tokens per call (N = 2 * 128 = 256, the largest MMA N)
-static_assert(GSDLQ_MATMUL_WORK_FLOATS >= 17 * MM_MAXB, "work: maxima and low-rank projections of every token");
 constexpr int MM_AHALF = MM_ROWS * MM_KB * 2;  // bytes of one fp16 A tile (16 KB): the weights' hi or lo parts
 constexpr int MM_ATILE = 2 * MM_AHALF;         // one stage's A tiles (hi, then lo)
-constexpr int MM_HDR = 4096;                   // table, barriers, tensor-memory slot, token scales
+constexpr int MM_HDR = 12288;                  // table, barriers, tensor-memory slot, token scales, projections
 
 // Per token b and chunk of MM_PREP columns: the chunk's max|x_b| into amax[b] (as ordered bits) and its
 // part of S[j] * (Vt[j] . x_b) into tmp[16 b + j] (gsd_cpu_lowrank_proj; fp32 atomics, so the summation
@@ -141,21 +140,79 @@ template <int NB>
 constexpr int mm_tcols() {  // tensor-memory columns of the accumulator: a power of two >= 32
   return 16 * NB <= 32 ? 32 : 16 * NB <= 64 ? 64 : 16 * NB <= 128 ? 128 : 256;
 }
+constexpr int MM_CSTAGES = 4;                  // k-blocks of codes in flight per CTA (cp.async ring)
+constexpr int MM_CSTAGE = MM_ROWS * 32;        // code bytes of one k-block of a tile (4 KB)
+template <int NB>
+constexpr int mm_btile() {  // one k-block of the B operand: 16 NB rows (token hi / lo) x 128 bytes
+  return 16 * NB * 128;
+}
 template <int NB>
 constexpr int mm_smem() {
-  // header + two A stages + two B stages (16 NB rows of 128 bytes); with 256 accumulator columns at
-  // least 80 KB, so that no more than two CTAs share an SM's 512 tensor-memory columns (a third
-  // would wait in tcgen05.alloc)
-  constexpr int need = MM_HDR + 1024 + 2 * MM_ATILE + 2 * 16 * NB * 128;  // (+1 KB: the tiles' alignment)
+  // header + code ring + alignment slack + two A stages + two B stages; with 256 accumulator columns at
+  // least 80 KB, so that no more than two CTAs share an SM's 512 tensor-memory columns (a third would
+  // wait in tcgen05.alloc)
+  constexpr int need = MM_HDR + MM_CSTAGES * MM_CSTAGE + 1024 + 2 * MM_ATILE + 2 * mm_btile<NB>();
   return (mm_tcols<NB>() == 256 && need < 80 * 1024) ? 80 * 1024 : need;
 }
-static_assert(mm_smem<3>() * 9 > 227 * 1024 && mm_smem<5>() * 5 > 227 * 1024 && mm_smem<9>() * 3 > 227 * 1024,
+template <int NB>
+constexpr bool mm_tmem_fits() {  // the CTAs that shared memory lets an SM hold fit its 512 tensor-memory columns
+  return (227 * 1024 / mm_smem<NB>()) * mm_tcols<NB>() <= 512;
+}
+static_assert(mm_tmem_fits<1>() && mm_tmem_fits<2>() && mm_tmem_fits<3>() && mm_tmem_fits<4>() && mm_tmem_fits<5>() &&
+                  mm_tmem_fits<6>() && mm_tmem_fits<7>() && mm_tmem_fits<8>() && mm_tmem_fits<9>() &&
+                  mm_tmem_fits<12>() && mm_tmem_fits<16>(),
               "at most 512 tensor-memory columns of resident CTAs per SM");
 
-// NB: groups of 8 tokens (tokens padded to 8 NB with zero activations); N = 16 NB accumulator columns.
+// The B operand of every k-block, made once per call: token b's row of the block as fp16 hi (row 2b) and
+// lo (row 2b + 1) of x_b scaled by its power of two, in the swizzled layout of a 64-column tile, one
+// contiguous block of mm_btile<NB>() bytes per k-block (tokens past the batch are zero).
 template <int NB>
-__global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restrict__ x, int B,
-                                                           const uint8_t* __restrict__ codes,
+__global__ void __launch_bounds__(256) hexmm_xconv(const float* __restrict__ x, int B, int C,
+                                                   const unsigned* __restrict__ amax_bits, uint8_t* __restrict__ xs) {
+  constexpr int BP = 8 * NB;
+  const int kb = blockIdx.x;
+  uint8_t* blk = xs + (size_t)kb * mm_btile<NB>();
+  for (int e = threadIdx.x; e < BP * 8; e += 256) {
+    const int b = e >> 3, j = e & 7;
+    float v[8];
+    if (b < B) {
+      const float f = hexmm_xscale(amax_bits[b]);
+      const float4* xp = reinterpret_cast<const float4*>(x + (size_t)b * C + kb * MM_KB + 8 * j);
+      const float4 u0 = xp[0], u1 = xp[1];
+      v[0] = u0.x * f, v[1] = u0.y * f, v[2] = u0.z * f, v[3] = u0.w * f;
+      v[4] = u1.x * f, v[5] = u1.y * f, v[6] = u1.z * f, v[7] = u1.w * f;
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[t] = 0.f;
+    }
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const __half2 hh = __floats2half2_rn(v[2 * t], v[2 * t + 1]);
+      hi[t] = *reinterpret_cast<const uint32_t*>(&hh);
+      lo[t] = pack_h2(v[2 * t] - __low2float(hh), v[2 * t + 1] - __high2float(hh));
+    }
+    *reinterpret_cast<uint4*>(blk + sw128(2 * b, j)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(blk + sw128(2 * b + 1, j)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// NB: groups of 8 tokens (tokens padded to 8 NB with zero activations); N = 16 NB accumulator columns.
+// Thread t decodes half t / 128 of weight row t % 128 (32 columns of each 64-column block); warps 0-3
+// read the accumulator lanes of rows 0-127 at the end.
+template <int NB>
+__global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const uint8_t* __restrict__ xs, const float* __restrict__ x,
+                                                           int B, const uint8_t* __restrict__ codes,
                                                            const uint16_t* __restrict__ scales,
                                                            const float* __restrict__ xy, int n_pts,
                                                            const uint16_t* __restrict__ U, int k,
@@ -166,26 +223,45 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
                                                            const float* __restrict__ tmp) {
   constexpr int N = 16 * NB, BP = 8 * NB;
   constexpr uint32_t TCOLS = (uint32_t)mm_tcols<NB>();
-  constexpr int BTILE = N * 128;
+  constexpr int BTILE = mm_btile<NB>();
   extern __shared__ __align__(1024) uint8_t sm[];
   float2* tab = reinterpret_cast<float2*>(sm);                    // [0, 2048)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + 2064);       // tensor-memory address
-  float* xsc = reinterpret_cast<float*>(sm + 2080);               // [MM_MAXB] token scales
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + 2080);       // tensor-memory address
+  float* xsc = reinterpret_cast<float*>(sm + 2096);               // [MM_MAXB] token scales
+  float* s_tmp = reinterpret_cast<float*>(sm + 2608);             // [BP][16] low-rank projections
+  uint8_t* ring = sm + MM_HDR;                                    // code ring: [stage][row][32 bytes]
   const uint32_t sbase = smem_u32(sm);
-  const uint32_t bar0 = sbase + 2048;                             // two mbarriers (8 bytes each)
+  const uint32_t mbar = sbase + 2048, bbar = sbase + 2064;        // MMA-done and B-landed barriers, 2 each
   // the operand tiles start on a 1024-byte boundary of the shared window (the swizzle atoms' alignment)
-  const uint32_t a_base = (sbase + MM_HDR + 1023u) & ~1023u, b_base = a_base + 2 * MM_ATILE;
+  const uint32_t a_base = (sbase + MM_HDR + MM_CSTAGES * MM_CSTAGE + 1023u) & ~1023u;
+  const uint32_t b_base = a_base + 2 * MM_ATILE;
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int lr = tid & (MM_ROWS - 1), half = tid >> 7;  // weight row in the tile, column half of a block
   const int r0 = blockIdx.x * MM_ROWS, split = blockIdx.y;
   const int NP = C / 2, G = C / 64, nkb = C / MM_KB;
   const int kb0 = (int)((long long)nkb * split / nsplit), kb1 = (int)((long long)nkb * (split + 1) / nsplit);
   const int nk = kb1 - kb0;
+  const int row = r0 + lr;
+  const bool rok = row < R;
+  const uint8_t* cp = codes + (size_t)(rok ? row : 0) * NP + half * 16;
+  const uint16_t* scp = scales + (size_t)(rok ? row : 0) * G;
+  // this thread's 16 code bytes of k-block kb0 + i into ring stage i % MM_CSTAGES (one group per block,
+  // empty past the run, so that the group count stays uniform)
+  auto fetch = [&](int i) {
+    if (i < nk && rok) cp_async_16(ring + (i % MM_CSTAGES) * MM_CSTAGE + lr * 32 + half * 16, cp + (kb0 + i) * 32);
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int i = 0; i < MM_CSTAGES - 1; ++i) fetch(i);
 
   for (int i = tid; i < 256; i += MM_THREADS) tab[i] = i < n_pts ? make_float2(xy[2 * i], xy[2 * i + 1]) : make_float2(0.f, 0.f);
   for (int i = tid; i < BP; i += MM_THREADS) xsc[i] = i < B ? hexmm_xscale(amax_bits[i]) : 0.f;
+  for (int i = tid; i < BP * 16; i += MM_THREADS) s_tmp[i] = (i >> 4) < B ? tmp[i] : 0.f;
   if (tid == 0) {
-    mbar_init(bar0, 1u);
-    mbar_init(bar0 + 8u, 1u);
+    mbar_init(mbar, 1u);
+    mbar_init(mbar + 8u, 1u);
+    mbar_init(bbar, 1u);
+    mbar_init(bbar + 8u, 1u);
     mbar_fence_init();
   }
   if (warp == 0) tmem_alloc(smem_u32(tslot), TCOLS);
@@ -193,78 +269,99 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot);
+#ifdef GSDLQ_TRACE
+  // diagnostic builds: CTA blockIdx.x (< 160, run 0) stamps its set-up and its first six k-blocks
+  const bool trc = blockIdx.y == 0 && tid == 0;
+  if (trc) GSDLQ_TR_SET(0u, 0, tr_now());
+#endif
 
-  const int row = r0 + tid;
-  const bool rok = row < R;
-  const uint8_t* cp = codes + (size_t)(rok ? row : 0) * NP;
-  const uint16_t* scp = scales + (size_t)(rok ? row : 0) * G;
-  uint4 c0 = make_uint4(0u, 0u, 0u, 0u), c1 = make_uint4(0u, 0u, 0u, 0u);
-  uint16_t sc = 0;
-  if (rok && nk > 0) {
-    c0 = *reinterpret_cast<const uint4*>(cp + kb0 * 32);
-    c1 = *reinterpret_cast<const uint4*>(cp + kb0 * 32 + 16);
-    sc = scp[kb0];
+  // The row's kinks (CSR, ascending columns) are added to their decoded weights in the A tiles, so the
+  // tensor cores apply them with the lattice part.  e walks the row's list from this run's first column
+  // (found in batches of eight independent loads); (kc, kd) is the kink at e and (kc2, kd2) the one after
+  // it, loaded ahead so that the next block's test does not wait on a load.
+  uint32_t e = rok ? row_ptr[row] : 0u;
+  const uint32_t e_end = rok ? row_ptr[row + 1] : 0u;
+  while (e < e_end) {
+    int c8[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) c8[q] = e + q < e_end ? (int)kcols[e + q] : 0x7fffffff;
+    int below = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) below += c8[q] < kb0 * MM_KB;
+    e += below;
+    if (below < 8) break;
   }
+  int kc = e < e_end ? (int)kcols[e] : 0x7fffffff;
+  float kd = e < e_end ? kdel[e] : 0.f;
+  int kc2 = e + 1 < e_end ? (int)kcols[e + 1] : 0x7fffffff;
+  float kd2 = e + 1 < e_end ? kdel[e + 1] : 0.f;
+
+  uint16_t sc = (rok && nk > 0) ? scp[kb0] : (uint16_t)0;
   // instruction descriptor: D fp32, A and B fp16, both K-major, N, M = 128
   const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(MM_ROWS >> 4) << 24);
   bool bad = false;
-  for (int kb = kb0; kb < kb1; ++kb) {
-    const int i = kb - kb0, st = i & 1;
-    // the MMAs of two blocks ago read this stage: wait for their commit (bounded)
-    if (i >= 2) mbar_wait_bounded(bar0 + 8u * st, (uint32_t)(((i >> 1) - 1) & 1));
-    // ---- A: row tid's 64 weights, chunk j = weights 8j .. 8j+7 = code bytes 4j .. 4j+3 ----
+  for (int i = 0; i < nk; ++i) {
+    const int st = i & 1, kb = kb0 + i;
+    // the MMAs of two blocks ago read this stage's A and B tiles: wait for their commit (bounded)
+    if (i >= 2) mbar_wait_bounded(mbar + 8u * st, (uint32_t)(((i >> 1) - 1) & 1));
+#ifdef GSDLQ_TRACE
+    if (trc && i < 6) GSDLQ_TR_SET(0u, 1 + 4 * i, tr_now());
+#endif
+    if (tid == 0) {  // this block's B tile: one bulk copy from the converted activations
+      mbar_arrive_expect_tx(bbar + 8u * st, (uint32_t)BTILE);
+      bulk_g2s(b_base + st * BTILE, xs + (size_t)kb * BTILE, (uint32_t)BTILE, bbar + 8u * st);
+    }
+    fetch(i + MM_CSTAGES - 1);          // codes of the block MM_CSTAGES - 1 ahead
+    cp_async_wait<MM_CSTAGES - 1>();    // this thread's codes of block i have landed
+    // ---- A: 32 weights of row lr, chunks j = 4 half + jj (weights 8j .. 8j+7 = code bytes 4j .. 4j+3) ----
     const float s = h2f(sc);
-    const uint32_t cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const uint4 cw = *reinterpret_cast<const uint4*>(ring + (i % MM_CSTAGES) * MM_CSTAGE + lr * 32 + half * 16);
+    if (rok && i + 1 < nk) sc = scp[kb + 1];
+    const uint32_t cv[4] = {cw.x, cw.y, cw.z, cw.w};
     uint8_t* atile = sm + (a_base - sbase) + st * MM_ATILE;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int jj = 0; jj < 4; ++jj) {
       uint32_t h[4], l[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const int code = (int)((cv[j] >> (8 * q)) & 0xffu);
-        bad |= rok && code >= n_pts;
+        const int code = rok ? (int)((cv[jj] >> (8 * q)) & 0xffu) : 0;
+        bad |= code >= n_pts;
         const float2 p = tab[code];
         const float w0 = p.x * s, w1 = p.y * s;  // a3 dequant: one fp32 multiply per weight
         const __half2 hh = __floats2half2_rn(w0, w1);
         h[q] = *reinterpret_cast<const uint32_t*>(&hh);
         l[q] = pack_h2(w0 - __low2float(hh), w1 - __high2float(hh));  // fp16 hi + lo: about 22 bits
       }
-      *reinterpret_cast<uint4*>(atile + sw128(tid, j)) = make_uint4(h[0], h[1], h[2], h[3]);
-      *reinterpret_cast<uint4*>(atile + MM_AHALF + sw128(tid, j)) = make_uint4(l[0], l[1], l[2], l[3]);
+      *reinterpret_cast<uint4*>(atile + sw128(lr, 4 * half + jj)) = make_uint4(h[0], h[1], h[2], h[3]);
+      *reinterpret_cast<uint4*>(atile + MM_AHALF + sw128(lr, 4 * half + jj)) = make_uint4(l[0], l[1], l[2], l[3]);
     }
-    // the next block's codes into registers while this one is staged and multiplied
-    if (rok && kb + 1 < kb1) {
-      c0 = *reinterpret_cast<const uint4*>(cp + (kb + 1) * 32);
-      c1 = *reinterpret_cast<const uint4*>(cp + (kb + 1) * 32 + 16);
-      sc = scp[kb + 1];
-    }
-    // ---- B: token b, chunk j -> rows 2b (hi) and 2b + 1 (lo) ----
-    uint8_t* bt = sm + (b_base - sbase) + st * BTILE;
-    for (int e = tid; e < BP * 8; e += MM_THREADS) {
-      const int b = e >> 3, j = e & 7;
-      float v[8];
-      if (b < B) {
-        const float4* xp = reinterpret_cast<const float4*>(x + (size_t)b * C + kb * MM_KB + 8 * j);
-        const float4 u0 = xp[0], u1 = xp[1];
-        const float f = xsc[b];
-        v[0] = u0.x * f, v[1] = u0.y * f, v[2] = u0.z * f, v[3] = u0.w * f;
-        v[4] = u1.x * f, v[5] = u1.y * f, v[6] = u1.z * f, v[7] = u1.w * f;
-      } else {
-#pragma unroll
-        for (int t = 0; t < 8; ++t) v[t] = 0.f;
+    // the block's kinks in this thread's half: the weight's hi + lo halves plus the delta, split again (a
+    // column repeated in the list gets every delta); kinks of the other half are the other thread's
+    while (kc < (kb + 1) * MM_KB) {
+      const int lc = kc - kb * MM_KB;  // 0 .. 63
+      if ((lc >> 5) == half) {
+        const int off = sw128(lr, lc >> 3) + 2 * (lc & 7);
+        __half* ph = reinterpret_cast<__half*>(atile + off);
+        __half* pl = reinterpret_cast<__half*>(atile + MM_AHALF + off);
+        const float w = (__half2float(*ph) + __half2float(*pl)) + kd;
+        const __half hw = __float2half_rn(w);
+        *ph = hw;
+        *pl = __float2half_rn(w - __half2float(hw));
       }
-      uint32_t hi[4], lo[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const __half2 hh = __floats2half2_rn(v[2 * t], v[2 * t + 1]);
-        hi[t] = *reinterpret_cast<const uint32_t*>(&hh);
-        lo[t] = pack_h2(v[2 * t] - __low2float(hh), v[2 * t + 1] - __high2float(hh));
-      }
-      const int rh = 2 * b, rl = 2 * b + 1;
-      *reinterpret_cast<uint4*>(bt + sw128(rh, j)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      *reinterpret_cast<uint4*>(bt + sw128(rl, j)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      ++e;
+      kc = kc2;
+      kd = kd2;
+      kc2 = e + 1 < e_end ? (int)kcols[e + 1] : 0x7fffffff;
+      kd2 = e + 1 < e_end ? kdel[e + 1] : 0.f;
     }
-    fence_proxy_async_smem();  // the tiles' generic stores, visible to the tensor core's reads
+#ifdef GSDLQ_TRACE
+    if (trc && i < 6) GSDLQ_TR_SET(0u, 2 + 4 * i, tr_now());
+#endif
+    fence_proxy_async_smem();  // the A tiles' generic stores, visible to the tensor core's reads
+    mbar_wait_bounded(bbar + 8u * st, (uint32_t)((i >> 1) & 1));  // the B tile has landed
+#ifdef GSDLQ_TRACE
+    if (trc && i < 6) GSDLQ_TR_SET(0u, 3 + 4 * i, tr_now());
+#endif
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
@@ -274,13 +371,26 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
         umma_f16(tmem, umma_desc(a_base + st * MM_ATILE + kk * 32), bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
         umma_f16(tmem, umma_desc(a_base + st * MM_ATILE + MM_AHALF + kk * 32), bd, idesc, 1u);
       }
-      umma_commit(bar0 + 8u * st);  // arrives when every MMA issued so far has completed
+      umma_commit(mbar + 8u * st);  // arrives when every MMA issued so far has completed
+#ifdef GSDLQ_TRACE
+      if (trc && i < 6) GSDLQ_TR_SET(0u, 4 + 4 * i, tr_now());
+#endif
     }
   }
+  cp_async_wait<0>();
   if (bad) raise_flag(GSDLQ_FLAG_BAD_CODE);
-  // ---- the run's partial sums: lane tid = row tid; columns 2b, 2b + 1 = token b's hi and lo parts ----
-  if (nk > 0) {
-    mbar_wait_bounded(bar0 + 8u * ((nk - 1) & 1), (uint32_t)(((nk - 1) >> 1) & 1));
+  // a kink past the last column is never applied: the run that ends the row reports it
+  if (kb1 == nkb && half == 0 && e < e_end) raise_flag(GSDLQ_FLAG_BAD_KINK);
+#ifdef GSDLQ_TRACE
+  if (trc) GSDLQ_TR_SET(0u, 25, tr_now());
+#endif
+  // ---- the run's partial sums: warps 0-3, lane = row; columns 2b, 2b + 1 = token b's hi and lo parts; the
+  // low-rank term U[row] . tmp[b] is added once per (row, token), by the run whose index is b mod nsplit ----
+  if (nk > 0 && warp < 4) {
+    float u[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) u[j] = (rok && j < k) ? h2f(U[(size_t)row * k + j]) : 0.f;
+    mbar_wait_bounded(mbar + 8u * ((nk - 1) & 1), (uint32_t)(((nk - 1) >> 1) & 1));
     tc_fence_after();
 #pragma unroll 1
     for (int cb = 0; cb < N / 16; ++cb) {
@@ -289,27 +399,26 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         const int b = cb * 8 + t;
-        if (rok && b < B)
-          atomicAdd(y + (size_t)b * R + row, (__uint_as_float(v[2 * t]) + __uint_as_float(v[2 * t + 1])) / xsc[b]);
+        if (rok && b < B) {
+          float val = (__uint_as_float(v[2 * t]) + __uint_as_float(v[2 * t + 1])) / xsc[b];
+          if (b % nsplit == split) {
+            float lrv = 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) lrv = fmaf(u[j], s_tmp[b * 16 + j], lrv);
+            val += lrv;
+          }
+          atomicAdd(y + (size_t)b * R + row, val);
+        }
       }
     }
   }
-  // ---- kinks and the low-rank term, once per (row, token): tokens b = split (mod nsplit) ----
-  bool badk = false;
-  if (rok) {
-    for (int b = split; b < B; b += nsplit) {
-      float v = 0.f;
-      for (int j = 0; j < k; ++j) v = fmaf(h2f(U[(size_t)row * k + j]), tmp[(size_t)b * 16 + j], v);
-      const float* xb = x + (size_t)b * C;
-      for (uint32_t e = row_ptr[row]; e < row_ptr[row + 1]; ++e) {
-        const int col = kcols[e];
-        if (col < C) v = fmaf(kdel[e], xb[col], v);
-        else badk = true;
-      }
-      atomicAdd(y + (size_t)b * R + row, v);
-    }
+#ifdef GSDLQ_TRACE
+  if (trc) GSDLQ_TR_SET(0u, 26, tr_now());
+  if (trc) {
+    GSDLQ_TR_SET(0u, 27, tr_now());
+    GSDLQ_TR_SET(0u, 28, (unsigned long long)nk);
   }
-  if (badk) raise_flag(GSDLQ_FLAG_BAD_KINK);
+#endif
   // ---- release the tensor memory (every warp's loads are complete) ----
   tc_fence_before();
   __syncthreads();
@@ -319,11 +428,19 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const float* __restri
   }
 }
 
+// The work buffer: per-token maxima ([0, 512)), per-token low-rank projections ([512, 8704)), and from
+// MM_XS_OFF the converted activations, one B tile per k-block.
+constexpr size_t MM_XS_OFF = 16384;
+inline size_t mm_work_bytes(int batch, int cols) {
+  const int nb = (batch + 7) / 8;
+  return MM_XS_OFF + (size_t)(cols / MM_KB) * (size_t)(16 * nb * 128);
+}
+
 template <int NB>
-static cudaError_t hexmm_launch_nb(int tiles, int nkb, cudaStream_t s, const float* x, int B, const uint8_t* codes,
-                                   const uint16_t* scales, const float* xy, int n_pts, const uint16_t* U, int k,
-                                   const uint32_t* rp, const uint16_t* kc, const float* kd, float* y, int R, int C,
-                                   const unsigned* amax, const float* tmp) {
+static cudaError_t hexmm_launch_nb(int tiles, int nkb, cudaStream_t s, uint8_t* xs, const float* x, int B,
+                                   const uint8_t* codes, const uint16_t* scales, const float* xy, int n_pts,
+                                   const uint16_t* U, int k, const uint32_t* rp, const uint16_t* kc, const float* kd,
+                                   float* y, int R, int C, const unsigned* amax, const float* tmp) {
   constexpr int smem = mm_smem<NB>();
   static bool configured[64] = {};
   int dev = 0;
@@ -333,12 +450,15 @@ static cudaError_t hexmm_launch_nb(int tiles, int nkb, cudaStream_t s, const flo
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
+  hexmm_xconv<NB><<<nkb, 256, 0, s>>>(x, B, C, amax, xs);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
   // k-runs per row tile: the CTAs that fit an SM at once (shared memory) on every SM, at least one
   // k-block each
   const int per_sm = std::max(1, std::min(8, (227 * 1024) / smem));
   const int nsplit = std::max(1, std::min(nkb, (per_sm * num_sms() + tiles - 1) / tiles));
-  hexmm_kernel<NB><<<dim3(tiles, nsplit), MM_THREADS, smem, s>>>(x, B, codes, scales, xy, n_pts, U, k, rp, kc, kd, y, R,
-                                                                 C, nsplit, amax, tmp);
+  hexmm_kernel<NB><<<dim3(tiles, nsplit), MM_THREADS, smem, s>>>(xs, x, B, codes, scales, xy, n_pts, U, k, rp, kc, kd,
+                                                                 y, R, C, nsplit, amax, tmp);
   return cudaGetLastError();
 }
 
@@ -349,10 +469,17 @@ int record_cuda_error(cudaError_t e);
 
 using namespace gsdlq;
 
+extern "C" int gsdlq_hex2d_matmul_work_size(int batch, int cols, size_t* bytes) {
+  if (!bytes || batch < 1 || batch > MM_MAXB || cols <= 0 || cols % 64 != 0 || cols > 65535) return GSDLQ_ERR_INVALID;
+  *bytes = mm_work_bytes(batch, cols);
+  return GSDLQ_OK;
+}
+
 extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* codes, const uint16_t* scales,
                                   const float* xy_table, const uint16_t* U, const float* S, const uint16_t* Vt,
                                   const uint32_t* kink_row_ptr, const uint16_t* kink_cols, const float* kink_deltas,
-                                  float* y, float* work, int rows, int cols, int k_dim, int n_pts, gsdlq_stream_t stream) {
+                                  float* y, void* work, size_t work_bytes, int rows, int cols, int k_dim, int n_pts,
+                                  gsdlq_stream_t stream) {
   if (!x || !codes || !scales || !xy_table || !kink_row_ptr || !y || !work) return GSDLQ_ERR_INVALID;
   if (batch < 1 || batch > MM_MAXB || rows <= 0 || cols <= 0 || cols % 64 != 0 || cols > 65535) return GSDLQ_ERR_INVALID;
   if (k_dim < 0 || k_dim > 16 || (k_dim > 0 && (!U || !S || !Vt))) return GSDLQ_ERR_INVALID;
@@ -361,10 +488,12 @@ extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* code
   if ((reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(U) | reinterpret_cast<uintptr_t>(Vt)) & 1u)
     return GSDLQ_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(x) & 15u) return GSDLQ_ERR_INVALID;  // 16-byte activation loads
-  if ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(work)) & 3u) return GSDLQ_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(y) & 3u) || (reinterpret_cast<uintptr_t>(work) & 1023u)) return GSDLQ_ERR_INVALID;
+  if (work_bytes < mm_work_bytes(batch, cols)) return GSDLQ_ERR_INVALID;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   unsigned* amax = reinterpret_cast<unsigned*>(work);  // per-token max|x| (bits)
-  float* tmp = work + MM_MAXB;
+  float* tmp = reinterpret_cast<float*>(work) + MM_MAXB;
+  uint8_t* xs = static_cast<uint8_t*>(work) + MM_XS_OFF;  // converted activations
   cudaError_t e = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)batch * rows, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(work, 0, sizeof(float) * 17 * MM_MAXB, s);
   if (e != cudaSuccess) return record_cuda_error(e);
@@ -375,8 +504,8 @@ extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* code
   const float* kd = kink_deltas;
 #define GSDLQ_MM_CASE(nb)                                                                                               \
   case nb:                                                                                                              \
-    e = hexmm_launch_nb<nb>(tiles, nkb, s, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr, kink_cols, \
-                            kd, y, rows, cols, amax, tmp);                                                              \
+    e = hexmm_launch_nb<nb>(tiles, nkb, s, xs, x, batch, codes, scales, xy_table, n_pts, U, k_dim, kink_row_ptr,     \
+                            kink_cols, kd, y, rows, cols, amax, tmp);                                                   \
     break;
   switch ((batch + 7) / 8) {
     GSDLQ_MM_CASE(1) GSDLQ_MM_CASE(2) GSDLQ_MM_CASE(3) GSDLQ_MM_CASE(4) GSDLQ_MM_CASE(5) GSDLQ_MM_CASE(6)

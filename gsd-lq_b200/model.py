@@ -506,7 +506,7 @@ class GSDLQModel:
                  "q": torch.zeros((T, qd), **f32), "k": torch.zeros((T, kvd), **f32), "v": torch.zeros((T, kvd), **f32),
                  "att": torch.zeros((T, qd), **f32), "o": torch.zeros((T, self.hidden), **f32),
                  "g": torch.zeros((T, self.ffn_local), **f32), "u": torch.zeros((T, self.ffn_local), **f32),
-                 "work": torch.zeros(ops.MATMUL_WORK_FLOATS, **f32),
+                 "work": ops.matmul_work(T, max(h.cols for h in self.hex.values()), dev),
                  "ids": torch.zeros(T, dtype=torch.int32, device=dev),
                  "xy": {r: torch.from_numpy(ops.codebook(r)).to(dev) for r in (6, 8)}}
             self._pf = b
@@ -519,12 +519,7 @@ class GSDLQModel:
         b["ids"][:n].copy_(torch.tensor(ids, dtype=torch.int32))
 
         def mm(xin, name, yout):
-            h = self.hex[name]
-            L.check(lib.gsdlq_hex2d_matmul(xin.data_ptr(), n, ops.ptr(h.codes), ops.ptr(h.scales),
-                                           b["xy"][h.radius].data_ptr(), ops.ptr(h.U), ops.ptr(h.S), ops.ptr(h.Vt),
-                                           ops.ptr(h.row_ptr), ops.ptr(h.kink_cols), ops.ptr(h.kink_deltas),
-                                           yout.data_ptr(), b["work"].data_ptr(), h.rows, h.cols, h.k_dim,
-                                           h.n_pts, sh), "gsdlq_hex2d_matmul")
+            ops.hex2d_matmul(xin[:n], self.hex[name], b["xy"][self.hex[name].radius], yout, b["work"])
         x, xn = b["x"], b["xn"]
         L.check(lib.gsdlq_embed_rows(self.embed.data_ptr(), b["ids"].data_ptr(), n, self.vocab_size, H,
                                      x.data_ptr(), sh), "gsdlq_embed_rows")

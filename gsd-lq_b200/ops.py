@@ -149,16 +149,33 @@ def hex2d_matvec(x, h: DeviceHex, xy_table, tmp_k, y):
                                       h.k_dim, h.n_pts, stream_handle()), "hex2d_matvec")
 
 
-MATMUL_MAX_BATCH = 128         # GSDLQ_MATMUL_MAX_BATCH
-MATMUL_WORK_FLOATS = 17 * 128  # GSDLQ_MATMUL_WORK_FLOATS
+MATMUL_MAX_BATCH = 128  # GSDLQ_MATMUL_MAX_BATCH
+
+
+def matmul_work_bytes(batch: int, cols: int) -> int:
+    n = ctypes.c_size_t()
+    L.check(_lib().gsdlq_hex2d_matmul_work_size(batch, cols, ctypes.byref(n)), "hex2d_matmul_work_size")
+    return int(n.value)
+
+
+def matmul_work(batch: int, cols: int, device="cuda") -> torch.Tensor:
+    """Scratch for hex2d_matmul of up to ``batch`` tokens and ``cols`` columns (1024-byte aligned)."""
+    return torch.empty(matmul_work_bytes(batch, cols) + 1024, dtype=torch.uint8, device=device)
+
+
+def _aligned(work: torch.Tensor) -> tuple[int, int]:
+    p = work.data_ptr()
+    a = (p + 1023) & ~1023
+    return a, work.numel() * work.element_size() - (a - p)
 
 
 def hex2d_matmul(x, h: DeviceHex, xy_table, y, work):
-    """y[b] = the packed linear of x[b] for every row b of x ([batch][cols] -> [batch][rows]); work:
-    MATMUL_WORK_FLOATS floats of device scratch."""
+    """y[b] = the packed linear of x[b] for every row b of x ([batch][cols] -> [batch][rows]); work: a
+    matmul_work buffer."""
+    wp, wb = _aligned(work)
     L.check(_lib().gsdlq_hex2d_matmul(ptr(x), x.shape[0], ptr(h.codes), ptr(h.scales), ptr(xy_table), ptr(h.U),
                                       ptr(h.S), ptr(h.Vt), ptr(h.row_ptr), ptr(h.kink_cols), ptr(h.kink_deltas),
-                                      ptr(y), ptr(work), h.rows, h.cols, h.k_dim, h.n_pts, stream_handle()),
+                                      ptr(y), wp, wb, h.rows, h.cols, h.k_dim, h.n_pts, stream_handle()),
             "hex2d_matmul")
 
 

@@ -333,18 +333,20 @@ int gsdlq_rope_table(float *table, int max_seq, int head_dim, float rope_theta);
  * y[b] = gsd_cpu_hex2d_matvec(gsd_cpu_lowrank_proj(x[b])) for b < batch (gsd_lq_cpu_engine.c:111-183
  * applied to each token), as one dequant-GEMM on the tcgen05 tensor cores (accumulators in tensor
  * memory): the codes are decoded once per launch for all tokens.  x: [batch][cols] fp32, 16-byte
- * aligned; y: [batch][rows] fp32 (zeroed here, then accumulated); work: at least
- * GSDLQ_MATMUL_WORK_FLOATS floats of device scratch (per-token maxima and low-rank projections).
+ * aligned; y: [batch][rows] fp32 (zeroed here, then accumulated); work: device scratch of at least
+ * gsdlq_hex2d_matmul_work_size(batch, cols) bytes, 1024-byte aligned (per-token maxima and low-rank
+ * projections, and the activations converted once into the tensor cores' operand layout).
  * 1 <= batch <= GSDLQ_MATMUL_MAX_BATCH, cols a multiple of 64 and at most 65535, k_dim <= 16,
  * n_pts <= 256, codes 16-byte aligned.  Weights and activations enter the tensor cores as fp16
  * hi + lo parts (about 22 significant bits): results match the per-token matvec to about 1e-6
  * relative.  The partial sums are added with atomics, so the last bits may differ between runs. */
 #define GSDLQ_MATMUL_MAX_BATCH 128
-#define GSDLQ_MATMUL_WORK_FLOATS (17 * 128)
+int gsdlq_hex2d_matmul_work_size(int batch, int cols, size_t *bytes);
 int gsdlq_hex2d_matmul(const float *x, int batch, const uint8_t *codes, const uint16_t *scales,
                        const float *xy_table, const uint16_t *U, const float *S, const uint16_t *Vt,
                        const uint32_t *kink_row_ptr, const uint16_t *kink_cols, const float *kink_deltas,
-                       float *y, float *work, int rows, int cols, int k_dim, int n_pts, gsdlq_stream_t stream);
+                       float *y, void *work, size_t work_bytes, int rows, int cols, int k_dim, int n_pts,
+                       gsdlq_stream_t stream);
 
 /* ---- Chunked prefill: the per-token operations over the n rows of a chunk ---------------------
  * No counterpart in the reference, whose prefill runs forward_token once per prompt token

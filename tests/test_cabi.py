@@ -72,12 +72,13 @@ def test_batched_and_noalloc_argument_errors_before_launch():
     A = ctypes.c_void_p(0x100000)        # a 256-byte-aligned stand-in address
     odd = ctypes.c_void_p(0x100001)
 
-    def mm(x=A, batch=4, codes=A, y=A, work=A, rows=64, cols=128, k=0, n_pts=217, U=None, S=None, Vt=None):
-        return lib.gsdlq_hex2d_matmul(x, batch, codes, A, A, U, S, Vt, A, A, A, y, work, rows, cols, k, n_pts, None)
+    def mm(x=A, batch=4, codes=A, y=A, work=A, rows=64, cols=128, k=0, n_pts=217, U=None, S=None, Vt=None, wb=1 << 30):
+        return lib.gsdlq_hex2d_matmul(x, batch, codes, A, A, U, S, Vt, A, A, A, y, work, wb, rows, cols, k, n_pts, None)
 
     for kw in (dict(batch=0), dict(batch=129), dict(cols=100), dict(cols=65536), dict(cols=0), dict(rows=0),
                dict(k=17), dict(k=4), dict(n_pts=0), dict(n_pts=257), dict(codes=odd), dict(y=odd),
-               dict(work=odd), dict(x=None), dict(codes=None), dict(x=ctypes.c_void_p(0x100008))):
+               dict(work=odd), dict(x=None), dict(codes=None), dict(x=ctypes.c_void_p(0x100008)),
+               dict(work=ctypes.c_void_p(0x100100)), dict(wb=1024)):
         assert mm(**kw) == -1, kw
 
     def mv(x=A, codes=A, y=A, rows=64, cols=128, k=0, n_pts=217, U=None, tmp=None):

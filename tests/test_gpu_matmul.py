@@ -29,7 +29,7 @@ def test_matmul_vs_oracle(env, restated, rng, rows, cols, k, nnz, radius, batch)
     x[batch // 2] *= 40.0  # tokens of very different magnitude share the launch
     h = ops.DeviceHex(t)
     y = torch.full((batch, rows), 7.0, device="cuda")  # the entry point zeroes it
-    work = torch.zeros(ops.MATMUL_WORK_FLOATS, device="cuda")
+    work = ops.matmul_work(batch, cols)
     xy = dev(cb.xy_table(radius))
     for rep in range(2):
         ops.hex2d_matmul(dev(x), h, xy, y, work)
@@ -51,7 +51,7 @@ def test_matmul_batch1_matches_matvec(env, rng):
     y1, tk = torch.zeros(4096, device="cuda"), torch.zeros(16, device="cuda")
     ops.lowrank_proj(xd[0], h, tk)
     ops.hex2d_matvec(xd[0], h, xy, tk, y1)
-    y2, work = torch.zeros((1, 4096), device="cuda"), torch.zeros(ops.MATMUL_WORK_FLOATS, device="cuda")
+    y2, work = torch.zeros((1, 4096), device="cuda"), ops.matmul_work(1, 4096)
     ops.hex2d_matmul(xd, h, xy, y2, work)
     torch.cuda.synchronize()
     assert matvec_err(y2.cpu().numpy()[0], y1.cpu().numpy()) < MATVEC_TOL
@@ -62,11 +62,18 @@ def test_matmul_rejects_bad_arguments(env, rng):
     import gsdlq_b200.codebook as cb
     t = rand_hex(rng, 64, 128, k=0, nnz=0, radius=8)
     h = ops.DeviceHex(t)
-    xy, work = dev(cb.xy_table(8)), torch.zeros(ops.MATMUL_WORK_FLOATS, device="cuda")
+    xy, work = dev(cb.xy_table(8)), ops.matmul_work(ops.MATMUL_MAX_BATCH, 128)
+    wp, wb = ops._aligned(work)
     for batch in (0, ops.MATMUL_MAX_BATCH + 1):
         x = torch.zeros((max(batch, 1), 128), device="cuda")
         y = torch.zeros((max(batch, 1), 64), device="cuda")
         st = L.load().gsdlq_hex2d_matmul(ops.ptr(x), batch, ops.ptr(h.codes), ops.ptr(h.scales), ops.ptr(xy), None,
                                          None, None, ops.ptr(h.row_ptr), ops.ptr(h.kink_cols), ops.ptr(h.kink_deltas),
-                                         ops.ptr(y), ops.ptr(work), 64, 128, 0, h.n_pts, None)
+                                         ops.ptr(y), wp, wb, 64, 128, 0, h.n_pts, None)
         assert st == -1
+    # a work buffer below the size the batch needs is refused
+    x, y = torch.zeros((16, 128), device="cuda"), torch.zeros((16, 64), device="cuda")
+    st = L.load().gsdlq_hex2d_matmul(ops.ptr(x), 16, ops.ptr(h.codes), ops.ptr(h.scales), ops.ptr(xy), None, None, None,
+                                     ops.ptr(h.row_ptr), ops.ptr(h.kink_cols), ops.ptr(h.kink_deltas), ops.ptr(y), wp,
+                                     ops.matmul_work_bytes(16, 128) - 16, 64, 128, 0, h.n_pts, None)
+    assert st == -1
