@@ -11,6 +11,7 @@
 //
 // The reference has no batched prefill: it runs forward_token once per prompt token
 // (run_gpu_native_chat.py:1128-1131).
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
@@ -85,90 +86,216 @@ __global__ void rope_kv_rows_kernel(float* __restrict__ q, const float* __restri
   }
 }
 
-// Causal attention of one token's GQA group: CTA (token t, kv head g), 128 threads.  Positions go in
-// tiles of 32: thread (position j, head h) computes the score q_h . k_j * sm_scale, each head's running
-// maximum and sum are updated (online softmax), and thread d accumulates every head's sum of p_j v_j[d].
-constexpr int AR_THREADS = 128, AR_TILE = 32, AR_MAXGQ = 8, AR_MAXHD = 128;
-__global__ void __launch_bounds__(AR_THREADS) attention_rows_kernel(const float* __restrict__ q,
-                                                                    const uint16_t* __restrict__ kc,
-                                                                    const uint16_t* __restrict__ vc,
-                                                                    float* __restrict__ out, int layer, int pos0,
-                                                                    int n_heads, int n_kv, int hd, int max_seq,
-                                                                    float sm_scale) {
-  __shared__ float qs[AR_MAXGQ][AR_MAXHD];
-  __shared__ float ps[AR_MAXGQ][AR_TILE];
-  __shared__ float s_m[AR_MAXGQ], s_l[AR_MAXGQ], s_f[AR_MAXGQ];
-  const int t = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
-  const int gq = n_heads / n_kv, pos = pos0 + t;
-  const int len = (pos >= 0 && pos < max_seq) ? pos + 1 : 0;
-  if (len == 0 && tid == 0) raise_flag(GSDLQ_FLAG_BAD_POS);
-  const float* qt = q + ((size_t)t * n_heads + (size_t)g * gq) * hd;
-  for (int e = tid; e < gq * hd; e += AR_THREADS) qs[e / hd][e % hd] = qt[e];
-  if (tid < gq) {
-    s_m[tid] = -INFINITY;
-    s_l[tid] = 0.f;
-  }
-  float acc[AR_MAXGQ];
+// Causal attention of a chunk, tiled: CTA (block of AT_ROWS query rows, kv head g, split z).  The rows
+// are (token, head) pairs of one GQA group, token-major: row r is token t0 + r / gq, head g * gq + r % gq,
+// so every row of the CTA reads the same K and V.  Positions go in tiles of AT_POS: the fp16 K tile is
+// converted into shared memory transposed (kT[d][j]), V as is (vs[j][d]); thread (rg = tid / 16,
+// pg = tid % 16) computes the scores of rows 4rg .. 4rg+3 at positions 4pg .. 4pg+3 from float4 reads of
+// the pre-scaled qT[d][r] and of kT, runs the online softmax of its rows in registers (the 16 threads of a
+// row group are one half-warp, reduced by shuffles), writes its p into pT[j][r] and accumulates
+// out[4 rows][4 dims per 64] += p v.  With splits > 1 each split covers a contiguous range of the CTA's
+// position tiles and writes its unnormalised rows with their (max, sum) into the work buffer, and
+// attention_combine_kernel merges the splits.
+constexpr int AT_THREADS = 128, AT_ROWS = 32, AT_POS = 64, AT_MAXGQ = 8, AT_MAXSPLIT = 8;
+
+__host__ __device__ constexpr size_t at_smem_bytes(int hd) {
+  return sizeof(float) * ((size_t)hd * AT_ROWS + (size_t)hd * AT_POS + (size_t)AT_POS * hd + (size_t)AT_POS * AT_ROWS);
+}
+
+// swizzled float4 slot of row group rg in pT row j (spreads the row groups' stores over the banks)
+__device__ __forceinline__ int pt_slot(int j, int rg) { return j * AT_ROWS + 4 * (rg ^ ((j >> 2) & 7)); }
+
+template <int HD>
+__global__ void __launch_bounds__(AT_THREADS, 2)
+    attention_rows_kernel(const float* __restrict__ q, const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc,
+                          float* __restrict__ out, float* __restrict__ work, int layer, int pos0, int n, int n_heads,
+                          int n_kv, int max_seq, float sm_scale, int splits) {
+  constexpr int DC = HD / 64;  // 64-dim column groups of the thread's output
+  extern __shared__ __align__(16) float at_smem[];
+  float* qT = at_smem;                  // [HD][AT_ROWS]
+  float* kT = qT + HD * AT_ROWS;        // [HD][AT_POS]
+  float* vs = kT + HD * AT_POS;         // [AT_POS][HD]
+  float* pT = vs + AT_POS * HD;         // [AT_POS][AT_ROWS], swizzled slots
+  const int tid = threadIdx.x, rg = tid >> 4, pg = tid & 15;
+  const int g = blockIdx.y, z = blockIdx.z;
+  const int gq = n_heads / n_kv, qb = AT_ROWS / gq, used = qb * gq;
+  const int t0 = blockIdx.x * qb;
+  const int t_last = min(t0 + qb, n) - 1;
+  // rows past the chunk (or past qb * gq) repeat the last valid row and are not written
+  int lim[4], tok[4], head[4];
 #pragma unroll
-  for (int h = 0; h < AR_MAXGQ; ++h) acc[h] = 0.f;
-  __syncthreads();
-  const size_t stride = (size_t)n_kv * hd;
-  const uint16_t* kl = kc + (size_t)layer * max_seq * stride + (size_t)g * hd;
-  const uint16_t* vl = vc + (size_t)layer * max_seq * stride + (size_t)g * hd;
-  for (int j0 = 0; j0 < len; j0 += AR_TILE) {
-    // scores of the tile: thread (j, h) for j = tid % 32, heads h = tid / 32, + 4, ...
-    for (int e = tid; e < gq * AR_TILE; e += AR_THREADS) {
-      const int h = e / AR_TILE, j = e - h * AR_TILE, p = j0 + j;
-      float s = -INFINITY;
-      if (p < len) {
-        const uint16_t* kr = kl + (size_t)p * stride;
-        float d = 0.f;
-        for (int i = 0; i < hd; i += 2) {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(kr + i);
-          d = fmaf(qs[h][i], h2f((uint16_t)(w & 0xffffu)), d);
-          d = fmaf(qs[h][i + 1], h2f((uint16_t)(w >> 16)), d);
-        }
-        s = d * sm_scale;
+  for (int i = 0; i < 4; ++i) {
+    const int r = rg * 4 + i;
+    int t = r < used ? t0 + r / gq : t_last;
+    t = min(t, t_last);
+    tok[i] = (r < used && t0 + r / gq <= t_last) ? t : -1;
+    head[i] = g * gq + (r < used ? r % gq : 0);
+    lim[i] = pos0 + t;
+  }
+  // q rows, pre-scaled, transposed
+  for (int e = tid; e < AT_ROWS * HD; e += AT_THREADS) {
+    const int r = e / HD, d = e - r * HD;
+    int t = r < used ? t0 + r / gq : t_last;
+    t = min(t, t_last);
+    const int h = g * gq + (r < used ? r % gq : 0);
+    qT[d * AT_ROWS + r] = q[((size_t)t * n_heads + h) * HD + d] * sm_scale;
+  }
+  const int ntiles = (pos0 + t_last) / AT_POS + 1;
+  const int per = (ntiles + splits - 1) / splits;
+  const int tile0 = z * per, tile1 = min(ntiles, tile0 + per);
+  const size_t stride = (size_t)n_kv * HD;
+  const uint16_t* kl = kc + (size_t)layer * max_seq * stride + (size_t)g * HD;
+  const uint16_t* vl = vc + (size_t)layer * max_seq * stride + (size_t)g * HD;
+  const int kv_end = pos0 + t_last + 1;  // positions written so far for the CTA's last token
+  float m[4], lsum[4], acc[4][4 * DC];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    lsum[i] = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4 * DC; ++c) acc[i][c] = 0.f;
+  }
+  for (int tile = tile0; tile < tile1; ++tile) {
+    const int j0 = tile * AT_POS;
+    __syncthreads();  // the previous tile's kT / vs / pT are consumed (and qT written, on the first tile)
+    // K: lanes walk positions (conflict-free transposed stores); V: lanes walk dims (coalesced rows)
+#pragma unroll 4
+    for (int e = tid; e < AT_POS * HD / 8; e += AT_THREADS) {
+      const int j = e % AT_POS, d8 = e / AT_POS, p = j0 + j;
+      uint4 w = make_uint4(0, 0, 0, 0);
+      if (p < kv_end) w = __ldg(reinterpret_cast<const uint4*>(kl + (size_t)p * stride + d8 * 8));
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        kT[(d8 * 8 + 2 * i) * AT_POS + j] = h2f((uint16_t)(ww[i] & 0xffffu));
+        kT[(d8 * 8 + 2 * i + 1) * AT_POS + j] = h2f((uint16_t)(ww[i] >> 16));
       }
-      ps[h][j] = s;
+    }
+#pragma unroll 4
+    for (int e = tid; e < AT_POS * HD / 8; e += AT_THREADS) {
+      const int d8 = e % (HD / 8), j = e / (HD / 8), p = j0 + j;
+      uint4 w = make_uint4(0, 0, 0, 0);
+      if (p < kv_end) w = __ldg(reinterpret_cast<const uint4*>(vl + (size_t)p * stride + d8 * 8));
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+      float4* dst = reinterpret_cast<float4*>(vs + j * HD + d8 * 8);
+      dst[0] = make_float4(h2f((uint16_t)(ww[0] & 0xffffu)), h2f((uint16_t)(ww[0] >> 16)),
+                           h2f((uint16_t)(ww[1] & 0xffffu)), h2f((uint16_t)(ww[1] >> 16)));
+      dst[1] = make_float4(h2f((uint16_t)(ww[2] & 0xffffu)), h2f((uint16_t)(ww[2] >> 16)),
+                           h2f((uint16_t)(ww[3] & 0xffffu)), h2f((uint16_t)(ww[3] >> 16)));
     }
     __syncthreads();
-    // online softmax: one warp per head
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int h = warp; h < gq; h += AR_THREADS / 32) {
-      const float s = ps[h][lane];
-      const float mt = warp_max(s);
-      const float m_old = s_m[h], m_new = fmaxf(m_old, mt);
-      const float p = (s == -INFINITY) ? 0.f : expf(s - m_new);
-      const float sum = warp_sum(p);
-      ps[h][lane] = p;
-      __syncwarp();
-      if (lane == 0) {
-        const float f = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-        s_f[h] = f;
-        s_l[h] = s_l[h] * f + sum;
-        s_m[h] = m_new;
+    // scores of rows 4rg.. at positions 4pg..
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[i][c] = 0.f;
+#pragma unroll 8
+    for (int d = 0; d < HD; ++d) {
+      const float4 qv = *reinterpret_cast<const float4*>(qT + d * AT_ROWS + rg * 4);
+      const float4 kv = *reinterpret_cast<const float4*>(kT + d * AT_POS + pg * 4);
+      const float qq[4] = {qv.x, qv.y, qv.z, qv.w}, kk[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s[i][c] = fmaf(qq[i], kk[c], s[i][c]);
+    }
+    // online softmax per row, reduced over the half-warp of the row group
+    float f[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (j0 + pg * 4 + c > lim[i]) s[i][c] = -INFINITY;
+        tmax = fmaxf(tmax, s[i][c]);
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      const float mn = fmaxf(m[i], tmax);
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        s[i][c] = (s[i][c] == -INFINITY) ? 0.f : expf(s[i][c] - mn);
+        rs += s[i][c];
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
+      f[i] = (m[i] == -INFINITY) ? 0.f : expf(m[i] - mn);
+      if (mn == -INFINITY) f[i] = 1.f;
+      lsum[i] = lsum[i] * f[i] + rs;
+      m[i] = mn;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<float4*>(pT + pt_slot(pg * 4 + c, rg)) = make_float4(s[0][c], s[1][c], s[2][c], s[3][c]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4 * DC; ++c) acc[i][c] *= f[i];
+    __syncthreads();
+    // out rows 4rg.. at dims 4pg + 64 c ..
+#pragma unroll 4
+    for (int j = 0; j < AT_POS; ++j) {
+      const float4 pv = *reinterpret_cast<const float4*>(pT + pt_slot(j, rg));
+      const float pp[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+      for (int dc = 0; dc < DC; ++dc) {
+        const float4 vv = *reinterpret_cast<const float4*>(vs + j * HD + dc * 64 + pg * 4);
+        const float v4[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[i][dc * 4 + c] = fmaf(pp[i], v4[c], acc[i][dc * 4 + c]);
       }
     }
-    __syncthreads();
-    // P.V: thread d (< hd) for every head
-    if (tid < hd) {
-      float vcol[AR_TILE];
+  }
 #pragma unroll
-      for (int j = 0; j < AR_TILE; ++j) vcol[j] = (j0 + j < len) ? h2f(vl[(size_t)(j0 + j) * stride + tid]) : 0.f;
-      for (int h = 0; h < gq; ++h) {
-        float a = acc[h] * s_f[h];
+  for (int i = 0; i < 4; ++i) {
+    if (tok[i] < 0) continue;
+    const size_t row = (size_t)tok[i] * n_heads + head[i];
+    if (splits == 1) {
+      const float inv = 1.0f / lsum[i];
 #pragma unroll
-        for (int j = 0; j < AR_TILE; ++j) a = fmaf(ps[h][j], vcol[j], a);
-        acc[h] = a;
+      for (int dc = 0; dc < DC; ++dc)
+        *reinterpret_cast<float4*>(out + row * HD + dc * 64 + pg * 4) =
+            make_float4(acc[i][dc * 4] * inv, acc[i][dc * 4 + 1] * inv, acc[i][dc * 4 + 2] * inv, acc[i][dc * 4 + 3] * inv);
+    } else {
+      const size_t rows = (size_t)n * n_heads;
+      float* wa = work + ((size_t)z * rows + row) * HD;
+#pragma unroll
+      for (int dc = 0; dc < DC; ++dc)
+        *reinterpret_cast<float4*>(wa + dc * 64 + pg * 4) =
+            make_float4(acc[i][dc * 4], acc[i][dc * 4 + 1], acc[i][dc * 4 + 2], acc[i][dc * 4 + 3]);
+      if (pg == 0) {
+        float* wm = work + (size_t)AT_MAXSPLIT * rows * HD;
+        wm[((size_t)z * rows + row) * 2] = m[i];
+        wm[((size_t)z * rows + row) * 2 + 1] = lsum[i];
       }
     }
-    __syncthreads();
   }
-  if (tid < hd) {
-    float* ot = out + ((size_t)t * n_heads + (size_t)g * gq) * hd;
-    for (int h = 0; h < gq; ++h) ot[(size_t)h * hd + tid] = len > 0 ? acc[h] / s_l[h] : 0.f;
+}
+
+// merge of the splits of row (token blockIdx.x, head blockIdx.y): out = sum_z e^(m_z - M) acc_z / L
+__global__ void attention_combine_kernel(const float* __restrict__ work, float* __restrict__ out, int n, int n_heads,
+                                         int hd, int splits) {
+  const size_t rows = (size_t)n * n_heads, row = (size_t)blockIdx.x * n_heads + blockIdx.y;
+  const float* wm = work + (size_t)AT_MAXSPLIT * rows * hd;
+  float mx = -INFINITY;
+  for (int z = 0; z < splits; ++z) mx = fmaxf(mx, wm[((size_t)z * rows + row) * 2]);
+  float l = 0.f, a = 0.f;
+  for (int z = 0; z < splits; ++z) {
+    const float mz = wm[((size_t)z * rows + row) * 2];
+    if (mz == -INFINITY) continue;
+    const float e = expf(mz - mx);
+    l = fmaf(wm[((size_t)z * rows + row) * 2 + 1], e, l);
+    a = fmaf(work[((size_t)z * rows + row) * hd + threadIdx.x], e, a);
   }
+  out[row * hd + threadIdx.x] = a / l;
+}
+
+static size_t attention_rows_work(int n, int n_heads, int hd) {
+  return sizeof(float) * (size_t)AT_MAXSPLIT * n * n_heads * (hd + 2);
 }
 
 }  // namespace gsdlq
@@ -205,16 +332,53 @@ int gsdlq_rope_kv_rows(float* q, const float* k, const float* v, uint16_t* k_cac
   return GSDLQ_OK;
 }
 
-int gsdlq_attention_rows(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, float* out, int layer,
-                         int pos0, int n, int n_heads, int n_kv_heads, int head_dim, int max_seq, float sm_scale,
-                         gsdlq_stream_t stream) {
-  if (!q || !k_cache || !v_cache || !out || n <= 0 || layer < 0 || pos0 < 0 || pos0 + n > max_seq) return GSDLQ_ERR_INVALID;
-  if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || n_heads / n_kv_heads > AR_MAXGQ) return GSDLQ_ERR_INVALID;
-  if (head_dim <= 0 || head_dim > AR_MAXHD || head_dim % 2) return GSDLQ_ERR_INVALID;
-  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 3u) return GSDLQ_ERR_INVALID;
-  attention_rows_kernel<<<dim3(n, n_kv_heads), AR_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
-      q, k_cache, v_cache, out, layer, pos0, n_heads, n_kv_heads, head_dim, max_seq, sm_scale);
+int gsdlq_attention_rows_work_size(int n, int n_heads, int head_dim, size_t* bytes) {
+  if (!bytes || n <= 0 || n_heads <= 0 || head_dim <= 0) return GSDLQ_ERR_INVALID;
+  *bytes = attention_rows_work(n, n_heads, head_dim);
+  return GSDLQ_OK;
+}
+
+int gsdlq_attention_rows(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, float* out, void* work,
+                         size_t work_bytes, int layer, int pos0, int n, int n_heads, int n_kv_heads, int head_dim,
+                         int max_seq, float sm_scale, gsdlq_stream_t stream) {
+  if (!q || !k_cache || !v_cache || !out || !work || n <= 0 || layer < 0 || pos0 < 0 || pos0 + n > max_seq)
+    return GSDLQ_ERR_INVALID;
+  if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || n_heads / n_kv_heads > AT_MAXGQ) return GSDLQ_ERR_INVALID;
+  if (head_dim != 64 && head_dim != 128) return GSDLQ_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+       reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(work)) & 15u)
+    return GSDLQ_ERR_INVALID;
+  if (work_bytes < attention_rows_work(n, n_heads, head_dim)) return GSDLQ_ERR_INVALID;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int gq = n_heads / n_kv_heads, qb = AT_ROWS / gq;
+  const int blocks = (n + qb - 1) / qb;
+  // splits of the position range so that about two CTAs per SM are busy; none shorter than one tile
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int base = blocks * n_kv_heads, tiles = (pos0 + n - 1) / AT_POS + 1;
+  int splits = (2 * sms + base - 1) / base;
+  splits = std::max(1, std::min(std::min(splits, AT_MAXSPLIT), tiles));
+  const dim3 grid(blocks, n_kv_heads, splits);
+  float* wk = static_cast<float*>(work);
+  static bool attr = false;  // the 88 KB of the head_dim-128 tiles need the opt-in size
+  if (!attr) {
+    cudaFuncSetAttribute(attention_rows_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at_smem_bytes(128));
+    cudaFuncSetAttribute(attention_rows_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at_smem_bytes(64));
+    attr = true;
+  }
+  if (head_dim == 128) {
+    attention_rows_kernel<128><<<grid, AT_THREADS, at_smem_bytes(128), st>>>(
+        q, k_cache, v_cache, out, wk, layer, pos0, n, n_heads, n_kv_heads, max_seq, sm_scale, splits);
+  } else {
+    attention_rows_kernel<64><<<grid, AT_THREADS, at_smem_bytes(64), st>>>(
+        q, k_cache, v_cache, out, wk, layer, pos0, n, n_heads, n_kv_heads, max_seq, sm_scale, splits);
+  }
   GSDLQ_CUDA_CHECK_LAUNCH();
+  if (splits > 1) {
+    attention_combine_kernel<<<dim3(n, n_heads), head_dim, 0, st>>>(wk, out, n, n_heads, head_dim, splits);
+    GSDLQ_CUDA_CHECK_LAUNCH();
+  }
   return GSDLQ_OK;
 }
 

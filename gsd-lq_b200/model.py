@@ -507,6 +507,7 @@ class GSDLQModel:
                  "att": torch.zeros((T, qd), **f32), "o": torch.zeros((T, self.hidden), **f32),
                  "g": torch.zeros((T, self.ffn_local), **f32), "u": torch.zeros((T, self.ffn_local), **f32),
                  "work": ops.matmul_work(T, max(h.cols for h in self.hex.values()), dev),
+                 "awork": ops.attention_rows_work(T, self.n_heads_local, self.head_dim, dev),
                  "ids": torch.zeros(T, dtype=torch.int32, device=dev),
                  "xy": {r: torch.from_numpy(ops.codebook(r)).to(dev) for r in (6, 8)}}
             self._pf = b
@@ -536,7 +537,7 @@ class GSDLQModel:
                                            l, pos0, n, self.n_heads_local, self.n_kv_local, self.head_dim,
                                            self.max_seq, sh), "gsdlq_rope_kv_rows")
             L.check(lib.gsdlq_attention_rows(b["q"].data_ptr(), self.k_cache.data_ptr(), self.v_cache.data_ptr(),
-                                             b["att"].data_ptr(), l, pos0, n, self.n_heads_local, self.n_kv_local,
+                                             b["att"].data_ptr(), b["awork"].data_ptr(), b["awork"].numel(), l, pos0, n, self.n_heads_local, self.n_kv_local,
                                              self.head_dim, self.max_seq, sm, sh), "gsdlq_attention_rows")
             mm(b["att"], p + "attn_output.weight", b["o"])
             L.check(lib.gsdlq_vec_add(x.data_ptr(), x.data_ptr(), b["o"].data_ptr(), n * H, sh), "gsdlq_vec_add")

@@ -179,6 +179,14 @@ def hex2d_matmul(x, h: DeviceHex, xy_table, y, work):
             "hex2d_matmul")
 
 
+def attention_rows_work(n: int, n_heads: int, head_dim: int, device="cuda") -> torch.Tensor:
+    """Scratch for gsdlq_attention_rows of up to ``n`` tokens (float32; torch's allocations are 16-byte
+    aligned)."""
+    b = ctypes.c_size_t()
+    L.check(_lib().gsdlq_attention_rows_work_size(n, n_heads, head_dim, ctypes.byref(b)), "attention_rows_work_size")
+    return torch.empty(int(b.value), dtype=torch.uint8, device=device)
+
+
 def rope_and_store_kv(q, k, v, k_cache, v_cache, layer, pos, n_heads, n_kv, hd, max_seq, theta, interleaved=1):
     L.check(_lib().gsdlq_rope_and_store_kv(ptr(q), ptr(k), ptr(v), ptr(k_cache), ptr(v_cache), layer, pos, n_heads,
                                            n_kv, hd, max_seq, theta, interleaved, stream_handle()),

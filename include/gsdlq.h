@@ -357,16 +357,19 @@ int gsdlq_hex2d_matmul(const float *x, int batch, const uint8_t *codes, const ui
  *   rope_kv_rows:   gsd_cpu_rope_and_store_kv of every row, interleaved pairs, angles from the
  *                   gsdlq_rope_table table rope_cs [max_seq][head_dim/2] (gsd_lq_cpu_engine.c:186-262)
  *   attention_rows: gsd_cpu_gqa_attention of row t at position pos0 + t: causal over the cache
- *                   (gsd_lq_cpu_engine.c:265-330); head_dim <= 128, n_heads / n_kv_heads <= 8 */
+ *                   (gsd_lq_cpu_engine.c:265-330); head_dim 64 or 128, n_heads / n_kv_heads <= 8;
+ *                   q, out, work 16-byte aligned; work (device) of at least the bytes
+ *                   gsdlq_attention_rows_work_size gives for (n, n_heads, head_dim) */
 int gsdlq_embed_rows(const uint16_t *embed, const int *ids, int n, int vocab, int dim, float *out,
                      gsdlq_stream_t stream);
 int gsdlq_rmsnorm_rows(const float *x, const float *w, float *out, int n, int dim, float eps, gsdlq_stream_t stream);
 int gsdlq_rope_kv_rows(float *q, const float *k, const float *v, uint16_t *k_cache, uint16_t *v_cache,
                        const float *rope_cs, int layer, int pos0, int n, int n_heads, int n_kv_heads, int head_dim,
                        int max_seq, gsdlq_stream_t stream);
-int gsdlq_attention_rows(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, float *out, int layer,
-                         int pos0, int n, int n_heads, int n_kv_heads, int head_dim, int max_seq, float sm_scale,
-                         gsdlq_stream_t stream);
+int gsdlq_attention_rows_work_size(int n, int n_heads, int head_dim, size_t *bytes);
+int gsdlq_attention_rows(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, float *out, void *work,
+                         size_t work_bytes, int layer, int pos0, int n, int n_heads, int n_kv_heads, int head_dim,
+                         int max_seq, float sm_scale, gsdlq_stream_t stream);
 
 /* ---- The whole decode step in one launch ----------------------------------------------------
  * Engine-level entry point with no single reference counterpart: the reference's

@@ -52,3 +52,37 @@ def test_batched_prefill_matches_token_prefill_and_oracle(cuda_lib, name, over, 
     assert a.sample_token(la) == b.sample_token(lb) == oracle.argmax(lr)
     # decoding continues identically from either cache
     assert L.device_flags() == 0
+
+
+@pytest.mark.parametrize("n_heads,n_kv,hd,pos0,n", [
+    (32, 8, 128, 1024, 128), (32, 8, 128, 0, 128), (12, 2, 128, 300, 77), (32, 32, 64, 1900, 128),
+    (12, 2, 128, 0, 1), (16, 2, 64, 63, 65)])
+def test_attention_rows_vs_torch(cuda_lib, n_heads, n_kv, hd, pos0, n):
+    """gsdlq_attention_rows (position tiles, position splits merged by the combine kernel) against a
+    float64 torch restatement of causal GQA attention over the fp16 cache."""
+    import gsdlq_b200._lib as L
+    import gsdlq_b200.ops as ops
+    max_seq, layers, layer = 2048, 2, 1
+    g = torch.Generator(device="cpu").manual_seed(pos0 * 7 + n)
+    kc = torch.randn((layers, max_seq, n_kv, hd), generator=g).half().cuda()
+    vc = torch.randn((layers, max_seq, n_kv, hd), generator=g).half().cuda()
+    q = (torch.randn((n, n_heads, hd), generator=g) * 2.0).cuda()
+    out = torch.full((n, n_heads, hd), 7.0, device="cuda")
+    work = ops.attention_rows_work(n, n_heads, hd)
+    sm = 1.0 / hd ** 0.5
+    L.check(L.load().gsdlq_attention_rows(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), work.data_ptr(),
+                                          work.numel(), layer, pos0, n, n_heads, n_kv, hd, max_seq, sm, None),
+            "attention_rows")
+    torch.cuda.synchronize()
+    K, V = kc[layer].double().cpu(), vc[layer].double().cpu()
+    qd, gq = q.double().cpu(), n_heads // n_kv
+    ref = torch.empty((n, n_heads, hd), dtype=torch.float64)
+    for t in range(n):
+        length = pos0 + t + 1
+        for h in range(n_heads):
+            s = (K[:length, h // gq] @ qd[t, h]) * sm
+            p = torch.softmax(s, 0)
+            ref[t, h] = p @ V[:length, h // gq]
+    err = torch.max(torch.abs(out.double().cpu() - ref)).item()
+    assert err < 2e-5, err
+    assert L.device_flags() == 0
