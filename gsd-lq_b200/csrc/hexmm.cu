@@ -6,24 +6,28 @@
 //   y[b][r] = sum_c W[r][c] x[b][c] + sum_{kinks of r} delta * x[b][col] + sum_j U[r][j] tmp[b][j],
 //   W[r][2p + i] = xy[code(r, p)][i] * scale(r, p / 32),  tmp[b][j] = S[j] * (Vt[j] . x[b]).
 //
-// Layout of the work.  A CTA of 4 warps owns a tile of 128 weight rows and a contiguous run of 64-column
-// k-blocks (split-K over CTAs, so that every SM streams weights).  Per k-block, through two shared-memory
-// stages:
-//   - thread t decodes the 32 code bytes of row t (one scale group) through a 256-entry float2 table into
-//     fp32 weights, W = xy * scale as the reference's dequant defines them, splits them into fp16 hi + lo
-//     parts (about 22 significant bits together) and writes them as two A operands in the K-major
-//     128-byte-swizzle layout (a row's 64 columns are 128 bytes, 8 rows form a 1024-byte atom, 16-byte
-//     chunk j of row r sits at chunk j ^ (r % 8), so the tensor core's reads spread over all banks);
-//   - the block's activations of every token are written as the B operand in the same layout, token b as
-//     two rows: 2b = fp16 hi, 2b + 1 = fp16 lo of x_b scaled by a power of two that puts max|x_b| in
-//     [2^14, 2^15) (so both halves stay normal; about 22 significant bits together);
-//   - one thread issues eight tcgen05.mma (W hi and W lo for each 16-column k-step; M = 128, N = 2 x tokens
-//     padded to 8, fp16 in, fp32 accumulate in tensor memory) and commits them to the stage's mbarrier,
-//     which releases the stage for the block two ahead; the next block's codes are loaded meanwhile.
-// At the end each warp reads its 32 tensor-memory lanes (its rows) with tcgen05.ld, adds each token's hi
-// and lo columns, unscales, and adds the partial sums into y (zeroed by the entry point) with fp32 atomics,
-// so the summation order over the k-runs is not fixed.  The kink and low-rank terms are added once per
-// (row, token) by the CTA whose run index equals the token index modulo the number of runs.
+// One call is four launches: hexmm_prep (per-token max|x| and the low-rank projections tmp), hexmm_xconv
+// (the activations as fp16 hi / lo B tiles, plus an fp32 transposed copy), hexmm_sparse (the kink and
+// low-rank terms of every (token, row), stored into y, which they initialise) and hexmm_kernel, the dense
+// lattice part, added into y with fp32 atomics (so the summation order over the k-runs is not fixed).
+//
+// hexmm_kernel.  A CTA owns a tile of 128 weight rows (the tensor memory's lanes) and a contiguous run of
+// 64-column k-blocks (split-K over CTAs, so that every SM streams weights).  Eight decoder warps, an issuer
+// warp and a loader warp, linked by mbarriers; per k-block i:
+//   - decoder thread t (row t % 128, columns 32 (t / 128) .. + 31 of the block) takes its 16 code bytes and
+//     the row's scale from a cp.async ring, looks every code up in its lane's copy of the 256-entry decode
+//     table (conflict-free) and forms the fp16 hi and lo parts of W = (x, r1) * (scale, scale sqrt3/2) in
+//     fp16 arithmetic (hi the rounded product, lo the rounded remainder of a fused multiply-add: about 22
+//     significant bits together), stores both with tcgen05.st into its tensor-memory lane as the A operand
+//     of stage i % SA and arrives on the stage's full barrier;
+//   - the loader bulk-copies block i's B tile (token b as two K-major 128-byte-swizzled rows: 2b = fp16 hi,
+//     2b + 1 = fp16 lo of x_b scaled by a power of two that puts max|x_b| in [2^14, 2^15)) into shared
+//     stage i % SB once the MMAs that read that stage before have completed;
+//   - the issuer waits for both, issues eight tcgen05.mma (W hi and W lo per 16-column k-step; M = 128,
+//     N = 2 x tokens padded to 8; A from tensor memory, B by descriptor; fp32 accumulate in tensor memory)
+//     and commits them to the stages' empty barriers.
+// At the end the decoder warps read the accumulator lanes with tcgen05.ld, add each token's hi and lo
+// columns, unscale and add them into y.
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -36,52 +40,54 @@ constexpr int MM_ROWS = 128;      // weight rows per CTA (tensor-memory lanes)
 constexpr int MM_KB = 64;         // columns per k-block: one scale group
 constexpr int MM_THREADS = 256;   // two threads per weight row (its two 32-column halves of a block)
 constexpr int MM_MAXB = GSDLQ_MATMUL_MAX_BATCH;  // tokens per call (N = 2 * 128 = 256, the largest MMA N)
-constexpr int MM_AHALF = MM_ROWS * MM_KB * 2;  // bytes of one fp16 A tile (16 KB): the weights' hi or lo parts
-constexpr int MM_ATILE = 2 * MM_AHALF;         // one stage's A tiles (hi, then lo)
-constexpr int MM_HDR = 12288;                  // table, barriers, tensor-memory slot, token scales, projections
+// decode table, header and B stages by absolute shared-window address (the layout is described below)
+constexpr uint32_t MM_TAB_ABS = 0x1000u, MM_HDR_ABS = MM_TAB_ABS - 1024u, MM_B_ABS = MM_TAB_ABS + 0x10000u;
+constexpr float MM_WF = 1024.f;                // power-of-two factor on the decoded weights
 
-// Per token b and chunk of MM_PREP columns: the chunk's max|x_b| into amax[b] (as ordered bits) and its
-// part of S[j] * (Vt[j] . x_b) into tmp[16 b + j] (gsd_cpu_lowrank_proj; fp32 atomics, so the summation
-// order is not fixed).  Both start at zero.
-constexpr int MM_PREP = 1024;
-__global__ void __launch_bounds__(256) hexmm_prep(const float* __restrict__ x, int C, const uint16_t* __restrict__ Vt,
-                                                  const float* __restrict__ S, int k, unsigned* __restrict__ amax_bits,
-                                                  float* __restrict__ tmp) {
-  __shared__ float red[8][17];
-  const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const float* xb = x + (size_t)b * C;
-  const int c1 = min(C, (int)(blockIdx.y + 1) * MM_PREP);
-  float amax = 0.f, acc[16];
+// Per group of 8 tokens (warp w: token 8 blockIdx.x + w) and chunk of MM_PREP columns: the chunk's
+// max|x_b| into amax[b] (as ordered bits) and its part of S[j] * (Vt[j] . x_b) into tmp[16 b + j]
+// (gsd_cpu_lowrank_proj; fp32 atomics, so the summation order is not fixed).  Both start at zero.  The
+// warp stages x_b's chunk in shared memory; lane 2j + h then forms the dot product of Vt[j] with its
+// half h of the chunk from sixteen 16-byte loads issued together.
+constexpr int MM_PREP = 256;
+__global__ void __launch_bounds__(256) hexmm_prep(const float* __restrict__ x, int B, int C,
+                                                  const uint16_t* __restrict__ Vt, const float* __restrict__ S, int k,
+                                                  unsigned* __restrict__ amax_bits, float* __restrict__ tmp) {
+  __shared__ float xs[8][MM_PREP];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, b = blockIdx.x * 8 + w;
+  if (b >= B) return;
+  const int c0 = blockIdx.y * MM_PREP;
+  const int j = lane >> 1, h = lane & 1, cc = c0 + h * (MM_PREP / 2);
+  // the Vt loads first: they do not depend on x
+  uint4 vt[MM_PREP / 16];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-  for (int c = blockIdx.y * MM_PREP + threadIdx.x; c < c1; c += 256) {
-    const float v = xb[c];
+  for (int i = 0; i < MM_PREP / 16; ++i)
+    vt[i] = (j < k && cc + 8 * i + 8 <= C) ? __ldg(reinterpret_cast<const uint4*>(Vt + (size_t)j * C + cc + 8 * i))
+                                          : make_uint4(0u, 0u, 0u, 0u);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < MM_PREP / 32; ++i) {
+    const int c = c0 + lane + 32 * i;
+    const float v = c < C ? x[(size_t)b * C + c] : 0.f;
+    xs[w][lane + 32 * i] = v;
     amax = fmaxf(amax, fabsf(v));
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < k) acc[j] = fmaf(h2f(Vt[(size_t)j * C + c]), v, acc[j]);
   }
   amax = warp_max(amax);
+  if (lane == 0) atomicMax(amax_bits + b, __float_as_uint(amax));  // non-negative floats order as their bits
+  __syncwarp();
+  float acc = 0.f;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) acc[j] = warp_sum(acc[j]);
-  if (lane == 0) {
-    red[warp][16] = amax;
+  for (int i = 0; i < MM_PREP / 16; ++i) {
+    const uint32_t q[4] = {vt[i].x, vt[i].y, vt[i].z, vt[i].w};
 #pragma unroll
-    for (int j = 0; j < 16; ++j) red[warp][j] = acc[j];
+    for (int t = 0; t < 4; ++t) {
+      acc = fmaf(h2f((uint16_t)(q[t] & 0xffffu)), xs[w][h * (MM_PREP / 2) + 8 * i + 2 * t], acc);
+      acc = fmaf(h2f((uint16_t)(q[t] >> 16)), xs[w][h * (MM_PREP / 2) + 8 * i + 2 * t + 1], acc);
+    }
   }
-  __syncthreads();
-  if (threadIdx.x < 16 && threadIdx.x < k) {
-    float t = 0.f;
-    for (int w = 0; w < 8; ++w) t += red[w][threadIdx.x];
-    atomicAdd(tmp + (size_t)b * 16 + threadIdx.x, S[threadIdx.x] * t);
-  }
-  if (threadIdx.x == 32) {
-    float m = 0.f;
-    for (int w = 0; w < 8; ++w) m = fmaxf(m, red[w][16]);
-    atomicMax(amax_bits + b, __float_as_uint(m));  // non-negative floats order as their bits
-  }
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  if (h == 0 && j < k) atomicAdd(tmp + (size_t)b * 16 + j, S[j] * acc);
 }
-
 
 // the power of two that puts max|x_b| in [2^14, 2^15), so both fp16 halves of x_b stay normal
 __device__ __forceinline__ float hexmm_xscale(unsigned amax_bits) {
@@ -102,12 +108,6 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
 }
 // byte offset of 16-byte chunk j (columns 8j .. 8j+7) of row r in a swizzled 64-column tile
 __device__ __forceinline__ int sw128(int r, int j) { return (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4); }
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
-}
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -131,47 +131,94 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "r"(taddr)
       : "memory");
 }
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+// decode-table entry: byte permute of the code word and lane * 4 into (code << 8) | lane * 4, loaded with
+// MM_TAB_ABS as the immediate offset (the table is constant after the set-up barrier)
+__device__ __forceinline__ uint32_t mm_lookup(uint32_t word, uint32_t lane4, uint32_t sel) {
+  const uint32_t a = __byte_perm(word, lane4, sel);
+  uint32_t r;
+  asm("ld.shared.b32 %0, [%1+%2];" : "=r"(r) : "r"(a), "n"(MM_TAB_ABS));
+  return r;
+}
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);  // a in the low half
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <int NB>
-constexpr int mm_tcols() {  // tensor-memory columns of the accumulator: a power of two >= 32
-  return 16 * NB <= 32 ? 32 : 16 * NB <= 64 ? 64 : 16 * NB <= 128 ? 128 : 256;
-}
 constexpr int MM_CSTAGES = 4;                  // k-blocks of codes in flight per CTA (cp.async ring)
-constexpr int MM_CSTAGE = MM_ROWS * 32;        // code bytes of one k-block of a tile (4 KB)
+// Shared memory, by absolute shared-window address (the dynamic allocation starts at the system-reserved
+// bytes B below MM_HDR_ABS; the kernel checks that B leaves the header room):
+//   [MM_HDR_ABS, MM_TAB_ABS)           barriers, tensor-memory slot, token scales (1 KB)
+//   [MM_TAB_ABS, MM_TAB_ABS + 64 KB)   decode table: 256 rows of 256 bytes, row c = code c's entry in 32
+//                                      lane copies (128 bytes), then a free 128-byte half; the free halves
+//                                      of rows 0-127 hold the code ring, those of rows 128-159 the scales
+//   [MM_TAB_ABS + 64 KB, ...)          B stages (1024-byte aligned: the swizzle atoms)
 template <int NB>
 constexpr int mm_btile() {  // one k-block of the B operand: 16 NB rows (token hi / lo) x 128 bytes
   return 16 * NB * 128;
 }
+// Tensor memory: the accumulator (N = 16 NB columns, from column 0, rounded up to 64), then SA A stages of
+// 64 columns (32 columns of fp16 pairs for the hi parts of a block's 64 weights per row, 32 for the lo).
 template <int NB>
-constexpr int mm_smem() {
-  // header + code ring + alignment slack + two A stages + two B stages; with 256 accumulator columns at
-  // least 80 KB, so that no more than two CTAs share an SM's 512 tensor-memory columns (a third would
-  // wait in tcgen05.alloc)
-  constexpr int need = MM_HDR + MM_CSTAGES * MM_CSTAGE + 1024 + 2 * MM_ATILE + 2 * mm_btile<NB>();
-  return (mm_tcols<NB>() == 256 && need < 80 * 1024) ? 80 * 1024 : need;
+constexpr int mm_acc_cols() {
+  return (16 * NB + 63) / 64 * 64;
 }
 template <int NB>
-constexpr bool mm_tmem_fits() {  // the CTAs that shared memory lets an SM hold fit its 512 tensor-memory columns
-  return (227 * 1024 / mm_smem<NB>()) * mm_tcols<NB>() <= 512;
+constexpr int mm_astages() {  // A stages in tensor memory
+  return mm_acc_cols<NB>() == 128 ? 2 : 3;
 }
-static_assert(mm_tmem_fits<1>() && mm_tmem_fits<2>() && mm_tmem_fits<3>() && mm_tmem_fits<4>() && mm_tmem_fits<5>() &&
-                  mm_tmem_fits<6>() && mm_tmem_fits<7>() && mm_tmem_fits<8>() && mm_tmem_fits<9>() &&
-                  mm_tmem_fits<12>() && mm_tmem_fits<16>(),
-              "at most 512 tensor-memory columns of resident CTAs per SM");
+template <int NB>
+constexpr int mm_bstages() {  // B stages in shared memory
+  return NB <= 2 ? 6 : NB <= 4 ? 4 : NB <= 8 ? 2 : 3;
+}
+template <int NB>
+constexpr int mm_tcols() {  // the allocation: a power of two >= 32
+  return mm_acc_cols<NB>() + 64 * mm_astages<NB>() <= 256 ? 256 : 512;
+}
+template <int NB>
+constexpr int mm_smem() {  // the dynamic allocation for B = 0
+  return (int)MM_B_ABS + mm_bstages<NB>() * mm_btile<NB>();
+}
+template <int NB>
+constexpr int mm_per_sm() {  // resident CTAs per SM: shared memory and the 512 tensor-memory columns
+  return std::min(std::min(8, (227 * 1024) / (mm_smem<NB>() + 1024)), 512 / mm_tcols<NB>());
+}
+static_assert(mm_per_sm<1>() == 2 && mm_per_sm<4>() == 2 && mm_per_sm<8>() == 2 && mm_per_sm<16>() == 1,
+              "CTAs per SM");
+// ring slot of (stage, row, half): table row 32 stage + row / 4, free half, 32-byte pair of the row's
+// halves (XOR 16 on odd row quads, so that the 8 lanes of a 16-byte load phase hit 8 bank groups)
+__host__ __device__ constexpr uint32_t mm_ring(int st, int r, int h) {
+  return MM_TAB_ABS + (uint32_t)(st * 32 + r / 4) * 256u + 128u +
+         ((uint32_t)((r & 3) * 32 + h * 16) ^ (uint32_t)(((r >> 2) & 1) * 16));
+}
+// scale-ring slot of (stage, half, row): the 4-byte scale pair, rows of 32 in the free halves of 128 ..
+__host__ __device__ constexpr uint32_t mm_scring(int st, int h, int r) {
+  return MM_TAB_ABS + (uint32_t)(128 + st * 8 + h * 4 + r / 32) * 256u + 128u + (uint32_t)(r % 32) * 4u;
+}
 
 // The B operand of every k-block, made once per call: token b's row of the block as fp16 hi (row 2b) and
 // lo (row 2b + 1) of x_b scaled by its power of two, in the swizzled layout of a 64-column tile, one
 // contiguous block of mm_btile<NB>() bytes per k-block (tokens past the batch are zero).
+// Block kb also writes its columns of xT[c][b] = x_b[c] (fp32, BP tokens per column, zero past the batch),
+// which the sparse kernel reads one kink column at a time.
 template <int NB>
 __global__ void __launch_bounds__(256) hexmm_xconv(const float* __restrict__ x, int B, int C,
-                                                   const unsigned* __restrict__ amax_bits, uint8_t* __restrict__ xs) {
+                                                   const unsigned* __restrict__ amax_bits, uint8_t* __restrict__ xs,
+                                                   float* __restrict__ xT) {
   constexpr int BP = 8 * NB;
   const int kb = blockIdx.x;
   uint8_t* blk = xs + (size_t)kb * mm_btile<NB>();
+  for (int e = threadIdx.x; e < BP * MM_KB; e += 256) {
+    const int c = e / BP, b = e - c * BP;
+    xT[(size_t)(kb * MM_KB + c) * BP + b] = b < B ? x[(size_t)b * C + kb * MM_KB + c] : 0.f;
+  }
   for (int e = threadIdx.x; e < BP * 8; e += 256) {
     const int b = e >> 3, j = e & 7;
     float v[8];
@@ -207,61 +254,178 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// A-operand helpers: tcgen05.mma with A in tensor memory, B by shared-memory descriptor
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+// 16 consecutive 32-bit columns of this thread's tensor-memory lane
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive1(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Decode-table entry of code i: fp16 x (= r0 + r1 / 2, exact) low, fp16 r1 high, from the caller's xy table,
+// which must hold the A2 lattice points (x, r1 sqrt3/2) (checked, as the matvec checks it); codes past the
+// last point decode to (0, 0).  The weights are x * scale and r1 * (scale * sqrt3/2).
+__device__ __forceinline__ uint32_t mm_entry(const float* xy, int n_pts, int i) {
+  if (i >= n_pts) return 0u;
+  const float x = xy[2 * i], y = xy[2 * i + 1];
+  const float r1 = rintf(y * 1.1547005383792515f);
+  const float r0 = x - 0.5f * r1;
+  if (r0 != rintf(r0) || (float)((double)r1 * 0.8660254037844386) != y || fabsf(r0) > 16.f || fabsf(r1) > 16.f) {
+    raise_flag(GSDLQ_FLAG_BAD_TABLE);
+    return 0u;
+  }
+  return pack_h2(x, r1);
+}
+
+// The kink and low-rank terms, stored into y (this initialises y; the dense kernel adds to it).  One warp
+// per weight row, lane = token b, b + 32, ... (up to four chunks of 32): the row's kinks are loaded 32 at
+// a time and broadcast eight at a time, each adds delta * xT[col][b] (the activation loads of the eight
+// kinks and every token chunk issued together); then U[row] . tmp[b] (gsd_cpu_hex2d_matvec's kink loop
+// and gsd_cpu_lowrank_proj's second half, gsd_lq_cpu_engine.c:111-183).
+__global__ void __launch_bounds__(256) hexmm_sparse(const float* __restrict__ xT, int BP, int B, int R, int C,
+                                                    const uint32_t* __restrict__ row_ptr,
+                                                    const uint16_t* __restrict__ kcols,
+                                                    const float* __restrict__ kdel, const uint16_t* __restrict__ U,
+                                                    int k, const float* __restrict__ tmp, float* __restrict__ y) {
+  constexpr int TC = MM_MAXB / 32;  // token chunks
+  __shared__ float tmp_s[MM_MAXB * 17];  // tmp[b][j] at 17 b + j: lane b's reads hit 32 banks
+  for (int i = threadIdx.x; i < B * 16; i += blockDim.x) tmp_s[(i >> 4) * 17 + (i & 15)] = tmp[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= R) return;
+  const uint32_t e0 = row_ptr[row], e1 = row_ptr[row + 1];
+  const int nch = (B + 31) / 32;
+  float acc[TC];
+#pragma unroll
+  for (int t = 0; t < TC; ++t) acc[t] = 0.f;
+  for (uint32_t e = e0; e < e1; e += 32) {
+    const uint32_t my = e + lane;
+    int col = my < e1 ? (int)kcols[my] : 0;
+    float d = my < e1 ? kdel[my] : 0.f;
+    if (col >= C) {  // past the row: the reference rejects the matrix
+      raise_flag(GSDLQ_FLAG_BAD_KINK);
+      col = 0;
+      d = 0.f;
+    }
+    const int n = (int)min(32u, e1 - e);  // the kinks past the row's end have delta 0 and column 0
+    for (int j0 = 0; j0 < n; j0 += 8) {
+      int cj[8];
+      float dv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        cj[j] = __shfl_sync(0xffffffffu, col, j0 + j);
+        dv[j] = __shfl_sync(0xffffffffu, d, j0 + j);
+      }
+#pragma unroll
+      for (int t = 0; t < TC; ++t) {
+        if (t < nch) {
+          const int bb = min(32 * t + lane, BP - 1);
+          float xv[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xv[j] = __ldg(xT + (size_t)cj[j] * BP + bb);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[t] = fmaf(dv[j], xv[j], acc[t]);
+        }
+      }
+    }
+  }
+  float u[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) u[j] = j < k ? h2f(U[(size_t)row * k + j]) : 0.f;
+#pragma unroll
+  for (int t = 0; t < TC; ++t) {
+    const int b = 32 * t + lane;
+    if (t < nch && b < B) {
+      float lrv = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < k) lrv = fmaf(u[j], tmp_s[b * 17 + j], lrv);
+      y[(size_t)b * R + row] = acc[t] + lrv;
+    }
+  }
+}
+
 // NB: groups of 8 tokens (tokens padded to 8 NB with zero activations); N = 16 NB accumulator columns.
-// Thread t decodes half t / 128 of weight row t % 128 (32 columns of each 64-column block); warps 0-3
-// read the accumulator lanes of rows 0-127 at the end.
+// Threads 0-255 decode (thread t: half t / 128 of weight row t % 128, written into tensor-memory lane t % 128
+// by warp t / 32, whose lane quarter is warp % 4); warp 8 issues the MMAs, warp 9 bulk-copies the B tiles.
+constexpr int MM_ALL = MM_THREADS + 64;
 template <int NB>
-__global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const uint8_t* __restrict__ xs, const float* __restrict__ x,
-                                                           int B, const uint8_t* __restrict__ codes,
-                                                           const uint16_t* __restrict__ scales,
-                                                           const float* __restrict__ xy, int n_pts,
-                                                           const uint16_t* __restrict__ U, int k,
-                                                           const uint32_t* __restrict__ row_ptr,
-                                                           const uint16_t* __restrict__ kcols,
-                                                           const float* __restrict__ kdel, float* __restrict__ y,
-                                                           int R, int C, int nsplit, const unsigned* __restrict__ amax_bits,
-                                                           const float* __restrict__ tmp) {
-  constexpr int N = 16 * NB, BP = 8 * NB;
-  constexpr uint32_t TCOLS = (uint32_t)mm_tcols<NB>();
+__global__ void __launch_bounds__(MM_ALL) hexmm_kernel(const uint8_t* __restrict__ xs, int B,
+                                                       const uint8_t* __restrict__ codes,
+                                                       const uint16_t* __restrict__ scales,
+                                                       const float* __restrict__ xy, int n_pts,
+                                                       float* __restrict__ y, int R, int C, int nsplit,
+                                                       const unsigned* __restrict__ amax_bits) {
+  constexpr int N = 16 * NB, BP = 8 * NB, SA = mm_astages<NB>(), SB = mm_bstages<NB>();
+  constexpr uint32_t TCOLS = (uint32_t)mm_tcols<NB>(), ACOL = (uint32_t)mm_acc_cols<NB>();
   constexpr int BTILE = mm_btile<NB>();
   extern __shared__ __align__(1024) uint8_t sm[];
-  float2* tab = reinterpret_cast<float2*>(sm);                    // [0, 2048)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + 2080);       // tensor-memory address
-  float* xsc = reinterpret_cast<float*>(sm + 2096);               // [MM_MAXB] token scales
-  float* s_tmp = reinterpret_cast<float*>(sm + 2608);             // [BP][16] low-rank projections
-  uint8_t* ring = sm + MM_HDR;                                    // code ring: [stage][row][32 bytes]
   const uint32_t sbase = smem_u32(sm);
-  const uint32_t mbar = sbase + 2048, bbar = sbase + 2064;        // MMA-done and B-landed barriers, 2 each
-  // the operand tiles start on a 1024-byte boundary of the shared window (the swizzle atoms' alignment)
-  const uint32_t a_base = (sbase + MM_HDR + MM_CSTAGES * MM_CSTAGE + 1023u) & ~1023u;
-  const uint32_t b_base = a_base + 2 * MM_ATILE;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int lr = tid & (MM_ROWS - 1), half = tid >> 7;  // weight row in the tile, column half of a block
+  if (sbase > MM_HDR_ABS) {  // the layout's assumption on the reserved bytes
+    if (threadIdx.x == 0) raise_flag(GSDLQ_FLAG_UNSUPPORTED);
+    return;
+  }
+  // header: barriers afull[SA] | aempty[SA] | bfull[SB] | bempty[SB] (8 bytes each, 64 apart), the
+  // tensor-memory slot, token scales
+  uint8_t* hdr = sm + (MM_HDR_ABS - sbase);
+  const uint32_t afull = MM_HDR_ABS, aempty = MM_HDR_ABS + 64, bfull = MM_HDR_ABS + 128, bempty = MM_HDR_ABS + 192;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(hdr + 256);
+  float* inv_xsc = reinterpret_cast<float*>(hdr + 512);            // [MM_MAXB]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r0 = blockIdx.x * MM_ROWS, split = blockIdx.y;
   const int NP = C / 2, G = C / 64, nkb = C / MM_KB;
   const int kb0 = (int)((long long)nkb * split / nsplit), kb1 = (int)((long long)nkb * (split + 1) / nsplit);
   const int nk = kb1 - kb0;
+  // scale pairs by cp.async when every row's scales start on a 4-byte boundary
+  const bool sc_async = (G % 2 == 0) && ((reinterpret_cast<uintptr_t>(scales) & 3u) == 0);
+  const int lr = tid & (MM_ROWS - 1), half = (tid >> 7) & 1;
   const int row = r0 + lr;
-  const bool rok = row < R;
+  const bool rok = tid < MM_THREADS && row < R;
   const uint8_t* cp = codes + (size_t)(rok ? row : 0) * NP + half * 16;
   const uint16_t* scp = scales + (size_t)(rok ? row : 0) * G;
-  // this thread's 16 code bytes of k-block kb0 + i into ring stage i % MM_CSTAGES (one group per block,
-  // empty past the run, so that the group count stays uniform)
+  // decoder: this thread's 16 code bytes (and its row's pair of scales) of k-block kb0 + i into ring
+  // stage i % MM_CSTAGES (one group per block, empty past the run, so that the group count stays uniform)
   auto fetch = [&](int i) {
-    if (i < nk && rok) cp_async_16(ring + (i % MM_CSTAGES) * MM_CSTAGE + lr * 32 + half * 16, cp + (kb0 + i) * 32);
+    if (i < nk && rok) {
+      const int st = i % MM_CSTAGES;
+      cp_async_16(sm + (mm_ring(st, lr, half) - sbase), cp + (kb0 + i) * 32);
+      if (sc_async) cp_async_4(sm + (mm_scring(st, half, lr) - sbase), scp + ((kb0 + i) & ~1));
+    }
     cp_async_commit();
   };
+  if (tid < MM_THREADS) {
 #pragma unroll
-  for (int i = 0; i < MM_CSTAGES - 1; ++i) fetch(i);
-
-  for (int i = tid; i < 256; i += MM_THREADS) tab[i] = i < n_pts ? make_float2(xy[2 * i], xy[2 * i + 1]) : make_float2(0.f, 0.f);
-  for (int i = tid; i < BP; i += MM_THREADS) xsc[i] = i < B ? hexmm_xscale(amax_bits[i]) : 0.f;
-  for (int i = tid; i < BP * 16; i += MM_THREADS) s_tmp[i] = (i >> 4) < B ? tmp[i] : 0.f;
+    for (int i = 0; i < MM_CSTAGES - 1; ++i) fetch(i);
+    const uint32_t ent = mm_entry(xy, n_pts, tid);
+#pragma unroll 8
+    for (int i = 0; i < 32; ++i) st_shared_u32(MM_TAB_ABS + (uint32_t)tid * 256u + (uint32_t)((i + tid) & 31) * 4u, ent);
+    if (tid < BP) inv_xsc[tid] = tid < B ? 1.0f / (hexmm_xscale(amax_bits[tid]) * MM_WF) : 0.f;
+  }
   if (tid == 0) {
-    mbar_init(mbar, 1u);
-    mbar_init(mbar + 8u, 1u);
-    mbar_init(bbar, 1u);
-    mbar_init(bbar + 8u, 1u);
+#pragma unroll
+    for (int q = 0; q < SA; ++q) {
+      mbar_init(afull + 8u * q, (uint32_t)MM_THREADS);
+      mbar_init(aempty + 8u * q, 1u);
+    }
+#pragma unroll
+    for (int q = 0; q < SB; ++q) {
+      mbar_init(bfull + 8u * q, 1u);
+      mbar_init(bempty + 8u * q, 1u);
+    }
     mbar_fence_init();
   }
   if (warp == 0) tmem_alloc(smem_u32(tslot), TCOLS);
@@ -270,156 +434,163 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const uint8_t* __rest
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot);
 #ifdef GSDLQ_TRACE
-  // diagnostic builds: CTA blockIdx.x (< 160, run 0) stamps its set-up and its first six k-blocks
-  const bool trc = blockIdx.y == 0 && tid == 0;
-  if (trc) GSDLQ_TR_SET(0u, 0, tr_now());
+  const bool trc = blockIdx.y == 0;
 #endif
 
-  // The row's kinks (CSR, ascending columns) are added to their decoded weights in the A tiles, so the
-  // tensor cores apply them with the lattice part.  e walks the row's list from this run's first column
-  // (found in batches of eight independent loads); (kc, kd) is the kink at e and (kc2, kd2) the one after
-  // it, loaded ahead so that the next block's test does not wait on a load.
-  uint32_t e = rok ? row_ptr[row] : 0u;
-  const uint32_t e_end = rok ? row_ptr[row + 1] : 0u;
-  while (e < e_end) {
-    int c8[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) c8[q] = e + q < e_end ? (int)kcols[e + q] : 0x7fffffff;
-    int below = 0;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) below += c8[q] < kb0 * MM_KB;
-    e += below;
-    if (below < 8) break;
-  }
-  int kc = e < e_end ? (int)kcols[e] : 0x7fffffff;
-  float kd = e < e_end ? kdel[e] : 0.f;
-  int kc2 = e + 1 < e_end ? (int)kcols[e + 1] : 0x7fffffff;
-  float kd2 = e + 1 < e_end ? kdel[e + 1] : 0.f;
-
-  uint16_t sc = (rok && nk > 0) ? scp[kb0] : (uint16_t)0;
-  // instruction descriptor: D fp32, A and B fp16, both K-major, N, M = 128
-  const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(MM_ROWS >> 4) << 24);
-  bool bad = false;
-  for (int i = 0; i < nk; ++i) {
-    const int st = i & 1, kb = kb0 + i;
-    // the MMAs of two blocks ago read this stage's A and B tiles: wait for their commit (bounded)
-    if (i >= 2) mbar_wait_bounded(mbar + 8u * st, (uint32_t)(((i >> 1) - 1) & 1));
-#ifdef GSDLQ_TRACE
-    if (trc && i < 6) GSDLQ_TR_SET(0u, 1 + 4 * i, tr_now());
-#endif
-    if (tid == 0) {  // this block's B tile: one bulk copy from the converted activations
-      mbar_arrive_expect_tx(bbar + 8u * st, (uint32_t)BTILE);
-      bulk_g2s(b_base + st * BTILE, xs + (size_t)kb * BTILE, (uint32_t)BTILE, bbar + 8u * st);
-    }
-    fetch(i + MM_CSTAGES - 1);          // codes of the block MM_CSTAGES - 1 ahead
-    cp_async_wait<MM_CSTAGES - 1>();    // this thread's codes of block i have landed
-    // ---- A: 32 weights of row lr, chunks j = 4 half + jj (weights 8j .. 8j+7 = code bytes 4j .. 4j+3) ----
-    const float s = h2f(sc);
-    const uint4 cw = *reinterpret_cast<const uint4*>(ring + (i % MM_CSTAGES) * MM_CSTAGE + lr * 32 + half * 16);
-    if (rok && i + 1 < nk) sc = scp[kb + 1];
-    const uint32_t cv[4] = {cw.x, cw.y, cw.z, cw.w};
-    uint8_t* atile = sm + (a_base - sbase) + st * MM_ATILE;
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      uint32_t h[4], l[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int code = rok ? (int)((cv[jj] >> (8 * q)) & 0xffu) : 0;
-        bad |= code >= n_pts;
-        const float2 p = tab[code];
-        const float w0 = p.x * s, w1 = p.y * s;  // a3 dequant: one fp32 multiply per weight
-        const __half2 hh = __floats2half2_rn(w0, w1);
-        h[q] = *reinterpret_cast<const uint32_t*>(&hh);
-        l[q] = pack_h2(w0 - __low2float(hh), w1 - __high2float(hh));  // fp16 hi + lo: about 22 bits
+  if (warp == MM_THREADS / 32 + 1) {
+    // ---- B loader: block j's tile into stage j % SB once the MMAs of block j - SB have completed ----
+    if (lane == 0) {
+      int q = 0;
+      uint32_t pe = 1u;  // parity of the empty phase to wait for (none on the first pass)
+      for (int j = 0; j < nk; ++j) {
+        if (j >= SB) mbar_wait_bounded(bempty + 8u * q, pe);
+        mbar_arrive_expect_tx(bfull + 8u * q, (uint32_t)BTILE);
+        bulk_g2s(MM_B_ABS + q * BTILE, xs + (size_t)(kb0 + j) * BTILE, (uint32_t)BTILE, bfull + 8u * q);
+        if (++q == SB) q = 0, pe ^= 1u;
       }
-      *reinterpret_cast<uint4*>(atile + sw128(lr, 4 * half + jj)) = make_uint4(h[0], h[1], h[2], h[3]);
-      *reinterpret_cast<uint4*>(atile + MM_AHALF + sw128(lr, 4 * half + jj)) = make_uint4(l[0], l[1], l[2], l[3]);
     }
-    // the block's kinks in this thread's half: the weight's hi + lo halves plus the delta, split again (a
-    // column repeated in the list gets every delta); kinks of the other half are the other thread's
-    while (kc < (kb + 1) * MM_KB) {
-      const int lc = kc - kb * MM_KB;  // 0 .. 63
-      if ((lc >> 5) == half) {
-        const int off = sw128(lr, lc >> 3) + 2 * (lc & 7);
-        __half* ph = reinterpret_cast<__half*>(atile + off);
-        __half* pl = reinterpret_cast<__half*>(atile + MM_AHALF + off);
-        const float w = (__half2float(*ph) + __half2float(*pl)) + kd;
-        const __half hw = __float2half_rn(w);
-        *ph = hw;
-        *pl = __float2half_rn(w - __half2float(hw));
+  } else if (warp == MM_THREADS / 32) {
+    // ---- issuer ----
+    if (lane == 0) {
+#ifdef GSDLQ_TRACE
+      if (trc) GSDLQ_TR_SET(0u, 21, tr_now());
+#endif
+      // instruction descriptor: D fp32, A and B fp16, both K-major, N, M = 128
+      const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(MM_ROWS >> 4) << 24);
+      int qa = 0, qb = 0;
+      uint32_t pa = 0u, pb = 0u;  // stage indices and their phase parities
+      for (int i = 0; i < nk; ++i) {
+        mbar_wait_bounded(afull + 8u * qa, pa);  // the decoders' A parts of block i
+        mbar_wait_bounded(bfull + 8u * qb, pb);  // its B tile
+        tc_fence_after();
+#ifdef GSDLQ_TRACE
+        if (trc && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 5, tr_now());
+#endif
+#pragma unroll
+        for (int kk = 0; kk < MM_KB / 16; ++kk) {
+          const uint64_t bd = umma_desc(MM_B_ABS + qb * BTILE + kk * 32);
+          const uint32_t aa = tmem + ACOL + 64u * (uint32_t)qa + 8u * (uint32_t)kk;
+          umma_f16_ts(tmem, aa, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tmem, aa + 32u, bd, idesc, 1u);
+        }
+        umma_commit(aempty + 8u * qa);  // arrive when every MMA issued so far has completed
+        umma_commit(bempty + 8u * qb);
+        if (++qa == SA) qa = 0, pa ^= 1u;
+        if (++qb == SB) qb = 0, pb ^= 1u;
+#ifdef GSDLQ_TRACE
+        if (trc && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 6, tr_now());
+#endif
       }
-      ++e;
-      kc = kc2;
-      kd = kd2;
-      kc2 = e + 1 < e_end ? (int)kcols[e + 1] : 0x7fffffff;
-      kd2 = e + 1 < e_end ? kdel[e + 1] : 0.f;
     }
+  } else {
+    // ---- decoders ----
+    const uint32_t lane4 = (uint32_t)lane * 4u;
+    const uint32_t my_lane = (uint32_t)((warp & 3) * 32) << 16;  // this warp's tensor-memory lane quarter
+    uint32_t cmax = 0u;  // byte-wise maximum of the codes seen (the bad-code check)
+    bool bad_scale = false;
+    int q = 0;
+    uint32_t pe = 1u;  // A stage and the parity of its empty phase to wait for (none on the first pass)
+    for (int i = 0; i < nk; ++i) {
+      const int kb = kb0 + i, st = i & (MM_CSTAGES - 1);
 #ifdef GSDLQ_TRACE
-    if (trc && i < 6) GSDLQ_TR_SET(0u, 2 + 4 * i, tr_now());
+      if (trc && tid == 0 && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2), tr_now());
 #endif
-    fence_proxy_async_smem();  // the A tiles' generic stores, visible to the tensor core's reads
-    mbar_wait_bounded(bbar + 8u * st, (uint32_t)((i >> 1) & 1));  // the B tile has landed
+      fetch(i + MM_CSTAGES - 1);          // codes of the block MM_CSTAGES - 1 ahead
+      cp_async_wait<MM_CSTAGES - 1>();    // this thread's codes of block i have landed
 #ifdef GSDLQ_TRACE
-    if (trc && i < 6) GSDLQ_TR_SET(0u, 3 + 4 * i, tr_now());
+      if (trc && tid == 0 && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 1, tr_now());
 #endif
-    __syncthreads();
-    if (tid == 0) {
+      uint32_t scw;
+      if (sc_async) {
+        scw = ld_shared_u32(mm_scring(st, half, lr));
+        scw = (kb & 1) ? scw >> 16 : scw & 0xffffu;
+      } else {
+        scw = rok ? scp[kb] : 0u;
+      }
+      // W = (x, r1) * (scale, scale sqrt3/2) in fp16 hi + lo parts, computed in fp16 arithmetic: hi is the
+      // rounded product, lo the rounded remainder (one fused multiply-add each: exact before rounding), and
+      // the y part's factor scale sqrt3/2 (not an fp16 number) enters as its own fp16 hi + lo pair
+      // The weights carry the factor MM_WF = 2^10 (removed in the epilogue), which keeps the lo parts of
+      // weights above 2^-12 normal; |lattice x| <= 12, so scales up to 4.8 stay below fp16's 65504.
+      const float s = h2f((uint16_t)scw) * MM_WF, sy = s * 0.8660254037844386f;
+      if (!(fabsf(s) <= 5.0f * MM_WF)) bad_scale = true;
+      const __half syh = __float2half_rn(sy);
+      const __half syl = __float2half_rn(sy - __half2float(syh));
+      const __half2 sc2 = __halves2half2(__float2half_rn(s), syh);
+      const __half2 sl2 = __halves2half2(__float2half_rn(0.f), syl);
+      const uint4 cw = *reinterpret_cast<const uint4*>(sm + (mm_ring(st, lr, half) - sbase));
+      const uint32_t cv[4] = {cw.x, cw.y, cw.z, cw.w};
+      uint32_t hi[16], lo[16];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        cmax = __vmaxu4(cmax, cv[jj]);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          // one byte permute makes (code << 8) | lane * 4, the entry of this lane's table copy
+          const uint32_t ent = mm_lookup(cv[jj], lane4, 0x6604u | (uint32_t)(p << 4));
+          const __half2 v = *reinterpret_cast<const __half2*>(&ent);
+          const __half2 h = __hmul2(v, sc2);
+          __half2 l = __hfma2(v, sc2, __hneg2(h));
+          l = __hfma2(v, sl2, l);
+          hi[4 * jj + p] = *reinterpret_cast<const uint32_t*>(&h);
+          lo[4 * jj + p] = *reinterpret_cast<const uint32_t*>(&l);
+        }
+      }
+#ifdef GSDLQ_TRACE
+      if (trc && tid == 0 && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 2, (unsigned long long)hi[15] * 0ull + tr_now());
+#endif
+      // stage q is free once the MMAs of block i - SA have completed
+      if (i >= SA) mbar_wait_bounded(aempty + 8u * q, pe);
       tc_fence_after();
-#pragma unroll
-      for (int kk = 0; kk < MM_KB / 16; ++kk) {
-        const uint64_t bd = umma_desc(b_base + st * BTILE + kk * 32);
-        umma_f16(tmem, umma_desc(a_base + st * MM_ATILE + kk * 32), bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-        umma_f16(tmem, umma_desc(a_base + st * MM_ATILE + MM_AHALF + kk * 32), bd, idesc, 1u);
-      }
-      umma_commit(mbar + 8u * st);  // arrives when every MMA issued so far has completed
 #ifdef GSDLQ_TRACE
-      if (trc && i < 6) GSDLQ_TR_SET(0u, 4 + 4 * i, tr_now());
+      if (trc && tid == 0 && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 3, tr_now());
+#endif
+      __syncwarp();
+      const uint32_t acol = tmem + my_lane + ACOL + 64u * (uint32_t)q + 16u * (uint32_t)half;
+      tmem_st16(acol, hi);
+      tmem_st16(acol + 32u, lo);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive1(afull + 8u * q);
+      if (++q == SA) q = 0, pe ^= 1u;
+#ifdef GSDLQ_TRACE
+      if (trc && tid == 0 && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 4, tr_now());
 #endif
     }
-  }
-  cp_async_wait<0>();
-  if (bad) raise_flag(GSDLQ_FLAG_BAD_CODE);
-  // a kink past the last column is never applied: the run that ends the row reports it
-  if (kb1 == nkb && half == 0 && e < e_end) raise_flag(GSDLQ_FLAG_BAD_KINK);
-#ifdef GSDLQ_TRACE
-  if (trc) GSDLQ_TR_SET(0u, 25, tr_now());
-#endif
-  // ---- the run's partial sums: warps 0-3, lane = row; columns 2b, 2b + 1 = token b's hi and lo parts; the
-  // low-rank term U[row] . tmp[b] is added once per (row, token), by the run whose index is b mod nsplit ----
-  if (nk > 0 && warp < 4) {
-    float u[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) u[j] = (rok && j < k) ? h2f(U[(size_t)row * k + j]) : 0.f;
-    mbar_wait_bounded(mbar + 8u * ((nk - 1) & 1), (uint32_t)(((nk - 1) >> 1) & 1));
+    cp_async_wait<0>();
+    {  // a code byte >= n_pts has no point in the table
+      const uint32_t mx = max(max(cmax & 0xffu, (cmax >> 8) & 0xffu), max((cmax >> 16) & 0xffu, cmax >> 24));
+      if (rok && (int)mx >= n_pts) raise_flag(GSDLQ_FLAG_BAD_CODE);
+      if (rok && bad_scale) raise_flag(GSDLQ_FLAG_RANGE);
+    }
+    // ---- the run's partial sums: column pair (2b, 2b + 1) = token b's hi and lo parts; warp w reads the
+    // lanes of its quarter, the 16-column groups cb with cb % 2 == w / 4 ----
+    mbar_wait_bounded(aempty + 8u * ((nk - 1) % SA), (uint32_t)(((nk - 1) / SA) & 1));
     tc_fence_after();
+    __syncwarp();
+#ifdef GSDLQ_TRACE
+    if (trc && tid == 0) GSDLQ_TR_SET(0u, 25, tr_now());
+#endif
+    const int erow = r0 + (warp & 3) * 32 + lane;
 #pragma unroll 1
-    for (int cb = 0; cb < N / 16; ++cb) {
+    for (int cb = warp >> 2; cb < N / 16; cb += 2) {
       uint32_t v[16];
-      tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(cb * 16), v);
+      tmem_ld16(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(cb * 16), v);
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         const int b = cb * 8 + t;
-        if (rok && b < B) {
-          float val = (__uint_as_float(v[2 * t]) + __uint_as_float(v[2 * t + 1])) / xsc[b];
-          if (b % nsplit == split) {
-            float lrv = 0.f;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) lrv = fmaf(u[j], s_tmp[b * 16 + j], lrv);
-            val += lrv;
-          }
-          atomicAdd(y + (size_t)b * R + row, val);
-        }
+        if (erow < R && b < B)
+          atomicAdd(y + (size_t)b * R + erow, (__uint_as_float(v[2 * t]) + __uint_as_float(v[2 * t + 1])) * inv_xsc[b]);  // includes 1 / MM_WF
       }
     }
-  }
 #ifdef GSDLQ_TRACE
-  if (trc) GSDLQ_TR_SET(0u, 26, tr_now());
-  if (trc) {
-    GSDLQ_TR_SET(0u, 27, tr_now());
-    GSDLQ_TR_SET(0u, 28, (unsigned long long)nk);
-  }
+    if (trc && tid == 0) {
+      GSDLQ_TR_SET(0u, 26, tr_now());
+      GSDLQ_TR_SET(0u, 28, (unsigned long long)nk);
+    }
 #endif
-  // ---- release the tensor memory (every warp's loads are complete) ----
+  }
+  // ---- release the tensor memory (every warp's tensor-memory accesses are complete) ----
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -428,12 +599,13 @@ __global__ void __launch_bounds__(MM_THREADS) hexmm_kernel(const uint8_t* __rest
   }
 }
 
-// The work buffer: per-token maxima ([0, 512)), per-token low-rank projections ([512, 8704)), and from
-// MM_XS_OFF the converted activations, one B tile per k-block.
+// The work buffer: per-token maxima ([0, 512)), per-token low-rank projections ([512, 8704)), from
+// MM_XS_OFF the converted activations (one B tile per k-block), then the transposed fp32 activations.
 constexpr size_t MM_XS_OFF = 16384;
+inline size_t mm_xs_bytes(int nb, int cols) { return (size_t)(cols / MM_KB) * (size_t)(16 * nb * 128); }
 inline size_t mm_work_bytes(int batch, int cols) {
   const int nb = (batch + 7) / 8;
-  return MM_XS_OFF + (size_t)(cols / MM_KB) * (size_t)(16 * nb * 128);
+  return MM_XS_OFF + mm_xs_bytes(nb, cols) + sizeof(float) * (size_t)cols * 8 * nb;
 }
 
 template <int NB>
@@ -450,15 +622,24 @@ static cudaError_t hexmm_launch_nb(int tiles, int nkb, cudaStream_t s, uint8_t* 
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  hexmm_xconv<NB><<<nkb, 256, 0, s>>>(x, B, C, amax, xs);
+  float* xT = reinterpret_cast<float*>(xs + mm_xs_bytes(NB, C));
+  hexmm_xconv<NB><<<nkb, 256, 0, s>>>(x, B, C, amax, xs, xT);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  // k-runs per row tile: the CTAs that fit an SM at once (shared memory) on every SM, at least one
-  // k-block each
-  const int per_sm = std::max(1, std::min(8, (227 * 1024) / smem));
-  const int nsplit = std::max(1, std::min(nkb, (per_sm * num_sms() + tiles - 1) / tiles));
-  hexmm_kernel<NB><<<dim3(tiles, nsplit), MM_THREADS, smem, s>>>(xs, x, B, codes, scales, xy, n_pts, U, k, rp, kc, kd,
-                                                                 y, R, C, nsplit, amax, tmp);
+  hexmm_sparse<<<(R + 7) / 8, 256, 0, s>>>(xT, 8 * NB, B, R, C, rp, kc, kd, U, k, tmp, y);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // k-runs per row tile: the split that minimises (waves of resident CTAs) x (k-blocks per run + the
+  // set-up and epilogue, about two blocks' worth)
+  const int slots = mm_per_sm<NB>() * num_sms();
+  int nsplit = 1;
+  long long best = -1;
+  for (int ns = 1; ns <= std::min(nkb, 64); ++ns) {
+    const long long cost = (long long)((tiles * ns + slots - 1) / slots) * ((nkb + ns - 1) / ns + 2);
+    if (best < 0 || cost < best) best = cost, nsplit = ns;
+  }
+  hexmm_kernel<NB><<<dim3(tiles, nsplit), MM_ALL, smem, s>>>(xs, B, codes, scales, xy, n_pts, y, R, C, nsplit,
+                                                                      amax);
   return cudaGetLastError();
 }
 
@@ -485,8 +666,8 @@ extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* code
   if (k_dim < 0 || k_dim > 16 || (k_dim > 0 && (!U || !S || !Vt))) return GSDLQ_ERR_INVALID;
   if (n_pts < 1 || n_pts > 256) return GSDLQ_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(codes) & 15u) return GSDLQ_ERR_INVALID;  // 16-byte code loads
-  if ((reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(U) | reinterpret_cast<uintptr_t>(Vt)) & 1u)
-    return GSDLQ_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(U)) & 1u) return GSDLQ_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(Vt) & 15u) return GSDLQ_ERR_INVALID;  // 16-byte loads of Vt rows
   if (reinterpret_cast<uintptr_t>(x) & 15u) return GSDLQ_ERR_INVALID;  // 16-byte activation loads
   if ((reinterpret_cast<uintptr_t>(y) & 3u) || (reinterpret_cast<uintptr_t>(work) & 1023u)) return GSDLQ_ERR_INVALID;
   if (work_bytes < mm_work_bytes(batch, cols)) return GSDLQ_ERR_INVALID;
@@ -494,10 +675,10 @@ extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* code
   unsigned* amax = reinterpret_cast<unsigned*>(work);  // per-token max|x| (bits)
   float* tmp = reinterpret_cast<float*>(work) + MM_MAXB;
   uint8_t* xs = static_cast<uint8_t*>(work) + MM_XS_OFF;  // converted activations
-  cudaError_t e = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)batch * rows, s);
-  if (e == cudaSuccess) e = cudaMemsetAsync(work, 0, sizeof(float) * 17 * MM_MAXB, s);
+  cudaError_t e = cudaMemsetAsync(work, 0, sizeof(float) * 17 * MM_MAXB, s);
   if (e != cudaSuccess) return record_cuda_error(e);
-  hexmm_prep<<<dim3(batch, (cols + MM_PREP - 1) / MM_PREP), 256, 0, s>>>(x, cols, Vt, S, k_dim, amax, tmp);
+  hexmm_prep<<<dim3((batch + 7) / 8, (cols + MM_PREP - 1) / MM_PREP), 256, 0, s>>>(x, batch, cols, Vt, S, k_dim, amax,
+                                                                                  tmp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return record_cuda_error(e);
   const int tiles = (rows + MM_ROWS - 1) / MM_ROWS, nkb = cols / MM_KB;

@@ -45,7 +45,8 @@ extern "C" {
 #define GSDLQ_FLAG_TIMEOUT 0x10u   /* a bounded device-side wait gave up */
 #define GSDLQ_FLAG_BAD_TOKEN 0x20u /* token id >= vocab: embedding row skipped */
 #define GSDLQ_FLAG_UNSUPPORTED 0x40u /* a kernel found a device limit it was not built for and did nothing */
-#define GSDLQ_FLAG_RANGE 0x80u     /* a low-rank partial sum left the +-2^22 fixed-point range (clamped) */
+#define GSDLQ_FLAG_RANGE 0x80u     /* a low-rank partial sum left the +-2^22 fixed-point range (clamped), or
+                                      a scale above 5 reached the batched linear's fp16 weight parts */
 
 typedef void *gsdlq_stream_t;
 
@@ -332,14 +333,16 @@ int gsdlq_rope_table(float *table, int max_seq, int head_dim, float rope_theta);
 /* ---- Batched packed linear (B tokens) ---------------------------------------------------------
  * y[b] = gsd_cpu_hex2d_matvec(gsd_cpu_lowrank_proj(x[b])) for b < batch (gsd_lq_cpu_engine.c:111-183
  * applied to each token), as one dequant-GEMM on the tcgen05 tensor cores (accumulators in tensor
- * memory): the codes are decoded once per launch for all tokens.  x: [batch][cols] fp32, 16-byte
- * aligned; y: [batch][rows] fp32 (zeroed here, then accumulated); work: device scratch of at least
- * gsdlq_hex2d_matmul_work_size(batch, cols) bytes, 1024-byte aligned (per-token maxima and low-rank
- * projections, and the activations converted once into the tensor cores' operand layout).
- * 1 <= batch <= GSDLQ_MATMUL_MAX_BATCH, cols a multiple of 64 and at most 65535, k_dim <= 16,
- * n_pts <= 256, codes 16-byte aligned.  Weights and activations enter the tensor cores as fp16
- * hi + lo parts (about 22 significant bits): results match the per-token matvec to about 1e-6
- * relative.  The partial sums are added with atomics, so the last bits may differ between runs. */
+ * memory): the codes are decoded once per launch for all tokens; the kink and low-rank terms are
+ * added in fp32 by a separate sparse pass.  x: [batch][cols] fp32, 16-byte aligned; y: [batch][rows]
+ * fp32 (written here); work: device scratch of at least gsdlq_hex2d_matmul_work_size(batch, cols)
+ * bytes, 1024-byte aligned (per-token maxima and low-rank projections, and the activations converted
+ * once into the tensor cores' operand layout and transposed).  1 <= batch <= GSDLQ_MATMUL_MAX_BATCH,
+ * cols a multiple of 64 and at most 65535, k_dim <= 16, n_pts <= 256, codes and Vt 16-byte aligned,
+ * xy_table the A2 lattice points (as the matvec requires), scales at most 5 (GSDLQ_FLAG_RANGE
+ * otherwise).  Weights and activations enter the tensor cores as fp16 hi + lo parts (about 22
+ * significant bits): results match the per-token matvec to about 1e-6 relative.  The partial sums
+ * are added with atomics, so the last bits may differ between runs. */
 #define GSDLQ_MATMUL_MAX_BATCH 128
 int gsdlq_hex2d_matmul_work_size(int batch, int cols, size_t *bytes);
 int gsdlq_hex2d_matmul(const float *x, int batch, const uint8_t *codes, const uint16_t *scales,
