@@ -88,6 +88,9 @@ SIGNATURES = {
     "gsdlq_attention": ([ctypes.POINTER(AttnJob), vp], i32),
     "gsdlq_rope_table": ([vp, i32, i32, f32], i32),
     "gsdlq_greedy_advance": ([vp, vp, vp, vp, vp, i32, vp], i32),
+    "gsdlq_advance_eos": ([vp, vp, vp, vp, vp, i32, i32, vp, vp], i32),
+    "gsdlq_sample_work_size": ([i32, szp], i32),
+    "gsdlq_sample_top_p": ([vp, i32, f32, f32, vp, vp, vp, ctypes.c_size_t, vp, vp, vp], i32),
     "gsdlq_unit_kinks": ([vp, vp, vp, i32, i32, vp, vp, vp], i32),
     "gsdlq_decode_plan_create": ([ctypes.POINTER(DecodeDesc), ctypes.POINTER(vp)], i32),
     "gsdlq_decode_step": ([vp, vp], i32),

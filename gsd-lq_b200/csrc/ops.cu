@@ -378,6 +378,27 @@ __global__ void greedy_advance_kernel(unsigned long long* key, int* token, int* 
   *key = 0ull;
 }
 
+// gsdlq_greedy_advance with the reference chat loop's EOS stop (run_gpu_native_chat.py:1142-1144): once
+// the picked token is eos_id, *done is set and nothing more advances (the EOS token is not stored)
+__global__ void advance_eos_kernel(unsigned long long* key, int* token, int* pos, int* step, int* out_ids, int max_out,
+                                   int eos_id, int* done) {
+  if (*done) {
+    *key = 0ull;
+    return;
+  }
+  const unsigned long long k = *key;
+  const int t = (int)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
+  *key = 0ull;
+  if (t == eos_id) {
+    *done = 1;
+    return;
+  }
+  *token = t;
+  if (out_ids != nullptr && *step < max_out) out_ids[*step] = t;
+  *step += 1;
+  *pos += 1;
+}
+
 static int host_codebook(int radius, float* xy, int max_pts) {
   if (radius < 1 || radius > 8) return GSDLQ_ERR_INVALID;
   const double h = std::sqrt(3.0) / 2.0;
@@ -601,6 +622,15 @@ int gsdlq_dequant(const uint8_t* codes, const uint16_t* scales, const float* xy_
 int gsdlq_argmax(const float* logits, int n, int* out_index, gsdlq_stream_t stream) {
   if (!logits || !out_index || n <= 0) return GSDLQ_ERR_INVALID;
   argmax_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(logits, n, out_index);
+  GSDLQ_CUDA_CHECK_LAUNCH();
+  return GSDLQ_OK;
+}
+
+int gsdlq_advance_eos(unsigned long long* argmax_key, int* token, int* pos, int* step, int* out_ids, int max_out,
+                      int eos_id, int* done, gsdlq_stream_t stream) {
+  if (!argmax_key || !token || !pos || !step || !done) return GSDLQ_ERR_INVALID;
+  advance_eos_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(argmax_key, token, pos, step, out_ids, max_out,
+                                                                     eos_id, done);
   GSDLQ_CUDA_CHECK_LAUNCH();
   return GSDLQ_OK;
 }

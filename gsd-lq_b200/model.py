@@ -408,12 +408,16 @@ class GSDLQModel:
             # eager warm-up (sets kernel attributes and NCCL state outside capture); the step's
             # device-side bookkeeping (token, pos, greedy key) is restored so that the warm-up
             # leaves no trace and the replay that follows does the real work
-            saved = (self.state.clone(), self.key.clone(), self.out_ids.clone())
+            smp = getattr(self, "_smp", None)
+            saved = (self.state.clone(), self.key.clone(), self.out_ids.clone(),
+                     smp["done"].clone() if smp is not None else None)
             fn()
             torch.cuda.synchronize(self.device)
             self.state.copy_(saved[0])
             self.key.copy_(saved[1])
             self.out_ids.copy_(saved[2])
+            if smp is not None:
+                smp["done"].copy_(saved[3])
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 fn()
@@ -471,10 +475,48 @@ class GSDLQModel:
         cp = np.cumsum(p[idx])
         cut = int(np.argmax(cp > top_p)) + 1
         top, pt = idx[:cut], p[idx[:cut]]
-        pt = pt / pt.sum()
+        ps = pt.sum()
+        if ps <= 0 or np.isnan(ps):  # the reference's p_sum guard (gsd_lq_cpu_runtime.py:439-441)
+            return int(top[0])
+        pt = pt / ps
         return int(np.random.choice(top, p=pt))
 
+    def sample_device(self, temperature: float = 0.0, top_p: float = 0.9, u: float | None = None) -> int:
+        """sample_token on the device over the last step's logits (gsdlq_sample_top_p).  u: the uniform
+        draw np.random.choice would make; by default np.random.random_sample(), taken only when
+        temperature > 0 (the reference draws only then), so that picks follow the reference's under the
+        same NumPy seed."""
+        if self.tp is not None:
+            raise NotImplementedError("device sampling needs the whole vocabulary on one GPU; under tensor "
+                                      "parallelism use sample_token(logits_host())")
+        if u is None:
+            u = float(np.random.random_sample()) if temperature > 0.0 else 0.0
+        sb = self._sample_bufs()
+        sb["u"][0] = u
+        L.check(L.load().gsdlq_sample_top_p(self.logits.data_ptr(), self.vocab_local, float(temperature), float(top_p),
+                                            sb["u"].data_ptr(), None, sb["work"].data_ptr(), sb["work"].numel(),
+                                            None, sb["index"].data_ptr(), ops.stream_handle()), "gsdlq_sample_top_p")
+        return int(sb["index"].item())
+
+    def _sample_bufs(self):
+        b = getattr(self, "_smp", None)
+        if b is None:
+            n = ctypes.c_size_t()
+            L.check(L.load().gsdlq_sample_work_size(self.vocab_local, ctypes.byref(n)), "gsdlq_sample_work_size")
+            b = {"work": torch.zeros(int(n.value), dtype=torch.uint8, device=self.device),
+                 "u": torch.zeros(self.max_seq, dtype=torch.float64, device=self.device),
+                 "index": torch.zeros(1, dtype=torch.int32, device=self.device),
+                 "done": torch.zeros(1, dtype=torch.int32, device=self.device)}
+            self._smp = b
+        return b
+
     PREFILL_CHUNK = 128  # tokens per chunk of batched prefill (the dequant-GEMM's largest batch)
+
+    @property
+    def batched_prefill_supported(self) -> bool:
+        """The chunk kernels' shape limits: head_dim 64 or 128 (gsdlq_attention_rows), at most 8 query heads
+        per kv head."""
+        return self.head_dim in (64, 128) and self.n_heads_local // self.n_kv_local <= 8
 
     def prefill(self, ids, start_pos: int = 0, batched: bool | None = None):
         """Fill the KV cache for ``ids`` at positions start_pos.. (no logits).
@@ -482,10 +524,11 @@ class GSDLQModel:
         Batched (default on one GPU): chunks of up to 128 tokens, every packed linear as one tensor-core
         dequant-GEMM over the chunk, causal attention over the chunk's rows.  Token by token (as the
         reference does, run_gpu_native_chat.py:1128-1131) with batched=False, under tensor parallelism,
-        or with GSDLQ_PREFILL=token."""
+        for shapes outside batched_prefill_supported, or with GSDLQ_PREFILL=token."""
         ids = [int(t) for t in ids]
         if batched is None:
-            batched = self.tp is None and os.environ.get("GSDLQ_PREFILL", "batched") != "token"
+            batched = (self.tp is None and os.environ.get("GSDLQ_PREFILL", "batched") != "token"
+                       and self.batched_prefill_supported)
         if not batched:
             for i, t in enumerate(ids):
                 self.set_state(t, start_pos + i)
@@ -550,19 +593,64 @@ class GSDLQModel:
             mm(b["g"], p + "ffn_down.weight", b["o"])
             L.check(lib.gsdlq_vec_add(x.data_ptr(), x.data_ptr(), b["o"].data_ptr(), n * H, sh), "gsdlq_vec_add")
 
-    def generate(self, prompt_ids, max_new_tokens: int) -> list[int]:
-        """Greedy generation with the loop on the device: one graph replay per token, one D2H at the end.
+    def generate(self, prompt_ids, max_new_tokens: int, temperature: float = 0.0, top_p: float = 0.9,
+                 eos_id: int | None = None, check_every: int = 16) -> list[int]:
+        """Generation with the loop on the device: one graph replay per token (layers, LM head, then the
+        pick and the bookkeeping), no host round trip per token.
 
-        Returns the generated ids (the reference's greedy smoke loop, run_gpu_native_chat.py:1039-1055,
-        without the EOS stop, which would need a host round trip per token)."""
+        temperature <= 0: greedy (the reference's smoke loop, run_gpu_native_chat.py:1039-1055); else
+        temperature + top-p picks on the device with the reference's rules (sample_token,
+        gsd_lq_cpu_runtime.py:422-443), one np.random.random_sample() draw per token taken up front,
+        which is the sequence the reference's np.random.choice calls would consume.  eos_id: stop when
+        the pick is eos_id, without returning it (the reference chat loop, run_gpu_native_chat.py:
+        1142-1144); the host looks at the device's done flag every check_every tokens and the steps
+        after the stop do no more bookkeeping."""
         ids = list(prompt_ids)
         if len(ids) + max_new_tokens > self.max_seq:
             raise ValueError("prompt + new tokens exceed max_seq")
+        sampled = temperature > 0.0
+        if sampled and self.tp is not None:
+            raise NotImplementedError("device sampling needs the whole vocabulary on one GPU")
         self.prefill(ids[:-1])
         self.set_state(ids[-1], len(ids) - 1)
-        for _ in range(max_new_tokens):
-            self.step(with_head=True)   # the head's advance kernel feeds the next replay
-        return self.out_ids[:max_new_tokens].cpu().tolist()
+        if not sampled and eos_id is None:
+            for _ in range(max_new_tokens):
+                self.step(with_head=True)   # the head's advance kernel feeds the next replay
+            return self.out_ids[:max_new_tokens].cpu().tolist()
+        sb = self._sample_bufs()
+        if sampled:
+            sb["u"][:max_new_tokens].copy_(torch.from_numpy(np.random.random_sample(max_new_tokens)))
+        sb["done"].zero_()
+        eos = -1 if eos_id is None else int(eos_id)
+        name = f"head_gen_{float(temperature)!r}_{float(top_p)!r}_{eos}"
+
+        def run_head_gen():
+            lib, st = L.load(), self.state.data_ptr()
+            self.linear(self.head_job)
+            if sampled:
+                L.check(lib.gsdlq_sample_top_p(self.logits.data_ptr(), self.vocab_local, float(temperature),
+                                               float(top_p), sb["u"].data_ptr(), st + 8, sb["work"].data_ptr(),
+                                               sb["work"].numel(), self.key.data_ptr(), None, ops.stream_handle()),
+                        "gsdlq_sample_top_p")
+            L.check(lib.gsdlq_advance_eos(self.key.data_ptr(), st, st + 4, st + 8, self.out_ids.data_ptr(),
+                                          self.out_ids.numel(), eos, sb["done"].data_ptr(), ops.stream_handle()),
+                    "gsdlq_advance_eos")
+
+        for i in range(max_new_tokens):
+            if self._plans:
+                L.check(L.load().gsdlq_decode_step(self._plans["layers"], ops.stream_handle()), "gsdlq_decode_step")
+            elif self.use_graph:
+                self._graph("layers", self._run_layers).replay()
+            else:
+                self._run_layers()
+            if self.use_graph:
+                self._graph(name, run_head_gen).replay()
+            else:
+                run_head_gen()
+            if eos_id is not None and (i + 1) % check_every == 0 and int(sb["done"].item()):
+                break
+        n = int(self.state[2].item())
+        return self.out_ids[:n].cpu().tolist()
 
     def release(self):
         self._graphs.clear()

@@ -179,6 +179,19 @@ def hex2d_matmul(x, h: DeviceHex, xy_table, y, work):
             "hex2d_matmul")
 
 
+def sample_top_p(logits: torch.Tensor, temperature: float, top_p: float, u: float) -> int:
+    """gsdlq_sample_top_p over a device logits vector with the uniform draw u; returns the pick."""
+    n = logits.numel()
+    b = ctypes.c_size_t()
+    L.check(_lib().gsdlq_sample_work_size(n, ctypes.byref(b)), "sample_work_size")
+    work = torch.empty(int(b.value), dtype=torch.uint8, device=logits.device)
+    ud = torch.tensor([u], dtype=torch.float64, device=logits.device)
+    out = torch.full((1,), -2, dtype=torch.int32, device=logits.device)
+    L.check(_lib().gsdlq_sample_top_p(ptr(logits), n, float(temperature), float(top_p), ptr(ud), None, ptr(work),
+                                      work.numel(), None, ptr(out), stream_handle()), "sample_top_p")
+    return int(out.item())
+
+
 def attention_rows_work(n: int, n_heads: int, head_dim: int, device="cuda") -> torch.Tensor:
     """Scratch for gsdlq_attention_rows of up to ``n`` tokens (float32; torch's allocations are 16-byte
     aligned)."""

@@ -325,6 +325,32 @@ int gsdlq_attention(const gsdlq_attn_job_t *job, gsdlq_stream_t stream);
 int gsdlq_greedy_advance(unsigned long long *argmax_key, int *token, int *pos, int *step, int *out_ids,
                          int max_out, gsdlq_stream_t stream);
 
+/* gsdlq_greedy_advance with an EOS stop (the reference chat loop, run_gpu_native_chat.py:1142-1144):
+ * when the picked token equals eos_id, *done is set to 1 and token, pos, step and out_ids stay as
+ * they are (the EOS token is not stored); while *done is set, calls only clear *argmax_key.
+ * eos_id < 0: no stop. */
+int gsdlq_advance_eos(unsigned long long *argmax_key, int *token, int *pos, int *step, int *out_ids, int max_out,
+                      int eos_id, int *done, gsdlq_stream_t stream);
+
+/* ---- Temperature + top-p sampling (gsd_lq_cpu_runtime.py:422-443, sample_token) ------------------
+ * One pick from logits[n] (device) with the reference's rules: NaN -> -1e4, +-inf -> 100 / -1e4;
+ * greedy argmax when temperature <= 0; p = softmax(logits / max(temperature, 1e-4)); the nucleus is
+ * the descending-order prefix up to and including the first entry whose running sum exceeds top_p
+ * (the top entry alone when none does); the pick is the first nucleus entry whose running share of
+ * the nucleus exceeds the uniform draw u in [0, 1) -- the draw np.random.choice makes
+ * (np.random.random_sample()), so that picks match the reference's under the same NumPy seed.
+ * u: device double; u_index: NULL (u[0]) or a device int selecting u[*u_index] (the decode step, for a
+ * captured loop).  Writes *out_index and / or *argmax_key (in the greedy-argmax key format, so that
+ * gsdlq_greedy_advance / gsdlq_advance_eos take the pick).  work: n floats of device scratch.
+ * Running sums are exact here (2^-56 fixed point) and rounded in the reference: picks agree except
+ * where a target lies within rounding distance of a running sum (top_p >= 1 is one such case), and
+ * equal probabilities are taken in ascending index order (NumPy's argsort order for them is
+ * unspecified). */
+int gsdlq_sample_work_size(int n, size_t *bytes);
+int gsdlq_sample_top_p(const float *logits, int n, float temperature, float top_p, const double *u,
+                       const int *u_index, void *work, size_t work_bytes, unsigned long long *argmax_key,
+                       int *out_index, gsdlq_stream_t stream);
+
 /* HOST function: (cos, sin) of the RoPE angles for positions [0, max_seq) into
  * table (host, max_seq*head_dim floats), computed with the reference's formula
  * (gsd_lq_cpu_engine.c:215-218) so that rotations match it bit for bit. */
