@@ -52,11 +52,17 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ x, const float* __
 
 // one CTA per token: interleaved pairs (2i, 2i+1) of every q and k head rotated by (cos, sin) of the
 // token's position; k (rotated) and v stored as fp16 at [layer][pos][kv head][dim]
+// With pos_dev (batched decode): row t is sequence t, at position pos_dev[t], with its own cache at
+// seq_stride elements after the previous sequence's.
 __global__ void rope_kv_rows_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                                     uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
                                     const float2* __restrict__ cs, int layer, int pos0, int n_heads, int n_kv, int hd,
-                                    int max_seq) {
-  const int t = blockIdx.x, pos = pos0 + t, half = hd / 2;
+                                    int max_seq, const int* __restrict__ pos_dev, size_t seq_stride) {
+  const int t = blockIdx.x, pos = pos_dev ? pos_dev[t] : pos0 + t, half = hd / 2;
+  if (pos_dev) {
+    kc += (size_t)t * seq_stride;
+    vc += (size_t)t * seq_stride;
+  }
   if (pos < 0 || pos >= max_seq) {
     if (threadIdx.x == 0) raise_flag(GSDLQ_FLAG_BAD_POS);
     return;
@@ -294,6 +300,189 @@ __global__ void attention_combine_kernel(const float* __restrict__ work, float* 
   out[row * hd + threadIdx.x] = a / l;
 }
 
+// Batched decode attention: sequence b's one query token (at position pos[b], its K/V already appended)
+// over positions 0 .. pos[b] of its own cache.  CTA (sequence b, kv head g, split z), 4 warps; the split
+// covers a contiguous range of 32-position tiles, dealt to the warps in turn.  Lane j of a warp scores
+// position 32 tile + j against the GQ query heads (its K row read whole, q from shared memory), the
+// warp keeps each head's running max and sum (online softmax), and the P.V step runs lanes over head
+// dimensions (HD / 32 each) with each position's weight broadcast, reading V rows whole.  The warps'
+// partials merge in shared memory; with splits > 1 the CTA writes its unnormalised rows and (max, sum)
+// for attention_combine_kernel, as gsdlq_attention_rows does.
+constexpr int AD_THREADS = 128;
+template <int HD, int GQ>
+__global__ void __launch_bounds__(AD_THREADS)
+    attention_decode_kernel(const float* __restrict__ q, const uint16_t* __restrict__ kc,
+                            const uint16_t* __restrict__ vc, size_t seq_stride, float* __restrict__ out,
+                            float* __restrict__ work, int layer, const int* __restrict__ pos, int B, int n_heads,
+                            int n_kv, int max_seq, float sm_scale, int splits) {
+  constexpr int DL = HD / 32;  // dimensions per lane in the P.V step
+  __shared__ float qs[GQ][HD];
+  __shared__ float wm[4][GQ], wl[4][GQ];
+  __shared__ float wacc[4][GQ][HD];
+  const int b = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int p_last = pos[b];
+  const bool ok = p_last >= 0 && p_last < max_seq;
+  if (!ok && tid == 0) raise_flag(GSDLQ_FLAG_BAD_POS);
+  const int len = ok ? p_last + 1 : 0;
+  const float* qb = q + ((size_t)b * n_heads + (size_t)g * GQ) * HD;
+  for (int e = tid; e < GQ * HD; e += AD_THREADS) qs[e / HD][e % HD] = qb[e] * sm_scale;
+  __syncthreads();
+  const size_t stride = (size_t)n_kv * HD;
+  const uint16_t* kl = kc + (size_t)b * seq_stride + (size_t)layer * max_seq * stride + (size_t)g * HD;
+  const uint16_t* vl = vc + (size_t)b * seq_stride + (size_t)layer * max_seq * stride + (size_t)g * HD;
+  const int ntiles = (len + 31) / 32, per = (ntiles + splits - 1) / splits;
+  const int tile0 = z * per, tile1 = min(ntiles, tile0 + per);
+  float m[GQ], l[GQ], acc[GQ][DL];
+#pragma unroll
+  for (int h = 0; h < GQ; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DL; ++d) acc[h][d] = 0.f;
+  }
+  for (int tile = tile0 + warp; tile < tile1; tile += 4) {
+    const int p = tile * 32 + lane;
+    float s[GQ];
+#pragma unroll
+    for (int h = 0; h < GQ; ++h) s[h] = 0.f;
+    if (p < len) {
+      const uint4* kr = reinterpret_cast<const uint4*>(kl + (size_t)p * stride);
+      uint4 kv[HD / 8];
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c) kv[c] = __ldg(kr + c);
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c) {
+        const uint32_t w4[4] = {kv[c].x, kv[c].y, kv[c].z, kv[c].w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float k0 = h2f((uint16_t)(w4[t] & 0xffffu)), k1 = h2f((uint16_t)(w4[t] >> 16));
+#pragma unroll
+          for (int h = 0; h < GQ; ++h) s[h] = fmaf(qs[h][8 * c + 2 * t + 1], k1, fmaf(qs[h][8 * c + 2 * t], k0, s[h]));
+        }
+      }
+    }
+    float pw[GQ];
+#pragma unroll
+    for (int h = 0; h < GQ; ++h) {
+      const float sv = p < len ? s[h] : -INFINITY;
+      const float mt = warp_max(sv);
+      const float mn = fmaxf(m[h], mt);  // finite: the tile holds at least one position
+      pw[h] = p < len ? expf(sv - mn) : 0.f;
+      const float f = m[h] == -INFINITY ? 0.f : expf(m[h] - mn);
+      l[h] = l[h] * f + warp_sum(pw[h]);
+      m[h] = mn;
+#pragma unroll
+      for (int d = 0; d < DL; ++d) acc[h][d] *= f;
+    }
+    const int nvalid = min(32, len - tile * 32);
+    for (int j = 0; j < nvalid; ++j) {
+      const uint16_t* vr = vl + (size_t)(tile * 32 + j) * stride + lane * DL;
+      float vv[DL];
+      if (DL == 4) {
+        const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(vr));
+        vv[0] = h2f((uint16_t)(w2.x & 0xffffu));
+        vv[1] = h2f((uint16_t)(w2.x >> 16));
+        vv[2 % DL] = h2f((uint16_t)(w2.y & 0xffffu));
+        vv[3 % DL] = h2f((uint16_t)(w2.y >> 16));
+      } else {
+        const uint32_t w1 = __ldg(reinterpret_cast<const uint32_t*>(vr));
+        vv[0] = h2f((uint16_t)(w1 & 0xffffu));
+        vv[1 % DL] = h2f((uint16_t)(w1 >> 16));
+      }
+#pragma unroll
+      for (int h = 0; h < GQ; ++h) {
+        const float pj = __shfl_sync(0xffffffffu, pw[h], j);
+#pragma unroll
+        for (int d = 0; d < DL; ++d) acc[h][d] = fmaf(pj, vv[d], acc[h][d]);
+      }
+    }
+  }
+  // merge the warps
+  if (lane == 0) {
+#pragma unroll
+    for (int h = 0; h < GQ; ++h) {
+      wm[warp][h] = m[h];
+      wl[warp][h] = l[h];
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < GQ; ++h)
+#pragma unroll
+    for (int d = 0; d < DL; ++d) wacc[warp][h][lane * DL + d] = acc[h][d];
+  __syncthreads();
+  const size_t rows = (size_t)B * n_heads;
+  for (int e = tid; e < GQ * HD; e += AD_THREADS) {
+    const int h = e / HD, d = e % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][h]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      if (wm[w][h] == -INFINITY) continue;
+      const float f = expf(wm[w][h] - M);
+      L = fmaf(wl[w][h], f, L);
+      A = fmaf(wacc[w][h][d], f, A);
+    }
+    const size_t row = (size_t)b * n_heads + (size_t)g * GQ + h;
+    if (splits == 1) {
+      out[row * HD + d] = L > 0.f ? A / L : 0.f;
+    } else {
+      work[((size_t)z * rows + row) * HD + d] = A;
+      if (d == 0) {
+        float* wmw = work + (size_t)AT_MAXSPLIT * rows * HD;
+        wmw[((size_t)z * rows + row) * 2] = M;
+        wmw[((size_t)z * rows + row) * 2 + 1] = L;
+      }
+    }
+  }
+}
+
+// Greedy pick per row of a batch of logits (the reference's greedy sample_token: NaN -> -1e4, +inf -> 100,
+// -inf -> -1e4, the first maximum) and the batch's bookkeeping: ids[b] = pick; out_ids[b][pos[b] + 1] =
+// pick (when out_ids); pos[b] += 1 (when pos).
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restrict__ logits, int n, int* __restrict__ ids,
+                                                          int* __restrict__ pos, int* __restrict__ out_ids,
+                                                          int out_stride) {
+  __shared__ unsigned long long red[32];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const float* lr = logits + (size_t)b * n;
+  unsigned long long best = 0ull;
+  for (int i = tid; i < n; i += 1024) {
+    float v = lr[i];
+    v = isnan(v) ? -1e4f : (isinf(v) ? (v > 0.f ? 100.f : -1e4f) : v) + 0.0f;
+    const uint32_t bits = __float_as_uint(v);
+    const uint32_t key = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+    const unsigned long long k = ((unsigned long long)key << 32) | (0xffffffffu - (uint32_t)i);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long u = __shfl_xor_sync(0xffffffffu, best, o);
+    best = u > best ? u : best;
+  }
+  if ((tid & 31) == 0) red[tid >> 5] = best;
+  __syncthreads();
+  if (tid < 32) {
+    best = red[tid];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long u = __shfl_xor_sync(0xffffffffu, best, o);
+      best = u > best ? u : best;
+    }
+    if (tid == 0) {
+      const int pick = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffull));
+      ids[b] = pick;
+      if (pos) {
+        const int p = pos[b];
+        if (out_ids && p + 1 >= 0 && p + 1 < out_stride) out_ids[(size_t)b * out_stride + p + 1] = pick;
+        pos[b] = p + 1;
+      }
+    }
+  }
+}
+
 static size_t attention_rows_work(int n, int n_heads, int hd) {
   return sizeof(float) * (size_t)AT_MAXSPLIT * n * n_heads * (hd + 2);
 }
@@ -327,7 +516,21 @@ int gsdlq_rope_kv_rows(float* q, const float* k, const float* v, uint16_t* k_cac
   if (pos0 + n > max_seq) return GSDLQ_ERR_INVALID;
   rope_kv_rows_kernel<<<n, 128, 0, static_cast<cudaStream_t>(stream)>>>(
       q, k, v, k_cache, v_cache, reinterpret_cast<const float2*>(rope_cs), layer, pos0, n_heads, n_kv_heads, head_dim,
-      max_seq);
+      max_seq, nullptr, 0);
+  GSDLQ_CUDA_CHECK_LAUNCH();
+  return GSDLQ_OK;
+}
+
+int gsdlq_rope_kv_batch(float* q, const float* k, const float* v, uint16_t* k_cache, uint16_t* v_cache,
+                        size_t seq_stride, const float* rope_cs, int layer, const int* pos, int batch, int n_heads,
+                        int n_kv_heads, int head_dim, int max_seq, gsdlq_stream_t stream) {
+  if (!q || !k || !v || !k_cache || !v_cache || !rope_cs || !pos || batch <= 0 || layer < 0 || max_seq <= 0)
+    return GSDLQ_ERR_INVALID;
+  if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || head_dim % 2) return GSDLQ_ERR_INVALID;
+  if (seq_stride < (size_t)(layer + 1) * max_seq * n_kv_heads * head_dim) return GSDLQ_ERR_INVALID;
+  rope_kv_rows_kernel<<<batch, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      q, k, v, k_cache, v_cache, reinterpret_cast<const float2*>(rope_cs), layer, 0, n_heads, n_kv_heads, head_dim,
+      max_seq, pos, seq_stride);
   GSDLQ_CUDA_CHECK_LAUNCH();
   return GSDLQ_OK;
 }
@@ -377,6 +580,69 @@ int gsdlq_attention_rows(const float* q, const uint16_t* k_cache, const uint16_t
   GSDLQ_CUDA_CHECK_LAUNCH();
   if (splits > 1) {
     attention_combine_kernel<<<dim3(n, n_heads), head_dim, 0, st>>>(wk, out, n, n_heads, head_dim, splits);
+    GSDLQ_CUDA_CHECK_LAUNCH();
+  }
+  return GSDLQ_OK;
+}
+
+int gsdlq_argmax_rows(const float* logits, int rows, int n, int* ids, int* pos, int* out_ids, int out_stride,
+                      gsdlq_stream_t stream) {
+  if (!logits || !ids || rows <= 0 || n <= 0 || (out_ids && (!pos || out_stride <= 0))) return GSDLQ_ERR_INVALID;
+  argmax_rows_kernel<<<rows, 1024, 0, static_cast<cudaStream_t>(stream)>>>(logits, n, ids, pos, out_ids, out_stride);
+  GSDLQ_CUDA_CHECK_LAUNCH();
+  return GSDLQ_OK;
+}
+
+int gsdlq_attention_decode_batch(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, size_t seq_stride,
+                                 float* out, void* work, size_t work_bytes, int layer, const int* pos, int batch,
+                                 int n_heads, int n_kv_heads, int head_dim, int max_seq, float sm_scale,
+                                 gsdlq_stream_t stream) {
+  if (!q || !k_cache || !v_cache || !out || !work || !pos || batch <= 0 || layer < 0 || max_seq <= 0)
+    return GSDLQ_ERR_INVALID;
+  if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads) return GSDLQ_ERR_INVALID;
+  const int gq = n_heads / n_kv_heads;
+  if (head_dim != 64 && head_dim != 128) return GSDLQ_ERR_INVALID;
+  if (gq != 1 && gq != 2 && gq != 4 && gq != 6 && gq != 8) return GSDLQ_ERR_INVALID;
+  if (seq_stride < (size_t)(layer + 1) * max_seq * n_kv_heads * head_dim) return GSDLQ_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(work)) &
+      15u)
+    return GSDLQ_ERR_INVALID;
+  if ((seq_stride * 2) % 16) return GSDLQ_ERR_INVALID;
+  if (work_bytes < attention_rows_work(batch, n_heads, head_dim)) return GSDLQ_ERR_INVALID;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // splits of the position range so that about four CTAs per SM are busy (each split at least one tile)
+  const int base = batch * n_kv_heads, tiles = (max_seq + 31) / 32;
+  int splits = (4 * sms + base - 1) / base;
+  splits = std::max(1, std::min(std::min(splits, AT_MAXSPLIT), tiles));
+  const dim3 grid(batch, n_kv_heads, splits);
+  float* wk = static_cast<float*>(work);
+#define GSDLQ_AD(hd, g)                                                                                          \
+  attention_decode_kernel<hd, g><<<grid, AD_THREADS, 0, st>>>(q, k_cache, v_cache, seq_stride, out, wk, layer, pos, \
+                                                               batch, n_heads, n_kv_heads, max_seq, sm_scale, splits)
+  if (head_dim == 64) {
+    switch (gq) {
+      case 1: GSDLQ_AD(64, 1); break;
+      case 2: GSDLQ_AD(64, 2); break;
+      case 4: GSDLQ_AD(64, 4); break;
+      case 6: GSDLQ_AD(64, 6); break;
+      default: GSDLQ_AD(64, 8); break;
+    }
+  } else {
+    switch (gq) {
+      case 1: GSDLQ_AD(128, 1); break;
+      case 2: GSDLQ_AD(128, 2); break;
+      case 4: GSDLQ_AD(128, 4); break;
+      case 6: GSDLQ_AD(128, 6); break;
+      default: GSDLQ_AD(128, 8); break;
+    }
+  }
+#undef GSDLQ_AD
+  GSDLQ_CUDA_CHECK_LAUNCH();
+  if (splits > 1) {
+    attention_combine_kernel<<<dim3(batch, n_heads), head_dim, 0, st>>>(wk, out, batch, n_heads, head_dim, splits);
     GSDLQ_CUDA_CHECK_LAUNCH();
   }
   return GSDLQ_OK;

@@ -556,9 +556,14 @@ class GSDLQModel:
             self._pf = b
         return b
 
-    def _prefill_chunk(self, ids, pos0: int):
+    def _prefill_chunk(self, ids, pos0: int, k_cache=None, v_cache=None, max_seq: int | None = None):
+        """One chunk of batched prefill into (k_cache, v_cache) ([layers][max_seq][kv heads][head_dim]
+        fp16; the model's own cache by default)."""
         lib, sh = L.load(), ops.stream_handle()
         b = self._prefill_bufs()
+        kc = self.k_cache if k_cache is None else k_cache
+        vc = self.v_cache if v_cache is None else v_cache
+        S = self.max_seq if max_seq is None else max_seq
         n, H, F = len(ids), self.hidden, self.ffn_local
         b["ids"][:n].copy_(torch.tensor(ids, dtype=torch.int32))
 
@@ -575,13 +580,13 @@ class GSDLQModel:
             mm(xn, p + "attn_q.weight", b["q"])
             mm(xn, p + "attn_k.weight", b["k"])
             mm(xn, p + "attn_v.weight", b["v"])
-            L.check(lib.gsdlq_rope_kv_rows(b["q"].data_ptr(), b["k"].data_ptr(), b["v"].data_ptr(),
-                                           self.k_cache.data_ptr(), self.v_cache.data_ptr(), self.rope_cs.data_ptr(),
-                                           l, pos0, n, self.n_heads_local, self.n_kv_local, self.head_dim,
-                                           self.max_seq, sh), "gsdlq_rope_kv_rows")
-            L.check(lib.gsdlq_attention_rows(b["q"].data_ptr(), self.k_cache.data_ptr(), self.v_cache.data_ptr(),
-                                             b["att"].data_ptr(), b["awork"].data_ptr(), b["awork"].numel(), l, pos0, n, self.n_heads_local, self.n_kv_local,
-                                             self.head_dim, self.max_seq, sm, sh), "gsdlq_attention_rows")
+            L.check(lib.gsdlq_rope_kv_rows(b["q"].data_ptr(), b["k"].data_ptr(), b["v"].data_ptr(), kc.data_ptr(),
+                                           vc.data_ptr(), self.rope_cs.data_ptr(), l, pos0, n, self.n_heads_local,
+                                           self.n_kv_local, self.head_dim, S, sh), "gsdlq_rope_kv_rows")
+            L.check(lib.gsdlq_attention_rows(b["q"].data_ptr(), kc.data_ptr(), vc.data_ptr(), b["att"].data_ptr(),
+                                             b["awork"].data_ptr(), b["awork"].numel(), l, pos0, n,
+                                             self.n_heads_local, self.n_kv_local, self.head_dim, S, sm, sh),
+                    "gsdlq_attention_rows")
             mm(b["att"], p + "attn_output.weight", b["o"])
             L.check(lib.gsdlq_vec_add(x.data_ptr(), x.data_ptr(), b["o"].data_ptr(), n * H, sh), "gsdlq_vec_add")
             L.check(lib.gsdlq_rmsnorm_rows(x.data_ptr(), self.norms[p + "ffn_norm.weight"].data_ptr(), xn.data_ptr(),

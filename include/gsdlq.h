@@ -400,6 +400,28 @@ int gsdlq_attention_rows(const float *q, const uint16_t *k_cache, const uint16_t
                          size_t work_bytes, int layer, int pos0, int n, int n_heads, int n_kv_heads, int head_dim,
                          int max_seq, float sm_scale, gsdlq_stream_t stream);
 
+/* ---- Batched decode: B independent sequences, one token each per step -------------------------
+ * No counterpart in the reference (batch 1 only).  Each sequence has its own KV cache, seq_stride
+ * elements after the previous one's ([B][layers][max_seq][n_kv_heads][head_dim] fp16 for
+ * seq_stride = layers * max_seq * n_kv_heads * head_dim), and its own position pos[b] (device ints).
+ *   rope_kv_batch:         gsd_cpu_rope_and_store_kv (gsd_lq_cpu_engine.c:186-262) of row b at pos[b]
+ *                          into sequence b's cache (interleaved pairs, angles from rope_cs)
+ *   attention_decode_batch: gsd_cpu_gqa_attention (gsd_lq_cpu_engine.c:265-330) of row b over
+ *                          positions 0 .. pos[b] of sequence b's cache; head_dim 64 or 128, 1, 2, 4,
+ *                          6 or 8 query heads per kv head; work: gsdlq_attention_rows_work_size(B, ...)
+ *   argmax_rows:           greedy pick of every row of logits[rows][n] (the reference's greedy rule)
+ *                          into ids[b]; with pos: out_ids[b * out_stride + pos[b] + 1] = pick (when
+ *                          out_ids and inside out_stride) and pos[b] += 1 */
+int gsdlq_rope_kv_batch(float *q, const float *k, const float *v, uint16_t *k_cache, uint16_t *v_cache,
+                        size_t seq_stride, const float *rope_cs, int layer, const int *pos, int batch, int n_heads,
+                        int n_kv_heads, int head_dim, int max_seq, gsdlq_stream_t stream);
+int gsdlq_attention_decode_batch(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, size_t seq_stride,
+                                 float *out, void *work, size_t work_bytes, int layer, const int *pos, int batch,
+                                 int n_heads, int n_kv_heads, int head_dim, int max_seq, float sm_scale,
+                                 gsdlq_stream_t stream);
+int gsdlq_argmax_rows(const float *logits, int rows, int n, int *ids, int *pos, int *out_ids, int out_stride,
+                      gsdlq_stream_t stream);
+
 /* ---- The whole decode step in one launch ----------------------------------------------------
  * Engine-level entry point with no single reference counterpart: the reference's
  * Model.forward_token (run_gpu_native_chat.py:921-984) walks the layers on the host, one kernel
