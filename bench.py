@@ -42,6 +42,8 @@ GU_TRAFFIC = 66_794_752 + 727_296
 GU_ALGO = 66_527_368
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 REF_TIME_BUDGET_S = 240.0  # the reference arm's timed tokens are capped to about this much host time
+SWEEP_SHAPES = ((4096, 4096), (4096, 14336), (14336, 4096), (32768, 4096))  # (rows, cols) of W
+SWEEP_BATCHES = (1, 4, 16, 64)
 
 
 def peaks():
@@ -75,14 +77,37 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override n_layers (debug only; not a bench number)")
     ap.add_argument("--step", choices=["fused", "per-op"], default="per-op",
                     help="one persistent launch per token (fused) or the per-operation launches in CUDA graphs")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="sequences decoded in lockstep (B > 1: batched decode through the tensor-core GEMM, one GPU)")
+    ap.add_argument("--max-seq", type=int, default=2048, help="KV cache length per sequence (batched decode)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="the unpack-matvec / dequant-GEMM bandwidth sweep (4 shapes x 2 modes x B = 1/4/16/64)")
     return ap.parse_args()
+
+
+def metric_name(args) -> str:
+    """BASELINE's metric for its headline config; the same quantity named for the other configs."""
+    if args.sweep:
+        return "packed linear GB/s (unpack-matvec at B=1, dequant-GEMM at B=1/4/16/64) % of HBM peak"
+    if args.batch == 1 and args.model == "mistral-7b" and args.mode == "precision":
+        return METRIC
+    return f"decode tok/s batch{args.batch} {args.model}-shape {args.mode.capitalize()}"
 
 
 def workload_config(args, world: int) -> dict:
     """The `config` object of both arms' lines (the same workload, whatever runs it)."""
-    return {"workload": f"{args.model}-shape {args.mode} greedy decode, batch 1, KV length {args.prompt} at the "
-                        f"first timed token, random-init N(0,0.02^2) weights",
-            "model": args.model, "mode": args.mode, "prompt": args.prompt, "global_batch": 1,
+    if args.sweep:
+        return {"workload": "packed linears of shapes 4096x4096, 4096x14336, 14336x4096, 32768x4096 (rows x cols), "
+                            "N(0,0.02^2) weights packed in Precision and Turbo, batch 1/4/16/64",
+                "shapes": [list(s) for s in SWEEP_SHAPES], "batches": list(SWEEP_BATCHES), "global_batch": None,
+                "parallelism": "tp1",
+                "l2": "every timed call reads a different copy of the matrix; the copies total more than L2"}
+    kv = f"KV length {args.prompt} at the first timed token"
+    if args.batch > 1:
+        kv += f" (every sequence), {args.max_seq}-entry KV cache per sequence"
+    return {"workload": f"{args.model}-shape {args.mode} greedy decode, batch {args.batch}, {kv}, random-init "
+                        f"N(0,0.02^2) weights",
+            "model": args.model, "mode": args.mode, "prompt": args.prompt, "global_batch": args.batch,
             "parallelism": f"tp{world}",
             "l2": "inputs larger than L2: every step streams all packed weights"}
 
@@ -493,7 +518,7 @@ def run_ours(args):
     if rank == 0:
         conf = workload_config(args, world)
         line = {
-            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "metric": metric_name(args), "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": vs_published(args, tok_s), "dtype": "f32",
             "data": "synthetic", "config": conf,
@@ -525,6 +550,278 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def _clone_hex(h):
+    from gsdlq_b200.ops import DeviceHex
+    t = {k: (getattr(h, k).clone() if getattr(h, k, None) is not None else None)
+         for k in ("codes", "scales", "row_ptr", "kink_cols", "kink_deltas", "U", "S", "Vt")}
+    return DeviceHex(None, rows=h.rows, cols=h.cols, k_dim=h.k_dim, radius=h.radius, nnz=h.nnz, **t)
+
+
+def _event_us(fn, reps):
+    import torch
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(reps):
+        fn(i)
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) * 1e3 / reps
+
+
+def run_batch(args):
+    """Batched greedy decode: args.batch sequences in lockstep (BatchDecoder), one GPU."""
+    import math
+    import numpy as np
+    import torch
+    world, rank, local = init_dist(args)
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"impl": "ours", "unavailable": "batched decode runs on one GPU (--batch > 1 with N=1)"}))
+        return
+    device = torch.device("cuda", local)
+    from gsdlq_b200.model import GSDLQModel
+    from gsdlq_b200.batch import BatchDecoder
+    from gsdlq_b200 import _lib as L, ops
+    import gsdlq_b200.packer as P
+    cfg, dm, pack_s = build_model(args, device)
+    S, B, P0, V = args.max_seq, args.batch, args.prompt, cfg["vocab_size"]
+    model = GSDLQModel(dm, device=device, max_seq=S)
+    host_model = None if args.no_cpu_baseline else P.device_model_to_host(dm)
+    del dm
+    bd = BatchDecoder(model, B, max_seq=S)
+    rng = np.random.default_rng(args.seed + 1)
+    prompts = [rng.integers(0, V, P0).tolist() for _ in range(B)]
+    torch.cuda.synchronize()
+    t0 = time.time()
+    for b, pr in enumerate(prompts):
+        bd.prefill(b, pr[:-1])
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+    bd.set_tokens([pr[-1] for pr in prompts], [P0 - 1] * B)
+    state = {"pos": P0 - 1}
+
+    def steps(n):
+        for _ in range(n):
+            if state["pos"] >= S:
+                state["pos"] = P0 - 1
+                bd.pos.fill_(P0 - 1)  # device-side position reset (wrap), stream-ordered
+            bd.step()
+            state["pos"] += 1
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    steps(args.warmup)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("decode")
+    ms = time_region(steps, args.steps, 1)
+    torch.cuda.nvtx.range_pop()
+    clocks = sampler.stop()
+    flags = L.device_flags()
+    if flags:
+        raise RuntimeError(f"device flags raised during the bench: {L.flag_names(flags)}")
+    out = bd.out_ids.cpu().numpy()
+    ids_sha = hashlib.sha256(out[:, P0:P0 + 16].astype(np.int32).tobytes()).hexdigest()[:16]
+    ms_step = ms / args.steps
+    tok_s = B * args.steps / (ms / 1e3)
+    span = S - (P0 - 1)
+    mean_pos = P0 + min(span, args.warmup + args.steps) / 2
+    kv_bytes = 2 * model.n_layers * int(mean_pos + 1) * model.n_kv_local * model.head_dim * 2  # per sequence
+    w_bytes = sum(h.nbytes() for h in model.hex.values()) + B * model.hidden * 2
+    step_bytes = w_bytes + B * kv_bytes
+    pk, pk_src = peaks()
+    hbm = float(pk["hbm_gbs"])
+    # the two kernel kinds that carry the step's bytes, each timed alone: one layer's batched decode
+    # attention (its KV rows) and the largest linear's dequant-GEMM
+    pos_mid = torch.full((B,), int(mean_pos), dtype=torch.int32, device=device)
+    sm = 1.0 / math.sqrt(model.head_dim)
+    lib, sh = L.load(), ops.stream_handle()
+
+    def attn(i):
+        L.check(lib.gsdlq_attention_decode_batch(bd.q.data_ptr(), bd.k_cache.data_ptr(), bd.v_cache.data_ptr(),
+                                                 bd.seq_stride, bd.att.data_ptr(), bd.awork.data_ptr(),
+                                                 bd.awork.numel(), i % model.n_layers, pos_mid.data_ptr(), B,
+                                                 model.n_heads_local, model.n_kv_local, model.head_dim, S, sm, sh),
+                "attention_decode_batch")
+    attn(0)
+    attn_us = _event_us(attn, 3 * model.n_layers)
+    attn_bytes = kv_bytes // model.n_layers * B
+    names = [f"blk.{l}.ffn_gate.weight" for l in range(model.n_layers)]
+    gx = torch.randn((B, model.hidden), device=device)
+
+    def gate(i):
+        h = model.hex[names[i % len(names)]]
+        ops.hex2d_matmul(gx, h, bd.xy[h.radius], bd.g, bd.work)
+    gate(0)
+    gate_us = _event_us(gate, 2 * len(names))
+    gate_bytes = model.hex[names[0]].nbytes()
+    kinds = {"attention": {"us": round(attn_us, 2), "bytes": attn_bytes, "gbs": round(attn_bytes / attn_us / 1e3, 1),
+                           "launches_per_step": model.n_layers},
+             "ffn_gate_gemm": {"us": round(gate_us, 2), "bytes": gate_bytes,
+                               "gbs": round(gate_bytes / gate_us / 1e3, 1), "launches_per_step": model.n_layers}}
+    dom = max(kinds, key=lambda k: kinds[k]["us"] * kinds[k]["launches_per_step"])
+    kd = kinds[dom]
+    # e2e through the public surface: host token ids and positions in, greedy picks out, every step
+    n_e2e = min(args.e2e_steps, S - P0)
+    e2e = None
+    if n_e2e > 0:
+        ids_h = np.array([pr[-1] for pr in prompts], np.int32)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(n_e2e):
+            bd.set_tokens(ids_h, np.full(B, P0 - 1 + i, np.int32))
+            bd.step()
+            ids_h = bd.ids.cpu().numpy()
+        e.record()
+        torch.cuda.synchronize()
+        e_ms = s.elapsed_time(e) / n_e2e
+        e2e = {"value": B * 1e3 / e_ms, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B,
+               "api": "BatchDecoder.set_tokens(ids, positions) + step() + the picks read back"}
+    cpu = None
+    if host_model is not None:
+        cpu = cpu_reference_sample(host_model, P0, args.seed + 2)
+        cpu["sample"] += "; the reference decodes one sequence at a time, so its batch rate is this rate"
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    splits = max(1, min(8, -(-4 * sms // (B * model.n_kv_local)), -(-S // 32)))
+    per_layer = 1 + 3 * 4 + 1 + 1 + (1 if splits > 1 else 0) + 4 + 1 + 1 + 2 * 4 + 1 + 4 + 1
+    launches = 1 + per_layer * model.n_layers + 1 + 4 + 1
+    line = {
+        "metric": metric_name(args), "value": tok_s, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(args, 1),
+        "step_bytes": step_bytes, "step_gbs": step_bytes / (ms_step / 1e3) / 1e9,
+        "step_hbm_frac": step_bytes / (ms_step / 1e3) / 1e9 / hbm,
+        "roofline": {"bound": "hbm", "kernel": "attention_decode_kernel" if dom == "attention" else "hexmm_kernel",
+                     "achieved": kd["gbs"], "peak": hbm, "unit": "GB/s", "frac": kd["gbs"] / hbm,
+                     "peak_source": f"{pk_src} hbm_gbs", "bytes_per_launch": kd["bytes"], "launch_ms": kd["us"] / 1e3,
+                     "traffic": None},
+        "kinds": kinds, "ids_sha": ids_sha, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * args.steps,
+        "clocks": clocks, "pack_s": round(pack_s, 2), "prefill_s": round(prefill_s, 3),
+        "prefill_tok_s": round(B * (P0 - 1) / prefill_s, 1), "avg_bpw": round(model.avg_bpw, 4),
+        "n_layers": model.n_layers,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_sweep(args):
+    """The packed-linear bandwidth sweep: each shape and mode, the drop-in unpack-matvec at B = 1 and the
+    dequant-GEMM at B = 1/4/16/64, each call reading a different copy of the matrix."""
+    import numpy as np
+    import torch
+    world, rank, local = init_dist(args)
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"impl": "ours", "unavailable": "the sweep runs on one GPU"}))
+        return
+    device = torch.device("cuda", local)
+    import gsdlq_b200.packer as P
+    from gsdlq_b200 import _lib as L, ops
+    pk, pk_src = peaks()
+    hbm = float(pk["hbm_gbs"])
+    sampler = ClockSampler(local)
+    sampler.start()
+    rows_out, head = [], None
+    torch.manual_seed(args.seed)
+    for mode in ("precision", "turbo"):
+        for (R, C) in SWEEP_SHAPES:
+            w = torch.randn(R, C, device=device) * 0.02
+            h = P.pack_matrix_cuda(w, mode, seed=args.seed)
+            del w
+            nb = h.nbytes()
+            copies = [h] + [_clone_hex(h) for _ in range(max(1, -(-3 * 126 * 2 ** 20 // nb)) - 1)]
+            xy = torch.from_numpy(ops.codebook(h.radius)).to(device)
+            x = torch.randn((max(SWEEP_BATCHES), C), device=device)
+            y = torch.zeros((max(SWEEP_BATCHES), R), device=device)
+            tk = torch.zeros(16, device=device)
+            work = ops.matmul_work(max(SWEEP_BATCHES), C, device)
+
+            def mv(i):
+                c = copies[i % len(copies)]
+                if c.k_dim:
+                    ops.lowrank_proj(x[0], c, tk)
+                ops.hex2d_matvec(x[0], c, xy, tk, y[0])
+            mv(0)
+            us = _event_us(mv, 4 * len(copies))
+            rows_out.append({"shape": [R, C], "mode": mode, "batch": 1, "kernel": "unpack-matvec (hexmv)",
+                             "us": round(us, 2), "gbs": round(nb / us / 1e3, 1), "hbm_frac": round(nb / us / 1e3 / hbm, 3),
+                             "bytes": nb})
+            for B in SWEEP_BATCHES:
+                def mm(i, B=B):
+                    ops.hex2d_matmul(x[:B], copies[i % len(copies)], xy, y[:B], work)
+                mm(0)
+                us = _event_us(mm, 4 * len(copies))
+                e = {"shape": [R, C], "mode": mode, "batch": B, "kernel": "dequant-GEMM (hexmm, tcgen05)",
+                     "us": round(us, 2), "gbs": round(nb / us / 1e3, 1), "hbm_frac": round(nb / us / 1e3 / hbm, 3),
+                     "useful_tflops": round(2.0 * R * C * B / us / 1e6, 2), "bytes": nb}
+                rows_out.append(e)
+                if (R, C) == (14336, 4096) and mode == "precision" and B == 16:
+                    head = e
+            del copies, h
+            torch.cuda.empty_cache()
+    clocks = sampler.stop()
+    flags = L.device_flags()
+    if flags:
+        raise RuntimeError(f"device flags raised during the sweep: {L.flag_names(flags)}")
+    line = {"metric": metric_name(args), "value": head["gbs"], "unit": "GB/s", "n_gpus": 1, "steps": None,
+            "warmup": 1, "ms_per_step": head["us"] / 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(args, 1),
+            "value_is": "14336x4096 Precision, batch 16, dequant-GEMM",
+            "roofline": {"bound": "hbm", "kernel": "hexmm_kernel", "achieved": head["gbs"], "peak": hbm, "unit": "GB/s",
+                         "frac": head["gbs"] / hbm, "peak_source": f"{pk_src} hbm_gbs", "traffic": None},
+            "sweep": rows_out, "clocks": clocks,
+            "tensor_pipe": "sm__pipe_tensor_cycles_active from ncu, in the profiles folder (hexmm_kernel summary)"}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_sweep(args):
+    """The reference's unpack-matvec (its C engine) on the host cores for each sweep shape and mode; the
+    reference has no batched path, so batch B costs B matvecs."""
+    import numpy as np
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    cores = use_all_cores()
+    import gsdlq_b200.packer as P
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    eng, kind = reference_engine()
+    tabs = {r: oracle.codebook(r) for r in (6, 8)}
+    rows_out, head = [], None
+    rng = np.random.default_rng(args.seed)
+    for mode in ("precision", "turbo"):
+        for (R, C) in SWEEP_SHAPES:
+            cfg = {"n_layers": 0}
+            t = P.random_packed_matrix(R, C, mode, seed=args.seed) if hasattr(P, "random_packed_matrix") else None
+            if t is None:
+                raise RuntimeError("packer.random_packed_matrix missing")
+            rec = oracle.hex_record({"radius": t.radius, "k_dim": t.k_dim, "rows": t.rows, "cols": t.cols},
+                                    {k: memoryview(np.ascontiguousarray(v)).cast("B") for k, v in t.blobs().items()},
+                                    tabs)
+            x = rng.standard_normal(C).astype(np.float32)
+            eng.matvec(x, rec, np.zeros(16, np.float32))
+            n, t0 = 0, time.perf_counter()
+            while n < 3 or time.perf_counter() - t0 < 1.0:
+                eng.matvec(x, rec, np.zeros(16, np.float32))
+                n += 1
+            us = (time.perf_counter() - t0) / n * 1e6
+            nb = t.nbytes()
+            e = {"shape": [R, C], "mode": mode, "batch": 1, "us": round(us, 1), "gbs": round(nb / us / 1e3, 2),
+                 "bytes": nb, "calls": n}
+            rows_out.append(e)
+            if (R, C) == (14336, 4096) and mode == "precision":
+                head = e
+    line = {"metric": metric_name(args), "value": head["gbs"], "unit": "GB/s", "n_gpus": world, "steps": None,
+            "warmup": 1, "ms_per_step": head["us"] / 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": workload_config(args, world), "value_is": "14336x4096 Precision, one matvec",
+            "cpu_baseline": {"value": head["gbs"], "unit": "GB/s", "cores": cores, "kind": kind,
+                             "sample": "repeated matvecs of one packed matrix per shape and mode for about 1 s each"},
+            "e2e": {"value": head["gbs"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "sweep": rows_out, "runs_on": f"host cores ({cores} OpenMP threads), no GPU"}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args):
     """The reference's C engine on the host cores (no GPU, no library of this repository)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -547,7 +844,7 @@ def run_reference(args):
               f"argmax) after {max(1, args.warmup)} warm-up tokens, OpenMP threads = {cores}; packed bytes of the "
               f"same shapes drawn with NumPy (random_packed_model)")
     conf = workload_config(args, world)
-    line = {"metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": n,
+    line = {"metric": metric_name(args), "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": n,
             "warmup": max(1, args.warmup), "ms_per_step": 1e3 * secs / n, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": vs_published(args, tok_s), "dtype": "f32",
             "data": "synthetic", "impl": "reference", "config": conf,
@@ -561,6 +858,10 @@ def run_reference(args):
 if __name__ == "__main__":
     a = parse()
     if a.impl == "reference":
-        run_reference(a)
+        run_reference_sweep(a) if a.sweep else run_reference(a)
+    elif a.sweep:
+        run_sweep(a)
+    elif a.batch > 1:
+        run_batch(a)
     else:
         run_ours(a)

@@ -247,6 +247,40 @@ def random_model(cfg: dict, mode: str = "precision", seed: int = 0, std: float =
                        extra={"packer": {"name": "gsdlq_b200.packer", "seed": seed, "std": std}})
 
 
+def _random_hex(rng, draw, r: int, c: int, mode: str, scale) -> HexTensor:
+    """One format-valid packed tensor (see random_packed_model); draw(n) gives n uniform codes."""
+    R, k, kn = mode_params(mode, c)
+    codes = draw(r * c // 2)
+    scales = np.full(r * c // 64, scale, np.uint16)
+    if kn:
+        kn = min(kn, c)
+        # distinct ascending columns per row: one random offset inside each of kn equal bins
+        bins = (np.arange(kn, dtype=np.int64) * c) // kn
+        width = np.diff(np.append(bins, c))
+        cols = (bins[None, :] + (rng.random((r, kn)) * width[None, :]).astype(np.int64)).astype(np.uint16)
+        deltas = (rng.standard_normal(r * kn, dtype=np.float32) * np.float32(0.002))
+        row_ptr = (np.arange(r + 1, dtype=np.uint64) * kn).astype(np.uint32)
+        kc = cols.reshape(-1)
+    else:
+        kc, deltas, row_ptr = np.zeros(0, np.uint16), np.zeros(0, np.float32), np.zeros(r + 1, np.uint32)
+    U = S = Vt = None
+    if k:
+        U = (rng.standard_normal(r * k, dtype=np.float32) * np.float32(0.05)).astype(np.float16).view(np.uint16)
+        S = np.sort(rng.random(k, dtype=np.float32))[::-1].copy() * np.float32(0.5)
+        Vt = (rng.standard_normal(k * c, dtype=np.float32) * np.float32(0.05)).astype(np.float16).view(np.uint16)
+    return HexTensor(rows=r, cols=c, radius=R, k_dim=k, codes=codes, scales=scales, row_ptr=row_ptr,
+                     kink_cols=kc, kink_deltas=deltas, U=U, S=S, Vt=Vt)
+
+
+def random_packed_matrix(rows: int, cols: int, mode: str = "precision", seed: int = 0) -> HexTensor:
+    """One format-valid packed matrix of the given shape, drawn as random_packed_model draws its tensors."""
+    rng = np.random.default_rng(seed)
+    R, _, _ = mode_params(mode, 64)
+    scale = np.float16(0.02 * 3.0 / (R * float(FIT))).view(np.uint16)
+    n_pts = codebook.num_points(R)
+    return _random_hex(rng, lambda n: rng.integers(0, n_pts, n, dtype=np.uint8), rows, cols, mode, scale)
+
+
 def random_packed_model(cfg: dict, mode: str = "precision", seed: int = 0) -> PackedModel:
     """Format-valid packed tensors of a whole decoder, drawn directly with NumPy (no quantisation).
 
@@ -275,27 +309,7 @@ def random_packed_model(cfg: dict, mode: str = "precision", seed: int = 0) -> Pa
     for name in hex_names(cfg["n_layers"]):
         key = name.split(".")[-2]
         r, c = shapes[key] if key in shapes else (cfg["vocab_size"], cfg["hidden_size"])
-        _, k, kn = mode_params(mode, c)
-        codes = draw(r * c // 2)
-        scales = np.full(r * c // 64, scale, np.uint16)
-        if kn:
-            kn = min(kn, c)
-            # distinct ascending columns per row: one random offset inside each of kn equal bins
-            bins = (np.arange(kn, dtype=np.int64) * c) // kn
-            width = np.diff(np.append(bins, c))
-            cols = (bins[None, :] + (rng.random((r, kn)) * width[None, :]).astype(np.int64)).astype(np.uint16)
-            deltas = (rng.standard_normal(r * kn, dtype=np.float32) * np.float32(0.002))
-            row_ptr = (np.arange(r + 1, dtype=np.uint64) * kn).astype(np.uint32)
-            kc = cols.reshape(-1)
-        else:
-            kc, deltas, row_ptr = np.zeros(0, np.uint16), np.zeros(0, np.float32), np.zeros(r + 1, np.uint32)
-        U = S = Vt = None
-        if k:
-            U = (rng.standard_normal(r * k, dtype=np.float32) * np.float32(0.05)).astype(np.float16).view(np.uint16)
-            S = np.sort(rng.random(k, dtype=np.float32))[::-1].copy() * np.float32(0.5)
-            Vt = (rng.standard_normal(k * c, dtype=np.float32) * np.float32(0.05)).astype(np.float16).view(np.uint16)
-        hexes[name] = HexTensor(rows=r, cols=c, radius=R, k_dim=k, codes=codes, scales=scales, row_ptr=row_ptr,
-                                kink_cols=kc, kink_deltas=deltas, U=U, S=S, Vt=Vt)
+        hexes[name] = _random_hex(rng, draw, r, c, mode, scale)
     H = cfg["hidden_size"]
     dense = {"token_embd.weight":
              (rng.standard_normal((cfg["vocab_size"], H), dtype=np.float32) * np.float32(0.02)).astype(np.float16),
@@ -307,7 +321,8 @@ def random_packed_model(cfg: dict, mode: str = "precision", seed: int = 0) -> Pa
                        extra={"packer": {"name": "gsdlq_b200.packer.random_packed_model", "seed": seed}})
 
 
-__all__ = ["pack_matrix", "quantize_lattice", "dequant", "random_model", "random_packed_model", "make_config",
+__all__ = ["pack_matrix", "quantize_lattice", "dequant", "random_model", "random_packed_model", "random_packed_matrix",
+           "make_config",
            "CONFIGS", "MODES", "LINEAR_NAMES", "linear_shapes"]
 
 
