@@ -38,7 +38,7 @@ METRIC = "decode tok/s batch1 Mistral-7B-shape Precision; unpack-matvec HBM GB/s
 PUBLISHED_TOKS = {"precision": 6.5, "turbo": 12.5}  # the reference's Mistral-7B decode rates (README.md:32-33)
 # DRAM bytes (read + write) of one gate/up launch of a Mistral-7B Precision layer, from one ncu capture on a
 # B200, and the algorithmic bytes of that launch (a tensor-parallel rank's launch scales both)
-GU_TRAFFIC = 66_794_752 + 727_296
+GU_TRAFFIC = 66_802_432 + 711_168
 GU_ALGO = 66_527_368
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 REF_TIME_BUDGET_S = 240.0  # the reference arm's timed tokens are capped to about this much host time
