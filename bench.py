@@ -638,7 +638,7 @@ def run_batch(args):
     lib, sh = L.load(), ops.stream_handle()
 
     def attn(i):
-        L.check(lib.gsdlq_attention_decode_batch(bd.q.data_ptr(), bd.k_cache.data_ptr(), bd.v_cache.data_ptr(),
+        L.check(lib.gsdlq_attention_decode_batch(bd.q.data_ptr(), 0, bd.k_cache.data_ptr(), bd.v_cache.data_ptr(),
                                                  bd.seq_stride, bd.att.data_ptr(), bd.awork.data_ptr(),
                                                  bd.awork.numel(), i % model.n_layers, pos_mid.data_ptr(), B,
                                                  model.n_heads_local, model.n_kv_local, model.head_dim, S, sm, sh),
@@ -684,8 +684,10 @@ def run_batch(args):
         cpu["sample"] += "; the reference decodes one sequence at a time, so its batch rate is this rate"
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     splits = max(1, min(8, -(-4 * sms // (B * model.n_kv_local)), -(-S // 32)))
-    per_layer = 1 + 3 * 4 + 1 + 1 + (1 if splits > 1 else 0) + 4 + 1 + 1 + 2 * 4 + 1 + 4 + 1
-    launches = 1 + per_layer * model.n_layers + 1 + 4 + 1
+    qkv_g = 1 if any(k.endswith("qkv") for k in bd.fused) else 3
+    gu_g = 1 if any(k.endswith("gu") for k in bd.fused) else 2
+    per_layer = 1 + 3 * qkv_g + 1 + 1 + (1 if splits > 1 else 0) + 3 + 1 + 1 + 3 * gu_g + 1 + 3 + 1
+    launches = 1 + per_layer * model.n_layers + 1 + 3 + 1  # a GEMM call is 3 kernels
     line = {
         "metric": metric_name(args), "value": tok_s, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",

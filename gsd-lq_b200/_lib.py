@@ -104,9 +104,10 @@ SIGNATURES = {
     "gsdlq_rmsnorm_rows": ([vp, vp, vp, i32, i32, f32, vp], i32),
     "gsdlq_rope_kv_rows": ([vp] * 6 + [i32] * 7 + [vp], i32),
     "gsdlq_attention_rows_work_size": ([i32, i32, i32, ctypes.POINTER(ctypes.c_size_t)], i32),
-    "gsdlq_rope_kv_batch": ([vp] * 5 + [ctypes.c_size_t, vp, i32, vp] + [i32] * 5 + [vp], i32),
-    "gsdlq_attention_decode_batch": ([vp] * 3 + [ctypes.c_size_t, vp, vp, ctypes.c_size_t, i32, vp] + [i32] * 5
-                                     + [f32, vp], i32),
+    "gsdlq_rope_kv_batch": ([vp] * 3 + [i32] + [vp] * 2 + [ctypes.c_size_t, vp, i32, vp] + [i32] * 5 + [vp], i32),
+    "gsdlq_attention_decode_batch": ([vp, i32, vp, vp, ctypes.c_size_t, vp, vp, ctypes.c_size_t, i32, vp]
+                                     + [i32] * 5 + [f32, vp], i32),
+    "gsdlq_swiglu_rows": ([vp, vp, i32, i32, vp], i32),
     "gsdlq_argmax_rows": ([vp, i32, i32, vp, vp, vp, i32, vp], i32),
     "gsdlq_attention_rows": ([vp] * 5 + [ctypes.c_size_t] + [i32] * 7 + [f32, vp], i32),
 }

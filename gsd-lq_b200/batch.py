@@ -9,7 +9,8 @@ and position:
   SwiGLU, down linear + residual -> rmsnorm_rows, LM head linear, argmax_rows (greedy pick, position + 1)
 
 Every packed linear is one call of the tensor-core dequant-GEMM (gsdlq_hex2d_matmul) over the B rows, so
-the weights are decoded once per step for all sequences.  The step is captured as one CUDA graph and
+the weights are decoded once per step for all sequences; without a low-rank term (Turbo) q/k/v and gate/up
+run as one GEMM each over their stacked rows.  The step is captured as one CUDA graph and
 replayed; tokens and positions stay on the device between steps.
 """
 from __future__ import annotations
@@ -21,6 +22,24 @@ import torch
 
 from . import _lib as L
 from . import ops
+
+
+def _stack_rows(hs):
+    """One packed matrix whose rows are those of ``hs`` in order (same columns, radius, no low-rank term):
+    codes, scales and kinks concatenate, the kink row pointers are offset."""
+    import torch
+    from .ops import DeviceHex
+    rps, off = [], 0
+    for i, h in enumerate(hs):
+        rp = h.row_ptr.view(torch.int32).long()
+        rps.append((rp if i == 0 else rp[1:]) + off)
+        off += int(rp[-1].item())
+    kc = [h.kink_cols for h in hs if h.kink_cols is not None and h.nnz]
+    kd = [h.kink_deltas for h in hs if h.kink_deltas is not None and h.nnz]
+    return DeviceHex(None, rows=sum(h.rows for h in hs), cols=hs[0].cols, k_dim=0, radius=hs[0].radius,
+                     codes=torch.cat([h.codes for h in hs]), scales=torch.cat([h.scales for h in hs]),
+                     row_ptr=torch.cat(rps).to(torch.int32), kink_cols=torch.cat(kc) if kc else None,
+                     kink_deltas=torch.cat(kd) if kd else None, U=None, S=None, Vt=None, nnz=off)
 
 
 class BatchDecoder:
@@ -58,6 +77,18 @@ class BatchDecoder:
         self.ids = torch.zeros(B, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
         self.out_ids = torch.zeros((B, S), dtype=torch.int32, device=dev)
+        # Linears that read the same input and have no low-rank term (Turbo) run as one GEMM over their
+        # stacked rows: q/k/v, and gate/up.  With a low-rank term each matrix has its own Vt, so they stay apart.
+        self.fused = {}
+        for l in range(Lc):
+            p = f"blk.{l}."
+            for key, names in (("qkv", ("attn_q", "attn_k", "attn_v")), ("gu", ("ffn_gate", "ffn_up"))):
+                hs = [m.hex[p + n + ".weight"] for n in names]
+                if all(h.k_dim == 0 and h.radius == hs[0].radius and h.cols == hs[0].cols for h in hs):
+                    self.fused[p + key] = _stack_rows(hs)
+        if self.fused:
+            self.qkv = torch.zeros((B, qd + 2 * kv * hd), **f32)
+            self.gu = torch.zeros((B, 2 * F), **f32)
         self._graph = None
 
     # ------------------------------------------------------------------ state
@@ -84,7 +115,7 @@ class BatchDecoder:
 
     # ------------------------------------------------------------------ the step
     def _mm(self, xin, name, yout):
-        h = self.m.hex[name]
+        h = self.fused[name] if name in self.fused else self.m.hex[name]
         ops.hex2d_matmul(xin, h, self.xy[h.radius], yout, self.work)
 
     def _run(self, with_pick: bool = True):
@@ -98,14 +129,21 @@ class BatchDecoder:
             p = f"blk.{l}."
             L.check(lib.gsdlq_rmsnorm_rows(x.data_ptr(), m.norms[p + "attn_norm.weight"].data_ptr(), xn.data_ptr(), B,
                                            H, m.rms_eps, sh), "gsdlq_rmsnorm_rows")
-            self._mm(xn, p + "attn_q.weight", self.q)
-            self._mm(xn, p + "attn_k.weight", self.k)
-            self._mm(xn, p + "attn_v.weight", self.v)
-            L.check(lib.gsdlq_rope_kv_batch(self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
-                                            self.k_cache.data_ptr(), self.v_cache.data_ptr(), self.seq_stride,
-                                            m.rope_cs.data_ptr(), l, self.pos.data_ptr(), B, m.n_heads_local,
-                                            m.n_kv_local, m.head_dim, self.S, sh), "gsdlq_rope_kv_batch")
-            L.check(lib.gsdlq_attention_decode_batch(self.q.data_ptr(), self.k_cache.data_ptr(),
+            if p + "qkv" in self.fused:  # one GEMM; q, k, v are column ranges of its rows
+                self._mm(xn, p + "qkv", self.qkv)
+                qd, kvd, stride = m.n_heads_local * m.head_dim, m.n_kv_local * m.head_dim, self.qkv.shape[1]
+                qp = self.qkv.data_ptr()
+                kp, vp = qp + 4 * qd, qp + 4 * (qd + kvd)
+            else:
+                self._mm(xn, p + "attn_q.weight", self.q)
+                self._mm(xn, p + "attn_k.weight", self.k)
+                self._mm(xn, p + "attn_v.weight", self.v)
+                qp, kp, vp, stride = self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), 0
+            L.check(lib.gsdlq_rope_kv_batch(qp, kp, vp, stride, self.k_cache.data_ptr(), self.v_cache.data_ptr(),
+                                            self.seq_stride, m.rope_cs.data_ptr(), l, self.pos.data_ptr(), B,
+                                            m.n_heads_local, m.n_kv_local, m.head_dim, self.S, sh),
+                    "gsdlq_rope_kv_batch")
+            L.check(lib.gsdlq_attention_decode_batch(qp, stride, self.k_cache.data_ptr(),
                                                      self.v_cache.data_ptr(), self.seq_stride, self.att.data_ptr(),
                                                      self.awork.data_ptr(), self.awork.numel(), l,
                                                      self.pos.data_ptr(), B, m.n_heads_local, m.n_kv_local,
@@ -114,10 +152,14 @@ class BatchDecoder:
             L.check(lib.gsdlq_vec_add(x.data_ptr(), x.data_ptr(), self.o.data_ptr(), B * H, sh), "gsdlq_vec_add")
             L.check(lib.gsdlq_rmsnorm_rows(x.data_ptr(), m.norms[p + "ffn_norm.weight"].data_ptr(), xn.data_ptr(), B,
                                            H, m.rms_eps, sh), "gsdlq_rmsnorm_rows")
-            self._mm(xn, p + "ffn_gate.weight", self.g)
-            self._mm(xn, p + "ffn_up.weight", self.u)
-            L.check(lib.gsdlq_swiglu(self.g.data_ptr(), self.u.data_ptr(), self.g.data_ptr(), B * F, sh),
-                    "gsdlq_swiglu")
+            if p + "gu" in self.fused:  # one GEMM over the stacked gate and up rows, then SwiGLU per row
+                self._mm(xn, p + "gu", self.gu)
+                L.check(lib.gsdlq_swiglu_rows(self.gu.data_ptr(), self.g.data_ptr(), B, F, sh), "gsdlq_swiglu_rows")
+            else:
+                self._mm(xn, p + "ffn_gate.weight", self.g)
+                self._mm(xn, p + "ffn_up.weight", self.u)
+                L.check(lib.gsdlq_swiglu(self.g.data_ptr(), self.u.data_ptr(), self.g.data_ptr(), B * F, sh),
+                        "gsdlq_swiglu")
             self._mm(self.g, p + "ffn_down.weight", self.o)
             L.check(lib.gsdlq_vec_add(x.data_ptr(), x.data_ptr(), self.o.data_ptr(), B * H, sh), "gsdlq_vec_add")
         L.check(lib.gsdlq_rmsnorm_rows(x.data_ptr(), m.norms["output_norm.weight"].data_ptr(), xn.data_ptr(), B, H,

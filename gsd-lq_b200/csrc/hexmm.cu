@@ -6,10 +6,11 @@
 //   y[b][r] = sum_c W[r][c] x[b][c] + sum_{kinks of r} delta * x[b][col] + sum_j U[r][j] tmp[b][j],
 //   W[r][2p + i] = xy[code(r, p)][i] * scale(r, p / 32),  tmp[b][j] = S[j] * (Vt[j] . x[b]).
 //
-// One call is four launches: hexmm_prep (per-token max|x| and the low-rank projections tmp), hexmm_xconv
-// (the activations as fp16 hi / lo B tiles, plus an fp32 transposed copy), hexmm_sparse (the kink and
-// low-rank terms of every (token, row), stored into y, which they initialise) and hexmm_kernel, the dense
-// lattice part, added into y with fp32 atomics (so the summation order over the k-runs is not fixed).
+// One call is three launches: hexmm_prep (y zeroed, per-token max|x|, the low-rank projections tmp and a
+// transposed fp32 copy of the activations), hexmm_xs_sparse (the activations as fp16 hi / lo B tiles, and
+// the kink and low-rank terms of every (token, row) added into y) and hexmm_kernel, the dense lattice part,
+// added into y with fp32 atomics (so the summation order is not fixed).  hexmm_kernel is a programmatic
+// dependent launch: its set-up runs while hexmm_xs_sparse does, and only its B-tile loads wait for it.
 //
 // hexmm_kernel.  A CTA owns a tile of 128 weight rows (the tensor memory's lanes) and a contiguous run of
 // 64-column k-blocks (split-K over CTAs, so that every SM streams weights).  Eight decoder warps, an issuer
@@ -52,41 +53,58 @@ constexpr float MM_WF = 1024.f;                // power-of-two factor on the dec
 constexpr int MM_PREP = 256;
 __global__ void __launch_bounds__(256) hexmm_prep(const float* __restrict__ x, int B, int C,
                                                   const uint16_t* __restrict__ Vt, const float* __restrict__ S, int k,
-                                                  unsigned* __restrict__ amax_bits, float* __restrict__ tmp) {
-  __shared__ float xs[8][MM_PREP];
+                                                  unsigned* __restrict__ amax_bits, float* __restrict__ tmp,
+                                                  float* __restrict__ xT, int BP, float* __restrict__ y, size_t yn) {
+  __shared__ __align__(16) float xs[8][MM_PREP];
+  {  // y starts at zero: the sparse pass and the dense kernel both add into it
+    const size_t nthr = (size_t)gridDim.x * gridDim.y * blockDim.x;
+    size_t i = ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; i < yn; i += nthr) y[i] = 0.f;
+  }
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, b = blockIdx.x * 8 + w;
-  if (b >= B) return;
+  const bool live = b < B;
   const int c0 = blockIdx.y * MM_PREP;
   const int j = lane >> 1, h = lane & 1, cc = c0 + h * (MM_PREP / 2);
   // the Vt loads first: they do not depend on x
   uint4 vt[MM_PREP / 16];
 #pragma unroll
   for (int i = 0; i < MM_PREP / 16; ++i)
-    vt[i] = (j < k && cc + 8 * i + 8 <= C) ? __ldg(reinterpret_cast<const uint4*>(Vt + (size_t)j * C + cc + 8 * i))
-                                          : make_uint4(0u, 0u, 0u, 0u);
+    vt[i] = (live && j < k && cc + 8 * i + 8 <= C)
+                ? __ldg(reinterpret_cast<const uint4*>(Vt + (size_t)j * C + cc + 8 * i))
+                : make_uint4(0u, 0u, 0u, 0u);
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < MM_PREP / 32; ++i) {
     const int c = c0 + lane + 32 * i;
-    const float v = c < C ? x[(size_t)b * C + c] : 0.f;
+    const float v = (live && c < C) ? x[(size_t)b * C + c] : 0.f;
     xs[w][lane + 32 * i] = v;
     amax = fmaxf(amax, fabsf(v));
   }
   amax = warp_max(amax);
-  if (lane == 0) atomicMax(amax_bits + b, __float_as_uint(amax));  // non-negative floats order as their bits
+  if (live && lane == 0) atomicMax(amax_bits + b, __float_as_uint(amax));  // non-negative floats order as bits
   __syncwarp();
-  float acc = 0.f;
+  if (live) {
+    float acc = 0.f;
 #pragma unroll
-  for (int i = 0; i < MM_PREP / 16; ++i) {
-    const uint32_t q[4] = {vt[i].x, vt[i].y, vt[i].z, vt[i].w};
+    for (int i = 0; i < MM_PREP / 16; ++i) {
+      const uint32_t q[4] = {vt[i].x, vt[i].y, vt[i].z, vt[i].w};
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      acc = fmaf(h2f((uint16_t)(q[t] & 0xffffu)), xs[w][h * (MM_PREP / 2) + 8 * i + 2 * t], acc);
-      acc = fmaf(h2f((uint16_t)(q[t] >> 16)), xs[w][h * (MM_PREP / 2) + 8 * i + 2 * t + 1], acc);
+      for (int t = 0; t < 4; ++t) {
+        acc = fmaf(h2f((uint16_t)(q[t] & 0xffffu)), xs[w][h * (MM_PREP / 2) + 8 * i + 2 * t], acc);
+        acc = fmaf(h2f((uint16_t)(q[t] >> 16)), xs[w][h * (MM_PREP / 2) + 8 * i + 2 * t + 1], acc);
+      }
     }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    if (h == 0 && j < k) atomicAdd(tmp + (size_t)b * 16 + j, S[j] * acc);
   }
-  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-  if (h == 0 && j < k) atomicAdd(tmp + (size_t)b * 16 + j, S[j] * acc);
+  // xT[c][8 blockIdx.x .. + 7] for the CTA's columns (zero past the batch): one 32-byte row piece each
+  __syncthreads();
+  const int c = c0 + threadIdx.x;
+  if (threadIdx.x < MM_PREP && c < C) {
+    float4* dst = reinterpret_cast<float4*>(xT + (size_t)c * BP + blockIdx.x * 8);
+    dst[0] = make_float4(xs[0][threadIdx.x], xs[1][threadIdx.x], xs[2][threadIdx.x], xs[3][threadIdx.x]);
+    dst[1] = make_float4(xs[4][threadIdx.x], xs[5][threadIdx.x], xs[6][threadIdx.x], xs[7][threadIdx.x]);
+  }
 }
 
 // the power of two that puts max|x_b| in [2^14, 2^15), so both fp16 halves of x_b stay normal
@@ -206,19 +224,11 @@ __host__ __device__ constexpr uint32_t mm_scring(int st, int h, int r) {
 // The B operand of every k-block, made once per call: token b's row of the block as fp16 hi (row 2b) and
 // lo (row 2b + 1) of x_b scaled by its power of two, in the swizzled layout of a 64-column tile, one
 // contiguous block of mm_btile<NB>() bytes per k-block (tokens past the batch are zero).
-// Block kb also writes its columns of xT[c][b] = x_b[c] (fp32, BP tokens per column, zero past the batch),
-// which the sparse kernel reads one kink column at a time.
 template <int NB>
-__global__ void __launch_bounds__(256) hexmm_xconv(const float* __restrict__ x, int B, int C,
-                                                   const unsigned* __restrict__ amax_bits, uint8_t* __restrict__ xs,
-                                                   float* __restrict__ xT) {
+__device__ void hexmm_xconv_block(const float* __restrict__ x, int B, int C, const unsigned* __restrict__ amax_bits,
+                                  uint8_t* __restrict__ xs, int kb) {
   constexpr int BP = 8 * NB;
-  const int kb = blockIdx.x;
   uint8_t* blk = xs + (size_t)kb * mm_btile<NB>();
-  for (int e = threadIdx.x; e < BP * MM_KB; e += 256) {
-    const int c = e / BP, b = e - c * BP;
-    xT[(size_t)(kb * MM_KB + c) * BP + b] = b < B ? x[(size_t)b * C + kb * MM_KB + c] : 0.f;
-  }
   for (int e = threadIdx.x; e < BP * 8; e += 256) {
     const int b = e >> 3, j = e & 7;
     float v[8];
@@ -291,21 +301,20 @@ __device__ __forceinline__ uint32_t mm_entry(const float* xy, int n_pts, int i) 
   return pack_h2(x, r1);
 }
 
-// The kink and low-rank terms, stored into y (this initialises y; the dense kernel adds to it).  One warp
+// The kink and low-rank terms, added into y (zeroed by hexmm_prep; the dense kernel adds to it too).  One warp
 // per weight row, lane = token b, b + 32, ... (up to four chunks of 32): the row's kinks are loaded 32 at
 // a time and broadcast eight at a time, each adds delta * xT[col][b] (the activation loads of the eight
 // kinks and every token chunk issued together); then U[row] . tmp[b] (gsd_cpu_hex2d_matvec's kink loop
 // and gsd_cpu_lowrank_proj's second half, gsd_lq_cpu_engine.c:111-183).
-__global__ void __launch_bounds__(256) hexmm_sparse(const float* __restrict__ xT, int BP, int B, int R, int C,
-                                                    const uint32_t* __restrict__ row_ptr,
-                                                    const uint16_t* __restrict__ kcols,
-                                                    const float* __restrict__ kdel, const uint16_t* __restrict__ U,
-                                                    int k, const float* __restrict__ tmp, float* __restrict__ y) {
+__device__ void hexmm_sparse_rows(const float* __restrict__ xT, int BP, int B, int R, int C,
+                                  const uint32_t* __restrict__ row_ptr, const uint16_t* __restrict__ kcols,
+                                  const float* __restrict__ kdel, const uint16_t* __restrict__ U, int k,
+                                  const float* __restrict__ tmp, float* __restrict__ y, int rb, float* tmp_s) {
   constexpr int TC = MM_MAXB / 32;  // token chunks
-  __shared__ float tmp_s[MM_MAXB * 17];  // tmp[b][j] at 17 b + j: lane b's reads hit 32 banks
+  // tmp_s: tmp[b][j] at 17 b + j, so that lane b's reads hit 32 banks
   for (int i = threadIdx.x; i < B * 16; i += blockDim.x) tmp_s[(i >> 4) * 17 + (i & 15)] = tmp[i];
   __syncthreads();
-  const int lane = threadIdx.x & 31, row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31, row = rb * 8 + (threadIdx.x >> 5);
   if (row >= R) return;
   const uint32_t e0 = row_ptr[row], e1 = row_ptr[row + 1];
   const int nch = (B + 31) / 32;
@@ -354,9 +363,30 @@ __global__ void __launch_bounds__(256) hexmm_sparse(const float* __restrict__ xT
 #pragma unroll
       for (int j = 0; j < 16; ++j)
         if (j < k) lrv = fmaf(u[j], tmp_s[b * 17 + j], lrv);
-      y[(size_t)b * R + row] = acc[t] + lrv;
+      atomicAdd(y + (size_t)b * R + row, acc[t] + lrv);
     }
   }
+}
+
+// The B tiles (CTAs 0 .. nkb - 1, one k-block each) and the sparse terms (the rest, 8 rows each) in one
+// launch: both need only hexmm_prep's results.  Every CTA lets the dense kernel launch at once
+// (programmatic dependent launch); that kernel waits for this one only before its first B-tile copy.
+template <int NB>
+__global__ void __launch_bounds__(256) hexmm_xs_sparse(const float* __restrict__ x, int B, int C,
+                                                       const unsigned* __restrict__ amax_bits,
+                                                       uint8_t* __restrict__ xs, int nkb,
+                                                       const float* __restrict__ xT, int R,
+                                                       const uint32_t* __restrict__ row_ptr,
+                                                       const uint16_t* __restrict__ kcols,
+                                                       const float* __restrict__ kdel,
+                                                       const uint16_t* __restrict__ U, int k,
+                                                       const float* __restrict__ tmp, float* __restrict__ y) {
+  __shared__ float tmp_s[MM_MAXB * 17];
+  asm volatile("griddepcontrol.launch_dependents;");
+  if ((int)blockIdx.x < nkb)
+    hexmm_xconv_block<NB>(x, B, C, amax_bits, xs, blockIdx.x);
+  else
+    hexmm_sparse_rows(xT, 8 * NB, B, R, C, row_ptr, kcols, kdel, U, k, tmp, y, blockIdx.x - nkb, tmp_s);
 }
 
 // NB: groups of 8 tokens (tokens padded to 8 NB with zero activations); N = 16 NB accumulator columns.
@@ -440,6 +470,8 @@ __global__ void __launch_bounds__(MM_ALL) hexmm_kernel(const uint8_t* __restrict
   if (warp == MM_THREADS / 32 + 1) {
     // ---- B loader: block j's tile into stage j % SB once the MMAs of block j - SB have completed ----
     if (lane == 0) {
+      // the tiles are written by the launch before this one (programmatic dependent launch): wait for it
+      asm volatile("griddepcontrol.wait;" ::: "memory");
       int q = 0;
       uint32_t pe = 1u;  // parity of the empty phase to wait for (none on the first pass)
       for (int j = 0; j < nk; ++j) {
@@ -622,12 +654,9 @@ static cudaError_t hexmm_launch_nb(int tiles, int nkb, cudaStream_t s, uint8_t* 
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  float* xT = reinterpret_cast<float*>(xs + mm_xs_bytes(NB, C));
-  hexmm_xconv<NB><<<nkb, 256, 0, s>>>(x, B, C, amax, xs, xT);
+  const float* xT = reinterpret_cast<const float*>(xs + mm_xs_bytes(NB, C));
+  hexmm_xs_sparse<NB><<<nkb + (R + 7) / 8, 256, 0, s>>>(x, B, C, amax, xs, nkb, xT, R, rp, kc, kd, U, k, tmp, y);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  hexmm_sparse<<<(R + 7) / 8, 256, 0, s>>>(xT, 8 * NB, B, R, C, rp, kc, kd, U, k, tmp, y);
-  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // k-runs per row tile: the split that minimises (waves of resident CTAs) x (k-blocks per run + the
   // set-up and epilogue, about two blocks' worth)
@@ -638,9 +667,18 @@ static cudaError_t hexmm_launch_nb(int tiles, int nkb, cudaStream_t s, uint8_t* 
     const long long cost = (long long)((tiles * ns + slots - 1) / slots) * ((nkb + ns - 1) / ns + 2);
     if (best < 0 || cost < best) best = cost, nsplit = ns;
   }
-  hexmm_kernel<NB><<<dim3(tiles, nsplit), MM_ALL, smem, s>>>(xs, B, codes, scales, xy, n_pts, y, R, C, nsplit,
-                                                                      amax);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(tiles, nsplit);
+  cfg.blockDim = dim3(MM_ALL);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, hexmm_kernel<NB>, (const uint8_t*)xs, B, codes, scales, xy, n_pts, y, R, C, nsplit,
+                            amax);
 }
 
 int num_sms();
@@ -677,8 +715,12 @@ extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* code
   uint8_t* xs = static_cast<uint8_t*>(work) + MM_XS_OFF;  // converted activations
   cudaError_t e = cudaMemsetAsync(work, 0, sizeof(float) * 17 * MM_MAXB, s);
   if (e != cudaSuccess) return record_cuda_error(e);
-  hexmm_prep<<<dim3((batch + 7) / 8, (cols + MM_PREP - 1) / MM_PREP), 256, 0, s>>>(x, batch, cols, Vt, S, k_dim, amax,
-                                                                                  tmp);
+  {
+    const int nb = (batch + 7) / 8;
+    float* xT = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + MM_XS_OFF + mm_xs_bytes(nb, cols));
+    hexmm_prep<<<dim3(nb, (cols + MM_PREP - 1) / MM_PREP), 256, 0, s>>>(x, batch, cols, Vt, S, k_dim, amax, tmp, xT,
+                                                                        8 * nb, y, (size_t)batch * rows);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return record_cuda_error(e);
   const int tiles = (rows + MM_ROWS - 1) / MM_ROWS, nkb = cols / MM_KB;

@@ -57,8 +57,10 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ x, const float* __
 __global__ void rope_kv_rows_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                                     uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
                                     const float2* __restrict__ cs, int layer, int pos0, int n_heads, int n_kv, int hd,
-                                    int max_seq, const int* __restrict__ pos_dev, size_t seq_stride) {
+                                    int max_seq, const int* __restrict__ pos_dev, size_t seq_stride,
+                                    int row_stride) {
   const int t = blockIdx.x, pos = pos_dev ? pos_dev[t] : pos0 + t, half = hd / 2;
+  // row t of q, k, v: row_stride elements apart (0: packed, [n][heads][hd])
   if (pos_dev) {
     kc += (size_t)t * seq_stride;
     vc += (size_t)t * seq_stride;
@@ -68,7 +70,7 @@ __global__ void rope_kv_rows_kernel(float* __restrict__ q, const float* __restri
     return;
   }
   const float2* c = cs + (size_t)pos * half;
-  float* qt = q + (size_t)t * n_heads * hd;
+  float* qt = q + (size_t)t * (row_stride ? row_stride : n_heads * hd);
   for (int e = threadIdx.x; e < n_heads * half; e += blockDim.x) {
     const int h = e / half, i = e - h * half;
     float* p = qt + (size_t)h * hd + 2 * i;
@@ -78,8 +80,8 @@ __global__ void rope_kv_rows_kernel(float* __restrict__ q, const float* __restri
     p[1] = __fadd_rn(__fmul_rn(a, r.y), __fmul_rn(b, r.x));
   }
   const size_t base = ((size_t)layer * max_seq + pos) * n_kv * hd;
-  const float* kt = k + (size_t)t * n_kv * hd;
-  const float* vt = v + (size_t)t * n_kv * hd;
+  const float* kt = k + (size_t)t * (row_stride ? row_stride : n_kv * hd);
+  const float* vt = v + (size_t)t * (row_stride ? row_stride : n_kv * hd);
   for (int e = threadIdx.x; e < n_kv * half; e += blockDim.x) {
     const int h = e / half, i = e - h * half;
     const size_t o = (size_t)h * hd + 2 * i;
@@ -314,7 +316,7 @@ __global__ void __launch_bounds__(AD_THREADS)
     attention_decode_kernel(const float* __restrict__ q, const uint16_t* __restrict__ kc,
                             const uint16_t* __restrict__ vc, size_t seq_stride, float* __restrict__ out,
                             float* __restrict__ work, int layer, const int* __restrict__ pos, int B, int n_heads,
-                            int n_kv, int max_seq, float sm_scale, int splits) {
+                            int n_kv, int max_seq, float sm_scale, int splits, int q_stride) {
   constexpr int DL = HD / 32;  // dimensions per lane in the P.V step
   __shared__ float qs[GQ][HD];
   __shared__ float wm[4][GQ], wl[4][GQ];
@@ -325,7 +327,7 @@ __global__ void __launch_bounds__(AD_THREADS)
   const bool ok = p_last >= 0 && p_last < max_seq;
   if (!ok && tid == 0) raise_flag(GSDLQ_FLAG_BAD_POS);
   const int len = ok ? p_last + 1 : 0;
-  const float* qb = q + ((size_t)b * n_heads + (size_t)g * GQ) * HD;
+  const float* qb = q + (size_t)b * (q_stride ? q_stride : n_heads * HD) + (size_t)g * GQ * HD;
   for (int e = tid; e < GQ * HD; e += AD_THREADS) qs[e / HD][e % HD] = qb[e] * sm_scale;
   __syncthreads();
   const size_t stride = (size_t)n_kv * HD;
@@ -375,26 +377,35 @@ __global__ void __launch_bounds__(AD_THREADS)
 #pragma unroll
       for (int d = 0; d < DL; ++d) acc[h][d] *= f;
     }
+    // P.V: eight positions' V rows loaded together, then their weights broadcast and applied
     const int nvalid = min(32, len - tile * 32);
-    for (int j = 0; j < nvalid; ++j) {
-      const uint16_t* vr = vl + (size_t)(tile * 32 + j) * stride + lane * DL;
-      float vv[DL];
-      if (DL == 4) {
-        const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(vr));
-        vv[0] = h2f((uint16_t)(w2.x & 0xffffu));
-        vv[1] = h2f((uint16_t)(w2.x >> 16));
-        vv[2 % DL] = h2f((uint16_t)(w2.y & 0xffffu));
-        vv[3 % DL] = h2f((uint16_t)(w2.y >> 16));
-      } else {
-        const uint32_t w1 = __ldg(reinterpret_cast<const uint32_t*>(vr));
-        vv[0] = h2f((uint16_t)(w1 & 0xffffu));
-        vv[1 % DL] = h2f((uint16_t)(w1 >> 16));
+    for (int j0 = 0; j0 < nvalid; j0 += 8) {
+      float vv[8][DL];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const int j = min(j0 + jj, nvalid - 1);  // past the tile's last position: re-read it, weight 0 below
+        const uint16_t* vr = vl + (size_t)(tile * 32 + j) * stride + lane * DL;
+        if (DL == 4) {
+          const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(vr));
+          vv[jj][0] = h2f((uint16_t)(w2.x & 0xffffu));
+          vv[jj][1 % DL] = h2f((uint16_t)(w2.x >> 16));
+          vv[jj][2 % DL] = h2f((uint16_t)(w2.y & 0xffffu));
+          vv[jj][3 % DL] = h2f((uint16_t)(w2.y >> 16));
+        } else {
+          const uint32_t w1 = __ldg(reinterpret_cast<const uint32_t*>(vr));
+          vv[jj][0] = h2f((uint16_t)(w1 & 0xffffu));
+          vv[jj][1 % DL] = h2f((uint16_t)(w1 >> 16));
+        }
       }
 #pragma unroll
-      for (int h = 0; h < GQ; ++h) {
-        const float pj = __shfl_sync(0xffffffffu, pw[h], j);
+      for (int jj = 0; jj < 8; ++jj) {
 #pragma unroll
-        for (int d = 0; d < DL; ++d) acc[h][d] = fmaf(pj, vv[d], acc[h][d]);
+        for (int h = 0; h < GQ; ++h) {
+          float pj = __shfl_sync(0xffffffffu, pw[h], (j0 + jj) & 31);
+          if (j0 + jj >= nvalid) pj = 0.f;
+#pragma unroll
+          for (int d = 0; d < DL; ++d) acc[h][d] = fmaf(pj, vv[jj][d], acc[h][d]);
+        }
       }
     }
   }
@@ -483,6 +494,16 @@ __global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restri
   }
 }
 
+// gsd_cpu_swiglu (gsd_lq_cpu_engine.c:97-108) of rows laid out [gate | up]: out[r][i] = silu(g) * u with
+// g = gate_up[r][i], u = gate_up[r][n + i] (the output of one linear over the stacked gate and up rows)
+__global__ void swiglu_rows_kernel(const float* __restrict__ gu, float* __restrict__ out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
+  if (i < n) {
+    const float g = gu[(size_t)r * 2 * n + i];
+    out[(size_t)r * n + i] = (g / (1.0f + expf(-g))) * gu[(size_t)r * 2 * n + n + i];
+  }
+}
+
 static size_t attention_rows_work(int n, int n_heads, int hd) {
   return sizeof(float) * (size_t)AT_MAXSPLIT * n * n_heads * (hd + 2);
 }
@@ -516,21 +537,22 @@ int gsdlq_rope_kv_rows(float* q, const float* k, const float* v, uint16_t* k_cac
   if (pos0 + n > max_seq) return GSDLQ_ERR_INVALID;
   rope_kv_rows_kernel<<<n, 128, 0, static_cast<cudaStream_t>(stream)>>>(
       q, k, v, k_cache, v_cache, reinterpret_cast<const float2*>(rope_cs), layer, pos0, n_heads, n_kv_heads, head_dim,
-      max_seq, nullptr, 0);
+      max_seq, nullptr, 0, 0);
   GSDLQ_CUDA_CHECK_LAUNCH();
   return GSDLQ_OK;
 }
 
-int gsdlq_rope_kv_batch(float* q, const float* k, const float* v, uint16_t* k_cache, uint16_t* v_cache,
-                        size_t seq_stride, const float* rope_cs, int layer, const int* pos, int batch, int n_heads,
-                        int n_kv_heads, int head_dim, int max_seq, gsdlq_stream_t stream) {
+int gsdlq_rope_kv_batch(float* q, const float* k, const float* v, int row_stride, uint16_t* k_cache,
+                        uint16_t* v_cache, size_t seq_stride, const float* rope_cs, int layer, const int* pos, int batch,
+                        int n_heads, int n_kv_heads, int head_dim, int max_seq, gsdlq_stream_t stream) {
   if (!q || !k || !v || !k_cache || !v_cache || !rope_cs || !pos || batch <= 0 || layer < 0 || max_seq <= 0)
     return GSDLQ_ERR_INVALID;
   if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || head_dim % 2) return GSDLQ_ERR_INVALID;
   if (seq_stride < (size_t)(layer + 1) * max_seq * n_kv_heads * head_dim) return GSDLQ_ERR_INVALID;
+  if (row_stride < 0 || (row_stride > 0 && row_stride < n_heads * head_dim)) return GSDLQ_ERR_INVALID;
   rope_kv_rows_kernel<<<batch, 128, 0, static_cast<cudaStream_t>(stream)>>>(
       q, k, v, k_cache, v_cache, reinterpret_cast<const float2*>(rope_cs), layer, 0, n_heads, n_kv_heads, head_dim,
-      max_seq, pos, seq_stride);
+      max_seq, pos, seq_stride, row_stride);
   GSDLQ_CUDA_CHECK_LAUNCH();
   return GSDLQ_OK;
 }
@@ -585,6 +607,13 @@ int gsdlq_attention_rows(const float* q, const uint16_t* k_cache, const uint16_t
   return GSDLQ_OK;
 }
 
+int gsdlq_swiglu_rows(const float* gate_up, float* out, int rows, int n, gsdlq_stream_t stream) {
+  if (!gate_up || !out || rows <= 0 || n <= 0) return GSDLQ_ERR_INVALID;
+  swiglu_rows_kernel<<<dim3((n + 255) / 256, rows), 256, 0, static_cast<cudaStream_t>(stream)>>>(gate_up, out, n);
+  GSDLQ_CUDA_CHECK_LAUNCH();
+  return GSDLQ_OK;
+}
+
 int gsdlq_argmax_rows(const float* logits, int rows, int n, int* ids, int* pos, int* out_ids, int out_stride,
                       gsdlq_stream_t stream) {
   if (!logits || !ids || rows <= 0 || n <= 0 || (out_ids && (!pos || out_stride <= 0))) return GSDLQ_ERR_INVALID;
@@ -593,9 +622,9 @@ int gsdlq_argmax_rows(const float* logits, int rows, int n, int* ids, int* pos, 
   return GSDLQ_OK;
 }
 
-int gsdlq_attention_decode_batch(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, size_t seq_stride,
-                                 float* out, void* work, size_t work_bytes, int layer, const int* pos, int batch,
-                                 int n_heads, int n_kv_heads, int head_dim, int max_seq, float sm_scale,
+int gsdlq_attention_decode_batch(const float* q, int q_stride, const uint16_t* k_cache, const uint16_t* v_cache,
+                                 size_t seq_stride, float* out, void* work, size_t work_bytes, int layer, const int* pos,
+                                 int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, float sm_scale,
                                  gsdlq_stream_t stream) {
   if (!q || !k_cache || !v_cache || !out || !work || !pos || batch <= 0 || layer < 0 || max_seq <= 0)
     return GSDLQ_ERR_INVALID;
@@ -608,6 +637,7 @@ int gsdlq_attention_decode_batch(const float* q, const uint16_t* k_cache, const 
       15u)
     return GSDLQ_ERR_INVALID;
   if ((seq_stride * 2) % 16) return GSDLQ_ERR_INVALID;
+  if (q_stride < 0 || (q_stride > 0 && q_stride < n_heads * head_dim)) return GSDLQ_ERR_INVALID;
   if (work_bytes < attention_rows_work(batch, n_heads, head_dim)) return GSDLQ_ERR_INVALID;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   int dev = 0, sms = 148;
@@ -621,7 +651,8 @@ int gsdlq_attention_decode_batch(const float* q, const uint16_t* k_cache, const 
   float* wk = static_cast<float*>(work);
 #define GSDLQ_AD(hd, g)                                                                                          \
   attention_decode_kernel<hd, g><<<grid, AD_THREADS, 0, st>>>(q, k_cache, v_cache, seq_stride, out, wk, layer, pos, \
-                                                               batch, n_heads, n_kv_heads, max_seq, sm_scale, splits)
+                                                               batch, n_heads, n_kv_heads, max_seq, sm_scale, splits, \
+                                                               q_stride)
   if (head_dim == 64) {
     switch (gq) {
       case 1: GSDLQ_AD(64, 1); break;

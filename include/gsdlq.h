@@ -409,16 +409,21 @@ int gsdlq_attention_rows(const float *q, const uint16_t *k_cache, const uint16_t
  *   attention_decode_batch: gsd_cpu_gqa_attention (gsd_lq_cpu_engine.c:265-330) of row b over
  *                          positions 0 .. pos[b] of sequence b's cache; head_dim 64 or 128, 1, 2, 4,
  *                          6 or 8 query heads per kv head; work: gsdlq_attention_rows_work_size(B, ...)
+ *                          row_stride / q_stride: elements between consecutive rows of q (and k, v),
+ *                          0 for packed rows -- a nonzero stride reads q, k, v out of one linear's output
+ *                          over the stacked q, k and v rows
+ *   swiglu_rows:           gsd_cpu_swiglu (gsd_lq_cpu_engine.c:97-108) of rows laid out [gate | up]
  *   argmax_rows:           greedy pick of every row of logits[rows][n] (the reference's greedy rule)
  *                          into ids[b]; with pos: out_ids[b * out_stride + pos[b] + 1] = pick (when
  *                          out_ids and inside out_stride) and pos[b] += 1 */
-int gsdlq_rope_kv_batch(float *q, const float *k, const float *v, uint16_t *k_cache, uint16_t *v_cache,
-                        size_t seq_stride, const float *rope_cs, int layer, const int *pos, int batch, int n_heads,
-                        int n_kv_heads, int head_dim, int max_seq, gsdlq_stream_t stream);
-int gsdlq_attention_decode_batch(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, size_t seq_stride,
-                                 float *out, void *work, size_t work_bytes, int layer, const int *pos, int batch,
-                                 int n_heads, int n_kv_heads, int head_dim, int max_seq, float sm_scale,
+int gsdlq_rope_kv_batch(float *q, const float *k, const float *v, int row_stride, uint16_t *k_cache,
+                        uint16_t *v_cache, size_t seq_stride, const float *rope_cs, int layer, const int *pos, int batch,
+                        int n_heads, int n_kv_heads, int head_dim, int max_seq, gsdlq_stream_t stream);
+int gsdlq_attention_decode_batch(const float *q, int q_stride, const uint16_t *k_cache, const uint16_t *v_cache,
+                                 size_t seq_stride, float *out, void *work, size_t work_bytes, int layer, const int *pos,
+                                 int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, float sm_scale,
                                  gsdlq_stream_t stream);
+int gsdlq_swiglu_rows(const float *gate_up, float *out, int rows, int n, gsdlq_stream_t stream);
 int gsdlq_argmax_rows(const float *logits, int rows, int n, int *ids, int *pos, int *out_ids, int out_stride,
                       gsdlq_stream_t stream);
 
