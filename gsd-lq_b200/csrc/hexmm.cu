@@ -170,13 +170,14 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-constexpr int MM_CSTAGES = 4;                  // k-blocks of codes in flight per CTA (cp.async ring)
+constexpr int MM_CSTAGES = 6;                  // k-blocks of codes in flight per CTA (cp.async ring)
 // Shared memory, by absolute shared-window address (the dynamic allocation starts at the system-reserved
 // bytes B below MM_HDR_ABS; the kernel checks that B leaves the header room):
 //   [MM_HDR_ABS, MM_TAB_ABS)           barriers, tensor-memory slot, token scales (1 KB)
 //   [MM_TAB_ABS, MM_TAB_ABS + 64 KB)   decode table: 256 rows of 256 bytes, row c = code c's entry in 32
 //                                      lane copies (128 bytes), then a free 128-byte half; the free halves
-//                                      of rows 0-127 hold the code ring, those of rows 128-159 the scales
+//                                      of rows 0-191 hold the code ring (6 stages), those of rows 192-239
+//                                      the scales
 //   [MM_TAB_ABS + 64 KB, ...)          B stages (1024-byte aligned: the swizzle atoms)
 template <int NB>
 constexpr int mm_btile() {  // one k-block of the B operand: 16 NB rows (token hi / lo) x 128 bytes
@@ -210,21 +211,48 @@ constexpr int mm_per_sm() {  // resident CTAs per SM: shared memory and the 512 
 }
 static_assert(mm_per_sm<1>() == 2 && mm_per_sm<4>() == 2 && mm_per_sm<8>() == 2 && mm_per_sm<16>() == 1,
               "CTAs per SM");
+// The small-batch kernel (up to MM_SMALL_NB token groups): integer A (32 columns per stage, no lo part) and
+// SC accumulator slots of N = 16 NB columns, one per k-block in flight (the scale is applied per block).
+constexpr int MM_SMALL_NB = 4;
+template <int NB>
+constexpr int ms_acc_stages() {
+  return NB <= 2 ? 4 : 2;
+}
+template <int NB>
+constexpr int ms_slot() {  // accumulator columns per slot: N rounded up to 32
+  return (16 * NB + 31) / 32 * 32;
+}
+template <int NB>
+constexpr int ms_acol() {  // first A-stage column: after the accumulator slots
+  return ms_slot<NB>() * ms_acc_stages<NB>();
+}
+constexpr int MS_ASTAGES = 3;
+template <int NB>
+constexpr int ms_tcols() {
+  return ms_acol<NB>() + 32 * MS_ASTAGES <= 256 ? 256 : 512;
+}
+static_assert(ms_tcols<1>() == 256 && ms_tcols<2>() == 256 && ms_tcols<3>() == 256 && ms_tcols<4>() == 256,
+              "two small-batch CTAs share an SM's 512 tensor-memory columns");
+static_assert(mm_per_sm<MM_SMALL_NB>() <= 2, "the small-batch kernel's CTAs per SM fit 512 tensor-memory columns");
 // ring slot of (stage, row, half): table row 32 stage + row / 4, free half, 32-byte pair of the row's
 // halves (XOR 16 on odd row quads, so that the 8 lanes of a 16-byte load phase hit 8 bank groups)
 __host__ __device__ constexpr uint32_t mm_ring(int st, int r, int h) {
   return MM_TAB_ABS + (uint32_t)(st * 32 + r / 4) * 256u + 128u +
          ((uint32_t)((r & 3) * 32 + h * 16) ^ (uint32_t)(((r >> 2) & 1) * 16));
 }
-// scale-ring slot of (stage, half, row): the 4-byte scale pair, rows of 32 in the free halves of 128 ..
+// scale-ring slot of (stage, half, row): the 4-byte scale pair, rows of 32 in the free halves of 192 ..
 __host__ __device__ constexpr uint32_t mm_scring(int st, int h, int r) {
-  return MM_TAB_ABS + (uint32_t)(128 + st * 8 + h * 4 + r / 32) * 256u + 128u + (uint32_t)(r % 32) * 4u;
+  return MM_TAB_ABS + (uint32_t)(32 * MM_CSTAGES + st * 8 + h * 4 + r / 32) * 256u + 128u + (uint32_t)(r % 32) * 4u;
 }
+static_assert(32 * MM_CSTAGES + 8 * MM_CSTAGES <= 256, "the code and scale rings fit the table rows' free halves");
 
 // The B operand of every k-block, made once per call: token b's row of the block as fp16 hi (row 2b) and
 // lo (row 2b + 1) of x_b scaled by its power of two, in the swizzled layout of a 64-column tile, one
 // contiguous block of mm_btile<NB>() bytes per k-block (tokens past the batch are zero).
-template <int NB>
+// A2: the pair (x[2p], x[2p+1]) is written as (a, b) = (x[2p], x[2p]/2 + sqrt3/2 x[2p+1]), the activations
+// the integer lattice coordinates (r0, r1) of a code multiply: r0 a + r1 b = x-coord x[2p] + y-coord x[2p+1]
+// with (x-coord, y-coord) = (r0 + r1/2, r1 sqrt3/2) the code's point (the small-batch kernel's operands).
+template <int NB, bool A2 = false>
 __device__ void hexmm_xconv_block(const float* __restrict__ x, int B, int C, const unsigned* __restrict__ amax_bits,
                                   uint8_t* __restrict__ xs, int kb) {
   constexpr int BP = 8 * NB;
@@ -238,6 +266,10 @@ __device__ void hexmm_xconv_block(const float* __restrict__ x, int B, int C, con
       const float4 u0 = xp[0], u1 = xp[1];
       v[0] = u0.x * f, v[1] = u0.y * f, v[2] = u0.z * f, v[3] = u0.w * f;
       v[4] = u1.x * f, v[5] = u1.y * f, v[6] = u1.z * f, v[7] = u1.w * f;
+      if (A2) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) v[2 * t + 1] = fmaf(0.8660254037844386f, v[2 * t + 1], 0.5f * v[2 * t]);
+      }
     } else {
 #pragma unroll
       for (int t = 0; t < 8; ++t) v[t] = 0.f;
@@ -371,7 +403,7 @@ __device__ void hexmm_sparse_rows(const float* __restrict__ xT, int BP, int B, i
 // The B tiles (CTAs 0 .. nkb - 1, one k-block each) and the sparse terms (the rest, 8 rows each) in one
 // launch: both need only hexmm_prep's results.  Every CTA lets the dense kernel launch at once
 // (programmatic dependent launch); that kernel waits for this one only before its first B-tile copy.
-template <int NB>
+template <int NB, bool A2>
 __global__ void __launch_bounds__(256) hexmm_xs_sparse(const float* __restrict__ x, int B, int C,
                                                        const unsigned* __restrict__ amax_bits,
                                                        uint8_t* __restrict__ xs, int nkb,
@@ -384,7 +416,7 @@ __global__ void __launch_bounds__(256) hexmm_xs_sparse(const float* __restrict__
   __shared__ float tmp_s[MM_MAXB * 17];
   asm volatile("griddepcontrol.launch_dependents;");
   if ((int)blockIdx.x < nkb)
-    hexmm_xconv_block<NB>(x, B, C, amax_bits, xs, blockIdx.x);
+    hexmm_xconv_block<NB, A2>(x, B, C, amax_bits, xs, blockIdx.x);
   else
     hexmm_sparse_rows(xT, 8 * NB, B, R, C, row_ptr, kcols, kdel, U, k, tmp, y, blockIdx.x - nkb, tmp_s);
 }
@@ -523,7 +555,7 @@ __global__ void __launch_bounds__(MM_ALL) hexmm_kernel(const uint8_t* __restrict
     int q = 0;
     uint32_t pe = 1u;  // A stage and the parity of its empty phase to wait for (none on the first pass)
     for (int i = 0; i < nk; ++i) {
-      const int kb = kb0 + i, st = i & (MM_CSTAGES - 1);
+      const int kb = kb0 + i, st = i % MM_CSTAGES;
 #ifdef GSDLQ_TRACE
       if (trc && tid == 0 && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2), tr_now());
 #endif
@@ -631,6 +663,283 @@ __global__ void __launch_bounds__(MM_ALL) hexmm_kernel(const uint8_t* __restrict
   }
 }
 
+// Decode-table entry of the small-batch kernel: the code's integer lattice coordinates (r0, r1) as fp16
+// (exact), from the caller's xy table (checked to be the A2 lattice, as mm_entry does).
+__device__ __forceinline__ uint32_t ms_entry(const float* xy, int n_pts, int i) {
+  if (i >= n_pts) return 0u;
+  const float x = xy[2 * i], y = xy[2 * i + 1];
+  const float r1 = rintf(y * 1.1547005383792515f);
+  const float r0 = x - 0.5f * r1;
+  if (r0 != rintf(r0) || (float)((double)r1 * 0.8660254037844386) != y || fabsf(r0) > 16.f || fabsf(r1) > 16.f) {
+    raise_flag(GSDLQ_FLAG_BAD_TABLE);
+    return 0u;
+  }
+  return pack_h2(r0, r1);
+}
+
+// The small-batch dense kernel (up to 8 MM_SMALL_NB tokens).  The weights enter the tensor cores as their
+// integer lattice coordinates (exact in fp16, no lo part, no scale) against the A2-transformed activations,
+// and every 64-column k-block (one scale group) accumulates into its own tensor-memory slot: decoder
+// thread t reads its row's slot of block i - (SC - 1) with tcgen05.ld and adds scale x (hi + lo) of each
+// token in its half of the slot to registers, then frees the slot.  Per code the decoders do one byte
+// permute and one shared load.  Roles, rings, the table layout and the loader are those of hexmm_kernel.
+template <int NB>
+__global__ void __launch_bounds__(MM_ALL) hexmm_small_kernel(const uint8_t* __restrict__ xs, int B,
+                                                             const uint8_t* __restrict__ codes,
+                                                             const uint16_t* __restrict__ scales,
+                                                             const float* __restrict__ xy, int n_pts,
+                                                             float* __restrict__ y, int R, int C, int nsplit,
+                                                             const unsigned* __restrict__ amax_bits) {
+  constexpr int N = 16 * NB, BP = 8 * NB, SA = MS_ASTAGES, SB = mm_bstages<NB>(), SC = ms_acc_stages<NB>();
+  constexpr int HT = 4 * NB;  // tokens in a thread's half of a slot
+  constexpr uint32_t TCOLS = (uint32_t)ms_tcols<NB>(), ACOL = (uint32_t)ms_acol<NB>(), SLOT = (uint32_t)ms_slot<NB>();
+  constexpr int BTILE = mm_btile<NB>();
+  extern __shared__ __align__(1024) uint8_t sm[];
+  const uint32_t sbase = smem_u32(sm);
+  if (sbase > MM_HDR_ABS) {  // the layout's assumption on the reserved bytes
+    if (threadIdx.x == 0) raise_flag(GSDLQ_FLAG_UNSUPPORTED);
+    return;
+  }
+  // header: afull[SA] | aempty[SA] | bfull[SB] | bempty[SB] | cfull[SC] | cfree[SC] (8 bytes each), the
+  // tensor-memory slot, token scales
+  uint8_t* hdr = sm + (MM_HDR_ABS - sbase);
+  const uint32_t afull = MM_HDR_ABS, aempty = MM_HDR_ABS + 32, bfull = MM_HDR_ABS + 64, bempty = MM_HDR_ABS + 128;
+  const uint32_t cfull = MM_HDR_ABS + 192, cfree = MM_HDR_ABS + 224;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(hdr + 256);
+  float* inv_xsc = reinterpret_cast<float*>(hdr + 512);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r0 = blockIdx.x * MM_ROWS, split = blockIdx.y;
+  const int NP = C / 2, G = C / 64, nkb = C / MM_KB;
+  const int kb0 = (int)((long long)nkb * split / nsplit), kb1 = (int)((long long)nkb * (split + 1) / nsplit);
+  const int nk = kb1 - kb0;
+  const bool sc_async = (G % 2 == 0) && ((reinterpret_cast<uintptr_t>(scales) & 3u) == 0);
+  const int lr = tid & (MM_ROWS - 1), half = (tid >> 7) & 1;
+  const int row = r0 + lr;
+  const bool rok = tid < MM_THREADS && row < R;
+  const uint8_t* cp = codes + (size_t)(rok ? row : 0) * NP + half * 16;
+  const uint16_t* scp = scales + (size_t)(rok ? row : 0) * G;
+  auto fetch = [&](int i) {
+    if (i < nk && rok) {
+      const int st = i % MM_CSTAGES;
+      cp_async_16(sm + (mm_ring(st, lr, half) - sbase), cp + (kb0 + i) * 32);
+      if (sc_async) cp_async_4(sm + (mm_scring(st, half, lr) - sbase), scp + ((kb0 + i) & ~1));
+    }
+    cp_async_commit();
+  };
+  if (tid < MM_THREADS) {
+#pragma unroll
+    for (int i = 0; i < MM_CSTAGES - 1; ++i) fetch(i);
+    const uint32_t ent = ms_entry(xy, n_pts, tid);
+#pragma unroll 8
+    for (int i = 0; i < 32; ++i) st_shared_u32(MM_TAB_ABS + (uint32_t)tid * 256u + (uint32_t)((i + tid) & 31) * 4u, ent);
+    if (tid < BP) inv_xsc[tid] = tid < B ? 1.0f / hexmm_xscale(amax_bits[tid]) : 0.f;
+  }
+  if (tid == 0) {
+#pragma unroll
+    for (int q = 0; q < SA; ++q) {
+      mbar_init(afull + 8u * q, (uint32_t)MM_THREADS);
+      mbar_init(aempty + 8u * q, 1u);
+    }
+#pragma unroll
+    for (int q = 0; q < SB; ++q) {
+      mbar_init(bfull + 8u * q, 1u);
+      mbar_init(bempty + 8u * q, 1u);
+    }
+#pragma unroll
+    for (int q = 0; q < SC; ++q) {
+      mbar_init(cfull + 8u * q, 1u);
+      mbar_init(cfree + 8u * q, (uint32_t)MM_THREADS);
+    }
+    mbar_fence_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), TCOLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot);
+
+  if (warp == MM_THREADS / 32 + 1) {
+    // ---- B loader (as in hexmm_kernel) ----
+    if (lane == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      int q = 0;
+      uint32_t pe = 1u;
+      for (int j = 0; j < nk; ++j) {
+        if (j >= SB) mbar_wait_bounded(bempty + 8u * q, pe);
+        mbar_arrive_expect_tx(bfull + 8u * q, (uint32_t)BTILE);
+        bulk_g2s(MM_B_ABS + q * BTILE, xs + (size_t)(kb0 + j) * BTILE, (uint32_t)BTILE, bfull + 8u * q);
+        if (++q == SB) q = 0, pe ^= 1u;
+      }
+    }
+  } else if (warp == MM_THREADS / 32) {
+    // ---- issuer: block i's four MMAs into accumulator slot i % SC (which the decoders have freed) ----
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(MM_ROWS >> 4) << 24);
+      int qa = 0, qb = 0, qc = 0;
+      uint32_t pa = 0u, pb = 0u, pc = 1u;
+#ifdef GSDLQ_TRACE
+      const bool trc = blockIdx.y == 0;
+      if (trc) GSDLQ_TR_SET(0u, 21, tr_now());
+#endif
+      for (int i = 0; i < nk; ++i) {
+        mbar_wait_bounded(afull + 8u * qa, pa);
+        mbar_wait_bounded(bfull + 8u * qb, pb);
+        if (i >= SC) mbar_wait_bounded(cfree + 8u * qc, pc);
+        tc_fence_after();
+#ifdef GSDLQ_TRACE
+        if (trc && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 5, tr_now());
+#endif
+#pragma unroll
+        for (int kk = 0; kk < MM_KB / 16; ++kk) {
+          const uint64_t bd = umma_desc(MM_B_ABS + qb * BTILE + kk * 32);
+          umma_f16_ts(tmem + SLOT * (uint32_t)qc, tmem + ACOL + 32u * (uint32_t)qa + 8u * (uint32_t)kk, bd, idesc,
+                      kk > 0 ? 1u : 0u);
+        }
+        umma_commit(aempty + 8u * qa);
+        umma_commit(bempty + 8u * qb);
+        umma_commit(cfull + 8u * qc);
+#ifdef GSDLQ_TRACE
+        if (trc && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 6, tr_now());
+#endif
+        if (++qa == SA) qa = 0, pa ^= 1u;
+        if (++qb == SB) qb = 0, pb ^= 1u;
+        if (++qc == SC) qc = 0, pc ^= 1u;
+      }
+    }
+  } else {
+    // ---- decoders ----
+    const uint32_t lane4 = (uint32_t)lane * 4u;
+    const uint32_t my_lane = (uint32_t)((warp & 3) * 32) << 16;
+    uint32_t cmax = 0u;
+    float yacc[HT];
+#pragma unroll
+    for (int t = 0; t < HT; ++t) yacc[t] = 0.f;
+    float shist[SC];  // the scales of the blocks whose slots are still to be read, oldest first
+#pragma unroll
+    for (int t = 0; t < SC; ++t) shist[t] = 0.f;
+    int qa = 0, qc = 0;
+    uint32_t pea = 1u, pfc = 0u;
+    // block j's slot: wait for its MMAs, add scale x (hi + lo) per token of this thread's half, free it
+    auto drain = [&](float sj) {
+      mbar_wait_bounded(cfull + 8u * qc, pfc);
+      tc_fence_after();
+      __syncwarp();
+      // the slot's N columns in aligned 16-column loads (8 tokens each); this thread keeps its half's tokens
+      uint32_t v[16];
+#pragma unroll
+      for (int c = 0; c < N / 16; ++c) {
+        tmem_ld16(tmem + my_lane + SLOT * (uint32_t)qc + (uint32_t)(16 * c), v);
+        if (half == 0) {
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            if (8 * c + t < HT)
+              yacc[8 * c + t] = fmaf(sj, __uint_as_float(v[2 * t]) + __uint_as_float(v[2 * t + 1]), yacc[8 * c + t]);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            if (8 * c + t >= HT && 8 * c + t < 2 * HT)
+              yacc[8 * c + t - HT] =
+                  fmaf(sj, __uint_as_float(v[2 * t]) + __uint_as_float(v[2 * t + 1]), yacc[8 * c + t - HT]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive1(cfree + 8u * qc);
+      if (++qc == SC) qc = 0, pfc ^= 1u;
+    };
+#ifdef GSDLQ_TRACE
+    const bool trd = blockIdx.y == 0 && tid == 0;
+#endif
+    for (int i = 0; i < nk; ++i) {
+      const int kb = kb0 + i, st = i % MM_CSTAGES;
+#ifdef GSDLQ_TRACE
+      if (trd && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2), tr_now());
+#endif
+      fetch(i + MM_CSTAGES - 1);
+      cp_async_wait<MM_CSTAGES - 1>();
+#ifdef GSDLQ_TRACE
+      if (trd && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 1, tr_now());
+#endif
+      uint32_t scw;
+      if (sc_async) {
+        scw = ld_shared_u32(mm_scring(st, half, lr));
+        scw = (kb & 1) ? scw >> 16 : scw & 0xffffu;
+      } else {
+        scw = rok ? scp[kb] : 0u;
+      }
+      const uint4 cw = *reinterpret_cast<const uint4*>(sm + (mm_ring(st, lr, half) - sbase));
+      const uint32_t cv[4] = {cw.x, cw.y, cw.z, cw.w};
+      uint32_t a[16];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        cmax = __vmaxu4(cmax, cv[jj]);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) a[4 * jj + p] = mm_lookup(cv[jj], lane4, 0x6604u | (uint32_t)(p << 4));
+      }
+#ifdef GSDLQ_TRACE
+      if (trd && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 2, (unsigned long long)a[15] * 0ull + tr_now());
+#endif
+      if (i >= SA) mbar_wait_bounded(aempty + 8u * qa, pea);
+      tc_fence_after();
+#ifdef GSDLQ_TRACE
+      if (trd && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 3, tr_now());
+#endif
+      __syncwarp();
+      tmem_st16(tmem + my_lane + ACOL + 32u * (uint32_t)qa + 16u * (uint32_t)half, a);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive1(afull + 8u * qa);
+#ifdef GSDLQ_TRACE
+      if (trd && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 7 * (i - 2) + 4, tr_now());
+#endif
+      if (++qa == SA) qa = 0, pea ^= 1u;
+      // the scale of block i joins the history; the slot of block i - (SC - 1) is read
+#pragma unroll
+      for (int t = 0; t < SC - 1; ++t) shist[t] = shist[t + 1];
+      shist[SC - 1] = h2f((uint16_t)scw);
+      if (i >= SC - 1) drain(shist[0]);
+#ifdef GSDLQ_TRACE
+      if (trd && i >= 2 && i < 5) GSDLQ_TR_SET(0u, 22 + (i - 2), tr_now());
+#endif
+    }
+#ifdef GSDLQ_TRACE
+    if (trd) GSDLQ_TR_SET(0u, 25, tr_now());
+    if (trd) GSDLQ_TR_SET(0u, 28, (unsigned long long)nk);
+#endif
+    // the last SC - 1 blocks' slots (fewer when the run is shorter)
+    for (int t = 0; t < SC - 1; ++t) {
+      if (nk - (SC - 1) + t >= 0) {
+        float sj = 0.f;
+#pragma unroll
+        for (int u = 0; u < SC; ++u)
+          if (u == t + 1) sj = shist[u];
+        drain(sj);
+      }
+    }
+    cp_async_wait<0>();
+    {
+      const uint32_t mx = max(max(cmax & 0xffu, (cmax >> 8) & 0xffu), max((cmax >> 16) & 0xffu, cmax >> 24));
+      if (rok && (int)mx >= n_pts) raise_flag(GSDLQ_FLAG_BAD_CODE);
+    }
+    if (row < R && tid < MM_THREADS) {
+#pragma unroll
+      for (int t = 0; t < HT; ++t) {
+        const int b = half * HT + t;
+        if (b < B) atomicAdd(y + (size_t)b * R + row, yacc[t] * inv_xsc[b]);
+      }
+    }
+#ifdef GSDLQ_TRACE
+    if (trd) GSDLQ_TR_SET(0u, 26, tr_now());
+#endif
+  }
+  // ---- release the tensor memory ----
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TCOLS);
+  }
+}
+
 // The work buffer: per-token maxima ([0, 512)), per-token low-rank projections ([512, 8704)), from
 // MM_XS_OFF the converted activations (one B tile per k-block), then the transposed fp32 activations.
 constexpr size_t MM_XS_OFF = 16384;
@@ -645,17 +954,26 @@ static cudaError_t hexmm_launch_nb(int tiles, int nkb, cudaStream_t s, uint8_t* 
                                    const uint8_t* codes, const uint16_t* scales, const float* xy, int n_pts,
                                    const uint16_t* U, int k, const uint32_t* rp, const uint16_t* kc, const float* kd,
                                    float* y, int R, int C, const unsigned* amax, const float* tmp) {
+  // up to MM_SMALL_NB token groups: the small-batch kernel (integer A, a scale per k-block slot)
+  constexpr bool SMALL = NB <= MM_SMALL_NB;
   constexpr int smem = mm_smem<NB>();
+  void (*kern)(const uint8_t*, int, const uint8_t*, const uint16_t*, const float*, int, float*, int, int, int,
+               const unsigned*);
+  if constexpr (SMALL)
+    kern = hexmm_small_kernel<NB>;
+  else
+    kern = hexmm_kernel<NB>;
   static bool configured[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
   if (!configured[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(hexmm_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   const float* xT = reinterpret_cast<const float*>(xs + mm_xs_bytes(NB, C));
-  hexmm_xs_sparse<NB><<<nkb + (R + 7) / 8, 256, 0, s>>>(x, B, C, amax, xs, nkb, xT, R, rp, kc, kd, U, k, tmp, y);
+  hexmm_xs_sparse<NB, SMALL><<<nkb + (R + 7) / 8, 256, 0, s>>>(x, B, C, amax, xs, nkb, xT, R, rp, kc, kd, U, k, tmp,
+                                                               y);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // k-runs per row tile: the split that minimises (waves of resident CTAs) x (k-blocks per run + the
@@ -677,8 +995,7 @@ static cudaError_t hexmm_launch_nb(int tiles, int nkb, cudaStream_t s, uint8_t* 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, hexmm_kernel<NB>, (const uint8_t*)xs, B, codes, scales, xy, n_pts, y, R, C, nsplit,
-                            amax);
+  return cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)xs, B, codes, scales, xy, n_pts, y, R, C, nsplit, amax);
 }
 
 int num_sms();
