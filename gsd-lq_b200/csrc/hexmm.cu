@@ -344,11 +344,14 @@ __device__ void hexmm_sparse_rows(const float* __restrict__ xT, int BP, int B, i
                                   const float* __restrict__ tmp, float* __restrict__ y, int rb, float* tmp_s) {
   constexpr int TC = MM_MAXB / 32;  // token chunks
   // tmp_s: tmp[b][j] at 17 b + j, so that lane b's reads hit 32 banks
-  for (int i = threadIdx.x; i < B * 16; i += blockDim.x) tmp_s[(i >> 4) * 17 + (i & 15)] = tmp[i];
-  __syncthreads();
+  if (k > 0) {
+    for (int i = threadIdx.x; i < B * 16; i += blockDim.x) tmp_s[(i >> 4) * 17 + (i & 15)] = tmp[i];
+    __syncthreads();
+  }
   const int lane = threadIdx.x & 31, row = rb * 8 + (threadIdx.x >> 5);
   if (row >= R) return;
   const uint32_t e0 = row_ptr[row], e1 = row_ptr[row + 1];
+  if (e0 == e1 && k == 0) return;  // nothing to add (Turbo rows)
   const int nch = (B + 31) / 32;
   float acc[TC];
 #pragma unroll
