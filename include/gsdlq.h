@@ -365,8 +365,8 @@ int gsdlq_rope_table(float *table, int max_seq, int head_dim, float rope_theta);
  * bytes, 1024-byte aligned (per-token maxima and low-rank projections, and the activations converted
  * once into the tensor cores' operand layout and transposed).  1 <= batch <= GSDLQ_MATMUL_MAX_BATCH,
  * cols a multiple of 64 and at most 65535, k_dim <= 16, n_pts <= 256, codes and Vt 16-byte aligned,
- * xy_table the A2 lattice points (as the matvec requires), scales at most 5 (GSDLQ_FLAG_RANGE
- * otherwise).  Weights and activations enter the tensor cores as fp16 hi + lo parts (about 22
+ * xy_table the A2 lattice points (as the matvec requires); above 32 tokens scales at most 5
+ * (GSDLQ_FLAG_RANGE otherwise).  Weights and activations enter the tensor cores as fp16 hi + lo parts (about 22
  * significant bits): results match the per-token matvec to about 1e-6 relative.  The partial sums
  * are added with atomics, so the last bits may differ between runs. */
 #define GSDLQ_MATMUL_MAX_BATCH 128
