@@ -19,7 +19,7 @@ def env(cuda_lib):
 
 @pytest.mark.parametrize("rows,cols,k,nnz,radius", [
     (16, 64, 0, 0, 8), (100, 512, 16, 2, 8), (1024, 4096, 16, 16, 8), (4096, 4096, 8, 16, 6), (700, 14336, 16, 56, 8)])
-@pytest.mark.parametrize("batch", [1, 3, 16, 64, 128])
+@pytest.mark.parametrize("batch", [1, 3, 16, 24, 32, 40, 64, 100, 128])  # token groups 1-4: small kernel
 def test_matmul_vs_oracle(env, restated, rng, rows, cols, k, nnz, radius, batch):
     ops, L = env
     import gsdlq_b200.codebook as cb
