@@ -66,11 +66,16 @@ def test_batch_decode_matches_single_sequence(cuda_lib, name, over, mode, batch)
         lr = om.forward_token(t, pos, return_logits=pos == len(pr) - 1)
     assert float(np.max(np.abs(lr - got[0][0]))) < LOGIT_TOL
     assert L.device_flags() == 0
-    # generate: the same continuations as the step loop above
+    # generate: the same continuations as the step loop above (its own batched prefill may differ from the
+    # first one in the last bits -- the GEMM adds with atomics -- so a pick may differ only at a near-tie,
+    # after which that sequence is not compared further)
     bd2 = BatchDecoder(m, batch, max_seq=320)
     outs = bd2.generate(prompts, steps)
     for b in range(batch):
-        assert outs[b] == [int(picks[s][b]) for s in range(steps)]
+        for s in range(steps):
+            if outs[b][s] != int(picks[s][b]):
+                assert top2_margin(got[s][b]) < NEAR_TIE, (b, s)
+                break
     bd.release()
     bd2.release()
     m.release()
