@@ -80,7 +80,7 @@ class HexTensor:
     def nbytes(self) -> int:
         return int(sum(a.nbytes for a in self.blobs().values()))
 
-    def validate(self, check_codes: bool = True) -> None:
+    def validate(self, check_codes: bool = True, check_values: bool = False) -> None:
         r, c, k = self.rows, self.cols, self.k_dim
         if r <= 0 or c <= 0:
             raise FormatError(f"bad shape {r}x{c}")
@@ -113,6 +113,16 @@ class HexTensor:
             raise FormatError("kink column index out of range")
         if check_codes and self.codes.size and int(self.codes.max()) >= self.n_pts:
             raise FormatError(f"code index >= n_pts={self.n_pts}")
+        if check_values:
+            # fp16 blobs are stored as u16 bit patterns: exponent all ones is inf or NaN
+            for name in ("scales", "U", "Vt"):
+                a = getattr(self, name)
+                if a is not None and a.size and np.any((a & 0x7C00) == 0x7C00):
+                    raise FormatError(f"{name}: non-finite fp16 values")
+            for name in ("S", "kink_deltas"):
+                a = getattr(self, name)
+                if a is not None and a.size and not np.all(np.isfinite(a)):
+                    raise FormatError(f"{name}: non-finite values")
 
     def row_slice(self, r0: int, r1: int) -> "HexTensor":
         """Rows [r0, r1) as a new packed tensor (column-parallel sharding)."""
@@ -182,10 +192,25 @@ def compute_avg_bpw(hexes: dict[str, HexTensor]) -> float:
     return 8.0 * sum(t.nbytes() for t in hexes.values()) / max(w, 1)
 
 
+INT_CONFIG_KEYS = ("n_layers", "hidden_size", "n_heads", "n_kv_heads", "head_dim", "ffn_size", "vocab_size")
+
+
 def check_config(cfg: dict) -> None:
+    """Shape keys are positive integers and rms_eps / rope_theta positive finite numbers, checked before any
+    arithmetic on them (the reference reads them unchecked, gsd_lq_cpu_runtime.py:136-145)."""
+    if not isinstance(cfg, dict):
+        raise FormatError("config must be a JSON object")
     for k in CONFIG_KEYS:
         if k not in cfg:
             raise FormatError(f"config is missing {k!r}")
+    for k in INT_CONFIG_KEYS:
+        v = cfg[k]
+        if isinstance(v, bool) or not isinstance(v, int) or v <= 0:
+            raise FormatError(f"config {k}={v!r} is not a positive integer")
+    for k in ("rms_eps", "rope_theta"):
+        v = cfg[k]
+        if isinstance(v, bool) or not isinstance(v, (int, float)) or not np.isfinite(v) or v <= 0:
+            raise FormatError(f"config {k}={v!r} is not a positive finite number")
     if cfg["n_heads"] % cfg["n_kv_heads"]:
         raise FormatError("n_heads must be a multiple of n_kv_heads")
     if cfg["head_dim"] % 2:
@@ -229,10 +254,11 @@ def write_gsd2(path: str, model: PackedModel) -> None:
         for bn, a in t.blobs().items():
             m[bn] = put(a)
         metas[name] = m
-    header = {"format_version": 2, "mode": model.mode, "alignment": ALIGN,
-              "avg_bpw": float(model.avg_bpw or compute_avg_bpw(model.hex)),
-              "config": model.config, "tensors": metas}
-    header.update(model.extra)
+    # keys carried over from a file that was read come first: the layout keys below describe this file
+    header = dict(model.extra)
+    header.update({"format_version": 2, "mode": model.mode, "alignment": ALIGN,
+                   "avg_bpw": float(model.avg_bpw or compute_avg_bpw(model.hex)),
+                   "config": model.config, "tensors": metas})
     hb = json.dumps(header).encode("utf-8")
     # pad the header so that the blob region starts on an aligned file offset
     pad = (-(12 + len(hb))) % ALIGN
@@ -249,8 +275,13 @@ def write_gsd2(path: str, model: PackedModel) -> None:
 
 
 def read_gsd2(path: str, mmap: bool = True, check_codes: bool = True,
-              progress: Callable[[str], None] | None = None) -> PackedModel:
-    """Parse and validate a .gsd2 file.  Blobs are read-only memory-mapped views when ``mmap``."""
+              progress: Callable[[str], None] | None = None, check_values: bool = True) -> PackedModel:
+    """Parse and validate a .gsd2 file.  Blobs are read-only memory-mapped views when ``mmap``.
+
+    ``check_codes`` scans every code against the codebook size; ``check_values`` checks that scales, norm
+    weights, S, U, Vt and kink deltas are finite.  A header that states an ``alignment`` (this writer's files)
+    must keep every blob offset on it; the reference's own files state none and may place blobs anywhere.
+    """
     size = os.path.getsize(path)
     with open(path, "rb") as f:
         magic = f.read(4)
@@ -266,16 +297,25 @@ def read_gsd2(path: str, mmap: bool = True, check_codes: bool = True,
             header = json.loads(f.read(hlen).decode("utf-8"))
         except (UnicodeDecodeError, json.JSONDecodeError) as e:
             raise FormatError(f"header is not JSON: {e}") from None
+    if not isinstance(header, dict):
+        raise FormatError("header must be a JSON object")
+    align = header.get("alignment", 1)
+    if isinstance(align, bool) or not isinstance(align, int) or align <= 0 or align & (align - 1):
+        raise FormatError(f"alignment {align!r} is not a positive power of two")
     base = 12 + hlen
     data = np.memmap(path, dtype=np.uint8, mode="r") if mmap else np.fromfile(path, dtype=np.uint8)
 
     def blob(meta: dict, dt, what: str) -> np.ndarray:
         try:
-            o, n = int(meta["offset"]), int(meta["nbytes"])
-        except (KeyError, TypeError, ValueError):
+            o, n = meta["offset"], meta["nbytes"]
+            if isinstance(o, bool) or isinstance(n, bool) or not isinstance(o, int) or not isinstance(n, int):
+                raise TypeError
+        except (KeyError, TypeError):
             raise FormatError(f"{what}: malformed blob descriptor") from None
         if o < 0 or n < 0 or base + o + n > size:
             raise FormatError(f"{what}: blob [{o}, {o + n}) runs past the end of the file")
+        if o % align:
+            raise FormatError(f"{what}: offset {o} breaks the header's {align}-byte alignment")
         if n % np.dtype(dt).itemsize:
             raise FormatError(f"{what}: {n} bytes is not a whole number of {np.dtype(dt)}")
         return data[base + o:base + o + n].view(dt)
@@ -285,17 +325,27 @@ def read_gsd2(path: str, mmap: bool = True, check_codes: bool = True,
     cfg = header["config"]
     check_config(cfg)
     tensors = header["tensors"]
+    if not isinstance(tensors, dict) or not all(isinstance(v, dict) for v in tensors.values()):
+        raise FormatError("tensors must map names to JSON objects")
     L = cfg["n_layers"]
     dense: dict[str, np.ndarray] = {}
     for name in dense_names(L):
         if name not in tensors:
             raise FormatError(f"missing tensor {name}")
-        m = tensors[name]["data"]
+        m = tensors[name].get("data")
+        if not isinstance(m, dict):
+            raise FormatError(f"{name}: missing data descriptor")
         dt = np.float16 if name == "token_embd.weight" else np.float32
         a = blob(m, dt, name)
-        shape = tuple(m.get("shape", [a.size]))
+        shape = m.get("shape", [a.size])
+        if not isinstance(shape, list) or not all(isinstance(d, int) and not isinstance(d, bool) and d >= 0
+                                                  for d in shape):
+            raise FormatError(f"{name}: shape {shape!r} is not a list of sizes")
+        shape = tuple(shape)
         if int(np.prod(shape)) != a.size:
             raise FormatError(f"{name}: shape {shape} does not match {a.size} elements")
+        if check_values and not np.all(np.isfinite(a)):
+            raise FormatError(f"{name}: non-finite values")
         dense[name] = a.reshape(shape)
     H, V = cfg["hidden_size"], cfg["vocab_size"]
     if dense["token_embd.weight"].shape != (V, H):
@@ -324,7 +374,7 @@ def read_gsd2(path: str, mmap: bool = True, check_codes: bool = True,
         except KeyError as e:
             raise FormatError(f"{name}: missing field {e}") from None
         try:
-            t.validate(check_codes=check_codes)
+            t.validate(check_codes=check_codes, check_values=check_values)
         except FormatError as e:
             raise FormatError(f"{name}: {e}") from None
         hexes[name] = t

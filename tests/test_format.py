@@ -166,12 +166,104 @@ def test_out_of_range_code_rejected(tmp_path):
     (lambda h: h["tensors"]["blk.0.attn_q.weight"].__setitem__("cols", 96), "multiple of 64"),
     (lambda h: h["config"].__setitem__("n_kv_heads", 3), "multiple of n_kv_heads"),
     (lambda h: h["tensors"].pop("blk.0.ffn_up.weight"), "missing tensor"),
+    (lambda h: h["config"].__setitem__("n_kv_heads", 0), "positive integer"),
+    (lambda h: h["config"].__setitem__("n_layers", "1"), "positive integer"),
+    (lambda h: h["config"].__setitem__("head_dim", 64.0), "positive integer"),
+    (lambda h: h["config"].__setitem__("rms_eps", -1e-5), "positive finite"),
+    (lambda h: h["config"].__setitem__("rope_theta", None), "positive finite"),
+    (lambda h: h.__setitem__("config", [1, 2]), "JSON object"),
+    (lambda h: h.__setitem__("alignment", 96), "power of two"),
+    (lambda h: h["tensors"].__setitem__("output_norm.weight", {"x": 1}), "data descriptor"),
+    (lambda h: h["tensors"].__setitem__("blk.0.attn_k.weight", 7), "JSON objects"),
+    (lambda h: h["tensors"]["blk.0.attn_q.weight"]["codes"].__setitem__("offset", 0.5), "malformed"),
+    (lambda h: h["tensors"]["blk.0.attn_q.weight"]["scales"].__setitem__("nbytes", True), "malformed"),
+    (lambda h: h["tensors"]["blk.0.attn_q.weight"]["codes"].__setitem__(
+        "offset", h["tensors"]["blk.0.attn_q.weight"]["codes"]["offset"] + 4), "alignment"),
+    (lambda h: h["tensors"]["token_embd.weight"]["data"].__setitem__("shape", [32, -64]), "list of sizes"),
 ])
 def test_header_violations(tmp_path, mutate, msg):
     p = _tiny_file(tmp_path)
     _rewrite_header(p, mutate)
     with pytest.raises(G.FormatError, match=msg):
         G.read_gsd2(p)
+
+
+def test_header_not_an_object(tmp_path):
+    p = _tiny_file(tmp_path)
+    raw = open(p, "rb").read()
+    hlen = struct.unpack("<Q", raw[4:12])[0]
+    open(p, "wb").write(raw[:12] + b"[]".ljust(hlen) + raw[12 + hlen:])
+    with pytest.raises(G.FormatError, match="JSON object"):
+        G.read_gsd2(p)
+
+
+def _poke(p, tensor, blob, index, value):
+    """Overwrite element ``index`` of one blob in place (``value`` a numpy scalar of the blob's type)."""
+    raw = bytearray(open(p, "rb").read())
+    hlen = struct.unpack("<Q", raw[4:12])[0]
+    meta = json.loads(raw[12:12 + hlen])["tensors"][tensor][blob]
+    b = np.asarray(value).tobytes()
+    off = 12 + hlen + meta["offset"] + index * len(b)
+    raw[off:off + len(b)] = b
+    open(p, "wb").write(bytes(raw))
+
+
+@pytest.mark.parametrize("tensor,blob,value", [
+    ("blk.0.ffn_down.weight", "scales", np.uint16(0x7C00)),      # fp16 +inf
+    ("blk.0.attn_v.weight", "scales", np.uint16(0xFE01)),        # fp16 NaN
+    ("output_norm.weight", "data", np.float32(np.nan)),
+    ("token_embd.weight", "data", np.float16(np.inf)),
+])
+def test_non_finite_values_rejected(tmp_path, tensor, blob, value):
+    p = _tiny_file(tmp_path)
+    _poke(p, tensor, blob, 3, value)
+    with pytest.raises(G.FormatError, match="non-finite"):
+        G.read_gsd2(p)
+    G.read_gsd2(p, check_values=False)  # the structure is intact: only the value check objects
+
+
+def test_non_finite_low_rank_and_kinks_rejected(tmp_path):
+    cfg = P.make_config("tiny", n_layers=1, hidden_size=64, n_heads=1, n_kv_heads=1, head_dim=64,
+                        ffn_size=128, vocab_size=32)
+    for blob, value in (("S", np.float32(np.inf)), ("kink_deltas", np.float32(np.nan)),
+                        ("U", np.uint16(0x7C00)), ("Vt", np.uint16(0xFC00))):
+        p = str(tmp_path / f"{blob}.gsd2")
+        G.write_gsd2(p, P.random_model(cfg, "precision", seed=6))
+        _poke(p, "blk.0.ffn_gate.weight", blob, 1, value)
+        with pytest.raises(G.FormatError, match=f"{blob}: non-finite"):
+            G.read_gsd2(p)
+
+
+def test_unaligned_reference_layout_reads(tmp_path):
+    """A file laid out like the reference's writer (blobs back to back, no ``alignment`` key) reads the
+    same tensors as the aligned file it was made from."""
+    p = _tiny_file(tmp_path)
+    raw = open(p, "rb").read()
+    hlen = struct.unpack("<Q", raw[4:12])[0]
+    hdr = json.loads(raw[12:12 + hlen])
+    body = bytearray()
+    for meta in hdr["tensors"].values():
+        for v in meta.values():
+            if isinstance(v, dict) and "offset" in v:
+                src = 12 + hlen + v["offset"]
+                body += raw[src:src + v["nbytes"]]
+                v["offset"] = len(body) - v["nbytes"]
+    hdr.pop("alignment")
+    hb = json.dumps(hdr).encode()
+    q = str(tmp_path / "packed.gsd2")
+    open(q, "wb").write(G.MAGIC + struct.pack("<Q", len(hb)) + hb + bytes(body))
+    assert (12 + len(hb)) % 4 or any(
+        v["offset"] % 256 for m in hdr["tensors"].values() for v in m.values() if isinstance(v, dict) and "offset" in v)
+    a, b = G.read_gsd2(p), G.read_gsd2(q)
+    for n, t in a.hex.items():
+        for k, x in t.blobs().items():
+            assert np.array_equal(x, getattr(b.hex[n], k)), (n, k)
+    for n, x in a.dense.items():
+        assert np.array_equal(x, b.dense[n]), n
+    # writing what was read restores the aligned layout
+    r = str(tmp_path / "rewritten.gsd2")
+    G.write_gsd2(r, b)
+    G.read_gsd2(r)
 
 
 def test_kink_invariants():
