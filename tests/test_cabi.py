@@ -124,3 +124,59 @@ int main(void) {
     ver, msg, n6, n8, st, bad = out.stdout.strip().split("|")
     assert ver.startswith("0.") and msg == "invalid argument"
     assert (int(n6), int(n8), int(st), int(bad)) == (127, 217, 0, -1)
+
+
+def test_row_batch_and_sampling_argument_errors_before_launch():
+    """The prefill row kernels, the batched-decode kernels and the sampler refuse bad shapes, strides and
+    alignments on the host before any CUDA call (the stand-in addresses are never dereferenced)."""
+    lib = L.load()
+    A = ctypes.c_void_p(0x100000)
+    odd = ctypes.c_void_p(0x100004)      # 4-byte but not 16-byte aligned
+    nb = ctypes.c_size_t()
+
+    # work sizes are host arithmetic: the exact figures the callers allocate
+    assert lib.gsdlq_sample_work_size(1000, ctypes.byref(nb)) == 0 and nb.value == 4000
+    assert lib.gsdlq_sample_work_size(0, ctypes.byref(nb)) == -1
+    assert lib.gsdlq_sample_work_size(10, None) == -1
+    assert lib.gsdlq_attention_rows_work_size(5, 4, 64, ctypes.byref(nb)) == 0 and nb.value == 4 * 8 * 5 * 4 * 66
+    assert lib.gsdlq_attention_rows_work_size(0, 4, 64, ctypes.byref(nb)) == -1
+    work_ok = nb.value
+
+    def smp(logits=A, n=100, u=A, work=A, wb=400, key=A, idx=None):
+        return lib.gsdlq_sample_top_p(logits, n, 0.7, 0.9, u, None, work, wb, key, idx, None)
+
+    for kw in (dict(logits=None), dict(n=0), dict(u=None), dict(work=None), dict(wb=396), dict(key=None),
+               dict(work=ctypes.c_void_p(0x100002))):
+        assert smp(**kw) == -1, kw
+
+    def rows(q=A, k=A, v=A, out=A, work=A, wb=work_ok, pos0=0, n=5, nh=4, nkv=2, hd=64, max_seq=16):
+        return lib.gsdlq_attention_rows(q, k, v, out, work, wb, 0, pos0, n, nh, nkv, hd, max_seq, 0.125, None)
+
+    for kw in (dict(q=None), dict(n=0), dict(pos0=-1), dict(pos0=12), dict(nkv=3), dict(nh=16, nkv=1),
+               dict(hd=96), dict(hd=32), dict(q=odd), dict(out=odd), dict(work=odd), dict(wb=work_ok - 4)):
+        assert rows(**kw) == -1, kw
+
+    seq = 2 * 16 * 2 * 64  # (layer + 1) * max_seq * n_kv * head_dim for layer 1
+
+    def dec(q_stride=0, k=A, work=A, wb=1 << 20, layer=1, batch=3, nh=4, nkv=2, hd=64, seq_stride=seq):
+        return lib.gsdlq_attention_decode_batch(A, q_stride, k, A, seq_stride, A, work, wb, layer, A, batch, nh, nkv,
+                                                hd, 16, 0.125, None)
+
+    for kw in (dict(batch=0), dict(layer=-1), dict(nh=6, nkv=2), dict(nh=16, nkv=1), dict(hd=32),
+               dict(seq_stride=seq - 1), dict(seq_stride=seq + 1), dict(k=odd), dict(work=odd),
+               dict(q_stride=-1), dict(q_stride=4 * 64 - 1), dict(wb=16)):
+        assert dec(**kw) == -1, kw
+
+    def rkb(row_stride=0, hd=64, seq_stride=seq, layer=1, batch=3):
+        return lib.gsdlq_rope_kv_batch(A, A, A, row_stride, A, A, seq_stride, A, layer, A, batch, 4, 2, hd, 16, None)
+
+    for kw in (dict(hd=63), dict(seq_stride=seq - 1), dict(row_stride=-1), dict(row_stride=100), dict(batch=0),
+               dict(layer=-1)):
+        assert rkb(**kw) == -1, kw
+    assert lib.gsdlq_rope_kv_rows(A, A, A, A, A, A, 0, 10, 7, 4, 2, 64, 16, None) == -1   # 10 + 7 > 16
+    assert lib.gsdlq_embed_rows(A, A, 0, 32, 64, A, None) == -1
+    assert lib.gsdlq_rmsnorm_rows(A, A, A, 2, 0, 1e-5, None) == -1
+    assert lib.gsdlq_swiglu_rows(A, A, 0, 64, None) == -1
+    assert lib.gsdlq_argmax_rows(A, 2, 100, A, None, A, 16, None) == -1   # out_ids without positions
+    assert lib.gsdlq_argmax_rows(A, 2, 100, A, A, A, 0, None) == -1
+    assert lib.gsdlq_advance_eos(A, A, A, A, None, 0, 2, None, None) == -1
