@@ -71,3 +71,38 @@ def test_bench_metric_and_config_names(monkeypatch):
     a.sweep = True
     assert "GB/s" in bench.metric_name(a)
     assert bench.workload_config(a, 1)["shapes"] == [list(s) for s in bench.SWEEP_SHAPES]
+
+
+def _run_bench(args, env_extra=None):
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    env.update(env_extra or {})
+    return subprocess.run([sys.executable, os.path.join(root, "bench.py")] + args, capture_output=True, text=True,
+                          env=env, timeout=300, cwd=root)
+
+
+def test_reference_arm_prints_the_contract_line():
+    """bench.py --impl reference (the reference's C engine on the host cores) prints one JSON line with the
+    contract's keys, its own cpu_baseline and an e2e that moves no bytes over PCIe; ranks other than 0 exit
+    quietly."""
+    import json
+    r = _run_bench(["--impl", "reference", "--model", "tiny", "--prompt", "16", "--steps", "2", "--warmup", "3"])
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    j = json.loads(lines[0])
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+              "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert k in j, k
+    assert j["impl"] == "reference" and j["unit"] == "tok/s" and j["value"] > 0 and j["n_gpus"] == 1
+    assert j["steps"] == 2 and j["warmup"] == 3 and j["higher_is_better"] is True
+    assert j["metric"] == "decode tok/s batch1 tiny-shape Precision" and j["config"]["global_batch"] == 1
+    cb = j["cpu_baseline"]
+    assert cb["value"] == j["value"] and cb["cores"] >= 1 and cb["kind"] in ("reference", "port") and cb["sample"]
+    assert j["e2e"] == {"value": j["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    r = _run_bench(["--impl", "reference", "--model", "tiny", "--prompt", "16", "--steps", "2", "--warmup", "3"],
+                   {"RANK": "1", "WORLD_SIZE": "2"})
+    assert r.returncode == 0 and not r.stdout.strip(), (r.stdout, r.stderr[-2000:])
