@@ -199,6 +199,8 @@ class BatchDecoder:
         if len(prompts) != self.B:
             raise ValueError(f"{self.B} prompts expected")
         for b, pr in enumerate(prompts):
+            if len(pr) == 0:
+                raise ValueError("every prompt needs at least one token")
             if len(pr) + max_new_tokens > self.S:
                 raise ValueError("prompt + new tokens exceed max_seq")
             self.prefill(b, pr[:-1])
