@@ -29,6 +29,7 @@
 //     and commits them to the stages' empty barriers.
 // At the end the decoder warps read the accumulator lanes with tcgen05.ld, add each token's hi and lo
 // columns, unscale and add them into y.
+#include <atomic>
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -966,13 +967,13 @@ static cudaError_t hexmm_launch_nb(int tiles, int nkb, cudaStream_t s, uint8_t* 
     kern = hexmm_small_kernel<NB>;
   else
     kern = hexmm_kernel<NB>;
-  static bool configured[64] = {};
+  static std::atomic<bool> configured[64];  // per device: the dynamic shared-memory opt-in is done
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  if (!configured[dev]) {
+  if (!configured[dev].load(std::memory_order_acquire)) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   const float* xT = reinterpret_cast<const float*>(xs + mm_xs_bytes(NB, C));
   hexmm_xs_sparse<NB, SMALL><<<nkb + (R + 7) / 8, 256, 0, s>>>(x, B, C, amax, xs, nkb, xT, R, rp, kc, kd, U, k, tmp,

@@ -11,6 +11,7 @@
 //
 // The reference has no batched prefill: it runs forward_token once per prompt token
 // (run_gpu_native_chat.py:1128-1131).
+#include <atomic>
 #include <algorithm>
 #include <cmath>
 
@@ -586,11 +587,17 @@ int gsdlq_attention_rows(const float* q, const uint16_t* k_cache, const uint16_t
   splits = std::max(1, std::min(std::min(splits, AT_MAXSPLIT), tiles));
   const dim3 grid(blocks, n_kv_heads, splits);
   float* wk = static_cast<float*>(work);
-  static bool attr = false;  // the 88 KB of the head_dim-128 tiles need the opt-in size
-  if (!attr) {
-    cudaFuncSetAttribute(attention_rows_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at_smem_bytes(128));
-    cudaFuncSetAttribute(attention_rows_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at_smem_bytes(64));
-    attr = true;
+  // the 88 KB of the head_dim-128 tiles need the opt-in size, set once per device
+  static std::atomic<bool> smem_set[64];
+  const int di = (dev >= 0 && dev < 64) ? dev : 0;
+  if (!smem_set[di].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(attention_rows_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)at_smem_bytes(128));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_rows_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)at_smem_bytes(64));
+    if (e != cudaSuccess) return record_cuda_error(e);
+    smem_set[di].store(true, std::memory_order_release);
   }
   if (head_dim == 128) {
     attention_rows_kernel<128><<<grid, AT_THREADS, at_smem_bytes(128), st>>>(
