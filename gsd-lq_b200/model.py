@@ -611,8 +611,12 @@ class GSDLQModel:
         1142-1144); the host looks at the device's done flag every check_every tokens and the steps
         after the stop do no more bookkeeping."""
         ids = list(prompt_ids)
-        if len(ids) + max_new_tokens > self.max_seq:
+        if not ids:
+            raise ValueError("the prompt needs at least one token")
+        if max_new_tokens < 0 or len(ids) + max_new_tokens > self.max_seq:
             raise ValueError("prompt + new tokens exceed max_seq")
+        if check_every < 1:
+            raise ValueError("check_every must be at least 1")
         sampled = temperature > 0.0
         if sampled and self.tp is not None:
             raise NotImplementedError("device sampling needs the whole vocabulary on one GPU")
@@ -628,6 +632,9 @@ class GSDLQModel:
         sb["done"].zero_()
         eos = -1 if eos_id is None else int(eos_id)
         name = f"head_gen_{float(temperature)!r}_{float(top_p)!r}_{eos}"
+        # the sampling settings are baked into the captured head: keep only the latest such graph
+        for old in [k for k in self._graphs if k.startswith("head_gen_") and k != name]:
+            del self._graphs[old]
 
         def run_head_gen():
             lib, st = L.load(), self.state.data_ptr()
