@@ -7,6 +7,7 @@ CPU path.
 from __future__ import annotations
 
 import ctypes
+import warnings
 
 import numpy as np
 import torch
@@ -113,7 +114,11 @@ class Arena:
             raise MemoryError("arena overflow")
         dst = self.buf[self.off:self.off + n]
         if n:
-            dst.copy_(torch.from_numpy(a.reshape(-1).view(np.uint8)), non_blocking=False)
+            # read-only memory-mapped blobs go straight to the device: torch only reads the view
+            with warnings.catch_warnings():
+                warnings.filterwarnings("ignore", message="The given NumPy array is not writable")
+                src = torch.from_numpy(a.reshape(-1).view(np.uint8))
+            dst.copy_(src, non_blocking=False)
         self.off += (n + self.ALIGN - 1) // self.ALIGN * self.ALIGN
         return dst
 

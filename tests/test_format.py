@@ -431,3 +431,22 @@ def test_arena_alignment_and_upload_from_mmap(tmp_path):
     with pytest.raises(MemoryError):
         ar.put(np.zeros(Arena.ALIGN + 1, np.uint8))
     assert torch.is_tensor(outs[0])
+
+
+def test_arena_places_mapped_blobs_on_256_byte_boundaries():
+    """The upload arena copies read-only memory-mapped blobs as they are, each at a 256-byte-aligned offset
+    (checked here on a host arena: the placement logic is the same for a device one)."""
+    import warnings
+    import gsdlq_b200.ops as ops
+    m = G.read_gsd2(os.path.join(GOLDEN, "tiny_precision.gsd2"))
+    blobs = [a for t in list(m.hex.values())[:3] for a in t.blobs().values()]
+    assert not blobs[0].flags.writeable
+    ar = ops.Arena(ops.Arena.bytes_needed(blobs), "cpu")
+    with warnings.catch_warnings():
+        warnings.simplefilter("error")
+        views = [ar.put(a) for a in blobs]
+    for a, v in zip(blobs, views):
+        assert v.data_ptr() % 256 == 0
+        assert np.array_equal(v.numpy(), np.ascontiguousarray(a).reshape(-1).view(np.uint8))
+    with pytest.raises(MemoryError):
+        ar.put(np.zeros(512, np.uint8))
