@@ -439,6 +439,10 @@ class GSDLQModel:
             if with_head:
                 self._run_head()
 
+    def synchronize(self):
+        """Wait for the model's device work (timing, or before reading results another way)."""
+        torch.cuda.synchronize(self.device)
+
     def set_state(self, token_id: int, pos: int):
         if not 0 <= pos < self.max_seq:
             raise ValueError(f"pos {pos} outside [0, {self.max_seq})")
@@ -599,7 +603,8 @@ class GSDLQModel:
             L.check(lib.gsdlq_vec_add(x.data_ptr(), x.data_ptr(), b["o"].data_ptr(), n * H, sh), "gsdlq_vec_add")
 
     def generate(self, prompt_ids, max_new_tokens: int, temperature: float = 0.0, top_p: float = 0.9,
-                 eos_id: int | None = None, check_every: int = 16) -> list[int]:
+                 eos_id: int | None = None, check_every: int = 16, start_pos: int = 0,
+                 on_tokens=None) -> list[int]:
         """Generation with the loop on the device: one graph replay per token (layers, LM head, then the
         pick and the bookkeeping), no host round trip per token.
 
@@ -609,7 +614,13 @@ class GSDLQModel:
         which is the sequence the reference's np.random.choice calls would consume.  eos_id: stop when
         the pick is eos_id, without returning it (the reference chat loop, run_gpu_native_chat.py:
         1142-1144); the host looks at the device's done flag every check_every tokens and the steps
-        after the stop do no more bookkeeping."""
+        after the stop do no more bookkeeping.
+
+        start_pos: the KV cache already holds prompt_ids[:start_pos] at positions 0 .. start_pos - 1 (a
+        previous turn's tokens, as the reference's chat loop reuses them, run_gpu_native_chat.py:1112-1114),
+        so only the rest of the prompt is prefilled.  on_tokens(ids): called with the ids produced since
+        its last call, every check_every tokens and once at the end (streaming); each call reads the
+        device's step counter, one host synchronisation per check_every tokens."""
         ids = list(prompt_ids)
         if not ids:
             raise ValueError("the prompt needs at least one token")
@@ -617,12 +628,15 @@ class GSDLQModel:
             raise ValueError("prompt + new tokens exceed max_seq")
         if check_every < 1:
             raise ValueError("check_every must be at least 1")
+        if not 0 <= start_pos < len(ids):
+            raise ValueError("start_pos must lie inside the prompt (its last token is always run)")
         sampled = temperature > 0.0
         if sampled and self.tp is not None:
             raise NotImplementedError("device sampling needs the whole vocabulary on one GPU")
-        self.prefill(ids[:-1])
+        self.prefill(ids[start_pos:-1], start_pos=start_pos)
         self.set_state(ids[-1], len(ids) - 1)
-        if not sampled and eos_id is None:
+        checks = eos_id is not None or on_tokens is not None
+        if not sampled and not checks:
             for _ in range(max_new_tokens):
                 self.step(with_head=True)   # the head's advance kernel feeds the next replay
             return self.out_ids[:max_new_tokens].cpu().tolist()
@@ -648,6 +662,7 @@ class GSDLQModel:
                                           self.out_ids.numel(), eos, sb["done"].data_ptr(), ops.stream_handle()),
                     "gsdlq_advance_eos")
 
+        emitted = 0
         for i in range(max_new_tokens):
             if self._plans:
                 L.check(L.load().gsdlq_decode_step(self._plans["layers"], ops.stream_handle()), "gsdlq_decode_step")
@@ -659,10 +674,19 @@ class GSDLQModel:
                 self._graph(name, run_head_gen).replay()
             else:
                 run_head_gen()
-            if eos_id is not None and (i + 1) % check_every == 0 and int(sb["done"].item()):
-                break
+            if checks and (i + 1) % check_every == 0:
+                if on_tokens is not None:
+                    n = int(self.state[2].item())
+                    if n > emitted:
+                        on_tokens(self.out_ids[emitted:n].cpu().tolist())
+                        emitted = n
+                if eos_id is not None and int(sb["done"].item()):
+                    break
         n = int(self.state[2].item())
-        return self.out_ids[:n].cpu().tolist()
+        out = self.out_ids[:n].cpu().tolist()
+        if on_tokens is not None and n > emitted:
+            on_tokens(out[emitted:])
+        return out
 
     def release(self):
         self._graphs.clear()

@@ -7,6 +7,7 @@ committed so the tests never need the reference at run time:
     python tests/golden/make_golden.py            # everything
     python tests/golden/make_golden.py sampling   # only sampling_ref.npz
     python tests/golden/make_golden.py tokenizer  # only tokenizer_ref.json
+    python tests/golden/make_golden.py chat       # only chat_prompt_ref.json
 
 What it records (all produced by the reference's own code):
   codebook.npz     _get_turbo_codebook(6|8) from both reference copies
@@ -21,6 +22,8 @@ What it records (all produced by the reference's own code):
   sampling_ref.npz the reference's sample_token picks (temperature + top-p) on fixed logits
                    under fixed np.random seeds
   tokenizer_ref.json the reference's SentencePiece-BPE encode/decode on a test vocabulary
+  chat_prompt_ref.json the reference's chat prompt template over fixed histories (its rules text
+                   replaced by a test string)
 """
 from __future__ import annotations
 
@@ -189,12 +192,46 @@ def tokenizer_main():
     print("tokenizer cases", len(enc), len(dec))
 
 
+CHAT_SYSTEM = "Test rules: answer briefly.\nSecond line."
+CHAT_HISTORIES = [
+    [],
+    [["hi", "Hello!"]],
+    [["first question", "first answer"], ["second", "reply with \"quotes\" and </s> inside"]],
+    [["a", ""], ["", "b"], ["x y z", "  padded  "]],
+]
+CHAT_MESSAGES = ["What is 2+2?", "", "multi\nline [INST] message"]
+
+
+def chat_main():
+    """chat_prompt_ref.json: the reference's format_mistral_prompt (run_gpu_native_chat.py:996-1013) over
+    fixed histories and messages, in both of its layouts.  Its module-level rules text is replaced by
+    CHAT_SYSTEM for the recording, so no text of the reference's own ends up in the fixture."""
+    import json
+    sys.path.insert(0, os.path.join(reference_tree(), "gsd_lq_v2"))
+    import run_gpu_native_chat as RG
+
+    RG.SYSTEM_RULES = CHAT_SYSTEM
+    cases = []
+    for h in CHAT_HISTORIES:
+        for msg in CHAT_MESSAGES:
+            hist = [tuple(t) for t in h]
+            cases.append({"history": h, "message": msg,
+                          "lightweight": RG.format_mistral_prompt(hist, msg, is_cpu=True),
+                          "with_system": RG.format_mistral_prompt(hist, msg, is_cpu=False)})
+    with open(os.path.join(HERE, "chat_prompt_ref.json"), "w", encoding="utf-8") as f:
+        json.dump({"system": CHAT_SYSTEM, "cases": cases}, f, ensure_ascii=False, indent=0)
+    print("chat prompt cases", len(cases))
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["sampling"]:
         sampling_main()
     elif sys.argv[1:] == ["tokenizer"]:
         tokenizer_main()
+    elif sys.argv[1:] == ["chat"]:
+        chat_main()
     else:
         main()
         sampling_main()
         tokenizer_main()
+        chat_main()
