@@ -180,3 +180,20 @@ def test_row_batch_and_sampling_argument_errors_before_launch():
     assert lib.gsdlq_argmax_rows(A, 2, 100, A, None, A, 16, None) == -1   # out_ids without positions
     assert lib.gsdlq_argmax_rows(A, 2, 100, A, A, A, 0, None) == -1
     assert lib.gsdlq_advance_eos(A, A, A, A, None, 0, 2, None, None) == -1
+
+
+def test_matvec_width_limit_refused_before_launch():
+    """Rows wider than GSDLQ_MATVEC_MAX_COLS (the fused matvec holds a whole input row in shared memory)
+    are refused as unsupported by the drop-in and the no-allocation matvec, before any device work; only
+    widths that are refused are tried here (a width that passes would go on to launch)."""
+    import re
+    lib = L.load()
+    hdr = open(L.HEADER).read()
+    limit = int(re.search(r"#define GSDLQ_MATVEC_MAX_COLS (\d+)", hdr).group(1))
+    assert limit % 64 == 0 and 32768 <= limit < 65472
+    A = ctypes.c_void_p(0x100000)
+    for cols in (limit + 64, 65472):
+        for rows in (16, 4096):
+            assert lib.gsdlq_hex2d_matvec(A, A, A, A, None, None, A, A, A, A, rows, cols, 0, 217, None) == -3
+            assert lib.gsdlq_hex2d_matvec_noalloc(A, A, A, A, None, None, A, A, A, A, rows, cols, 0, 217,
+                                                  None) == -3

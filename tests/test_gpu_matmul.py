@@ -41,6 +41,38 @@ def test_matmul_vs_oracle(env, restated, rng, rows, cols, k, nnz, radius, batch)
     assert L.device_flags() == 0
 
 
+@pytest.mark.parametrize("batch", [1, 5, 40])
+def test_matmul_widest_rows(env, restated, rng, batch):
+    """65472 columns, the widest multiple of 64 a u16 kink column reaches, with a kink in every row's last
+    column: the GEMM takes the width (its activations stream from global memory) where the fused matvec
+    refuses it as unsupported (GSDLQ_MATVEC_MAX_COLS)."""
+    ops, L = env
+    import gsdlq_b200.codebook as cb
+    rows, cols = 48, 65472
+    t = rand_hex(rng, rows, cols, k=16, nnz=8, radius=8)
+    kc = t.kink_cols.reshape(rows, 8).copy()
+    kc[:, -1] = cols - 1
+    t.kink_cols = np.sort(kc, axis=1).astype(np.uint16).reshape(-1)
+    t.validate()
+    rec = oracle_rec(t)
+    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    h = ops.DeviceHex(t)
+    y = torch.zeros((batch, rows), device="cuda")
+    xy = dev(cb.xy_table(8))
+    ops.hex2d_matmul(dev(x), h, xy, y, ops.matmul_work(batch, cols))
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    for b in range(batch):
+        yr = restated.matvec(np.ascontiguousarray(x[b]), rec, np.zeros(16, np.float32))
+        assert matvec_err(got[b], yr) < MATVEC_TOL, b
+    tk, y1 = torch.zeros(16, device="cuda"), torch.zeros(rows, device="cuda")
+    lib = L.load()
+    assert lib.gsdlq_hex2d_matvec(dev(x[0]).data_ptr(), h.codes.data_ptr(), h.scales.data_ptr(), xy.data_ptr(),
+                                  h.U.data_ptr(), tk.data_ptr(), h.row_ptr.data_ptr(), h.kink_cols.data_ptr(),
+                                  h.kink_deltas.data_ptr(), y1.data_ptr(), rows, cols, 16, 217, None) == -3
+    assert L.device_flags() == 0
+
+
 def test_matmul_batch1_matches_matvec(env, rng):
     ops, L = env
     import gsdlq_b200.codebook as cb
