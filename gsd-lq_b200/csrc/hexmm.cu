@@ -1015,14 +1015,18 @@ extern "C" int gsdlq_hex2d_matmul_work_size(int batch, int cols, size_t* bytes) 
   return GSDLQ_OK;
 }
 
-extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* codes, const uint16_t* scales,
-                                  const float* xy_table, const uint16_t* U, const float* S, const uint16_t* Vt,
-                                  const uint32_t* kink_row_ptr, const uint16_t* kink_cols, const float* kink_deltas,
-                                  float* y, void* work, size_t work_bytes, int rows, int cols, int k_dim, int n_pts,
-                                  gsdlq_stream_t stream) {
+// The GEMM call.  tmp_ext (batch 1 only): the caller's low-rank projection S (Vt x) of the token, used
+// instead of computing it from S and Vt (the drop-in matvec's contract, whose caller ran
+// gsdlq_lowrank_proj).
+static int hexmm_entry(const float* x, int batch, const uint8_t* codes, const uint16_t* scales,
+                       const float* xy_table, const uint16_t* U, const float* S, const uint16_t* Vt,
+                       const uint32_t* kink_row_ptr, const uint16_t* kink_cols, const float* kink_deltas, float* y,
+                       void* work, size_t work_bytes, int rows, int cols, int k_dim, int n_pts, cudaStream_t s,
+                       const float* tmp_ext) {
   if (!x || !codes || !scales || !xy_table || !kink_row_ptr || !y || !work) return GSDLQ_ERR_INVALID;
   if (batch < 1 || batch > MM_MAXB || rows <= 0 || cols <= 0 || cols % 64 != 0 || cols > 65535) return GSDLQ_ERR_INVALID;
-  if (k_dim < 0 || k_dim > 16 || (k_dim > 0 && (!U || !S || !Vt))) return GSDLQ_ERR_INVALID;
+  if (k_dim < 0 || k_dim > 16) return GSDLQ_ERR_INVALID;
+  if (tmp_ext ? batch != 1 || (k_dim > 0 && !U) : k_dim > 0 && (!U || !S || !Vt)) return GSDLQ_ERR_INVALID;
   if (n_pts < 1 || n_pts > 256) return GSDLQ_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(codes) & 15u) return GSDLQ_ERR_INVALID;  // 16-byte code loads
   if ((reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(U)) & 1u) return GSDLQ_ERR_INVALID;
@@ -1030,17 +1034,21 @@ extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* code
   if (reinterpret_cast<uintptr_t>(x) & 15u) return GSDLQ_ERR_INVALID;  // 16-byte activation loads
   if ((reinterpret_cast<uintptr_t>(y) & 3u) || (reinterpret_cast<uintptr_t>(work) & 1023u)) return GSDLQ_ERR_INVALID;
   if (work_bytes < mm_work_bytes(batch, cols)) return GSDLQ_ERR_INVALID;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   unsigned* amax = reinterpret_cast<unsigned*>(work);  // per-token max|x| (bits)
   float* tmp = reinterpret_cast<float*>(work) + MM_MAXB;
   uint8_t* xs = static_cast<uint8_t*>(work) + MM_XS_OFF;  // converted activations
   cudaError_t e = cudaMemsetAsync(work, 0, sizeof(float) * 17 * MM_MAXB, s);
   if (e != cudaSuccess) return record_cuda_error(e);
+  if (tmp_ext && k_dim > 0) {  // token 0's projection slot: tmp[j], j < k_dim
+    e = cudaMemcpyAsync(tmp, tmp_ext, sizeof(float) * k_dim, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return record_cuda_error(e);
+  }
   {
     const int nb = (batch + 7) / 8;
     float* xT = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + MM_XS_OFF + mm_xs_bytes(nb, cols));
-    hexmm_prep<<<dim3(nb, (cols + MM_PREP - 1) / MM_PREP), 256, 0, s>>>(x, batch, cols, Vt, S, k_dim, amax, tmp, xT,
-                                                                        8 * nb, y, (size_t)batch * rows);
+    // with tmp_ext the prep pass only converts x (k = 0: no projection of its own)
+    hexmm_prep<<<dim3(nb, (cols + MM_PREP - 1) / MM_PREP), 256, 0, s>>>(
+        x, batch, cols, tmp_ext ? nullptr : Vt, S, tmp_ext ? 0 : k_dim, amax, tmp, xT, 8 * nb, y, (size_t)batch * rows);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return record_cuda_error(e);
@@ -1060,3 +1068,34 @@ extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* code
   if (e != cudaSuccess) return record_cuda_error(e);
   return GSDLQ_OK;
 }
+
+extern "C" int gsdlq_hex2d_matmul(const float* x, int batch, const uint8_t* codes, const uint16_t* scales,
+                                  const float* xy_table, const uint16_t* U, const float* S, const uint16_t* Vt,
+                                  const uint32_t* kink_row_ptr, const uint16_t* kink_cols, const float* kink_deltas,
+                                  float* y, void* work, size_t work_bytes, int rows, int cols, int k_dim, int n_pts,
+                                  gsdlq_stream_t stream) {
+  return hexmm_entry(x, batch, codes, scales, xy_table, U, S, Vt, kink_row_ptr, kink_cols, kink_deltas, y, work,
+                     work_bytes, rows, cols, k_dim, n_pts, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+namespace gsdlq {
+
+// The drop-in matvec of a matrix the fused batch-1 kernel cannot plan (rows wider than its shared
+// memory holds, or more strips than its per-CTA accumulator covers): this GEMM with one token and the
+// caller's low-rank projection.  work: 1024-byte aligned, hexmm_wide_work_bytes(cols) bytes; x is first
+// copied to its end, where the GEMM's 16-byte activation loads are aligned whatever the caller's x.
+size_t hexmm_wide_work_bytes(int cols) { return mm_work_bytes(1, cols) + sizeof(float) * (size_t)cols; }
+
+int hexmm_matvec_wide(const float* x, const uint8_t* codes, const uint16_t* scales, const float* xy_table,
+                      const uint16_t* U, const float* tmp_k, const uint32_t* kink_row_ptr, const uint16_t* kink_cols,
+                      const float* kink_deltas, float* y, void* work, int rows, int cols, int k_dim, int n_pts,
+                      cudaStream_t s) {
+  if (!x || !work || cols <= 0 || cols % 64 != 0 || cols > 65535 || (k_dim > 0 && !tmp_k)) return GSDLQ_ERR_INVALID;
+  float* xa = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + mm_work_bytes(1, cols));
+  const cudaError_t e = cudaMemcpyAsync(xa, x, sizeof(float) * (size_t)cols, cudaMemcpyDeviceToDevice, s);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  return hexmm_entry(xa, 1, codes, scales, xy_table, U, nullptr, nullptr, kink_row_ptr, kink_cols, kink_deltas, y,
+                     work, mm_work_bytes(1, cols), rows, cols, k_dim, n_pts, s, tmp_k);
+}
+
+}  // namespace gsdlq

@@ -304,7 +304,15 @@ struct DropinWs {
   size_t bytes = 0;
 };
 static DropinWs g_mv_ws[64];
-static std::mutex g_mv_mu;  // guards g_mv_ws: the grow (free + malloc) and the launch that reads it
+static DropinWs g_wide_ws[64];  // the GEMM's work for matrices the fused kernel cannot plan
+static std::mutex g_mv_mu;  // guards g_mv_ws and g_wide_ws: the grow (free + malloc) and the launch that reads it
+
+// in hexmm.cu: the GEMM with one token, for matrices the fused kernel cannot plan
+size_t hexmm_wide_work_bytes(int cols);
+int hexmm_matvec_wide(const float* x, const uint8_t* codes, const uint16_t* scales, const float* xy_table,
+                      const uint16_t* U, const float* tmp_k, const uint32_t* kink_row_ptr, const uint16_t* kink_cols,
+                      const float* kink_deltas, float* y, void* work, int rows, int cols, int k_dim, int n_pts,
+                      cudaStream_t s);
 
 }  // namespace gsdlq
 
@@ -360,12 +368,30 @@ extern "C" int gsdlq_hex2d_matvec(const float* x, const uint8_t* codes, const ui
   P.n_pts = n_pts;
   P.tmp_k_ext = k_dim > 0 ? tmp_k : nullptr;
   const int st = hexmv_plan(P);
-  if (st != GSDLQ_OK) return st;
-  const size_t need = hexmv_ws_bytes_for(P.n_strips, P.nmat);
+  if (st != GSDLQ_OK && st != GSDLQ_ERR_UNSUPPORTED) return st;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return record_cuda_error(e);
   if (dev < 0 || dev >= 64) return GSDLQ_ERR_UNSUPPORTED;
+  if (st == GSDLQ_ERR_UNSUPPORTED) {
+    // beyond the fused kernel's shared memory (rows wider than GSDLQ_MATVEC_MAX_COLS, or very tall and
+    // wide): the dequant-GEMM with one token, same result within the matvec tolerance
+    const size_t wneed = hexmm_wide_work_bytes(cols) + 1024;
+    std::lock_guard<std::mutex> lock(g_mv_mu);
+    DropinWs& w = g_wide_ws[dev];
+    if (w.bytes < wneed) {
+      if (w.p) cudaFree(w.p);
+      w.p = nullptr;
+      w.bytes = 0;
+      e = cudaMalloc(&w.p, wneed);
+      if (e != cudaSuccess) return record_cuda_error(e);
+      w.bytes = wneed;
+    }
+    void* wa = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(w.p) + 1023) & ~static_cast<uintptr_t>(1023));
+    return hexmm_matvec_wide(x, codes, scales, xy_table, U, tmp_k, kink_row_ptr, kink_cols, kink_deltas, y, wa, rows,
+                             cols, k_dim, n_pts, static_cast<cudaStream_t>(stream));
+  }
+  const size_t need = hexmv_ws_bytes_for(P.n_strips, P.nmat);
   std::lock_guard<std::mutex> lock(g_mv_mu);
   DropinWs& ws = g_mv_ws[dev];
   if (ws.bytes < need) {

@@ -88,10 +88,12 @@ int gsdlq_lowrank_proj(const float *x, const uint16_t *Vt, const float *S, float
  * larger matrix comes).  Back-to-back calls on one stream may share it; calls on DIFFERENT
  * streams of one device must not run at the same time (the reference's function is synchronous).
  * Callers with several streams use gsdlq_linear with a workspace per stream.
- * Width: a CTA holds the whole input row in shared memory (about 4 bytes per column), so cols above
- * GSDLQ_MATVEC_MAX_COLS return GSDLQ_ERR_UNSUPPORTED before anything touches the device (the
- * reference's limit is the u16 kink column, 65535); the same holds for gsdlq_linear and
- * gsdlq_hex2d_matvec_noalloc.  gsdlq_hex2d_matmul takes any cols up to 65535. */
+ * Width: the fused kernel holds a whole input row in shared memory (about 4 bytes per column), up to
+ * GSDLQ_MATVEC_MAX_COLS columns.  Wider rows (to 65535, the reference's u16 kink column), and matrices
+ * too tall for its per-CTA accumulator at such widths, go through the dequant-GEMM with one token
+ * (gsdlq_hex2d_matmul's kernels, same result within the tolerance, codes 16-byte aligned), with a
+ * second per-device scratch area.  gsdlq_linear and gsdlq_hex2d_matvec_noalloc return
+ * GSDLQ_ERR_UNSUPPORTED for those shapes instead, before anything touches the device. */
 #define GSDLQ_MATVEC_MAX_COLS 48640
 int gsdlq_hex2d_matvec(const float *x, const uint8_t *codes, const uint16_t *scales,
                        const float *xy_table, const uint16_t *U, const float *tmp_k,

@@ -44,8 +44,9 @@ def test_matmul_vs_oracle(env, restated, rng, rows, cols, k, nnz, radius, batch)
 @pytest.mark.parametrize("batch", [1, 5, 40])
 def test_matmul_widest_rows(env, restated, rng, batch):
     """65472 columns, the widest multiple of 64 a u16 kink column reaches, with a kink in every row's last
-    column: the GEMM takes the width (its activations stream from global memory) where the fused matvec
-    refuses it as unsupported (GSDLQ_MATVEC_MAX_COLS)."""
+    column: the GEMM takes the width (its activations stream from global memory); the fused matvec cannot
+    (GSDLQ_MATVEC_MAX_COLS), so the drop-in matvec hands such rows to the GEMM, and the no-allocation
+    matvec refuses them."""
     ops, L = env
     import gsdlq_b200.codebook as cb
     rows, cols = 48, 65472
@@ -65,11 +66,21 @@ def test_matmul_widest_rows(env, restated, rng, batch):
     for b in range(batch):
         yr = restated.matvec(np.ascontiguousarray(x[b]), rec, np.zeros(16, np.float32))
         assert matvec_err(got[b], yr) < MATVEC_TOL, b
-    tk, y1 = torch.zeros(16, device="cuda"), torch.zeros(rows, device="cuda")
+    # the drop-in pair (projection, then matvec) on token 0, its x at an offset that is not 16-byte aligned
+    tk, y1 = torch.zeros(16, device="cuda"), torch.full((rows,), 7.0, device="cuda")
+    xbuf = torch.zeros(cols + 1, device="cuda")
+    xbuf[1:].copy_(dev(x[0]))
+    x0 = xbuf[1:]
+    ops.lowrank_proj(x0, h, tk)
+    ops.hex2d_matvec(x0, h, xy, tk, y1)
+    torch.cuda.synchronize()
+    yr = restated.matvec(np.ascontiguousarray(x[0]), rec, np.zeros(16, np.float32))
+    assert matvec_err(y1.cpu().numpy(), yr) < MATVEC_TOL
     lib = L.load()
-    assert lib.gsdlq_hex2d_matvec(dev(x[0]).data_ptr(), h.codes.data_ptr(), h.scales.data_ptr(), xy.data_ptr(),
-                                  h.U.data_ptr(), tk.data_ptr(), h.row_ptr.data_ptr(), h.kink_cols.data_ptr(),
-                                  h.kink_deltas.data_ptr(), y1.data_ptr(), rows, cols, 16, 217, None) == -3
+    assert lib.gsdlq_hex2d_matvec_noalloc(x0.data_ptr(), h.codes.data_ptr(), h.scales.data_ptr(), xy.data_ptr(),
+                                          h.U.data_ptr(), tk.data_ptr(), h.row_ptr.data_ptr(),
+                                          h.kink_cols.data_ptr(), h.kink_deltas.data_ptr(), y1.data_ptr(), rows,
+                                          cols, 16, 217, None) == -3
     assert L.device_flags() == 0
 
 
