@@ -34,9 +34,12 @@ def _rand_hex(rng, rows, cols, k, nnz_per_row, radius=8):
     return rec
 
 
-@pytest.mark.parametrize("rows,cols,k,nnz", [(64, 128, 16, 4), (33, 256, 0, 0), (128, 1024, 8, 3)])
+@pytest.mark.parametrize("rows,cols,k,nnz", [(64, 128, 16, 4), (33, 256, 0, 0), (128, 1024, 8, 3),
+                                             (1, 64, 1, 1), (5, 65472, 16, 8)])  # widest row a u16 kink reaches
 def test_matvec_restatement_bitexact_vs_reference(restated, reference_engine, rng, rows, cols, k, nnz):
     rec = _rand_hex(rng, rows, cols, k, nnz)
+    if nnz:
+        rec["kink_cols"][nnz - 1::nnz] = cols - 1  # the last column, in every row
     x = rng.standard_normal(cols).astype(np.float32)
     y1 = restated.matvec(x, rec)
     y2 = reference_engine.matvec(x, rec)
