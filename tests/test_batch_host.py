@@ -106,3 +106,43 @@ def test_reference_arm_prints_the_contract_line():
     r = _run_bench(["--impl", "reference", "--model", "tiny", "--prompt", "16", "--steps", "2", "--warmup", "3"],
                    {"RANK": "1", "WORLD_SIZE": "2"})
     assert r.returncode == 0 and not r.stdout.strip(), (r.stdout, r.stderr[-2000:])
+
+
+def _bench_module():
+    import importlib.util
+    import os
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("bench_mod_clocks", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    return bench
+
+
+def test_clock_sampler_reads_nvidia_smi_lines(tmp_path, monkeypatch):
+    """The bench's clock record (median SM clock, max clock, active slowdown reasons) from nvidia-smi's CSV
+    stream, here a stand-in script on PATH; malformed lines are skipped; no nvidia-smi at all gives an
+    explicit 'unavailable' record."""
+    import os
+    import time
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text("#!/bin/sh\ncat <<'EOF'\n"
+                    "0, 1965, 1965, 700.1, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active\n"
+                    "0, 1950, 1965, 990.0, 0x0000000000000004, Not Active, Not Active, Not Active, Active\n"
+                    "0, [N/A], 1965, 991.0, 0x0, Not Active, Not Active, Not Active, Not Active\n"
+                    "partial, line\n"
+                    "0, 1800, 1965, 995.0, 0x0000000000000004, Not Active, Not Active, Not Active, Active\n"
+                    "EOF\nexec sleep 30\n")
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}{os.pathsep}{os.environ['PATH']}")
+    bench = _bench_module()
+    s = bench.ClockSampler(0)
+    s.start()
+    time.sleep(0.3)
+    assert s.stop() == {"sm_mhz": 1950.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 3}
+    empty = tmp_path / "empty"
+    empty.mkdir()
+    monkeypatch.setenv("PATH", str(empty))
+    s = bench.ClockSampler(0)
+    s.start()
+    r = s.stop()
+    assert r["samples"] == 0 and r["sm_mhz"] is None and r["reasons"] == ["nvidia-smi unavailable"]
