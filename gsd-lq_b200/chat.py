@@ -88,16 +88,18 @@ class ChatSession:
                 raise ValueError(f"the message alone takes {len(ids)} tokens; the cache holds {S}")
         start = 0 if reset else shared_prefix(self.cached, ids)
         max_new = min(self.max_new_tokens, S - len(ids) - 1)
-        shown = [""]
+        shown = ""
         got: list[int] = []
 
         def stream(new_ids):
+            # the reference prints decode(all ids so far) minus what it printed before (:1146-1149)
+            nonlocal shown
             got.extend(new_ids)
             if on_text is not None:
                 text = self.tok.decode(got)
-                if len(text) > len(shown[0]):
-                    on_text(text[len(shown[0]):])
-                shown[0] = text
+                if len(text) > len(shown):
+                    on_text(text[len(shown):])
+                shown = text
 
         t0 = time.perf_counter()
         self.m.prefill(ids[start:-1], start_pos=start)
