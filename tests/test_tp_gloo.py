@@ -231,3 +231,26 @@ def test_device_shards_equal_host_shards(world, mode):
                 got = np.ascontiguousarray(d.blobs()[key]).reshape(-1).view(np.uint8)
                 want = np.ascontiguousarray(arr).reshape(-1).view(np.uint8)
                 assert np.array_equal(got, want), (name, key, rank)
+
+
+@pytest.mark.parametrize("model,world,ok", [
+    ("mistral-7b", 2, True), ("mistral-7b", 8, True), ("mistral-7b", 3, False),
+    ("qwen2.5-1.5b", 2, True), ("qwen2.5-1.5b", 4, False),      # 2 kv heads
+    ("smollm2-1.7b", 8, True),
+])
+def test_tp_shape_checks(model, world, ok):
+    """Tensor-parallel sharding refuses configurations whose heads, FFN or vocabulary do not split evenly,
+    or whose row-parallel shards are not whole 64-column scale groups, before anything is sliced."""
+    import gsdlq_b200.packer as P
+    import gsdlq_b200.tp as T
+    cfg = P.make_config(model)
+    if ok:
+        T.check_divisible(cfg, world)
+        loc = T.local_config(cfg, world)
+        assert loc["n_heads_local"] * world == cfg["n_heads"] and loc["ffn_size_local"] * world == cfg["ffn_size"]
+    else:
+        with pytest.raises(ValueError, match="divisible"):
+            T.check_divisible(cfg, world)
+    small = P.make_config("tiny", n_heads=2, n_kv_heads=2, head_dim=64, ffn_size=192, vocab_size=64)
+    with pytest.raises(ValueError, match="multiples of 64"):
+        T.check_divisible(small, 2)   # 192 / 2 = 96 FFN columns per rank
