@@ -450,3 +450,22 @@ def test_arena_places_mapped_blobs_on_256_byte_boundaries():
         assert np.array_equal(v.numpy(), np.ascontiguousarray(a).reshape(-1).view(np.uint8))
     with pytest.raises(MemoryError):
         ar.put(np.zeros(512, np.uint8))
+
+
+@pytest.mark.parametrize("mode", ["precision", "turbo"])
+def test_bench_generator_round_trip(tmp_path, mode):
+    """The bench's weight generator (random_packed_model) writes files the hardened reader accepts with every
+    check on, blob for blob; layout keys carried over from a read file never override the written layout."""
+    cfg = P.make_config("tiny")
+    m = P.random_packed_model(cfg, mode, seed=4)
+    m.extra = {"alignment": 512, "format_version": 1, "note": "kept"}
+    p = str(tmp_path / "g.gsd2")
+    G.write_gsd2(p, m)
+    r = G.read_gsd2(p, check_codes=True, check_values=True)
+    assert r.extra["alignment"] == 256 and r.extra["format_version"] == 2 and r.extra["note"] == "kept"
+    assert r.mode == mode
+    for n, t in m.hex.items():
+        for k, a in t.blobs().items():
+            assert np.array_equal(a, getattr(r.hex[n], k)), (n, k)
+    for n, a in m.dense.items():
+        assert np.array_equal(np.asarray(a).reshape(-1), r.dense[n].reshape(-1)), n
