@@ -55,6 +55,22 @@ def peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
+def prefill_roofline(cfg: dict, tokens: int, secs: float, pk: dict, pk_src: str, sequences: int = 1) -> dict:
+    """Tensor-pipe roofline of a prefill of ``tokens`` prompt tokens per sequence from position 0: 2 flops per
+    packed weight of every layer linear per token (the LM head does not run), plus causal attention
+    (QK^T and PV: 4 * heads * head_dim flops per query-key pair, t + 1 keys for token t), against the
+    measured dense bf16 burst peak."""
+    H, F = cfg["hidden_size"], cfg["ffn_size"]
+    q, kv = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+    weights = cfg["n_layers"] * (q * H + 2 * kv * H + H * q + 3 * F * H)
+    pairs = tokens * (tokens + 1) // 2
+    flops = sequences * (2 * weights * tokens + cfg["n_layers"] * 4 * q * pairs)
+    peak = float(pk["bf16_tflops"])
+    achieved = flops / secs / 1e12
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "flops": flops, "peak_source": f"{pk_src} bf16_tflops"}
+
+
 def vs_published(args, tok_s):
     """value / the reference's published decode rate, for the one model it publishes (Mistral-7B)."""
     return tok_s / PUBLISHED_TOKS[args.mode] if args.model == "mistral-7b" else None
@@ -539,6 +555,7 @@ def run_ours(args):
             "prefill_s": round(prefill_s, 3) if prefill_s is not None else None,
             "prefill_tok_s": round((P0 - 1) / prefill_s, 1) if prefill_s else None,
             "prefill_token_by_token_s": round(prefill_token_s, 3),
+            "prefill_roofline": prefill_roofline(cfg, P0 - 1, prefill_s, pk, pk_src) if prefill_s else None,
             "avg_bpw": round(model.avg_bpw, 4), "step": "fused" if model.fused_step else "per-op",
             "n_layers": model.n_layers, "l2_prefetch": model.prefetch,
             "tp_exchange": model.tp.exchange if model.tp is not None else None,
@@ -700,7 +717,9 @@ def run_batch(args):
                      "traffic": None},
         "kinds": kinds, "ids_sha": ids_sha, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * args.steps,
         "clocks": clocks, "pack_s": round(pack_s, 2), "prefill_s": round(prefill_s, 3),
-        "prefill_tok_s": round(B * (P0 - 1) / prefill_s, 1), "avg_bpw": round(model.avg_bpw, 4),
+        "prefill_tok_s": round(B * (P0 - 1) / prefill_s, 1),
+        "prefill_roofline": prefill_roofline(cfg, P0 - 1, prefill_s, pk, pk_src, sequences=B),
+        "avg_bpw": round(model.avg_bpw, 4),
         "n_layers": model.n_layers,
     }
     print(json.dumps(line), flush=True)

@@ -146,3 +146,18 @@ def test_clock_sampler_reads_nvidia_smi_lines(tmp_path, monkeypatch):
     s.start()
     r = s.stop()
     assert r["samples"] == 0 and r["sm_mhz"] is None and r["reasons"] == ["nvidia-smi unavailable"]
+
+
+def test_prefill_roofline_counts_linear_and_causal_attention_flops():
+    """The bench's prefill tensor roofline: 2 flops per layer weight per token plus 4 * heads * head_dim per
+    causal query-key pair, counted here by brute force over the tokens."""
+    import gsdlq_b200.packer as P
+    bench = _bench_module()
+    cfg = P.make_config("qwen2.5-1.5b")
+    shapes = P.linear_shapes(cfg)
+    T, L = 37, cfg["n_layers"]
+    weights = L * sum(r * c for r, c in shapes.values())
+    flops = 2 * weights * T + sum(L * 4 * cfg["n_heads"] * cfg["head_dim"] * (t + 1) for t in range(T))
+    r = bench.prefill_roofline(cfg, T, 0.5, {"bf16_tflops": 1000.0}, "measured", sequences=3)
+    assert r["flops"] == 3 * flops and r["bound"] == "tensor" and r["unit"] == "TFLOP/s"
+    assert abs(r["achieved"] - 3 * flops / 0.5 / 1e12) < 1e-9 and abs(r["frac"] - r["achieved"] / 1000.0) < 1e-12
