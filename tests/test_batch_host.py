@@ -161,3 +161,21 @@ def test_prefill_roofline_counts_linear_and_causal_attention_flops():
     r = bench.prefill_roofline(cfg, T, 0.5, {"bf16_tflops": 1000.0}, "measured", sequences=3)
     assert r["flops"] == 3 * flops and r["bound"] == "tensor" and r["unit"] == "TFLOP/s"
     assert abs(r["achieved"] - 3 * flops / 0.5 / 1e12) < 1e-9 and abs(r["frac"] - r["achieved"] / 1000.0) < 1e-12
+
+
+def test_batch_decoder_refuses_bad_setups_before_allocating():
+    """BatchDecoder checks tensor parallelism, the batch range, the attention shapes and the cache length
+    on the host, before it touches the device (a stand-in model: nothing here needs a GPU)."""
+    import types
+    import pytest
+    from gsdlq_b200.batch import BatchDecoder
+    ok = dict(tp=None, batched_prefill_supported=True, max_seq=256)
+    with pytest.raises(NotImplementedError, match="one GPU"):
+        BatchDecoder(types.SimpleNamespace(**{**ok, "tp": object()}), 4)
+    for b in (0, 129):
+        with pytest.raises(ValueError, match="batch must be"):
+            BatchDecoder(types.SimpleNamespace(**ok), b)
+    with pytest.raises(NotImplementedError, match="head_dim"):
+        BatchDecoder(types.SimpleNamespace(**{**ok, "batched_prefill_supported": False}), 4)
+    with pytest.raises(ValueError, match="max_seq"):
+        BatchDecoder(types.SimpleNamespace(**ok), 4, max_seq=512)
