@@ -179,3 +179,26 @@ def test_batch_decoder_refuses_bad_setups_before_allocating():
         BatchDecoder(types.SimpleNamespace(**{**ok, "batched_prefill_supported": False}), 4)
     with pytest.raises(ValueError, match="max_seq"):
         BatchDecoder(types.SimpleNamespace(**ok), 4, max_seq=512)
+
+
+def test_generate_refuses_bad_arguments_before_the_device():
+    """GSDLQModel.generate's host checks (empty prompt, cache length, check interval, reuse position, device
+    sampling under tensor parallelism) run before any device work: here on a stand-in model object."""
+    import types
+    import pytest
+    from gsdlq_b200.model import GSDLQModel
+    m = types.SimpleNamespace(max_seq=32, tp=None)
+    gen = GSDLQModel.generate
+    with pytest.raises(ValueError, match="at least one token"):
+        gen(m, [], 4)
+    with pytest.raises(ValueError, match="exceed max_seq"):
+        gen(m, [1] * 30, 3)
+    with pytest.raises(ValueError, match="exceed max_seq"):
+        gen(m, [1, 2], -1)
+    with pytest.raises(ValueError, match="check_every"):
+        gen(m, [1, 2], 4, check_every=0)
+    for sp in (-1, 2, 5):
+        with pytest.raises(ValueError, match="start_pos"):
+            gen(m, [1, 2], 4, start_pos=sp)
+    with pytest.raises(NotImplementedError, match="whole vocabulary"):
+        gen(types.SimpleNamespace(max_seq=32, tp=object()), [1, 2], 4, temperature=0.7)
