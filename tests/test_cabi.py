@@ -110,8 +110,11 @@ int main(void) {
   float rope[4 * 8 * 2];
   int n6 = gsdlq_codebook(6, xy, 256), n8 = gsdlq_codebook(8, xy, 256);
   int st = gsdlq_rope_table(rope, 4, 16, 10000.0f);
-  printf("%s|%s|%d|%d|%d|%d\n", gsdlq_version(), gsdlq_status_string(GSDLQ_ERR_INVALID), n6, n8, st,
-         gsdlq_hex2d_matvec(0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 16, 64, 0, 217, 0));
+  size_t mm = 0, at = 0, sp = 0;
+  int w1 = gsdlq_hex2d_matmul_work_size(16, 4096, &mm), w2 = gsdlq_attention_rows_work_size(128, 32, 128, &at);
+  int w3 = gsdlq_sample_work_size(32768, &sp);
+  printf("%s|%s|%d|%d|%d|%d|%d %zu|%d %zu|%d %zu\n", gsdlq_version(), gsdlq_status_string(GSDLQ_ERR_INVALID), n6,
+         n8, st, gsdlq_hex2d_matvec(0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 16, 64, 0, 217, 0), w1, mm, w2, at, w3, sp);
   return 0;
 }
 ''')
@@ -121,9 +124,18 @@ int main(void) {
     assert r.returncode == 0, r.stderr
     out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert out.returncode == 0, out.stderr
-    ver, msg, n6, n8, st, bad = out.stdout.strip().split("|")
+    ver, msg, n6, n8, st, bad, mm, at, sp = out.stdout.strip().split("|")
     assert ver.startswith("0.") and msg == "invalid argument"
     assert (int(n6), int(n8), int(st), int(bad)) == (127, 217, 0, -1)
+    # the work sizes seen from C equal those seen through ctypes
+    lib = L.load()
+    for got, fn, args in ((mm, lib.gsdlq_hex2d_matmul_work_size, (16, 4096)),
+                          (at, lib.gsdlq_attention_rows_work_size, (128, 32, 128)),
+                          (sp, lib.gsdlq_sample_work_size, (32768,))):
+        n = ctypes.c_size_t()
+        assert fn(*args, ctypes.byref(n)) == 0
+        status, size = got.split()
+        assert int(status) == 0 and int(size) == n.value > 0
 
 
 def test_row_batch_and_sampling_argument_errors_before_launch():
